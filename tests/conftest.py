@@ -1,0 +1,32 @@
+"""Shared pytest configuration.
+
+Tests marked ``gpu`` run the CUDA path on a B200 and compare it with the CPU
+oracle; everything else runs on the CPU-only host (oracle vs golden vectors,
+host-side load logic, C-ABI symbol exports, multi-rank host logic over gloo).
+"""
+
+import json
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def fixtures() -> dict:
+    return {k: bytes.fromhex(v) for k, v in json.loads((GOLDEN / "onnx_fixtures.json").read_text()).items()}
+
+
+@pytest.fixture(scope="session")
+def expected() -> dict:
+    return json.loads((GOLDEN / "expected.json").read_text())

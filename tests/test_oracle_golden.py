@@ -1,0 +1,235 @@
+"""Pin the CPU oracle to the reference's own known answers (CPU only).
+
+Each case reproduces an assertion from the reference's tests, recorded with its
+file:line in ``tests/golden/expected.json``.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import flex_oracle as fo
+from tynx_b200.onnx import ir
+
+
+def _model(fixtures, name, **kw):
+    return fo.OracleModel(ir.load_training_graph(fixtures[name], **kw))
+
+
+def test_gemm_forward_backward(fixtures, expected):
+    case = expected["gemm_forward_backward"]
+    model = _model(fixtures, case["model"],
+                   initializer_names={"weight": "head.weight", "bias": "head.bias"})
+    x = fo.T(np.asarray(case["input"], np.float32), requires_grad=True)
+    y = model(x)
+    fo.sum_(y).backward()
+    np.testing.assert_allclose(y.data.reshape(-1), case["output"], rtol=1e-6)
+    np.testing.assert_allclose(x.grad.reshape(-1), case["input_grad"], rtol=1e-6)
+    params = dict(model.named_parameters())
+    assert sorted(params) == ["head.bias", "head.weight"]
+    np.testing.assert_allclose(params["head.weight"].grad.reshape(-1), case["weight_grad"])
+    np.testing.assert_allclose(params["head.bias"].grad.reshape(-1), case["bias_grad"])
+
+
+def test_gemm_sgd_next_forward(fixtures, expected):
+    case = expected["gemm_sgd_next_forward"]
+    model = _model(fixtures, case["model"])
+    opt = fo.SGD(model.named_parameters(), lr=case["lr"])
+    x = np.asarray(case["input"], np.float32)
+    fo.sum_(model(x)).backward()
+    opt.step()
+    np.testing.assert_allclose(model(x).data.reshape(-1), case["next_output"], rtol=1e-6)
+
+
+def test_clip_gemm(fixtures, expected):
+    case = expected["clip_gemm"]
+    model = _model(fixtures, case["model"])
+    y = model(np.asarray(case["input"], np.float32))
+    fo.sum_(y).backward()
+    np.testing.assert_allclose(y.data.reshape(-1), case["output"])
+    p = dict(model.named_parameters())
+    np.testing.assert_allclose(p["weight"].grad.reshape(-1), case["weight_grad"])
+    np.testing.assert_allclose(p["bias"].grad.reshape(-1), case["bias_grad"])
+
+
+def test_gather_accumulation(fixtures, expected):
+    case = expected["gather_accumulation"]
+    model = _model(fixtures, case["model"])
+    idx = np.asarray(case["indices"], np.int64)
+    y = model(idx)
+    assert y.data.tolist() == case["output"]
+    fo.sum_(y).backward()
+    w = dict(model.named_parameters())["embedding.weight"]
+    assert w.grad.tolist() == case["weight_grad"]
+    fo.SGD(model.named_parameters(), lr=case["lr"]).step()
+    np.testing.assert_allclose(model(idx).data.reshape(-1), case["next_output"], rtol=1e-6)
+
+
+def test_layer_norm(fixtures, expected):
+    case = expected["layer_norm"]
+    model = _model(fixtures, case["model"])
+    x = np.asarray(case["input"], np.float32)
+    y = model(x)
+    np.testing.assert_allclose(y.data.reshape(-1), case["output"], atol=case["abs"])
+    fo.sum_(y).backward()
+    p = dict(model.named_parameters())
+    np.testing.assert_allclose(p["norm.weight"].grad.reshape(-1), case["weight_grad"],
+                               atol=case["abs"])
+    np.testing.assert_allclose(p["norm.bias"].grad.reshape(-1), case["bias_grad"],
+                               atol=case["abs"])
+    fo.SGD(model.named_parameters(), lr=case["lr"]).step()
+    np.testing.assert_allclose(model(x).data.reshape(-1), case["next_output"], atol=case["abs"])
+
+
+def test_batched_matmul(fixtures, expected):
+    case = expected["batched_matmul"]
+    model = _model(fixtures, case["model"])
+    y = model(np.asarray(case["input"], np.float32))
+    assert y.shape == (2, 2, 2)
+    np.testing.assert_allclose(y.data.reshape(-1), case["output"])
+    fo.sum_(y).backward()
+    w = dict(model.named_parameters())["projection.weight"]
+    np.testing.assert_allclose(w.grad.reshape(-1), case["weight_grad"])
+
+
+def _scalar_param(value):
+    return fo.T(np.asarray([value], np.float32), requires_grad=True)
+
+
+def test_adam_constant_gradient(expected):
+    case = expected["adam_constant_gradient"]
+    p = _scalar_param(case["weight"])
+    opt = fo.Adam([p], lr=case["lr"])
+    for want in case["trajectory"]:
+        p.grad = np.asarray([case["grad"]], np.float32)
+        opt.step()
+        assert abs(p.data[0] - want) < 1e-6
+
+
+def test_adam_vs_adamw(expected):
+    case = expected["adam_vs_adamw_decay"]
+    for decoupled, want in ((False, case["adam"]), (True, case["adamw"])):
+        p = _scalar_param(case["weight"])
+        p.grad = np.asarray([case["grad"]], np.float32)
+        fo.Adam([p], lr=case["lr"], betas=tuple(case["betas"]), eps=case["eps"],
+                weight_decay=case["weight_decay"], decoupled=decoupled).step()
+        assert abs(p.data[0] - want) < 1e-6
+
+
+def test_amsgrad(expected):
+    case = expected["amsgrad"]
+    p = _scalar_param(case["weight"])
+    opt = fo.Adam([p], lr=case["lr"], betas=tuple(case["betas"]), eps=case["eps"], amsgrad=True)
+    for g in case["grads"]:
+        p.grad = np.asarray([g], np.float32)
+        opt.step()
+    assert abs(p.data[0] - case["final"]) < 1e-6
+
+
+def test_softmax_and_log_softmax(expected):
+    case = expected["softmax_axis0"]
+    y = fo.softmax(fo.T(np.asarray(case["input"], np.float32)), case["axis"])
+    np.testing.assert_allclose(y.data, case["output"], atol=case["abs"])
+    case = expected["log_softmax_stable"]
+    y = fo.log_softmax(fo.T(np.asarray(case["input"], np.float32)), 0)
+    np.testing.assert_allclose(y.data, case["output"], atol=case["abs"])
+
+
+def test_gelu_exact(expected):
+    case = expected["gelu_exact_erf"]
+    y = fo.gelu(fo.T(np.asarray(case["input"], np.float32)))
+    np.testing.assert_allclose(y.data, case["output"], atol=case["abs"])
+
+
+def test_mse(expected):
+    case = expected["mse"]
+    loss = fo.mse_loss(fo.T(np.asarray(case["prediction"], np.float32)), case["target"])
+    assert abs(loss.item() - case["loss"]) < 1e-6
+
+
+def test_ppo_trains(fixtures, expected):
+    case = expected["ppo_training"]
+    names = {"policy_weight": "policy.weight", "policy_bias": "policy.bias",
+             "value_weight": "value.weight", "value_bias": "value.bias"}
+    model = _model(fixtures, case["model"], initializer_names=names)
+    obs = np.asarray(case["observations"], np.float32)
+    actions = np.asarray(case["actions"], np.int64)
+    ln, vn = model.graph.outputs
+    out = model(obs)
+    old = fo.Categorical(out[ln].detach()).log_prob(actions).data
+    np.testing.assert_allclose(old, [expected["ppo_initial_log_prob"]["old_log_prob"]] * 4,
+                               rtol=1e-6)
+
+    def loss_fn():
+        o = model(obs)
+        loss = fo.ppo_loss(o[ln], o[vn], actions, old, case["advantages"], case["returns"])
+        vl = fo.mse_loss(fo.reshape(o[vn], (4,)), case["returns"])
+        return loss, vl
+
+    l0, v0 = loss_fn()
+    opt = fo.Adam(model.named_parameters(), lr=case["lr"])
+    for _ in range(case["steps"]):
+        opt.zero_grad()
+        loss, _ = loss_fn()
+        loss.backward()
+        opt.step()
+    l1, v1 = loss_fn()
+    assert l1.item() < l0.item()
+    assert v1.item() < v0.item() * case["final_value_loss_ratio_below"]
+    probs = fo.Categorical(model(obs)[ln]).probs.data
+    chosen = probs[np.arange(4), actions].mean()
+    assert chosen > case["chosen_probability_above"]
+
+
+@pytest.mark.parametrize("name", ["_CNN_MODEL", "_RECOMMENDER_MODEL", "_TRANSFORMER_MODEL"])
+def test_composed_models_train(fixtures, expected, name):
+    spec = expected["composed_training"]
+    case = spec["cases"][name]
+    graph = ir.load_training_graph(fixtures[name])
+    assert graph.report.warnings == []
+    assert sorted(graph.report.trainable_parameters) == case["trainable"]
+    model = fo.OracleModel(graph)
+    dtype = np.int64 if case.get("input_dtype") == "int64" else np.float32
+    x = np.asarray(case["input"], dtype)
+    target = np.asarray(case["target"], np.float32)
+    opt = fo.Adam(model.named_parameters(), lr=spec["lr"])
+    initial = fo.mse_loss(model(x), target).item()
+    for _ in range(spec["steps"]):
+        opt.zero_grad()
+        loss = fo.mse_loss(model(x), target)
+        loss.backward()
+        opt.step()
+    final = fo.mse_loss(model(x), target).item()
+    assert final < initial * spec["final_ratio_below"]
+    assert all(p.grad is not None for _, p in model.named_parameters())
+
+
+def test_conv_finite_differences():
+    """Central differences check the conv backward (as the reference's robustness
+    test does for conv and LayerNorm, test_training_robustness.py:17-59).  The
+    convolution is linear in each argument, so a large step is exact up to f32
+    rounding."""
+    rng = np.random.default_rng(0)
+    x = fo.T(rng.standard_normal((2, 3, 6, 5)).astype(np.float32), requires_grad=True)
+    w = fo.T(rng.standard_normal((4, 3, 3, 3)).astype(np.float32), requires_grad=True)
+    b = fo.T(rng.standard_normal(4).astype(np.float32), requires_grad=True)
+    probe = rng.standard_normal((2, 4, 3, 2)).astype(np.float32)
+
+    def f():
+        y = fo.conv2d(x, w, b, (2, 2), (1, 1, 1, 0), (1, 1))
+        return float((y.data.astype(np.float64) * probe).sum()), y
+
+    _, y = f()
+    y.backward(probe)
+    for tensor in (x, w, b):
+        flat = tensor.data.reshape(-1)
+        for i in rng.choice(flat.size, min(6, flat.size), replace=False):
+            old = flat[i]
+            flat[i] = old + np.float32(0.5)
+            up, _ = f()
+            flat[i] = old - np.float32(0.5)
+            down, _ = f()
+            flat[i] = old
+            assert math.isclose(tensor.grad.reshape(-1)[i], (up - down) / 1.0, rel_tol=1e-3,
+                                abs_tol=1e-3)
