@@ -1,0 +1,409 @@
+"""Training-step throughput of the B200 engine (samples/s, fwd+bwd+Adam).
+
+Default workload: the MLP classifier (784->1024 relu ->1024 relu ->10, fp32
+storage, global batch 4096 sharded across ranks, cross-entropy, Adam 1e-3).
+One step = zero_grad, forward, fused softmax-cross-entropy, backward (with the
+NCCL gradient all-reduce inside backward when N > 1) and one Adam step,
+captured once with ``tynx_b200.compile`` and replayed as a CUDA graph.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--math tf32|3xtf32|fp32] [--impl ours|reference]
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
+on the engine's stream with an L2 flush (a 512 MiB write, larger than the
+126 MB L2) between steps outside the events; the per-rank total is the sum of
+the K step times; barrier + synchronize on both sides; the job time is the max
+over ranks.  ``e2e`` repeats the measurement through the public API with the
+step's inputs copied from pinned host memory and the loss read back each step
+(host clock, max over ranks).  ``--impl reference`` times the CPU oracle (the
+numpy restatement of the reference's Flex training step) on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+class Clocks:
+    """Sample SM clocks and throttle reasons with nvidia-smi during a region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        query = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={query}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(int(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def _flush_l2(tx, buf):
+    # writing 512 MiB evicts the 126 MB L2
+    from tynx_b200 import _native as N
+
+    ctx = buf.ctx
+    ctx.check(N.lib.tx_memset(ctx.handle, buf.ptr, 0, buf.nbytes))
+
+
+def _cpu_step_fn(wl):
+    """The oracle's training step on the workload (for the CPU baseline)."""
+    from oracle import flex_oracle as fo
+    from tynx_b200.onnx import ir
+
+    model = fo.OracleModel(ir.load_training_graph(wl.onnx))
+    opt = fo.Adam(model.named_parameters(), lr=wl.lr)
+    key = "ids" if wl.name == "transformer" else ("obs" if wl.loss == "ppo" else "x")
+
+    def step(batch):
+        opt.zero_grad()
+        if wl.loss == "ppo":
+            out = model(batch["obs"])
+            n = batch["obs"].shape[0]
+            loss = fo.ppo_loss(out["logits"], out["value"], batch["actions"],
+                               np.zeros(n, np.float32), batch["advantages"], batch["returns"])
+        else:
+            loss = fo.cross_entropy(model(batch[key]), batch["y"])
+        loss.backward()
+        opt.step()
+        return loss.item()
+
+    return step
+
+
+def cpu_baseline(wl, budget_s: float = 15.0) -> dict:
+    """Time the oracle's step on the host cores (bounded sample)."""
+    step = _cpu_step_fn(wl)
+    b0 = wl.make_batch(0)
+    step(b0)  # cold step, excluded
+    times = []
+    start = time.perf_counter()
+    i = 1
+    while time.perf_counter() - start < budget_s and i < 50:
+        t0 = time.perf_counter()
+        step(wl.make_batch(i))
+        times.append(time.perf_counter() - t0)
+        i += 1
+    med = float(np.median(times))
+    cores = os.cpu_count() or 1
+    return {"value": wl.batch / med, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} full {wl.name} steps (batch {wl.batch}) of the numpy oracle "
+                      f"(multithreaded BLAS, {cores} host threads), median step {med * 1e3:.1f} ms"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return
+    from tynx_b200 import workloads
+
+    wl = workloads.WORKLOADS[args.workload]()
+    step = _cpu_step_fn(wl)
+    for i in range(args.warmup):
+        step(wl.make_batch(i))
+    times = []
+    for i in range(args.steps):
+        b = wl.make_batch(args.warmup + i)
+        t0 = time.perf_counter()
+        step(b)
+        times.append(time.perf_counter() - t0)
+    total = float(sum(times))
+    value = wl.batch * args.steps / total
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": "train samples/s (fwd+bwd+Adam)", "value": value,
+        "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "global_batch": wl.batch},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of the numpy restatement of the Flex "
+                                   f"training step at batch {wl.batch} ({cores} host threads)"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--workload", default="mlp_classifier")
+    parser.add_argument("--math", default="tf32", choices=["tf32", "3xtf32", "fp32"])
+    parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-budget", type=float, default=15.0)
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world, rank, local = _dist_env()
+    os.environ.setdefault("TYNX_CUDA_MATH", args.math)
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    import tynx_b200 as tx
+    from tynx_b200 import _core, workloads
+    from tynx_b200 import _native as N
+    from tynx_b200.distributed import init_data_parallel, shard
+
+    tx.set_math_mode(args.math)
+    wl = workloads.WORKLOADS[args.workload]()
+    if wl.loss != "cross_entropy":
+        raise SystemExit("bench.py times the cross-entropy workloads")
+    per_rank = wl.batch // world
+    rows = shard(wl.batch, world, rank)
+    ctx = _core.context()
+    model = tx.load(wl.onnx, trainable="auto")
+    opt = tx.optim.Adam(model.named_parameters(), lr=wl.lr)
+    if world > 1:
+        init_data_parallel(world, rank)
+        model.enable_data_parallel(bucket_mb=8)
+    key = "ids" if args.workload == "transformer" else "x"
+    xdtype = "int64" if key == "ids" else "float32"
+
+    @tx.compile(fullgraph=True)
+    def train_step(x, y):
+        opt.zero_grad()
+        loss = tx.nn.functional.cross_entropy(model(x), y)
+        loss.backward()
+        opt.step()
+        return loss
+
+    # device-resident batches (one per step) for the kernel-time measurement
+    n_batches = args.warmup + args.steps
+    host = [wl.make_batch(i) for i in range(n_batches)]
+    dev = [(tx.Tensor(b[key][rows], dtype=xdtype), tx.Tensor(b["y"][rows])) for b in host]
+    flush = tx.zeros(128 << 20)  # 512 MiB
+
+    stream = ctypes_stream(ctx)
+    ext = torch.cuda.ExternalStream(stream, device=torch.device("cuda", ctx.index))
+
+    def barrier():
+        tx.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (first call captures, later calls replay)
+    for i in range(args.warmup):
+        train_step(*dev[i])
+    entry = train_step.entry_for(*dev[0])
+    launches_per_step = entry.kernel_count if entry is not None else None
+    barrier()
+
+    # ---- device-timed steps --------------------------------------------------------
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with Clocks(ctx.index) as clocks:
+        barrier()
+        for i in range(args.steps):
+            # stage this step's batch into the graph's input buffers, then evict L2
+            for dst, src in zip(entry.static_inputs, dev[args.warmup + i]):
+                ctx.check(N.lib.tx_d2d(ctx.handle, dst.ptr, src.ptr, src.nbytes))
+            _flush_l2(tx, flush)
+            starts[i].record(ext)
+            ctx.check(N.lib.tx_exec_launch(entry.exec), "graph replay")
+            ends[i].record(ext)
+            entry.apply_post_state()
+        barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = float(sum(step_ms))
+    if world > 1:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = wl.batch * args.steps / (total_ms / 1e3)
+
+    # ---- roofline of the dominant kernel (the largest forward GEMM) -----------------
+    roofline = gemm_roofline(tx, ctx, ext, wl, per_rank, args.math)
+
+    # ---- end to end through the public API with host buffers -------------------------
+    pin_x = [_core.pinned(b[key][rows]) for b in host[args.warmup:]]
+    pin_y = [_core.pinned(b["y"][rows]) for b in host[args.warmup:]]
+    barrier()
+    t0 = time.perf_counter()
+    losses = []
+    for i in range(args.steps):
+        x = tx.Tensor(pin_x[i], dtype=xdtype)
+        y = tx.Tensor(pin_y[i])
+        losses.append(train_step(x, y).item())
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    h2d = pin_x[0].nbytes + pin_y[0].nbytes
+    e2e = {"value": wl.batch * args.steps / e2e_s, "unit": "samples/s",
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4}
+
+    if rank == 0:
+        line = {
+            "metric": "train samples/s (fwd+bwd+Adam)",
+            "value": value,
+            "unit": "samples/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "tf32" if args.math == "tf32" else args.math,
+            "data": "synthetic (seeded numpy; BASELINE names no dataset)",
+            "config": {"workload": wl.name, "global_batch": wl.batch, "per_gpu_batch": per_rank,
+                       "parallelism": f"dp{world}", "math": args.math,
+                       "l2": "flushed between steps (512 MiB write)",
+                       "flop_per_step": wl.flop_per_step},
+            "achieved_tflops": wl.flop_per_step / (ms_per_step / 1e3) / 1e12,
+            "roofline": roofline,
+            "e2e": e2e,
+            "gpu_launches": (launches_per_step * args.steps) if launches_per_step else None,
+            "clocks": clocks.summary(),
+            "final_loss": losses[-1],
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget)
+        elif world == 1:
+            line["cpu_baseline"] = None
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def ctypes_stream(ctx) -> int:
+    import ctypes as C
+
+    from tynx_b200 import _native as N
+
+    out = C.c_void_p()
+    ctx.check(N.lib.tx_stream(ctx.handle, C.byref(out)))
+    return out.value
+
+
+def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
+    """Time the step's largest forward GEMM alone (CUDA events on the engine stream)."""
+    import torch
+
+    from tynx_b200 import _core
+
+    peaks, source = _peaks()
+    # largest GEMM of the MLP classifier / policy: hidden x hidden forward
+    if wl.name in ("mlp_classifier", "mlp_policy"):
+        hidden = 1024 if wl.name == "mlp_classifier" else 256
+        M, N_, K = per_rank, hidden, hidden
+    elif wl.name == "transformer":
+        M, N_, K = per_rank * 128, 1024, 256
+    else:
+        M, N_, K = per_rank * 256, 64, 288
+    rng = np.random.default_rng(0)
+    A = tx.Tensor(rng.standard_normal((M, K)).astype(np.float32))
+    B = tx.Tensor(rng.standard_normal((N_, K)).astype(np.float32))
+    Cm = tx.zeros(M, N_)
+    bias = tx.zeros(N_)
+
+    def launch():
+        _core.gemm(ctx, M, N_, K, A.ptr, K, False, B.ptr, K, True, Cm.ptr, N_, bias=bias.ptr,
+                   act="relu")
+
+    for _ in range(5):
+        launch()
+    tx.synchronize()
+    reps = 50
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(ext)
+    for _ in range(reps):
+        launch()
+    e.record(ext)
+    e.synchronize()
+    ms = s.elapsed_time(e) / reps
+    flops = 2.0 * M * N_ * K
+    achieved = flops / (ms / 1e3) / 1e12
+    # dense TF32 peak: the measured dense bf16 rate halved (B200: tf32 dense = 1/2 bf16 dense)
+    if math == "fp32":
+        peak = 80.0
+        note = "fp32 SIMT nominal (no tensor cores)"
+    else:
+        peak = peaks["bf16_tflops"] / 2.0
+        note = f"dense TF32 = 1/2 of {source} bf16 burst ({peaks['bf16_tflops']} TF/s)"
+    return {"bound": "tensor", "kernel": f"gemm {M}x{N_}x{K} +bias+relu ({math})",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None, "duration_us": ms * 1e3, "peak_source": note}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,323 @@
+/*
+ * tynx_cuda.h -- C ABI of libtynx_cuda.so, the B200 (sm_100a) training-step
+ * engine for imported ONNX graphs.
+ *
+ * The reference (blaind/tynx) runs every tensor operation through Burn
+ * (burn-flex on CPU, burn-autodiff for backward rules, CubeCL/wgpu on GPUs);
+ * there is no C ABI upstream.  This header is the drop-in boundary a
+ * `tynx-cuda-sys` crate binds with `extern "C"`.  Each
+ * group names the reference function or type it replaces (path:line inside
+ * the reference project).
+ *
+ * Conventions
+ *   - Every function returns int: 0 (TX_OK) on success, a TX_ERR_* code
+ *     otherwise.  The message of the first error is latched per context and
+ *     read with tx_last_error(), the analogue of LAST_DEVICE_ERROR /
+ *     take_device_error (crates/tynx/src/device.rs:55-81).
+ *   - Pointers named d_* are device pointers; h_* are host pointers.
+ *   - Tensors are dense row-major.  float tensors are IEEE fp32; index
+ *     tensors are int64 (ONNX/Flex semantics).
+ *   - All work is enqueued on the context's compute stream in call order.
+ *     Functions that return host data (tx_d2h, tx_sync) synchronise.
+ *   - A context is confined to the host thread that created it, matching
+ *     Tynx's thread confinement (crates/tynx-python/src/tensor.rs:54-92).
+ */
+#ifndef TYNX_CUDA_H
+#define TYNX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TYNX_CUDA_ABI_VERSION 1
+
+/* ---- status codes (TynxError, crates/tynx/src/error.rs:1-122) ----------- */
+enum {
+  TX_OK = 0,
+  TX_ERR_INVALID = 1,      /* bad argument (TynxError::TypeMismatch / InvalidModel) */
+  TX_ERR_SHAPE = 2,        /* shape mismatch (TynxError::Shape) */
+  TX_ERR_INDEX = 3,        /* index outside [-size, size) (normalize_indices, tensor.rs:2504) */
+  TX_ERR_OOM = 4,          /* device allocation failed */
+  TX_ERR_CUDA = 5,         /* CUDA runtime error (TynxError::AsynchronousDevice, error.rs:54-55) */
+  TX_ERR_TIMEOUT = 6,      /* bounded wait expired (TynxError::DeviceSynchronization, error.rs:58-59) */
+  TX_ERR_UNSUPPORTED = 7,  /* operator or attribute not implemented on this device */
+  TX_ERR_DEVICE = 8,       /* a kernel raised the context's device error flag */
+  TX_ERR_NCCL = 9,         /* collective failure */
+  TX_ERR_CAPTURE = 10      /* operation not allowed while capturing a CUDA graph */
+};
+
+/* ---- math modes for fp32 contractions (TYNX_CUDA_MATH) ------------------ */
+enum {
+  TX_MATH_TF32 = 0,   /* tcgen05 kind::tf32, fp32 accumulate (rel 1e-3 class) */
+  TX_MATH_3XTF32 = 1, /* split-operand 3xTF32 on tcgen05 (fp32 class, 1e-5) */
+  TX_MATH_FP32 = 2    /* SIMT FFMA, exact fp32 products */
+};
+
+typedef struct tx_ctx tx_ctx;
+typedef struct tx_graph tx_graph;
+typedef struct tx_record tx_record;
+typedef struct tx_exec tx_exec;
+typedef struct tx_optim tx_optim;
+
+/* =========================================================================
+ * Context, placement, synchronisation
+ * replaces: Device selection and errors -- default_device (crates/tynx/src/device.rs:214-227),
+ *           synchronize (device.rs:84-90), take_device_error (device.rs:79-81),
+ *           PyDevice::py_new (crates/tynx-python/src/device.rs:50-61)
+ * ========================================================================= */
+int tx_abi_version(void);
+int tx_device_count(int *out);
+int tx_ctx_create(int device, int math_mode, tx_ctx **out);
+int tx_ctx_destroy(tx_ctx *ctx);
+int tx_ctx_set_math(tx_ctx *ctx, int math_mode);
+int tx_ctx_get_math(tx_ctx *ctx, int *out);
+/* Copy the latched first error message (NUL-terminated) and clear it.
+ * Returns the latched code (0 if none). */
+int tx_last_error(tx_ctx *ctx, char *buf, size_t n);
+/* Wait for all work on the context's streams; gives up after timeout_ms
+ * (0 = no limit) with TX_ERR_TIMEOUT.  Surfaces device-side error flags. */
+int tx_sync(tx_ctx *ctx, uint64_t timeout_ms);
+/* The compute stream as a cudaStream_t, for interop with other libraries. */
+int tx_stream(tx_ctx *ctx, void **out);
+
+/* =========================================================================
+ * Device memory (replaces Burn tensor storage behind DynTensor,
+ * crates/tynx/src/tensor.rs:156-185).  Stream-ordered caching allocator.
+ * ========================================================================= */
+int tx_alloc(tx_ctx *ctx, size_t bytes, void **d_out);
+int tx_free(tx_ctx *ctx, void *d_ptr);
+int tx_h2d(tx_ctx *ctx, void *d_dst, const void *h_src, size_t bytes);
+int tx_d2h(tx_ctx *ctx, void *h_dst, const void *d_src, size_t bytes);
+int tx_d2d(tx_ctx *ctx, void *d_dst, const void *d_src, size_t bytes);
+int tx_memset(tx_ctx *ctx, void *d_ptr, int value, size_t bytes);
+int tx_fill_f32(tx_ctx *ctx, float *d_ptr, int64_t n, float value);
+int tx_host_alloc(size_t bytes, void **h_out); /* pinned host memory */
+int tx_host_free(void *h_ptr);
+/* Bytes currently held by the allocator (in use, cached). */
+int tx_mem_stats(tx_ctx *ctx, uint64_t *in_use, uint64_t *cached);
+
+/* =========================================================================
+ * Whole-step capture (replaces Graph::run_values replay,
+ * crates/tynx-capture/src/lib.rs:747-882, and CompiledFunction,
+ * crates/tynx-python/python/tynx/compiler.py:131-205).
+ * Between begin and end, all work issued on the context is recorded into a
+ * CUDA graph; allocations come from an arena owned by the resulting exec.
+ * ========================================================================= */
+int tx_capture_begin(tx_ctx *ctx);
+int tx_capture_end(tx_ctx *ctx, tx_exec **out);
+int tx_capture_abort(tx_ctx *ctx);
+int tx_capture_active(tx_ctx *ctx, int *out);
+int tx_exec_launch(tx_exec *exec);
+int tx_exec_destroy(tx_exec *exec);
+/* Number of kernel nodes (and all nodes) recorded in a captured graph. */
+int tx_exec_node_count(tx_exec *exec, int64_t *kernels, int64_t *total);
+
+/* =========================================================================
+ * Kernels behind the DynTensor method surface (crates/tynx/src/tensor.rs).
+ * These are the eager-op entry points used by Tensor and by the loss code.
+ * ========================================================================= */
+
+/* Dense fp32 contraction C = alpha * op(A) @ op(B) (+ beta * C) (+ bias) with
+ * an optional fused activation epilogue.
+ * replaces: DynTensor::matmul (tensor.rs:1715-1786), execute_gemm + add_bias
+ * (crates/tynx-train/src/imported_model/executor.rs:499-524, 606-613) and
+ * Burn's matmul backward (dA = dY B^T, dB = A^T dY). */
+enum { TX_ACT_NONE = 0, TX_ACT_RELU = 1, TX_ACT_TANH = 2, TX_ACT_GELU = 3 };
+typedef struct tx_gemm_desc {
+  int64_t M, N, K;
+  const float *A; int64_t lda; int32_t trans_a; /* A: MxK row-major, or KxM when trans_a */
+  const float *B; int64_t ldb; int32_t trans_b; /* B: KxN row-major, or NxK when trans_b */
+  float *C; int64_t ldc;                       /* C: MxN row-major */
+  float alpha, beta;                           /* beta != 0 reads C before writing */
+  const float *bias; float bias_scale;         /* optional per-column bias, length N */
+  int32_t act;                                 /* TX_ACT_* applied after bias */
+  float *preact; int64_t ld_preact;            /* optional: store value before act */
+  /* optional dgrad fusion: multiply the result by act'(src) where src is the
+   * saved forward output (relu, tanh) or pre-activation (gelu) */
+  const float *dact_src; int64_t ld_dact; int32_t dact;
+  int64_t batch; int64_t stride_a, stride_b, stride_c; /* strided batch (batch<=1: single) */
+} tx_gemm_desc;
+int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc);
+
+/* Elementwise.  replaces: DynTensor activations (tensor.rs:2002-2240) and
+ * broadcast arithmetic (tensor.rs:1637-1700). */
+enum {
+  TX_UN_NEG = 0, TX_UN_EXP = 1, TX_UN_LOG = 2, TX_UN_RELU = 3, TX_UN_TANH = 4,
+  TX_UN_GELU = 5, TX_UN_SIGMOID = 6, TX_UN_CLAMP = 7, TX_UN_SQRT = 8, TX_UN_ABS = 9,
+  TX_UN_SCALE = 10, /* y = a*x + b */
+  TX_UN_POW = 11    /* y = x^a */
+};
+int tx_unary(tx_ctx *ctx, int op, const float *d_x, float *d_y, int64_t n, float a, float b);
+/* dx (+)= dy * op'(x or y).  `src` is y for EXP/TANH/SIGMOID/RELU, x otherwise. */
+int tx_unary_bwd(tx_ctx *ctx, int op, const float *d_src, const float *d_dy, float *d_dx,
+                 int64_t n, float a, float b, int accumulate);
+
+enum {
+  TX_BIN_ADD = 0, TX_BIN_SUB = 1, TX_BIN_MUL = 2, TX_BIN_DIV = 3, TX_BIN_MIN = 4,
+  TX_BIN_MAX = 5, TX_BIN_LE = 6, /* 1.0f where a<=b else 0 */
+  TX_BIN_GE = 7, TX_BIN_POW = 8
+};
+#define TX_MAX_DIMS 8
+/* out[i] = a[i] op b[i] with numpy broadcasting expressed as element strides
+ * (0 on broadcast axes) over the output shape. */
+int tx_binary(tx_ctx *ctx, int op, const float *d_a, const int64_t *a_strides,
+              const float *d_b, const int64_t *b_strides, float *d_out,
+              const int64_t *out_shape, int ndim);
+/* Sum (mean when `mean`) of x over every axis where out_shape[i]==1 and
+ * in_shape[i]>1 (out has the same rank; broadcast-gradient reduction). */
+int tx_reduce_to(tx_ctx *ctx, const float *d_x, const int64_t *in_shape, float *d_out,
+                 const int64_t *out_shape, int ndim, int mean, int accumulate);
+/* Copy with arbitrary element strides (transpose / expand materialisation). */
+int tx_strided_copy(tx_ctx *ctx, const void *d_src, const int64_t *src_strides, void *d_dst,
+                    const int64_t *shape, int ndim, int elem_bytes);
+
+/* Softmax / log-softmax over the last axis of a [rows, cols] view.
+ * replaces: softmax / log_softmax (crates/tynx/src/interpreter/softmax.rs:9-17,
+ * tensor.rs:2234-2242) and their Burn backward rules. */
+int tx_softmax_fwd(tx_ctx *ctx, const float *d_x, float *d_y, int64_t rows, int64_t cols, int log);
+int tx_softmax_bwd(tx_ctx *ctx, const float *d_y, const float *d_dy, float *d_dx,
+                   int64_t rows, int64_t cols, int log, int accumulate);
+
+/* Fused softmax cross-entropy: loss = -mean_r log_softmax(z)[r, y_r] and
+ * (when d_dlogits is non-null) dlogits = scale * (softmax(z) - onehot(y)) / rows,
+ * where scale is read from the device scalar d_scale (null = 1).
+ * Labels outside [0, cols) raise the device error flag (TX_ERR_INDEX).
+ * replaces: nn.functional.cross_entropy (crates/tynx-python/python/tynx/nn/functional.py:133-145)
+ * = log_softmax -> gather -> squeeze -> neg -> mean and its taped backward. */
+int tx_softmax_xent_fwd(tx_ctx *ctx, const float *d_logits, const int64_t *d_labels,
+                        int64_t rows, int64_t cols, float *d_loss);
+int tx_softmax_xent_bwd(tx_ctx *ctx, const float *d_logits, const int64_t *d_labels,
+                        int64_t rows, int64_t cols, const float *d_scale, float *d_dlogits,
+                        int accumulate);
+
+/* LayerNormalization over the trailing `cols` elements of each row.
+ * replaces: layer_normalization_values (crates/tynx/src/interpreter/normalization.rs:135-190). */
+int tx_layernorm_fwd(tx_ctx *ctx, const float *d_x, const float *d_gamma, const float *d_beta,
+                     float *d_y, float *d_mean, float *d_rstd, int64_t rows, int64_t cols,
+                     float eps);
+int tx_layernorm_bwd(tx_ctx *ctx, const float *d_x, const float *d_gamma, const float *d_mean,
+                     const float *d_rstd, const float *d_dy, float *d_dx, float *d_dgamma,
+                     float *d_dbeta, int64_t rows, int64_t cols, int accumulate_dx,
+                     int accumulate_params);
+
+/* Row gather out[i, :] = table[idx[i], :] (negative indices wrap once) and its
+ * backward scatter-add.  replaces: gather_values (crates/tynx/src/interpreter/gather.rs:18-58),
+ * DynTensor::select (tensor.rs:1450) and Burn select_assign. */
+int tx_gather_rows(tx_ctx *ctx, const float *d_table, int64_t rows, int64_t width,
+                   const int64_t *d_idx, int64_t n_idx, float *d_out);
+int tx_scatter_add_rows(tx_ctx *ctx, float *d_table, int64_t rows, int64_t width,
+                        const int64_t *d_idx, int64_t n_idx, const float *d_src);
+/* out[r] = x[r, idx[r]] for a [rows, cols] x (Tensor.gather on the last axis,
+ * crates/tynx-python/src/tensor.rs:1769) and its backward. */
+int tx_take_last(tx_ctx *ctx, const float *d_x, const int64_t *d_idx, float *d_out,
+                 int64_t rows, int64_t cols);
+int tx_take_last_bwd(tx_ctx *ctx, const int64_t *d_idx, const float *d_dout, float *d_dx,
+                     int64_t rows, int64_t cols, int accumulate);
+
+/* Column sum db[n] (+)= sum_m dy[m, n] (bias gradient, Gemm `dC = sum_rows dY * beta`). */
+int tx_bias_grad(tx_ctx *ctx, const float *d_dy, float *d_db, int64_t M, int64_t N, float scale,
+                 int accumulate);
+
+/* =========================================================================
+ * Optimizers (replaces AdamEngine::step_parameters,
+ * crates/tynx-train/src/optimizer/adam.rs:431-527; Sgd::step_parameters,
+ * crates/tynx-train/src/optimizer.rs:310-356).  One multi-tensor launch per
+ * step; per-tensor step counters live on the device so a captured step
+ * replays with correct bias corrections.
+ * ========================================================================= */
+typedef struct tx_optim_cfg {
+  int32_t kind;        /* 0 = Adam (coupled L2), 1 = AdamW (decoupled), 2 = SGD */
+  double lr, beta1, beta2, eps, weight_decay;
+  int32_t amsgrad;
+  double momentum, dampening; int32_t nesterov; /* SGD */
+} tx_optim_cfg;
+int tx_optim_create(tx_ctx *ctx, const tx_optim_cfg *cfg, int n_tensors, float *const *d_values,
+                    float *const *d_grads, const int64_t *numel, tx_optim **out);
+int tx_optim_set_lr(tx_optim *opt, double lr);
+int tx_optim_set_hparams(tx_optim *opt, const tx_optim_cfg *cfg);
+/* One step over the tensors whose active[i] != 0 (tensors without a gradient
+ * are skipped, adam.rs:439-441). */
+int tx_optim_step(tx_optim *opt, const uint8_t *active);
+/* Read or write per-tensor state: which = 0 m, 1 v, 2 vmax, 3 momentum. */
+int tx_optim_state_ptr(tx_optim *opt, int tensor, int which, float **d_out);
+int tx_optim_get_steps(tx_optim *opt, int64_t *h_steps);
+int tx_optim_set_steps(tx_optim *opt, const int64_t *h_steps);
+int tx_optim_destroy(tx_optim *opt);
+
+/* =========================================================================
+ * Imported-graph engine (replaces ImportedModel::run_with_tracking /
+ * executor::run, crates/tynx-train/src/imported_model.rs:109-113,
+ * imported_model/executor.rs:107-161, the Burn autodiff tape walked by
+ * backward_parameters, crates/tynx-train/src/autograd.rs:56-95, and
+ * ParameterSlot value/grad storage, crates/tynx-train/src/parameter.rs:88-333).
+ * ========================================================================= */
+enum {
+  TX_OP_GEMM = 1, TX_OP_MATMUL, TX_OP_CONV, TX_OP_GATHER, TX_OP_LAYERNORM, TX_OP_ADD,
+  TX_OP_SUB, TX_OP_MUL, TX_OP_DIV, TX_OP_RELU, TX_OP_TANH, TX_OP_GELU, TX_OP_SIGMOID,
+  TX_OP_EXP, TX_OP_LOG, TX_OP_NEG, TX_OP_SOFTMAX, TX_OP_LOGSOFTMAX, TX_OP_REDUCEMEAN,
+  TX_OP_REDUCESUM, TX_OP_GAP, TX_OP_RESHAPE, TX_OP_TRANSPOSE, TX_OP_FLATTEN,
+  TX_OP_SQUEEZE, TX_OP_UNSQUEEZE, TX_OP_IDENTITY, TX_OP_CLIP, TX_OP_PRELU
+};
+enum { TX_VAL_INPUT = 0, TX_VAL_PARAM = 1, TX_VAL_CONST = 2, TX_VAL_ACT = 3 };
+enum { TX_DT_F32 = 0, TX_DT_I64 = 1 };
+typedef struct tx_value_desc {
+  int32_t kind;       /* TX_VAL_* */
+  int32_t dtype;      /* TX_DT_* */
+  int32_t ndim;       /* for PARAM/CONST: static rank; INPUT: -1 if unknown */
+  int64_t shape[TX_MAX_DIMS];
+  const void *h_data; /* PARAM/CONST initial contents (host), else NULL */
+} tx_value_desc;
+typedef struct tx_node_desc {
+  int32_t op;                /* TX_OP_* */
+  int32_t n_in, n_out;
+  int32_t in[4], out[3];     /* value ids; -1 for an absent optional input */
+  int64_t iattr[8];          /* op-specific integers */
+  double fattr[4];           /* op-specific reals */
+  int32_t n_ints; int64_t ints[16]; /* list attributes (perm, pads, strides, axes, shape) */
+} tx_node_desc;
+int tx_graph_create(tx_ctx *ctx, const tx_value_desc *values, int n_values,
+                    const tx_node_desc *nodes, int n_nodes, const int32_t *outputs,
+                    int n_outputs, tx_graph **out);
+int tx_graph_destroy(tx_graph *g);
+/* Parameter slots in value-id order of TX_VAL_PARAM entries. */
+int tx_graph_param_count(tx_graph *g, int *out);
+int tx_graph_param(tx_graph *g, int index, int32_t *value_id, float **d_value, float **d_grad,
+                   int64_t *numel);
+int tx_graph_grad_defined(tx_graph *g, int index, int *out);
+int tx_graph_set_grad_defined(tx_graph *g, int index, int defined);
+/* Shape inference for given input shapes; fills output ranks and shapes. */
+int tx_graph_infer(tx_graph *g, const int64_t *in_shapes, const int32_t *in_ndims,
+                   int64_t *out_shapes, int32_t *out_ndims);
+/* Forward.  Writes outputs into caller-provided buffers.  With tracking, a
+ * record holding the saved activations is returned for backward. */
+int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const int64_t *in_shapes,
+                     const int32_t *in_ndims, void *const *d_outputs, int tracking,
+                     tx_record **rec_out);
+/* Backward through one record: d_outputs[i] may be NULL (zero gradient).
+ * Parameter gradients accumulate into the slots (grad += new, or = new when
+ * the slot has no gradient yet, parameter.rs:300-333).  d_inputs[i] non-NULL
+ * requests the input gradient (written, not accumulated). */
+int tx_graph_backward(tx_graph *g, tx_record *rec, const float *const *d_outputs,
+                      float *const *d_inputs);
+int tx_record_free(tx_record *rec);
+
+/* =========================================================================
+ * Data parallelism over NCCL (no counterpart in the reference, which is
+ * single-device; §e of the engine design).  One process per GPU.
+ * ========================================================================= */
+int tx_dp_unique_id(uint8_t *out128);
+int tx_dp_init(tx_ctx *ctx, int world, int rank, const uint8_t *id128, uint64_t timeout_ms);
+int tx_dp_destroy(tx_ctx *ctx);
+/* Average every parameter gradient of g across ranks inside backward, in
+ * buckets of about bucket_bytes on the communication stream, overlapped with
+ * the remaining backward.  0 disables. */
+int tx_graph_set_dp(tx_graph *g, int enabled, int64_t bucket_bytes);
+int tx_dp_allreduce(tx_ctx *ctx, float *d_buf, int64_t n, int average);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TYNX_CUDA_H */

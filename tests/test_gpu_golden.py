@@ -1,0 +1,251 @@
+"""The reference's own known answers, reproduced through the CUDA engine's public API.
+
+Each case mirrors an assertion in the reference's tests (file:line recorded in
+``tests/golden/expected.json``) and runs on ``Device("cuda")``.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tx():
+    import tynx_b200 as tx
+
+    tx.set_math_mode("fp32")  # the goldens are exact small-integer fp32 cases
+    yield tx
+    tx.set_math_mode("tf32")
+
+
+def _load(tx, fixtures, name, **kw):
+    return tx.load(fixtures[name], trainable="auto", simplify=False, **kw)
+
+
+def test_gemm_forward_backward(tx, fixtures, expected):
+    case = expected["gemm_forward_backward"]
+    model = _load(tx, fixtures, case["model"],
+                  initializer_names={"weight": "head.weight", "bias": "head.bias"})
+    x = tx.Tensor(case["input"], requires_grad=True)
+    y = model(x)
+    y.sum().backward()
+    assert y.flatten().tolist() == pytest.approx(case["output"])
+    assert x.grad.flatten().tolist() == pytest.approx(case["input_grad"])
+    params = dict(model.named_parameters())
+    assert sorted(params) == ["head.bias", "head.weight"]
+    assert params["head.weight"].grad.flatten().tolist() == pytest.approx(case["weight_grad"])
+    assert params["head.bias"].grad.tolist() == pytest.approx(case["bias_grad"])
+
+
+def test_gemm_sgd_next_forward(tx, fixtures, expected):
+    case = expected["gemm_sgd_next_forward"]
+    model = _load(tx, fixtures, case["model"])
+    opt = tx.optim.SGD(model.named_parameters(), lr=case["lr"])
+    x = tx.Tensor(case["input"])
+    model(x).sum().backward()
+    opt.step()
+    assert model(x).flatten().tolist() == pytest.approx(case["next_output"])
+
+
+def test_clip_gemm(tx, fixtures, expected):
+    case = expected["clip_gemm"]
+    model = _load(tx, fixtures, case["model"])
+    y = model(tx.Tensor(case["input"]))
+    assert y.flatten().tolist() == pytest.approx(case["output"])
+    y.sum().backward()
+    p = dict(model.named_parameters())
+    assert p["weight"].grad.flatten().tolist() == pytest.approx(case["weight_grad"])
+    assert p["bias"].grad.tolist() == pytest.approx(case["bias_grad"])
+
+
+def test_gather_accumulates_repeated_rows(tx, fixtures, expected):
+    case = expected["gather_accumulation"]
+    model = _load(tx, fixtures, case["model"])
+    idx = tx.Tensor(case["indices"], dtype="int64")
+    y = model(idx)
+    assert y.tolist() == case["output"]
+    y.sum().backward()
+    w = dict(model.named_parameters())["embedding.weight"]
+    assert w.grad.tolist() == case["weight_grad"]
+    tx.optim.SGD(model.named_parameters(), lr=case["lr"]).step()
+    assert model(idx).flatten().tolist() == pytest.approx(case["next_output"])
+
+
+def test_gather_out_of_range_raises_index_error(tx, fixtures):
+    model = _load(tx, fixtures, "_GATHER_MODEL")
+    with pytest.raises(IndexError):
+        model(tx.Tensor([0, 3], dtype="int64")).tolist()
+
+
+def test_layer_norm(tx, fixtures, expected):
+    case = expected["layer_norm"]
+    model = _load(tx, fixtures, case["model"])
+    x = tx.Tensor(case["input"])
+    y = model(x)
+    assert y.flatten().tolist() == pytest.approx(case["output"], abs=case["abs"])
+    y.sum().backward()
+    p = dict(model.named_parameters())
+    assert p["norm.weight"].grad.flatten().tolist() == pytest.approx(case["weight_grad"],
+                                                                       abs=case["abs"])
+    assert p["norm.bias"].grad.tolist() == pytest.approx(case["bias_grad"], abs=case["abs"])
+    tx.optim.SGD(model.named_parameters(), lr=case["lr"]).step()
+    assert model(x).flatten().tolist() == pytest.approx(case["next_output"], abs=case["abs"])
+
+
+def test_batched_matmul(tx, fixtures, expected):
+    case = expected["batched_matmul"]
+    model = _load(tx, fixtures, case["model"])
+    y = model(tx.Tensor(case["input"]))
+    assert y.shape == (2, 2, 2)
+    assert y.flatten().tolist() == pytest.approx(case["output"])
+    y.sum().backward()
+    w = dict(model.named_parameters())["projection.weight"]
+    assert w.grad.flatten().tolist() == pytest.approx(case["weight_grad"])
+
+
+def test_adam_goldens(tx, fixtures, expected):
+    model = _load(tx, fixtures, "_GEMM_MODEL")
+    w = dict(model.named_parameters())["weight"]
+    opt = tx.optim.Adam([w], lr=0.1)
+    for want in expected["adam_constant_gradient"]["trajectory"]:
+        w.grad = tx.Tensor([[2.0]])
+        opt.step()
+        assert w.item() == pytest.approx(want, abs=1e-6)
+    case = expected["adam_vs_adamw_decay"]
+    for cls, want in ((tx.optim.Adam, case["adam"]), (tx.optim.AdamW, case["adamw"])):
+        m = _load(tx, fixtures, "_GEMM_MODEL")
+        p = dict(m.named_parameters())["weight"]
+        p.grad = tx.Tensor([[1.0]])
+        cls([p], lr=0.1, betas=(0.0, 0.0), eps=0.0, weight_decay=0.5).step()
+        assert p.item() == pytest.approx(want, abs=1e-6)
+    case = expected["amsgrad"]
+    m = _load(tx, fixtures, "_GEMM_MODEL")
+    p = dict(m.named_parameters())["weight"]
+    opt = tx.optim.Adam([p], lr=0.1, betas=(0.0, 0.0), eps=0.0, amsgrad=True)
+    for g in case["grads"]:
+        p.grad = tx.Tensor([[g]])
+        opt.step()
+    assert p.item() == pytest.approx(case["final"], abs=1e-6)
+
+
+def test_softmax_gelu_mse_goldens(tx, expected):
+    case = expected["softmax_axis0"]
+    y = tx.Tensor(case["input"]).softmax(case["axis"])
+    assert np.allclose(y.numpy(), case["output"], atol=case["abs"])
+    case = expected["log_softmax_stable"]
+    y = tx.Tensor(case["input"]).log_softmax(0)
+    assert np.allclose(y.numpy(), case["output"], atol=case["abs"])
+    case = expected["gelu_exact_erf"]
+    assert np.allclose(tx.Tensor(case["input"]).gelu().numpy(), case["output"], atol=case["abs"])
+    case = expected["mse"]
+    loss = tx.nn.functional.mse_loss(tx.Tensor(case["prediction"]), tx.Tensor(case["target"]))
+    assert loss.item() == pytest.approx(case["loss"], abs=1e-6)
+
+
+def _ppo_setup(tx, fixtures):
+    names = {"policy_weight": "policy.weight", "policy_bias": "policy.bias",
+             "value_weight": "value.weight", "value_bias": "value.bias"}
+    return _load(tx, fixtures, "_ACTOR_CRITIC_MODEL", initializer_names=names)
+
+
+def test_ppo_trains_with_user_composed_loss(tx, fixtures, expected):
+    case = expected["ppo_training"]
+    model = _ppo_setup(tx, fixtures)
+    ln, vn = model.outputs
+    obs = tx.Tensor(case["observations"])
+    actions = tx.Tensor(case["actions"], dtype="int64")
+    returns = tx.Tensor(case["returns"])
+    adv = tx.Tensor(case["advantages"])
+    old = tx.distributions.Categorical(logits=model(obs)[ln]).log_prob(actions).detach()
+    assert old.tolist() == pytest.approx([-math.log(2.0)] * 4)
+
+    def ppo_loss():
+        out = model(obs)
+        policy = tx.distributions.Categorical(logits=out[ln])
+        ratio = (policy.log_prob(actions) - old).exp()
+        policy_loss = -tx.minimum(ratio * adv, ratio.clamp(0.8, 1.2) * adv).mean()
+        value_loss = tx.nn.functional.mse_loss(out[vn].squeeze(1), returns)
+        return policy_loss + value_loss * 0.5 - policy.entropy().mean() * 0.01, value_loss
+
+    l0, v0 = ppo_loss()
+    l0, v0 = l0.item(), v0.item()
+    opt = tx.optim.Adam(model.named_parameters(), lr=case["lr"])
+    for _ in range(case["steps"]):
+        opt.zero_grad()
+        loss, _ = ppo_loss()
+        loss.backward()
+        opt.step()
+    l1, v1 = ppo_loss()
+    assert l1.item() < l0
+    assert v1.item() < v0 * case["final_value_loss_ratio_below"]
+    probs = tx.distributions.Categorical(logits=model(obs)[ln]).probs
+    chosen = probs.gather(1, actions.unsqueeze(1)).mean().item()
+    assert chosen > case["chosen_probability_above"]
+
+
+def test_captured_ppo_step_matches_eager(tx, fixtures):
+    """Capture == eager within 1e-6 over 40 steps (test_ppo.py:95-194)."""
+    eager, captured = _ppo_setup(tx, fixtures), _ppo_setup(tx, fixtures)
+    eager_opt = tx.optim.Adam(eager.named_parameters(), lr=0.03)
+    captured_opt = tx.optim.Adam(captured.named_parameters(), lr=0.03)
+    ln, vn = eager.outputs
+    calls = 0
+
+    def update(model, opt, obs, actions, returns, adv, old):
+        opt.zero_grad()
+        out = model(obs)
+        policy = tx.distributions.Categorical(logits=out[ln])
+        ratio = (policy.log_prob(actions) - old).exp()
+        policy_loss = -tx.minimum(ratio * adv, ratio.clamp(0.8, 1.2) * adv).mean()
+        value_loss = tx.nn.functional.mse_loss(out[vn].squeeze(1), returns)
+        loss = policy_loss + value_loss * 0.5 - policy.entropy().mean() * 0.01
+        loss.backward()
+        opt.step()
+        return loss
+
+    @tx.compile(fullgraph=True)
+    def captured_update(obs, actions, returns, adv, old):
+        nonlocal calls
+        calls += 1
+        return update(captured, captured_opt, obs, actions, returns, adv, old)
+
+    obs = tx.Tensor([[1.0, 0.0], [0.0, 1.0], [1.0, 1.0], [-1.0, 1.0]])
+    actions = tx.Tensor([0, 1, 0, 1], dtype="int64")
+    returns = tx.Tensor([1.0, -1.0, 0.0, -2.0])
+    adv = tx.Tensor([1.0, 1.0, 1.0, 1.0])
+    old = tx.Tensor([-math.log(2.0)] * 4)
+    for _ in range(40):
+        le = update(eager, eager_opt, obs, actions, returns, adv, old)
+        lc = captured_update(obs, actions, returns, adv, old)
+        assert lc.item() == pytest.approx(le.item(), abs=1e-6)
+    e, c = dict(eager.named_parameters()), dict(captured.named_parameters())
+    for name in e:
+        assert c[name].flatten().tolist() == pytest.approx(e[name].flatten().tolist(), abs=1e-6)
+    assert calls == 1
+    assert captured_update.compile_count == 1
+    assert captured_update.replay_count == 39
+
+
+@pytest.mark.parametrize("name", ["_CNN_MODEL", "_RECOMMENDER_MODEL", "_TRANSFORMER_MODEL"])
+def test_composed_models_converge(tx, fixtures, expected, name):
+    spec = expected["composed_training"]
+    case = spec["cases"][name]
+    model = tx.load(fixtures[name], trainable="auto", simplify=False)
+    report = model.require_trainable()
+    assert report.warnings == []
+    assert sorted(report.trainable_parameters) == case["trainable"]
+    x = tx.Tensor(case["input"], dtype=case.get("input_dtype", "float32"))
+    target = tx.Tensor(case["target"])
+    opt = tx.optim.Adam(model.named_parameters(), lr=spec["lr"])
+    initial = tx.nn.functional.mse_loss(model(x), target).item()
+    for _ in range(spec["steps"]):
+        opt.zero_grad()
+        loss = tx.nn.functional.mse_loss(model(x), target)
+        loss.backward()
+        opt.step()
+    final = tx.nn.functional.mse_loss(model(x), target).item()
+    assert final < initial * spec["final_ratio_below"]
+    assert all(p.grad is not None for _, p in model.named_parameters())

@@ -1,0 +1,240 @@
+"""Kernel-level parity on the GPU: each C-ABI kernel against the CPU oracle.
+
+Tolerances: exact-fp32 kernels (SIMT GEMM, elementwise, reductions) 1e-5
+relative; TF32 tensor-core GEMM 2e-3 relative to the output's scale (operands
+rounded to 10-bit mantissas, fp32 accumulation); the optimizer is bit-exact.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tx():
+    import tynx_b200 as tx
+
+    return tx
+
+
+def _rel(a, b):
+    scale = max(float(np.abs(b).max()), 1e-30)
+    return float(np.abs(a - b).max()) / scale
+
+
+def _gemm(tx, A, B, ta, tb, math, *, alpha=1.0, beta=0.0, C0=None, bias=None, act="none"):
+    from tynx_b200 import _core
+
+    ctx = _core.context()
+    ctx.math = math
+    try:
+        M = A.shape[1] if ta else A.shape[0]
+        K = A.shape[0] if ta else A.shape[1]
+        N = B.shape[0] if tb else B.shape[1]
+        a = tx.Tensor(A)
+        b = tx.Tensor(B)
+        c = tx.Tensor(C0 if C0 is not None else np.zeros((M, N), np.float32))
+        bb = tx.Tensor(bias) if bias is not None else None
+        _core.gemm(ctx, M, N, K, a.ptr, A.shape[1], ta, b.ptr, B.shape[1], tb, c.ptr, N,
+                   alpha=alpha, beta=beta, bias=bb.ptr if bb is not None else None, act=act)
+        return c.numpy()
+    finally:
+        ctx.math = "tf32"
+
+
+SHAPES = [
+    (128, 128, 64), (256, 384, 256), (300, 200, 100), (4096, 1024, 784), (512, 10, 1024),
+    (1024, 1024, 4096), (64, 256, 32), (1000, 64, 72),
+]
+
+
+@pytest.mark.parametrize("math,tol", [("fp32", 1e-5), ("tf32", 3e-3)])
+@pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_matches_fp64(tx, math, tol, ta, tb, M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    want = (A.T if ta else A).astype(np.float64) @ (B.T if tb else B).astype(np.float64)
+    got = _gemm(tx, A, B, ta, tb, math)
+    assert _rel(got, want) < tol
+
+
+@pytest.mark.parametrize("math,tol", [("fp32", 1e-5), ("tf32", 3e-3)])
+@pytest.mark.parametrize("act", ["none", "relu", "tanh", "gelu"])
+def test_gemm_epilogue(tx, math, tol, act):
+    from oracle import flex_oracle as fo
+
+    rng = np.random.default_rng(5)
+    M, N, K = 512, 384, 256
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = rng.standard_normal((N, K)).astype(np.float32) * 0.1
+    bias = rng.standard_normal(N).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    z = A.astype(np.float64) @ W.T.astype(np.float64) + bias + 0.5 * C0
+    fn = {"none": lambda v: v, "relu": lambda v: np.maximum(v, 0), "tanh": np.tanh,
+          "gelu": lambda v: fo.gelu(fo.T(v.astype(np.float32))).data}[act]
+    got = _gemm(tx, A, W, 0, 1, math, beta=0.5, C0=C0, bias=bias, act=act)
+    # errors are relative to the pre-activation scale: the contraction's rounding
+    # is what the tolerance bounds, and act is 1-Lipschitz for all four choices
+    assert float(np.abs(got - fn(z)).max()) < tol * float(np.abs(z).max())
+
+
+def test_softmax_xent_matches_oracle(tx):
+    from oracle import flex_oracle as fo
+    from tynx_b200 import nn
+
+    rng = np.random.default_rng(1)
+    for rows, cols in [(4096, 10), (256, 2), (37, 1000), (8192, 16)]:
+        z = (rng.standard_normal((rows, cols)) * 3).astype(np.float32)
+        y = rng.integers(0, cols, rows).astype(np.int64)
+        zt = tx.Tensor(z, requires_grad=True)
+        loss = nn.functional.cross_entropy(zt, tx.Tensor(y))
+        loss.backward()
+        ref_z = fo.T(z, requires_grad=True)
+        ref = fo.cross_entropy(ref_z, y)
+        ref.backward()
+        assert abs(loss.item() - ref.item()) <= 1e-5 * max(1.0, abs(ref.item()))
+        assert _rel(zt.grad.numpy(), ref_z.grad) < 1e-5
+
+
+def test_cross_entropy_rejects_out_of_range_labels(tx):
+    from tynx_b200 import nn
+
+    z = tx.Tensor(np.zeros((4, 3), np.float32))
+    y = tx.Tensor(np.array([0, 1, 3, 2], np.int64))
+    with pytest.raises(IndexError):
+        nn.functional.cross_entropy(z, y).item()
+    # the context stays usable after a latched device error
+    assert nn.functional.cross_entropy(z, tx.Tensor(np.array([0, 1, 2, 2], np.int64))).item() == \
+        pytest.approx(np.log(3.0), rel=1e-6)
+
+
+def test_layernorm_matches_oracle(tx):
+    from oracle import flex_oracle as fo
+    from tynx_b200 import _native as N
+    from tynx_b200._core import context
+
+    ctx = context()
+    rng = np.random.default_rng(2)
+    rows, cols = 3000, 256
+    x = rng.standard_normal((rows, cols)).astype(np.float32) * 2 + 1
+    g = rng.standard_normal(cols).astype(np.float32)
+    b = rng.standard_normal(cols).astype(np.float32)
+    dy = rng.standard_normal((rows, cols)).astype(np.float32)
+    X, G, B, DY = (tx.Tensor(v) for v in (x, g, b, dy))
+    Y = tx.zeros(rows, cols)
+    mean, rstd = tx.zeros(rows), tx.zeros(rows)
+    DX, DG, DB = tx.zeros(rows, cols), tx.zeros(cols), tx.zeros(cols)
+    ctx.check(N.lib.tx_layernorm_fwd(ctx.handle, X.ptr, G.ptr, B.ptr, Y.ptr, mean.ptr, rstd.ptr,
+                                     rows, cols, C.c_float(1e-5)))
+    ctx.check(N.lib.tx_layernorm_bwd(ctx.handle, X.ptr, G.ptr, mean.ptr, rstd.ptr, DY.ptr, DX.ptr,
+                                     DG.ptr, DB.ptr, rows, cols, 0, 0))
+    tx_ = fo.T(x, requires_grad=True)
+    tg = fo.T(g, requires_grad=True)
+    tb = fo.T(b, requires_grad=True)
+    (y,) = fo.layer_norm(tx_, tg, tb, -1, 1e-5, 1)
+    y.backward(dy)
+    assert _rel(Y.numpy(), y.data) < 1e-5
+    assert _rel(DX.numpy(), tx_.grad) < 1e-4
+    assert _rel(DG.numpy(), tg.grad) < 1e-4
+    assert _rel(DB.numpy(), tb.grad) < 1e-5
+
+
+def test_adam_is_bit_exact_with_oracle(tx):
+    from oracle import flex_oracle as fo
+    from tynx_b200 import optim
+    from tynx_b200.imported import ImportedModel
+    from tynx_b200.workloads import mlp_policy
+
+    wl = mlp_policy()
+    model = ImportedModel(wl.onnx)
+    params = model.parameters()
+    opt = optim.Adam(params, lr=3e-4)
+    rng = np.random.default_rng(3)
+    ref_params = [fo.T(p.numpy(), requires_grad=True) for p in params]
+    ref_opt = fo.Adam(ref_params, lr=3e-4)
+    for _ in range(5):
+        for p, r in zip(params, ref_params):
+            g = rng.standard_normal(p.shape).astype(np.float32)
+            p.grad = tx.Tensor(g)
+            r.grad = g
+        opt.step()
+        ref_opt.step()
+    for p, r in zip(params, ref_params):
+        np.testing.assert_array_equal(p.numpy(), r.data)
+
+
+def test_adamw_amsgrad_sgd_match_oracle(tx):
+    from oracle import flex_oracle as fo
+    from tynx_b200 import optim
+    from tynx_b200.imported import ImportedModel
+    from tynx_b200.workloads import mlp_policy
+
+    rng = np.random.default_rng(4)
+    cases = [
+        (lambda ps: optim.AdamW(ps, lr=1e-2, weight_decay=0.1),
+         lambda ps: fo.Adam(ps, lr=1e-2, weight_decay=0.1, decoupled=True)),
+        (lambda ps: optim.Adam(ps, lr=1e-2, amsgrad=True, weight_decay=0.01),
+         lambda ps: fo.Adam(ps, lr=1e-2, amsgrad=True, weight_decay=0.01)),
+        (lambda ps: optim.SGD(ps, lr=0.1, momentum=0.9, nesterov=True),
+         lambda ps: fo.SGD(ps, lr=0.1, momentum=0.9, nesterov=True)),
+        (lambda ps: optim.SGD(ps, lr=0.1, momentum=0.5, dampening=0.1, weight_decay=0.01),
+         lambda ps: fo.SGD(ps, lr=0.1, momentum=0.5, dampening=0.1, weight_decay=0.01)),
+    ]
+    for make, make_ref in cases:
+        model = ImportedModel(mlp_policy().onnx)
+        params = model.parameters()
+        opt = make(params)
+        refs = [fo.T(p.numpy(), requires_grad=True) for p in params]
+        ref_opt = make_ref(refs)
+        for _ in range(4):
+            for p, r in zip(params, refs):
+                g = rng.standard_normal(p.shape).astype(np.float32)
+                p.grad = tx.Tensor(g)
+                r.grad = g
+            opt.step()
+            ref_opt.step()
+        for p, r in zip(params, refs):
+            np.testing.assert_allclose(p.numpy(), r.data, rtol=1e-6, atol=1e-7)
+
+
+def test_gather_scatter_rows(tx):
+    from tynx_b200 import _native as N
+    from tynx_b200._core import context
+
+    ctx = context()
+    rng = np.random.default_rng(6)
+    table = rng.standard_normal((1000, 256)).astype(np.float32)
+    idx = rng.integers(-1000, 1000, 5000).astype(np.int64)
+    T, I = tx.Tensor(table), tx.Tensor(idx)
+    out = tx.zeros(5000, 256)
+    ctx.check(N.lib.tx_gather_rows(ctx.handle, T.ptr, 1000, 256, I.ptr, 5000, out.ptr))
+    np.testing.assert_array_equal(out.numpy(), table[np.where(idx < 0, idx + 1000, idx)])
+    src = rng.integers(-3, 4, (5000, 256)).astype(np.float32)  # integers: exact in any order
+    acc = tx.zeros(1000, 256)
+    ctx.check(N.lib.tx_scatter_add_rows(ctx.handle, acc.ptr, 1000, 256, I.ptr, 5000,
+                                        tx.Tensor(src).ptr))
+    want = np.zeros((1000, 256), np.float32)
+    np.add.at(want, np.where(idx < 0, idx + 1000, idx), src)
+    np.testing.assert_array_equal(acc.numpy(), want)
+
+
+def test_bias_grad_and_reductions(tx):
+    from tynx_b200 import _native as N
+    from tynx_b200._core import context
+
+    ctx = context()
+    rng = np.random.default_rng(8)
+    for M, Nn in [(4096, 1024), (8192, 16), (7, 3), (32768, 256)]:
+        dy = rng.standard_normal((M, Nn)).astype(np.float32)
+        db = tx.zeros(Nn)
+        ctx.check(N.lib.tx_bias_grad(ctx.handle, tx.Tensor(dy).ptr, db.ptr, M, Nn, C.c_float(1.0), 0))
+        assert _rel(db.numpy(), dy.astype(np.float64).sum(0)) < 1e-5
+    x = rng.standard_normal((16, 33, 8)).astype(np.float32)
+    t = tx.Tensor(x)
+    np.testing.assert_allclose(t.mean(1).numpy(), x.mean(1), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(t.sum().numpy(), [x.astype(np.float64).sum()], rtol=1e-5)

@@ -1,0 +1,108 @@
+"""Host-side checks that need no GPU: the C ABI library, the header, lowering."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_library_exports_every_declared_symbol():
+    header = (ROOT / "include" / "tynx_cuda.h").read_text()
+    declared = set(re.findall(r"^int (tx_\w+)\(", header, re.M))
+    from tynx_b200 import _native
+
+    lib = _native.lib
+    missing = [name for name in declared if not hasattr(lib, name)]
+    assert not missing, missing
+    assert declared == set(_native.SIGNATURES), declared ^ set(_native.SIGNATURES)
+    assert lib.tx_abi_version() == 1
+
+
+def test_no_gpu_calls_fail_cleanly_without_a_device():
+    from tynx_b200 import _native
+
+    if _native.device_count() > 0:
+        pytest.skip("a GPU is present")
+    handle = C.c_void_p()
+    assert _native.lib.tx_ctx_create(0, 0, C.byref(handle)) != 0
+    assert not handle.value
+
+
+def test_cpu_devices_are_rejected():
+    from tynx_b200 import Device
+
+    with pytest.raises(ValueError, match="CUDA only"):
+        Device("cpu")
+    assert str(Device("cuda:3")) == "cuda:3"
+
+
+def test_workload_graphs_lower_and_match_parameter_counts():
+    from tynx_b200 import workloads
+    from tynx_b200.imported import lower
+    from tynx_b200.onnx import ir
+
+    expected = {"mlp_policy": 84488, "mlp_classifier": 1863690, "ppo": 337425, "cnn": 94538,
+                "transformer": 5280258}
+    for name, make in workloads.WORKLOADS.items():
+        kw = {"minibatch": 64, "rollout": 256} if name == "ppo" else {}
+        wl = make(**kw)
+        graph = ir.load_training_graph(wl.onnx)
+        assert graph.report.warnings == [] and graph.report.errors == []
+        assert graph.report.backward_issues == []
+        assert sum(p.size for p in graph.parameters.values()) == expected[name]
+        values, nodes, outputs, *_ = lower(graph)
+        assert len(outputs) == len(graph.outputs)
+        assert all(n.op > 0 for n in nodes)
+
+
+def test_reference_fixtures_lower(fixtures):
+    from tynx_b200.imported import lower
+    from tynx_b200.onnx import ir
+
+    for name in ["_GEMM_MODEL", "_GATHER_MODEL", "_LAYER_NORM_MODEL", "_BATCHED_MATMUL_MODEL",
+                 "_CLIPPED_GEMM_MODEL", "_CNN_MODEL", "_RECOMMENDER_MODEL", "_TRANSFORMER_MODEL",
+                 "_ACTOR_CRITIC_MODEL", "_CONV_MODEL", "_MATMUL_MODEL"]:
+        lower(ir.load_training_graph(fixtures[name]))
+
+
+def test_onnx_codec_round_trip():
+    from tynx_b200.onnx import proto
+
+    w = np.arange(6, dtype=np.float32).reshape(2, 3)
+    data = proto.encode_model(
+        [proto.encode_node("Gemm", ["x", "w"], ["y"], name="g", transB=1, alpha=0.5)],
+        [proto.encode_tensor("w", w)],
+        [proto.encode_value_info("x", proto.FLOAT, ["batch", 3])],
+        [proto.encode_value_info("y", proto.FLOAT, ["batch", 2])])
+    model = proto.decode_model(data)
+    node = model.graph.nodes[0]
+    assert node.op_type == "Gemm" and node.attr("transB") == 1
+    assert node.attr("alpha") == pytest.approx(0.5)
+    np.testing.assert_array_equal(model.graph.initializers[0].array, w)
+    assert model.graph.inputs[0].shape == ["batch", 3]
+
+
+def test_trainability_roles_follow_consumers(fixtures):
+    from tynx_b200.onnx import ir
+
+    graph = ir.load_training_graph(fixtures["_GEMM_MODEL"],
+                                   initializer_names={"weight": "head.weight", "bias": "head.bias"})
+    assert sorted(graph.report.trainable_parameters) == ["head.bias", "head.weight"]
+    assert graph.report.output_parameters["y"] == ["head.bias", "head.weight"]
+    with pytest.raises(ValueError, match="not a declared"):
+        ir.load_training_graph(fixtures["_GEMM_MODEL"], outputs=["missing"])
+    # an initializer consumed by Add has no trainable role and stays constant with a warning
+    from tynx_b200.onnx import proto
+
+    data = proto.encode_model(
+        [proto.encode_node("Add", ["x", "b"], ["y"], name="add")],
+        [proto.encode_tensor("b", np.zeros(2, np.float32))],
+        [proto.encode_value_info("x", proto.FLOAT, [2])],
+        [proto.encode_value_info("y", proto.FLOAT, [2])])
+    g = ir.load_training_graph(data)
+    assert g.report.trainable_parameters == []
+    assert any("no registered trainable role" in w for w in g.report.warnings)

@@ -1,0 +1,110 @@
+// Internal declarations shared by the libtynx_cuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "../../include/tynx_cuda.h"
+
+// Device-side error codes written into ctx->d_err[0] by kernels.  Kernels never
+// trap: they record the first problem, skip the offending access and return.
+enum { DEVERR_NONE = 0, DEVERR_INDEX = 1, DEVERR_TIMEOUT = 2, DEVERR_LABEL = 3 };
+
+struct tx_arena {
+  std::vector<std::pair<char *, size_t>> chunks;
+  size_t offset = 0;  // within chunks.back()
+  std::unordered_set<void *> blocks;
+  std::vector<void *> pinned;  // host staging for copies recorded during capture
+};
+
+struct tx_allocator {
+  // size class (bytes) -> cached device blocks, reused in stream order
+  std::map<size_t, std::vector<void *>> free_blocks;
+  std::unordered_map<void *, size_t> live;
+  uint64_t in_use = 0, cached = 0;
+  tx_arena *arena = nullptr;  // non-null while capturing
+  std::unordered_map<void *, tx_arena *> arena_owner;
+  std::vector<void *> quarantine;  // eager blocks freed during a capture
+};
+
+struct tx_ctx {
+  int device = 0;
+  int math = TX_MATH_TF32;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;  // compute
+  cudaStream_t comm = nullptr;    // collectives
+  tx_allocator alloc;
+  int err_code = 0;
+  std::string err_msg;
+  int *d_err = nullptr;  // device error flag [4]
+  bool capturing = false;
+  // data parallel
+  void *nccl = nullptr;
+  int world = 1, rank = 0;
+  uint64_t dp_timeout_ms = 60000;
+};
+
+struct tx_exec {
+  tx_ctx *ctx = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  tx_arena *arena = nullptr;
+};
+
+// ---- error helpers ---------------------------------------------------------
+int tx_fail(tx_ctx *ctx, int code, const std::string &msg);
+int tx_cuda_fail(tx_ctx *ctx, cudaError_t err, const char *what);
+#define TX_CUDA(ctx, expr)                                    \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return tx_cuda_fail(ctx, _e, #expr); \
+  } while (0)
+#define TX_LAUNCHED(ctx, name)                                      \
+  do {                                                              \
+    cudaError_t _e = cudaGetLastError();                            \
+    if (_e != cudaSuccess) return tx_cuda_fail(ctx, _e, name);      \
+  } while (0)
+#define TX_TRY(expr)             \
+  do {                           \
+    int _rc = (expr);            \
+    if (_rc != TX_OK) return _rc; \
+  } while (0)
+
+// ---- allocation (stream ordered on ctx->stream) -----------------------------
+void *tx_alloc_raw(tx_ctx *ctx, size_t bytes);
+void tx_free_raw(tx_ctx *ctx, void *p);
+
+// RAII scratch buffer from the context allocator.
+struct Scratch {
+  tx_ctx *ctx;
+  void *ptr = nullptr;
+  Scratch(tx_ctx *c, size_t bytes) : ctx(c) { ptr = bytes ? tx_alloc_raw(c, bytes) : nullptr; }
+  ~Scratch() {
+    if (ptr) tx_free_raw(ctx, ptr);
+  }
+  template <class T>
+  T *as() const { return reinterpret_cast<T *>(ptr); }
+  Scratch(const Scratch &) = delete;
+  Scratch &operator=(const Scratch &) = delete;
+};
+
+// ---- GEMM internals -----------------------------------------------------------
+int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d);
+// Returns TX_ERR_UNSUPPORTED (without latching) when the shape/layout cannot use
+// the tensor-core path; the dispatcher then uses the SIMT kernel.
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass);
+int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d);
+
+// grid sizing helper
+inline unsigned grid_for(int64_t n, int threads, int64_t max_blocks = 148 * 16) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return (unsigned)b;
+}

@@ -1,0 +1,1549 @@
+// Imported-graph engine: forward node loop, reverse tape, parameter slots.
+//
+// Replaces, for the CUDA placement:
+//   * executor::run (crates/tynx-train/src/imported_model/executor.rs:107-161) -- the
+//     topological node loop with live parameter slots (resolve_value 555-593);
+//   * the Burn autodiff tape walked by backward_parameters
+//     (crates/tynx-train/src/autograd.rs:56-95) -- here an explicit list of
+//     backward rules, one per forward node, run in reverse order;
+//   * ParameterSlot value/grad storage and accumulate_grad
+//     (crates/tynx-train/src/parameter.rs:88-333).
+// Parameters live in one flat device buffer (values) and one flat gradient
+// buffer, laid out in the order their gradients become final during backward,
+// so bucketed all-reduce ranges are contiguous.
+//
+// Fusions planned at build time:
+//   * Gemm/MatMul followed by its only consumer Relu/Tanh/Gelu -> bias +
+//     activation in the GEMM epilogue (Gelu also stores the pre-activation);
+//   * in backward, the dgrad GEMM producing the gradient of such a fused
+//     output multiplies by act' in its epilogue, handing the producer its
+//     pre-activation gradient directly.
+#include <math.h>
+
+#include <algorithm>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <string>
+
+#include "common.h"
+
+int dp_allreduce_range(tx_ctx *ctx, float *buf, int64_t n);  // dp.cu
+int dp_event_fork(tx_ctx *ctx);                               // compute -> comm
+int dp_event_join(tx_ctx *ctx);                               // comm -> compute
+
+namespace {
+
+using Shape = std::vector<int64_t>;
+
+int64_t numel_of(const Shape &s) {
+  int64_t n = 1;
+  for (int64_t d : s) n *= d;
+  return n;
+}
+
+std::string shape_str(const Shape &s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? "," : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+// ---- engine-only kernels -----------------------------------------------------------------
+__global__ void k_gather_axis(const float *__restrict__ data, const int64_t *__restrict__ idx,
+                              float *__restrict__ out, int64_t outer, int64_t axis_n, int64_t inner,
+                              int64_t n_idx, int *flag) {
+  int64_t total = outer * n_idx * inner;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t in_ = i % inner;
+    int64_t t = i / inner;
+    int64_t j = t % n_idx;
+    int64_t o = t / n_idx;
+    int64_t k = idx[j];
+    if (k < 0) k += axis_n;
+    if (k < 0 || k >= axis_n) {
+      if (atomicCAS(flag, 0, DEVERR_INDEX) == 0) {
+        flag[1] = (int)idx[j];
+        flag[2] = (int)axis_n;
+      }
+      out[i] = 0.f;
+    } else {
+      out[i] = data[(o * axis_n + k) * inner + in_];
+    }
+  }
+}
+
+__global__ void k_gather_axis_bwd(float *__restrict__ ddata, const int64_t *__restrict__ idx,
+                                  const float *__restrict__ dout, int64_t outer, int64_t axis_n,
+                                  int64_t inner, int64_t n_idx) {
+  int64_t total = outer * n_idx * inner;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t in_ = i % inner;
+    int64_t t = i / inner;
+    int64_t j = t % n_idx;
+    int64_t o = t / n_idx;
+    int64_t k = idx[j];
+    if (k < 0) k += axis_n;
+    if (k >= 0 && k < axis_n) atomicAdd(&ddata[(o * axis_n + k) * inner + in_], dout[i]);
+  }
+}
+
+struct BDims {
+  int64_t shape[TX_MAX_DIMS];
+  int64_t s[TX_MAX_DIMS];
+};
+
+// out[i] (+)= scale * in[offset(i)] with broadcast strides
+__global__ void k_broadcast_scale(const float *__restrict__ in, float *__restrict__ out, BDims d,
+                                  int ndim, int64_t n, float scale, int acc) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, off = 0;
+    for (int k = ndim - 1; k >= 0; --k) {
+      int64_t c = rem % d.shape[k];
+      rem /= d.shape[k];
+      off += c * d.s[k];
+    }
+    float v = scale * in[off];
+    out[i] = acc ? out[i] + v : v;
+  }
+}
+
+__global__ void k_axpy(float *__restrict__ y, const float *__restrict__ x, int64_t n, float a) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] += a * x[i];
+}
+
+// im2col for NCHW: cols[(n*OH + oh)*OW + ow][c*KH*KW + kh*KW + kw]
+__global__ void k_im2col(const float *__restrict__ x, float *__restrict__ cols, int64_t N, int64_t C,
+                         int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
+                         int sh, int sw, int pt, int pl, int dh, int dw, int64_t ldc) {
+  int64_t K = C * KH * KW;
+  int64_t total = N * OH * OW * K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k = i % K;
+    int64_t m = i / K;
+    int64_t kw = k % KW, kh = (k / KW) % KH, c = k / (KW * KH);
+    int64_t ow = m % OW, oh = (m / OW) % OH, n = m / (OW * OH);
+    int64_t ih = oh * sh - pt + kh * dh, iw = ow * sw - pl + kw * dw;
+    float v = 0.f;
+    if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = x[((n * C + c) * H + ih) * W + iw];
+    cols[m * ldc + k] = v;
+  }
+}
+
+// col2im (gather form: each input pixel sums its contributions, no atomics)
+__global__ void k_col2im(const float *__restrict__ dcols, float *__restrict__ dx, int64_t N,
+                         int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t OH,
+                         int64_t OW, int sh, int sw, int pt, int pl, int dh, int dw, int64_t ldc,
+                         int acc) {
+  int64_t total = N * C * H * W;
+  int64_t K = C * KH * KW;
+  (void)K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t iw = i % W, ih = (i / W) % H, c = (i / (W * H)) % C, n = i / (W * H * C);
+    float s = 0.f;
+    for (int64_t kh = 0; kh < KH; ++kh) {
+      int64_t t = ih + pt - kh * dh;
+      if (t < 0 || t % sh) continue;
+      int64_t oh = t / sh;
+      if (oh >= OH) continue;
+      for (int64_t kw = 0; kw < KW; ++kw) {
+        int64_t u = iw + pl - kw * dw;
+        if (u < 0 || u % sw) continue;
+        int64_t ow = u / sw;
+        if (ow >= OW) continue;
+        s += dcols[((n * OH + oh) * OW + ow) * ldc + (c * KH + kh) * KW + kw];
+      }
+    }
+    dx[i] = acc ? dx[i] + s : s;
+  }
+}
+
+// [N*HW, C] <-> [N, C, HW]
+__global__ void k_nhwc_to_nchw(const float *__restrict__ src, float *__restrict__ dst, int64_t N,
+                               int64_t C, int64_t HW, const float *__restrict__ bias, int act) {
+  int64_t total = N * C * HW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t p = i % HW, c = (i / HW) % C, n = i / (HW * C);
+    float v = src[(n * HW + p) * C + c];
+    if (bias) v += bias[c];
+    if (act == TX_ACT_RELU) v = v > 0.f ? v : 0.f;
+    dst[i] = v;
+  }
+}
+
+__global__ void k_nchw_to_nhwc(const float *__restrict__ src, float *__restrict__ dst, int64_t N,
+                               int64_t C, int64_t HW) {
+  int64_t total = N * C * HW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t c = i % C, p = (i / C) % HW, n = i / (C * HW);
+    dst[i] = src[(n * C + c) * HW + p];
+  }
+}
+
+}  // namespace
+
+// ============================================================================
+// graph structures
+// ============================================================================
+struct GValue {
+  int kind = TX_VAL_ACT;
+  int dtype = TX_DT_F32;
+  Shape shape;                 // static shape (PARAM/CONST)
+  void *dev = nullptr;         // PARAM: slice of flat values; CONST: own buffer
+  float *grad = nullptr;       // PARAM: slice of flat grads
+  int param_index = -1;
+  bool grad_defined = false;
+  std::vector<int> consumers;  // node indices
+  int producer = -1;
+  bool is_output = false;
+  int input_index = -1;
+};
+
+struct GNode {
+  tx_node_desc d;
+  int fused_act = TX_ACT_NONE;  // GEMM/MATMUL: absorbed activation
+  int fused_into = -1;          // activation node absorbed by node index
+  int fused_out = -1;           // value written by the fused epilogue
+};
+
+struct tx_graph {
+  tx_ctx *ctx = nullptr;
+  std::vector<GValue> values;
+  std::vector<GNode> nodes;
+  std::vector<int> inputs;   // value ids of TX_VAL_INPUT in declaration order
+  std::vector<int> outputs;  // value ids
+  std::vector<int> params;   // value ids in param-index order (declaration order)
+  std::vector<int64_t> param_offset;  // offset in flat buffers
+  float *flat_values = nullptr;
+  float *flat_grads = nullptr;
+  int64_t flat_len = 0;
+  // DP
+  bool dp = false;
+  int64_t bucket_bytes = 0;
+  std::vector<int> grad_final_order;  // param indices in the order grads become final
+};
+
+struct tx_record {
+  tx_graph *g = nullptr;
+  std::vector<Shape> shapes;         // per value
+  std::vector<void *> buf;           // per value device buffer
+  std::vector<bool> owned;           // buffer owned by the record
+  std::vector<void *> extra;         // per node saved extras
+  std::vector<std::vector<void *>> extra2;
+  bool tracking = false;
+};
+
+namespace {
+
+int fail(tx_graph *g, int code, const std::string &msg) { return tx_fail(g->ctx, code, msg); }
+
+// ---- shape inference ------------------------------------------------------------------------
+bool broadcast_shapes(const Shape &a, const Shape &b, Shape &out) {
+  size_t n = std::max(a.size(), b.size());
+  out.assign(n, 1);
+  for (size_t i = 0; i < n; ++i) {
+    int64_t da = i < n - a.size() ? 1 : a[i - (n - a.size())];
+    int64_t db = i < n - b.size() ? 1 : b[i - (n - b.size())];
+    if (da != db && da != 1 && db != 1) return false;
+    out[i] = da == 1 ? db : da;
+  }
+  return true;
+}
+
+// element strides of `s` broadcast to `out` (0 on broadcast axes)
+void bstrides(const Shape &s, const Shape &out, int64_t *st) {
+  size_t n = out.size();
+  int64_t stride = 1;
+  for (int64_t i = (int64_t)n - 1; i >= 0; --i) {
+    int64_t j = i - (int64_t)(n - s.size());
+    if (j < 0) {
+      st[i] = 0;
+      continue;
+    }
+    st[i] = s[j] == 1 && out[i] != 1 ? 0 : stride;
+    stride *= s[j];
+  }
+}
+
+int norm_axis(int64_t axis, int64_t rank) { return (int)(axis < 0 ? axis + rank : axis); }
+
+int infer_node(tx_graph *g, const GNode &n, std::vector<Shape> &S) {
+  const tx_node_desc &d = n.d;
+  auto in = [&](int i) -> const Shape & { return S[d.in[i]]; };
+  Shape &out = S[d.out[0]];
+  switch (d.op) {
+    case TX_OP_GEMM: {
+      const Shape &a = in(0), &b = in(1);
+      if (a.size() != 2 || b.size() != 2) return fail(g, TX_ERR_SHAPE, "Gemm requires rank-2 inputs");
+      int64_t M = d.iattr[0] ? a[1] : a[0], K = d.iattr[0] ? a[0] : a[1];
+      int64_t K2 = d.iattr[1] ? b[1] : b[0], N = d.iattr[1] ? b[0] : b[1];
+      if (K != K2) return fail(g, TX_ERR_SHAPE, "Gemm inner dimensions differ: " + shape_str(a) + " x " + shape_str(b));
+      out = {M, N};
+      return TX_OK;
+    }
+    case TX_OP_MATMUL: {
+      Shape a = in(0), b = in(1);
+      if (a.size() < 2 || b.size() < 2)
+        return fail(g, TX_ERR_UNSUPPORTED, "MatMul with rank-1 operands is not supported on CUDA");
+      if (a.back() != b[b.size() - 2])
+        return fail(g, TX_ERR_SHAPE, "MatMul inner dimensions differ: " + shape_str(a) + " x " + shape_str(b));
+      if (b.size() == 2) {
+        out = a;
+        out.back() = b[1];
+        return TX_OK;
+      }
+      if (a.size() != b.size())
+        return fail(g, TX_ERR_UNSUPPORTED, "MatMul batch broadcasting is not supported on CUDA");
+      for (size_t i = 0; i + 2 < a.size(); ++i)
+        if (a[i] != b[i]) return fail(g, TX_ERR_UNSUPPORTED, "MatMul batch broadcasting is not supported on CUDA");
+      out = a;
+      out.back() = b.back();
+      return TX_OK;
+    }
+    case TX_OP_CONV: {
+      const Shape &x = in(0), &w = in(1);
+      if (x.size() != 4 || w.size() != 4) return fail(g, TX_ERR_UNSUPPORTED, "only 2-D Conv is supported on CUDA");
+      if (d.iattr[0] != 1) return fail(g, TX_ERR_UNSUPPORTED, "grouped Conv is not supported on CUDA");
+      if (x[1] != w[1]) return fail(g, TX_ERR_SHAPE, "Conv channel mismatch");
+      int64_t sh = d.ints[0], sw = d.ints[1], pt = d.ints[2], pl = d.ints[3], pb = d.ints[4],
+              pr = d.ints[5], dh = d.ints[6], dw = d.ints[7];
+      int64_t oh = (x[2] + pt + pb - dh * (w[2] - 1) - 1) / sh + 1;
+      int64_t ow = (x[3] + pl + pr - dw * (w[3] - 1) - 1) / sw + 1;
+      out = {x[0], w[0], oh, ow};
+      return TX_OK;
+    }
+    case TX_OP_GATHER: {
+      const Shape &x = in(0), &idx = in(1);
+      int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+      out.clear();
+      for (int i = 0; i < ax; ++i) out.push_back(x[i]);
+      for (int64_t v : idx) out.push_back(v);
+      for (size_t i = ax + 1; i < x.size(); ++i) out.push_back(x[i]);
+      return TX_OK;
+    }
+    case TX_OP_LAYERNORM: {
+      out = in(0);
+      int ax = norm_axis(d.iattr[0], (int64_t)out.size());
+      Shape st = out;
+      for (size_t i = ax; i < st.size(); ++i) st[i] = 1;
+      if (d.n_out > 1) S[d.out[1]] = st;
+      if (d.n_out > 2) S[d.out[2]] = st;
+      return TX_OK;
+    }
+    case TX_OP_ADD: case TX_OP_SUB: case TX_OP_MUL: case TX_OP_DIV:
+      if (!broadcast_shapes(in(0), in(1), out))
+        return fail(g, TX_ERR_SHAPE, "cannot broadcast " + shape_str(in(0)) + " with " + shape_str(in(1)));
+      return TX_OK;
+    case TX_OP_RELU: case TX_OP_TANH: case TX_OP_GELU: case TX_OP_SIGMOID: case TX_OP_EXP:
+    case TX_OP_LOG: case TX_OP_NEG: case TX_OP_IDENTITY: case TX_OP_CLIP:
+    case TX_OP_SOFTMAX: case TX_OP_LOGSOFTMAX:
+      out = in(0);
+      return TX_OK;
+    case TX_OP_REDUCEMEAN: case TX_OP_REDUCESUM: {
+      const Shape &x = in(0);
+      std::vector<bool> red(x.size(), d.n_ints == 0);
+      for (int i = 0; i < d.n_ints; ++i) red[norm_axis(d.ints[i], (int64_t)x.size())] = true;
+      out.clear();
+      for (size_t i = 0; i < x.size(); ++i) {
+        if (!red[i]) out.push_back(x[i]);
+        else if (d.iattr[0]) out.push_back(1);
+      }
+      return TX_OK;
+    }
+    case TX_OP_GAP: {
+      out = in(0);
+      for (size_t i = 2; i < out.size(); ++i) out[i] = 1;
+      return TX_OK;
+    }
+    case TX_OP_RESHAPE: {
+      const Shape &x = in(0);
+      out.clear();
+      int64_t known = 1, infer = -1;
+      for (int i = 0; i < d.n_ints; ++i) {
+        int64_t s = d.ints[i];
+        if (s == 0 && !d.iattr[0]) s = x[i];
+        if (s == -1) {
+          infer = i;
+          s = 1;
+        } else {
+          known *= s;
+        }
+        out.push_back(s);
+      }
+      if (infer >= 0) out[infer] = known ? numel_of(x) / known : 0;
+      if (numel_of(out) != numel_of(x))
+        return fail(g, TX_ERR_SHAPE, "Reshape " + shape_str(x) + " -> " + shape_str(out));
+      return TX_OK;
+    }
+    case TX_OP_FLATTEN: {
+      const Shape &x = in(0);
+      int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+      int64_t lead = 1;
+      for (int i = 0; i < ax; ++i) lead *= x[i];
+      out = {lead, numel_of(x) / (lead ? lead : 1)};
+      return TX_OK;
+    }
+    case TX_OP_TRANSPOSE: {
+      const Shape &x = in(0);
+      out.assign(x.size(), 0);
+      for (size_t i = 0; i < x.size(); ++i)
+        out[i] = x[d.n_ints ? d.ints[i] : (int64_t)x.size() - 1 - (int64_t)i];
+      return TX_OK;
+    }
+    case TX_OP_SQUEEZE: {
+      const Shape &x = in(0);
+      std::vector<bool> drop(x.size(), false);
+      if (d.n_ints == 0)
+        for (size_t i = 0; i < x.size(); ++i) drop[i] = x[i] == 1;
+      for (int i = 0; i < d.n_ints; ++i) drop[norm_axis(d.ints[i], (int64_t)x.size())] = true;
+      out.clear();
+      for (size_t i = 0; i < x.size(); ++i)
+        if (!drop[i]) out.push_back(x[i]);
+      return TX_OK;
+    }
+    case TX_OP_UNSQUEEZE: {
+      const Shape &x = in(0);
+      int64_t r = (int64_t)x.size() + d.n_ints;
+      std::vector<bool> ins(r, false);
+      for (int i = 0; i < d.n_ints; ++i) ins[norm_axis(d.ints[i], r)] = true;
+      out.clear();
+      size_t j = 0;
+      for (int64_t i = 0; i < r; ++i) out.push_back(ins[i] ? 1 : x[j++]);
+      return TX_OK;
+    }
+  }
+  return fail(g, TX_ERR_UNSUPPORTED, "operator " + std::to_string(d.op) + " is not supported on CUDA");
+}
+
+bool is_alias_op(int op) {
+  return op == TX_OP_RESHAPE || op == TX_OP_FLATTEN || op == TX_OP_SQUEEZE ||
+         op == TX_OP_UNSQUEEZE || op == TX_OP_IDENTITY;
+}
+
+int act_of_op(int op) {
+  switch (op) {
+    case TX_OP_RELU: return TX_ACT_RELU;
+    case TX_OP_TANH: return TX_ACT_TANH;
+    case TX_OP_GELU: return TX_ACT_GELU;
+  }
+  return TX_ACT_NONE;
+}
+
+int unary_code(int op) {
+  switch (op) {
+    case TX_OP_RELU: return TX_UN_RELU;
+    case TX_OP_TANH: return TX_UN_TANH;
+    case TX_OP_GELU: return TX_UN_GELU;
+    case TX_OP_SIGMOID: return TX_UN_SIGMOID;
+    case TX_OP_EXP: return TX_UN_EXP;
+    case TX_OP_LOG: return TX_UN_LOG;
+    case TX_OP_NEG: return TX_UN_NEG;
+    case TX_OP_CLIP: return TX_UN_CLAMP;
+  }
+  return -1;
+}
+
+// forward output saved for the backward factor (true) or the input (false)
+bool unary_uses_output(int op) {
+  return op == TX_OP_RELU || op == TX_OP_TANH || op == TX_OP_SIGMOID || op == TX_OP_EXP;
+}
+
+}  // namespace
+
+// ============================================================================
+// build
+// ============================================================================
+extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_values,
+                               const tx_node_desc *nodes, int n_nodes, const int32_t *outputs,
+                               int n_outputs, tx_graph **out) {
+  if (!ctx || !out || n_values <= 0 || n_nodes < 0) return TX_ERR_INVALID;
+  if (ctx->capturing) return tx_fail(ctx, TX_ERR_CAPTURE, "graph creation is not capturable");
+  *out = nullptr;
+  std::unique_ptr<tx_graph> g(new tx_graph());
+  g->ctx = ctx;
+  g->values.resize(n_values);
+  for (int i = 0; i < n_values; ++i) {
+    GValue &v = g->values[i];
+    v.kind = vals[i].kind;
+    v.dtype = vals[i].dtype;
+    if (vals[i].ndim > TX_MAX_DIMS) return tx_fail(ctx, TX_ERR_INVALID, "value rank above 8");
+    if (vals[i].ndim >= 0) v.shape.assign(vals[i].shape, vals[i].shape + vals[i].ndim);
+    if (v.kind == TX_VAL_INPUT) {
+      v.input_index = (int)g->inputs.size();
+      g->inputs.push_back(i);
+    }
+    if (v.kind == TX_VAL_PARAM) {
+      if (v.dtype != TX_DT_F32) return tx_fail(ctx, TX_ERR_INVALID, "parameters must be float32");
+      v.param_index = (int)g->params.size();
+      g->params.push_back(i);
+    }
+  }
+  g->nodes.resize(n_nodes);
+  for (int i = 0; i < n_nodes; ++i) {
+    g->nodes[i].d = nodes[i];
+    const tx_node_desc &d = nodes[i];
+    if (d.n_in < 0 || d.n_in > 4 || d.n_out < 1 || d.n_out > 3 || d.n_ints < 0 || d.n_ints > 16)
+      return tx_fail(ctx, TX_ERR_INVALID, "malformed node descriptor");
+    for (int k = 0; k < d.n_in; ++k) {
+      if (d.in[k] < -1 || d.in[k] >= n_values) return tx_fail(ctx, TX_ERR_INVALID, "node input id out of range");
+      if (d.in[k] >= 0) g->values[d.in[k]].consumers.push_back(i);
+    }
+    for (int k = 0; k < d.n_out; ++k) {
+      if (d.out[k] < 0 || d.out[k] >= n_values) return tx_fail(ctx, TX_ERR_INVALID, "node output id out of range");
+      g->values[d.out[k]].producer = i;
+    }
+  }
+  for (int i = 0; i < n_outputs; ++i) {
+    if (outputs[i] < 0 || outputs[i] >= n_values) return tx_fail(ctx, TX_ERR_INVALID, "output id out of range");
+    g->outputs.push_back(outputs[i]);
+    g->values[outputs[i]].is_output = true;
+  }
+
+  // ---- fusion plan: Gemm/MatMul(2-D weight) -> sole-consumer activation ----------------
+  for (int i = 0; i < n_nodes; ++i) {
+    GNode &n = g->nodes[i];
+    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL) continue;
+    GValue &y = g->values[n.d.out[0]];
+    if (y.is_output || y.consumers.size() != 1) continue;
+    GNode &a = g->nodes[y.consumers[0]];
+    int act = act_of_op(a.d.op);
+    if (act == TX_ACT_NONE || a.d.in[0] != n.d.out[0]) continue;
+    n.fused_act = act;
+    n.fused_out = a.d.out[0];
+    a.fused_into = i;
+  }
+
+  // ---- parameter storage: order = when gradients become final in backward -----------------
+  std::vector<int> first_use(g->params.size(), n_nodes);
+  for (int i = 0; i < n_nodes; ++i)
+    for (int k = 0; k < g->nodes[i].d.n_in; ++k) {
+      int v = g->nodes[i].d.in[k];
+      if (v >= 0 && g->values[v].kind == TX_VAL_PARAM)
+        first_use[g->values[v].param_index] = std::min(first_use[g->values[v].param_index], i);
+    }
+  std::vector<int> order(g->params.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = (int)i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return first_use[a] > first_use[b]; });
+  g->grad_final_order = order;
+  g->param_offset.assign(g->params.size(), 0);
+  int64_t off = 0;
+  for (int p : order) {
+    g->param_offset[p] = off;
+    int64_t n = numel_of(g->values[g->params[p]].shape);
+    off += (n + 63) & ~int64_t(63);
+  }
+  g->flat_len = off;
+  if (off > 0) {
+    TX_CUDA(ctx, cudaMalloc(&g->flat_values, off * sizeof(float)));
+    TX_CUDA(ctx, cudaMalloc(&g->flat_grads, off * sizeof(float)));
+    TX_CUDA(ctx, cudaMemsetAsync(g->flat_grads, 0, off * sizeof(float), ctx->stream));
+    TX_CUDA(ctx, cudaMemsetAsync(g->flat_values, 0, off * sizeof(float), ctx->stream));
+  }
+  for (size_t p = 0; p < g->params.size(); ++p) {
+    GValue &v = g->values[g->params[p]];
+    v.dev = g->flat_values + g->param_offset[p];
+    v.grad = g->flat_grads + g->param_offset[p];
+    if (vals[g->params[p]].h_data)
+      TX_CUDA(ctx, cudaMemcpy(v.dev, vals[g->params[p]].h_data, numel_of(v.shape) * sizeof(float),
+                              cudaMemcpyHostToDevice));
+  }
+  for (int i = 0; i < n_values; ++i) {
+    GValue &v = g->values[i];
+    if (v.kind != TX_VAL_CONST) continue;
+    size_t bytes = numel_of(v.shape) * (v.dtype == TX_DT_I64 ? 8 : 4);
+    TX_CUDA(ctx, cudaMalloc(&v.dev, bytes ? bytes : 8));
+    if (vals[i].h_data && bytes)
+      TX_CUDA(ctx, cudaMemcpy(v.dev, vals[i].h_data, bytes, cudaMemcpyHostToDevice));
+  }
+  TX_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  *out = g.release();
+  return TX_OK;
+}
+
+extern "C" int tx_graph_destroy(tx_graph *g) {
+  if (!g) return TX_OK;
+  cudaStreamSynchronize(g->ctx->stream);
+  for (GValue &v : g->values)
+    if (v.kind == TX_VAL_CONST && v.dev) cudaFree(v.dev);
+  if (g->flat_values) cudaFree(g->flat_values);
+  if (g->flat_grads) cudaFree(g->flat_grads);
+  delete g;
+  return TX_OK;
+}
+
+extern "C" int tx_graph_param_count(tx_graph *g, int *out) {
+  if (!g || !out) return TX_ERR_INVALID;
+  *out = (int)g->params.size();
+  return TX_OK;
+}
+
+extern "C" int tx_graph_param(tx_graph *g, int i, int32_t *vid, float **value, float **grad, int64_t *numel) {
+  if (!g || i < 0 || i >= (int)g->params.size()) return TX_ERR_INVALID;
+  GValue &v = g->values[g->params[i]];
+  if (vid) *vid = g->params[i];
+  if (value) *value = (float *)v.dev;
+  if (grad) *grad = v.grad;
+  if (numel) *numel = numel_of(v.shape);
+  return TX_OK;
+}
+
+extern "C" int tx_graph_grad_defined(tx_graph *g, int i, int *out) {
+  if (!g || !out || i < 0 || i >= (int)g->params.size()) return TX_ERR_INVALID;
+  *out = g->values[g->params[i]].grad_defined ? 1 : 0;
+  return TX_OK;
+}
+
+extern "C" int tx_graph_set_grad_defined(tx_graph *g, int i, int defined) {
+  if (!g || i < 0 || i >= (int)g->params.size()) return TX_ERR_INVALID;
+  g->values[g->params[i]].grad_defined = defined != 0;
+  return TX_OK;
+}
+
+extern "C" int tx_graph_set_dp(tx_graph *g, int enabled, int64_t bucket_bytes) {
+  if (!g) return TX_ERR_INVALID;
+  if (enabled && g->ctx->world <= 1 && g->ctx->nccl == nullptr)
+    return tx_fail(g->ctx, TX_ERR_INVALID, "data parallelism needs tx_dp_init first");
+  g->dp = enabled != 0;
+  g->bucket_bytes = bucket_bytes > 0 ? bucket_bytes : (8 << 20);
+  return TX_OK;
+}
+
+static int infer_all(tx_graph *g, const int64_t *in_shapes, const int32_t *in_ndims,
+                     std::vector<Shape> &S) {
+  S.assign(g->values.size(), Shape());
+  size_t off = 0;
+  for (size_t i = 0; i < g->inputs.size(); ++i) {
+    int nd = in_ndims[i];
+    if (nd < 0 || nd > TX_MAX_DIMS) return fail(g, TX_ERR_INVALID, "input rank out of range");
+    S[g->inputs[i]].assign(in_shapes + off, in_shapes + off + nd);
+    off += nd;
+    const GValue &v = g->values[g->inputs[i]];
+    if (!v.shape.empty() && v.shape.size() != (size_t)nd)
+      return fail(g, TX_ERR_SHAPE, "input " + std::to_string(i) + " has rank " + std::to_string(nd) +
+                                       ", expected " + std::to_string(v.shape.size()));
+  }
+  for (size_t i = 0; i < g->values.size(); ++i)
+    if (g->values[i].kind == TX_VAL_PARAM || g->values[i].kind == TX_VAL_CONST) S[i] = g->values[i].shape;
+  for (const GNode &n : g->nodes) TX_TRY(infer_node(g, n, S));
+  return TX_OK;
+}
+
+extern "C" int tx_graph_infer(tx_graph *g, const int64_t *in_shapes, const int32_t *in_ndims,
+                              int64_t *out_shapes, int32_t *out_ndims) {
+  if (!g) return TX_ERR_INVALID;
+  std::vector<Shape> S;
+  TX_TRY(infer_all(g, in_shapes, in_ndims, S));
+  size_t off = 0;
+  for (size_t i = 0; i < g->outputs.size(); ++i) {
+    const Shape &s = S[g->outputs[i]];
+    out_ndims[i] = (int32_t)s.size();
+    for (int64_t v : s) out_shapes[off++] = v;
+  }
+  return TX_OK;
+}
+
+// ============================================================================
+// forward
+// ============================================================================
+namespace {
+
+struct Fwd {
+  tx_graph *g;
+  tx_ctx *ctx;
+  tx_record *r;
+
+  float *F(int v) { return (float *)r->buf[v]; }
+  const Shape &S(int v) { return r->shapes[v]; }
+
+  int alloc_value(int v) {
+    if (r->buf[v]) return TX_OK;
+    size_t bytes = numel_of(r->shapes[v]) * (g->values[v].dtype == TX_DT_I64 ? 8 : 4);
+    r->buf[v] = tx_alloc_raw(ctx, bytes ? bytes : 4);
+    if (!r->buf[v]) return TX_ERR_OOM;
+    r->owned[v] = true;
+    return TX_OK;
+  }
+
+  int gemm_node(int ni) {
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    int yv = n.fused_act ? n.fused_out : d.out[0];
+    TX_TRY(alloc_value(yv));
+    const Shape &a = S(d.in[0]), &b = S(d.in[1]);
+    tx_gemm_desc q;
+    memset(&q, 0, sizeof q);
+    q.alpha = 1.f;
+    q.batch = 1;
+    q.act = n.fused_act;
+    if (n.fused_act == TX_ACT_GELU) {
+      r->extra[ni] = tx_alloc_raw(ctx, numel_of(S(yv)) * 4);
+      if (!r->extra[ni]) return TX_ERR_OOM;
+    }
+    if (d.op == TX_OP_GEMM) {
+      q.trans_a = (int)d.iattr[0];
+      q.trans_b = (int)d.iattr[1];
+      q.M = q.trans_a ? a[1] : a[0];
+      q.K = q.trans_a ? a[0] : a[1];
+      q.N = q.trans_b ? b[0] : b[1];
+      q.A = F(d.in[0]);
+      q.lda = a[1];
+      q.B = F(d.in[1]);
+      q.ldb = b[1];
+      q.alpha = (float)d.fattr[0];
+      if (d.n_in > 2 && d.in[2] >= 0) {
+        const Shape &c = S(d.in[2]);
+        int64_t cn = numel_of(c);
+        if (!(cn == q.N && (c.size() == 1 || (c.size() == 2 && c[0] == 1))))
+          return fail(g, TX_ERR_UNSUPPORTED, "Gemm bias must have shape [N] or [1, N] on CUDA");
+        q.bias = F(d.in[2]);
+        q.bias_scale = (float)d.fattr[1];
+      }
+    } else {  // MATMUL
+      q.K = a.back();
+      q.N = b.back();
+      if (b.size() == 2) {
+        q.M = numel_of(a) / q.K;
+        q.A = F(d.in[0]);
+        q.lda = q.K;
+        q.B = F(d.in[1]);
+        q.ldb = q.N;
+      } else {
+        q.M = a[a.size() - 2];
+        q.batch = numel_of(a) / (q.M * q.K);
+        q.A = F(d.in[0]);
+        q.lda = q.K;
+        q.stride_a = q.M * q.K;
+        q.B = F(d.in[1]);
+        q.ldb = q.N;
+        q.stride_b = q.K * q.N;
+        q.stride_c = q.M * q.N;
+      }
+    }
+    q.C = F(yv);
+    q.ldc = q.N;
+    if (n.fused_act == TX_ACT_GELU) {
+      q.preact = (float *)r->extra[ni];
+      q.ld_preact = q.N;
+    }
+    return gemm_dispatch(ctx, q);
+  }
+
+  int conv_node(int ni) {
+    const tx_node_desc &d = g->nodes[ni].d;
+    const Shape &x = S(d.in[0]), &w = S(d.in[1]);
+    int yv = d.out[0];
+    TX_TRY(alloc_value(yv));
+    const Shape &y = S(yv);
+    int64_t N = x[0], C = x[1], H = x[2], W = x[3], OC = w[0], KH = w[2], KW = w[3], OH = y[2], OW = y[3];
+    int64_t K = C * KH * KW, M = N * OH * OW;
+    int64_t ldk = (K + 3) & ~int64_t(3);
+    float *cols = (float *)tx_alloc_raw(ctx, M * ldk * 4);
+    float *tmp = (float *)tx_alloc_raw(ctx, M * OC * 4);
+    if (!cols || !tmp) return TX_ERR_OOM;
+    r->extra[ni] = cols;  // saved for wgrad
+    k_im2col<<<grid_for(M * K, 256), 256, 0, ctx->stream>>>(F(d.in[0]), cols, N, C, H, W, KH, KW, OH, OW,
+                                                           (int)d.ints[0], (int)d.ints[1], (int)d.ints[2],
+                                                           (int)d.ints[3], (int)d.ints[6], (int)d.ints[7], ldk);
+    TX_LAUNCHED(ctx, "k_im2col");
+    if (ldk != K) TX_CUDA(ctx, cudaMemset2DAsync(cols + K, ldk * 4, 0, (ldk - K) * 4, M, ctx->stream));
+    // W is [OC, C*KH*KW] row-major; pad K for TMA by copying into [OC, ldk]
+    float *wk = (float *)F(d.in[1]);
+    float *wpad = nullptr;
+    if (ldk != K) {
+      wpad = (float *)tx_alloc_raw(ctx, OC * ldk * 4);
+      TX_CUDA(ctx, cudaMemsetAsync(wpad, 0, OC * ldk * 4, ctx->stream));
+      TX_CUDA(ctx, cudaMemcpy2DAsync(wpad, ldk * 4, wk, K * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
+      wk = wpad;
+    }
+    tx_gemm_desc q;
+    memset(&q, 0, sizeof q);
+    q.M = M; q.N = OC; q.K = ldk;
+    q.A = cols; q.lda = ldk; q.trans_a = 0;
+    q.B = wk; q.ldb = ldk; q.trans_b = 1;
+    q.C = tmp; q.ldc = OC; q.alpha = 1.f; q.batch = 1;
+    int rc = gemm_dispatch(ctx, q);
+    if (wpad) tx_free_raw(ctx, wpad);
+    TX_TRY(rc);
+    const float *bias = (d.n_in > 2 && d.in[2] >= 0) ? F(d.in[2]) : nullptr;
+    k_nhwc_to_nchw<<<grid_for(N * OC * OH * OW, 256), 256, 0, ctx->stream>>>(tmp, F(yv), N, OC, OH * OW, bias, 0);
+    TX_LAUNCHED(ctx, "k_nhwc_to_nchw");
+    tx_free_raw(ctx, tmp);
+    return TX_OK;
+  }
+
+  int node(int ni) {
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    if (n.fused_into >= 0) return TX_OK;  // done by the producing GEMM
+    if (is_alias_op(d.op)) {
+      r->buf[d.out[0]] = r->buf[d.in[0]];
+      r->owned[d.out[0]] = false;
+      return TX_OK;
+    }
+    switch (d.op) {
+      case TX_OP_GEMM: case TX_OP_MATMUL: return gemm_node(ni);
+      case TX_OP_CONV: return conv_node(ni);
+      default: break;
+    }
+    int yv = d.out[0];
+    TX_TRY(alloc_value(yv));
+    const Shape &y = S(yv);
+    int64_t ny = numel_of(y);
+    switch (d.op) {
+      case TX_OP_GATHER: {
+        const Shape &x = S(d.in[0]);
+        int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        int64_t outer = 1, inner = 1;
+        for (int i = 0; i < ax; ++i) outer *= x[i];
+        for (size_t i = ax + 1; i < x.size(); ++i) inner *= x[i];
+        int64_t nidx = numel_of(S(d.in[1]));
+        if (g->values[d.in[1]].dtype != TX_DT_I64) return fail(g, TX_ERR_INVALID, "Gather indices must be int64");
+        if (ax == 0) return tx_gather_rows(ctx, F(d.in[0]), x[0], inner, (const int64_t *)r->buf[d.in[1]], nidx, F(yv));
+        k_gather_axis<<<grid_for(ny, 256), 256, 0, ctx->stream>>>(F(d.in[0]), (const int64_t *)r->buf[d.in[1]], F(yv),
+                                                                 outer, x[ax], inner, nidx, ctx->d_err);
+        TX_LAUNCHED(ctx, "k_gather_axis");
+        return TX_OK;
+      }
+      case TX_OP_LAYERNORM: {
+        const Shape &x = S(d.in[0]);
+        int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        int64_t rows = 1;
+        for (int i = 0; i < ax; ++i) rows *= x[i];
+        int64_t cols = numel_of(x) / (rows ? rows : 1);
+        float *mean = nullptr, *rstd = nullptr;
+        if (d.n_out > 1) { TX_TRY(alloc_value(d.out[1])); mean = F(d.out[1]); }
+        if (d.n_out > 2) { TX_TRY(alloc_value(d.out[2])); rstd = F(d.out[2]); }
+        if (!mean) { mean = (float *)tx_alloc_raw(ctx, rows * 4); r->extra[ni] = mean; }
+        if (!rstd) {
+          rstd = (float *)tx_alloc_raw(ctx, rows * 4);
+          r->extra2[ni].push_back(rstd);
+        }
+        const float *beta = (d.n_in > 2 && d.in[2] >= 0) ? F(d.in[2]) : nullptr;
+        return tx_layernorm_fwd(ctx, F(d.in[0]), F(d.in[1]), beta, F(yv), mean, rstd, rows, cols,
+                                (float)d.fattr[0]);
+      }
+      case TX_OP_ADD: case TX_OP_SUB: case TX_OP_MUL: case TX_OP_DIV: {
+        int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS];
+        bstrides(S(d.in[0]), y, sa);
+        bstrides(S(d.in[1]), y, sb);
+        int op = d.op == TX_OP_ADD ? TX_BIN_ADD : d.op == TX_OP_SUB ? TX_BIN_SUB : d.op == TX_OP_MUL ? TX_BIN_MUL : TX_BIN_DIV;
+        return tx_binary(ctx, op, F(d.in[0]), sa, F(d.in[1]), sb, F(yv), y.data(), (int)y.size());
+      }
+      case TX_OP_RELU: case TX_OP_TANH: case TX_OP_GELU: case TX_OP_SIGMOID: case TX_OP_EXP:
+      case TX_OP_LOG: case TX_OP_NEG:
+        return tx_unary(ctx, unary_code(d.op), F(d.in[0]), F(yv), ny, 0.f, 0.f);
+      case TX_OP_CLIP: {
+        float lo = d.iattr[0] ? (float)d.fattr[0] : -INFINITY;
+        float hi = d.iattr[1] ? (float)d.fattr[1] : INFINITY;
+        return tx_unary(ctx, TX_UN_CLAMP, F(d.in[0]), F(yv), ny, lo, hi);
+      }
+      case TX_OP_SOFTMAX: case TX_OP_LOGSOFTMAX: {
+        const Shape &x = S(d.in[0]);
+        int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        if (ax != (int)x.size() - 1) return fail(g, TX_ERR_UNSUPPORTED, "Softmax over a non-final axis is not supported on CUDA");
+        int64_t cols = x.back();
+        return tx_softmax_fwd(ctx, F(d.in[0]), F(yv), ny / cols, cols, d.op == TX_OP_LOGSOFTMAX);
+      }
+      case TX_OP_REDUCEMEAN: case TX_OP_REDUCESUM: case TX_OP_GAP: {
+        const Shape &x = S(d.in[0]);
+        Shape keep = x;
+        if (d.op == TX_OP_GAP) {
+          for (size_t i = 2; i < keep.size(); ++i) keep[i] = 1;
+        } else if (d.n_ints == 0) {
+          for (auto &k : keep) k = 1;
+        } else {
+          for (int i = 0; i < d.n_ints; ++i) keep[norm_axis(d.ints[i], (int64_t)x.size())] = 1;
+        }
+        return tx_reduce_to(ctx, F(d.in[0]), x.data(), F(yv), keep.data(), (int)x.size(),
+                            d.op != TX_OP_REDUCESUM, 0);
+      }
+      case TX_OP_TRANSPOSE: {
+        const Shape &x = S(d.in[0]);
+        int nd = (int)x.size();
+        int64_t xs[TX_MAX_DIMS], ss[TX_MAX_DIMS];
+        int64_t st = 1;
+        for (int i = nd - 1; i >= 0; --i) { xs[i] = st; st *= x[i]; }
+        for (int i = 0; i < nd; ++i) ss[i] = xs[d.n_ints ? d.ints[i] : nd - 1 - i];
+        return tx_strided_copy(ctx, F(d.in[0]), ss, F(yv), y.data(), nd, g->values[d.in[0]].dtype == TX_DT_I64 ? 8 : 4);
+      }
+    }
+    return fail(g, TX_ERR_UNSUPPORTED, "operator " + std::to_string(d.op) + " has no CUDA forward");
+  }
+};
+
+}  // namespace
+
+extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const int64_t *in_shapes,
+                                const int32_t *in_ndims, void *const *d_outputs, int tracking,
+                                tx_record **rec_out) {
+  if (!g) return TX_ERR_INVALID;
+  if (rec_out) *rec_out = nullptr;
+  tx_ctx *ctx = g->ctx;
+  std::unique_ptr<tx_record> r(new tx_record());
+  r->g = g;
+  r->tracking = tracking != 0;
+  TX_TRY(infer_all(g, in_shapes, in_ndims, r->shapes));
+  size_t nv = g->values.size();
+  r->buf.assign(nv, nullptr);
+  r->owned.assign(nv, false);
+  r->extra.assign(g->nodes.size(), nullptr);
+  r->extra2.assign(g->nodes.size(), {});
+  for (size_t i = 0; i < g->inputs.size(); ++i) r->buf[g->inputs[i]] = const_cast<void *>(d_inputs[i]);
+  for (size_t i = 0; i < nv; ++i)
+    if (g->values[i].kind == TX_VAL_PARAM || g->values[i].kind == TX_VAL_CONST) r->buf[i] = g->values[i].dev;
+  // outputs are written straight into the caller's buffers, unless an output
+  // aliases another value (reshape of an input, an output listed twice...)
+  for (size_t i = 0; i < g->outputs.size(); ++i) {
+    int v = g->outputs[i];
+    const GValue &gv = g->values[v];
+    if (gv.kind != TX_VAL_ACT || gv.producer < 0) continue;
+    const GNode &p = g->nodes[gv.producer];
+    if (is_alias_op(p.d.op) || r->buf[v]) continue;
+    r->buf[v] = d_outputs[i];
+  }
+  Fwd f{g, ctx, r.get()};
+  int rc = TX_OK;
+  for (size_t i = 0; i < g->nodes.size() && rc == TX_OK; ++i) rc = f.node((int)i);
+  if (rc == TX_OK) {
+    for (size_t i = 0; i < g->outputs.size(); ++i) {
+      int v = g->outputs[i];
+      if (r->buf[v] != d_outputs[i]) {
+        size_t bytes = numel_of(r->shapes[v]) * (g->values[v].dtype == TX_DT_I64 ? 8 : 4);
+        rc = tx_d2d(ctx, d_outputs[i], r->buf[v], bytes);
+        if (rc) break;
+      }
+    }
+  }
+  if (rc != TX_OK || !tracking || !rec_out) {
+    tx_record_free(r.release());
+    return rc;
+  }
+  *rec_out = r.release();
+  return TX_OK;
+}
+
+extern "C" int tx_record_free(tx_record *r) {
+  if (!r) return TX_OK;
+  tx_ctx *ctx = r->g->ctx;
+  for (size_t i = 0; i < r->buf.size(); ++i)
+    if (r->owned[i]) tx_free_raw(ctx, r->buf[i]);
+  for (void *p : r->extra) tx_free_raw(ctx, p);
+  for (auto &v : r->extra2)
+    for (void *p : v) tx_free_raw(ctx, p);
+  delete r;
+  return TX_OK;
+}
+
+// ============================================================================
+// backward
+// ============================================================================
+namespace {
+
+struct Bwd {
+  tx_graph *g;
+  tx_ctx *ctx;
+  tx_record *r;
+  std::vector<float *> grad;       // per value gradient buffer
+  std::vector<bool> grad_owned;
+  std::vector<bool> grad_preact;   // gradient already multiplied by act' (fused dgrad)
+  std::vector<bool> needs;         // value needs a gradient
+  std::vector<float *> param_tmp;  // unused
+  // DP bucketing
+  std::vector<bool> param_done;
+  size_t next_final = 0;      // index into g->grad_final_order
+  int64_t bucket_start = 0;   // flat offset of the first not-yet-reduced element
+  std::vector<int> param_pending;  // remaining contributions per param
+
+  float *F(int v) { return (float *)r->buf[v]; }
+  const Shape &S(int v) { return r->shapes[v]; }
+
+  // Returns the buffer to write the gradient of value v into and whether the
+  // write must accumulate.  Parameter slots honour grad_defined.
+  int target(int v, float **out, int *acc) {
+    GValue &gv = g->values[v];
+    if (gv.kind == TX_VAL_PARAM) {
+      *out = gv.grad;
+      *acc = gv.grad_defined ? 1 : 0;
+      return TX_OK;
+    }
+    if (grad[v]) {
+      *out = grad[v];
+      *acc = 1;
+      return TX_OK;
+    }
+    grad[v] = (float *)tx_alloc_raw(ctx, numel_of(S(v)) * 4 + 4);
+    if (!grad[v]) return TX_ERR_OOM;
+    grad_owned[v] = true;
+    *out = grad[v];
+    *acc = 0;
+    return TX_OK;
+  }
+
+  void wrote(int v) {
+    GValue &gv = g->values[v];
+    if (gv.kind == TX_VAL_PARAM) {
+      gv.grad_defined = true;
+      param_contribution_done(gv.param_index);
+    }
+  }
+
+  // ---- DP: launch all-reduce for contiguous ranges of final gradients ----------
+  void param_contribution_done(int p) {
+    if (--param_pending[p] > 0) return;
+    param_done[p] = true;
+    if (!g->dp) return;
+    int64_t end = bucket_start;
+    while (next_final < g->grad_final_order.size() && param_done[g->grad_final_order[next_final]]) {
+      int q = g->grad_final_order[next_final];
+      int64_t n = numel_of(g->values[g->params[q]].shape);
+      end = g->param_offset[q] + ((n + 63) & ~int64_t(63));
+      ++next_final;
+    }
+    if ((end - bucket_start) * 4 >= g->bucket_bytes) flush(end);
+  }
+
+  int flush(int64_t end) {
+    if (end <= bucket_start) return TX_OK;
+    TX_TRY(dp_event_fork(ctx));
+    TX_TRY(dp_allreduce_range(ctx, g->flat_grads + bucket_start, end - bucket_start));
+    bucket_start = end;
+    return TX_OK;
+  }
+
+  int gemm_backward(int ni) {
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    int yv = n.fused_act ? n.fused_out : d.out[0];
+    float *dy = grad[yv];
+    if (!dy) return TX_OK;
+    // gradient with respect to the pre-activation
+    float *dz = dy;
+    float *dz_tmp = nullptr;
+    if (n.fused_act && !grad_preact[yv]) {
+      int64_t ny = numel_of(S(yv));
+      dz_tmp = (float *)tx_alloc_raw(ctx, ny * 4);
+      if (!dz_tmp) return TX_ERR_OOM;
+      if (n.fused_act == TX_ACT_GELU)
+        TX_TRY(tx_unary_bwd(ctx, TX_UN_GELU, (const float *)r->extra[ni], dy, dz_tmp, ny, 0.f, 0.f, 0));
+      else
+        TX_TRY(tx_unary_bwd(ctx, n.fused_act == TX_ACT_RELU ? TX_UN_RELU : TX_UN_TANH, F(yv), dy, dz_tmp, ny, 0.f, 0.f, 0));
+      dz = dz_tmp;
+    }
+    const Shape &a = S(d.in[0]), &b = S(d.in[1]);
+    int rc = TX_OK;
+    if (d.op == TX_OP_GEMM) {
+      int ta = (int)d.iattr[0], tb = (int)d.iattr[1];
+      int64_t M = ta ? a[1] : a[0], K = ta ? a[0] : a[1], N = tb ? b[0] : b[1];
+      float alpha = (float)d.fattr[0];
+      // bias
+      if (rc == TX_OK && d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
+        float *t; int acc;
+        rc = target(d.in[2], &t, &acc);
+        if (rc == TX_OK) rc = tx_bias_grad(ctx, dz, t, M, N, (float)d.fattr[1], acc);
+        if (rc == TX_OK) wrote(d.in[2]);
+      }
+      // dB
+      if (rc == TX_OK && needs[d.in[1]]) {
+        float *t; int acc;
+        rc = target(d.in[1], &t, &acc);
+        tx_gemm_desc q; memset(&q, 0, sizeof q);
+        q.alpha = alpha; q.beta = acc ? 1.f : 0.f; q.batch = 1;
+        if (!tb) {  // dB[K,N] = op(A)^T dY
+          q.M = K; q.N = N; q.K = M;
+          q.A = F(d.in[0]); q.lda = a[1]; q.trans_a = ta ? 0 : 1;
+          q.B = dz; q.ldb = N; q.trans_b = 0;
+          q.C = t; q.ldc = N;
+        } else {    // dB[N,K] = dY^T op(A)
+          q.M = N; q.N = K; q.K = M;
+          q.A = dz; q.lda = N; q.trans_a = 1;
+          q.B = F(d.in[0]); q.ldb = a[1]; q.trans_b = ta ? 1 : 0;
+          q.C = t; q.ldc = K;
+        }
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
+        if (rc == TX_OK) wrote(d.in[1]);
+      }
+      // dA
+      if (rc == TX_OK && needs[d.in[0]]) {
+        float *t; int acc;
+        rc = dgrad_target(d.in[0], &t, &acc);
+        tx_gemm_desc q; memset(&q, 0, sizeof q);
+        q.alpha = alpha; q.beta = acc ? 1.f : 0.f; q.batch = 1;
+        if (!ta) {  // dA[M,K] = dY op(B)^T
+          q.M = M; q.N = K; q.K = N;
+          q.A = dz; q.lda = N; q.trans_a = 0;
+          q.B = F(d.in[1]); q.ldb = b[1]; q.trans_b = tb ? 0 : 1;
+          q.C = t; q.ldc = K;
+          fuse_dact(d.in[0], q);
+        } else {    // dA[K,M] = op(B) dY^T
+          q.M = K; q.N = M; q.K = N;
+          q.A = F(d.in[1]); q.lda = b[1]; q.trans_a = tb ? 1 : 0;
+          q.B = dz; q.ldb = N; q.trans_b = 1;
+          q.C = t; q.ldc = M;
+        }
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
+        if (rc == TX_OK) wrote(d.in[0]);
+      }
+    } else {  // MATMUL
+      int64_t K = a.back(), N = b.back();
+      bool weight2d = b.size() == 2;
+      int64_t M = weight2d ? numel_of(a) / K : a[a.size() - 2];
+      int64_t batch = weight2d ? 1 : numel_of(a) / (M * K);
+      if (rc == TX_OK && needs[d.in[1]]) {  // dB = A^T dY
+        float *t; int acc;
+        rc = target(d.in[1], &t, &acc);
+        tx_gemm_desc q; memset(&q, 0, sizeof q);
+        q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
+        q.M = K; q.N = N; q.K = M;
+        q.A = F(d.in[0]); q.lda = K; q.trans_a = 1; q.stride_a = M * K;
+        q.B = dz; q.ldb = N; q.trans_b = 0; q.stride_b = M * N;
+        q.C = t; q.ldc = N; q.stride_c = K * N;
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
+        if (rc == TX_OK) wrote(d.in[1]);
+      }
+      if (rc == TX_OK && needs[d.in[0]]) {  // dA = dY B^T
+        float *t; int acc;
+        rc = dgrad_target(d.in[0], &t, &acc);
+        tx_gemm_desc q; memset(&q, 0, sizeof q);
+        q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
+        q.M = M; q.N = K; q.K = N;
+        q.A = dz; q.lda = N; q.trans_a = 0; q.stride_a = M * N;
+        q.B = F(d.in[1]); q.ldb = N; q.trans_b = 1; q.stride_b = weight2d ? 0 : K * N;
+        q.C = t; q.ldc = K; q.stride_c = M * K;
+        if (weight2d) { q.M = M; q.batch = 1; }
+        fuse_dact(d.in[0], q);
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
+        if (rc == TX_OK) wrote(d.in[0]);
+      }
+    }
+    if (dz_tmp) tx_free_raw(ctx, dz_tmp);
+    return rc;
+  }
+
+  int dgrad_target(int v, float **t, int *acc) { return target(v, t, acc); }
+
+  // If v is the (sole-consumer) output of a fused Gemm+act, fold act' into this
+  // dgrad epilogue so the producer receives its pre-activation gradient.
+  void fuse_dact(int v, tx_gemm_desc &q) {
+    const GValue &gv = g->values[v];
+    if (gv.kind != TX_VAL_ACT || gv.producer < 0 || gv.is_output) return;
+    const GNode &p = g->nodes[gv.producer];
+    if (p.fused_into < 0 || gv.consumers.size() != 1 || q.beta != 0.f) return;
+    const GNode &prod = g->nodes[p.fused_into];
+    if (prod.fused_out != v) return;
+    q.dact = prod.fused_act;
+    q.dact_src = prod.fused_act == TX_ACT_GELU ? (const float *)r->extra[p.fused_into] : F(v);
+    q.ld_dact = q.N;
+    grad_preact[v] = true;
+  }
+
+  int conv_backward(int ni) {
+    const tx_node_desc &d = g->nodes[ni].d;
+    float *dy = grad[d.out[0]];
+    if (!dy) return TX_OK;
+    const Shape &x = S(d.in[0]), &w = S(d.in[1]), &y = S(d.out[0]);
+    int64_t N = x[0], C = x[1], H = x[2], W = x[3], OC = w[0], KH = w[2], KW = w[3], OH = y[2], OW = y[3];
+    int64_t K = C * KH * KW, M = N * OH * OW;
+    int64_t ldk = (K + 3) & ~int64_t(3);
+    float *dyt = (float *)tx_alloc_raw(ctx, M * OC * 4);  // [M, OC]
+    if (!dyt) return TX_ERR_OOM;
+    k_nchw_to_nhwc<<<grid_for(M * OC, 256), 256, 0, ctx->stream>>>(dy, dyt, N, OC, OH * OW);
+    TX_LAUNCHED(ctx, "k_nchw_to_nhwc");
+    int rc = TX_OK;
+    if (d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
+      float *t; int acc;
+      rc = target(d.in[2], &t, &acc);
+      if (rc == TX_OK) rc = tx_bias_grad(ctx, dyt, t, M, OC, 1.f, acc);
+      if (rc == TX_OK) wrote(d.in[2]);
+    }
+    if (rc == TX_OK && needs[d.in[1]]) {  // dW[OC, K] = dyt^T cols
+      float *t; int acc;
+      rc = target(d.in[1], &t, &acc);
+      float *dw = t;
+      float *dwpad = nullptr;
+      if (rc == TX_OK && ldk != K) {
+        dwpad = (float *)tx_alloc_raw(ctx, OC * ldk * 4);
+        dw = dwpad;
+      }
+      tx_gemm_desc q; memset(&q, 0, sizeof q);
+      q.M = OC; q.N = ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
+      q.A = dyt; q.lda = OC; q.trans_a = 1;
+      q.B = (const float *)r->extra[ni]; q.ldb = ldk; q.trans_b = 0;
+      q.C = dw; q.ldc = ldk; q.beta = (acc && !dwpad) ? 1.f : 0.f;
+      if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
+      if (rc == TX_OK && dwpad) {
+        if (acc) {
+          float *tmp = (float *)tx_alloc_raw(ctx, OC * K * 4);
+          TX_CUDA(ctx, cudaMemcpy2DAsync(tmp, K * 4, dwpad, ldk * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
+          k_axpy<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(t, tmp, OC * K, 1.f);
+          tx_free_raw(ctx, tmp);
+        } else {
+          TX_CUDA(ctx, cudaMemcpy2DAsync(t, K * 4, dwpad, ldk * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
+        }
+      }
+      if (dwpad) tx_free_raw(ctx, dwpad);
+      if (rc == TX_OK) wrote(d.in[1]);
+    }
+    if (rc == TX_OK && needs[d.in[0]]) {  // dcols[M, K] = dyt W ; dx = col2im(dcols)
+      float *dcols = (float *)tx_alloc_raw(ctx, M * ldk * 4);
+      tx_gemm_desc q; memset(&q, 0, sizeof q);
+      q.M = M; q.N = K; q.K = OC; q.alpha = 1.f; q.batch = 1;
+      q.A = dyt; q.lda = OC; q.trans_a = 0;
+      q.B = F(d.in[1]); q.ldb = K; q.trans_b = 0;
+      q.C = dcols; q.ldc = ldk;
+      rc = gemm_dispatch(ctx, q);
+      float *t; int acc;
+      if (rc == TX_OK) rc = target(d.in[0], &t, &acc);
+      if (rc == TX_OK) {
+        k_col2im<<<grid_for(N * C * H * W, 256), 256, 0, ctx->stream>>>(
+            dcols, t, N, C, H, W, KH, KW, OH, OW, (int)d.ints[0], (int)d.ints[1], (int)d.ints[2],
+            (int)d.ints[3], (int)d.ints[6], (int)d.ints[7], ldk, acc);
+        TX_LAUNCHED(ctx, "k_col2im");
+        wrote(d.in[0]);
+      }
+      tx_free_raw(ctx, dcols);
+    }
+    tx_free_raw(ctx, dyt);
+    return rc;
+  }
+
+  // dX (+)= reduce_to_shape(src) for broadcast binary backward
+  int reduce_into(int v, const float *src, const Shape &from, float scale) {
+    float *t; int acc;
+    TX_TRY(target(v, &t, &acc));
+    Shape xs = S(v);
+    Shape padded(from.size() - xs.size(), 1);
+    padded.insert(padded.end(), xs.begin(), xs.end());
+    int rc;
+    if (numel_of(padded) == numel_of(from)) {
+      if (scale == 1.f && !acc) rc = tx_d2d(ctx, t, src, numel_of(from) * 4);
+      else if (!acc) rc = tx_unary(ctx, TX_UN_SCALE, src, t, numel_of(from), scale, 0.f);
+      else {
+        k_axpy<<<grid_for(numel_of(from), 256), 256, 0, ctx->stream>>>(t, src, numel_of(from), scale);
+        TX_LAUNCHED(ctx, "k_axpy");
+        rc = TX_OK;
+      }
+    } else {
+      if (scale != 1.f) return fail(g, TX_ERR_UNSUPPORTED, "scaled broadcast reduction");
+      rc = tx_reduce_to(ctx, src, from.data(), t, padded.data(), (int)from.size(), 0, acc);
+    }
+    if (rc == TX_OK) wrote(v);
+    return rc;
+  }
+
+  int node(int ni) {
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    if (n.fused_into >= 0) {
+      // activation folded into the producing GEMM: hand the gradient over
+      int src = d.out[0];
+      GNode &p = g->nodes[n.fused_into];
+      (void)p;
+      (void)src;
+      return TX_OK;
+    }
+    bool any = false;
+    for (int k = 0; k < d.n_in; ++k)
+      if (d.in[k] >= 0 && needs[d.in[k]]) any = true;
+    if (!any) return TX_OK;
+    switch (d.op) {
+      case TX_OP_GEMM: case TX_OP_MATMUL: return gemm_backward(ni);
+      case TX_OP_CONV: return conv_backward(ni);
+      default: break;
+    }
+    int yv = d.out[0];
+    float *dy = grad[yv];
+    if (!dy) return TX_OK;
+    const Shape &y = S(yv);
+    int64_t ny = numel_of(y);
+    int xv = d.in[0];
+    if (is_alias_op(d.op)) {
+      if (!needs[xv]) return TX_OK;
+      GValue &gx = g->values[xv];
+      if (gx.kind != TX_VAL_PARAM && !grad[xv] && grad_owned[yv]) {  // hand the buffer over
+        grad[xv] = dy;
+        grad_owned[xv] = true;
+        grad_owned[yv] = false;
+        grad_preact[xv] = grad_preact[yv];
+        wrote(xv);
+        return TX_OK;
+      }
+      float *t; int acc;
+      TX_TRY(target(xv, &t, &acc));
+      if (acc) {
+        k_axpy<<<grid_for(ny, 256), 256, 0, ctx->stream>>>(t, dy, ny, 1.f);
+        TX_LAUNCHED(ctx, "k_axpy");
+      } else {
+        TX_TRY(tx_d2d(ctx, t, dy, ny * 4));
+      }
+      wrote(xv);
+      return TX_OK;
+    }
+    switch (d.op) {
+      case TX_OP_GATHER: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        int64_t outer = 1, inner = 1;
+        for (int i = 0; i < ax; ++i) outer *= x[i];
+        for (size_t i = ax + 1; i < x.size(); ++i) inner *= x[i];
+        int64_t nidx = numel_of(S(d.in[1]));
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        if (!acc) TX_CUDA(ctx, cudaMemsetAsync(t, 0, numel_of(x) * 4, ctx->stream));
+        if (ax == 0) {
+          TX_TRY(tx_scatter_add_rows(ctx, t, x[0], inner, (const int64_t *)r->buf[d.in[1]], nidx, dy));
+        } else {
+          k_gather_axis_bwd<<<grid_for(ny, 256), 256, 0, ctx->stream>>>(t, (const int64_t *)r->buf[d.in[1]], dy,
+                                                                       outer, x[ax], inner, nidx);
+          TX_LAUNCHED(ctx, "k_gather_axis_bwd");
+        }
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_LAYERNORM: {
+        const Shape &x = S(xv);
+        int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        int64_t rows = 1;
+        for (int i = 0; i < ax; ++i) rows *= x[i];
+        int64_t cols = numel_of(x) / (rows ? rows : 1);
+        const float *mean = d.n_out > 1 ? F(d.out[1]) : (const float *)r->extra[ni];
+        const float *rstd = d.n_out > 2 ? F(d.out[2]) : (const float *)r->extra2[ni][0];
+        float *dx = nullptr, *dg = nullptr, *db = nullptr;
+        int ax_acc = 0, p_acc = 0;
+        if (needs[xv]) TX_TRY(target(xv, &dx, &ax_acc));
+        int gv = d.in[1], bv = (d.n_in > 2 ? d.in[2] : -1);
+        int gacc = 0, bacc = 0;
+        if (needs[gv]) TX_TRY(target(gv, &dg, &gacc));
+        if (bv >= 0 && needs[bv]) TX_TRY(target(bv, &db, &bacc));
+        // the kernel takes one accumulate flag for both parameter gradients
+        float *dg_tmp = nullptr, *db_tmp = nullptr;
+        p_acc = gacc;
+        if (db && bacc != gacc) {
+          db_tmp = (float *)tx_alloc_raw(ctx, cols * 4);
+          TX_CUDA(ctx, cudaMemsetAsync(db_tmp, 0, cols * 4, ctx->stream));
+          if (bacc) TX_CUDA(ctx, cudaMemcpyAsync(db_tmp, db, cols * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+        }
+        TX_TRY(tx_layernorm_bwd(ctx, F(xv), F(gv), mean, rstd, dy, dx, dg, db_tmp ? db_tmp : db, rows, cols,
+                                ax_acc, p_acc));
+        if (db_tmp) {
+          TX_CUDA(ctx, cudaMemcpyAsync(db, db_tmp, cols * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+          tx_free_raw(ctx, db_tmp);
+        }
+        (void)dg_tmp;
+        if (dx) wrote(xv);
+        if (dg) wrote(gv);
+        if (db) wrote(bv);
+        return TX_OK;
+      }
+      case TX_OP_ADD: case TX_OP_SUB: {
+        if (needs[d.in[0]]) TX_TRY(reduce_into(d.in[0], dy, y, 1.f));
+        if (needs[d.in[1]]) {
+          if (d.op == TX_OP_ADD) {
+            TX_TRY(reduce_into(d.in[1], dy, y, 1.f));
+          } else {
+            float *neg = (float *)tx_alloc_raw(ctx, ny * 4);
+            TX_TRY(tx_unary(ctx, TX_UN_NEG, dy, neg, ny, 0.f, 0.f));
+            int rc = reduce_into(d.in[1], neg, y, 1.f);
+            tx_free_raw(ctx, neg);
+            TX_TRY(rc);
+          }
+        }
+        return TX_OK;
+      }
+      case TX_OP_MUL: case TX_OP_DIV: {
+        int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS], sy[TX_MAX_DIMS];
+        const Shape &A = S(d.in[0]), &B = S(d.in[1]);
+        bstrides(A, y, sa);
+        bstrides(B, y, sb);
+        bstrides(y, y, sy);
+        float *tmp = (float *)tx_alloc_raw(ctx, ny * 4);
+        if (!tmp) return TX_ERR_OOM;
+        int rc = TX_OK;
+        if (needs[d.in[0]]) {  // dA = dy * B  (or dy / B)
+          rc = tx_binary(ctx, d.op == TX_OP_MUL ? TX_BIN_MUL : TX_BIN_DIV, dy, sy, F(d.in[1]), sb, tmp, y.data(), (int)y.size());
+          if (rc == TX_OK) rc = reduce_into(d.in[0], tmp, y, 1.f);
+        }
+        if (rc == TX_OK && needs[d.in[1]]) {
+          if (d.op == TX_OP_MUL) {  // dB = dy * A
+            rc = tx_binary(ctx, TX_BIN_MUL, dy, sy, F(d.in[0]), sa, tmp, y.data(), (int)y.size());
+          } else {  // dB = -dy * y / B
+            rc = tx_binary(ctx, TX_BIN_MUL, dy, sy, F(yv), sy, tmp, y.data(), (int)y.size());
+            if (rc == TX_OK) rc = tx_binary(ctx, TX_BIN_DIV, tmp, sy, F(d.in[1]), sb, tmp, y.data(), (int)y.size());
+            if (rc == TX_OK) rc = tx_unary(ctx, TX_UN_NEG, tmp, tmp, ny, 0.f, 0.f);
+          }
+          if (rc == TX_OK) rc = reduce_into(d.in[1], tmp, y, 1.f);
+        }
+        tx_free_raw(ctx, tmp);
+        return rc;
+      }
+      case TX_OP_RELU: case TX_OP_TANH: case TX_OP_GELU: case TX_OP_SIGMOID: case TX_OP_EXP:
+      case TX_OP_LOG: case TX_OP_NEG: case TX_OP_CLIP: {
+        if (!needs[xv]) return TX_OK;
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        const float *src = unary_uses_output(d.op) ? F(yv) : F(xv);
+        float lo = 0.f, hi = 0.f;
+        if (d.op == TX_OP_CLIP) {
+          lo = d.iattr[0] ? (float)d.fattr[0] : -INFINITY;
+          hi = d.iattr[1] ? (float)d.fattr[1] : INFINITY;
+        }
+        TX_TRY(tx_unary_bwd(ctx, unary_code(d.op), src, dy, t, ny, lo, hi, acc));
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_SOFTMAX: case TX_OP_LOGSOFTMAX: {
+        if (!needs[xv]) return TX_OK;
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        int64_t cols = y.back();
+        TX_TRY(tx_softmax_bwd(ctx, F(yv), dy, t, ny / cols, cols, d.op == TX_OP_LOGSOFTMAX, acc));
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_REDUCEMEAN: case TX_OP_REDUCESUM: case TX_OP_GAP: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        Shape keep = x;
+        if (d.op == TX_OP_GAP) {
+          for (size_t i = 2; i < keep.size(); ++i) keep[i] = 1;
+        } else if (d.n_ints == 0) {
+          for (auto &k : keep) k = 1;
+        } else {
+          for (int i = 0; i < d.n_ints; ++i) keep[norm_axis(d.ints[i], (int64_t)x.size())] = 1;
+        }
+        int64_t nred = numel_of(x) / numel_of(keep);
+        float scale = d.op == TX_OP_REDUCESUM ? 1.f : 1.f / (float)nred;
+        BDims bd;
+        int64_t st[TX_MAX_DIMS];
+        bstrides(keep, x, st);
+        for (size_t i = 0; i < x.size(); ++i) { bd.shape[i] = x[i]; bd.s[i] = st[i]; }
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        k_broadcast_scale<<<grid_for(numel_of(x), 256), 256, 0, ctx->stream>>>(dy, t, bd, (int)x.size(), numel_of(x), scale, acc);
+        TX_LAUNCHED(ctx, "k_broadcast_scale");
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_TRANSPOSE: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        int nd = (int)x.size();
+        // dX[perm^-1] : element of dx at index i corresponds to dy at permuted index
+        int64_t ys[TX_MAX_DIMS], ss[TX_MAX_DIMS];
+        int64_t st = 1;
+        for (int i = nd - 1; i >= 0; --i) { ys[i] = st; st *= y[i]; }
+        for (int i = 0; i < nd; ++i) {
+          int p = (int)(d.n_ints ? d.ints[i] : nd - 1 - i);  // y axis i = x axis p
+          ss[p] = ys[i];
+        }
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        if (!acc) {
+          TX_TRY(tx_strided_copy(ctx, dy, ss, t, x.data(), nd, 4));
+        } else {
+          float *tmp = (float *)tx_alloc_raw(ctx, ny * 4);
+          TX_TRY(tx_strided_copy(ctx, dy, ss, tmp, x.data(), nd, 4));
+          k_axpy<<<grid_for(ny, 256), 256, 0, ctx->stream>>>(t, tmp, ny, 1.f);
+          tx_free_raw(ctx, tmp);
+        }
+        wrote(xv);
+        return TX_OK;
+      }
+    }
+    return fail(g, TX_ERR_UNSUPPORTED, "operator " + std::to_string(d.op) + " has no CUDA backward");
+  }
+};
+
+}  // namespace
+
+extern "C" int tx_graph_backward(tx_graph *g, tx_record *r, const float *const *d_outputs,
+                                 float *const *d_inputs) {
+  if (!g || !r || r->g != g) return TX_ERR_INVALID;
+  tx_ctx *ctx = g->ctx;
+  size_t nv = g->values.size();
+  Bwd b{g, ctx, r};
+  b.grad.assign(nv, nullptr);
+  b.grad_owned.assign(nv, false);
+  b.grad_preact.assign(nv, false);
+  b.needs.assign(nv, false);
+  b.param_done.assign(g->params.size(), false);
+  b.param_pending.assign(g->params.size(), 0);
+  // which values need gradients: parameters, requested inputs, and anything downstream
+  for (size_t i = 0; i < nv; ++i)
+    if (g->values[i].kind == TX_VAL_PARAM) b.needs[i] = true;
+  for (size_t i = 0; i < g->inputs.size(); ++i)
+    if (d_inputs && d_inputs[i]) b.needs[g->inputs[i]] = true;
+  for (const GNode &n : g->nodes) {
+    bool any = false;
+    for (int k = 0; k < n.d.n_in; ++k)
+      if (n.d.in[k] >= 0 && b.needs[n.d.in[k]]) any = true;
+    if (any && n.d.op != TX_OP_GATHER)
+      for (int k = 0; k < n.d.n_out; ++k) b.needs[n.d.out[k]] = true;
+    if (n.d.op == TX_OP_GATHER && b.needs[n.d.in[0]]) b.needs[n.d.out[0]] = true;
+  }
+  // contributions per parameter (for DP bucket readiness)
+  for (const GNode &n : g->nodes)
+    for (int k = 0; k < n.d.n_in; ++k) {
+      int v = n.d.in[k];
+      if (v >= 0 && g->values[v].kind == TX_VAL_PARAM) b.param_pending[g->values[v].param_index]++;
+    }
+  if (g->dp) {
+    for (size_t p = 0; p < g->params.size(); ++p)
+      if (b.param_pending[p] == 0) b.param_pending[p] = 1;  // unused params still reduce
+  }
+  // seed output gradients
+  for (size_t i = 0; i < g->outputs.size(); ++i) {
+    int v = g->outputs[i];
+    if (!d_outputs[i]) continue;
+    int64_t nel = numel_of(r->shapes[v]);
+    if (b.grad[v]) {  // output listed twice
+      k_axpy<<<grid_for(nel, 256), 256, 0, ctx->stream>>>(b.grad[v], d_outputs[i], nel, 1.f);
+      TX_LAUNCHED(ctx, "k_axpy");
+    } else {
+      // own copy: later accumulation must never write into the caller's tensor
+      b.grad[v] = (float *)tx_alloc_raw(ctx, nel * 4 + 4);
+      if (!b.grad[v]) return TX_ERR_OOM;
+      b.grad_owned[v] = true;
+      TX_TRY(tx_d2d(ctx, b.grad[v], d_outputs[i], nel * 4));
+    }
+  }
+  // the value an absorbed activation produces is the one the GEMM backward reads
+  int rc = TX_OK;
+  for (int i = (int)g->nodes.size() - 1; i >= 0 && rc == TX_OK; --i) rc = b.node(i);
+  if (rc == TX_OK && g->dp) {
+    // parameters no node touched still take part in the reduction
+    for (size_t p = 0; p < g->params.size(); ++p)
+      if (!b.param_done[p]) {
+        b.param_pending[p] = 1;
+        GValue &gv = g->values[g->params[p]];
+        if (!gv.grad_defined) {
+          cudaMemsetAsync(gv.grad, 0, numel_of(gv.shape) * 4, ctx->stream);
+          gv.grad_defined = true;
+        }
+        b.param_contribution_done((int)p);
+      }
+    rc = b.flush(g->flat_len);
+    if (rc == TX_OK) rc = dp_event_join(ctx);
+  }
+  if (rc == TX_OK && d_inputs) {
+    for (size_t i = 0; i < g->inputs.size(); ++i) {
+      if (!d_inputs[i]) continue;
+      int v = g->inputs[i];
+      size_t bytes = numel_of(r->shapes[v]) * 4;
+      if (b.grad[v]) rc = tx_d2d(ctx, d_inputs[i], b.grad[v], bytes);
+      else rc = tx_memset(ctx, d_inputs[i], 0, bytes);
+      if (rc) break;
+    }
+  }
+  for (size_t i = 0; i < nv; ++i)
+    if (b.grad_owned[i]) tx_free_raw(ctx, b.grad[i]);
+  return rc;
+}

@@ -1,0 +1,140 @@
+// SIMT fp32 GEMM with the fused epilogue, and the GEMM dispatcher.
+//
+// The SIMT kernel is the exact-fp32 mode (TX_MATH_FP32: FFMA products, no
+// operand rounding) and serves shapes the tensor-core kernel cannot take
+// (strides that are not 16-byte multiples, tiny N such as 10-class heads).
+// Semantics follow execute_gemm + add_bias
+// (crates/tynx-train/src/imported_model/executor.rs:499-524, 606-613):
+//   C = alpha * op(A) op(B) + bias_scale * bias   (then activation)
+// plus beta * C for gradient accumulation (parameter.rs:300-333) and an
+// optional act' multiply for backward (dgrad) fusion.
+#include <math.h>
+
+#include "common.h"
+
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4;
+
+__device__ __forceinline__ float act_f(int act, float v) {
+  switch (act) {
+    case TX_ACT_RELU: return v > 0.f ? v : 0.f;
+    case TX_ACT_TANH: return tanhf(v);
+    case TX_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  }
+  return v;
+}
+
+// derivative from the saved tensor: relu/tanh use the forward output, gelu the pre-activation
+__device__ __forceinline__ float dact_f(int act, float s) {
+  switch (act) {
+    case TX_ACT_RELU: return s > 0.f ? 1.f : 0.f;
+    case TX_ACT_TANH: return 1.f - s * s;
+    case TX_ACT_GELU: {
+      float cdf = 0.5f * (1.0f + erff(s * 0.70710678118654752f));
+      return cdf + s * expf(-0.5f * s * s) * 0.39894228040143268f;
+    }
+  }
+  return 1.f;
+}
+
+__global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Bs[BK][BN + 4];
+  const int64_t bz = blockIdx.z;
+  const float *A = d.A + bz * d.stride_a;
+  const float *B = d.B + bz * d.stride_b;
+  float *C = d.C + bz * d.stride_c;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+  for (int64_t k0 = 0; k0 < d.K; k0 += BK) {
+    // 64x16 A tile and 16x64 B tile: 1024 elements each, 4 per thread
+    for (int e = threadIdx.x; e < BM * BK; e += 256) {
+      int mm, kk;
+      if (d.trans_a) { mm = e % BM; kk = e / BM; }  // A stored K x M: consecutive threads along m
+      else { kk = e % BK; mm = e / BK; }
+      int64_t gm = m0 + mm, gk = k0 + kk;
+      float v = 0.f;
+      if (gm < d.M && gk < d.K) v = d.trans_a ? A[gk * d.lda + gm] : A[gm * d.lda + gk];
+      As[kk][mm] = v;
+    }
+    for (int e = threadIdx.x; e < BK * BN; e += 256) {
+      int nn, kk;
+      if (d.trans_b) { kk = e % BK; nn = e / BK; }  // B stored N x K
+      else { nn = e % BN; kk = e / BN; }
+      int64_t gn = n0 + nn, gk = k0 + kk;
+      float v = 0.f;
+      if (gn < d.N && gk < d.K) v = d.trans_b ? B[gn * d.ldb + gk] : B[gk * d.ldb + gn];
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) a[i] = As[kk][ty * TM + i];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx * TN + j];
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    int64_t gm = m0 + ty * TM + i;
+    if (gm >= d.M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      int64_t gn = n0 + tx * TN + j;
+      if (gn >= d.N) continue;
+      float v = d.alpha * acc[i][j];
+      if (d.bias) v += d.bias[gn] * d.bias_scale;
+      if (d.beta != 0.f) v += d.beta * C[gm * d.ldc + gn];
+      if (d.preact) d.preact[bz * d.stride_c + gm * d.ld_preact + gn] = v;
+      v = act_f(d.act, v);
+      if (d.dact) v *= dact_f(d.dact, d.dact_src[bz * d.stride_c + gm * d.ld_dact + gn]);
+      C[gm * d.ldc + gn] = v;
+    }
+  }
+}
+
+}  // namespace
+
+int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
+  int64_t batch = d.batch > 1 ? d.batch : 1;
+  if (batch > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "GEMM batch above 65535");
+  dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + BM - 1) / BM), (unsigned)batch);
+  if (grid.y > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "GEMM M too large for SIMT grid");
+  k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(d);
+  TX_LAUNCHED(ctx, "k_gemm_simt");
+  return TX_OK;
+}
+
+int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d) {
+  if (d.M <= 0 || d.N <= 0) return TX_OK;
+  if (ctx->math != TX_MATH_FP32) {
+    int rc = gemm_tcgen05(ctx, d, ctx->math == TX_MATH_3XTF32);
+    if (rc != TX_ERR_UNSUPPORTED) return rc;
+  }
+  return gemm_simt(ctx, d);
+}
+
+extern "C" int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc) {
+  if (!ctx || !desc) return TX_ERR_INVALID;
+  const tx_gemm_desc &d = *desc;
+  if (d.M < 0 || d.N < 0 || d.K < 0) return tx_fail(ctx, TX_ERR_SHAPE, "negative GEMM extent");
+  if (d.act < 0 || d.act > TX_ACT_GELU || d.dact < 0 || d.dact > TX_ACT_GELU)
+    return TX_ERR_INVALID;
+  if (d.dact && !d.dact_src) return TX_ERR_INVALID;
+  return gemm_dispatch(ctx, d);
+}

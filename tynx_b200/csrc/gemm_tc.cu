@@ -1,0 +1,443 @@
+// tcgen05 / TMEM / TMA fp32 contraction for sm_100a (kind::tf32).
+//
+// One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
+//   warp 0      TMA producer: loads 128x32 A and BNx32 B fp32 tiles per stage
+//               (128-byte swizzle) into a STAGES-deep shared-memory ring;
+//   warp 1      allocates TMEM (BN fp32 columns x 128 lanes) and, from one
+//               thread, issues tcgen05.mma.kind::tf32 (K = 8 per instruction,
+//               4 per stage), committing each stage back to the producer;
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (one row per thread),
+//               apply alpha / bias / beta*C / activation / act' and store.
+// Operands may be K-major or MN-major on either side, so the forward
+// (X W^T), dgrad (dY W) and wgrad (dY^T X) products of a Gemm all map onto
+// the same kernel without transposes.  No TMA multicast is used anywhere.
+//
+// Every mbarrier wait is bounded (~2 s of %globaltimer).  On expiry the CTA
+// raises the context's device error flag, stops issuing work, waits (bounded)
+// for its own MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "common.h"
+
+namespace {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 32;                       // fp32 elements per 128-byte swizzle row
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+template <int BN>
+struct TcCfg {
+  static constexpr int A_BYTES = TC_BM * TC_BK * 4;
+  static constexpr int B_BYTES = BN * TC_BK * 4;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196 * 1024 / STAGE) > 8 ? 8 : (196 * 1024 / STAGE);
+  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and raises the flags) when the limit expires
+// or another role of the CTA has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *err, int site) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t start = global_ns();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - start > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (atomicCAS(err, 0, DEVERR_TIMEOUT) == 0) err[1] = site;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint64_t *bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 layout, version 1).  K-major tiles
+// use the 128-byte swizzle (layout 2: 8 rows x 128 B atoms); MN-major fp32 tiles
+// use the 128-byte swizzle with 32-byte atomicity (layout 1: 4 rows x 128 B
+// atoms), the only MN-major layout the tf32 MMA accepts.
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float act_f(int act, float v) {
+  switch (act) {
+    case TX_ACT_RELU: return v > 0.f ? v : 0.f;
+    case TX_ACT_TANH: return tanhf(v);
+    case TX_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  }
+  return v;
+}
+
+__device__ __forceinline__ float dact_f(int act, float s) {
+  switch (act) {
+    case TX_ACT_RELU: return s > 0.f ? 1.f : 0.f;
+    case TX_ACT_TANH: return 1.f - s * s;
+    case TX_ACT_GELU: {
+      float cdf = 0.5f * (1.0f + erff(s * 0.70710678118654752f));
+      return cdf + s * expf(-0.5f * s * s) * 0.39894228040143268f;
+    }
+  }
+  return 1.f;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+              const tx_gemm_desc d, int *err) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + STAGES * Cfg::STAGE);
+  uint64_t *empty = full + STAGES;
+  uint64_t *accb = empty + STAGES;
+  uint32_t *tmem_holder = (uint32_t *)(accb + 1);
+  volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * TC_BM;
+  const int n0 = blockIdx.x * BN;
+  const int bz = blockIdx.z;
+  const int num_k = (int)((d.K + TC_BK - 1) / TC_BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < num_k; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 1)) break;
+        mbar_expect_tx(&full[s], Cfg::STAGE);
+        const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
+        const uint32_t b_dst = a_dst + Cfg::A_BYTES;
+        const int k0 = kb * TC_BK;
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, bz);
+        } else {
+          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, bz);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, bz);
+        } else {
+          tma_load_3d(b_dst, &mapB, &full[s], k0, n0, bz);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(TC_BM >> 4) << 24);
+      bool ok = true;
+      for (int kb = 0; kb < num_k; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (!mbar_wait(&full[s], round & 1, abort_flag, err, 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE);
+        const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+        for (int k = 0; k < TC_BK / 8; ++k) {
+          // K-major: advance 32 bytes inside the swizzled 128-byte row (SBO =
+          // 8 rows).  MN-major: 8 K rows (1024 bytes) per instruction, LBO =
+          // the 4 KB stride between 32-element MN blocks, SBO = 4 rows.
+          const uint64_t ad = A_MN ? smem_desc(a_base + k * 1024, 4096, 512, kLayoutSW128Base32B)
+                                   : smem_desc(a_base + k * 32, 16, 1024, kLayoutSW128);
+          const uint64_t bd = B_MN ? smem_desc(b_base + k * 1024, 4096, 512, kLayoutSW128Base32B)
+                                   : smem_desc(b_base + k * 32, 16, 1024, kLayoutSW128);
+          tc_mma_tf32(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);
+      }
+      (void)ok;
+      tc_commit(accb);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrants 2,3,0,1
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const bool have = mbar_wait(accb, 0, abort_flag, err, 3);
+    tc_fence_after();
+    if (have && !*abort_flag) {
+      const int64_t gm = (int64_t)m0 + row;
+      const bool row_ok = gm < d.M;
+      float *C = d.C + (int64_t)bz * d.stride_c;
+      const int64_t cbase = bz * d.stride_c;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
+        if (!row_ok) continue;
+        const int64_t gn0 = (int64_t)n0 + c;
+        if (gn0 >= d.N) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t gn = gn0 + j;
+          if (gn < d.N) {
+            float x = d.alpha * v[j];
+            if (d.bias) x += d.bias[gn] * d.bias_scale;
+            if (d.beta != 0.f) x += d.beta * C[gm * d.ldc + gn];
+            if (d.preact) d.preact[cbase + gm * d.ld_preact + gn] = x;
+            x = act_f(d.act, x);
+            if (d.dact) x *= dact_f(d.dact, d.dact_src[cbase + gm * d.ld_dact + gn]);
+            v[j] = x;
+          }
+        }
+        const bool vec = (gn0 + 32 <= d.N) && ((d.ldc & 3) == 0) &&
+                         ((((uintptr_t)(C + gm * d.ldc + gn0)) & 15) == 0);
+        if (vec) {
+          float4 *dst = reinterpret_cast<float4 *>(C + gm * d.ldc + gn0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (gn0 + j < d.N) C[gm * d.ldc + gn0 + j] = v[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool load_encode() {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  });
+  return g_encode != nullptr;
+}
+
+// 3-D fp32 tensor map: dims {inner, outer, batch}; box {32, box_outer, 1}; 128-byte
+// swizzle (32-byte atomicity for MN-major operands, see smem_desc).
+bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld,
+              int64_t batch, int64_t batch_stride, int box_outer, bool mn_major) {
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+  int64_t bs = batch > 1 ? batch_stride : ld * outer;
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(((bs * 4) + 15) & ~int64_t(15))};
+  cuuint32_t box[3] = {32u, (cuuint32_t)box_outer, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
+              int64_t batch) {
+  auto kern = k_gemm_tc<BN, A_MN, B_MN>;
+  static bool configured[64] = {};
+  int dev = ctx->device & 63;
+  if (!configured[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN>::SMEM);
+    configured[dev] = true;
+  }
+  dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)batch);
+  kern<<<grid, 192, TcCfg<BN>::SMEM, ctx->stream>>>(ma, mb, d, ctx->d_err);
+  TX_LAUNCHED(ctx, "k_gemm_tc");
+  return TX_OK;
+}
+
+template <int BN>
+int launch_bn(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
+              int64_t batch) {
+  const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
+  if (a_mn && b_mn) return launch_tc<BN, true, true>(ctx, d, ma, mb, batch);
+  if (a_mn) return launch_tc<BN, true, false>(ctx, d, ma, mb, batch);
+  if (b_mn) return launch_tc<BN, false, true>(ctx, d, ma, mb, batch);
+  return launch_tc<BN, false, false>(ctx, d, ma, mb, batch);
+}
+
+int pick_bn(tx_ctx *ctx, int64_t M, int64_t N, int64_t batch) {
+  int best = 128;
+  double best_eff = -1;
+  const int cands[3] = {256, 128, 64};
+  for (int bn : cands) {
+    if (bn > 64 && N <= bn / 2) continue;  // mostly-empty tiles
+    int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn) * batch;
+    int64_t waves = (tiles + ctx->num_sms - 1) / ctx->num_sms;
+    double eff = (double)tiles / (double)(waves * ctx->num_sms);
+    // larger tiles amortise better; accept them unless they waste SMs
+    double score = eff + (bn == 256 ? 0.05 : bn == 128 ? 0.03 : 0.0);
+    if (score > best_eff) {
+      best_eff = score;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass) {
+  if (three_pass) return TX_ERR_UNSUPPORTED;  // 3xTF32 runs on the exact SIMT path
+  if (d.K <= 0 || d.M <= 0 || d.N <= 0) return TX_ERR_UNSUPPORTED;
+  const int64_t batch = d.batch > 1 ? d.batch : 1;
+  if (d.M >= (1ll << 31) || d.N >= (1ll << 31) || d.K >= (1ll << 31) || batch > 65535)
+    return TX_ERR_UNSUPPORTED;
+  // TMA: 16-byte aligned bases and row strides that are 16-byte multiples
+  if (((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) || (d.lda & 3) || (d.ldb & 3))
+    return TX_ERR_UNSUPPORTED;
+  if (batch > 1 && ((d.stride_a & 3) || (d.stride_b & 3))) return TX_ERR_UNSUPPORTED;
+  // rows shorter than one swizzle row waste most of each tile; SIMT is better
+  const int64_t a_inner = d.trans_a ? d.M : d.K;
+  const int64_t b_inner = d.trans_b ? d.K : d.N;
+  if (a_inner < 16 || b_inner < 16) return TX_ERR_UNSUPPORTED;
+  if (!load_encode()) return TX_ERR_UNSUPPORTED;
+
+  const int bn = pick_bn(ctx, d.M, d.N, batch);
+  CUtensorMap ma, mb;
+  bool ok;
+  if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
+    ok = make_map(&ma, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
+  else  // A stored M x K (K-major): box 32(K) x 128(M)
+    ok = make_map(&ma, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
+  if (!ok) return TX_ERR_UNSUPPORTED;
+  if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N)
+    ok = make_map(&mb, d.B, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
+  else  // B stored K x N (MN-major): box 32(N) x 32(K)
+    ok = make_map(&mb, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
+  if (!ok) return TX_ERR_UNSUPPORTED;
+
+  switch (bn) {
+    case 256: return launch_bn<256>(ctx, d, ma, mb, batch);
+    case 64: return launch_bn<64>(ctx, d, ma, mb, batch);
+    default: return launch_bn<128>(ctx, d, ma, mb, batch);
+  }
+}

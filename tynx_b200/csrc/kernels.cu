@@ -1,0 +1,1123 @@
+// Bandwidth-bound kernels of the training step (sm_100a).
+//
+// Each kernel restates the arithmetic of the Burn operator the reference calls
+// through DynTensor (crates/tynx/src/tensor.rs) so that results agree with the
+// Flex CPU backend within fp32 rounding.  Rows are handled one warp per row with
+// shuffle reductions; elementwise work is vectorised to 128-bit accesses where
+// alignment allows; every reduction across blocks is two-phase (partials to a
+// scratch buffer, then a fixed-order sum) so results are deterministic.
+#include <math.h>
+
+#include "common.h"
+
+namespace {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void raise_flag(int *flag, int code, int a, int b) {
+  if (atomicCAS(flag, 0, code) == 0) {
+    flag[1] = a;
+    flag[2] = b;
+  }
+}
+
+// ---- activations (exact-erf GELU as in crates/tynx/src/interpreter/unary.rs:234) --------
+__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_grad(float x) {
+  float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+  float pdf = expf(-0.5f * x * x) * 0.39894228040143268f;
+  return cdf + x * pdf;
+}
+
+__device__ __forceinline__ float unary_f(int op, float x, float a, float b) {
+  switch (op) {
+    case TX_UN_NEG: return -x;
+    case TX_UN_EXP: return expf(x);
+    case TX_UN_LOG: return logf(x);
+    case TX_UN_RELU: return x > 0.f ? x : 0.f;
+    case TX_UN_TANH: return tanhf(x);
+    case TX_UN_GELU: return gelu_f(x);
+    case TX_UN_SIGMOID: return 1.0f / (1.0f + expf(-x));
+    case TX_UN_CLAMP: return fminf(fmaxf(x, a), b);
+    case TX_UN_SQRT: return sqrtf(x);
+    case TX_UN_ABS: return fabsf(x);
+    case TX_UN_SCALE: return a * x + b;
+    case TX_UN_POW: return powf(x, a);
+  }
+  return x;
+}
+
+// derivative factor; `s` is the saved forward output for EXP/TANH/SIGMOID/RELU
+// and the forward input otherwise
+__device__ __forceinline__ float unary_grad(int op, float s, float a, float b) {
+  switch (op) {
+    case TX_UN_NEG: return -1.f;
+    case TX_UN_EXP: return s;
+    case TX_UN_LOG: return 1.0f / s;
+    case TX_UN_RELU: return s > 0.f ? 1.f : 0.f;
+    case TX_UN_TANH: return 1.f - s * s;
+    case TX_UN_GELU: return gelu_grad(s);
+    case TX_UN_SIGMOID: return s * (1.f - s);
+    case TX_UN_CLAMP: return (s >= a && s <= b) ? 1.f : 0.f;
+    case TX_UN_SQRT: return 0.5f / sqrtf(s);
+    case TX_UN_ABS: return s > 0.f ? 1.f : (s < 0.f ? -1.f : 0.f);
+    case TX_UN_SCALE: return a;
+    case TX_UN_POW: return a * powf(s, a - 1.f);
+  }
+  return 1.f;
+}
+
+__global__ void k_fill(float *y, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = v;
+}
+
+__global__ void k_unary(int op, const float *__restrict__ x, float *__restrict__ y, int64_t n,
+                        float a, float b) {
+  int64_t n4 = n >> 2;
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  float4 *y4 = reinterpret_cast<float4 *>(y);
+  bool vec = ((((uintptr_t)x) | ((uintptr_t)y)) & 15) == 0;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t start = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (vec) {
+    for (int64_t i = start; i < n4; i += stride) {
+      float4 v = x4[i];
+      v.x = unary_f(op, v.x, a, b);
+      v.y = unary_f(op, v.y, a, b);
+      v.z = unary_f(op, v.z, a, b);
+      v.w = unary_f(op, v.w, a, b);
+      y4[i] = v;
+    }
+    for (int64_t i = (n4 << 2) + start; i < n; i += stride) y[i] = unary_f(op, x[i], a, b);
+  } else {
+    for (int64_t i = start; i < n; i += stride) y[i] = unary_f(op, x[i], a, b);
+  }
+}
+
+__global__ void k_unary_bwd(int op, const float *__restrict__ s, const float *__restrict__ dy,
+                            float *__restrict__ dx, int64_t n, float a, float b, int acc) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float g = dy[i] * unary_grad(op, s[i], a, b);
+    dx[i] = acc ? dx[i] + g : g;
+  }
+}
+
+struct Dims {
+  int64_t shape[TX_MAX_DIMS];
+  int64_t sa[TX_MAX_DIMS];
+  int64_t sb[TX_MAX_DIMS];
+};
+
+__device__ __forceinline__ float binary_f(int op, float a, float b) {
+  switch (op) {
+    case TX_BIN_ADD: return a + b;
+    case TX_BIN_SUB: return a - b;
+    case TX_BIN_MUL: return a * b;
+    case TX_BIN_DIV: return a / b;
+    case TX_BIN_MIN: return a <= b ? a : b;
+    case TX_BIN_MAX: return a >= b ? a : b;
+    case TX_BIN_LE: return a <= b ? 1.f : 0.f;
+    case TX_BIN_GE: return a >= b ? 1.f : 0.f;
+    case TX_BIN_POW: return powf(a, b);
+  }
+  return 0.f;
+}
+
+__global__ void k_binary(int op, const float *__restrict__ A, const float *__restrict__ B,
+                         float *__restrict__ out, Dims d, int ndim, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, oa = 0, ob = 0;
+    for (int k = ndim - 1; k >= 0; --k) {
+      int64_t c = rem % d.shape[k];
+      rem /= d.shape[k];
+      oa += c * d.sa[k];
+      ob += c * d.sb[k];
+    }
+    out[i] = binary_f(op, A[oa], B[ob]);
+  }
+}
+
+__global__ void k_binary_same(int op, const float *__restrict__ A, const float *__restrict__ B,
+                              float *__restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = binary_f(op, A[i], B[i]);
+}
+
+// Reduction of x (shape `in`) to `out` (same rank, 1 on reduced axes).
+struct RDims {
+  int64_t in[TX_MAX_DIMS];
+  int64_t out[TX_MAX_DIMS];
+  int64_t in_stride[TX_MAX_DIMS];
+};
+
+__device__ __forceinline__ int64_t out_to_in_base(const RDims &d, int ndim, int64_t o) {
+  int64_t base = 0;
+  for (int k = ndim - 1; k >= 0; --k) {
+    int64_t c = o % d.out[k];
+    o /= d.out[k];
+    base += c * d.in_stride[k];
+  }
+  return base;
+}
+
+__device__ __forceinline__ int64_t red_offset(const RDims &d, int ndim, int64_t r) {
+  int64_t off = 0;
+  for (int k = ndim - 1; k >= 0; --k) {
+    if (d.out[k] == 1 && d.in[k] > 1) {
+      int64_t c = r % d.in[k];
+      r /= d.in[k];
+      off += c * d.in_stride[k];
+    }
+  }
+  return off;
+}
+
+// one thread per output element
+__global__ void k_reduce_thread(const float *__restrict__ x, float *__restrict__ y, RDims d,
+                                int ndim, int64_t n_out, int64_t n_red, float scale, int acc) {
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < n_out;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    int64_t base = out_to_in_base(d, ndim, o);
+    float s = 0.f;
+    for (int64_t r = 0; r < n_red; ++r) s += x[base + red_offset(d, ndim, r)];
+    s *= scale;
+    y[o] = acc ? y[o] + s : s;
+  }
+}
+
+// one block per output element (tree reduction)
+__global__ void k_reduce_block(const float *__restrict__ x, float *__restrict__ y, RDims d,
+                               int ndim, int64_t n_out, int64_t n_red, float scale, int acc) {
+  __shared__ float part[32];
+  for (int64_t o = blockIdx.x; o < n_out; o += gridDim.x) {
+    int64_t base = out_to_in_base(d, ndim, o);
+    float s = 0.f;
+    for (int64_t r = threadIdx.x; r < n_red; r += blockDim.x) s += x[base + red_offset(d, ndim, r)];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) {
+        v *= scale;
+        y[o] = acc ? y[o] + v : v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+struct CDims {
+  int64_t shape[TX_MAX_DIMS];
+  int64_t ss[TX_MAX_DIMS];
+};
+
+template <typename T>
+__global__ void k_strided_copy(const T *__restrict__ src, T *__restrict__ dst, CDims d, int ndim,
+                               int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, off = 0;
+    for (int k = ndim - 1; k >= 0; --k) {
+      int64_t c = rem % d.shape[k];
+      rem /= d.shape[k];
+      off += c * d.ss[k];
+    }
+    dst[i] = src[off];
+  }
+}
+
+// ---- softmax over the last axis: one warp per row ---------------------------------
+__global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
+                              int64_t cols, int log_mode) {
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  int lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
+       r += warps) {
+    const float *xr = x + r * cols;
+    float *yr = y + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = lane; c < cols; c += kWarp) m = fmaxf(m, xr[c]);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) s += expf(xr[c] - m);
+    s = warp_sum(s);
+    if (log_mode) {
+      float lse = logf(s);
+      for (int64_t c = lane; c < cols; c += kWarp) yr[c] = (xr[c] - m) - lse;
+    } else {
+      float inv = 1.0f / s;
+      for (int64_t c = lane; c < cols; c += kWarp) yr[c] = expf(xr[c] - m) * inv;
+    }
+  }
+}
+
+__global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restrict__ dy,
+                              float *__restrict__ dx, int64_t rows, int64_t cols, int log_mode,
+                              int acc) {
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  int lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
+       r += warps) {
+    const float *yr = y + r * cols;
+    const float *gr = dy + r * cols;
+    float *dr = dx + r * cols;
+    float s = 0.f;
+    if (log_mode) {
+      for (int64_t c = lane; c < cols; c += kWarp) s += gr[c];
+    } else {
+      for (int64_t c = lane; c < cols; c += kWarp) s += gr[c] * yr[c];
+    }
+    s = warp_sum(s);
+    for (int64_t c = lane; c < cols; c += kWarp) {
+      float g = log_mode ? gr[c] - expf(yr[c]) * s : yr[c] * (gr[c] - s);
+      dr[c] = acc ? dr[c] + g : g;
+    }
+  }
+}
+
+// ---- fused softmax cross-entropy ----------------------------------------------------
+// phase 1: per-row loss = logsumexp(z) - z[y]
+__global__ void k_xent_rows(const float *__restrict__ z, const int64_t *__restrict__ labels,
+                            float *__restrict__ row_loss, int64_t rows, int64_t cols, int *flag) {
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  int lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
+       r += warps) {
+    const float *zr = z + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = lane; c < cols; c += kWarp) m = fmaxf(m, zr[c]);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) s += expf(zr[c] - m);
+    s = warp_sum(s);
+    if (lane == 0) {
+      int64_t y = labels[r];
+      if (y < 0 || y >= cols) {
+        raise_flag(flag, DEVERR_LABEL, (int)y, (int)cols);
+        row_loss[r] = 0.f;
+      } else {
+        // -log_softmax(z)[y] = -( (z_y - m) - log(s) )
+        row_loss[r] = -((zr[y] - m) - logf(s));
+      }
+    }
+  }
+}
+
+// phase 2: fixed-order mean over rows (single block)
+__global__ void k_mean_rows(const float *__restrict__ v, int64_t n, float *__restrict__ out) {
+  __shared__ float part[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) out[0] = t / (float)n;
+  }
+}
+
+__global__ void k_xent_bwd(const float *__restrict__ z, const int64_t *__restrict__ labels,
+                           const float *__restrict__ scale_ptr, float *__restrict__ dz,
+                           int64_t rows, int64_t cols, int acc) {
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  int lane = threadIdx.x & 31;
+  float scale = (scale_ptr ? scale_ptr[0] : 1.f) / (float)rows;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
+       r += warps) {
+    const float *zr = z + r * cols;
+    float *dr = dz + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = lane; c < cols; c += kWarp) m = fmaxf(m, zr[c]);
+    m = warp_max(m);
+    float s = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) s += expf(zr[c] - m);
+    s = warp_sum(s);
+    float inv = 1.0f / s;
+    int64_t y = labels[r];
+    for (int64_t c = lane; c < cols; c += kWarp) {
+      float p = expf(zr[c] - m) * inv;
+      float g = scale * (p - (c == y ? 1.f : 0.f));
+      dr[c] = acc ? dr[c] + g : g;
+    }
+  }
+}
+
+// ---- LayerNorm over trailing `cols` (normalization.rs:135-190) ---------------------------
+__global__ void k_layernorm_fwd(const float *__restrict__ x, const float *__restrict__ gamma,
+                                const float *__restrict__ beta, float *__restrict__ y,
+                                float *__restrict__ mean_out, float *__restrict__ rstd_out,
+                                int64_t rows, int64_t cols, float eps) {
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  int lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
+       r += warps) {
+    const float *xr = x + r * cols;
+    float s = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) s += xr[c];
+    float mu = warp_sum(s) / (float)cols;
+    float q = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) {
+      float d = xr[c] - mu;
+      q += d * d;
+    }
+    float var = warp_sum(q) / (float)cols;
+    float rstd = 1.0f / sqrtf(var + eps);  // (var + eps)^(-1/2)
+    float *yr = y + r * cols;
+    for (int64_t c = lane; c < cols; c += kWarp) {
+      float v = (xr[c] - mu) * rstd * gamma[c];
+      yr[c] = beta ? v + beta[c] : v;
+    }
+    if (lane == 0) {
+      if (mean_out) mean_out[r] = mu;
+      if (rstd_out) rstd_out[r] = rstd;
+    }
+  }
+}
+
+// dx per row; per-block partial column sums of dy*xhat and dy for dgamma/dbeta
+__global__ void k_layernorm_bwd(const float *__restrict__ x, const float *__restrict__ gamma,
+                                const float *__restrict__ mean_in, const float *__restrict__ rstd_in,
+                                const float *__restrict__ dy, float *__restrict__ dx,
+                                float *__restrict__ part_g, float *__restrict__ part_b, int64_t rows,
+                                int64_t cols, int acc_dx) {
+  extern __shared__ float sm[];  // [warps][cols] for dgamma partial, then dbeta partial
+  int nw = blockDim.x / kWarp;
+  int w = threadIdx.x / kWarp;
+  int lane = threadIdx.x & 31;
+  float *pg = sm;
+  float *pb = sm + (int64_t)nw * cols;
+  for (int64_t c = lane; c < cols; c += kWarp) {
+    pg[w * cols + c] = 0.f;
+    pb[w * cols + c] = 0.f;
+  }
+  for (int64_t r = blockIdx.x * (int64_t)nw + w; r < rows; r += (int64_t)gridDim.x * nw) {
+    const float *xr = x + r * cols;
+    const float *gr = dy + r * cols;
+    float mu = mean_in[r], rs = rstd_in[r];
+    float s1 = 0.f, s2 = 0.f;
+    for (int64_t c = lane; c < cols; c += kWarp) {
+      float xh = (xr[c] - mu) * rs;
+      float g = gr[c] * gamma[c];
+      s1 += g;
+      s2 += g * xh;
+      pg[w * cols + c] += gr[c] * xh;
+      pb[w * cols + c] += gr[c];
+    }
+    s1 = warp_sum(s1) / (float)cols;
+    s2 = warp_sum(s2) / (float)cols;
+    if (dx) {
+      float *dr = dx + r * cols;
+      for (int64_t c = lane; c < cols; c += kWarp) {
+        float xh = (xr[c] - mu) * rs;
+        float v = rs * (gr[c] * gamma[c] - s1 - xh * s2);
+        dr[c] = acc_dx ? dr[c] + v : v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    float a = 0.f, b = 0.f;
+    for (int i = 0; i < nw; ++i) {
+      a += pg[i * cols + c];
+      b += pb[i * cols + c];
+    }
+    part_g[blockIdx.x * cols + c] = a;
+    part_b[blockIdx.x * cols + c] = b;
+  }
+}
+
+// out[c] (+)= scale * sum_p part[p, c]   (fixed order)
+__global__ void k_sum_partials(const float *__restrict__ part, int64_t np, int64_t cols,
+                               float *__restrict__ out, float scale, int acc) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int64_t p = 0; p < np; ++p) s += part[p * cols + c];
+    s *= scale;
+    out[c] = acc ? out[c] + s : s;
+  }
+}
+
+// ---- gather / scatter (gather.rs:18-58; select / select_assign) -------------------------
+__global__ void k_gather_rows(const float *__restrict__ table, int64_t rows, int64_t width,
+                              const int64_t *__restrict__ idx, int64_t n, float *__restrict__ out,
+                              int *flag) {
+  int64_t total = n * width;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / width, c = i - r * width;
+    int64_t k = idx[r];
+    if (k < 0) k += rows;
+    if (k < 0 || k >= rows) {
+      if (c == 0) raise_flag(flag, DEVERR_INDEX, (int)idx[r], (int)rows);
+      out[i] = 0.f;
+    } else {
+      out[i] = table[k * width + c];
+    }
+  }
+}
+
+__global__ void k_gather_rows4(const float4 *__restrict__ table, int64_t rows, int64_t w4,
+                               const int64_t *__restrict__ idx, int64_t n, float4 *__restrict__ out,
+                               int *flag) {
+  int64_t total = n * w4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / w4, c = i - r * w4;
+    int64_t k = idx[r];
+    if (k < 0) k += rows;
+    if (k < 0 || k >= rows) {
+      if (c == 0) raise_flag(flag, DEVERR_INDEX, (int)idx[r], (int)rows);
+      out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      out[i] = table[k * w4 + c];
+    }
+  }
+}
+
+__global__ void k_scatter_add_rows(float *__restrict__ table, int64_t rows, int64_t width,
+                                   const int64_t *__restrict__ idx, int64_t n,
+                                   const float *__restrict__ src) {
+  int64_t total = n * width;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / width, c = i - r * width;
+    int64_t k = idx[r];
+    if (k < 0) k += rows;
+    if (k >= 0 && k < rows) atomicAdd(&table[k * width + c], src[i]);
+  }
+}
+
+__global__ void k_take_last(const float *__restrict__ x, const int64_t *__restrict__ idx,
+                            float *__restrict__ out, int64_t rows, int64_t cols, int *flag) {
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k = idx[r];
+    if (k < 0) k += cols;
+    if (k < 0 || k >= cols) {
+      raise_flag(flag, DEVERR_INDEX, (int)idx[r], (int)cols);
+      out[r] = 0.f;
+    } else {
+      out[r] = x[r * cols + k];
+    }
+  }
+}
+
+__global__ void k_take_last_bwd(const int64_t *__restrict__ idx, const float *__restrict__ dout,
+                                float *__restrict__ dx, int64_t rows, int64_t cols, int acc) {
+  int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / cols, c = i - r * cols;
+    int64_t k = idx[r];
+    if (k < 0) k += cols;
+    float g = (c == k) ? dout[r] : 0.f;
+    dx[i] = acc ? dx[i] + g : g;
+  }
+}
+
+// ---- column sums (bias gradient) --------------------------------------------------------
+// block (32, 8): 32 columns x 8 row lanes, rows [blockIdx.y*rows_per, ...)
+__global__ void k_colsum_partial(const float *__restrict__ dy, int64_t M, int64_t N,
+                                 int64_t rows_per, float *__restrict__ part) {
+  __shared__ float sm[8][33];
+  int64_t c = blockIdx.x * 32 + threadIdx.x;
+  int64_t r0 = blockIdx.y * rows_per;
+  int64_t r1 = r0 + rows_per < M ? r0 + rows_per : M;
+  float s = 0.f;
+  if (c < N)
+    for (int64_t r = r0 + threadIdx.y; r < r1; r += 8) s += dy[r * N + c];
+  sm[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += sm[i][threadIdx.x];
+    part[blockIdx.y * N + c] = t;
+  }
+}
+
+// ---- multi-tensor optimizers (adam.rs:431-527, optimizer.rs:310-356) ---------------------
+struct OptTensor {
+  float *w;
+  const float *g;
+  float *m;
+  float *v;
+  float *vmax;
+  int64_t n;
+};
+struct OptChunk {
+  int32_t tensor;
+  int64_t start, len;
+};
+struct OptHparams {
+  float lr, beta1, beta2, eps, wd, one_minus_b1, one_minus_b2, decay_factor;
+  double beta1_d, beta2_d;
+  float momentum, one_minus_dampening;
+};
+
+// Adam / AdamW: one block per chunk.  Step counters: t = steps[i] + 1 for the
+// math; the last block to finish (atomic ticket) commits the increments.
+__global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__restrict__ chunks,
+                       int n_chunks, const OptHparams *__restrict__ hp_ptr, int64_t *steps,
+                       const int32_t *__restrict__ active_list, int n_active, int kind,
+                       int amsgrad, unsigned *ticket) {
+  const OptHparams hp = *hp_ptr;
+  const OptChunk ch = chunks[blockIdx.x];
+  const OptTensor t = tensors[ch.tensor];
+  const int64_t step = steps[ch.tensor] + 1;
+  // bias corrections in double, rounded to f32 like mul_scalar/div_scalar(f64) on f32 data
+  const float bc1 = (float)(1.0 - pow(hp.beta1_d, (double)step));
+  const float bc2 = (float)(1.0 - pow(hp.beta2_d, (double)step));
+  const bool coupled = (kind == 0) && hp.wd != 0.f;
+  const bool decoupled = (kind == 1) && hp.wd != 0.f;
+  for (int64_t i = ch.start + threadIdx.x; i < ch.start + ch.len; i += blockDim.x) {
+    float w = t.w[i];
+    float d = t.g[i];
+    if (coupled) d = __fadd_rn(d, __fmul_rn(w, hp.wd));
+    float m = __fadd_rn(__fmul_rn(t.m[i], hp.beta1), __fmul_rn(d, hp.one_minus_b1));
+    float v = __fadd_rn(__fmul_rn(t.v[i], hp.beta2), __fmul_rn(__fmul_rn(d, d), hp.one_minus_b2));
+    float den = v;
+    if (amsgrad) {
+      den = fmaxf(t.vmax[i], v);
+      t.vmax[i] = den;
+    }
+    float mh = __fdiv_rn(m, bc1);
+    float vh = __fdiv_rn(den, bc2);
+    float upd = __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), hp.eps)), hp.lr);
+    if (decoupled) w = __fmul_rn(w, hp.decay_factor);
+    t.w[i] = __fsub_rn(w, upd);
+    t.m[i] = m;
+    t.v[i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned done = atomicAdd(ticket, 1u);
+    if (done == (unsigned)n_chunks - 1) {
+      for (int i = 0; i < n_active; ++i) steps[active_list[i]] += 1;
+      __threadfence();
+      *ticket = 0u;
+    }
+  }
+}
+
+__global__ void k_sgd(const OptTensor *__restrict__ tensors, const OptChunk *__restrict__ chunks,
+                      const OptHparams *__restrict__ hp_ptr, int64_t *steps, int n_chunks,
+                      const int32_t *__restrict__ active_list, int n_active, int nesterov,
+                      unsigned *ticket) {
+  const OptHparams hp = *hp_ptr;
+  const OptChunk ch = chunks[blockIdx.x];
+  const OptTensor t = tensors[ch.tensor];
+  const bool first = steps[ch.tensor] == 0;
+  for (int64_t i = ch.start + threadIdx.x; i < ch.start + ch.len; i += blockDim.x) {
+    float w = t.w[i];
+    float d = t.g[i];
+    if (hp.wd != 0.f) d = __fadd_rn(d, __fmul_rn(w, hp.wd));
+    if (hp.momentum != 0.f) {
+      float buf = first ? d
+                        : __fadd_rn(__fmul_rn(t.m[i], hp.momentum), __fmul_rn(d, hp.one_minus_dampening));
+      t.m[i] = buf;
+      d = nesterov ? __fadd_rn(d, __fmul_rn(buf, hp.momentum)) : buf;
+    }
+    t.w[i] = __fsub_rn(w, __fmul_rn(d, hp.lr));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned done = atomicAdd(ticket, 1u);
+    if (done == (unsigned)n_chunks - 1) {
+      for (int i = 0; i < n_active; ++i) steps[active_list[i]] += 1;
+      __threadfence();
+      *ticket = 0u;
+    }
+  }
+}
+
+}  // namespace
+
+// ============================================================================
+// host entry points
+// ============================================================================
+static inline unsigned rows_grid(int64_t rows, int warps_per_block) {
+  int64_t b = (rows + warps_per_block - 1) / warps_per_block;
+  if (b < 1) b = 1;
+  if (b > 148 * 32) b = 148 * 32;
+  return (unsigned)b;
+}
+
+extern "C" int tx_fill_f32(tx_ctx *ctx, float *y, int64_t n, float v) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (n <= 0) return TX_OK;
+  k_fill<<<grid_for(n, 256), 256, 0, ctx->stream>>>(y, n, v);
+  TX_LAUNCHED(ctx, "k_fill");
+  return TX_OK;
+}
+
+extern "C" int tx_unary(tx_ctx *ctx, int op, const float *x, float *y, int64_t n, float a, float b) {
+  if (!ctx || op < 0 || op > TX_UN_POW) return TX_ERR_INVALID;
+  if (n <= 0) return TX_OK;
+  k_unary<<<grid_for((n + 3) / 4, 256), 256, 0, ctx->stream>>>(op, x, y, n, a, b);
+  TX_LAUNCHED(ctx, "k_unary");
+  return TX_OK;
+}
+
+extern "C" int tx_unary_bwd(tx_ctx *ctx, int op, const float *s, const float *dy, float *dx,
+                            int64_t n, float a, float b, int acc) {
+  if (!ctx || op < 0 || op > TX_UN_POW) return TX_ERR_INVALID;
+  if (n <= 0) return TX_OK;
+  k_unary_bwd<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, s, dy, dx, n, a, b, acc);
+  TX_LAUNCHED(ctx, "k_unary_bwd");
+  return TX_OK;
+}
+
+extern "C" int tx_binary(tx_ctx *ctx, int op, const float *A, const int64_t *sa, const float *B,
+                         const int64_t *sb, float *out, const int64_t *shape, int ndim) {
+  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS || op < 0 || op > TX_BIN_POW) return TX_ERR_INVALID;
+  int64_t n = 1;
+  bool contiguous = true;
+  int64_t expect = 1;
+  for (int k = ndim - 1; k >= 0; --k) {
+    if (sa[k] != expect && shape[k] != 1) contiguous = false;
+    if (sb[k] != expect && shape[k] != 1) contiguous = false;
+    expect *= shape[k];
+  }
+  for (int k = 0; k < ndim; ++k) n *= shape[k];
+  if (n <= 0) return TX_OK;
+  if (contiguous) {
+    k_binary_same<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, A, B, out, n);
+  } else {
+    Dims d;
+    for (int k = 0; k < ndim; ++k) {
+      d.shape[k] = shape[k];
+      d.sa[k] = sa[k];
+      d.sb[k] = sb[k];
+    }
+    k_binary<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, A, B, out, d, ndim, n);
+  }
+  TX_LAUNCHED(ctx, "k_binary");
+  return TX_OK;
+}
+
+extern "C" int tx_reduce_to(tx_ctx *ctx, const float *x, const int64_t *in_shape, float *y,
+                            const int64_t *out_shape, int ndim, int mean, int acc) {
+  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS) return TX_ERR_INVALID;
+  RDims d;
+  int64_t n_out = 1, n_red = 1, stride = 1;
+  for (int k = ndim - 1; k >= 0; --k) {
+    d.in[k] = in_shape[k];
+    d.out[k] = out_shape[k];
+    d.in_stride[k] = stride;
+    stride *= in_shape[k];
+    if (out_shape[k] != in_shape[k] && out_shape[k] != 1)
+      return tx_fail(ctx, TX_ERR_SHAPE, "tx_reduce_to: output extent must equal input or be 1");
+    n_out *= out_shape[k];
+    if (out_shape[k] == 1) n_red *= in_shape[k];
+  }
+  if (n_out <= 0) return TX_OK;
+  float scale = mean ? 1.0f / (float)(n_red > 0 ? n_red : 1) : 1.0f;
+  if (n_out >= 4096 || n_red <= 32) {
+    k_reduce_thread<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(x, y, d, ndim, n_out, n_red,
+                                                                   scale, acc);
+  } else {
+    unsigned blocks = n_out < 148 * 8 ? (unsigned)n_out : 148 * 8;
+    k_reduce_block<<<blocks, 256, 0, ctx->stream>>>(x, y, d, ndim, n_out, n_red, scale, acc);
+  }
+  TX_LAUNCHED(ctx, "k_reduce");
+  return TX_OK;
+}
+
+extern "C" int tx_strided_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *dst,
+                               const int64_t *shape, int ndim, int elem_bytes) {
+  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS) return TX_ERR_INVALID;
+  CDims d;
+  int64_t n = 1;
+  for (int k = 0; k < ndim; ++k) {
+    d.shape[k] = shape[k];
+    d.ss[k] = ss[k];
+    n *= shape[k];
+  }
+  if (n <= 0) return TX_OK;
+  if (elem_bytes == 4)
+    k_strided_copy<float><<<grid_for(n, 256), 256, 0, ctx->stream>>>((const float *)src, (float *)dst, d, ndim, n);
+  else if (elem_bytes == 8)
+    k_strided_copy<int64_t><<<grid_for(n, 256), 256, 0, ctx->stream>>>((const int64_t *)src, (int64_t *)dst, d, ndim, n);
+  else
+    return TX_ERR_INVALID;
+  TX_LAUNCHED(ctx, "k_strided_copy");
+  return TX_OK;
+}
+
+extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int log) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0 || cols <= 0) return TX_OK;
+  k_softmax_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, y, rows, cols, log);
+  TX_LAUNCHED(ctx, "k_softmax_fwd");
+  return TX_OK;
+}
+
+extern "C" int tx_softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows,
+                              int64_t cols, int log, int acc) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0 || cols <= 0) return TX_OK;
+  k_softmax_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(y, dy, dx, rows, cols, log, acc);
+  TX_LAUNCHED(ctx, "k_softmax_bwd");
+  return TX_OK;
+}
+
+extern "C" int tx_softmax_xent_fwd(tx_ctx *ctx, const float *z, const int64_t *labels, int64_t rows,
+                                   int64_t cols, float *loss) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return tx_fail(ctx, TX_ERR_SHAPE, "cross entropy over zero rows");
+  Scratch rl(ctx, rows * sizeof(float));
+  if (!rl.ptr) return TX_ERR_OOM;
+  k_xent_rows<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(z, labels, rl.as<float>(), rows, cols,
+                                                         ctx->d_err);
+  TX_LAUNCHED(ctx, "k_xent_rows");
+  k_mean_rows<<<1, 1024, 0, ctx->stream>>>(rl.as<float>(), rows, loss);
+  TX_LAUNCHED(ctx, "k_mean_rows");
+  return TX_OK;
+}
+
+extern "C" int tx_softmax_xent_bwd(tx_ctx *ctx, const float *z, const int64_t *labels, int64_t rows,
+                                   int64_t cols, const float *scale, float *dz, int acc) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return TX_OK;
+  k_xent_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(z, labels, scale, dz, rows, cols, acc);
+  TX_LAUNCHED(ctx, "k_xent_bwd");
+  return TX_OK;
+}
+
+extern "C" int tx_layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta,
+                                float *y, float *mean, float *rstd, int64_t rows, int64_t cols,
+                                float eps) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return TX_OK;
+  k_layernorm_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows,
+                                                             cols, eps);
+  TX_LAUNCHED(ctx, "k_layernorm_fwd");
+  return TX_OK;
+}
+
+extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma, const float *mean,
+                                const float *rstd, const float *dy, float *dx, float *dgamma,
+                                float *dbeta, int64_t rows, int64_t cols, int acc_dx, int acc_p) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return TX_OK;
+  const int warps = 4;
+  size_t smem = 2 * (size_t)warps * cols * sizeof(float);
+  if (smem > 200 * 1024) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "LayerNorm width too large");
+  int64_t blocks = (rows + warps * 8 - 1) / (warps * 8);
+  if (blocks > ctx->num_sms * 4) blocks = ctx->num_sms * 4;
+  if (blocks < 1) blocks = 1;
+  Scratch part(ctx, 2 * blocks * cols * sizeof(float));
+  if (!part.ptr) return TX_ERR_OOM;
+  float *pg = part.as<float>();
+  float *pb = pg + blocks * cols;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_layernorm_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_layernorm_bwd<<<(unsigned)blocks, warps * 32, smem, ctx->stream>>>(x, gamma, mean, rstd, dy, dx,
+                                                                      pg, pb, rows, cols, acc_dx);
+  TX_LAUNCHED(ctx, "k_layernorm_bwd");
+  if (dgamma) {
+    k_sum_partials<<<grid_for(cols, 256), 256, 0, ctx->stream>>>(pg, blocks, cols, dgamma, 1.f, acc_p);
+    TX_LAUNCHED(ctx, "k_sum_partials");
+  }
+  if (dbeta) {
+    k_sum_partials<<<grid_for(cols, 256), 256, 0, ctx->stream>>>(pb, blocks, cols, dbeta, 1.f, acc_p);
+    TX_LAUNCHED(ctx, "k_sum_partials");
+  }
+  return TX_OK;
+}
+
+extern "C" int tx_gather_rows(tx_ctx *ctx, const float *table, int64_t rows, int64_t width,
+                              const int64_t *idx, int64_t n, float *out) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (n <= 0 || width <= 0) return TX_OK;
+  bool vec = (width % 4 == 0) && ((((uintptr_t)table) | ((uintptr_t)out)) & 15) == 0;
+  if (vec) {
+    k_gather_rows4<<<grid_for(n * width / 4, 256), 256, 0, ctx->stream>>>(
+        (const float4 *)table, rows, width / 4, idx, n, (float4 *)out, ctx->d_err);
+  } else {
+    k_gather_rows<<<grid_for(n * width, 256), 256, 0, ctx->stream>>>(table, rows, width, idx, n, out,
+                                                                    ctx->d_err);
+  }
+  TX_LAUNCHED(ctx, "k_gather_rows");
+  return TX_OK;
+}
+
+extern "C" int tx_scatter_add_rows(tx_ctx *ctx, float *table, int64_t rows, int64_t width,
+                                   const int64_t *idx, int64_t n, const float *src) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (n <= 0 || width <= 0) return TX_OK;
+  k_scatter_add_rows<<<grid_for(n * width, 256), 256, 0, ctx->stream>>>(table, rows, width, idx, n, src);
+  TX_LAUNCHED(ctx, "k_scatter_add_rows");
+  return TX_OK;
+}
+
+extern "C" int tx_take_last(tx_ctx *ctx, const float *x, const int64_t *idx, float *out,
+                            int64_t rows, int64_t cols) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return TX_OK;
+  k_take_last<<<grid_for(rows, 256), 256, 0, ctx->stream>>>(x, idx, out, rows, cols, ctx->d_err);
+  TX_LAUNCHED(ctx, "k_take_last");
+  return TX_OK;
+}
+
+extern "C" int tx_take_last_bwd(tx_ctx *ctx, const int64_t *idx, const float *dout, float *dx,
+                                int64_t rows, int64_t cols, int acc) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return TX_OK;
+  k_take_last_bwd<<<grid_for(rows * cols, 256), 256, 0, ctx->stream>>>(idx, dout, dx, rows, cols, acc);
+  TX_LAUNCHED(ctx, "k_take_last_bwd");
+  return TX_OK;
+}
+
+extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, int64_t N,
+                            float scale, int acc) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (N <= 0) return TX_OK;
+  if (M <= 0) {
+    if (!acc) TX_CUDA(ctx, cudaMemsetAsync(db, 0, N * sizeof(float), ctx->stream));
+    return TX_OK;
+  }
+  // split the rows so that the grid fills the machine
+  int64_t col_blocks = (N + 31) / 32;
+  int64_t splits = (ctx->num_sms * 4 + col_blocks - 1) / col_blocks;
+  int64_t max_splits = (M + 63) / 64;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  if (splits > 65535) splits = 65535;
+  int64_t rows_per = (M + splits - 1) / splits;
+  Scratch part(ctx, splits * N * sizeof(float));
+  if (!part.ptr) return TX_ERR_OOM;
+  k_colsum_partial<<<dim3((unsigned)col_blocks, (unsigned)splits), dim3(32, 8), 0, ctx->stream>>>(
+      dy, M, N, rows_per, part.as<float>());
+  TX_LAUNCHED(ctx, "k_colsum_partial");
+  k_sum_partials<<<grid_for(N, 256), 256, 0, ctx->stream>>>(part.as<float>(), splits, N, db, scale, acc);
+  TX_LAUNCHED(ctx, "k_sum_partials");
+  return TX_OK;
+}
+
+// ----------------------------------------------------------------------------
+// optimizers
+// ----------------------------------------------------------------------------
+struct tx_optim {
+  tx_ctx *ctx;
+  tx_optim_cfg cfg;
+  int n;
+  std::vector<OptTensor> host_tensors;
+  OptTensor *d_tensors = nullptr;
+  int64_t *d_steps = nullptr;
+  OptHparams *d_hp = nullptr;
+  unsigned *d_ticket = nullptr;
+  std::vector<float *> state;  // m, v, vmax per tensor (SGD: momentum in m)
+  // chunk tables keyed by active mask
+  std::map<std::vector<uint8_t>, std::pair<OptChunk *, int>> tables;
+  std::map<std::vector<uint8_t>, std::pair<int32_t *, int>> active_lists;
+};
+
+static const int64_t kChunk = 8192;
+static int build_table(tx_optim *o, const std::vector<uint8_t> &key);
+
+static int upload_hparams(tx_optim *o) {
+  if (o->ctx->capturing)
+    return tx_fail(o->ctx, TX_ERR_CAPTURE,
+                   "optimizer hyper-parameters cannot change while a step is being captured");
+  OptHparams h;
+  const tx_optim_cfg &c = o->cfg;
+  h.lr = (float)c.lr;
+  h.beta1 = (float)c.beta1;
+  h.beta2 = (float)c.beta2;
+  h.eps = (float)c.eps;
+  h.wd = (float)c.weight_decay;
+  h.one_minus_b1 = (float)(1.0 - c.beta1);
+  h.one_minus_b2 = (float)(1.0 - c.beta2);
+  h.decay_factor = (float)(1.0 - c.lr * c.weight_decay);
+  h.beta1_d = c.beta1;
+  h.beta2_d = c.beta2;
+  h.momentum = (float)c.momentum;
+  h.one_minus_dampening = (float)(1.0 - c.dampening);
+  // stream-ordered after earlier steps that read the old values
+  TX_CUDA(o->ctx, cudaMemcpyAsync(o->d_hp, &h, sizeof h, cudaMemcpyHostToDevice, o->ctx->stream));
+  TX_CUDA(o->ctx, cudaStreamSynchronize(o->ctx->stream));
+  return TX_OK;
+}
+
+extern "C" int tx_optim_create(tx_ctx *ctx, const tx_optim_cfg *cfg, int n, float *const *values,
+                               float *const *grads, const int64_t *numel, tx_optim **out) {
+  if (!ctx || !cfg || !out || n <= 0) return TX_ERR_INVALID;
+  if (ctx->capturing) return tx_fail(ctx, TX_ERR_CAPTURE, "optimizer creation is not capturable");
+  tx_optim *o = new tx_optim();
+  o->ctx = ctx;
+  o->cfg = *cfg;
+  o->n = n;
+  for (int i = 0; i < n; ++i) {
+    OptTensor t{values[i], grads[i], nullptr, nullptr, nullptr, numel[i]};
+    size_t bytes = numel[i] * sizeof(float);
+    int nstate = cfg->kind == 2 ? (cfg->momentum != 0.0 ? 1 : 0) : (cfg->amsgrad ? 3 : 2);
+    float *bufs[3] = {nullptr, nullptr, nullptr};
+    for (int s = 0; s < nstate; ++s) {
+      if (cudaMalloc(&bufs[s], bytes ? bytes : 4) != cudaSuccess) {
+        delete o;
+        return tx_fail(ctx, TX_ERR_OOM, "optimizer state allocation failed");
+      }
+      cudaMemsetAsync(bufs[s], 0, bytes ? bytes : 4, ctx->stream);
+    }
+    t.m = bufs[0];
+    t.v = bufs[1];
+    t.vmax = bufs[2];
+    o->state.push_back(bufs[0]);
+    o->state.push_back(bufs[1]);
+    o->state.push_back(bufs[2]);
+    o->host_tensors.push_back(t);
+  }
+  TX_CUDA(ctx, cudaMalloc(&o->d_tensors, n * sizeof(OptTensor)));
+  TX_CUDA(ctx, cudaMalloc(&o->d_steps, n * sizeof(int64_t)));
+  TX_CUDA(ctx, cudaMalloc(&o->d_hp, sizeof(OptHparams)));
+  TX_CUDA(ctx, cudaMalloc(&o->d_ticket, sizeof(unsigned)));
+  TX_CUDA(ctx, cudaMemcpyAsync(o->d_tensors, o->host_tensors.data(), n * sizeof(OptTensor),
+                               cudaMemcpyHostToDevice, ctx->stream));
+  TX_CUDA(ctx, cudaMemsetAsync(o->d_steps, 0, n * sizeof(int64_t), ctx->stream));
+  TX_CUDA(ctx, cudaMemsetAsync(o->d_ticket, 0, sizeof(unsigned), ctx->stream));
+  int rc = upload_hparams(o);
+  if (rc) {
+    delete o;
+    return rc;
+  }
+  *out = o;
+  // the chunk table for "every tensor has a gradient" is built up front so a
+  // captured step never has to create one
+  std::vector<uint8_t> all(n, 1);
+  return build_table(o, all);
+}
+
+extern "C" int tx_optim_set_hparams(tx_optim *o, const tx_optim_cfg *cfg) {
+  if (!o || !cfg) return TX_ERR_INVALID;
+  if (cfg->kind != o->cfg.kind || cfg->amsgrad != o->cfg.amsgrad)
+    return tx_fail(o->ctx, TX_ERR_INVALID, "optimizer kind and amsgrad cannot change");
+  o->cfg = *cfg;
+  return upload_hparams(o);
+}
+
+extern "C" int tx_optim_set_lr(tx_optim *o, double lr) {
+  if (!o) return TX_ERR_INVALID;
+  o->cfg.lr = lr;
+  return upload_hparams(o);
+}
+
+static int build_table(tx_optim *o, const std::vector<uint8_t> &key) {
+  tx_ctx *ctx = o->ctx;
+  const uint8_t *active = key.data();
+  {
+    std::vector<OptChunk> chunks;
+    std::vector<int32_t> list;
+    for (int i = 0; i < o->n; ++i) {
+      if (!active[i]) continue;
+      list.push_back(i);
+      for (int64_t s = 0; s < o->host_tensors[i].n; s += kChunk) {
+        int64_t len = o->host_tensors[i].n - s < kChunk ? o->host_tensors[i].n - s : kChunk;
+        chunks.push_back({i, s, len});
+      }
+    }
+    OptChunk *d_chunks = nullptr;
+    int32_t *d_list = nullptr;
+    if (!chunks.empty()) {
+      TX_CUDA(ctx, cudaMalloc(&d_chunks, chunks.size() * sizeof(OptChunk)));
+      TX_CUDA(ctx, cudaMalloc(&d_list, list.size() * sizeof(int32_t)));
+      TX_CUDA(ctx, cudaMemcpy(d_chunks, chunks.data(), chunks.size() * sizeof(OptChunk),
+                              cudaMemcpyHostToDevice));
+      TX_CUDA(ctx, cudaMemcpy(d_list, list.data(), list.size() * sizeof(int32_t),
+                              cudaMemcpyHostToDevice));
+    }
+    o->tables.emplace(key, std::make_pair(d_chunks, (int)chunks.size()));
+    o->active_lists[key] = {d_list, (int)list.size()};
+  }
+  return TX_OK;
+}
+
+extern "C" int tx_optim_step(tx_optim *o, const uint8_t *active) {
+  if (!o) return TX_ERR_INVALID;
+  tx_ctx *ctx = o->ctx;
+  std::vector<uint8_t> key(active, active + o->n);
+  auto it = o->tables.find(key);
+  if (it == o->tables.end()) {
+    TX_TRY(build_table(o, key));
+    it = o->tables.find(key);
+  }
+  int n_chunks = it->second.second;
+  if (n_chunks == 0) return TX_OK;
+  auto al = o->active_lists[key];
+  if (o->cfg.kind == 2) {
+    k_sgd<<<n_chunks, 256, 0, ctx->stream>>>(o->d_tensors, it->second.first, o->d_hp, o->d_steps,
+                                             n_chunks, al.first, al.second, o->cfg.nesterov,
+                                             o->d_ticket);
+  } else {
+    k_adam<<<n_chunks, 256, 0, ctx->stream>>>(o->d_tensors, it->second.first, n_chunks, o->d_hp,
+                                              o->d_steps, al.first, al.second, o->cfg.kind,
+                                              o->cfg.amsgrad, o->d_ticket);
+  }
+  TX_LAUNCHED(ctx, "optimizer step");
+  return TX_OK;
+}
+
+extern "C" int tx_optim_state_ptr(tx_optim *o, int tensor, int which, float **out) {
+  if (!o || !out || tensor < 0 || tensor >= o->n || which < 0 || which > 3) return TX_ERR_INVALID;
+  if (which == 3) which = 0;  // SGD momentum lives in slot 0
+  *out = o->state[tensor * 3 + which];
+  return *out ? TX_OK : TX_ERR_INVALID;
+}
+
+extern "C" int tx_optim_get_steps(tx_optim *o, int64_t *h) {
+  if (!o || !h) return TX_ERR_INVALID;
+  TX_CUDA(o->ctx, cudaMemcpyAsync(h, o->d_steps, o->n * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                                  o->ctx->stream));
+  TX_CUDA(o->ctx, cudaStreamSynchronize(o->ctx->stream));
+  return TX_OK;
+}
+
+extern "C" int tx_optim_set_steps(tx_optim *o, const int64_t *h) {
+  if (!o || !h) return TX_ERR_INVALID;
+  TX_CUDA(o->ctx, cudaMemcpyAsync(o->d_steps, h, o->n * sizeof(int64_t), cudaMemcpyHostToDevice,
+                                  o->ctx->stream));
+  TX_CUDA(o->ctx, cudaStreamSynchronize(o->ctx->stream));
+  return TX_OK;
+}
+
+extern "C" int tx_optim_destroy(tx_optim *o) {
+  if (!o) return TX_OK;
+  cudaStreamSynchronize(o->ctx->stream);
+  for (float *p : o->state)
+    if (p) cudaFree(p);
+  for (auto &kv : o->tables)
+    if (kv.second.first) cudaFree(kv.second.first);
+  for (auto &kv : o->active_lists)
+    if (kv.second.first) cudaFree(kv.second.first);
+  cudaFree(o->d_tensors);
+  cudaFree(o->d_steps);
+  cudaFree(o->d_hp);
+  cudaFree(o->d_ticket);
+  delete o;
+  return TX_OK;
+}
