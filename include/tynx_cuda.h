@@ -192,6 +192,19 @@ int tx_softmax_xent_fwd(tx_ctx *ctx, const float *d_logits, const int64_t *d_lab
 int tx_softmax_xent_bwd(tx_ctx *ctx, const float *d_logits, const int64_t *d_labels,
                         int64_t rows, int64_t cols, const float *d_scale, float *d_dlogits,
                         int accumulate);
+/* Same result as tx_softmax_xent_fwd, for callers that cannot allocate device
+ * memory: a host runtime that owns all of its HBM up front, or code issuing
+ * work while a CUDA graph is being captured, where an allocation would be
+ * recorded into the graph.  It has no counterpart in the reference.
+ * The per-row losses go to a fixed 1 MiB device array built into the library
+ * (held on every GPU that loads it until the process exits), so rows must be
+ * at most 262144; larger inputs fail with TX_ERR_SHAPE.  Nothing is allocated:
+ * the first call on a device looks up that array's device address (make that
+ * first call before any stream capture).  All calls share the array, so calls
+ * whose work overlaps on the GPU (other streams, other host threads) race; calls
+ * issued in order on one context's stream do not. */
+int tx_softmax_xent_fwd_noalloc(tx_ctx *ctx, const float *d_logits, const int64_t *d_labels,
+                                int64_t rows, int64_t cols, float *d_loss);
 
 /* LayerNormalization over the trailing `cols` elements of each row.
  * replaces: layer_normalization_values (crates/tynx/src/interpreter/normalization.rs:135-190). */

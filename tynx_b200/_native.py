@@ -139,6 +139,7 @@ SIGNATURES = {
     "tx_softmax_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32],
     "tx_softmax_xent_fwd": [_vp, _vp, _vp, _i64, _i64, _vp],
     "tx_softmax_xent_bwd": [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32],
+    "tx_softmax_xent_fwd_noalloc": [_vp, _vp, _vp, _i64, _i64, _vp],
     "tx_layernorm_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f],
     "tx_layernorm_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32],
     "tx_gather_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],

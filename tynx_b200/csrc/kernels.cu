@@ -8,6 +8,8 @@
 // scratch buffer, then a fixed-order sum) so results are deterministic.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.h"
 
 namespace {
@@ -796,6 +798,53 @@ extern "C" int tx_softmax_xent_fwd(tx_ctx *ctx, const float *z, const int64_t *l
                                                          ctx->d_err);
   TX_LAUNCHED(ctx, "k_xent_rows");
   k_mean_rows<<<1, 1024, 0, ctx->stream>>>(rl.as<float>(), rows, loss);
+  TX_LAUNCHED(ctx, "k_mean_rows");
+  return TX_OK;
+}
+
+// ---- allocation-free variant of tx_softmax_xent_fwd ------------------------------------
+// The per-row losses live in a fixed file-scope device array instead of memory
+// from the context allocator, for callers that must not allocate device memory.
+// Every GPU that loads this library holds the array until the process exits.
+static constexpr int64_t kXentNoAllocMaxRows = 1 << 18;  // 262144 rows = 1 MiB
+static __device__ __align__(256) float g_xent_row_losses[kXentNoAllocMaxRows];
+static float *g_xent_row_losses_addr[64] = {};  // per device, set on first use
+static std::mutex g_xent_row_losses_mutex;
+
+// The array's name is only a host-side stand-in in host code: its device
+// address is resolved once per device, with that device current.
+static int xent_noalloc_scratch(tx_ctx *ctx, float **out) {
+  if (ctx->device < 0 || ctx->device >= 64)
+    return tx_fail(ctx, TX_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_xent_row_losses_mutex);
+  if (!g_xent_row_losses_addr[ctx->device]) {
+    int previous = 0;
+    TX_CUDA(ctx, cudaGetDevice(&previous));
+    TX_CUDA(ctx, cudaSetDevice(ctx->device));
+    void *addr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&addr, g_xent_row_losses);
+    cudaSetDevice(previous);
+    if (e != cudaSuccess) return tx_cuda_fail(ctx, e, "cudaGetSymbolAddress(g_xent_row_losses)");
+    g_xent_row_losses_addr[ctx->device] = (float *)addr;
+  }
+  *out = g_xent_row_losses_addr[ctx->device];
+  return TX_OK;
+}
+
+extern "C" int tx_softmax_xent_fwd_noalloc(tx_ctx *ctx, const float *z, const int64_t *labels,
+                                           int64_t rows, int64_t cols, float *loss) {
+  if (!ctx) return TX_ERR_INVALID;
+  if (rows <= 0) return tx_fail(ctx, TX_ERR_SHAPE, "cross entropy over zero rows");
+  if (rows > kXentNoAllocMaxRows)
+    return tx_fail(ctx, TX_ERR_SHAPE,
+                   "tx_softmax_xent_fwd_noalloc handles at most 262144 rows; use tx_softmax_xent_fwd");
+  float *scratch = nullptr;
+  TX_TRY(xent_noalloc_scratch(ctx, &scratch));
+  // every row in [0, rows) is written before it is read: nothing needs clearing
+  k_xent_rows<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(z, labels, scratch, rows, cols,
+                                                         ctx->d_err);
+  TX_LAUNCHED(ctx, "k_xent_rows");
+  k_mean_rows<<<1, 1024, 0, ctx->stream>>>(scratch, rows, loss);
   TX_LAUNCHED(ctx, "k_mean_rows");
   return TX_OK;
 }
