@@ -194,7 +194,7 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--workload", default="mlp_classifier")
-    parser.add_argument("--math", default="tf32", choices=["tf32", "3xtf32", "fp32"])
+    parser.add_argument("--math", default="tf32", choices=["tf32", "3xtf32", "fp32", "tf32trunc"])
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-budget", type=float, default=15.0)
@@ -382,15 +382,19 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
     for _ in range(5):
         launch()
     tx.synchronize()
-    reps = 50
-    s = torch.cuda.Event(enable_timing=True)
-    e = torch.cuda.Event(enable_timing=True)
-    s.record(ext)
-    for _ in range(reps):
+    # one event pair per launch: the device time of the kernel, not the host's
+    # enqueue rate; L2 is flushed before each launch (inputs > L2 is not given)
+    reps = 20
+    flush = tx.zeros(128 << 20)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(reps)]
+    for s, e in pairs:
+        _flush_l2(tx, flush)
+        s.record(ext)
         launch()
-    e.record(ext)
-    e.synchronize()
-    ms = s.elapsed_time(e) / reps
+        e.record(ext)
+    pairs[-1][1].synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in pairs) / reps
     flops = 2.0 * M * N_ * K
     achieved = flops / (ms / 1e3) / 1e12
     # dense TF32 peak: the measured dense bf16 rate halved (B200: tf32 dense = 1/2 bf16 dense)

@@ -51,9 +51,12 @@ enum {
 
 /* ---- math modes for fp32 contractions (TYNX_CUDA_MATH) ------------------ */
 enum {
-  TX_MATH_TF32 = 0,   /* tcgen05 kind::tf32, fp32 accumulate (rel 1e-3 class) */
-  TX_MATH_3XTF32 = 1, /* split-operand 3xTF32 on tcgen05 (fp32 class, 1e-5) */
-  TX_MATH_FP32 = 2    /* SIMT FFMA, exact fp32 products */
+  TX_MATH_TF32 = 0,      /* tcgen05 kind::tf32, operands rounded to nearest TF32 in shared
+                            memory, fp32 accumulate (rel 1e-3 class) */
+  TX_MATH_3XTF32 = 1,    /* split-operand 3xTF32 on tcgen05 (fp32 class, 1e-5) */
+  TX_MATH_FP32 = 2,      /* SIMT FFMA, exact fp32 products */
+  TX_MATH_TF32_TRUNC = 3 /* kind::tf32 on raw fp32 operands: the tensor core drops the
+                            13 low mantissa bits (truncation; fastest, biased) */
 };
 
 typedef struct tx_ctx tx_ctx;

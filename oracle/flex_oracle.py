@@ -35,6 +35,7 @@ receives as f64 (``mul_scalar(f64)``) are rounded to float32 before use.
 from __future__ import annotations
 
 import math
+from contextlib import contextmanager
 from typing import Callable, Optional
 
 import numpy as np
@@ -44,11 +45,24 @@ try:  # scipy ships in the image; the fallback keeps the oracle importable witho
 except Exception:  # pragma: no cover
     _erf = np.vectorize(math.erf)
 
-F32 = np.float32
+F32 = np.float32  # the working precision; `precision(np.float64)` switches it for checks
 
 
 def f32(x) -> np.float32:
-    return np.float32(x)
+    return F32(x)
+
+
+@contextmanager
+def precision(dtype):
+    """Run the oracle in another floating precision (float64 gives the exact
+    reference that fp32 implementations are measured against)."""
+    global F32
+    previous = F32
+    F32 = dtype
+    try:
+        yield
+    finally:
+        F32 = previous
 
 
 # =============================================================================
@@ -63,7 +77,7 @@ class T:
 
     def __init__(self, data, requires_grad: bool = False, name: str = ""):
         arr = np.asarray(data)
-        if arr.dtype == np.float64:
+        if arr.dtype.kind == "f" and arr.dtype != F32:
             arr = arr.astype(F32)
         self.data = arr
         self.grad: Optional[np.ndarray] = None

@@ -47,11 +47,12 @@ def _gemm(tx, A, B, ta, tb, math, *, alpha=1.0, beta=0.0, C0=None, bias=None, ac
 
 SHAPES = [
     (128, 128, 64), (256, 384, 256), (300, 200, 100), (4096, 1024, 784), (512, 10, 1024),
-    (1024, 1024, 4096), (64, 256, 32), (1000, 64, 72),
+    (1024, 1024, 4096), (64, 256, 32), (1000, 64, 72), (16384, 28, 32), (10, 1024, 4096),
 ]
 
 
-@pytest.mark.parametrize("math,tol", [("fp32", 1e-5), ("tf32", 3e-3)])
+@pytest.mark.parametrize("math,tol", [("fp32", 1e-5), ("tf32", 2e-3), ("3xtf32", 1e-5),
+                                      ("tf32trunc", 4e-3)])
 @pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_gemm_matches_fp64(tx, math, tol, ta, tb, M, N, K):

@@ -31,7 +31,7 @@ TX_ERR_DEVICE = 8
 TX_ERR_NCCL = 9
 TX_ERR_CAPTURE = 10
 
-TX_MATH = {"tf32": 0, "3xtf32": 1, "fp32": 2}
+TX_MATH = {"tf32": 0, "3xtf32": 1, "fp32": 2, "tf32trunc": 3}
 MAX_DIMS = 8
 
 ACT = {"none": 0, "relu": 1, "tanh": 2, "gelu": 3}

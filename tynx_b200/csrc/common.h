@@ -98,8 +98,9 @@ struct Scratch {
 int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d);
 // Returns TX_ERR_UNSUPPORTED (without latching) when the shape/layout cannot use
 // the tensor-core path; the dispatcher then uses the SIMT kernel.
-int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass);
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode);
 int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d);
+int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits);
 
 // grid sizing helper
 inline unsigned grid_for(int64_t n, int threads, int64_t max_blocks = 148 * 16) {

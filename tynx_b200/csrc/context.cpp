@@ -39,7 +39,7 @@ extern "C" int tx_device_count(int *out) {
 extern "C" int tx_ctx_create(int device, int math_mode, tx_ctx **out) {
   if (!out) return TX_ERR_INVALID;
   *out = nullptr;
-  if (math_mode < TX_MATH_TF32 || math_mode > TX_MATH_FP32) return TX_ERR_INVALID;
+  if (math_mode < TX_MATH_TF32 || math_mode > TX_MATH_TF32_TRUNC) return TX_ERR_INVALID;
   if (cudaSetDevice(device) != cudaSuccess) return TX_ERR_CUDA;
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return TX_ERR_CUDA;
@@ -63,7 +63,7 @@ extern "C" int tx_ctx_create(int device, int math_mode, tx_ctx **out) {
 }
 
 extern "C" int tx_ctx_set_math(tx_ctx *ctx, int math_mode) {
-  if (!ctx || math_mode < TX_MATH_TF32 || math_mode > TX_MATH_FP32) return TX_ERR_INVALID;
+  if (!ctx || math_mode < TX_MATH_TF32 || math_mode > TX_MATH_TF32_TRUNC) return TX_ERR_INVALID;
   ctx->math = math_mode;
   return TX_OK;
 }

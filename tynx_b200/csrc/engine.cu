@@ -547,13 +547,16 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     TX_CUDA(ctx, cudaMemsetAsync(g->flat_grads, 0, off * sizeof(float), ctx->stream));
     TX_CUDA(ctx, cudaMemsetAsync(g->flat_values, 0, off * sizeof(float), ctx->stream));
   }
+  // Every copy is ordered on the context's stream after the memsets above (the
+  // stream is non-blocking: a legacy-stream cudaMemcpy could run before them).
   for (size_t p = 0; p < g->params.size(); ++p) {
     GValue &v = g->values[g->params[p]];
     v.dev = g->flat_values + g->param_offset[p];
     v.grad = g->flat_grads + g->param_offset[p];
     if (vals[g->params[p]].h_data)
-      TX_CUDA(ctx, cudaMemcpy(v.dev, vals[g->params[p]].h_data, numel_of(v.shape) * sizeof(float),
-                              cudaMemcpyHostToDevice));
+      TX_CUDA(ctx, cudaMemcpyAsync(v.dev, vals[g->params[p]].h_data,
+                                   numel_of(v.shape) * sizeof(float), cudaMemcpyHostToDevice,
+                                   ctx->stream));
   }
   for (int i = 0; i < n_values; ++i) {
     GValue &v = g->values[i];
@@ -561,8 +564,10 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     size_t bytes = numel_of(v.shape) * (v.dtype == TX_DT_I64 ? 8 : 4);
     TX_CUDA(ctx, cudaMalloc(&v.dev, bytes ? bytes : 8));
     if (vals[i].h_data && bytes)
-      TX_CUDA(ctx, cudaMemcpy(v.dev, vals[i].h_data, bytes, cudaMemcpyHostToDevice));
+      TX_CUDA(ctx, cudaMemcpyAsync(v.dev, vals[i].h_data, bytes, cudaMemcpyHostToDevice,
+                                   ctx->stream));
   }
+  // the host arrays belong to the caller: finish reading them before returning
   TX_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   *out = g.release();
   return TX_OK;

@@ -38,10 +38,11 @@ __device__ __forceinline__ float dact_f(int act, float s) {
   return 1.f;
 }
 
-__global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
+// split > 0: blockIdx.z is the K split; raw partial sums go to part[split][M][N]
+__global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d, int split_len, float *part) {
   __shared__ float As[BK][BM + 4];
   __shared__ float Bs[BK][BN + 4];
-  const int64_t bz = blockIdx.z;
+  const int64_t bz = part ? 0 : blockIdx.z;
   const float *A = d.A + bz * d.stride_a;
   const float *B = d.B + bz * d.stride_b;
   float *C = d.C + bz * d.stride_c;
@@ -53,7 +54,26 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
-  for (int64_t k0 = 0; k0 < d.K; k0 += BK) {
+  // Two-level accumulation: 256-deep partial sums are folded into `tot`, so a
+  // long reduction (K = 4096 batch rows in a weight gradient) does not lose
+  // precision to one running fp32 sum.
+  float tot[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) tot[i][j] = 0.f;
+  const int64_t k_begin = part ? (int64_t)blockIdx.z * split_len : 0;
+  const int64_t k_end = part ? (k_begin + split_len < d.K ? k_begin + split_len : d.K) : d.K;
+  for (int64_t k0 = k_begin; k0 < k_end; k0 += BK) {
+    if (k0 != k_begin && ((k0 - k_begin) & 255) == 0) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          tot[i][j] += acc[i][j];
+          acc[i][j] = 0.f;
+        }
+    }
     // 64x16 A tile and 16x64 B tile: 1024 elements each, 4 per thread
     for (int e = threadIdx.x; e < BM * BK; e += 256) {
       int mm, kk;
@@ -61,7 +81,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
       else { kk = e % BK; mm = e / BK; }
       int64_t gm = m0 + mm, gk = k0 + kk;
       float v = 0.f;
-      if (gm < d.M && gk < d.K) v = d.trans_a ? A[gk * d.lda + gm] : A[gm * d.lda + gk];
+      if (gm < d.M && gk < k_end) v = d.trans_a ? A[gk * d.lda + gm] : A[gm * d.lda + gk];
       As[kk][mm] = v;
     }
     for (int e = threadIdx.x; e < BK * BN; e += 256) {
@@ -70,7 +90,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
       else { nn = e % BN; kk = e / BN; }
       int64_t gn = n0 + nn, gk = k0 + kk;
       float v = 0.f;
-      if (gn < d.N && gk < d.K) v = d.trans_b ? B[gn * d.ldb + gk] : B[gk * d.ldb + gn];
+      if (gn < d.N && gk < k_end) v = d.trans_b ? B[gn * d.ldb + gk] : B[gk * d.ldb + gn];
       Bs[kk][nn] = v;
     }
     __syncthreads();
@@ -90,6 +110,24 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
   }
 
 #pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] += tot[i][j];
+  if (part) {
+    float *P = part + (int64_t)blockIdx.z * d.M * d.N;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      int64_t gm = m0 + ty * TM + i;
+      if (gm >= d.M) continue;
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        int64_t gn = n0 + tx * TN + j;
+        if (gn < d.N) P[gm * d.N + gn] = acc[i][j];
+      }
+    }
+    return;
+  }
+#pragma unroll
   for (int i = 0; i < TM; ++i) {
     int64_t gm = m0 + ty * TM + i;
     if (gm >= d.M) continue;
@@ -108,14 +146,93 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d) {
   }
 }
 
+// Sum the split-K partials in a fixed order and apply the epilogue.  Block
+// (32, 8): each thread owns up to 4 consecutive columns of one row.
+__device__ __forceinline__ float split_epilogue(const tx_gemm_desc &d, float s, int64_t gm,
+                                                int64_t gn) {
+  float v = d.alpha * s;
+  if (d.bias) v += d.bias[gn] * d.bias_scale;
+  if (d.beta != 0.f) v += d.beta * d.C[gm * d.ldc + gn];
+  if (d.preact) d.preact[gm * d.ld_preact + gn] = v;
+  v = act_f(d.act, v);
+  if (d.dact) v *= dact_f(d.dact, d.dact_src[gm * d.ld_dact + gn]);
+  return v;
+}
+
+__global__ void k_gemm_split_reduce(tx_gemm_desc d, const float *__restrict__ part, int splits,
+                                    int vec) {
+  const int64_t gm = (int64_t)blockIdx.y * blockDim.y + threadIdx.y;
+  const int64_t gn = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (gm >= d.M || gn >= d.N) return;
+  const int64_t n = d.M * d.N;
+  const float *src = part + gm * d.N + gn;
+  if (vec && gn + 4 <= d.N) {
+    float4 s = *reinterpret_cast<const float4 *>(src);
+    for (int p = 1; p < splits; ++p) {
+      const float4 t = *reinterpret_cast<const float4 *>(src + (int64_t)p * n);
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+    float4 o = make_float4(split_epilogue(d, s.x, gm, gn), split_epilogue(d, s.y, gm, gn + 1),
+                           split_epilogue(d, s.z, gm, gn + 2), split_epilogue(d, s.w, gm, gn + 3));
+    if (((d.ldc & 3) == 0) && ((((uintptr_t)(d.C + gm * d.ldc + gn)) & 15) == 0)) {
+      *reinterpret_cast<float4 *>(d.C + gm * d.ldc + gn) = o;
+    } else {
+      d.C[gm * d.ldc + gn] = o.x;
+      d.C[gm * d.ldc + gn + 1] = o.y;
+      d.C[gm * d.ldc + gn + 2] = o.z;
+      d.C[gm * d.ldc + gn + 3] = o.w;
+    }
+    return;
+  }
+  for (int64_t c = gn; c < gn + 4 && c < d.N; ++c) {
+    float s = 0.f;
+    for (int p = 0; p < splits; ++p) s += part[(int64_t)p * n + gm * d.N + c];
+    d.C[gm * d.ldc + c] = split_epilogue(d, s, gm, c);
+  }
+}
+
 }  // namespace
+
+// Sum `splits` raw [M, N] partial products in a fixed order (IEEE fp32 adds) and
+// apply the epilogue of d.  Shared by the split-K paths of both GEMM kernels.
+int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits) {
+  const int vec = ((d.N & 3) == 0) && ((((uintptr_t)part) & 15) == 0);
+  dim3 block(32, 8);
+  dim3 grid((unsigned)((d.N + 127) / 128), (unsigned)((d.M + 7) / 8));
+  if (grid.y > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "split-K reduce: M too large");
+  k_gemm_split_reduce<<<grid, block, 0, ctx->stream>>>(d, part, splits, vec);
+  TX_LAUNCHED(ctx, "k_gemm_split_reduce");
+  return TX_OK;
+}
 
 int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
   int64_t batch = d.batch > 1 ? d.batch : 1;
   if (batch > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "GEMM batch above 65535");
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + BM - 1) / BM), (unsigned)batch);
   if (grid.y > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "GEMM M too large for SIMT grid");
-  k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(d);
+  // Skinny outputs with a long reduction (the weight gradient of a 10-class head:
+  // M = 10, N = 1024, K = batch) leave most SMs idle: split K across blocks.
+  const int64_t tiles = (int64_t)grid.x * grid.y;
+  if (batch == 1 && tiles < ctx->num_sms && d.K >= 8 * BK) {
+    int64_t splits = (2 * ctx->num_sms + tiles - 1) / tiles;
+    int64_t max_splits = d.K / (4 * BK);
+    if (splits > max_splits) splits = max_splits;
+    if (splits > 64) splits = 64;
+    if (splits >= 2) {
+      int64_t split_len = ((d.K + splits - 1) / splits + BK - 1) / BK * BK;
+      splits = (d.K + split_len - 1) / split_len;
+      Scratch part(ctx, (size_t)splits * d.M * d.N * sizeof(float));
+      if (!part.ptr) return TX_ERR_OOM;
+      grid.z = (unsigned)splits;
+      k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(d, (int)split_len, part.as<float>());
+      TX_LAUNCHED(ctx, "k_gemm_simt(split)");
+      return gemm_split_reduce(ctx, d, part.as<float>(), (int)splits);
+    }
+  }
+  k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(d, 0, nullptr);
   TX_LAUNCHED(ctx, "k_gemm_simt");
   return TX_OK;
 }
@@ -123,7 +240,8 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
 int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d) {
   if (d.M <= 0 || d.N <= 0) return TX_OK;
   if (ctx->math != TX_MATH_FP32) {
-    int rc = gemm_tcgen05(ctx, d, ctx->math == TX_MATH_3XTF32);
+    const int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
+    int rc = gemm_tcgen05(ctx, d, mode);
     if (rc != TX_ERR_UNSUPPORTED) return rc;
   }
   return gemm_simt(ctx, d);

@@ -2,19 +2,29 @@
 //
 // One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
 //   warp 0      TMA producer: loads 128x32 A and BNx32 B fp32 tiles per stage
-//               (128-byte swizzle) into a STAGES-deep shared-memory ring;
+//               into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM (BN fp32 columns x 128 lanes) and, from one
 //               thread, issues tcgen05.mma.kind::tf32 (K = 8 per instruction,
 //               4 per stage), committing each stage back to the producer;
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (one row per thread),
-//               apply alpha / bias / beta*C / activation / act' and store.
-// Operands may be K-major or MN-major on either side, so the forward
-// (X W^T), dgrad (dY W) and wgrad (dY^T X) products of a Gemm all map onto
-// the same kernel without transposes.  No TMA multicast is used anywhere.
+//   warps 2..5  operand conversion during the main loop (see MODE), then the
+//               epilogue: tcgen05.ld the accumulator, transpose each 32x32
+//               chunk through shared memory, and apply alpha / bias / beta*C /
+//               activation / act' with coalesced loads and stores.
+// MODE selects how fp32 operands become TF32:
+//   0  raw: the tensor core reads fp32 and drops the 13 low mantissa bits
+//      (truncation, biased toward zero);
+//   1  round to nearest: warps 2..5 round each landed stage in place
+//      (cvt.rna.tf32) before the MMA consumes it (unbiased; ~2^-11 relative);
+//   2  3xTF32: each operand is split into big = rna(x) and small = rna(x - big)
+//      and C += A_big B_big + A_big B_small + A_small B_big (fp32-class accuracy).
+// Operands may be K-major or MN-major on either side, so the forward (X W^T),
+// dgrad (dY W) and wgrad (dY^T X) products of a Gemm map onto the same kernel
+// without transposes.  No TMA multicast is used anywhere.
 //
 // Every mbarrier wait is bounded (~2 s of %globaltimer).  On expiry the CTA
-// raises the context's device error flag, stops issuing work, waits (bounded)
-// for its own MMAs, frees TMEM and returns.
+// raises the context's device error flag, stops issuing work, lets every role
+// reach the final barrier (no named barriers that an early exit could strand),
+// frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -26,16 +36,25 @@
 namespace {
 
 constexpr int TC_BM = 128;
-constexpr int TC_BK = 32;                       // fp32 elements per 128-byte swizzle row
+constexpr int TC_BK = 32;                         // fp32 elements per 128-byte swizzle row
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int kConvThreads = 128;                 // warps 2..5
 
-template <int BN>
+template <int BN, int MODE>
 struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK * 4;
   static constexpr int B_BYTES = BN * TC_BK * 4;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
+  // 3xTF32 keeps the small halves of both operands next to the big ones
+  static constexpr int STAGE = (A_BYTES + B_BYTES) * (MODE == 2 ? 2 : 1);
   static constexpr int STAGES = (196 * 1024 / STAGE) > 8 ? 8 : (196 * 1024 / STAGE);
-  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 512 /*barriers*/;
+  // The tensor core adds each MMA's products into the fp32 TMEM accumulator
+  // with a biased (toward zero) rounding, so the error grows with the number
+  // of MMAs in one chain.  k-blocks are dealt round-robin to NACC accumulators
+  // (BN columns each, within the 512 TMEM columns) that the epilogue sums with
+  // IEEE fp32 adds.
+  static constexpr int NACC = MODE == 2 ? (512 / BN > 4 ? 4 : 512 / BN) : (512 / BN >= 2 ? 2 : 1);
+  static constexpr int TMEM_COLS = BN * NACC;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -56,6 +75,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
@@ -119,6 +142,12 @@ __device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uin
       : "memory");
 }
 
+__device__ __forceinline__ float to_tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // Shared-memory matrix descriptor (sm_100 layout, version 1).  K-major tiles
 // use the 128-byte swizzle (layout 2: 8 rows x 128 B atoms); MN-major fp32 tiles
 // use the 128-byte swizzle with 32-byte atomicity (layout 1: 4 rows x 128 B
@@ -135,6 +164,16 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   d |= (uint64_t)1 << 46;  // version
   d |= (uint64_t)layout << 61;
   return d;
+}
+
+// descriptor of the k-th 8-deep slice of a staged operand tile
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
+  // K-major: advance 32 bytes inside the swizzled 128-byte row (SBO = 8 rows).
+  // MN-major: 8 K rows (1024 bytes) per instruction, LBO = the 4 KB stride
+  // between 32-element MN blocks, SBO = 4 rows.
+  return MN ? smem_desc(base + k * 1024, 4096, 512, kLayoutSW128Base32B)
+            : smem_desc(base + k * 32, 16, 1024, kLayoutSW128);
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -175,16 +214,54 @@ __device__ __forceinline__ float dact_f(int act, float s) {
   return 1.f;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+// Epilogue over one transposed 32x32 chunk: lane = column, rr walks rows.
+// The common cases (no beta, no pre-activation store, no act') run a tight
+// loop specialised on the activation; everything else takes the general path.
+template <int ACT>
+__device__ __forceinline__ void epi_rows_fast(const float *__restrict__ t, int lane,
+                                              float *__restrict__ cp, int64_t ldc, int rows,
+                                              float alpha, bool has_bias, float bias_v) {
+  if (has_bias) {
+#pragma unroll 8
+    for (int rr = 0; rr < rows; ++rr) {
+      float x = alpha * t[rr * 33 + lane];
+      x += bias_v;
+      cp[rr * ldc] = act_f(ACT, x);
+    }
+  } else {
+#pragma unroll 8
+    for (int rr = 0; rr < rows; ++rr) cp[rr * ldc] = act_f(ACT, alpha * t[rr * 33 + lane]);
+  }
+}
+
+__device__ __noinline__ void epi_rows_general(const float *__restrict__ t, int lane, const tx_gemm_desc &d,
+                                              float *C, int64_t cbase, int64_t row0, int64_t gn,
+                                              int rows, float bias_v) {
+  for (int rr = 0; rr < rows; ++rr) {
+    const int64_t gm = row0 + rr;
+    float x = d.alpha * t[rr * 33 + lane];
+    if (d.bias) x += bias_v;
+    if (d.beta != 0.f) x += d.beta * C[gm * d.ldc + gn];
+    if (d.preact) d.preact[cbase + gm * d.ld_preact + gn] = x;
+    x = act_f(d.act, x);
+    if (d.dact) x *= dact_f(d.dact, d.dact_src[cbase + gm * d.ld_dact + gn]);
+    C[gm * d.ldc + gn] = x;
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const tx_gemm_desc d, int *err) {
-  using Cfg = TcCfg<BN>;
+              const tx_gemm_desc d, int *err, int kb_per_cta) {
+  using Cfg = TcCfg<BN, MODE>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int NACC = Cfg::NACC;
+  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + STAGES * Cfg::STAGE);
-  uint64_t *empty = full + STAGES;
+  uint64_t *conv = full + STAGES;
+  uint64_t *empty = conv + STAGES;
   uint64_t *accb = empty + STAGES;
   uint32_t *tmem_holder = (uint32_t *)(accb + 1);
   volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
@@ -194,11 +271,18 @@ __global__ void __launch_bounds__(192, 1)
   const int m0 = blockIdx.y * TC_BM;
   const int n0 = blockIdx.x * BN;
   const int bz = blockIdx.z;
-  const int num_k = (int)((d.K + TC_BK - 1) / TC_BK);
+  // split-K (kb_per_cta > 0): blockIdx.z selects a range of k-blocks and a raw
+  // partial output slice; the operands have no batch dimension then
+  const int total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
+  const int kb_first = kb_per_cta > 0 ? bz * kb_per_cta : 0;
+  const int num_k = kb_per_cta > 0 ? min(kb_per_cta, total_kb - kb_first) : total_kb;
+  const int zc = kb_per_cta > 0 ? 0 : bz;
+  const int used_acc = num_k < NACC ? num_k : NACC;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kConvThreads);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
@@ -208,7 +292,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
-                 "r"(BN));
+                 "r"(Cfg::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -222,21 +306,21 @@ __global__ void __launch_bounds__(192, 1)
         const int s = kb % STAGES;
         const uint32_t round = kb / STAGES;
         if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 1)) break;
-        mbar_expect_tx(&full[s], Cfg::STAGE);
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
         const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
-        const uint32_t b_dst = a_dst + Cfg::A_BYTES;
-        const int k0 = kb * TC_BK;
+        const uint32_t b_dst = a_dst + A_BYTES;
+        const int k0 = (kb_first + kb) * TC_BK;
         if (A_MN) {
 #pragma unroll
-          for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, bz);
+          for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
         } else {
-          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, bz);
+          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
         }
         if (B_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, bz);
+          for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
         } else {
-          tma_load_3d(b_dst, &mapB, &full[s], k0, n0, bz);
+          tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
         }
       }
     }
@@ -245,75 +329,101 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
                              ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)(TC_BM >> 4) << 24);
-      bool ok = true;
       for (int kb = 0; kb < num_k; ++kb) {
         const int s = kb % STAGES;
         const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&full[s], round & 1, abort_flag, err, 2)) {
-          ok = false;
-          break;
-        }
+        uint64_t *ready = MODE == 0 ? &full[s] : &conv[s];
+        if (!mbar_wait(ready, round & 1, abort_flag, err, 2)) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE);
-        const uint32_t b_base = a_base + Cfg::A_BYTES;
+        const uint32_t b_base = a_base + A_BYTES;
+        const uint32_t acc = tmem + (uint32_t)((kb % NACC) * BN);
+        const bool fresh = kb < NACC;  // first k-block of this accumulator
 #pragma unroll
         for (int k = 0; k < TC_BK / 8; ++k) {
-          // K-major: advance 32 bytes inside the swizzled 128-byte row (SBO =
-          // 8 rows).  MN-major: 8 K rows (1024 bytes) per instruction, LBO =
-          // the 4 KB stride between 32-element MN blocks, SBO = 4 rows.
-          const uint64_t ad = A_MN ? smem_desc(a_base + k * 1024, 4096, 512, kLayoutSW128Base32B)
-                                   : smem_desc(a_base + k * 32, 16, 1024, kLayoutSW128);
-          const uint64_t bd = B_MN ? smem_desc(b_base + k * 1024, 4096, 512, kLayoutSW128Base32B)
-                                   : smem_desc(b_base + k * 32, 16, 1024, kLayoutSW128);
-          tc_mma_tf32(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          const uint64_t ad = operand_desc<A_MN>(a_base, k);
+          const uint64_t bd = operand_desc<B_MN>(b_base, k);
+          tc_mma_tf32(acc, ad, bd, idesc, (fresh && k == 0) ? 0u : 1u);
+          if (MODE == 2) {
+            const uint32_t sa = a_base + A_BYTES + B_BYTES, sb = sa + A_BYTES;
+            tc_mma_tf32(acc, ad, operand_desc<B_MN>(sb, k), idesc, 1u);
+            tc_mma_tf32(acc, operand_desc<A_MN>(sa, k), bd, idesc, 1u);
+          }
         }
         tc_commit(&empty[s]);
       }
-      (void)ok;
       tc_commit(accb);  // arrives once every MMA issued above has completed
     }
   } else {
+    const int ct = threadIdx.x - 64;  // 0..127
+    if (MODE != 0) {
+      // operand conversion, one stage behind the producer and one ahead of the MMA
+      constexpr int N4 = (A_BYTES + B_BYTES) / 16;
+      for (int kb = 0; kb < num_k; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (!mbar_wait(&full[s], round & 1, abort_flag, err, 4)) break;
+        float4 *p = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE);
+        float4 *q = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE + A_BYTES + B_BYTES);
+#pragma unroll 4
+        for (int i = ct; i < N4; i += kConvThreads) {
+          float4 v = p[i];
+          float4 big = make_float4(to_tf32_rn(v.x), to_tf32_rn(v.y), to_tf32_rn(v.z), to_tf32_rn(v.w));
+          p[i] = big;
+          if (MODE == 2)
+            q[i] = make_float4(to_tf32_rn(v.x - big.x), to_tf32_rn(v.y - big.y),
+                               to_tf32_rn(v.z - big.z), to_tf32_rn(v.w - big.w));
+        }
+        // make the generic-proxy writes visible to the tensor core (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&conv[s]);
+      }
+    }
     // epilogue warps 2..5 -> TMEM lane quadrants 2,3,0,1
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;
     const bool have = mbar_wait(accb, 0, abort_flag, err, 3);
     tc_fence_after();
     if (have && !*abort_flag) {
-      const int64_t gm = (int64_t)m0 + row;
-      const bool row_ok = gm < d.M;
+      // TMEM gives each thread one row; global memory wants a warp per row.
+      // Each 32x32 chunk is transposed through padded shared memory (the
+      // drained pipeline stages), then lanes walk columns so every load and
+      // store of the epilogue is a coalesced 128-byte row segment.
+      float *tile = reinterpret_cast<float *>(smem) + quad * (32 * 33);
+      const int64_t row0 = (int64_t)m0 + quad * 32;
       float *C = d.C + (int64_t)bz * d.stride_c;
       const int64_t cbase = bz * d.stride_c;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c, v);
-        if (!row_ok) continue;
-        const int64_t gn0 = (int64_t)n0 + c;
-        if (gn0 >= d.N) continue;
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c;
+        tmem_ld32(lane_base, v);
+#pragma unroll 1
+        for (int a = 1; a < used_acc; ++a) {
+          float w[32];
+          tmem_ld32(lane_base + (uint32_t)(a * BN), w);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t gn = gn0 + j;
-          if (gn < d.N) {
-            float x = d.alpha * v[j];
-            if (d.bias) x += d.bias[gn] * d.bias_scale;
-            if (d.beta != 0.f) x += d.beta * C[gm * d.ldc + gn];
-            if (d.preact) d.preact[cbase + gm * d.ld_preact + gn] = x;
-            x = act_f(d.act, x);
-            if (d.dact) x *= dact_f(d.dact, d.dact_src[cbase + gm * d.ld_dact + gn]);
-            v[j] = x;
+          for (int j = 0; j < 32; ++j) v[j] += w[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tile[lane * 33 + j] = v[j];
+        __syncwarp();
+        const int64_t gn = (int64_t)n0 + c + lane;
+        const bool col_ok = gn < d.N;
+        const float bias_v = (d.bias && col_ok) ? d.bias[gn] * d.bias_scale : 0.f;
+        int rows = d.M - row0 < 32 ? (int)(d.M - row0) : 32;
+        if (!col_ok || rows < 0) rows = 0;
+        if (d.beta == 0.f && !d.preact && !d.dact) {
+          float *cp = C + row0 * d.ldc + gn;
+          switch (d.act) {
+            case TX_ACT_RELU: epi_rows_fast<TX_ACT_RELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
+            case TX_ACT_TANH: epi_rows_fast<TX_ACT_TANH>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
+            case TX_ACT_GELU: epi_rows_fast<TX_ACT_GELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
+            default: epi_rows_fast<TX_ACT_NONE>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
           }
-        }
-        const bool vec = (gn0 + 32 <= d.N) && ((d.ldc & 3) == 0) &&
-                         ((((uintptr_t)(C + gm * d.ldc + gn0)) & 15) == 0);
-        if (vec) {
-          float4 *dst = reinterpret_cast<float4 *>(C + gm * d.ldc + gn0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (gn0 + j < d.N) C[gm * d.ldc + gn0 + j] = v[j];
+          epi_rows_general(tile, lane, d, C, cbase, row0, gn, rows, bias_v);
         }
+        __syncwarp();
       }
     }
   }
@@ -322,7 +432,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg::TMEM_COLS));
   }
 }
 
@@ -358,46 +469,88 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+// `z` = batch count, or the number of K splits when kb_per_cta > 0
+template <int BN, bool A_MN, bool B_MN, int MODE>
 int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
-              int64_t batch) {
-  auto kern = k_gemm_tc<BN, A_MN, B_MN>;
+              int64_t z, int kb_per_cta) {
+  auto kern = k_gemm_tc<BN, A_MN, B_MN, MODE>;
   static bool configured[64] = {};
   int dev = ctx->device & 63;
   if (!configured[dev]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN>::SMEM);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN, MODE>::SMEM);
     configured[dev] = true;
   }
-  dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)batch);
-  kern<<<grid, 192, TcCfg<BN>::SMEM, ctx->stream>>>(ma, mb, d, ctx->d_err);
+  dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
+  kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(ma, mb, d, ctx->d_err, kb_per_cta);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
 
-template <int BN>
+template <int BN, int MODE>
 int launch_bn(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
-              int64_t batch) {
+              int64_t z, int kb_per_cta) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_tc<BN, true, true>(ctx, d, ma, mb, batch);
-  if (a_mn) return launch_tc<BN, true, false>(ctx, d, ma, mb, batch);
-  if (b_mn) return launch_tc<BN, false, true>(ctx, d, ma, mb, batch);
-  return launch_tc<BN, false, false>(ctx, d, ma, mb, batch);
+  if (a_mn && b_mn) return launch_tc<BN, true, true, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+  if (a_mn) return launch_tc<BN, true, false, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+  if (b_mn) return launch_tc<BN, false, true, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+  return launch_tc<BN, false, false, MODE>(ctx, d, ma, mb, z, kb_per_cta);
 }
 
-int pick_bn(tx_ctx *ctx, int64_t M, int64_t N, int64_t batch) {
-  int best = 128;
-  double best_eff = -1;
+template <int MODE>
+int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const CUtensorMap &ma,
+                const CUtensorMap &mb, int64_t z, int kb_per_cta) {
+  switch (bn) {
+    case 256: return launch_bn<256, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+    case 64: return launch_bn<64, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+    default: return launch_bn<128, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+  }
+}
+
+int launch_any(tx_ctx *ctx, int mode, int bn, const tx_gemm_desc &d, const CUtensorMap &ma,
+               const CUtensorMap &mb, int64_t z, int kb_per_cta) {
+  switch (mode) {
+    case 0: return launch_mode<0>(ctx, bn, d, ma, mb, z, kb_per_cta);
+    case 2: return launch_mode<2>(ctx, bn, d, ma, mb, z, kb_per_cta);
+    default: return launch_mode<1>(ctx, bn, d, ma, mb, z, kb_per_cta);
+  }
+}
+
+struct Tiling {
+  int bn = 128;
+  int splits = 1;
+};
+
+// Pick the tile width and the K split from a small cost model: waves of CTAs
+// times the per-CTA k-block work (one 128 x BN x 32 step costs about BN + 96
+// "column units" including the fixed TMA/commit latency), plus the traffic of
+// the split reduction.  1 unit ~ 1.5 ns at the TF32 rate of one SM.
+Tiling pick_tiling(tx_ctx *ctx, int64_t M, int64_t N, int64_t K, int64_t batch, int max_bn) {
+  Tiling best;
+  double best_cost = 1e300;
+  const int total_kb = (int)((K + TC_BK - 1) / TC_BK);
   const int cands[3] = {256, 128, 64};
   for (int bn : cands) {
+    if (bn > max_bn) continue;
     if (bn > 64 && N <= bn / 2) continue;  // mostly-empty tiles
-    int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn) * batch;
-    int64_t waves = (tiles + ctx->num_sms - 1) / ctx->num_sms;
-    double eff = (double)tiles / (double)(waves * ctx->num_sms);
-    // larger tiles amortise better; accept them unless they waste SMs
-    double score = eff + (bn == 256 ? 0.05 : bn == 128 ? 0.03 : 0.0);
-    if (score > best_eff) {
-      best_eff = score;
-      best = bn;
+    const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn) * batch;
+    int max_split = 1;
+    if (batch == 1 && tiles < ctx->num_sms && total_kb >= 16) {
+      int64_t want = (ctx->num_sms + tiles - 1) / tiles;
+      int64_t most = total_kb / 8;  // at least 8 k-blocks (K = 256) per split
+      max_split = (int)(want < most ? want : most);
+      if (max_split > 32) max_split = 32;
+    }
+    for (int s = 1; s <= max_split; s = s < 4 ? s + 1 : s * 2) {
+      const int kb_per = (total_kb + s - 1) / s;
+      const int64_t ctas = tiles * s;
+      const int64_t waves = (ctas + ctx->num_sms - 1) / ctx->num_sms;
+      double cost = (double)waves * kb_per * (bn + 96) * 1.5e-3;  // microseconds
+      if (s > 1) cost += 2.0 + (double)(s + 1) * M * N * 4 / 5.0e6;  // reduce: ~5 TB/s
+      if (cost < best_cost) {
+        best_cost = cost;
+        best.bn = bn;
+        best.splits = s;
+      }
     }
   }
   return best;
@@ -405,8 +558,8 @@ int pick_bn(tx_ctx *ctx, int64_t M, int64_t N, int64_t batch) {
 
 }  // namespace
 
-int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass) {
-  if (three_pass) return TX_ERR_UNSUPPORTED;  // 3xTF32 runs on the exact SIMT path
+// mode: 0 raw fp32 operands (hardware truncation), 1 TF32 round-to-nearest, 2 3xTF32
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   if (d.K <= 0 || d.M <= 0 || d.N <= 0) return TX_ERR_UNSUPPORTED;
   const int64_t batch = d.batch > 1 ? d.batch : 1;
   if (d.M >= (1ll << 31) || d.N >= (1ll << 31) || d.K >= (1ll << 31) || batch > 65535)
@@ -415,13 +568,14 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass) {
   if (((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) || (d.lda & 3) || (d.ldb & 3))
     return TX_ERR_UNSUPPORTED;
   if (batch > 1 && ((d.stride_a & 3) || (d.stride_b & 3))) return TX_ERR_UNSUPPORTED;
-  // rows shorter than one swizzle row waste most of each tile; SIMT is better
+  // rows shorter than half a swizzle row waste most of each tile; SIMT is better
   const int64_t a_inner = d.trans_a ? d.M : d.K;
   const int64_t b_inner = d.trans_b ? d.K : d.N;
   if (a_inner < 16 || b_inner < 16) return TX_ERR_UNSUPPORTED;
   if (!load_encode()) return TX_ERR_UNSUPPORTED;
 
-  const int bn = pick_bn(ctx, d.M, d.N, batch);
+  const Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
+  const int bn = tiling.bn;
   CUtensorMap ma, mb;
   bool ok;
   if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
@@ -435,9 +589,28 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, bool three_pass) {
     ok = make_map(&mb, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
 
-  switch (bn) {
-    case 256: return launch_bn<256>(ctx, d, ma, mb, batch);
-    case 64: return launch_bn<64>(ctx, d, ma, mb, batch);
-    default: return launch_bn<128>(ctx, d, ma, mb, batch);
-  }
+  // Split K across CTAs when the output has fewer tiles than SMs (the weight
+  // gradients of small layers, whose reduction runs over the whole batch):
+  // raw partial tiles go to scratch and a fixed-order reduction applies the
+  // epilogue.  Shorter accumulation chains are also more accurate.
+  const int total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
+  int splits = tiling.splits;
+  if (splits <= 1) return launch_any(ctx, mode, bn, d, ma, mb, batch, 0);
+  const int kb_per = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kb_per - 1) / kb_per;
+  Scratch part(ctx, (size_t)splits * d.M * d.N * sizeof(float));
+  if (!part.ptr) return TX_ERR_OOM;
+  tx_gemm_desc raw = d;
+  raw.C = part.as<float>();
+  raw.ldc = d.N;
+  raw.stride_c = d.M * d.N;
+  raw.alpha = 1.f;
+  raw.beta = 0.f;
+  raw.bias = nullptr;
+  raw.act = TX_ACT_NONE;
+  raw.preact = nullptr;
+  raw.dact = TX_ACT_NONE;
+  raw.dact_src = nullptr;
+  TX_TRY(launch_any(ctx, mode, bn, raw, ma, mb, splits, kb_per));
+  return gemm_split_reduce(ctx, d, part.as<float>(), splits);
 }
