@@ -390,6 +390,10 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
              for _ in range(reps)]
     for s, e in pairs:
         _flush_l2(tx, flush)
+        # a device-side spin after the flush keeps the GPU busy while the host
+        # enqueues the launch, so the event pair brackets device work only
+        with torch.cuda.stream(ext):
+            torch.cuda._sleep(400000)
         s.record(ext)
         launch()
         e.record(ext)

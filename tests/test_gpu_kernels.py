@@ -84,6 +84,97 @@ def test_gemm_epilogue(tx, math, tol, act):
     assert float(np.abs(got - fn(z)).max()) < tol * float(np.abs(z).max())
 
 
+def _np_act(act, v):
+    from scipy.special import erf
+
+    return {"none": lambda x: x, "relu": lambda x: np.maximum(x, 0), "tanh": np.tanh,
+            "gelu": lambda x: 0.5 * x * (1 + erf(x / np.sqrt(2)))}[act](v)
+
+
+def _np_dact(act, s):
+    from scipy.special import erf
+
+    if act == "relu":
+        return (s > 0).astype(np.float64)
+    if act == "tanh":
+        return 1 - s * s
+    return 0.5 * (1 + erf(s / np.sqrt(2))) + s * np.exp(-0.5 * s * s) / np.sqrt(2 * np.pi)
+
+
+# Shapes the bandwidth-shaped kernels take (K <= 32; N <= 16 with A row-major;
+# M <= 16 with B row-major), with leading dimensions padded by `pad` so that
+# rows are not 16-byte aligned when pad is odd, and `batch` strided matrices.
+SKINNY = [
+    # M, N, K, ta, tb, pad, batch, act, dact, beta, preact
+    (4096, 1024, 10, 0, 0, 0, 1, "none", "relu", 0.0, False),   # head dgrad with relu'
+    (4096, 10, 1024, 0, 1, 0, 1, "relu", None, 0.0, True),      # head forward
+    (10, 1024, 4096, 1, 0, 0, 1, "none", None, 1.0, False),     # head wgrad, accumulated
+    (2049, 30, 27, 0, 1, 1, 1, "tanh", None, 0.5, False),       # conv1 im2col-like, ragged
+    (300, 333, 16, 1, 1, 3, 3, "gelu", None, 0.0, True),        # batched, MN-major A
+    (777, 1, 513, 0, 0, 1, 1, "none", "tanh", 0.0, False),      # N = 1, misaligned rows
+    (3, 333, 4097, 0, 0, 1, 1, "none", None, 0.0, False),       # M = 3, ragged K
+    (16, 96, 8192, 1, 0, 0, 1, "none", "gelu", 0.0, False),     # M = 16, long K
+    (8192, 16, 512, 0, 0, 0, 1, "tanh", None, 0.0, False),      # N = 16, B K x N
+]
+
+
+@pytest.mark.parametrize("math", ["fp32", "tf32"])
+@pytest.mark.parametrize("case", SKINNY, ids=[f"{c[0]}x{c[1]}x{c[2]}" for c in SKINNY])
+def test_skinny_gemm_full_epilogue(tx, math, case):
+    """Skinny shapes run exact-fp32 kernels in every math mode: 1e-5 of the
+    pre-activation scale even in TF32 mode."""
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    M, Nn, K, ta, tb, pad, batch, act, dact, beta, preact = case
+    rng = np.random.default_rng(M + 3 * Nn + 7 * K)
+    ar, ac = (K, M) if ta else (M, K)
+    br, bc = (Nn, K) if tb else (K, Nn)
+    lda, ldb, ldc = ac + pad, bc + pad, Nn + pad
+    A = rng.standard_normal((batch, ar, lda)).astype(np.float32)
+    B = rng.standard_normal((batch, br, ldb)).astype(np.float32)
+    C0 = rng.standard_normal((batch, M, ldc)).astype(np.float32)
+    S = rng.standard_normal((batch, M, ldc)).astype(np.float32) * (0.5 if dact == "tanh" else 1)
+    bias = rng.standard_normal(Nn).astype(np.float32)
+    ctx = _core.context()
+    ctx.math = math
+    try:
+        a, b, c, s, bb = (tx.Tensor(v) for v in (A, B, C0, S, bias))
+        p = tx.zeros(batch, M, ldc)
+        d = N.GemmDesc()
+        d.M, d.N, d.K = M, Nn, K
+        d.A, d.lda, d.trans_a = a.ptr, lda, ta
+        d.B, d.ldb, d.trans_b = b.ptr, ldb, tb
+        d.C, d.ldc = c.ptr, ldc
+        d.alpha, d.beta = 0.75, beta
+        d.bias, d.bias_scale = bb.ptr, 2.0
+        d.act = N.ACT[act]
+        if preact:
+            d.preact, d.ld_preact = p.ptr, ldc
+        if dact:
+            d.dact_src, d.ld_dact, d.dact = s.ptr, ldc, N.ACT[dact]
+        d.batch = batch
+        d.stride_a, d.stride_b, d.stride_c = ar * lda, br * ldb, M * ldc
+        ctx.check(N.lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
+        got, got_pre = c.numpy(), p.numpy()
+    finally:
+        ctx.math = "tf32"
+    for z in range(batch):
+        Az = A[z, :, :ac].astype(np.float64)
+        Bz = B[z, :, :bc].astype(np.float64)
+        prod = (Az.T if ta else Az) @ (Bz.T if tb else Bz)
+        pre = 0.75 * prod + 2.0 * bias + beta * C0[z, :, :Nn]
+        want = _np_act(act, pre)
+        if dact:
+            want = want * _np_dact(dact, S[z, :, :Nn].astype(np.float64))
+        scale = float(np.abs(pre).max())
+        assert float(np.abs(got[z, :, :Nn] - want).max()) < 1e-5 * scale
+        # padding columns are left alone
+        np.testing.assert_array_equal(got[z, :, Nn:], C0[z, :, Nn:])
+        if preact:
+            assert float(np.abs(got_pre[z, :, :Nn] - pre).max()) < 1e-5 * scale
+
+
 def test_softmax_xent_matches_oracle(tx):
     from oracle import flex_oracle as fo
     from tynx_b200 import nn

@@ -100,6 +100,9 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d);
 // the tensor-core path; the dispatcher then uses the SIMT kernel.
 int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode);
 int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d);
+// Bandwidth-shaped kernels for K <= 32, N <= 16 or M <= 16; TX_ERR_UNSUPPORTED
+// (not latched) for every other shape.
+int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d);
 int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits);
 
 // grid sizing helper

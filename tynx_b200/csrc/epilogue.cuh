@@ -1,0 +1,39 @@
+// Activation and activation-derivative math shared by every GEMM epilogue, so
+// the fused forward (Gemm -> Relu/Tanh/Gelu) and the fused dgrad (dY * act')
+// give the same bits whichever kernel a shape lands on.
+//
+// Relu / Tanh / exact-erf GELU follow the reference's unary ops
+// (crates/tynx/src/tensor.rs:2002, 2012, 2229; the ONNX `approximate`
+// attribute is not consulted there either).  Derivatives are taken from the
+// saved tensor: Relu and Tanh use the forward output y (mask y > 0; 1 - y^2),
+// GELU uses the pre-activation x (Phi(x) + x phi(x)).
+#pragma once
+
+#include <math.h>
+
+#include "tynx_cuda.h"
+
+namespace tx_epi {
+
+__device__ __forceinline__ float act(int a, float v) {
+  switch (a) {
+    case TX_ACT_RELU: return v > 0.f ? v : 0.f;
+    case TX_ACT_TANH: return tanhf(v);
+    case TX_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  }
+  return v;
+}
+
+__device__ __forceinline__ float dact(int a, float s) {
+  switch (a) {
+    case TX_ACT_RELU: return s > 0.f ? 1.f : 0.f;
+    case TX_ACT_TANH: return 1.f - s * s;
+    case TX_ACT_GELU: {
+      float cdf = 0.5f * (1.0f + erff(s * 0.70710678118654752f));
+      return cdf + s * expf(-0.5f * s * s) * 0.39894228040143268f;
+    }
+  }
+  return 1.f;
+}
+
+}  // namespace tx_epi

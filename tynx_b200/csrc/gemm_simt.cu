@@ -11,32 +11,14 @@
 #include <math.h>
 
 #include "common.h"
+#include "epilogue.cuh"
 
 namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4;
 
-__device__ __forceinline__ float act_f(int act, float v) {
-  switch (act) {
-    case TX_ACT_RELU: return v > 0.f ? v : 0.f;
-    case TX_ACT_TANH: return tanhf(v);
-    case TX_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-  }
-  return v;
-}
-
-// derivative from the saved tensor: relu/tanh use the forward output, gelu the pre-activation
-__device__ __forceinline__ float dact_f(int act, float s) {
-  switch (act) {
-    case TX_ACT_RELU: return s > 0.f ? 1.f : 0.f;
-    case TX_ACT_TANH: return 1.f - s * s;
-    case TX_ACT_GELU: {
-      float cdf = 0.5f * (1.0f + erff(s * 0.70710678118654752f));
-      return cdf + s * expf(-0.5f * s * s) * 0.39894228040143268f;
-    }
-  }
-  return 1.f;
-}
+__device__ __forceinline__ float act_f(int act, float v) { return tx_epi::act(act, v); }
+__device__ __forceinline__ float dact_f(int act, float s) { return tx_epi::dact(act, s); }
 
 // split > 0: blockIdx.z is the K split; raw partial sums go to part[split][M][N]
 __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d, int split_len, float *part) {
@@ -127,6 +109,19 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d, int split_len
     }
     return;
   }
+  // every load of the epilogue is issued before the first store (the stores
+  // may alias the loaded tensors, so interleaving would serialise them)
+  float cv[TM][TN], sv[TM][TN];
+  const float *S = d.dact_src ? d.dact_src + bz * d.stride_c : nullptr;
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int64_t gm = m0 + ty * TM + i, gn = n0 + tx * TN + j;
+      const bool ok = gm < d.M && gn < d.N;
+      cv[i][j] = (ok && d.beta != 0.f) ? C[gm * d.ldc + gn] : 0.f;
+      sv[i][j] = (ok && S) ? S[gm * d.ld_dact + gn] : 0.f;
+    }
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
     int64_t gm = m0 + ty * TM + i;
@@ -137,10 +132,10 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d, int split_len
       if (gn >= d.N) continue;
       float v = d.alpha * acc[i][j];
       if (d.bias) v += d.bias[gn] * d.bias_scale;
-      if (d.beta != 0.f) v += d.beta * C[gm * d.ldc + gn];
+      if (d.beta != 0.f) v += d.beta * cv[i][j];
       if (d.preact) d.preact[bz * d.stride_c + gm * d.ld_preact + gn] = v;
       v = act_f(d.act, v);
-      if (d.dact) v *= dact_f(d.dact, d.dact_src[bz * d.stride_c + gm * d.ld_dact + gn]);
+      if (d.dact) v *= dact_f(d.dact, sv[i][j]);
       C[gm * d.ldc + gn] = v;
     }
   }
@@ -167,8 +162,22 @@ __global__ void k_gemm_split_reduce(tx_gemm_desc d, const float *__restrict__ pa
   const int64_t n = d.M * d.N;
   const float *src = part + gm * d.N + gn;
   if (vec && gn + 4 <= d.N) {
+    // partials are added in split order; loads are issued four at a time
     float4 s = *reinterpret_cast<const float4 *>(src);
-    for (int p = 1; p < splits; ++p) {
+    int p = 1;
+    for (; p + 4 <= splits; p += 4) {
+      float4 t[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(src + (int64_t)(p + j) * n);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s.x += t[j].x;
+        s.y += t[j].y;
+        s.z += t[j].z;
+        s.w += t[j].w;
+      }
+    }
+    for (; p < splits; ++p) {
       const float4 t = *reinterpret_cast<const float4 *>(src + (int64_t)p * n);
       s.x += t.x;
       s.y += t.y;
@@ -239,6 +248,8 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
 
 int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d) {
   if (d.M <= 0 || d.N <= 0) return TX_OK;
+  const int skinny = gemm_skinny(ctx, d);
+  if (skinny != TX_ERR_UNSUPPORTED) return skinny;
   if (ctx->math != TX_MATH_FP32) {
     const int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
     int rc = gemm_tcgen05(ctx, d, mode);

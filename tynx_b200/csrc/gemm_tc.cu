@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "common.h"
+#include "epilogue.cuh"
 
 namespace {
 
@@ -193,26 +194,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ float act_f(int act, float v) {
-  switch (act) {
-    case TX_ACT_RELU: return v > 0.f ? v : 0.f;
-    case TX_ACT_TANH: return tanhf(v);
-    case TX_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-  }
-  return v;
-}
-
-__device__ __forceinline__ float dact_f(int act, float s) {
-  switch (act) {
-    case TX_ACT_RELU: return s > 0.f ? 1.f : 0.f;
-    case TX_ACT_TANH: return 1.f - s * s;
-    case TX_ACT_GELU: {
-      float cdf = 0.5f * (1.0f + erff(s * 0.70710678118654752f));
-      return cdf + s * expf(-0.5f * s * s) * 0.39894228040143268f;
-    }
-  }
-  return 1.f;
-}
+__device__ __forceinline__ float act_f(int act, float v) { return tx_epi::act(act, v); }
+__device__ __forceinline__ float dact_f(int act, float s) { return tx_epi::dact(act, s); }
 
 // Epilogue over one transposed 32x32 chunk: lane = column, rr walks rows.
 // The common cases (no beta, no pre-activation store, no act') run a tight
@@ -234,18 +217,79 @@ __device__ __forceinline__ void epi_rows_fast(const float *__restrict__ t, int l
   }
 }
 
-__device__ __noinline__ void epi_rows_general(const float *__restrict__ t, int lane, const tx_gemm_desc &d,
-                                              float *C, int64_t cbase, int64_t row0, int64_t gn,
-                                              int rows, float bias_v) {
+// Epilogue arguments that stay in registers across the chunk loop.
+struct EpiArgs {
+  float alpha, beta;
+  int act, dact;
+  float *C;
+  int64_t ldc;
+  float *preact;
+  int64_t ld_preact;
+  const float *dact_src;
+  int64_t ld_dact;
+};
+
+// Epilogue with beta * C, a pre-activation store or act', specialised on the
+// activation pair so that the 32 unrolled rows hold only the math they run
+// (a runtime switch inlined 32 times spreads each row's few instructions over
+// tens of KB of code and the warps stall on instruction fetch).  All loads of
+// the chunk's rows are issued before the first store: the stores may alias the
+// loaded tensors, so interleaving them would cost one round trip per row.
+template <int ACT, int DACT>
+__device__ __forceinline__ void epi_rows_spec(const float *__restrict__ t, int lane, const EpiArgs &e,
+                                              int64_t row0, int64_t gn, int rows, bool has_bias,
+                                              float bias_v) {
+  const bool beta = e.beta != 0.f;
+  float cv[32], sv[32];
+#pragma unroll
+  for (int rr = 0; rr < 32; ++rr) {
+    const bool ok = rr < rows;
+    cv[rr] = (ok && beta) ? e.C[(row0 + rr) * e.ldc + gn] : 0.f;
+    sv[rr] = (DACT != TX_ACT_NONE && ok) ? __ldg(e.dact_src + (row0 + rr) * e.ld_dact + gn) : 0.f;
+  }
+#pragma unroll
+  for (int rr = 0; rr < 32; ++rr) {
+    if (rr < rows) {
+      float x = e.alpha * t[rr * 33 + lane];
+      if (has_bias) x += bias_v;
+      if (beta) x += e.beta * cv[rr];
+      if (e.preact) e.preact[(row0 + rr) * e.ld_preact + gn] = x;
+      x = act_f(ACT, x);
+      if (DACT != TX_ACT_NONE) x *= dact_f(DACT, sv[rr]);
+      e.C[(row0 + rr) * e.ldc + gn] = x;
+    }
+  }
+}
+
+// Both an activation and act' in one epilogue (no workload lowers to this):
+// compact runtime loop.
+__device__ __noinline__ void epi_rows_any(const float *__restrict__ t, int lane, const EpiArgs &e,
+                                          int64_t row0, int64_t gn, int rows, bool has_bias,
+                                          float bias_v) {
+#pragma unroll 1
   for (int rr = 0; rr < rows; ++rr) {
     const int64_t gm = row0 + rr;
-    float x = d.alpha * t[rr * 33 + lane];
-    if (d.bias) x += bias_v;
-    if (d.beta != 0.f) x += d.beta * C[gm * d.ldc + gn];
-    if (d.preact) d.preact[cbase + gm * d.ld_preact + gn] = x;
-    x = act_f(d.act, x);
-    if (d.dact) x *= dact_f(d.dact, d.dact_src[cbase + gm * d.ld_dact + gn]);
-    C[gm * d.ldc + gn] = x;
+    float x = e.alpha * t[rr * 33 + lane];
+    if (has_bias) x += bias_v;
+    if (e.beta != 0.f) x += e.beta * e.C[gm * e.ldc + gn];
+    if (e.preact) e.preact[gm * e.ld_preact + gn] = x;
+    x = act_f(e.act, x);
+    x *= dact_f(e.dact, e.dact_src[gm * e.ld_dact + gn]);
+    e.C[gm * e.ldc + gn] = x;
+  }
+}
+
+// Hint the rows of a tensor this CTA's epilogue will read into L2 while the
+// main loop runs (bulk prefetch; in-bounds, 16-byte aligned spans only).
+__device__ __forceinline__ void prefetch_rows_l2(const float *base, int64_t ld, int64_t row0,
+                                                 int64_t rows, int64_t col0, int64_t cols, int lane) {
+  if (!base || cols <= 0 || rows <= 0) return;
+  const float *p0 = base + row0 * ld + col0;
+  uint32_t bytes = (uint32_t)(cols * 4) & ~15u;
+  if (((uintptr_t)p0 & 15) || (ld & 3) || bytes == 0) return;
+  for (int64_t r = lane; r < rows; r += 32) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p0 + r * ld), "r"(bytes)
+                 : "memory");
   }
 }
 
@@ -356,6 +400,16 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int ct = threadIdx.x - 64;  // 0..127
+    {
+      // the epilogue's reads of C (beta) and of the act' source hit L2, not DRAM
+      const int q = warp & 3;
+      const int64_t r0 = (int64_t)m0 + q * 32;
+      const int64_t nrows = d.M - r0 < 32 ? d.M - r0 : 32;
+      const int64_t ncols = d.N - n0 < BN ? d.N - n0 : BN;
+      const int64_t cb = (int64_t)bz * d.stride_c;
+      if (d.dact) prefetch_rows_l2(d.dact_src + cb, d.ld_dact, r0, nrows, n0, ncols, lane);
+      if (d.beta != 0.f) prefetch_rows_l2(d.C + cb, d.ldc, r0, nrows, n0, ncols, lane);
+    }
     if (MODE != 0) {
       // operand conversion, one stage behind the producer and one ahead of the MMA
       constexpr int N4 = (A_BYTES + B_BYTES) / 16;
@@ -392,6 +446,9 @@ __global__ void __launch_bounds__(192, 1)
       const int64_t row0 = (int64_t)m0 + quad * 32;
       float *C = d.C + (int64_t)bz * d.stride_c;
       const int64_t cbase = bz * d.stride_c;
+      const EpiArgs ea{d.alpha, d.beta, d.act, d.dact, C, d.ldc,
+                       d.preact ? d.preact + cbase : nullptr, d.ld_preact,
+                       d.dact_src ? d.dact_src + cbase : nullptr, d.ld_dact};
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -420,8 +477,23 @@ __global__ void __launch_bounds__(192, 1)
             case TX_ACT_GELU: epi_rows_fast<TX_ACT_GELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
             default: epi_rows_fast<TX_ACT_NONE>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
           }
+        } else if (!d.dact) {
+          const bool hb = d.bias != nullptr;
+          switch (d.act) {
+            case TX_ACT_RELU: epi_rows_spec<TX_ACT_RELU, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+            case TX_ACT_TANH: epi_rows_spec<TX_ACT_TANH, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+            case TX_ACT_GELU: epi_rows_spec<TX_ACT_GELU, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+            default: epi_rows_spec<TX_ACT_NONE, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+          }
+        } else if (d.act == TX_ACT_NONE) {
+          const bool hb = d.bias != nullptr;
+          switch (d.dact) {
+            case TX_ACT_RELU: epi_rows_spec<TX_ACT_NONE, TX_ACT_RELU>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+            case TX_ACT_TANH: epi_rows_spec<TX_ACT_NONE, TX_ACT_TANH>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+            default: epi_rows_spec<TX_ACT_NONE, TX_ACT_GELU>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
+          }
         } else {
-          epi_rows_general(tile, lane, d, C, cbase, row0, gn, rows, bias_v);
+          epi_rows_any(tile, lane, ea, row0, gn, rows, d.bias != nullptr, bias_v);
         }
         __syncwarp();
       }

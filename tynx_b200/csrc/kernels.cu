@@ -454,8 +454,18 @@ __global__ void k_sum_partials(const float *__restrict__ part, int64_t np, int64
                                float *__restrict__ out, float scale, int acc) {
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols;
        c += (int64_t)gridDim.x * blockDim.x) {
+    // partials added in index order, four loads in flight
     float s = 0.f;
-    for (int64_t p = 0; p < np; ++p) s += part[p * cols + c];
+    int64_t p = 0;
+    for (; p + 4 <= np; p += 4) {
+      const float v0 = part[p * cols + c], v1 = part[(p + 1) * cols + c];
+      const float v2 = part[(p + 2) * cols + c], v3 = part[(p + 3) * cols + c];
+      s += v0;
+      s += v1;
+      s += v2;
+      s += v3;
+    }
+    for (; p < np; ++p) s += part[p * cols + c];
     s *= scale;
     out[c] = acc ? out[c] + s : s;
   }
@@ -541,6 +551,54 @@ __global__ void k_take_last_bwd(const int64_t *__restrict__ idx, const float *__
 
 // ---- column sums (bias gradient) --------------------------------------------------------
 // block (32, 8): 32 columns x 8 row lanes, rows [blockIdx.y*rows_per, ...)
+// float4 columns (N % 4 == 0, 16-byte aligned rows): block (32, 8) covers 128
+// columns; each thread sums rows r0 + ty, r0 + ty + 8, ... in order with four
+// loads in flight, then the 8 row groups are combined in a fixed order.
+__global__ void k_colsum_partial4(const float *__restrict__ dy, int64_t M, int64_t N,
+                                  int64_t rows_per, float *__restrict__ part) {
+  __shared__ float4 sm[8][32];
+  const int64_t c = ((int64_t)blockIdx.x * 32 + threadIdx.x) * 4;
+  const int64_t r0 = blockIdx.y * rows_per;
+  const int64_t r1 = r0 + rows_per < M ? r0 + rows_per : M;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c < N) {
+    int64_t r = r0 + threadIdx.y;
+    for (; r + 24 < r1; r += 32) {
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const float4 *>(dy + (r + 8 * j) * N + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s.x += v[j].x;
+        s.y += v[j].y;
+        s.z += v[j].z;
+        s.w += v[j].w;
+      }
+    }
+    for (; r < r1; r += 8) {
+      const float4 v = *reinterpret_cast<const float4 *>(dy + r * N + c);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+  }
+  sm[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < N) {
+    float4 t = sm[0][threadIdx.x];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) {
+      const float4 u = sm[i][threadIdx.x];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    *reinterpret_cast<float4 *>(part + blockIdx.y * N + c) = t;
+  }
+}
+
 __global__ void k_colsum_partial(const float *__restrict__ dy, int64_t M, int64_t N,
                                  int64_t rows_per, float *__restrict__ part) {
   __shared__ float sm[8][33];
@@ -985,7 +1043,8 @@ extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, 
     return TX_OK;
   }
   // split the rows so that the grid fills the machine
-  int64_t col_blocks = (N + 31) / 32;
+  const bool vec = (N % 4 == 0) && ((((uintptr_t)dy) & 15) == 0);
+  int64_t col_blocks = vec ? (N + 127) / 128 : (N + 31) / 32;
   int64_t splits = (ctx->num_sms * 4 + col_blocks - 1) / col_blocks;
   int64_t max_splits = (M + 63) / 64;
   if (splits > max_splits) splits = max_splits;
@@ -994,8 +1053,12 @@ extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, 
   int64_t rows_per = (M + splits - 1) / splits;
   Scratch part(ctx, splits * N * sizeof(float));
   if (!part.ptr) return TX_ERR_OOM;
-  k_colsum_partial<<<dim3((unsigned)col_blocks, (unsigned)splits), dim3(32, 8), 0, ctx->stream>>>(
-      dy, M, N, rows_per, part.as<float>());
+  if (vec)
+    k_colsum_partial4<<<dim3((unsigned)col_blocks, (unsigned)splits), dim3(32, 8), 0, ctx->stream>>>(
+        dy, M, N, rows_per, part.as<float>());
+  else
+    k_colsum_partial<<<dim3((unsigned)col_blocks, (unsigned)splits), dim3(32, 8), 0, ctx->stream>>>(
+        dy, M, N, rows_per, part.as<float>());
   TX_LAUNCHED(ctx, "k_colsum_partial");
   k_sum_partials<<<grid_for(N, 256), 256, 0, ctx->stream>>>(part.as<float>(), splits, N, db, scale, acc);
   TX_LAUNCHED(ctx, "k_sum_partials");
