@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.h"
@@ -48,7 +49,11 @@ struct TcCfg {
   // 3xTF32 keeps the small halves of both operands next to the big ones
   static constexpr int STAGE = (A_BYTES + B_BYTES) * (MODE == 2 ? 2 : 1);
   static constexpr int STAGES = (196 * 1024 / STAGE) > 8 ? 8 : (196 * 1024 / STAGE);
-  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 512 /*barriers*/;
+  static constexpr int TAIL = 2048;  // barriers, TMEM address, abort flag, per-warp bias rows
+  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + TAIL;
+  // The TMA epilogue reuses the drained stages: per epilogue warp, two output,
+  // two pre-activation, two act'-source and two C tiles of 32 x 32 fp32.
+  static_assert(STAGES * STAGE >= 4 * 8 * 4096, "epilogue tiles must fit in the stage memory");
   // The tensor core adds each MMA's products into the fp32 TMEM accumulator
   // with a biased (toward zero) rounding, so the error grows with the number
   // of MMAs in one chain.  k-blocks are dealt round-robin to NACC accumulators
@@ -111,6 +116,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Wait for a phase regardless of the abort flag (a copy in flight must land
+// before its shared memory is released), still bounded in time.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  while (!mbar_try(bar, parity) && global_ns() - start < kWaitLimitNs) {
+  }
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint64_t *bar,
                                             int x, int y, int z) {
   asm volatile(
@@ -118,6 +131,38 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// A 32 x 32 fp32 tile as TMA writes and reads it with the 128-byte swizzle:
+// row r is 128 bytes at r * 128, and its 16-byte chunk j sits at chunk
+// j ^ (r & 7).  A thread that owns row r moves the row with 8 float4 accesses;
+// the 8 lanes of one shared-memory phase hit 8 different chunks.
+__device__ __forceinline__ void tile_row_load(const uint8_t *tile, int r, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 t = *reinterpret_cast<const float4 *>(tile + r * 128 + ((j ^ (r & 7)) << 4));
+    v[4 * j] = t.x;
+    v[4 * j + 1] = t.y;
+    v[4 * j + 2] = t.z;
+    v[4 * j + 3] = t.w;
+  }
+}
+__device__ __forceinline__ void tile_row_store(uint8_t *tile, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4 *>(tile + r * 128 + ((j ^ (r & 7)) << 4)) =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -293,10 +338,38 @@ __device__ __forceinline__ void prefetch_rows_l2(const float *base, int64_t ld, 
   }
 }
 
+// Row-form epilogue of one 32-column chunk (this thread's accumulator row):
+// x = alpha * acc + bias (+ beta * C), optionally stored as the pre-activation,
+// then act and * act'(s).  ACT / DACT are compile-time (-1: runtime values).
+template <int ACT, int DACT>
+__device__ __forceinline__ void chunk_math(float (&v)[32], const float (&sv)[32], const float (&cv)[32],
+                                           const float *bw, const tx_gemm_desc &d, bool use_beta,
+                                           uint8_t *pre_tile, int lane) {
+  const int act = ACT >= 0 ? ACT : d.act;
+  const int dact = DACT >= 0 ? DACT : d.dact;
+  const bool has_bias = d.bias != nullptr;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = d.alpha * v[j];
+    if (has_bias) x += bw[j];
+    if (use_beta) x += d.beta * cv[j];
+    v[j] = x;
+  }
+  if (pre_tile) tile_row_store(pre_tile, lane, v);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = act_f(act, v[j]);
+    if (dact != TX_ACT_NONE) x *= dact_f(dact, sv[j]);
+    v[j] = x;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const tx_gemm_desc d, int *err, int kb_per_cta) {
+              const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
+              const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
+              int tma_epi) {
   using Cfg = TcCfg<BN, MODE>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -307,8 +380,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t *conv = full + STAGES;
   uint64_t *empty = conv + STAGES;
   uint64_t *accb = empty + STAGES;
-  uint32_t *tmem_holder = (uint32_t *)(accb + 1);
+  uint64_t *ebar = accb + 1;  // two act'/C tile-load slots per epilogue warp
+  uint32_t *tmem_holder = (uint32_t *)(ebar + 8);
   volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
+  float *bias_rows = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -330,6 +405,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&ebar[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -437,7 +513,92 @@ __global__ void __launch_bounds__(192, 1)
     const int quad = warp & 3;
     const bool have = mbar_wait(accb, 0, abort_flag, err, 3);
     tc_fence_after();
-    if (have && !*abort_flag) {
+    if (have && !*abort_flag && tma_epi) {
+      // TMA epilogue.  Each thread keeps its accumulator row: the act' source
+      // and the beta*C input arrive as swizzled 32 x 32 tiles (TMA loads into a
+      // two-slot ring, issued two chunks ahead); results go to swizzled output
+      // (and pre-activation) tiles that one lane stores with TMA, double
+      // buffered.  The drained pipeline stages hold the tiles.
+      constexpr int NCH = BN / 32;
+      uint8_t *eb = smem + quad * (8 * 4096);
+      const bool need_s = d.dact != TX_ACT_NONE;
+      const bool need_c = d.beta != 0.f;
+      const bool need_p = d.preact != nullptr;
+      const bool loads = need_s || need_c;
+      const int row_tile = m0 + quad * 32;
+      float *bw = bias_rows + quad * 32;
+      auto issue = [&](int c) {
+        const int slot = c & 1;
+        uint64_t *bar = &ebar[quad * 2 + slot];
+        mbar_expect_tx(bar, (need_s ? 4096u : 0u) + (need_c ? 4096u : 0u));
+        if (need_s) tma_load_3d(smem_u32(eb + (4 + slot) * 4096), &mapS, bar, n0 + 32 * c, row_tile, bz);
+        if (need_c) tma_load_3d(smem_u32(eb + (6 + slot) * 4096), &mapC, bar, n0 + 32 * c, row_tile, bz);
+      };
+      int issued = 0, consumed = 0;
+      if (loads && lane == 0)
+        for (; issued < (NCH < 2 ? NCH : 2); ++issued) issue(issued);
+      issued = __shfl_sync(0xffffffffu, issued, 0);
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c) {
+        const int slot = c & 1;
+        float v[32], sv[32], cv[32];
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32);
+        tmem_ld32(lane_base, v);
+#pragma unroll 1
+        for (int a = 1; a < used_acc; ++a) {
+          float w[32];
+          tmem_ld32(lane_base + (uint32_t)(a * BN), w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += w[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[j] = cv[j] = 0.f;
+        if (loads) {
+          if (!mbar_wait(&ebar[quad * 2 + slot], (c >> 1) & 1, abort_flag, err, 5)) break;
+          ++consumed;
+          if (need_s) tile_row_load(eb + (4 + slot) * 4096, lane, sv);
+          if (need_c) tile_row_load(eb + (6 + slot) * 4096, lane, cv);
+          __syncwarp();
+          if (lane == 0 && c + 2 < NCH) issue(c + 2);
+          if (c + 2 < NCH) ++issued;
+        }
+        const int64_t gnb = (int64_t)n0 + c * 32 + lane;
+        bw[lane] = (d.bias && gnb < d.N) ? d.bias[gnb] * d.bias_scale : 0.f;
+        if (lane == 0 && c >= 2) bulk_wait_read<1>();  // the tiles of chunk c - 2 are free
+        __syncwarp();
+        uint8_t *pre_tile = need_p ? eb + (2 + slot) * 4096 : nullptr;
+        if (!d.dact) {
+          switch (d.act) {
+            case TX_ACT_RELU: chunk_math<TX_ACT_RELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_TANH: chunk_math<TX_ACT_TANH, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_GELU: chunk_math<TX_ACT_GELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            default: chunk_math<TX_ACT_NONE, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+          }
+        } else if (d.act == TX_ACT_NONE) {
+          switch (d.dact) {
+            case TX_ACT_RELU: chunk_math<TX_ACT_NONE, TX_ACT_RELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_TANH: chunk_math<TX_ACT_NONE, TX_ACT_TANH>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            default: chunk_math<TX_ACT_NONE, TX_ACT_GELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+          }
+        } else {
+          chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
+        }
+        tile_row_store(eb + slot * 4096, lane, v);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&mapC, smem_u32(eb + slot * 4096), n0 + 32 * c, row_tile, bz);
+          if (need_p) tma_store_3d(&mapP, smem_u32(pre_tile), n0 + 32 * c, row_tile, bz);
+          bulk_commit();
+        }
+        __syncwarp();
+      }
+      // after an abort, let the tile loads already in flight land before the
+      // shared memory is released (bounded like every other wait)
+      for (int c = consumed; c < issued; ++c) mbar_drain(&ebar[quad * 2 + (c & 1)], (c >> 1) & 1);
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+    } else if (have && !*abort_flag) {
       // TMEM gives each thread one row; global memory wants a warp per row.
       // Each 32x32 chunk is transposed through padded shared memory (the
       // drained pipeline stages), then lanes walk columns so every load and
@@ -541,10 +702,16 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// Tensor maps of one launch: the operands, and for the TMA epilogue the
+// output (also the beta * C input), the act' source and the pre-activation.
+struct Maps {
+  CUtensorMap a, b, c, s, p;
+  int tma_epi = 0;
+};
+
 // `z` = batch count, or the number of K splits when kb_per_cta > 0
 template <int BN, bool A_MN, bool B_MN, int MODE>
-int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
-              int64_t z, int kb_per_cta) {
+int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
   auto kern = k_gemm_tc<BN, A_MN, B_MN, MODE>;
   static bool configured[64] = {};
   int dev = ctx->device & 63;
@@ -553,38 +720,56 @@ int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const C
     configured[dev] = true;
   }
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
-  kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(ma, mb, d, ctx->d_err, kb_per_cta);
+  kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
+                                                          kb_per_cta, m.tma_epi);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
 
 template <int BN, int MODE>
-int launch_bn(tx_ctx *ctx, const tx_gemm_desc &d, const CUtensorMap &ma, const CUtensorMap &mb,
-              int64_t z, int kb_per_cta) {
+int launch_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_tc<BN, true, true, MODE>(ctx, d, ma, mb, z, kb_per_cta);
-  if (a_mn) return launch_tc<BN, true, false, MODE>(ctx, d, ma, mb, z, kb_per_cta);
-  if (b_mn) return launch_tc<BN, false, true, MODE>(ctx, d, ma, mb, z, kb_per_cta);
-  return launch_tc<BN, false, false, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+  if (a_mn && b_mn) return launch_tc<BN, true, true, MODE>(ctx, d, m, z, kb_per_cta);
+  if (a_mn) return launch_tc<BN, true, false, MODE>(ctx, d, m, z, kb_per_cta);
+  if (b_mn) return launch_tc<BN, false, true, MODE>(ctx, d, m, z, kb_per_cta);
+  return launch_tc<BN, false, false, MODE>(ctx, d, m, z, kb_per_cta);
 }
 
 template <int MODE>
-int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const CUtensorMap &ma,
-                const CUtensorMap &mb, int64_t z, int kb_per_cta) {
+int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
   switch (bn) {
-    case 256: return launch_bn<256, MODE>(ctx, d, ma, mb, z, kb_per_cta);
-    case 64: return launch_bn<64, MODE>(ctx, d, ma, mb, z, kb_per_cta);
-    default: return launch_bn<128, MODE>(ctx, d, ma, mb, z, kb_per_cta);
+    case 256: return launch_bn<256, MODE>(ctx, d, m, z, kb_per_cta);
+    case 64: return launch_bn<64, MODE>(ctx, d, m, z, kb_per_cta);
+    default: return launch_bn<128, MODE>(ctx, d, m, z, kb_per_cta);
   }
 }
 
-int launch_any(tx_ctx *ctx, int mode, int bn, const tx_gemm_desc &d, const CUtensorMap &ma,
-               const CUtensorMap &mb, int64_t z, int kb_per_cta) {
+int launch_any(tx_ctx *ctx, int mode, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z,
+               int kb_per_cta) {
   switch (mode) {
-    case 0: return launch_mode<0>(ctx, bn, d, ma, mb, z, kb_per_cta);
-    case 2: return launch_mode<2>(ctx, bn, d, ma, mb, z, kb_per_cta);
-    default: return launch_mode<1>(ctx, bn, d, ma, mb, z, kb_per_cta);
+    case 0: return launch_mode<0>(ctx, bn, d, m, z, kb_per_cta);
+    case 2: return launch_mode<2>(ctx, bn, d, m, z, kb_per_cta);
+    default: return launch_mode<1>(ctx, bn, d, m, z, kb_per_cta);
   }
+}
+
+// A row-major [batch][M][N] fp32 tensor TMA can tile: 16-byte aligned base,
+// row and batch strides that are 16-byte multiples.
+bool tma_tileable(const float *p, int64_t ld, int64_t batch, int64_t stride) {
+  return p && ((uintptr_t)p & 15) == 0 && (ld & 3) == 0 && (batch <= 1 || (stride & 3) == 0);
+}
+
+// Output-side maps (32 x 32 boxes, 128-byte swizzle); false: use the
+// register epilogue instead.
+bool make_epilogue_maps(Maps &m, const tx_gemm_desc &d, int64_t z) {
+  if (!tma_tileable(d.C, d.ldc, z, d.stride_c)) return false;
+  if (d.dact && !tma_tileable(d.dact_src, d.ld_dact, z, d.stride_c)) return false;
+  if (d.preact && !tma_tileable(d.preact, d.ld_preact, z, d.stride_c)) return false;
+  if (!make_map(&m.c, d.C, d.N, d.M, d.ldc, z, d.stride_c, 32, false)) return false;
+  if (d.dact && !make_map(&m.s, d.dact_src, d.N, d.M, d.ld_dact, z, d.stride_c, 32, false)) return false;
+  if (d.preact && !make_map(&m.p, d.preact, d.N, d.M, d.ld_preact, z, d.stride_c, 32, false)) return false;
+  m.tma_epi = 1;
+  return true;
 }
 
 struct Tiling {
@@ -648,17 +833,18 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
 
   const Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
   const int bn = tiling.bn;
-  CUtensorMap ma, mb;
+  Maps m;
+  memset(&m, 0, sizeof m);
   bool ok;
   if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
-    ok = make_map(&ma, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
+    ok = make_map(&m.a, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
   else  // A stored M x K (K-major): box 32(K) x 128(M)
-    ok = make_map(&ma, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
+    ok = make_map(&m.a, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
   if (!ok) return TX_ERR_UNSUPPORTED;
   if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N)
-    ok = make_map(&mb, d.B, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
+    ok = make_map(&m.b, d.B, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
   else  // B stored K x N (MN-major): box 32(N) x 32(K)
-    ok = make_map(&mb, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
+    ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
 
   // Split K across CTAs when the output has fewer tiles than SMs (the weight
@@ -667,7 +853,10 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   // epilogue.  Shorter accumulation chains are also more accurate.
   const int total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
   int splits = tiling.splits;
-  if (splits <= 1) return launch_any(ctx, mode, bn, d, ma, mb, batch, 0);
+  if (splits <= 1) {
+    make_epilogue_maps(m, d, batch);
+    return launch_any(ctx, mode, bn, d, m, batch, 0);
+  }
   const int kb_per = (total_kb + splits - 1) / splits;
   splits = (total_kb + kb_per - 1) / kb_per;
   Scratch part(ctx, (size_t)splits * d.M * d.N * sizeof(float));
@@ -683,6 +872,7 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   raw.preact = nullptr;
   raw.dact = TX_ACT_NONE;
   raw.dact_src = nullptr;
-  TX_TRY(launch_any(ctx, mode, bn, raw, ma, mb, splits, kb_per));
+  make_epilogue_maps(m, raw, splits);
+  TX_TRY(launch_any(ctx, mode, bn, raw, m, splits, kb_per));
   return gemm_split_reduce(ctx, d, part.as<float>(), splits);
 }
