@@ -142,8 +142,18 @@ typedef struct tx_gemm_desc {
    * saved forward output (relu, tanh) or pre-activation (gelu) */
   const float *dact_src; int64_t ld_dact; int32_t dact;
   int64_t batch; int64_t stride_a, stride_b, stride_c; /* strided batch (batch<=1: single) */
+  int32_t flags;                               /* TX_GEMM_* below; 0 = none */
 } tx_gemm_desc;
+/* flags: in TX_MATH_TF32 (round-to-nearest) mode the contraction rounds each
+ * operand element to TF32 (cvt.rna).  An operand whose buffer already holds
+ * such values (A_TF32 / B_TF32) is used as is; ROUND_OUT stores C rounded the
+ * same way, for a result that only feeds further contractions.  Other math
+ * modes ignore the flags. */
+enum { TX_GEMM_A_TF32 = 1, TX_GEMM_B_TF32 = 2, TX_GEMM_ROUND_OUT = 4 };
 int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc);
+/* dst[i] = src[i] rounded to TF32 (round to nearest, ties away from zero;
+ * dst may equal src).  The operand shadow of TX_GEMM_A_TF32 / B_TF32. */
+int tx_round_tf32(tx_ctx *ctx, const float *d_src, float *d_dst, int64_t n);
 
 /* Elementwise.  replaces: DynTensor activations (tensor.rs:2002-2240) and
  * broadcast arithmetic (tensor.rs:1637-1700). */

@@ -175,6 +175,66 @@ def test_skinny_gemm_full_epilogue(tx, math, case):
             assert float(np.abs(got_pre[z, :, :Nn] - pre).max()) < 1e-5 * scale
 
 
+def _np_round_tf32(x):
+    """Round float32 to a 10-bit mantissa, to nearest with ties away from zero
+    (add half of the dropped 13-bit field to the magnitude, then truncate)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    sign = u & np.uint32(0x80000000)
+    mag = (u & np.uint32(0x7FFFFFFF)) + np.uint32(0x1000)
+    return ((mag & np.uint32(0xFFFFE000)) | sign).view(np.float32)
+
+
+def test_round_tf32_matches_definition(tx):
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    rng = np.random.default_rng(11)
+    x = np.concatenate([rng.standard_normal(100003).astype(np.float32) * 1e3,
+                        (rng.standard_normal(1000) * 1e-40).astype(np.float32),  # subnormals
+                        np.array([0.0, -0.0, 1.0 + 2.0 ** -11, -(1.0 + 2.0 ** -11)], np.float32)])
+    ctx = _core.context()
+    src = tx.Tensor(x)
+    dst = tx.zeros(x.size)
+    ctx.check(N.lib.tx_round_tf32(ctx.handle, src.ptr, dst.ptr, x.size))
+    np.testing.assert_array_equal(dst.numpy().view(np.uint32), _np_round_tf32(x).view(np.uint32))
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 1), (1, 0)])
+def test_pre_rounded_operands_and_rounded_output(tx, ta, tb):
+    """TF32 mode: operands flagged as already rounded skip the kernel's own
+    rounding (same bits), and ROUND_OUT stores round_tf32 of the same result."""
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    rng = np.random.default_rng(12)
+    M, Nn, K = 1024, 768, 512
+    A = _np_round_tf32(rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32))
+    B = _np_round_tf32(rng.standard_normal((Nn, K) if tb else (K, Nn)).astype(np.float32))
+    bias = rng.standard_normal(Nn).astype(np.float32)
+    ctx = _core.context()
+    ctx.math = "tf32"
+    a, b, bb = tx.Tensor(A), tx.Tensor(B), tx.Tensor(bias)
+
+    def run(flags):
+        c = tx.zeros(M, Nn)
+        d = N.GemmDesc()
+        d.M, d.N, d.K = M, Nn, K
+        d.A, d.lda, d.trans_a = a.ptr, A.shape[1], ta
+        d.B, d.ldb, d.trans_b = b.ptr, B.shape[1], tb
+        d.C, d.ldc = c.ptr, Nn
+        d.alpha, d.bias, d.bias_scale, d.act, d.batch = 1.0, bb.ptr, 1.0, N.ACT["relu"], 1
+        d.flags = flags
+        ctx.check(N.lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
+        return c.numpy()
+
+    base = run(0)
+    np.testing.assert_array_equal(run(N.TX_GEMM_A_TF32), base)
+    np.testing.assert_array_equal(run(N.TX_GEMM_B_TF32), base)
+    np.testing.assert_array_equal(run(N.TX_GEMM_A_TF32 | N.TX_GEMM_B_TF32), base)
+    rounded = run(N.TX_GEMM_A_TF32 | N.TX_GEMM_B_TF32 | N.TX_GEMM_ROUND_OUT)
+    np.testing.assert_array_equal(rounded.view(np.uint32), _np_round_tf32(base).view(np.uint32))
+
+
 def test_softmax_xent_matches_oracle(tx):
     from oracle import flex_oracle as fo
     from tynx_b200 import nn

@@ -35,6 +35,7 @@ TX_MATH = {"tf32": 0, "3xtf32": 1, "fp32": 2, "tf32trunc": 3}
 MAX_DIMS = 8
 
 ACT = {"none": 0, "relu": 1, "tanh": 2, "gelu": 3}
+TX_GEMM_A_TF32, TX_GEMM_B_TF32, TX_GEMM_ROUND_OUT = 1, 2, 4
 UN = {"neg": 0, "exp": 1, "log": 2, "relu": 3, "tanh": 4, "gelu": 5, "sigmoid": 6, "clamp": 7,
       "sqrt": 8, "abs": 9, "scale": 10, "pow": 11}
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "min": 4, "max": 5, "le": 6, "ge": 7, "pow": 8}
@@ -66,7 +67,7 @@ class GemmDesc(C.Structure):
         ("preact", C.c_void_p), ("ld_preact", C.c_int64),
         ("dact_src", C.c_void_p), ("ld_dact", C.c_int64), ("dact", C.c_int32),
         ("batch", C.c_int64), ("stride_a", C.c_int64), ("stride_b", C.c_int64),
-        ("stride_c", C.c_int64),
+        ("stride_c", C.c_int64), ("flags", C.c_int32),
     ]
 
 
@@ -147,6 +148,7 @@ SIGNATURES = {
     "tx_take_last": [_vp, _vp, _vp, _vp, _i64, _i64],
     "tx_take_last_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i32],
     "tx_bias_grad": [_vp, _vp, _vp, _i64, _i64, _f, _i32],
+    "tx_round_tf32": [_vp, _vp, _vp, _i64],
     "tx_optim_create": [_vp, C.POINTER(OptimCfg), _i32, C.POINTER(_vp), C.POINTER(_vp), _p64,
                         C.POINTER(_vp)],
     "tx_optim_set_lr": [_vp, C.c_double],

@@ -212,6 +212,10 @@ struct GNode {
   int fused_act = TX_ACT_NONE;  // GEMM/MATMUL: absorbed activation
   int fused_into = -1;          // activation node absorbed by node index
   int fused_out = -1;           // value written by the fused epilogue
+  // TF32 mode: the epilogue may store its result rounded to TF32, because every
+  // reader of it rounds it so anyway (GEMM operands) or only looks at its sign
+  // (the relu mask); set at graph creation
+  bool round_out = false;
 };
 
 struct tx_graph {
@@ -224,6 +228,7 @@ struct tx_graph {
   std::vector<int64_t> param_offset;  // offset in flat buffers
   float *flat_values = nullptr;
   float *flat_grads = nullptr;
+  float *flat_tf32 = nullptr;  // TF32-rounded copy of flat_values (GEMM operands)
   int64_t flat_len = 0;
   // DP
   bool dp = false;
@@ -238,6 +243,8 @@ struct tx_record {
   std::vector<bool> owned;           // buffer owned by the record
   std::vector<void *> extra;         // per node saved extras
   std::vector<std::vector<void *>> extra2;
+  std::vector<bool> tf32;  // per value: the buffer holds TF32-rounded values
+  bool shadow = false;     // parameters read by GEMMs come from flat_tf32
   bool tracking = false;
 };
 
@@ -521,6 +528,24 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     a.fused_into = i;
   }
 
+  // ---- TF32 output rounding: results whose every reader is a contraction --------------------
+  for (int i = 0; i < n_nodes; ++i) {
+    GNode &n = g->nodes[i];
+    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL) continue;
+    if (n.fused_act == TX_ACT_TANH) continue;  // tanh' reads the stored output
+    const int yv = n.fused_act ? n.fused_out : n.d.out[0];
+    const GValue &y = g->values[yv];
+    if (y.is_output || y.consumers.empty()) continue;
+    bool ok = true;
+    for (int c : y.consumers) {
+      const tx_node_desc &cd = g->nodes[c].d;
+      if (cd.op != TX_OP_GEMM && cd.op != TX_OP_MATMUL) { ok = false; break; }
+      for (int k = 2; k < cd.n_in; ++k)
+        if (cd.in[k] == yv) ok = false;  // a bias is not a contraction operand
+    }
+    n.round_out = ok;
+  }
+
   // ---- parameter storage: order = when gradients become final in backward -----------------
   std::vector<int> first_use(g->params.size(), n_nodes);
   for (int i = 0; i < n_nodes; ++i)
@@ -580,6 +605,7 @@ extern "C" int tx_graph_destroy(tx_graph *g) {
     if (v.kind == TX_VAL_CONST && v.dev) cudaFree(v.dev);
   if (g->flat_values) cudaFree(g->flat_values);
   if (g->flat_grads) cudaFree(g->flat_grads);
+  if (g->flat_tf32) cudaFree(g->flat_tf32);
   delete g;
   return TX_OK;
 }
@@ -660,6 +686,19 @@ extern "C" int tx_graph_infer(tx_graph *g, const int64_t *in_shapes, const int32
 // ============================================================================
 namespace {
 
+// Pointer a contraction reads value v from, and whether those values are
+// already TF32-rounded (TX_GEMM_A_TF32 / B_TF32): parameters come from the
+// rounded shadow refreshed at the start of the forward.
+const float *gemm_operand(tx_graph *g, tx_record *r, int v, bool *tf32) {
+  const GValue &gv = g->values[v];
+  if (r->shadow && gv.kind == TX_VAL_PARAM) {
+    *tf32 = true;
+    return g->flat_tf32 + g->param_offset[gv.param_index];
+  }
+  *tf32 = r->tf32[v];
+  return (const float *)r->buf[v];
+}
+
 struct Fwd {
   tx_graph *g;
   tx_ctx *ctx;
@@ -688,6 +727,7 @@ struct Fwd {
     q.alpha = 1.f;
     q.batch = 1;
     q.act = n.fused_act;
+    bool a32 = false, b32 = false;
     if (n.fused_act == TX_ACT_GELU) {
       r->extra[ni] = tx_alloc_raw(ctx, numel_of(S(yv)) * 4);
       if (!r->extra[ni]) return TX_ERR_OOM;
@@ -698,9 +738,9 @@ struct Fwd {
       q.M = q.trans_a ? a[1] : a[0];
       q.K = q.trans_a ? a[0] : a[1];
       q.N = q.trans_b ? b[0] : b[1];
-      q.A = F(d.in[0]);
+      q.A = gemm_operand(g, r, d.in[0], &a32);
       q.lda = a[1];
-      q.B = F(d.in[1]);
+      q.B = gemm_operand(g, r, d.in[1], &b32);
       q.ldb = b[1];
       q.alpha = (float)d.fattr[0];
       if (d.n_in > 2 && d.in[2] >= 0) {
@@ -716,17 +756,17 @@ struct Fwd {
       q.N = b.back();
       if (b.size() == 2) {
         q.M = numel_of(a) / q.K;
-        q.A = F(d.in[0]);
+        q.A = gemm_operand(g, r, d.in[0], &a32);
         q.lda = q.K;
-        q.B = F(d.in[1]);
+        q.B = gemm_operand(g, r, d.in[1], &b32);
         q.ldb = q.N;
       } else {
         q.M = a[a.size() - 2];
         q.batch = numel_of(a) / (q.M * q.K);
-        q.A = F(d.in[0]);
+        q.A = gemm_operand(g, r, d.in[0], &a32);
         q.lda = q.K;
         q.stride_a = q.M * q.K;
-        q.B = F(d.in[1]);
+        q.B = gemm_operand(g, r, d.in[1], &b32);
         q.ldb = q.N;
         q.stride_b = q.K * q.N;
         q.stride_c = q.M * q.N;
@@ -737,6 +777,11 @@ struct Fwd {
     if (n.fused_act == TX_ACT_GELU) {
       q.preact = (float *)r->extra[ni];
       q.ld_preact = q.N;
+    }
+    q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0);
+    if (n.round_out && ctx->math == TX_MATH_TF32) {
+      q.flags |= TX_GEMM_ROUND_OUT;
+      r->tf32[yv] = true;
     }
     return gemm_dispatch(ctx, q);
   }
@@ -901,6 +946,15 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
   r->owned.assign(nv, false);
   r->extra.assign(g->nodes.size(), nullptr);
   r->extra2.assign(g->nodes.size(), {});
+  r->tf32.assign(nv, false);
+  if (ctx->math == TX_MATH_TF32 && g->flat_len > 0) {
+    // the contractions of this forward (and of its backward) read parameters
+    // from a TF32-rounded copy, refreshed here so that it always matches the
+    // fp32 values whatever changed them since
+    if (!g->flat_tf32) TX_CUDA(ctx, cudaMalloc(&g->flat_tf32, g->flat_len * sizeof(float)));
+    TX_TRY(tx_round_tf32(ctx, g->flat_values, g->flat_tf32, g->flat_len));
+    r->shadow = true;
+  }
   for (size_t i = 0; i < g->inputs.size(); ++i) r->buf[g->inputs[i]] = const_cast<void *>(d_inputs[i]);
   for (size_t i = 0; i < nv; ++i)
     if (g->values[i].kind == TX_VAL_PARAM || g->values[i].kind == TX_VAL_CONST) r->buf[i] = g->values[i].dev;
@@ -1061,16 +1115,20 @@ struct Bwd {
         rc = target(d.in[1], &t, &acc);
         tx_gemm_desc q; memset(&q, 0, sizeof q);
         q.alpha = alpha; q.beta = acc ? 1.f : 0.f; q.batch = 1;
+        bool x32 = false;
+        const float *x = gemm_operand(g, r, d.in[0], &x32);
         if (!tb) {  // dB[K,N] = op(A)^T dY
           q.M = K; q.N = N; q.K = M;
-          q.A = F(d.in[0]); q.lda = a[1]; q.trans_a = ta ? 0 : 1;
+          q.A = x; q.lda = a[1]; q.trans_a = ta ? 0 : 1;
           q.B = dz; q.ldb = N; q.trans_b = 0;
           q.C = t; q.ldc = N;
+          q.flags = x32 ? TX_GEMM_A_TF32 : 0;
         } else {    // dB[N,K] = dY^T op(A)
           q.M = N; q.N = K; q.K = M;
           q.A = dz; q.lda = N; q.trans_a = 1;
-          q.B = F(d.in[0]); q.ldb = a[1]; q.trans_b = ta ? 1 : 0;
+          q.B = x; q.ldb = a[1]; q.trans_b = ta ? 1 : 0;
           q.C = t; q.ldc = K;
+          q.flags = x32 ? TX_GEMM_B_TF32 : 0;
         }
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
         if (rc == TX_OK) wrote(d.in[1]);
@@ -1081,17 +1139,21 @@ struct Bwd {
         rc = dgrad_target(d.in[0], &t, &acc);
         tx_gemm_desc q; memset(&q, 0, sizeof q);
         q.alpha = alpha; q.beta = acc ? 1.f : 0.f; q.batch = 1;
+        bool w32 = false;
+        const float *w = gemm_operand(g, r, d.in[1], &w32);
         if (!ta) {  // dA[M,K] = dY op(B)^T
           q.M = M; q.N = K; q.K = N;
           q.A = dz; q.lda = N; q.trans_a = 0;
-          q.B = F(d.in[1]); q.ldb = b[1]; q.trans_b = tb ? 0 : 1;
+          q.B = w; q.ldb = b[1]; q.trans_b = tb ? 0 : 1;
           q.C = t; q.ldc = K;
+          q.flags = w32 ? TX_GEMM_B_TF32 : 0;
           fuse_dact(d.in[0], q);
         } else {    // dA[K,M] = op(B) dY^T
           q.M = K; q.N = M; q.K = N;
-          q.A = F(d.in[1]); q.lda = b[1]; q.trans_a = tb ? 1 : 0;
+          q.A = w; q.lda = b[1]; q.trans_a = tb ? 1 : 0;
           q.B = dz; q.ldb = N; q.trans_b = 1;
           q.C = t; q.ldc = M;
+          q.flags = w32 ? TX_GEMM_A_TF32 : 0;
         }
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
         if (rc == TX_OK) wrote(d.in[0]);
@@ -1107,7 +1169,9 @@ struct Bwd {
         tx_gemm_desc q; memset(&q, 0, sizeof q);
         q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
         q.M = K; q.N = N; q.K = M;
-        q.A = F(d.in[0]); q.lda = K; q.trans_a = 1; q.stride_a = M * K;
+        bool x32 = false;
+        q.A = gemm_operand(g, r, d.in[0], &x32); q.lda = K; q.trans_a = 1; q.stride_a = M * K;
+        q.flags = x32 ? TX_GEMM_A_TF32 : 0;
         q.B = dz; q.ldb = N; q.trans_b = 0; q.stride_b = M * N;
         q.C = t; q.ldc = N; q.stride_c = K * N;
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
@@ -1120,7 +1184,9 @@ struct Bwd {
         q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
         q.M = M; q.N = K; q.K = N;
         q.A = dz; q.lda = N; q.trans_a = 0; q.stride_a = M * N;
-        q.B = F(d.in[1]); q.ldb = N; q.trans_b = 1; q.stride_b = weight2d ? 0 : K * N;
+        bool w32 = false;
+        q.B = gemm_operand(g, r, d.in[1], &w32); q.ldb = N; q.trans_b = 1; q.stride_b = weight2d ? 0 : K * N;
+        q.flags = w32 ? TX_GEMM_B_TF32 : 0;
         q.C = t; q.ldc = K; q.stride_c = M * K;
         if (weight2d) { q.M = M; q.batch = 1; }
         fuse_dact(d.in[0], q);

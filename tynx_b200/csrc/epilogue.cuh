@@ -10,6 +10,7 @@
 #pragma once
 
 #include <math.h>
+#include <stdint.h>
 
 #include "tynx_cuda.h"
 
@@ -34,6 +35,15 @@ __device__ __forceinline__ float dact(int a, float s) {
     }
   }
   return 1.f;
+}
+
+// Round to TF32 (10-bit mantissa), to nearest with ties away from zero: the
+// rounding the tensor-core path applies to its operands, used to store a
+// result that only feeds further TF32 contractions.
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 }  // namespace tx_epi

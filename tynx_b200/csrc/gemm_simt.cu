@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(tx_gemm_desc d, int split_len
       if (d.preact) d.preact[bz * d.stride_c + gm * d.ld_preact + gn] = v;
       v = act_f(d.act, v);
       if (d.dact) v *= dact_f(d.dact, sv[i][j]);
-      C[gm * d.ldc + gn] = v;
+      C[gm * d.ldc + gn] = (d.flags & TX_GEMM_ROUND_OUT) ? tx_epi::round_tf32(v) : v;
     }
   }
 }
@@ -151,7 +151,7 @@ __device__ __forceinline__ float split_epilogue(const tx_gemm_desc &d, float s, 
   if (d.preact) d.preact[gm * d.ld_preact + gn] = v;
   v = act_f(d.act, v);
   if (d.dact) v *= dact_f(d.dact, d.dact_src[gm * d.ld_dact + gn]);
-  return v;
+  return (d.flags & TX_GEMM_ROUND_OUT) ? tx_epi::round_tf32(v) : v;
 }
 
 __global__ void k_gemm_split_reduce(tx_gemm_desc d, const float *__restrict__ part, int splits,
@@ -246,8 +246,10 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
   return TX_OK;
 }
 
-int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d) {
-  if (d.M <= 0 || d.N <= 0) return TX_OK;
+int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc) {
+  if (desc.M <= 0 || desc.N <= 0) return TX_OK;
+  tx_gemm_desc d = desc;
+  if (ctx->math != TX_MATH_TF32) d.flags = 0;  // TF32 operand / output rounding only applies there
   const int skinny = gemm_skinny(ctx, d);
   if (skinny != TX_ERR_UNSUPPORTED) return skinny;
   if (ctx->math != TX_MATH_FP32) {

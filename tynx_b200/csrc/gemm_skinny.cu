@@ -39,6 +39,7 @@ __device__ __forceinline__ EpiVals finish(const tx_gemm_desc &d, float acc, floa
   const float pre = v;
   v = tx_epi::act(d.act, v);
   if (d.dact) v *= tx_epi::dact(d.dact, s);
+  if (d.flags & TX_GEMM_ROUND_OUT) v = tx_epi::round_tf32(v);
   return {v, pre};
 }
 
@@ -134,6 +135,12 @@ __device__ __forceinline__ void small_k_epilogue(const tx_gemm_desc &d, const Ep
       o.y *= tx_epi::dact(dact, sv[i].y);
       o.z *= tx_epi::dact(dact, sv[i].z);
       o.w *= tx_epi::dact(dact, sv[i].w);
+    }
+    if (d.flags & TX_GEMM_ROUND_OUT) {
+      o.x = tx_epi::round_tf32(o.x);
+      o.y = tx_epi::round_tf32(o.y);
+      o.z = tx_epi::round_tf32(o.z);
+      o.w = tx_epi::round_tf32(o.w);
     }
     st4(er.C + gm * d.ldc + gn, o, vc, valid);
   }

@@ -248,17 +248,13 @@ __device__ __forceinline__ float dact_f(int act, float s) { return tx_epi::dact(
 template <int ACT>
 __device__ __forceinline__ void epi_rows_fast(const float *__restrict__ t, int lane,
                                               float *__restrict__ cp, int64_t ldc, int rows,
-                                              float alpha, bool has_bias, float bias_v) {
-  if (has_bias) {
+                                              float alpha, bool has_bias, float bias_v, bool round_out) {
 #pragma unroll 8
-    for (int rr = 0; rr < rows; ++rr) {
-      float x = alpha * t[rr * 33 + lane];
-      x += bias_v;
-      cp[rr * ldc] = act_f(ACT, x);
-    }
-  } else {
-#pragma unroll 8
-    for (int rr = 0; rr < rows; ++rr) cp[rr * ldc] = act_f(ACT, alpha * t[rr * 33 + lane]);
+  for (int rr = 0; rr < rows; ++rr) {
+    float x = alpha * t[rr * 33 + lane];
+    if (has_bias) x += bias_v;
+    x = act_f(ACT, x);
+    cp[rr * ldc] = round_out ? tx_epi::round_tf32(x) : x;
   }
 }
 
@@ -272,6 +268,7 @@ struct EpiArgs {
   int64_t ld_preact;
   const float *dact_src;
   int64_t ld_dact;
+  bool round_out;
 };
 
 // Epilogue with beta * C, a pre-activation store or act', specialised on the
@@ -301,7 +298,7 @@ __device__ __forceinline__ void epi_rows_spec(const float *__restrict__ t, int l
       if (e.preact) e.preact[(row0 + rr) * e.ld_preact + gn] = x;
       x = act_f(ACT, x);
       if (DACT != TX_ACT_NONE) x *= dact_f(DACT, sv[rr]);
-      e.C[(row0 + rr) * e.ldc + gn] = x;
+      e.C[(row0 + rr) * e.ldc + gn] = e.round_out ? tx_epi::round_tf32(x) : x;
     }
   }
 }
@@ -320,7 +317,7 @@ __device__ __noinline__ void epi_rows_any(const float *__restrict__ t, int lane,
     if (e.preact) e.preact[gm * e.ld_preact + gn] = x;
     x = act_f(e.act, x);
     x *= dact_f(e.dact, e.dact_src[gm * e.ld_dact + gn]);
-    e.C[gm * e.ldc + gn] = x;
+    e.C[gm * e.ldc + gn] = e.round_out ? tx_epi::round_tf32(x) : x;
   }
 }
 
@@ -356,11 +353,12 @@ __device__ __forceinline__ void chunk_math(float (&v)[32], const float (&sv)[32]
     v[j] = x;
   }
   if (pre_tile) tile_row_store(pre_tile, lane, v);
+  const bool round_out = (d.flags & TX_GEMM_ROUND_OUT) != 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     float x = act_f(act, v[j]);
     if (dact != TX_ACT_NONE) x *= dact_f(dact, sv[j]);
-    v[j] = x;
+    v[j] = round_out ? tx_epi::round_tf32(x) : x;
   }
 }
 
@@ -369,7 +367,7 @@ __global__ void __launch_bounds__(192, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
-              int tma_epi) {
+              int tma_epi, int conv_mask) {
   using Cfg = TcCfg<BN, MODE>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -487,8 +485,12 @@ __global__ void __launch_bounds__(192, 1)
       if (d.beta != 0.f) prefetch_rows_l2(d.C + cb, d.ldc, r0, nrows, n0, ncols, lane);
     }
     if (MODE != 0) {
-      // operand conversion, one stage behind the producer and one ahead of the MMA
+      // operand conversion, one stage behind the producer and one ahead of the MMA;
+      // in MODE 1 an operand that already holds TF32 values (conv_mask bit clear)
+      // is left alone
       constexpr int N4 = (A_BYTES + B_BYTES) / 16;
+      const int i_begin = (MODE == 2 || (conv_mask & 1)) ? ct : A_BYTES / 16 + ct;
+      const int i_end = (MODE == 2 || (conv_mask & 2)) ? N4 : A_BYTES / 16;
       for (int kb = 0; kb < num_k; ++kb) {
         const int s = kb % STAGES;
         const uint32_t round = kb / STAGES;
@@ -496,7 +498,7 @@ __global__ void __launch_bounds__(192, 1)
         float4 *p = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE);
         float4 *q = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE + A_BYTES + B_BYTES);
 #pragma unroll 4
-        for (int i = ct; i < N4; i += kConvThreads) {
+        for (int i = i_begin; i < i_end; i += kConvThreads) {
           float4 v = p[i];
           float4 big = make_float4(to_tf32_rn(v.x), to_tf32_rn(v.y), to_tf32_rn(v.z), to_tf32_rn(v.w));
           p[i] = big;
@@ -607,9 +609,10 @@ __global__ void __launch_bounds__(192, 1)
       const int64_t row0 = (int64_t)m0 + quad * 32;
       float *C = d.C + (int64_t)bz * d.stride_c;
       const int64_t cbase = bz * d.stride_c;
+      const bool round_out = (d.flags & TX_GEMM_ROUND_OUT) != 0;
       const EpiArgs ea{d.alpha, d.beta, d.act, d.dact, C, d.ldc,
                        d.preact ? d.preact + cbase : nullptr, d.ld_preact,
-                       d.dact_src ? d.dact_src + cbase : nullptr, d.ld_dact};
+                       d.dact_src ? d.dact_src + cbase : nullptr, d.ld_dact, round_out};
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -633,10 +636,10 @@ __global__ void __launch_bounds__(192, 1)
         if (d.beta == 0.f && !d.preact && !d.dact) {
           float *cp = C + row0 * d.ldc + gn;
           switch (d.act) {
-            case TX_ACT_RELU: epi_rows_fast<TX_ACT_RELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
-            case TX_ACT_TANH: epi_rows_fast<TX_ACT_TANH>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
-            case TX_ACT_GELU: epi_rows_fast<TX_ACT_GELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
-            default: epi_rows_fast<TX_ACT_NONE>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v); break;
+            case TX_ACT_RELU: epi_rows_fast<TX_ACT_RELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
+            case TX_ACT_TANH: epi_rows_fast<TX_ACT_TANH>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
+            case TX_ACT_GELU: epi_rows_fast<TX_ACT_GELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
+            default: epi_rows_fast<TX_ACT_NONE>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
           }
         } else if (!d.dact) {
           const bool hb = d.bias != nullptr;
@@ -707,6 +710,7 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
 struct Maps {
   CUtensorMap a, b, c, s, p;
   int tma_epi = 0;
+  int conv_mask = 3;  // MODE 1: operands to round in shared memory (bit 0 A, bit 1 B)
 };
 
 // `z` = batch count, or the number of K splits when kb_per_cta > 0
@@ -721,7 +725,7 @@ int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int 
   }
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
   kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
-                                                          kb_per_cta, m.tma_epi);
+                                                          kb_per_cta, m.tma_epi, m.conv_mask);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
@@ -831,10 +835,16 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   if (a_inner < 16 || b_inner < 16) return TX_ERR_UNSUPPORTED;
   if (!load_encode()) return TX_ERR_UNSUPPORTED;
 
-  const Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
-  const int bn = tiling.bn;
   Maps m;
   memset(&m, 0, sizeof m);
+  if (mode == 1) {
+    // round-to-nearest: only operands that do not already hold TF32 values
+    // are converted; with none left the plain pipeline is exact
+    m.conv_mask = ((d.flags & TX_GEMM_A_TF32) ? 0 : 1) | ((d.flags & TX_GEMM_B_TF32) ? 0 : 2);
+    if (m.conv_mask == 0) mode = 0;
+  }
+  const Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
+  const int bn = tiling.bn;
   bool ok;
   if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
     ok = make_map(&m.a, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
@@ -872,6 +882,7 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   raw.preact = nullptr;
   raw.dact = TX_ACT_NONE;
   raw.dact_src = nullptr;
+  raw.flags = d.flags & ~TX_GEMM_ROUND_OUT;  // partials stay exact; the reduction rounds
   make_epilogue_maps(m, raw, splits);
   TX_TRY(launch_any(ctx, mode, bn, raw, m, splits, kb_per));
   return gemm_split_reduce(ctx, d, part.as<float>(), splits);

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.h"
+#include "epilogue.cuh"
 
 namespace {
 
@@ -450,24 +451,92 @@ __global__ void k_layernorm_bwd(const float *__restrict__ x, const float *__rest
 }
 
 // out[c] (+)= scale * sum_p part[p, c]   (fixed order)
-__global__ void k_sum_partials(const float *__restrict__ part, int64_t np, int64_t cols,
+
+// Final column reduction of a [np, cols] partial-sum matrix: out = scale * sum
+// (+ out when acc).  Block (32, 8): with vec each thread owns 4 adjacent
+// columns, the 8 row groups take partial rows ty, ty + 8, ... in order with
+// four loads in flight, and the groups are combined in a fixed order.
+template <bool VEC>
+__global__ void k_colsum_final(const float *__restrict__ part, int64_t np, int64_t cols,
                                float *__restrict__ out, float scale, int acc) {
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    // partials added in index order, four loads in flight
-    float s = 0.f;
-    int64_t p = 0;
-    for (; p + 4 <= np; p += 4) {
-      const float v0 = part[p * cols + c], v1 = part[(p + 1) * cols + c];
-      const float v2 = part[(p + 2) * cols + c], v3 = part[(p + 3) * cols + c];
-      s += v0;
-      s += v1;
-      s += v2;
-      s += v3;
+  constexpr int W = VEC ? 4 : 1;
+  __shared__ float sm[8][32 * W];
+  const int64_t c = ((int64_t)blockIdx.x * 32 + threadIdx.x) * W;
+  float s[W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) s[j] = 0.f;
+  if (c < cols) {
+    int64_t p = threadIdx.y;
+    for (; p + 24 < np; p += 32) {
+      float v[4][W];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (VEC) {
+          const float4 t = *reinterpret_cast<const float4 *>(part + (p + 8 * i) * cols + c);
+          v[i][0] = t.x;
+          v[i][W > 1 ? 1 : 0] = t.y;
+          v[i][W > 2 ? 2 : 0] = t.z;
+          v[i][W > 3 ? 3 : 0] = t.w;
+        } else {
+          v[i][0] = part[(p + 8 * i) * cols + c];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < W; ++j) s[j] += v[i][j];
     }
-    for (; p < np; ++p) s += part[p * cols + c];
-    s *= scale;
-    out[c] = acc ? out[c] + s : s;
+    for (; p < np; p += 8) {
+#pragma unroll
+      for (int j = 0; j < W; ++j) s[j] += part[p * cols + c + j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < W; ++j) sm[threadIdx.y][threadIdx.x * W + j] = s[j];
+  __syncthreads();
+  if (threadIdx.y == 0 && c < cols) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      float t = sm[0][threadIdx.x * W + j];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) t += sm[i][threadIdx.x * W + j];
+      t *= scale;
+      out[c + j] = acc ? out[c + j] + t : t;
+    }
+  }
+}
+
+int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out, float scale,
+                  int acc) {
+  const bool vec = (cols % 4 == 0) && ((((uintptr_t)part) & 15) == 0);
+  const int64_t per_block = vec ? 128 : 32;
+  const int64_t blocks = (cols + per_block - 1) / per_block;
+  if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
+  if (vec)
+    k_colsum_final<true><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  else
+    k_colsum_final<false><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  TX_LAUNCHED(ctx, "k_colsum_final");
+  return TX_OK;
+}
+
+// ---- TF32 operand shadow ---------------------------------------------------------------
+__global__ void k_round_tf32(const float *__restrict__ src, float *__restrict__ dst, int64_t n) {
+  const int64_t n4 = n / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool vec = ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) == 0;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (vec) {
+    for (; i < n4; i += stride) {
+      const float4 v = reinterpret_cast<const float4 *>(src)[i];
+      reinterpret_cast<float4 *>(dst)[i] =
+          make_float4(tx_epi::round_tf32(v.x), tx_epi::round_tf32(v.y), tx_epi::round_tf32(v.z),
+                      tx_epi::round_tf32(v.w));
+    }
+    for (i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+      dst[i] = tx_epi::round_tf32(src[i]);
+  } else {
+    for (; i < n; i += stride) dst[i] = tx_epi::round_tf32(src[i]);
   }
 }
 
@@ -981,12 +1050,10 @@ extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma,
                                                                       pg, pb, rows, cols, acc_dx);
   TX_LAUNCHED(ctx, "k_layernorm_bwd");
   if (dgamma) {
-    k_sum_partials<<<grid_for(cols, 256), 256, 0, ctx->stream>>>(pg, blocks, cols, dgamma, 1.f, acc_p);
-    TX_LAUNCHED(ctx, "k_sum_partials");
+    TX_TRY(colsum_finish(ctx, pg, blocks, cols, dgamma, 1.f, acc_p));
   }
   if (dbeta) {
-    k_sum_partials<<<grid_for(cols, 256), 256, 0, ctx->stream>>>(pb, blocks, cols, dbeta, 1.f, acc_p);
-    TX_LAUNCHED(ctx, "k_sum_partials");
+    TX_TRY(colsum_finish(ctx, pb, blocks, cols, dbeta, 1.f, acc_p));
   }
   return TX_OK;
 }
@@ -1034,6 +1101,14 @@ extern "C" int tx_take_last_bwd(tx_ctx *ctx, const int64_t *idx, const float *do
   return TX_OK;
 }
 
+extern "C" int tx_round_tf32(tx_ctx *ctx, const float *src, float *dst, int64_t n) {
+  if (!ctx || (n > 0 && (!src || !dst))) return TX_ERR_INVALID;
+  if (n <= 0) return TX_OK;
+  k_round_tf32<<<grid_for((n + 3) / 4, 256), 256, 0, ctx->stream>>>(src, dst, n);
+  TX_LAUNCHED(ctx, "k_round_tf32");
+  return TX_OK;
+}
+
 extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, int64_t N,
                             float scale, int acc) {
   if (!ctx) return TX_ERR_INVALID;
@@ -1060,8 +1135,7 @@ extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, 
     k_colsum_partial<<<dim3((unsigned)col_blocks, (unsigned)splits), dim3(32, 8), 0, ctx->stream>>>(
         dy, M, N, rows_per, part.as<float>());
   TX_LAUNCHED(ctx, "k_colsum_partial");
-  k_sum_partials<<<grid_for(N, 256), 256, 0, ctx->stream>>>(part.as<float>(), splits, N, db, scale, acc);
-  TX_LAUNCHED(ctx, "k_sum_partials");
+  TX_TRY(colsum_finish(ctx, part.as<float>(), splits, N, db, scale, acc));
   return TX_OK;
 }
 
