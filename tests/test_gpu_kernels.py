@@ -235,6 +235,107 @@ def test_pre_rounded_operands_and_rounded_output(tx, ta, tb):
     np.testing.assert_array_equal(rounded.view(np.uint32), _np_round_tf32(base).view(np.uint32))
 
 
+def _strides(shape):
+    st, acc = [], 1
+    for e in reversed(shape):
+        st.append(acc)
+        acc *= e
+    return st[::-1]
+
+
+BROADCAST = [
+    ((32768, 256), (32768, 256)),            # residual add (one merged axis)
+    ((32768, 256), (256,)),                  # bias row
+    ((256, 4, 128, 128), ()),                # attention scale
+    ((256, 1, 128, 64), (1, 4, 1, 64)),      # both sides broadcast
+    ((7, 3, 5), (7, 1, 5)),                  # ragged, not float4-able
+    ((4, 6, 1, 2), (6, 3, 1)),
+]
+
+
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div", "min", "max", "le", "ge"])
+@pytest.mark.parametrize("sa,sb", BROADCAST, ids=[f"{a}-{b}" for a, b in BROADCAST])
+def test_broadcast_binary_matches_numpy(tx, op, sa, sb):
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    rng = np.random.default_rng(len(sa) * 7 + len(sb))
+    a = rng.standard_normal(sa).astype(np.float32)
+    b = (rng.standard_normal(sb) + (3.0 if op == "div" else 0.0)).astype(np.float32)
+    shape = np.broadcast_shapes(sa, sb)
+    nd = len(shape)
+
+    def bstride(s):
+        s = (1,) * (nd - len(s)) + tuple(s)
+        st = _strides(s)
+        return [0 if s[k] == 1 and shape[k] != 1 else st[k] for k in range(nd)]
+
+    ctx = _core.context()
+    A, B, out = tx.Tensor(a), tx.Tensor(b), tx.zeros(*shape)
+    ctx.check(N.lib.tx_binary(ctx.handle, N.BIN[op], A.ptr, N.i64_array(bstride(sa)), B.ptr,
+                              N.i64_array(bstride(sb)), out.ptr, N.i64_array(shape), nd))
+    want = {"add": np.add, "sub": np.subtract, "mul": np.multiply, "div": np.divide,
+            "min": np.minimum, "max": np.maximum,
+            "le": lambda x, y: (x <= y).astype(np.float32),
+            "ge": lambda x, y: (x >= y).astype(np.float32)}[op](a, b)
+    np.testing.assert_array_equal(out.numpy(), want.astype(np.float32))
+
+
+@pytest.mark.parametrize("shape,perm,dtype", [
+    ((256, 128, 4, 64), (0, 2, 1, 3), np.float32),   # head split
+    ((256, 4, 128, 64), (0, 2, 1, 3), np.float32),   # head merge
+    ((512, 3, 33, 17), (0, 2, 3, 1), np.float32),    # NCHW -> NHWC, ragged
+    ((1000, 3), (1, 0), np.float32),
+    ((64, 5, 8), (2, 0, 1), np.int64),
+])
+def test_strided_copy_transposes(tx, shape, perm, dtype):
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(shape) * 100).astype(dtype)
+    st = _strides(shape)
+    out_shape = [shape[p] for p in perm]
+    ctx = _core.context()
+    X = tx.Tensor(x, dtype="int64" if dtype == np.int64 else "float32")
+    out = tx.Tensor(np.zeros(out_shape, dtype), dtype="int64" if dtype == np.int64 else "float32")
+    ctx.check(N.lib.tx_strided_copy(ctx.handle, X.ptr, N.i64_array([st[p] for p in perm]), out.ptr,
+                                    N.i64_array(out_shape), len(shape), x.itemsize))
+    np.testing.assert_array_equal(out.numpy(), np.transpose(x, perm))
+
+
+@pytest.mark.parametrize("shape,keep", [
+    ((256, 128, 256), (1, 0, 1)),     # mean over the sequence
+    ((512, 128, 8, 8), (1, 1, 0, 0)), # global average pool
+    ((32768, 256), (0, 1)),           # bias gradient (column sums)
+    ((300, 7, 5), (0, 1, 0)),         # two reduced blocks: generic kernel
+    ((8, 9), (1, 1)),                 # nothing reduced
+    ((3, 4000), (1, 0)),              # long rows
+])
+@pytest.mark.parametrize("mean", [0, 1])
+def test_reduce_to_matches_numpy(tx, shape, keep, mean):
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N
+
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal(shape).astype(np.float32)
+    out_shape = [e if k else 1 for e, k in zip(shape, keep)]
+    axes = tuple(i for i, k in enumerate(keep) if not k)
+    want = (x.astype(np.float64).mean(axis=axes, keepdims=True) if mean else
+            x.astype(np.float64).sum(axis=axes, keepdims=True)) if axes else x.astype(np.float64)
+    ctx = _core.context()
+    X = tx.Tensor(x)
+    prior = rng.standard_normal(out_shape).astype(np.float32)
+    for acc in (0, 1):
+        out = tx.Tensor(prior)
+        ctx.check(N.lib.tx_reduce_to(ctx.handle, X.ptr, N.i64_array(shape), out.ptr,
+                                     N.i64_array(out_shape), len(shape), mean, acc))
+        expect = want + (prior if acc else 0)
+        n_red = int(np.prod([shape[a] for a in axes])) if axes else 1
+        tol = 1e-6 * max(1.0, np.sqrt(n_red)) * (1 if mean else np.sqrt(n_red))
+        assert np.abs(out.numpy() - expect).max() <= tol * max(1.0, np.abs(x).max()), (acc, n_red)
+
+
 def test_softmax_xent_matches_oracle(tx):
     from oracle import flex_oracle as fo
     from tynx_b200 import nn

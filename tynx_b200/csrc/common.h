@@ -105,6 +105,16 @@ int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d);
 int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d);
 int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits);
 
+// N-d bandwidth kernels on canonicalised shapes (nd.cu).  Strides in elements,
+// 0 = broadcast; outputs are contiguous.  nd_reduce returns TX_ERR_UNSUPPORTED
+// (not latched) for layouts that are not [outer, reduced, inner].
+int nd_binary(tx_ctx *ctx, int op, const float *A, const int64_t *sa, const float *B, const int64_t *sb,
+              float *out, const int64_t *shape, int ndim);
+int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const int64_t *shape, int ndim,
+            int elem_bytes, float scale, int acc);
+int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_t *out_shape, int ndim,
+              float *y, float scale, int acc);
+
 // grid sizing helper
 inline unsigned grid_for(int64_t n, int threads, int64_t max_blocks = 148 * 16) {
   int64_t b = (n + threads - 1) / threads;

@@ -94,21 +94,6 @@ struct BDims {
   int64_t s[TX_MAX_DIMS];
 };
 
-// out[i] (+)= scale * in[offset(i)] with broadcast strides
-__global__ void k_broadcast_scale(const float *__restrict__ in, float *__restrict__ out, BDims d,
-                                  int ndim, int64_t n, float scale, int acc) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t rem = i, off = 0;
-    for (int k = ndim - 1; k >= 0; --k) {
-      int64_t c = rem % d.shape[k];
-      rem /= d.shape[k];
-      off += c * d.s[k];
-    }
-    float v = scale * in[off];
-    out[i] = acc ? out[i] + v : v;
-  }
-}
 
 __global__ void k_axpy(float *__restrict__ y, const float *__restrict__ x, int64_t n, float a) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -1498,8 +1483,7 @@ struct Bwd {
         for (size_t i = 0; i < x.size(); ++i) { bd.shape[i] = x[i]; bd.s[i] = st[i]; }
         float *t; int acc;
         TX_TRY(target(xv, &t, &acc));
-        k_broadcast_scale<<<grid_for(numel_of(x), 256), 256, 0, ctx->stream>>>(dy, t, bd, (int)x.size(), numel_of(x), scale, acc);
-        TX_LAUNCHED(ctx, "k_broadcast_scale");
+        TX_TRY(nd_copy(ctx, dy, bd.s, t, x.data(), (int)x.size(), 4, scale, acc));
         wrote(xv);
         return TX_OK;
       }

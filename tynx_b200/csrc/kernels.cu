@@ -120,48 +120,9 @@ __global__ void k_unary_bwd(int op, const float *__restrict__ s, const float *__
   }
 }
 
-struct Dims {
-  int64_t shape[TX_MAX_DIMS];
-  int64_t sa[TX_MAX_DIMS];
-  int64_t sb[TX_MAX_DIMS];
-};
 
-__device__ __forceinline__ float binary_f(int op, float a, float b) {
-  switch (op) {
-    case TX_BIN_ADD: return a + b;
-    case TX_BIN_SUB: return a - b;
-    case TX_BIN_MUL: return a * b;
-    case TX_BIN_DIV: return a / b;
-    case TX_BIN_MIN: return a <= b ? a : b;
-    case TX_BIN_MAX: return a >= b ? a : b;
-    case TX_BIN_LE: return a <= b ? 1.f : 0.f;
-    case TX_BIN_GE: return a >= b ? 1.f : 0.f;
-    case TX_BIN_POW: return powf(a, b);
-  }
-  return 0.f;
-}
 
-__global__ void k_binary(int op, const float *__restrict__ A, const float *__restrict__ B,
-                         float *__restrict__ out, Dims d, int ndim, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t rem = i, oa = 0, ob = 0;
-    for (int k = ndim - 1; k >= 0; --k) {
-      int64_t c = rem % d.shape[k];
-      rem /= d.shape[k];
-      oa += c * d.sa[k];
-      ob += c * d.sb[k];
-    }
-    out[i] = binary_f(op, A[oa], B[ob]);
-  }
-}
 
-__global__ void k_binary_same(int op, const float *__restrict__ A, const float *__restrict__ B,
-                              float *__restrict__ out, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = binary_f(op, A[i], B[i]);
-}
 
 // Reduction of x (shape `in`) to `out` (same rank, 1 on reduced axes).
 struct RDims {
@@ -228,25 +189,7 @@ __global__ void k_reduce_block(const float *__restrict__ x, float *__restrict__ 
   }
 }
 
-struct CDims {
-  int64_t shape[TX_MAX_DIMS];
-  int64_t ss[TX_MAX_DIMS];
-};
 
-template <typename T>
-__global__ void k_strided_copy(const T *__restrict__ src, T *__restrict__ dst, CDims d, int ndim,
-                               int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t rem = i, off = 0;
-    for (int k = ndim - 1; k >= 0; --k) {
-      int64_t c = rem % d.shape[k];
-      rem /= d.shape[k];
-      off += c * d.ss[k];
-    }
-    dst[i] = src[off];
-  }
-}
 
 // ---- softmax over the last axis: one warp per row ---------------------------------
 __global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
@@ -857,29 +800,7 @@ extern "C" int tx_unary_bwd(tx_ctx *ctx, int op, const float *s, const float *dy
 extern "C" int tx_binary(tx_ctx *ctx, int op, const float *A, const int64_t *sa, const float *B,
                          const int64_t *sb, float *out, const int64_t *shape, int ndim) {
   if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS || op < 0 || op > TX_BIN_POW) return TX_ERR_INVALID;
-  int64_t n = 1;
-  bool contiguous = true;
-  int64_t expect = 1;
-  for (int k = ndim - 1; k >= 0; --k) {
-    if (sa[k] != expect && shape[k] != 1) contiguous = false;
-    if (sb[k] != expect && shape[k] != 1) contiguous = false;
-    expect *= shape[k];
-  }
-  for (int k = 0; k < ndim; ++k) n *= shape[k];
-  if (n <= 0) return TX_OK;
-  if (contiguous) {
-    k_binary_same<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, A, B, out, n);
-  } else {
-    Dims d;
-    for (int k = 0; k < ndim; ++k) {
-      d.shape[k] = shape[k];
-      d.sa[k] = sa[k];
-      d.sb[k] = sb[k];
-    }
-    k_binary<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, A, B, out, d, ndim, n);
-  }
-  TX_LAUNCHED(ctx, "k_binary");
-  return TX_OK;
+  return nd_binary(ctx, op, A, sa, B, sb, out, shape, ndim);
 }
 
 extern "C" int tx_reduce_to(tx_ctx *ctx, const float *x, const int64_t *in_shape, float *y,
@@ -899,6 +820,9 @@ extern "C" int tx_reduce_to(tx_ctx *ctx, const float *x, const int64_t *in_shape
   }
   if (n_out <= 0) return TX_OK;
   float scale = mean ? 1.0f / (float)(n_red > 0 ? n_red : 1) : 1.0f;
+  if (n_red == 1) return nd_copy(ctx, x, d.in_stride, y, out_shape, ndim, 4, scale, acc);
+  const int rc = nd_reduce(ctx, x, in_shape, out_shape, ndim, y, scale, acc);
+  if (rc != TX_ERR_UNSUPPORTED) return rc;
   if (n_out >= 4096 || n_red <= 32) {
     k_reduce_thread<<<grid_for(n_out, 256), 256, 0, ctx->stream>>>(x, y, d, ndim, n_out, n_red,
                                                                    scale, acc);
@@ -912,23 +836,8 @@ extern "C" int tx_reduce_to(tx_ctx *ctx, const float *x, const int64_t *in_shape
 
 extern "C" int tx_strided_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *dst,
                                const int64_t *shape, int ndim, int elem_bytes) {
-  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS) return TX_ERR_INVALID;
-  CDims d;
-  int64_t n = 1;
-  for (int k = 0; k < ndim; ++k) {
-    d.shape[k] = shape[k];
-    d.ss[k] = ss[k];
-    n *= shape[k];
-  }
-  if (n <= 0) return TX_OK;
-  if (elem_bytes == 4)
-    k_strided_copy<float><<<grid_for(n, 256), 256, 0, ctx->stream>>>((const float *)src, (float *)dst, d, ndim, n);
-  else if (elem_bytes == 8)
-    k_strided_copy<int64_t><<<grid_for(n, 256), 256, 0, ctx->stream>>>((const int64_t *)src, (int64_t *)dst, d, ndim, n);
-  else
-    return TX_ERR_INVALID;
-  TX_LAUNCHED(ctx, "k_strided_copy");
-  return TX_OK;
+  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS || (elem_bytes != 4 && elem_bytes != 8)) return TX_ERR_INVALID;
+  return nd_copy(ctx, src, ss, dst, shape, ndim, elem_bytes, 1.f, 0);
 }
 
 extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int log) {
