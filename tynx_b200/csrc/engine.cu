@@ -27,6 +27,7 @@
 #include <string>
 
 #include "common.h"
+#include "epilogue.cuh"
 
 int dp_allreduce_range(tx_ctx *ctx, float *buf, int64_t n);  // dp.cu
 int dp_event_fork(tx_ctx *ctx);                               // compute -> comm
@@ -101,76 +102,208 @@ __global__ void k_axpy(float *__restrict__ y, const float *__restrict__ x, int64
     y[i] += a * x[i];
 }
 
-// im2col for NCHW: cols[(n*OH + oh)*OW + ow][c*KH*KW + kh*KW + kw]
-__global__ void k_im2col(const float *__restrict__ x, float *__restrict__ cols, int64_t N, int64_t C,
-                         int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
-                         int sh, int sw, int pt, int pl, int dh, int dw, int64_t ldc) {
-  int64_t K = C * KH * KW;
-  int64_t total = N * OH * OW * K;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t k = i % K;
-    int64_t m = i / K;
-    int64_t kw = k % KW, kh = (k / KW) % KH, c = k / (KW * KH);
-    int64_t ow = m % OW, oh = (m / OW) % OH, n = m / (OW * OH);
-    int64_t ih = oh * sh - pt + kh * dh, iw = ow * sw - pl + kw * dw;
+// ---- convolution as a GEMM over channels-last columns ---------------------------------
+// The ONNX tensors are NCHW; inside a convolution the activations are moved to
+// NHWC so that an im2col column k = (kh * KW + kw) * C + c copies contiguous
+// channel runs (float4 when C % 4 == 0), and the weights are permuted to the
+// same (kh, kw, c) order once per forward.
+
+// out[b][c][r] (+)= in[b][r][c] * act'(src[b][r][c]) (+ bias[c]): a batched
+// transpose of [R, Cc] matrices through 32 x 32 shared-memory tiles, so both
+// the loads and the stores are 128-byte row segments.  `src` (optional) is
+// indexed like `in`.
+__global__ void k_transpose_b(const float *__restrict__ in, float *__restrict__ out, int64_t R, int64_t Cc,
+                              const float *__restrict__ bias, const float *__restrict__ src, int dact,
+                              int acc) {
+  __shared__ float tile[32][33];
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  const float *ib = in + b * R * Cc;
+  const float *sb = src ? src + b * R * Cc : nullptr;
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    const int64_t r = r0 + threadIdx.y + j, c = c0 + threadIdx.x;
     float v = 0.f;
-    if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = x[((n * C + c) * H + ih) * W + iw];
-    cols[m * ldc + k] = v;
+    if (r < R && c < Cc) {
+      v = ib[r * Cc + c];
+      if (sb) v *= tx_epi::dact(dact, sb[r * Cc + c]);
+    }
+    tile[threadIdx.y + j][threadIdx.x] = v;
+  }
+  __syncthreads();
+  float *ob = out + b * R * Cc;
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    const int64_t c = c0 + threadIdx.y + j, r = r0 + threadIdx.x;
+    if (r < R && c < Cc) {
+      float v = tile[threadIdx.x][threadIdx.y + j];
+      if (bias) v += bias[c];
+      float *o = ob + c * R + r;
+      *o = acc ? *o + v : v;
+    }
   }
 }
 
-// col2im (gather form: each input pixel sums its contributions, no atomics)
-__global__ void k_col2im(const float *__restrict__ dcols, float *__restrict__ dx, int64_t N,
-                         int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t OH,
-                         int64_t OW, int sh, int sw, int pt, int pl, int dh, int dw, int64_t ldc,
-                         int acc) {
-  int64_t total = N * C * H * W;
-  int64_t K = C * KH * KW;
-  (void)K;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t iw = i % W, ih = (i / W) % H, c = (i / (W * H)) % C, n = i / (W * H * C);
-    float s = 0.f;
-    for (int64_t kh = 0; kh < KH; ++kh) {
-      int64_t t = ih + pt - kh * dh;
-      if (t < 0 || t % sh) continue;
-      int64_t oh = t / sh;
-      if (oh >= OH) continue;
-      for (int64_t kw = 0; kw < KW; ++kw) {
-        int64_t u = iw + pl - kw * dw;
-        if (u < 0 || u % sw) continue;
-        int64_t ow = u / sw;
-        if (ow >= OW) continue;
-        s += dcols[((n * OH + oh) * OW + ow) * ldc + (c * KH + kh) * KW + kw];
+int transpose_b(tx_ctx *ctx, const float *in, float *out, int64_t B, int64_t R, int64_t Cc,
+                const float *bias = nullptr, const float *src = nullptr, int dact = TX_ACT_NONE, int acc = 0) {
+  if (B <= 0 || R <= 0 || Cc <= 0) return TX_OK;
+  if (B > 65535 || (R + 31) / 32 > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "transpose too large");
+  dim3 grid((unsigned)((Cc + 31) / 32), (unsigned)((R + 31) / 32), (unsigned)B);
+  k_transpose_b<<<grid, dim3(32, 8), 0, ctx->stream>>>(in, out, R, Cc, bias, src, dact, acc);
+  TX_LAUNCHED(ctx, "k_transpose_b");
+  return TX_OK;
+}
+
+struct ConvGeom {
+  int N, C, H, W, KH, KW, OH, OW, sh, sw, pt, pl, dh, dw;
+  int ldk;  // columns per im2col row (K = KH*KW*C rounded up to 4, zero padded)
+};
+
+// cols[m][(kh*KW + kw)*C + c] = xh[n][ih][iw][c] (0 outside the image and in
+// the padding columns), m = (n*OH + oh)*OW + ow.  V = 4: float4 channel runs.
+template <int V>
+__global__ void k_im2col_nhwc(const float *__restrict__ xh, float *__restrict__ cols, ConvGeom g,
+                              uint32_t units, int round_tf32) {
+  const uint32_t per_row = (uint32_t)g.ldk / V;
+  const uint32_t cv = (uint32_t)g.C / V;
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
+    const uint32_t m = u / per_row, kq = u - m * per_row;
+    const uint32_t tap = kq / cv, c = (kq - tap * cv) * V;
+    float v[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = 0.f;
+    if (tap < (uint32_t)(g.KH * g.KW)) {
+      const uint32_t kh = tap / g.KW, kw = tap - kh * g.KW;
+      const uint32_t ow = m % g.OW, t = m / g.OW, oh = t % g.OH, n = t / g.OH;
+      const int ih = (int)oh * g.sh - g.pt + (int)kh * g.dh, iw = (int)ow * g.sw - g.pl + (int)kw * g.dw;
+      if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
+        const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.C + c;
+        if (V == 4) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(p);
+          v[0] = t4.x;
+          v[V > 1 ? 1 : 0] = t4.y;
+          v[V > 2 ? 2 : 0] = t4.z;
+          v[V > 3 ? 3 : 0] = t4.w;
+        } else {
+          v[0] = *p;
+        }
+      }
+    } else if (V == 1) {
+      v[0] = 0.f;  // padding column
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+      if (round_tf32) v[j] = tx_epi::round_tf32(v[j]);
+    float *o = cols + (int64_t)u * V;
+    if (V == 4)
+      *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[V > 1 ? 1 : 0], v[V > 2 ? 2 : 0], v[V > 3 ? 3 : 0]);
+    else
+      *o = v[0];
+  }
+}
+
+// dxh[n][ih][iw][c] = sum over the taps that read (ih, iw) of dcols[m][(kh*KW + kw)*C + c]
+// (gather form: each input element is written once, no atomics).
+template <int V>
+__global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict__ dxh, ConvGeom g,
+                              uint32_t units) {
+  const uint32_t cv = (uint32_t)g.C / V;
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
+    const uint32_t pix = u / cv, c = (u - pix * cv) * V;
+    const uint32_t iw = pix % g.W, t = pix / g.W, ih = t % g.H, n = t / g.H;
+    float s[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) s[j] = 0.f;
+    for (int kh = 0; kh < g.KH; ++kh) {
+      const int a = (int)ih + g.pt - kh * g.dh;
+      if (a < 0 || a % g.sh) continue;
+      const int oh = a / g.sh;
+      if (oh >= g.OH) continue;
+      for (int kw = 0; kw < g.KW; ++kw) {
+        const int b = (int)iw + g.pl - kw * g.dw;
+        if (b < 0 || b % g.sw) continue;
+        const int ow = b / g.sw;
+        if (ow >= g.OW) continue;
+        const float *p = dcols + (((int64_t)n * g.OH + oh) * g.OW + ow) * g.ldk + (kh * g.KW + kw) * g.C + c;
+        if (V == 4) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(p);
+          s[0] += t4.x;
+          s[V > 1 ? 1 : 0] += t4.y;
+          s[V > 2 ? 2 : 0] += t4.z;
+          s[V > 3 ? 3 : 0] += t4.w;
+        } else {
+          s[0] += *p;
+        }
       }
     }
-    dx[i] = acc ? dx[i] + s : s;
+    float *o = dxh + (int64_t)u * V;
+    if (V == 4)
+      *reinterpret_cast<float4 *>(o) = make_float4(s[0], s[V > 1 ? 1 : 0], s[V > 2 ? 2 : 0], s[V > 3 ? 3 : 0]);
+    else
+      *o = s[0];
   }
 }
 
-// [N*HW, C] <-> [N, C, HW]
-__global__ void k_nhwc_to_nchw(const float *__restrict__ src, float *__restrict__ dst, int64_t N,
-                               int64_t C, int64_t HW, const float *__restrict__ bias, int act) {
-  int64_t total = N * C * HW;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t p = i % HW, c = (i / HW) % C, n = i / (HW * C);
-    float v = src[(n * HW + p) * C + c];
-    if (bias) v += bias[c];
-    if (act == TX_ACT_RELU) v = v > 0.f ? v : 0.f;
-    dst[i] = v;
+// wk[o][(kh*KW + kw)*C + c] = w[o][c][kh][kw], zero padded to ldk (optionally TF32-rounded)
+__global__ void k_weight_to_khwc(const float *__restrict__ w, float *__restrict__ wk, int OC, int C, int KH,
+                                 int KW, int ldk, int round_tf32) {
+  const int64_t n = (int64_t)OC * ldk;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int o = (int)(i / ldk), k = (int)(i - (int64_t)o * ldk);
+    float v = 0.f;
+    if (k < KH * KW * C) {
+      const int tap = k / C, c = k - tap * C, kh = tap / KW, kw = tap - kh * KW;
+      v = w[(((int64_t)o * C + c) * KH + kh) * KW + kw];
+    }
+    wk[i] = round_tf32 ? tx_epi::round_tf32(v) : v;
   }
 }
 
-__global__ void k_nchw_to_nhwc(const float *__restrict__ src, float *__restrict__ dst, int64_t N,
-                               int64_t C, int64_t HW) {
-  int64_t total = N * C * HW;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t c = i % C, p = (i / C) % HW, n = i / (C * HW);
-    dst[i] = src[(n * C + c) * HW + p];
+// dw[o][c][kh][kw] (+)= dwk[o][(kh*KW + kw)*C + c]
+__global__ void k_weight_from_khwc(const float *__restrict__ dwk, float *__restrict__ dw, int OC, int C, int KH,
+                                   int KW, int ldk, int acc) {
+  const int64_t n = (int64_t)OC * C * KH * KW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int kw = (int)(i % KW), kh = (int)((i / KW) % KH), c = (int)((i / (KW * KH)) % C),
+              o = (int)(i / ((int64_t)KW * KH * C));
+    const float v = dwk[(int64_t)o * ldk + (kh * KW + kw) * C + c];
+    dw[i] = acc ? dw[i] + v : v;
   }
+}
+
+ConvGeom conv_geom(const Shape &x, const Shape &w, const Shape &y, const tx_node_desc &d) {
+  ConvGeom g;
+  g.N = (int)x[0]; g.C = (int)x[1]; g.H = (int)x[2]; g.W = (int)x[3];
+  g.KH = (int)w[2]; g.KW = (int)w[3]; g.OH = (int)y[2]; g.OW = (int)y[3];
+  g.sh = (int)d.ints[0]; g.sw = (int)d.ints[1]; g.pt = (int)d.ints[2]; g.pl = (int)d.ints[3];
+  g.dh = (int)d.ints[6]; g.dw = (int)d.ints[7];
+  g.ldk = (g.KH * g.KW * g.C + 3) & ~3;
+  return g;
+}
+
+int im2col_nhwc(tx_ctx *ctx, const float *xh, float *cols, const ConvGeom &g, bool round_tf32) {
+  const int64_t M = (int64_t)g.N * g.OH * g.OW;
+  const bool vec = g.C % 4 == 0;
+  const int64_t units = M * g.ldk / (vec ? 4 : 1);
+  if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "im2col too large");
+  if (vec)
+    k_im2col_nhwc<4><<<grid_for(units, 256), 256, 0, ctx->stream>>>(xh, cols, g, (uint32_t)units, round_tf32);
+  else
+    k_im2col_nhwc<1><<<grid_for(units, 256), 256, 0, ctx->stream>>>(xh, cols, g, (uint32_t)units, round_tf32);
+  TX_LAUNCHED(ctx, "k_im2col_nhwc");
+  return TX_OK;
+}
+
+int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g) {
+  const bool vec = g.C % 4 == 0 && g.ldk % 4 == 0;
+  const int64_t units = (int64_t)g.N * g.H * g.W * g.C / (vec ? 4 : 1);
+  if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "col2im too large");
+  if (vec)
+    k_col2im_nhwc<4><<<grid_for(units, 256), 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+  else
+    k_col2im_nhwc<1><<<grid_for(units, 256), 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+  TX_LAUNCHED(ctx, "k_col2im_nhwc");
+  return TX_OK;
 }
 
 }  // namespace
@@ -499,15 +632,18 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     g->values[outputs[i]].is_output = true;
   }
 
-  // ---- fusion plan: Gemm/MatMul(2-D weight) -> sole-consumer activation ----------------
+  // ---- fusion plan: Gemm / MatMul / Conv -> sole-consumer activation ------------------
   for (int i = 0; i < n_nodes; ++i) {
     GNode &n = g->nodes[i];
-    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL) continue;
+    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL && n.d.op != TX_OP_CONV) continue;
     GValue &y = g->values[n.d.out[0]];
     if (y.is_output || y.consumers.size() != 1) continue;
     GNode &a = g->nodes[y.consumers[0]];
     int act = act_of_op(a.d.op);
     if (act == TX_ACT_NONE || a.d.in[0] != n.d.out[0]) continue;
+    // a convolution keeps no pre-activation: only activations whose
+    // derivative follows from the output fuse into it
+    if (n.d.op == TX_OP_CONV && act == TX_ACT_GELU) continue;
     n.fused_act = act;
     n.fused_out = a.d.out[0];
     a.fused_into = i;
@@ -772,46 +908,44 @@ struct Fwd {
   }
 
   int conv_node(int ni) {
-    const tx_node_desc &d = g->nodes[ni].d;
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
     const Shape &x = S(d.in[0]), &w = S(d.in[1]);
-    int yv = d.out[0];
+    const int yv = n.fused_act ? n.fused_out : d.out[0];
     TX_TRY(alloc_value(yv));
-    const Shape &y = S(yv);
-    int64_t N = x[0], C = x[1], H = x[2], W = x[3], OC = w[0], KH = w[2], KW = w[3], OH = y[2], OW = y[3];
-    int64_t K = C * KH * KW, M = N * OH * OW;
-    int64_t ldk = (K + 3) & ~int64_t(3);
-    float *cols = (float *)tx_alloc_raw(ctx, M * ldk * 4);
-    float *tmp = (float *)tx_alloc_raw(ctx, M * OC * 4);
-    if (!cols || !tmp) return TX_ERR_OOM;
-    r->extra[ni] = cols;  // saved for wgrad
-    k_im2col<<<grid_for(M * K, 256), 256, 0, ctx->stream>>>(F(d.in[0]), cols, N, C, H, W, KH, KW, OH, OW,
-                                                           (int)d.ints[0], (int)d.ints[1], (int)d.ints[2],
-                                                           (int)d.ints[3], (int)d.ints[6], (int)d.ints[7], ldk);
-    TX_LAUNCHED(ctx, "k_im2col");
-    if (ldk != K) TX_CUDA(ctx, cudaMemset2DAsync(cols + K, ldk * 4, 0, (ldk - K) * 4, M, ctx->stream));
-    // W is [OC, C*KH*KW] row-major; pad K for TMA by copying into [OC, ldk]
-    float *wk = (float *)F(d.in[1]);
-    float *wpad = nullptr;
-    if (ldk != K) {
-      wpad = (float *)tx_alloc_raw(ctx, OC * ldk * 4);
-      TX_CUDA(ctx, cudaMemsetAsync(wpad, 0, OC * ldk * 4, ctx->stream));
-      TX_CUDA(ctx, cudaMemcpy2DAsync(wpad, ldk * 4, wk, K * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
-      wk = wpad;
+    const Shape &y = S(d.out[0]);
+    const ConvGeom cg = conv_geom(x, w, y, d);
+    const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
+    const bool tf32 = ctx->math == TX_MATH_TF32;
+    // channels-last input, (kh, kw, c) columns, weights permuted to match;
+    // in TF32 mode both operands are stored rounded, so the GEMM reads them as is
+    Scratch xh(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
+        tmp(ctx, (size_t)M * OC * 4);
+    float *cols = (float *)tx_alloc_raw(ctx, (size_t)M * cg.ldk * 4);
+    if (!xh.ptr || !wk.ptr || !tmp.ptr || !cols) {
+      tx_free_raw(ctx, cols);
+      return TX_ERR_OOM;
     }
+    r->extra[ni] = cols;  // saved for wgrad
+    TX_TRY(transpose_b(ctx, F(d.in[0]), xh.as<float>(), cg.N, cg.C, (int64_t)cg.H * cg.W));
+    TX_TRY(im2col_nhwc(ctx, xh.as<float>(), cols, cg, tf32));
+    k_weight_to_khwc<<<grid_for(OC * cg.ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
+                                                                         cg.C, cg.KH, cg.KW, cg.ldk, tf32);
+    TX_LAUNCHED(ctx, "k_weight_to_khwc");
     tx_gemm_desc q;
     memset(&q, 0, sizeof q);
-    q.M = M; q.N = OC; q.K = ldk;
-    q.A = cols; q.lda = ldk; q.trans_a = 0;
-    q.B = wk; q.ldb = ldk; q.trans_b = 1;
-    q.C = tmp; q.ldc = OC; q.alpha = 1.f; q.batch = 1;
-    int rc = gemm_dispatch(ctx, q);
-    if (wpad) tx_free_raw(ctx, wpad);
-    TX_TRY(rc);
-    const float *bias = (d.n_in > 2 && d.in[2] >= 0) ? F(d.in[2]) : nullptr;
-    k_nhwc_to_nchw<<<grid_for(N * OC * OH * OW, 256), 256, 0, ctx->stream>>>(tmp, F(yv), N, OC, OH * OW, bias, 0);
-    TX_LAUNCHED(ctx, "k_nhwc_to_nchw");
-    tx_free_raw(ctx, tmp);
-    return TX_OK;
+    q.M = M; q.N = OC; q.K = cg.ldk;
+    q.A = cols; q.lda = cg.ldk; q.trans_a = 0;
+    q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 1;
+    q.C = tmp.as<float>(); q.ldc = OC; q.alpha = 1.f; q.batch = 1;
+    if (d.n_in > 2 && d.in[2] >= 0) {
+      q.bias = F(d.in[2]);
+      q.bias_scale = 1.f;
+    }
+    q.act = n.fused_act;
+    q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : 0;
+    TX_TRY(gemm_dispatch(ctx, q));
+    return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);
   }
 
   int node(int ni) {
@@ -1201,73 +1335,67 @@ struct Bwd {
   }
 
   int conv_backward(int ni) {
-    const tx_node_desc &d = g->nodes[ni].d;
-    float *dy = grad[d.out[0]];
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    const int yv = n.fused_act ? n.fused_out : d.out[0];
+    float *dy = grad[yv];
     if (!dy) return TX_OK;
     const Shape &x = S(d.in[0]), &w = S(d.in[1]), &y = S(d.out[0]);
-    int64_t N = x[0], C = x[1], H = x[2], W = x[3], OC = w[0], KH = w[2], KW = w[3], OH = y[2], OW = y[3];
-    int64_t K = C * KH * KW, M = N * OH * OW;
-    int64_t ldk = (K + 3) & ~int64_t(3);
-    float *dyt = (float *)tx_alloc_raw(ctx, M * OC * 4);  // [M, OC]
-    if (!dyt) return TX_ERR_OOM;
-    k_nchw_to_nhwc<<<grid_for(M * OC, 256), 256, 0, ctx->stream>>>(dy, dyt, N, OC, OH * OW);
-    TX_LAUNCHED(ctx, "k_nchw_to_nhwc");
-    int rc = TX_OK;
+    const ConvGeom cg = conv_geom(x, w, y, d);
+    const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
+    const int64_t K = (int64_t)cg.KH * cg.KW * cg.C;
+    const bool tf32 = ctx->math == TX_MATH_TF32;
+    // dY (NCHW) -> [M, OC]; a fused activation's derivative is applied on the way
+    Scratch dyt(ctx, (size_t)M * OC * 4);
+    if (!dyt.ptr) return TX_ERR_OOM;
+    const bool apply_dact = n.fused_act && !grad_preact[yv];
+    TX_TRY(transpose_b(ctx, dy, dyt.as<float>(), cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
+                       apply_dact ? F(yv) : nullptr, apply_dact ? n.fused_act : TX_ACT_NONE));
     if (d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
       float *t; int acc;
-      rc = target(d.in[2], &t, &acc);
-      if (rc == TX_OK) rc = tx_bias_grad(ctx, dyt, t, M, OC, 1.f, acc);
-      if (rc == TX_OK) wrote(d.in[2]);
+      TX_TRY(target(d.in[2], &t, &acc));
+      TX_TRY(tx_bias_grad(ctx, dyt.as<float>(), t, M, OC, 1.f, acc));
+      wrote(d.in[2]);
     }
-    if (rc == TX_OK && needs[d.in[1]]) {  // dW[OC, K] = dyt^T cols
+    if (needs[d.in[1]]) {  // dW_khwc[OC, ldk] = dY^T cols, then back to [OC, C, KH, KW]
       float *t; int acc;
-      rc = target(d.in[1], &t, &acc);
-      float *dw = t;
-      float *dwpad = nullptr;
-      if (rc == TX_OK && ldk != K) {
-        dwpad = (float *)tx_alloc_raw(ctx, OC * ldk * 4);
-        dw = dwpad;
-      }
+      TX_TRY(target(d.in[1], &t, &acc));
+      Scratch dwk(ctx, (size_t)OC * cg.ldk * 4);
+      if (!dwk.ptr) return TX_ERR_OOM;
       tx_gemm_desc q; memset(&q, 0, sizeof q);
-      q.M = OC; q.N = ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
-      q.A = dyt; q.lda = OC; q.trans_a = 1;
-      q.B = (const float *)r->extra[ni]; q.ldb = ldk; q.trans_b = 0;
-      q.C = dw; q.ldc = ldk; q.beta = (acc && !dwpad) ? 1.f : 0.f;
-      if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
-      if (rc == TX_OK && dwpad) {
-        if (acc) {
-          float *tmp = (float *)tx_alloc_raw(ctx, OC * K * 4);
-          TX_CUDA(ctx, cudaMemcpy2DAsync(tmp, K * 4, dwpad, ldk * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
-          k_axpy<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(t, tmp, OC * K, 1.f);
-          tx_free_raw(ctx, tmp);
-        } else {
-          TX_CUDA(ctx, cudaMemcpy2DAsync(t, K * 4, dwpad, ldk * 4, K * 4, OC, cudaMemcpyDeviceToDevice, ctx->stream));
-        }
-      }
-      if (dwpad) tx_free_raw(ctx, dwpad);
-      if (rc == TX_OK) wrote(d.in[1]);
+      q.M = OC; q.N = cg.ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
+      q.A = dyt.as<float>(); q.lda = OC; q.trans_a = 1;
+      q.B = (const float *)r->extra[ni]; q.ldb = cg.ldk; q.trans_b = 0;
+      q.C = dwk.as<float>(); q.ldc = cg.ldk;
+      q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+      TX_TRY(gemm_dispatch(ctx, q));
+      k_weight_from_khwc<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(dwk.as<float>(), t, (int)OC, cg.C,
+                                                                        cg.KH, cg.KW, cg.ldk, acc);
+      TX_LAUNCHED(ctx, "k_weight_from_khwc");
+      wrote(d.in[1]);
     }
-    if (rc == TX_OK && needs[d.in[0]]) {  // dcols[M, K] = dyt W ; dx = col2im(dcols)
-      float *dcols = (float *)tx_alloc_raw(ctx, M * ldk * 4);
-      tx_gemm_desc q; memset(&q, 0, sizeof q);
-      q.M = M; q.N = K; q.K = OC; q.alpha = 1.f; q.batch = 1;
-      q.A = dyt; q.lda = OC; q.trans_a = 0;
-      q.B = F(d.in[1]); q.ldb = K; q.trans_b = 0;
-      q.C = dcols; q.ldc = ldk;
-      rc = gemm_dispatch(ctx, q);
+    if (needs[d.in[0]]) {  // dcols[M, ldk] = dY W_khwc ; dx = col2im(dcols) -> NCHW
       float *t; int acc;
-      if (rc == TX_OK) rc = target(d.in[0], &t, &acc);
-      if (rc == TX_OK) {
-        k_col2im<<<grid_for(N * C * H * W, 256), 256, 0, ctx->stream>>>(
-            dcols, t, N, C, H, W, KH, KW, OH, OW, (int)d.ints[0], (int)d.ints[1], (int)d.ints[2],
-            (int)d.ints[3], (int)d.ints[6], (int)d.ints[7], ldk, acc);
-        TX_LAUNCHED(ctx, "k_col2im");
-        wrote(d.in[0]);
-      }
-      tx_free_raw(ctx, dcols);
+      TX_TRY(target(d.in[0], &t, &acc));
+      Scratch wk(ctx, (size_t)OC * cg.ldk * 4), dcols(ctx, (size_t)M * cg.ldk * 4),
+          dxh(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4);
+      if (!wk.ptr || !dcols.ptr || !dxh.ptr) return TX_ERR_OOM;
+      k_weight_to_khwc<<<grid_for(OC * cg.ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
+                                                                           cg.C, cg.KH, cg.KW, cg.ldk, tf32);
+      TX_LAUNCHED(ctx, "k_weight_to_khwc");
+      tx_gemm_desc q; memset(&q, 0, sizeof q);
+      q.M = M; q.N = cg.ldk; q.K = OC; q.alpha = 1.f; q.batch = 1;
+      q.A = dyt.as<float>(); q.lda = OC; q.trans_a = 0;
+      q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 0;
+      q.C = dcols.as<float>(); q.ldc = cg.ldk;
+      q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+      TX_TRY(gemm_dispatch(ctx, q));
+      TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
+      TX_TRY(transpose_b(ctx, dxh.as<float>(), t, cg.N, (int64_t)cg.H * cg.W, cg.C, nullptr, nullptr,
+                         TX_ACT_NONE, acc));
+      wrote(d.in[0]);
     }
-    tx_free_raw(ctx, dyt);
-    return rc;
+    return TX_OK;
   }
 
   // dX (+)= reduce_to_shape(src) for broadcast binary backward

@@ -203,12 +203,75 @@ __global__ void k_gemm_split_reduce(tx_gemm_desc d, const float *__restrict__ pa
   }
 }
 
+// Many splits of a small output: block (32, 8) covers 128 consecutive output
+// elements (4 per thread, flattened row-major), its 8 row groups take splits
+// ty, ty + 8, ... in order, and the groups are combined in a fixed order
+// before the epilogue.  N % 4 == 0 so that 4 consecutive elements share a row.
+__global__ void k_gemm_split_reduce_tree(tx_gemm_desc d, const float *__restrict__ part, int splits) {
+  __shared__ float4 sm[8][32];
+  const int64_t n = d.M * d.N;
+  const int64_t e = ((int64_t)blockIdx.x * 32 + threadIdx.x) * 4;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e < n) {
+    int p = threadIdx.y;
+    for (; p + 24 < splits; p += 32) {
+      float4 t[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(part + (int64_t)(p + 8 * j) * n + e);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s.x += t[j].x;
+        s.y += t[j].y;
+        s.z += t[j].z;
+        s.w += t[j].w;
+      }
+    }
+    for (; p < splits; p += 8) {
+      const float4 t = *reinterpret_cast<const float4 *>(part + (int64_t)p * n + e);
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+  }
+  sm[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || e >= n) return;
+  float4 t = sm[0][threadIdx.x];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    const float4 u = sm[i][threadIdx.x];
+    t.x += u.x;
+    t.y += u.y;
+    t.z += u.z;
+    t.w += u.w;
+  }
+  const int64_t gm = e / d.N, gn = e - gm * d.N;
+  const float4 o = make_float4(split_epilogue(d, t.x, gm, gn), split_epilogue(d, t.y, gm, gn + 1),
+                               split_epilogue(d, t.z, gm, gn + 2), split_epilogue(d, t.w, gm, gn + 3));
+  float *c = d.C + gm * d.ldc + gn;
+  if (((d.ldc & 3) == 0) && ((((uintptr_t)c) & 15) == 0)) {
+    *reinterpret_cast<float4 *>(c) = o;
+  } else {
+    c[0] = o.x;
+    c[1] = o.y;
+    c[2] = o.z;
+    c[3] = o.w;
+  }
+}
+
 }  // namespace
 
 // Sum `splits` raw [M, N] partial products in a fixed order (IEEE fp32 adds) and
 // apply the epilogue of d.  Shared by the split-K paths of both GEMM kernels.
 int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits) {
   const int vec = ((d.N & 3) == 0) && ((((uintptr_t)part) & 15) == 0);
+  if (vec && splits >= 16 && d.M * d.N <= (int64_t)ctx->num_sms * 512) {
+    const int64_t blocks = (d.M * d.N + 127) / 128;
+    k_gemm_split_reduce_tree<<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(d, part, splits);
+    TX_LAUNCHED(ctx, "k_gemm_split_reduce_tree");
+    return TX_OK;
+  }
   dim3 block(32, 8);
   dim3 grid((unsigned)((d.N + 127) / 128), (unsigned)((d.M + 7) / 8));
   if (grid.y > 65535) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "split-K reduce: M too large");

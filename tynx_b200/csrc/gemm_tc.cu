@@ -799,7 +799,10 @@ Tiling pick_tiling(tx_ctx *ctx, int64_t M, int64_t N, int64_t K, int64_t batch, 
       int64_t want = (ctx->num_sms + tiles - 1) / tiles;
       int64_t most = total_kb / 8;  // at least 8 k-blocks (K = 256) per split
       max_split = (int)(want < most ? want : most);
-      if (max_split > 32) max_split = 32;
+      // many splits only while their partial tiles stay small (a weight
+      // gradient with a tiny output and a reduction over every pixel)
+      const int cap = (double)M * N * 4 * 128 <= 64.0 * (1 << 20) ? 128 : 32;
+      if (max_split > cap) max_split = cap;
     }
     for (int s = 1; s <= max_split; s = s < 4 ? s + 1 : s * 2) {
       const int kb_per = (total_kb + s - 1) / s;
