@@ -198,6 +198,8 @@ def main() -> None:
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-budget", type=float, default=15.0)
+    parser.add_argument("--bucket-mb", type=float, default=2.0,
+                        help="gradient all-reduce bucket size when N > 1")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -229,7 +231,7 @@ def main() -> None:
     opt = tx.optim.Adam(model.named_parameters(), lr=wl.lr)
     if world > 1:
         init_data_parallel(world, rank)
-        model.enable_data_parallel(bucket_mb=8)
+        model.enable_data_parallel(bucket_mb=args.bucket_mb)
     key = "ids" if args.workload == "transformer" else "x"
     xdtype = "int64" if key == "ids" else "float32"
 
@@ -369,15 +371,25 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
         M, N_, K = per_rank * 128, 1024, 256
     else:
         M, N_, K = per_rank * 256, 64, 288
+    from tynx_b200 import _native as N
+
     rng = np.random.default_rng(0)
     A = tx.Tensor(rng.standard_normal((M, K)).astype(np.float32))
     B = tx.Tensor(rng.standard_normal((N_, K)).astype(np.float32))
     Cm = tx.zeros(M, N_)
     bias = tx.zeros(N_)
+    flags = 0
+    if math == "tf32":
+        # as in the step: the activation arrives TF32-rounded from the previous
+        # epilogue, the weight from the TF32 shadow, and the output is stored
+        # rounded for the next contraction
+        for t in (A, B):
+            ctx.check(N.lib.tx_round_tf32(ctx.handle, t.ptr, t.ptr, t.nbytes // 4))
+        flags = N.TX_GEMM_A_TF32 | N.TX_GEMM_B_TF32 | N.TX_GEMM_ROUND_OUT
 
     def launch():
         _core.gemm(ctx, M, N_, K, A.ptr, K, False, B.ptr, K, True, Cm.ptr, N_, bias=bias.ptr,
-                   act="relu")
+                   act="relu", flags=flags)
 
     for _ in range(5):
         launch()

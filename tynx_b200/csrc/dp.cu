@@ -136,6 +136,9 @@ int dp_allreduce_range(tx_ctx *ctx, float *buf, int64_t n) {
   if (n <= 0) return TX_OK;
   ncclResult_t r = ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclAvg, s->comm, ctx->comm);
   if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(ctx, r, "ncclAllReduce");
+  // a non-blocking communicator takes its next call only once this one has
+  // left ncclInProgress (the enqueue, not the reduction itself)
+  if (r == ncclInProgress) return nccl_wait(ctx, s->comm, ctx->dp_timeout_ms, "ncclAllReduce");
   return TX_OK;
 }
 
@@ -147,5 +150,6 @@ extern "C" int tx_dp_allreduce(tx_ctx *ctx, float *buf, int64_t n, int average) 
   ncclResult_t r = ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, average ? ncclAvg : ncclSum,
                                  s->comm, ctx->comm);
   if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(ctx, r, "ncclAllReduce");
+  if (r == ncclInProgress) TX_TRY(nccl_wait(ctx, s->comm, ctx->dp_timeout_ms, "ncclAllReduce"));
   return dp_event_join(ctx);
 }
