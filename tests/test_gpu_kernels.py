@@ -366,14 +366,15 @@ def test_cross_entropy_rejects_out_of_range_labels(tx):
         pytest.approx(np.log(3.0), rel=1e-6)
 
 
-def test_layernorm_matches_oracle(tx):
+@pytest.mark.parametrize("cols", [256, 100, 1024])  # register-resident rows, scalar path, mixed
+def test_layernorm_matches_oracle(tx, cols):
     from oracle import flex_oracle as fo
     from tynx_b200 import _native as N
     from tynx_b200._core import context
 
     ctx = context()
     rng = np.random.default_rng(2)
-    rows, cols = 3000, 256
+    rows = 3000
     x = rng.standard_normal((rows, cols)).astype(np.float32) * 2 + 1
     g = rng.standard_normal(cols).astype(np.float32)
     b = rng.standard_normal(cols).astype(np.float32)

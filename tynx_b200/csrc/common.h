@@ -115,6 +115,11 @@ int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const in
 int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_t *out_shape, int ndim,
               float *y, float scale, int acc);
 
+// LayerNorm forward; round_tf32 stores y rounded to TF32 (for an output that
+// only feeds contractions; the backward reads x, mean and rstd, not y).
+int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
+                  float *rstd, int64_t rows, int64_t cols, float eps, bool round_tf32);
+
 // grid sizing helper
 inline unsigned grid_for(int64_t n, int threads, int64_t max_blocks = 148 * 16) {
   int64_t b = (n + threads - 1) / threads;

@@ -650,21 +650,31 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
   }
 
   // ---- TF32 output rounding: results whose every reader is a contraction --------------------
+  // (directly, or through reshapes and transposes, which move values unchanged)
+  std::function<bool(int, int)> feeds_only_contractions = [&](int v, int depth) -> bool {
+    const GValue &gv = g->values[v];
+    if (gv.is_output || gv.consumers.empty() || depth > 8) return false;
+    for (int c : gv.consumers) {
+      const tx_node_desc &cd = g->nodes[c].d;
+      if (cd.op == TX_OP_GEMM || cd.op == TX_OP_MATMUL) {
+        for (int k = 2; k < cd.n_in; ++k)
+          if (cd.in[k] == v) return false;  // a bias is not a contraction operand
+      } else if (is_alias_op(cd.op) || cd.op == TX_OP_TRANSPOSE) {
+        if (cd.in[0] != v || !feeds_only_contractions(cd.out[0], depth + 1)) return false;
+      } else {
+        return false;
+      }
+    }
+    return true;
+  };
   for (int i = 0; i < n_nodes; ++i) {
     GNode &n = g->nodes[i];
-    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL) continue;
-    if (n.fused_act == TX_ACT_TANH) continue;  // tanh' reads the stored output
-    const int yv = n.fused_act ? n.fused_out : n.d.out[0];
-    const GValue &y = g->values[yv];
-    if (y.is_output || y.consumers.empty()) continue;
-    bool ok = true;
-    for (int c : y.consumers) {
-      const tx_node_desc &cd = g->nodes[c].d;
-      if (cd.op != TX_OP_GEMM && cd.op != TX_OP_MATMUL) { ok = false; break; }
-      for (int k = 2; k < cd.n_in; ++k)
-        if (cd.in[k] == yv) ok = false;  // a bias is not a contraction operand
+    if (n.d.op == TX_OP_GEMM || n.d.op == TX_OP_MATMUL) {
+      if (n.fused_act == TX_ACT_TANH) continue;  // tanh' reads the stored output
+      n.round_out = feeds_only_contractions(n.fused_act ? n.fused_out : n.d.out[0], 0);
+    } else if (n.d.op == TX_OP_LAYERNORM) {
+      n.round_out = feeds_only_contractions(n.d.out[0], 0);
     }
-    n.round_out = ok;
   }
 
   // ---- parameter storage: order = when gradients become final in backward -----------------
@@ -955,6 +965,7 @@ struct Fwd {
     if (is_alias_op(d.op)) {
       r->buf[d.out[0]] = r->buf[d.in[0]];
       r->owned[d.out[0]] = false;
+      r->tf32[d.out[0]] = r->tf32[d.in[0]];
       return TX_OK;
     }
     switch (d.op) {
@@ -996,8 +1007,10 @@ struct Fwd {
           r->extra2[ni].push_back(rstd);
         }
         const float *beta = (d.n_in > 2 && d.in[2] >= 0) ? F(d.in[2]) : nullptr;
-        return tx_layernorm_fwd(ctx, F(d.in[0]), F(d.in[1]), beta, F(yv), mean, rstd, rows, cols,
-                                (float)d.fattr[0]);
+        const bool rnd = g->nodes[ni].round_out && ctx->math == TX_MATH_TF32;
+        if (rnd) r->tf32[yv] = true;
+        return layernorm_fwd(ctx, F(d.in[0]), F(d.in[1]), beta, F(yv), mean, rstd, rows, cols,
+                             (float)d.fattr[0], rnd);
       }
       case TX_OP_ADD: case TX_OP_SUB: case TX_OP_MUL: case TX_OP_DIV: {
         int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS];
@@ -1041,6 +1054,7 @@ struct Fwd {
         int64_t st = 1;
         for (int i = nd - 1; i >= 0; --i) { xs[i] = st; st *= x[i]; }
         for (int i = 0; i < nd; ++i) ss[i] = xs[d.n_ints ? d.ints[i] : nd - 1 - i];
+        r->tf32[yv] = r->tf32[d.in[0]];  // a transpose moves values unchanged
         return tx_strided_copy(ctx, F(d.in[0]), ss, F(yv), y.data(), nd, g->values[d.in[0]].dtype == TX_DT_I64 ? 8 : 4);
       }
     }

@@ -673,6 +673,283 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- persistent variant ------------------------------------------------------------------
+// For operands that need no conversion (TF32 mode with pre-rounded operands,
+// or the truncating mode): one CTA per SM walks the output tiles (tile order:
+// N fastest, so CTAs that run together share A rows in L2).  The TMA / MMA
+// ring runs on across tiles, and TMEM holds two accumulator buffers, so the
+// MMA warp fills one while the epilogue warps drain the other.  The epilogue
+// has its own shared memory (the stages stay busy): per warp two output tiles
+// plus two pre-activation, act'-source and C tiles when the GEMM uses them.
+constexpr int kSmemMax = 232448;  // 227 KB opt-in
+constexpr int kPTail = 2048;
+
+template <int BN>
+struct PCfg {
+  static constexpr int NACC = BN == 256 ? 1 : 2;
+  static constexpr int ACC = BN * NACC;                 // columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC < 256 ? 256 : 2 * ACC;
+  static constexpr int A_BYTES = TC_BM * TC_BK * 4;
+  static constexpr int B_BYTES = BN * TC_BK * 4;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+};
+
+struct PWork {
+  int tiles_m, tiles_n, items;
+  int total_kb, kb_per;  // kb_per > 0: split-K, the third item index is the split
+  int stages;            // pipeline depth (runtime: the epilogue's tiles vary)
+  int ep_stride;         // epilogue bytes per warp
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
+               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, PWork w) {
+  using Cfg = PCfg<BN>;
+  constexpr int NACC = Cfg::NACC;
+  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int stages = w.stages;
+  uint8_t *ep = smem + stages * Cfg::STAGE;
+  uint8_t *tail = ep + 4 * w.ep_stride;
+  uint64_t *full = (uint64_t *)tail;
+  uint64_t *empty = full + 8;
+  uint64_t *tfull = empty + 8;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *ebar = tempty + 2;
+  uint32_t *tmem_holder = (uint32_t *)(ebar + 8);
+  volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
+  float *bias_rows = reinterpret_cast<float *>(tail + 1024);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool split = w.kb_per > 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+    }
+    for (int i = 0; i < 8; ++i) mbar_init(&ebar[i], 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(Cfg::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  // item -> (z, m tile, n tile) and its k-block range
+  auto decode = [&](int item, int &m0, int &n0, int &z, int &kb_first, int &num_k) {
+    const int nt = item % w.tiles_n;
+    const int t = item / w.tiles_n;
+    m0 = (t % w.tiles_m) * TC_BM;
+    n0 = nt * BN;
+    z = t / w.tiles_m;
+    kb_first = split ? z * w.kb_per : 0;
+    num_k = split ? min(w.kb_per, w.total_kb - kb_first) : w.total_kb;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t cnt = 0;
+      for (int item = blockIdx.x; item < w.items && !*abort_flag; item += gridDim.x) {
+        int m0, n0, z, kb_first, num_k;
+        decode(item, m0, n0, z, kb_first, num_k);
+        const int zc = split ? 0 : z;
+        for (int kb = 0; kb < num_k; ++kb, ++cnt) {
+          const int s = (int)(cnt % (uint32_t)stages);
+          const uint32_t round = cnt / (uint32_t)stages;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 11)) break;
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+          const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
+          const uint32_t b_dst = a_dst + A_BYTES;
+          const int k0 = (kb_first + kb) * TC_BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
+          } else {
+            tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
+          } else {
+            tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(TC_BM >> 4) << 24);
+      uint32_t cnt = 0;
+      int it = 0;
+      for (int item = blockIdx.x; item < w.items && !*abort_flag; item += gridDim.x, ++it) {
+        int m0, n0, z, kb_first, num_k;
+        decode(item, m0, n0, z, kb_first, num_k);
+        const int buf = it & 1;
+        const uint32_t use = (uint32_t)it >> 1;
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, err, 12)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb, ++cnt) {
+          const int s = (int)(cnt % (uint32_t)stages);
+          const uint32_t round = cnt / (uint32_t)stages;
+          if (!mbar_wait(&full[s], round & 1, abort_flag, err, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE);
+          const uint32_t b_base = a_base + A_BYTES;
+          const uint32_t acc = tmem + (uint32_t)(buf * Cfg::ACC + (kb % NACC) * BN);
+          const bool fresh = kb < NACC;
+#pragma unroll
+          for (int k = 0; k < TC_BK / 8; ++k)
+            tc_mma_tf32(acc, operand_desc<A_MN>(a_base, k), operand_desc<B_MN>(b_base, k), idesc,
+                        (fresh && k == 0) ? 0u : 1u);
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&tfull[buf]);  // arrives when every MMA of this tile has completed
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    uint8_t *eb = ep + quad * w.ep_stride;
+    const bool need_s = d.dact != TX_ACT_NONE;
+    const bool need_c = d.beta != 0.f;
+    const bool need_p = d.preact != nullptr;
+    const bool loads = need_s || need_c;
+    // per-warp tile slots: out[2], then pre[2], s[2], c[2] when used
+    uint8_t *out_t = eb;
+    uint8_t *pre_t = eb + 8192;
+    uint8_t *s_t = pre_t + (need_p ? 8192 : 0);
+    uint8_t *c_t = s_t + (need_s ? 8192 : 0);
+    float *bw = bias_rows + quad * 32;
+    constexpr int NCH = BN / 32;
+    uint32_t issued = 0, consumed = 0, chunk_seq = 0;
+    int it = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < w.items && alive; item += gridDim.x, ++it) {
+      int m0, n0, z, kb_first, num_k;
+      decode(item, m0, n0, z, kb_first, num_k);
+      const int buf = it & 1;
+      const uint32_t use = (uint32_t)it >> 1;
+      const int row_tile = m0 + quad * 32;
+      const int used_acc = num_k < NACC ? num_k : NACC;
+      auto issue = [&](int c) {  // lane 0: act' / C tiles of chunk c into ring slot `issued & 1`
+        const int slot = issued & 1;
+        uint64_t *bar = &ebar[quad * 2 + slot];
+        mbar_expect_tx(bar, (need_s ? 4096u : 0u) + (need_c ? 4096u : 0u));
+        if (need_s) tma_load_3d(smem_u32(s_t + slot * 4096), &mapS, bar, n0 + 32 * c, row_tile, z);
+        if (need_c) tma_load_3d(smem_u32(c_t + slot * 4096), &mapC, bar, n0 + 32 * c, row_tile, z);
+      };
+      if (loads) {
+        for (int c = 0; c < (NCH < 2 ? NCH : 2); ++c) {
+          if (lane == 0) issue(c);
+          ++issued;
+        }
+      }
+      if (!mbar_wait(&tfull[buf], use & 1, abort_flag, err, 14)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c, ++chunk_seq) {
+        const int oslot = chunk_seq & 1;
+        float v[32], sv[32], cv[32];
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * Cfg::ACC + c * 32);
+        tmem_ld32(lane_base, v);
+#pragma unroll 1
+        for (int a = 1; a < used_acc; ++a) {
+          float t[32];
+          tmem_ld32(lane_base + (uint32_t)(a * BN), t);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += t[j];
+        }
+        if (c == NCH - 1) {
+          // this warp has read its rows of the accumulator: hand the buffer back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[j] = cv[j] = 0.f;
+        if (loads) {
+          const int lslot = consumed & 1;
+          if (!mbar_wait(&ebar[quad * 2 + lslot], (consumed >> 1) & 1, abort_flag, err, 15)) {
+            alive = false;
+            break;
+          }
+          ++consumed;
+          if (need_s) tile_row_load(s_t + lslot * 4096, lane, sv);
+          if (need_c) tile_row_load(c_t + lslot * 4096, lane, cv);
+          __syncwarp();
+          if (c + 2 < NCH) {
+            if (lane == 0) issue(c + 2);
+            ++issued;
+          }
+        }
+        const int64_t gnb = (int64_t)n0 + c * 32 + lane;
+        bw[lane] = (d.bias && gnb < d.N) ? d.bias[gnb] * d.bias_scale : 0.f;
+        if (lane == 0 && chunk_seq >= 2) bulk_wait_read<1>();  // tiles of chunk_seq - 2 are free
+        __syncwarp();
+        uint8_t *pre_tile = need_p ? pre_t + oslot * 4096 : nullptr;
+        if (!d.dact) {
+          switch (d.act) {
+            case TX_ACT_RELU: chunk_math<TX_ACT_RELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_TANH: chunk_math<TX_ACT_TANH, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_GELU: chunk_math<TX_ACT_GELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            default: chunk_math<TX_ACT_NONE, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+          }
+        } else if (d.act == TX_ACT_NONE) {
+          switch (d.dact) {
+            case TX_ACT_RELU: chunk_math<TX_ACT_NONE, TX_ACT_RELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            case TX_ACT_TANH: chunk_math<TX_ACT_NONE, TX_ACT_TANH>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+            default: chunk_math<TX_ACT_NONE, TX_ACT_GELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
+          }
+        } else {
+          chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
+        }
+        tile_row_store(out_t + oslot * 4096, lane, v);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&mapC, smem_u32(out_t + oslot * 4096), n0 + 32 * c, row_tile, z);
+          if (need_p) tma_store_3d(&mapP, smem_u32(pre_tile), n0 + 32 * c, row_tile, z);
+          bulk_commit();
+        }
+        __syncwarp();
+      }
+    }
+    for (uint32_t c = consumed; c < issued; ++c) mbar_drain(&ebar[quad * 2 + (c & 1)], (c >> 1) & 1);
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg::TMEM_COLS));
+  }
+}
+
 // ---- host side ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -781,6 +1058,57 @@ struct Tiling {
   int splits = 1;
 };
 
+template <int BN, bool A_MN, bool B_MN>
+int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem) {
+  auto kern = k_gemm_tcp<BN, A_MN, B_MN>;
+  static bool configured[64] = {};
+  const int dev = ctx->device & 63;
+  if (!configured[dev]) {
+    TX_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+    configured[dev] = true;
+  }
+  const int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
+  kern<<<grid, 192, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
+  TX_LAUNCHED(ctx, "k_gemm_tcp");
+  return TX_OK;
+}
+
+template <int BN>
+int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem) {
+  const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
+  if (a_mn && b_mn) return launch_p<BN, true, true>(ctx, d, m, w, smem);
+  if (a_mn) return launch_p<BN, true, false>(ctx, d, m, w, smem);
+  if (b_mn) return launch_p<BN, false, true>(ctx, d, m, w, smem);
+  return launch_p<BN, false, false>(ctx, d, m, w, smem);
+}
+
+// Persistent launch of d (raw split partials when kb_per > 0, z = splits or
+// batch).  TX_ERR_UNSUPPORTED when the stages would not fit next to the
+// epilogue's tiles.
+int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per) {
+  const int stage = (TC_BM + bn) * TC_BK * 4;
+  const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
+  PWork w;
+  w.ep_stride = kinds * 8192;
+  w.stages = (kSmemMax - 1024 - kPTail - 4 * w.ep_stride) / stage;
+  if (w.stages > 8) w.stages = 8;
+  if (w.stages < 2) return TX_ERR_UNSUPPORTED;
+  w.tiles_m = (int)((d.M + TC_BM - 1) / TC_BM);
+  w.tiles_n = (int)((d.N + bn - 1) / bn);
+  w.total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
+  w.kb_per = kb_per;
+  const int64_t items = (int64_t)w.tiles_m * w.tiles_n * z;
+  if (items > 0x7fffffff) return TX_ERR_UNSUPPORTED;
+  w.items = (int)items;
+  const int smem = 1024 + w.stages * stage + 4 * w.ep_stride + kPTail;
+  switch (bn) {
+    case 256: return launch_p_bn<256>(ctx, d, m, w, smem);
+    case 64: return launch_p_bn<64>(ctx, d, m, w, smem);
+    default: return launch_p_bn<128>(ctx, d, m, w, smem);
+  }
+}
+
+
 // Pick the tile width and the K split from a small cost model: waves of CTAs
 // times the per-CTA k-block work (one 128 x BN x 32 step costs about BN + 96
 // "column units" including the fixed TMA/commit latency), plus the traffic of
@@ -846,7 +1174,19 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
     m.conv_mask = ((d.flags & TX_GEMM_A_TF32) ? 0 : 1) | ((d.flags & TX_GEMM_B_TF32) ? 0 : 2);
     if (m.conv_mask == 0) mode = 0;
   }
-  const Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
+  Tiling tiling = pick_tiling(ctx, d.M, d.N, d.K, batch, mode == 2 ? 128 : 256);
+  // Without operand conversion, shapes with more 128 x 256 tiles than SMs run
+  // persistently: the epilogue of one tile overlaps the next tile's main loop
+  // (measured: 32768x1024x256 100 -> 70 us, 32768x256x256 33 -> 27 us); one
+  // wave gains nothing from it and keeps two interleaved accumulators.
+  bool persistent = false;
+  if (mode == 0 && tiling.splits == 1 && d.N > 128) {
+    const int64_t tiles256 = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + 255) / 256) * batch;
+    if (tiles256 > ctx->num_sms) {
+      persistent = true;
+      tiling.bn = 256;
+    }
+  }
   const int bn = tiling.bn;
   bool ok;
   if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
@@ -868,6 +1208,10 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   int splits = tiling.splits;
   if (splits <= 1) {
     make_epilogue_maps(m, d, batch);
+    if (persistent && m.tma_epi) {
+      const int rc = launch_persistent(ctx, bn, d, m, batch, 0);
+      if (rc != TX_ERR_UNSUPPORTED) return rc;
+    }
     return launch_any(ctx, mode, bn, d, m, batch, 0);
   }
   const int kb_per = (total_kb + splits - 1) / splits;
@@ -887,6 +1231,9 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   raw.dact_src = nullptr;
   raw.flags = d.flags & ~TX_GEMM_ROUND_OUT;  // partials stay exact; the reduction rounds
   make_epilogue_maps(m, raw, splits);
-  TX_TRY(launch_any(ctx, mode, bn, raw, m, splits, kb_per));
+  int rc = TX_ERR_UNSUPPORTED;
+  if (persistent && m.tma_epi) rc = launch_persistent(ctx, bn, raw, m, splits, kb_per);
+  if (rc == TX_ERR_UNSUPPORTED) rc = launch_any(ctx, mode, bn, raw, m, splits, kb_per);
+  TX_TRY(rc);
   return gemm_split_reduce(ctx, d, part.as<float>(), splits);
 }

@@ -8,6 +8,7 @@
 // scratch buffer, then a fixed-order sum) so results are deterministic.
 #include <math.h>
 
+#include <initializer_list>
 #include <mutex>
 
 #include "common.h"
@@ -313,7 +314,7 @@ __global__ void k_xent_bwd(const float *__restrict__ z, const int64_t *__restric
 __global__ void k_layernorm_fwd(const float *__restrict__ x, const float *__restrict__ gamma,
                                 const float *__restrict__ beta, float *__restrict__ y,
                                 float *__restrict__ mean_out, float *__restrict__ rstd_out,
-                                int64_t rows, int64_t cols, float eps) {
+                                int64_t rows, int64_t cols, float eps, int round_tf32) {
   int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
   int lane = threadIdx.x & 31;
   for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
@@ -332,12 +333,148 @@ __global__ void k_layernorm_fwd(const float *__restrict__ x, const float *__rest
     float *yr = y + r * cols;
     for (int64_t c = lane; c < cols; c += kWarp) {
       float v = (xr[c] - mu) * rstd * gamma[c];
-      yr[c] = beta ? v + beta[c] : v;
+      if (beta) v += beta[c];
+      yr[c] = round_tf32 ? tx_epi::round_tf32(v) : v;
     }
     if (lane == 0) {
       if (mean_out) mean_out[r] = mu;
       if (rstd_out) rstd_out[r] = rstd;
     }
+  }
+}
+
+// Register-resident variants for rows of VPL * 128 floats (cols % 128 == 0,
+// up to 1024): a warp per row, each lane holding VPL float4 of it, so the row
+// is read from HBM once.  Same formulas as the scalar kernels
+// (normalization.rs:135-190): mean, biased variance of the centred values,
+// rstd = (var + eps)^-1/2.
+template <int VPL>
+__global__ void k_layernorm_fwd_v(const float *__restrict__ x, const float *__restrict__ gamma,
+                                  const float *__restrict__ beta, float *__restrict__ y,
+                                  float *__restrict__ mean_out, float *__restrict__ rstd_out, int64_t rows,
+                                  float eps, int round_tf32) {
+  constexpr int cols = VPL * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows; r += warps) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + r * cols);
+    float4 v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      v[j] = xr[j * 32 + lane];
+      s += v[j].x + v[j].y + v[j].z + v[j].w;
+    }
+    const float mu = warp_sum(s) / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const float a = v[j].x - mu, b = v[j].y - mu, c = v[j].z - mu, e = v[j].w - mu;
+      q += a * a + b * b + c * c + e * e;
+    }
+    const float var = warp_sum(q) / (float)cols;
+    const float rstd = 1.0f / sqrtf(var + eps);
+    float4 *yr = reinterpret_cast<float4 *>(y + r * cols);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c4 = j * 32 + lane;
+      const float4 gm = reinterpret_cast<const float4 *>(gamma)[c4];
+      const float4 bt = beta ? reinterpret_cast<const float4 *>(beta)[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = (v[j].x - mu) * rstd * gm.x + bt.x;
+      o.y = (v[j].y - mu) * rstd * gm.y + bt.y;
+      o.z = (v[j].z - mu) * rstd * gm.z + bt.z;
+      o.w = (v[j].w - mu) * rstd * gm.w + bt.w;
+      if (round_tf32) {
+        o.x = tx_epi::round_tf32(o.x);
+        o.y = tx_epi::round_tf32(o.y);
+        o.z = tx_epi::round_tf32(o.z);
+        o.w = tx_epi::round_tf32(o.w);
+      }
+      yr[c4] = o;
+    }
+    if (lane == 0) {
+      if (mean_out) mean_out[r] = mu;
+      if (rstd_out) rstd_out[r] = rstd;
+    }
+  }
+}
+
+// Backward, 8 warps per block: dx per row from registers; each lane keeps the
+// dgamma / dbeta partial sums of its columns over the rows its warp visits,
+// and the 8 warps are combined in a fixed order into one partial row per block.
+template <int VPL>
+__global__ void __launch_bounds__(256) k_layernorm_bwd_v(const float *__restrict__ x, const float *__restrict__ gamma,
+                                  const float *__restrict__ mean_in, const float *__restrict__ rstd_in,
+                                  const float *__restrict__ dy, float *__restrict__ dx,
+                                  float *__restrict__ part_g, float *__restrict__ part_b, int64_t rows,
+                                  int acc_dx) {
+  constexpr int cols = VPL * 128;
+  __shared__ float4 sg[8][VPL * 32], sb[8][VPL * 32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float4 pg[VPL], pb[VPL], gm[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    pg[j] = pb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    gm[j] = reinterpret_cast<const float4 *>(gamma)[j * 32 + lane];
+  }
+  for (int64_t r = blockIdx.x * (int64_t)8 + w; r < rows; r += (int64_t)gridDim.x * 8) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + r * cols);
+    const float4 *gr = reinterpret_cast<const float4 *>(dy + r * cols);
+    const float mu = mean_in[r], rs = rstd_in[r];
+    float4 xh[VPL], g[VPL];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const float4 xv = xr[j * 32 + lane], dv = gr[j * 32 + lane];
+      xh[j] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
+      g[j] = make_float4(dv.x * gm[j].x, dv.y * gm[j].y, dv.z * gm[j].z, dv.w * gm[j].w);
+      s1 += g[j].x + g[j].y + g[j].z + g[j].w;
+      s2 += g[j].x * xh[j].x + g[j].y * xh[j].y + g[j].z * xh[j].z + g[j].w * xh[j].w;
+      pg[j].x += dv.x * xh[j].x;
+      pg[j].y += dv.y * xh[j].y;
+      pg[j].z += dv.z * xh[j].z;
+      pg[j].w += dv.w * xh[j].w;
+      pb[j].x += dv.x;
+      pb[j].y += dv.y;
+      pb[j].z += dv.z;
+      pb[j].w += dv.w;
+    }
+    s1 = warp_sum(s1) / (float)cols;
+    s2 = warp_sum(s2) / (float)cols;
+    if (dx) {
+      float4 *dr = reinterpret_cast<float4 *>(dx + r * cols);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        float4 o = make_float4(rs * (g[j].x - s1 - xh[j].x * s2), rs * (g[j].y - s1 - xh[j].y * s2),
+                               rs * (g[j].z - s1 - xh[j].z * s2), rs * (g[j].w - s1 - xh[j].w * s2));
+        if (acc_dx) {
+          const float4 p = dr[j * 32 + lane];
+          o.x += p.x;
+          o.y += p.y;
+          o.z += p.z;
+          o.w += p.w;
+        }
+        dr[j * 32 + lane] = o;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    sg[w][j * 32 + lane] = pg[j];
+    sb[w][j * 32 + lane] = pb[j];
+  }
+  __syncthreads();
+  for (int c4 = threadIdx.x; c4 < VPL * 32; c4 += blockDim.x) {
+    float4 a = sg[0][c4], b = sb[0][c4];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) {
+      const float4 u = sg[i][c4], t = sb[i][c4];
+      a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
+      b.x += t.x; b.y += t.y; b.z += t.z; b.w += t.w;
+    }
+    reinterpret_cast<float4 *>(part_g + blockIdx.x * (int64_t)cols)[c4] = a;
+    reinterpret_cast<float4 *>(part_b + blockIdx.x * (int64_t)cols)[c4] = b;
   }
 }
 
@@ -927,15 +1064,41 @@ extern "C" int tx_softmax_xent_bwd(tx_ctx *ctx, const float *z, const int64_t *l
   return TX_OK;
 }
 
+static bool ln_vec(int64_t cols, std::initializer_list<const void *> ptrs) {
+  if (cols % 128 || cols > 1024) return false;
+  for (const void *p : ptrs)
+    if (((uintptr_t)p) & 15) return false;
+  return true;
+}
+
+int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
+                  float *rstd, int64_t rows, int64_t cols, float eps, bool round_tf32) {
+  if (rows <= 0) return TX_OK;
+  if (ln_vec(cols, {x, gamma, beta, y})) {
+    const unsigned blocks = rows_grid(rows, 8);
+    const int rt = round_tf32 ? 1 : 0;
+    switch (cols / 128) {
+      case 1: k_layernorm_fwd_v<1><<<blocks, 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows, eps, rt); break;
+      case 2: k_layernorm_fwd_v<2><<<blocks, 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows, eps, rt); break;
+      case 4: k_layernorm_fwd_v<4><<<blocks, 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows, eps, rt); break;
+      case 8: k_layernorm_fwd_v<8><<<blocks, 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows, eps, rt); break;
+      default: goto scalar;
+    }
+    TX_LAUNCHED(ctx, "k_layernorm_fwd_v");
+    return TX_OK;
+  }
+scalar:
+  k_layernorm_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows,
+                                                             cols, eps, round_tf32 ? 1 : 0);
+  TX_LAUNCHED(ctx, "k_layernorm_fwd");
+  return TX_OK;
+}
+
 extern "C" int tx_layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta,
                                 float *y, float *mean, float *rstd, int64_t rows, int64_t cols,
                                 float eps) {
   if (!ctx) return TX_ERR_INVALID;
-  if (rows <= 0) return TX_OK;
-  k_layernorm_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, gamma, beta, y, mean, rstd, rows,
-                                                             cols, eps);
-  TX_LAUNCHED(ctx, "k_layernorm_fwd");
-  return TX_OK;
+  return layernorm_fwd(ctx, x, gamma, beta, y, mean, rstd, rows, cols, eps, false);
 }
 
 extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma, const float *mean,
@@ -943,6 +1106,25 @@ extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma,
                                 float *dbeta, int64_t rows, int64_t cols, int acc_dx, int acc_p) {
   if (!ctx) return TX_ERR_INVALID;
   if (rows <= 0) return TX_OK;
+  const int vpl = (int)(cols / 128);
+  if (ln_vec(cols, {x, gamma, dy, dx}) && (vpl == 1 || vpl == 2 || vpl == 4)) {
+    int64_t blocks = (rows + 31) / 32;
+    if (blocks > ctx->num_sms * 4) blocks = ctx->num_sms * 4;
+    Scratch part(ctx, 2 * blocks * cols * sizeof(float));
+    if (!part.ptr) return TX_ERR_OOM;
+    float *pg = part.as<float>();
+    float *pb = pg + blocks * cols;
+    switch (vpl) {
+      case 1: k_layernorm_bwd_v<1><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, gamma, mean, rstd, dy, dx, pg, pb, rows, acc_dx); break;
+      case 2: k_layernorm_bwd_v<2><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, gamma, mean, rstd, dy, dx, pg, pb, rows, acc_dx); break;
+      case 4: k_layernorm_bwd_v<4><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, gamma, mean, rstd, dy, dx, pg, pb, rows, acc_dx); break;
+      default: k_layernorm_bwd_v<4><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, gamma, mean, rstd, dy, dx, pg, pb, rows, acc_dx); break;
+    }
+    TX_LAUNCHED(ctx, "k_layernorm_bwd_v");
+    if (dgamma) TX_TRY(colsum_finish(ctx, pg, blocks, cols, dgamma, 1.f, acc_p));
+    if (dbeta) TX_TRY(colsum_finish(ctx, pb, blocks, cols, dbeta, 1.f, acc_p));
+    return TX_OK;
+  }
   const int warps = 4;
   size_t smem = 2 * (size_t)warps * cols * sizeof(float);
   if (smem > 200 * 1024) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "LayerNorm width too large");
