@@ -341,6 +341,7 @@ struct tx_graph {
   std::vector<GValue> values;
   std::vector<GNode> nodes;
   std::vector<int> inputs;   // value ids of TX_VAL_INPUT in declaration order
+  std::vector<bool> input_round;  // TF32 mode: input read only by contractions (rounded copy)
   std::vector<int> outputs;  // value ids
   std::vector<int> params;   // value ids in param-index order (declaration order)
   std::vector<int64_t> param_offset;  // offset in flat buffers
@@ -676,6 +677,10 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
       n.round_out = feeds_only_contractions(n.d.out[0], 0);
     }
   }
+  g->input_round.assign(g->inputs.size(), false);
+  for (size_t i = 0; i < g->inputs.size(); ++i)
+    g->input_round[i] = g->values[g->inputs[i]].dtype == TX_DT_F32 &&
+                        feeds_only_contractions(g->inputs[i], 0);
 
   // ---- parameter storage: order = when gradients become final in backward -----------------
   std::vector<int> first_use(g->params.size(), n_nodes);
@@ -1088,7 +1093,26 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
     TX_TRY(tx_round_tf32(ctx, g->flat_values, g->flat_tf32, g->flat_len));
     r->shadow = true;
   }
-  for (size_t i = 0; i < g->inputs.size(); ++i) r->buf[g->inputs[i]] = const_cast<void *>(d_inputs[i]);
+  for (size_t i = 0; i < g->inputs.size(); ++i) {
+    const int v = g->inputs[i];
+    r->buf[v] = const_cast<void *>(d_inputs[i]);
+    if (r->shadow && g->input_round[i] && numel_of(r->shapes[v]) >= (int64_t(1) << 20)) {
+      // an input only contractions read is rounded once here, not in every
+      // GEMM that reads it (the copy lives with the record: backward reads it)
+      const int64_t n = numel_of(r->shapes[v]);
+      void *copy = tx_alloc_raw(ctx, n * 4);
+      int rc = copy ? tx_round_tf32(ctx, (const float *)d_inputs[i], (float *)copy, n) : TX_ERR_OOM;
+      if (copy) {
+        r->buf[v] = copy;
+        r->owned[v] = true;
+        r->tf32[v] = true;
+      }
+      if (rc != TX_OK) {
+        tx_record_free(r.release());
+        return rc;
+      }
+    }
+  }
   for (size_t i = 0; i < nv; ++i)
     if (g->values[i].kind == TX_VAL_PARAM || g->values[i].kind == TX_VAL_CONST) r->buf[i] = g->values[i].dev;
   // outputs are written straight into the caller's buffers, unless an output

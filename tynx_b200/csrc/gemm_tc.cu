@@ -1180,11 +1180,13 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   // (measured: 32768x1024x256 100 -> 70 us, 32768x256x256 33 -> 27 us); one
   // wave gains nothing from it and keeps two interleaved accumulators.
   bool persistent = false;
-  if (mode == 0 && tiling.splits == 1 && d.N > 128) {
-    const int64_t tiles256 = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + 255) / 256) * batch;
-    if (tiles256 > ctx->num_sms) {
+  if (mode == 0 && tiling.splits == 1) {
+    // narrow outputs (batched attention products) need more waves to pay off
+    const int pbn = d.N > 128 ? 256 : d.N > 64 ? 128 : 64;
+    const int64_t tiles = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + pbn - 1) / pbn) * batch;
+    if (tiles > (pbn == 256 ? 1 : 2) * (int64_t)ctx->num_sms) {
       persistent = true;
-      tiling.bn = 256;
+      tiling.bn = pbn;
     }
   }
   const int bn = tiling.bn;

@@ -241,6 +241,86 @@ __global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restri
   }
 }
 
+// Register-resident softmax for rows of VPL * 128 floats: a warp per row,
+// one HBM read of x (and of y, dy in the backward).
+template <int VPL>
+__global__ void k_softmax_fwd_v(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int log_mode) {
+  constexpr int cols = VPL * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows; r += warps) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + r * cols);
+    float4 v[VPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      v[j] = xr[j * 32 + lane];
+      m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+    }
+    m = warp_max(m);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      s += expf(v[j].x - m) + expf(v[j].y - m) + expf(v[j].z - m) + expf(v[j].w - m);
+    s = warp_sum(s);
+    float4 *yr = reinterpret_cast<float4 *>(y + r * cols);
+    if (log_mode) {
+      const float lse = logf(s);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        yr[j * 32 + lane] = make_float4((v[j].x - m) - lse, (v[j].y - m) - lse, (v[j].z - m) - lse, (v[j].w - m) - lse);
+    } else {
+      const float inv = 1.0f / s;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        yr[j * 32 + lane] = make_float4(expf(v[j].x - m) * inv, expf(v[j].y - m) * inv, expf(v[j].z - m) * inv,
+                                        expf(v[j].w - m) * inv);
+    }
+  }
+}
+
+template <int VPL>
+__global__ void k_softmax_bwd_v(const float *__restrict__ y, const float *__restrict__ dy, float *__restrict__ dx,
+                                int64_t rows, int log_mode, int acc) {
+  constexpr int cols = VPL * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows; r += warps) {
+    const float4 *yr = reinterpret_cast<const float4 *>(y + r * cols);
+    const float4 *gr = reinterpret_cast<const float4 *>(dy + r * cols);
+    float4 yv[VPL], gv[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      yv[j] = yr[j * 32 + lane];
+      gv[j] = gr[j * 32 + lane];
+      s += log_mode ? gv[j].x + gv[j].y + gv[j].z + gv[j].w
+                    : gv[j].x * yv[j].x + gv[j].y * yv[j].y + gv[j].z * yv[j].z + gv[j].w * yv[j].w;
+    }
+    s = warp_sum(s);
+    float4 *dr = reinterpret_cast<float4 *>(dx + r * cols);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      float4 o;
+      if (log_mode) {
+        o = make_float4(gv[j].x - expf(yv[j].x) * s, gv[j].y - expf(yv[j].y) * s, gv[j].z - expf(yv[j].z) * s,
+                        gv[j].w - expf(yv[j].w) * s);
+      } else {
+        o = make_float4(yv[j].x * (gv[j].x - s), yv[j].y * (gv[j].y - s), yv[j].z * (gv[j].z - s),
+                        yv[j].w * (gv[j].w - s));
+      }
+      if (acc) {
+        const float4 p = dr[j * 32 + lane];
+        o.x += p.x;
+        o.y += p.y;
+        o.z += p.z;
+        o.w += p.w;
+      }
+      dr[j * 32 + lane] = o;
+    }
+  }
+}
+
 // ---- fused softmax cross-entropy ----------------------------------------------------
 // phase 1: per-row loss = logsumexp(z) - z[y]
 __global__ void k_xent_rows(const float *__restrict__ z, const int64_t *__restrict__ labels,
@@ -977,9 +1057,29 @@ extern "C" int tx_strided_copy(tx_ctx *ctx, const void *src, const int64_t *ss, 
   return nd_copy(ctx, src, ss, dst, shape, ndim, elem_bytes, 1.f, 0);
 }
 
+// rows whose width is a multiple of 128 (up to 1024) on 16-byte aligned buffers
+// take the register-resident float4 kernels
+static bool ln_vec(int64_t cols, std::initializer_list<const void *> ptrs) {
+  if (cols % 128 || cols > 1024) return false;
+  for (const void *p : ptrs)
+    if (((uintptr_t)p) & 15) return false;
+  return true;
+}
+
 extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int log) {
   if (!ctx) return TX_ERR_INVALID;
   if (rows <= 0 || cols <= 0) return TX_OK;
+  if (ln_vec(cols, {x, y}) && (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
+    const unsigned blocks = rows_grid(rows, 8);
+    switch (cols) {
+      case 128: k_softmax_fwd_v<1><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
+      case 256: k_softmax_fwd_v<2><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
+      case 512: k_softmax_fwd_v<4><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
+      default: k_softmax_fwd_v<8><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
+    }
+    TX_LAUNCHED(ctx, "k_softmax_fwd_v");
+    return TX_OK;
+  }
   k_softmax_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, y, rows, cols, log);
   TX_LAUNCHED(ctx, "k_softmax_fwd");
   return TX_OK;
@@ -989,6 +1089,17 @@ extern "C" int tx_softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, floa
                               int64_t cols, int log, int acc) {
   if (!ctx) return TX_ERR_INVALID;
   if (rows <= 0 || cols <= 0) return TX_OK;
+  if (ln_vec(cols, {y, dy, dx}) && (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
+    const unsigned blocks = rows_grid(rows, 8);
+    switch (cols) {
+      case 128: k_softmax_bwd_v<1><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
+      case 256: k_softmax_bwd_v<2><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
+      case 512: k_softmax_bwd_v<4><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
+      default: k_softmax_bwd_v<8><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
+    }
+    TX_LAUNCHED(ctx, "k_softmax_bwd_v");
+    return TX_OK;
+  }
   k_softmax_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(y, dy, dx, rows, cols, log, acc);
   TX_LAUNCHED(ctx, "k_softmax_bwd");
   return TX_OK;
@@ -1062,13 +1173,6 @@ extern "C" int tx_softmax_xent_bwd(tx_ctx *ctx, const float *z, const int64_t *l
   k_xent_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(z, labels, scale, dz, rows, cols, acc);
   TX_LAUNCHED(ctx, "k_xent_bwd");
   return TX_OK;
-}
-
-static bool ln_vec(int64_t cols, std::initializer_list<const void *> ptrs) {
-  if (cols % 128 || cols > 1024) return false;
-  for (const void *p : ptrs)
-    if (((uintptr_t)p) & 15) return false;
-  return true;
 }
 
 int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
