@@ -64,7 +64,7 @@ __device__ __forceinline__ void st4(float *p, float4 v, bool vec, int valid) {
   if (valid > 3) p[3] = v.w;
 }
 
-__device__ __forceinline__ bool vec_ok(const float *p, int64_t ld) {
+__host__ __device__ __forceinline__ bool vec_ok(const float *p, int64_t ld) {
   return p && ((ld & 3) == 0) && ((((uintptr_t)p) & 15) == 0);
 }
 
@@ -218,6 +218,105 @@ __global__ void __launch_bounds__(256) k_gemm_small_k(const tx_gemm_desc d) {
   }
 }
 
+// Aligned fast path (N % 4 == 0, C / act' source / pre-activation 16-byte
+// aligned with leading dimensions that are multiples of 4): the activation pair
+// is a template parameter and every access is a float4, so the unrolled rows
+// carry no alternative code; B is staged once per block and the block walks
+// row tiles, so its instructions are reused instead of fetched once per warp.
+template <int TCOLS, int ACT, int DACT>
+__global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int row_tiles) {
+  constexpr int TPR = TCOLS / 4;
+  constexpr int RG = 256 / TPR;
+  constexpr int ROWS = RG * 8;
+  __shared__ __align__(16) float Bs[SK_KMAX][TCOLS + 4];
+  __shared__ float As[ROWS][SK_KMAX + 1];
+  const int64_t bz = blockIdx.z;
+  const float *A = d.A + bz * d.stride_a;
+  const float *B = d.B + bz * d.stride_b;
+  float *C = d.C + bz * d.stride_c;
+  const float *S = d.dact_src ? d.dact_src + bz * d.stride_c : nullptr;
+  float *P = d.preact ? d.preact + bz * d.stride_c : nullptr;
+  const int64_t n0 = (int64_t)blockIdx.x * TCOLS;
+  const int K = (int)d.K;
+  for (int e = threadIdx.x; e < K * TCOLS; e += 256) {
+    int k, n;
+    if (d.trans_b) { k = e % K; n = e / K; }
+    else { n = e % TCOLS; k = e / TCOLS; }
+    const int64_t gn = n0 + n;
+    Bs[k][n] = gn < d.N ? (d.trans_b ? B[gn * d.ldb + k] : B[(int64_t)k * d.ldb + gn]) : 0.f;
+  }
+  const int cg = threadIdx.x % TPR, rg = threadIdx.x / TPR;
+  const int64_t gn = n0 + cg * 4;
+  const bool col_ok = gn < d.N;  // N % 4 == 0: a group is all in or all out
+  const bool beta = d.beta != 0.f;
+  float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (d.bias && col_ok) {
+    bias = make_float4(d.bias[gn] * d.bias_scale, d.bias[gn + 1] * d.bias_scale, d.bias[gn + 2] * d.bias_scale,
+                       d.bias[gn + 3] * d.bias_scale);
+  }
+  const bool round_out = (d.flags & TX_GEMM_ROUND_OUT) != 0;
+#pragma unroll 1
+  for (int rt = blockIdx.y; rt < row_tiles; rt += gridDim.y) {
+    const int64_t m0 = (int64_t)rt * ROWS;
+    __syncthreads();  // the previous tile's readers of As are done
+    for (int e = threadIdx.x; e < K * ROWS; e += 256) {
+      int k, m;
+      if (d.trans_a) { m = e % ROWS; k = e / ROWS; }
+      else { k = e % K; m = e / K; }
+      const int64_t gm = m0 + m;
+      As[m][k] = gm < d.M ? (d.trans_a ? A[(int64_t)k * d.lda + gm] : A[gm * d.lda + k]) : 0.f;
+    }
+    __syncthreads();
+    // epilogue inputs first: they do not depend on the products
+    float4 cold[8], sv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t gm = m0 + rg + RG * i;
+      const bool ok = col_ok && gm < d.M;
+      cold[i] = (ok && beta) ? *reinterpret_cast<const float4 *>(C + gm * d.ldc + gn) : make_float4(0.f, 0.f, 0.f, 0.f);
+      sv[i] = (ok && DACT != TX_ACT_NONE) ? *reinterpret_cast<const float4 *>(S + gm * d.ld_dact + gn)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const float4 b = *reinterpret_cast<const float4 *>(&Bs[k][cg * 4]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float a = As[rg + RG * i][k];
+        acc[i][0] = fmaf(a, b.x, acc[i][0]);
+        acc[i][1] = fmaf(a, b.y, acc[i][1]);
+        acc[i][2] = fmaf(a, b.z, acc[i][2]);
+        acc[i][3] = fmaf(a, b.w, acc[i][3]);
+      }
+    }
+    if (!col_ok) continue;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t gm = m0 + rg + RG * i;
+      if (gm >= d.M) continue;
+      float o[4];
+      const float bb[4] = {bias.x, bias.y, bias.z, bias.w};
+      const float cc[4] = {cold[i].x, cold[i].y, cold[i].z, cold[i].w};
+      const float ss[4] = {sv[i].x, sv[i].y, sv[i].z, sv[i].w};
+      float pre[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x = d.alpha * acc[i][j];
+        if (d.bias) x += bb[j];
+        if (beta) x += d.beta * cc[j];
+        pre[j] = x;
+        x = tx_epi::act(ACT, x);
+        if (DACT != TX_ACT_NONE) x *= tx_epi::dact(DACT, ss[j]);
+        o[j] = round_out ? tx_epi::round_tf32(x) : x;
+      }
+      if (P) *reinterpret_cast<float4 *>(P + gm * d.ld_preact + gn) = make_float4(pre[0], pre[1], pre[2], pre[3]);
+      *reinterpret_cast<float4 *>(C + gm * d.ldc + gn) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // ---- small N ----------------------------------------------------------------------------
 // Dynamic shared memory: Bs[NN][kc] (op(B) transposed to N x K, zero padded),
 // kc <= SN_KC.  Each lane holds 8 float4 of a row (K chunk <= 1024); the next
@@ -254,26 +353,23 @@ __global__ void __launch_bounds__(256) k_gemm_small_n(const tx_gemm_desc d, int 
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool avec = vec_ok(d.A, d.lda);
-  const int64_t stride = (int64_t)gridDim.x * 8;
-  float4 nxt[8];
-  auto load_row = [&](int64_t m) {
-    const float *arow = d.A + m * d.lda + k0;
+  // two rows per warp: every W float4 read from shared memory feeds both
+  const int64_t stride = (int64_t)gridDim.x * 16;
+  for (int64_t m = ((int64_t)blockIdx.x * 8 + warp) * 2; m < d.M; m += stride) {
+    const bool two = m + 1 < d.M;
+    const float *a0p = d.A + m * d.lda + k0;
+    const float *a1p = a0p + d.lda;
+    float4 a0[8], a1[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int kk = lane * 4 + 128 * j;
-      nxt[j] = kk < klen ? ld4(arow + kk, avec, klen - kk) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool in = kk < klen;
+      a0[j] = in ? ld4(a0p + kk, avec, klen - kk) : make_float4(0.f, 0.f, 0.f, 0.f);
+      a1[j] = (in && two) ? ld4(a1p + kk, avec, klen - kk) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-  };
-  int64_t m = (int64_t)blockIdx.x * 8 + warp;
-  if (m < d.M) load_row(m);
-  for (; m < d.M; m += stride) {
-    float4 a[8];
+    float acc0[NN], acc1[NN];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = nxt[j];
-    if (m + stride < d.M) load_row(m + stride);
-    float acc[NN];
-#pragma unroll
-    for (int n = 0; n < NN; ++n) acc[n] = 0.f;
+    for (int n = 0; n < NN; ++n) acc0[n] = acc1[n] = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int kk = lane * 4 + 128 * j;
@@ -281,35 +377,46 @@ __global__ void __launch_bounds__(256) k_gemm_small_n(const tx_gemm_desc d, int 
 #pragma unroll
         for (int n = 0; n < NN; ++n) {
           const float4 b = *reinterpret_cast<const float4 *>(&bsm[n * kc + kk]);
-          float t = acc[n];
-          t = fmaf(a[j].x, b.x, t);
-          t = fmaf(a[j].y, b.y, t);
-          t = fmaf(a[j].z, b.z, t);
-          t = fmaf(a[j].w, b.w, t);
-          acc[n] = t;
+          float t = acc0[n], u = acc1[n];
+          t = fmaf(a0[j].x, b.x, t);
+          u = fmaf(a1[j].x, b.x, u);
+          t = fmaf(a0[j].y, b.y, t);
+          u = fmaf(a1[j].y, b.y, u);
+          t = fmaf(a0[j].z, b.z, t);
+          u = fmaf(a1[j].z, b.z, u);
+          t = fmaf(a0[j].w, b.w, t);
+          u = fmaf(a1[j].w, b.w, u);
+          acc0[n] = t;
+          acc1[n] = u;
         }
       }
     }
 #pragma unroll
     for (int n = 0; n < NN; ++n) {
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], off);
+      for (int off = 16; off > 0; off >>= 1) {
+        acc0[n] += __shfl_xor_sync(0xffffffffu, acc0[n], off);
+        acc1[n] += __shfl_xor_sync(0xffffffffu, acc1[n], off);
+      }
     }
+    // lanes 0..N-1 finish row m, lanes 16..16+N-1 row m + 1
+    const int col = lane & 15;
+    const int64_t row = m + (lane >> 4);
     float v = 0.f;
 #pragma unroll
     for (int n = 0; n < NN; ++n)
-      if (n == lane) v = acc[n];
-    if (lane >= d.N) continue;
+      if (n == col) v = (lane >> 4) ? acc1[n] : acc0[n];
+    if (col >= d.N || row >= d.M) continue;
     if (part) {
-      part[(int64_t)blockIdx.y * d.M * d.N + m * d.N + lane] = v;
+      part[(int64_t)blockIdx.y * d.M * d.N + row * d.N + col] = v;
       continue;
     }
-    const float bias_v = d.bias ? d.bias[lane] * d.bias_scale : 0.f;
-    const float c_old = d.beta != 0.f ? d.C[m * d.ldc + lane] : 0.f;
-    const float s = d.dact ? d.dact_src[m * d.ld_dact + lane] : 0.f;
-    const EpiVals r = finish(d, v, bias_v, c_old, s);
-    if (d.preact) d.preact[m * d.ld_preact + lane] = r.pre;
-    d.C[m * d.ldc + lane] = r.out;
+    const float bias_v = d.bias ? d.bias[col] * d.bias_scale : 0.f;
+    const float c_old = d.beta != 0.f ? d.C[row * d.ldc + col] : 0.f;
+    const float sv = d.dact ? d.dact_src[row * d.ld_dact + col] : 0.f;
+    const EpiVals r = finish(d, v, bias_v, c_old, sv);
+    if (d.preact) d.preact[row * d.ld_preact + col] = r.pre;
+    d.C[row * d.ldc + col] = r.out;
   }
 }
 
@@ -403,10 +510,9 @@ int launch_small_n(tx_ctx *ctx, const tx_gemm_desc &d) {
     TX_CUDA(ctx, cudaFuncSetAttribute(k_gemm_small_n<NN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
     configured[ctx->device & 63] = true;
   }
-  // one block per SM (registers allow one): each stages op(B) once and walks
-  // many rows with the next row's loads in flight
-  int64_t rows_blocks = (d.M + 7) / 8;
-  int64_t cap = (int64_t)ctx->num_sms / splits;
+  // two blocks per SM: each stages op(B) once and walks many row pairs
+  int64_t rows_blocks = (d.M + 15) / 16;
+  int64_t cap = 2 * (int64_t)ctx->num_sms / splits;
   if (cap < 1) cap = 1;
   if (rows_blocks > cap) rows_blocks = cap;
   dim3 grid((unsigned)rows_blocks, (unsigned)splits);
@@ -452,9 +558,53 @@ int launch_small_m(tx_ctx *ctx, const tx_gemm_desc &d) {
   return gemm_split_reduce(ctx, d, part.as<float>(), (int)splits);
 }
 
+template <int TCOLS, int ACT, int DACT>
+int launch_small_k2(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
+  constexpr int ROWS = (256 / (TCOLS / 4)) * 8;
+  const int64_t col_tiles = (d.N + TCOLS - 1) / TCOLS, row_tiles = (d.M + ROWS - 1) / ROWS;
+  int64_t gy = 3 * (int64_t)ctx->num_sms / (col_tiles * batch);
+  if (gy < 1) gy = 1;
+  if (gy > row_tiles) gy = row_tiles;
+  if (col_tiles > 0x7fffffff || gy > 65535 || row_tiles > 0x7fffffff) return TX_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)col_tiles, (unsigned)gy, (unsigned)batch);
+  k_gemm_small_k2<TCOLS, ACT, DACT><<<grid, 256, 0, ctx->stream>>>(d, (int)row_tiles);
+  TX_LAUNCHED(ctx, "k_gemm_small_k2");
+  return TX_OK;
+}
+
+template <int TCOLS>
+int launch_small_k2_act(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
+  if (!d.dact) {
+    switch (d.act) {
+      case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_RELU, TX_ACT_NONE>(ctx, d, batch);
+      case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_TANH, TX_ACT_NONE>(ctx, d, batch);
+      case TX_ACT_GELU: return launch_small_k2<TCOLS, TX_ACT_GELU, TX_ACT_NONE>(ctx, d, batch);
+      default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_NONE>(ctx, d, batch);
+    }
+  }
+  if (d.act != TX_ACT_NONE) return TX_ERR_UNSUPPORTED;
+  switch (d.dact) {
+    case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_RELU>(ctx, d, batch);
+    case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_TANH>(ctx, d, batch);
+    default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_GELU>(ctx, d, batch);
+  }
+}
+
+bool small_k2_ok(const tx_gemm_desc &d, int64_t batch) {
+  if (d.N % 4 || !vec_ok(d.C, d.ldc)) return false;
+  if (d.dact && !vec_ok(d.dact_src, d.ld_dact)) return false;
+  if (d.preact && !vec_ok(d.preact, d.ld_preact)) return false;
+  if (batch > 1 && (d.stride_c % 4)) return false;
+  return true;
+}
+
 template <int TCOLS>
 int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
   constexpr int ROWS = (256 / (TCOLS / 4)) * 8;
+  if (small_k2_ok(d, batch)) {
+    const int rc = launch_small_k2_act<TCOLS>(ctx, d, batch);
+    if (rc != TX_ERR_UNSUPPORTED) return rc;
+  }
   dim3 grid((unsigned)((d.N + TCOLS - 1) / TCOLS), (unsigned)((d.M + ROWS - 1) / ROWS), (unsigned)batch);
   if ((d.N + TCOLS - 1) / TCOLS > 0x7fffffff || (d.M + ROWS - 1) / ROWS > 65535)
     return TX_ERR_UNSUPPORTED;
@@ -481,6 +631,7 @@ int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d) {
     if (d.N <= 2) return launch_small_n<2>(ctx, d);
     if (d.N <= 4) return launch_small_n<4>(ctx, d);
     if (d.N <= 8) return launch_small_n<8>(ctx, d);
+    if (d.N <= 10) return launch_small_n<10>(ctx, d);
     return launch_small_n<16>(ctx, d);
   }
   if (d.M <= 16 && !d.trans_b && d.N >= 64) {
