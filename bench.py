@@ -222,8 +222,6 @@ def main() -> None:
 
     tx.set_math_mode(args.math)
     wl = workloads.WORKLOADS[args.workload]()
-    if wl.loss != "cross_entropy":
-        raise SystemExit("bench.py times the cross-entropy workloads")
     per_rank = wl.batch // world
     rows = shard(wl.batch, world, rank)
     ctx = _core.context()
@@ -232,21 +230,60 @@ def main() -> None:
     if world > 1:
         init_data_parallel(world, rank)
         model.enable_data_parallel(bucket_mb=args.bucket_mb)
-    key = "ids" if args.workload == "transformer" else "x"
-    xdtype = "int64" if key == "ids" else "float32"
 
-    @tx.compile(fullgraph=True)
-    def train_step(x, y):
-        opt.zero_grad()
-        loss = tx.nn.functional.cross_entropy(model(x), y)
-        loss.backward()
-        opt.step()
-        return loss
+    if wl.loss == "ppo":
+        # the captured PPO minibatch update: clipped surrogate + 0.5 value MSE
+        # - 0.01 entropy; behaviour log-probs come from the initial policy
+        with tx.no_grad():
+            obs_all = wl.notes["rollout_obs"]
+            logits = model(tx.Tensor(obs_all))["logits"]
+        from tynx_b200.distributions import Categorical
+
+        dtypes = ("float32", "int64", "float32", "float32", "float32")
+        # log-probs of every rollout action under the initial policy
+        all_actions = np.empty(obs_all.shape[0], np.int64)
+        for j in range(obs_all.shape[0] // wl.batch):
+            b = wl.make_batch(j)
+            all_actions[b["index"]] = b["actions"]
+        with tx.no_grad():
+            old_all = Categorical(logits=logits).log_prob(tx.Tensor(all_actions, dtype="int64")).numpy()
+
+        def host_inputs(i):
+            b = wl.make_batch(i)
+            return (b["obs"], b["actions"], old_all[b["index"]], b["advantages"], b["returns"])
+
+        @tx.compile(fullgraph=True)
+        def train_step(obs, actions, old_logp, adv, ret):
+            opt.zero_grad()
+            out = model(obs)
+            policy = Categorical(logits=out["logits"])
+            ratio = (policy.log_prob(actions) - old_logp).exp()
+            policy_loss = -tx.minimum(ratio * adv, ratio.clamp(0.8, 1.2) * adv).mean()
+            value_loss = tx.nn.functional.mse_loss(out["value"].squeeze(1), ret)
+            loss = policy_loss + value_loss * 0.5 - policy.entropy().mean() * 0.01
+            loss.backward()
+            opt.step()
+            return loss
+    else:
+        key = "ids" if args.workload == "transformer" else "x"
+        dtypes = ("int64" if key == "ids" else "float32", "int64")
+
+        def host_inputs(i):
+            b = wl.make_batch(i)
+            return (b[key], b["y"])
+
+        @tx.compile(fullgraph=True)
+        def train_step(x, y):
+            opt.zero_grad()
+            loss = tx.nn.functional.cross_entropy(model(x), y)
+            loss.backward()
+            opt.step()
+            return loss
 
     # device-resident batches (one per step) for the kernel-time measurement
     n_batches = args.warmup + args.steps
-    host = [wl.make_batch(i) for i in range(n_batches)]
-    dev = [(tx.Tensor(b[key][rows], dtype=xdtype), tx.Tensor(b["y"][rows])) for b in host]
+    host = [host_inputs(i) for i in range(n_batches)]
+    dev = [tuple(tx.Tensor(a[rows], dtype=dt) for a, dt in zip(h, dtypes)) for h in host]
     flush = tx.zeros(128 << 20)  # 512 MiB
 
     stream = ctypes_stream(ctx)
@@ -292,22 +329,20 @@ def main() -> None:
     roofline = gemm_roofline(tx, ctx, ext, wl, per_rank, args.math)
 
     # ---- end to end through the public API with host buffers -------------------------
-    pin_x = [_core.pinned(b[key][rows]) for b in host[args.warmup:]]
-    pin_y = [_core.pinned(b["y"][rows]) for b in host[args.warmup:]]
+    pinned = [tuple(_core.pinned(np.ascontiguousarray(a[rows])) for a in h) for h in host[args.warmup:]]
     barrier()
     t0 = time.perf_counter()
     losses = []
     for i in range(args.steps):
-        x = tx.Tensor(pin_x[i], dtype=xdtype)
-        y = tx.Tensor(pin_y[i])
-        losses.append(train_step(x, y).item())
+        inputs = [tx.Tensor(a, dtype=dt) for a, dt in zip(pinned[i], dtypes)]
+        losses.append(train_step(*inputs).item())
     barrier()
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    h2d = pin_x[0].nbytes + pin_y[0].nbytes
+    h2d = sum(a.nbytes for a in pinned[0])
     e2e = {"value": wl.batch * args.steps / e2e_s, "unit": "samples/s",
            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4}
 
@@ -369,6 +404,8 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
         M, N_, K = per_rank, hidden, hidden
     elif wl.name == "transformer":
         M, N_, K = per_rank * 128, 1024, 256
+    elif wl.name == "ppo":
+        M, N_, K = per_rank, 512, 512
     else:
         M, N_, K = per_rank * 256, 64, 288
     from tynx_b200 import _native as N
@@ -420,9 +457,18 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
     else:
         peak = peaks["bf16_tflops"] / 2.0
         note = f"dense TF32 = 1/2 of {source} bf16 burst ({peaks['bf16_tflops']} TF/s)"
+    # DRAM bytes per launch of this kernel from an ncu capture of the same
+    # command (dram__bytes_read.sum + dram__bytes_write.sum), where one exists
+    traffic = None
+    tpath = ROOT / "profiles" / "roofline_traffic.json"
+    if tpath.exists() and math == "tf32":
+        entry = json.loads(tpath.read_text()).get(wl.name)
+        if entry and per_rank == wl.batch:
+            traffic = entry["traffic_bytes"]
     return {"bound": "tensor", "kernel": f"gemm {M}x{N_}x{K} +bias+relu ({math})",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": None, "duration_us": ms * 1e3, "peak_source": note}
+            "traffic": traffic, "traffic_unit": "bytes/launch", "duration_us": ms * 1e3,
+            "peak_source": note}
 
 
 if __name__ == "__main__":
