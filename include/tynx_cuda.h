@@ -143,6 +143,11 @@ typedef struct tx_gemm_desc {
   const float *dact_src; int64_t ld_dact; int32_t dact;
   int64_t batch; int64_t stride_a, stride_b, stride_c; /* strided batch (batch<=1: single) */
   int32_t flags;                               /* TX_GEMM_* below; 0 = none */
+  /* optional fused column sum (the bias gradient of the layer whose
+   * pre-activation gradient this product is): colsum[n] (+)= colsum_scale *
+   * sum over rows of C[:, n], taken before any TF32 output rounding;
+   * colsum_acc != 0 adds to colsum.  batch must be 1. */
+  float *colsum; float colsum_scale; int32_t colsum_acc;
 } tx_gemm_desc;
 /* flags: in TX_MATH_TF32 (round-to-nearest) mode the contraction rounds each
  * operand element to TF32 (cvt.rna).  An operand whose buffer already holds

@@ -235,6 +235,53 @@ def test_pre_rounded_operands_and_rounded_output(tx, ta, tb):
     np.testing.assert_array_equal(rounded.view(np.uint32), _np_round_tf32(base).view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K,ta,tb,dact", [
+    (4096, 1024, 1024, 0, 0, "relu"),   # tcgen05 dgrad with act' (TMA epilogue sums)
+    (4096, 1024, 10, 0, 0, "relu"),     # small-K head dgrad (block sums)
+    (300, 256, 16, 1, 1, "tanh"),       # small-K, MN-major A, ragged rows
+    (4096, 10, 1024, 0, 1, None),       # small-N: no fused sums, summed afterwards
+    (1000, 384, 200, 0, 1, "gelu"),     # tcgen05 with a ragged last tile
+])
+@pytest.mark.parametrize("acc", [0, 1])
+def test_fused_column_sums(tx, M, N, K, ta, tb, dact, acc):
+    """colsum (+)= scale * sum over rows of the unrounded result; C is stored
+    either exactly or TF32-rounded (when the kernel fused the sums)."""
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N_
+
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    S = rng.standard_normal((M, N)).astype(np.float32) * 0.5
+    prior = rng.standard_normal(N).astype(np.float32)
+    ctx = _core.context()
+    ctx.math = "tf32"
+    a, b, s = tx.Tensor(A), tx.Tensor(B), tx.Tensor(S)
+
+    def run(colsum, flags):
+        c = tx.zeros(M, N)
+        d = N_.GemmDesc()
+        d.M, d.N, d.K = M, N, K
+        d.A, d.lda, d.trans_a = a.ptr, A.shape[1], ta
+        d.B, d.ldb, d.trans_b = b.ptr, B.shape[1], tb
+        d.C, d.ldc = c.ptr, N
+        d.alpha, d.batch, d.flags = 1.0, 1, flags
+        if dact:
+            d.dact_src, d.ld_dact, d.dact = s.ptr, N, N_.ACT[dact]
+        if colsum is not None:
+            d.colsum, d.colsum_scale, d.colsum_acc = colsum.ptr, 0.5, acc
+        ctx.check(N_.lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
+        return c.numpy()
+
+    ref = run(None, 0)
+    cs = tx.Tensor(prior)
+    got = run(cs, N_.TX_GEMM_ROUND_OUT)
+    want = 0.5 * ref.astype(np.float64).sum(axis=0) + (prior if acc else 0)
+    scale = float(np.abs(ref).sum(axis=0).max())
+    assert float(np.abs(cs.numpy() - want).max()) <= 1e-5 * scale
+    assert (got == ref).all() or (got.view(np.uint32) == _np_round_tf32(ref).view(np.uint32)).all()
+
+
 def _strides(shape):
     st, acc = [], 1
     for e in reversed(shape):

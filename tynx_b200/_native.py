@@ -68,6 +68,7 @@ class GemmDesc(C.Structure):
         ("dact_src", C.c_void_p), ("ld_dact", C.c_int64), ("dact", C.c_int32),
         ("batch", C.c_int64), ("stride_a", C.c_int64), ("stride_b", C.c_int64),
         ("stride_c", C.c_int64), ("flags", C.c_int32),
+        ("colsum", C.c_void_p), ("colsum_scale", C.c_float), ("colsum_acc", C.c_int32),
     ]
 
 

@@ -95,14 +95,27 @@ struct Scratch {
 };
 
 // ---- GEMM internals -----------------------------------------------------------
+// Fused column sums (tx_gemm_desc::colsum).  gemm_dispatch provides a partial
+// buffer of ceil(M / 32) x N floats; a kernel path that can fuse the sums
+// writes `rows` partial rows of unrounded column sums and sets fused.  A path
+// that cannot fuse stores C unrounded (it ignores TX_GEMM_ROUND_OUT) and the
+// dispatcher sums C afterwards.
+struct FusedSum {
+  float *part = nullptr;
+  int64_t rows = 0;
+  bool fused = false;
+};
+
 int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d);
+int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out, float scale, int acc);
 // Returns TX_ERR_UNSUPPORTED (without latching) when the shape/layout cannot use
 // the tensor-core path; the dispatcher then uses the SIMT kernel.
-int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode);
-int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d);
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode, FusedSum *fs = nullptr);
+// `rounded` (optional) tells whether C was stored TF32-rounded.
+int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d, bool *rounded = nullptr);
 // Bandwidth-shaped kernels for K <= 32, N <= 16 or M <= 16; TX_ERR_UNSUPPORTED
 // (not latched) for every other shape.
-int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d);
+int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d, FusedSum *fs = nullptr);
 int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits);
 
 // N-d bandwidth kernels on canonicalised shapes (nd.cu).  Strides in elements,

@@ -1170,6 +1170,8 @@ struct Bwd {
   std::vector<float *> grad;       // per value gradient buffer
   std::vector<bool> grad_owned;
   std::vector<bool> grad_preact;   // gradient already multiplied by act' (fused dgrad)
+  std::vector<bool> grad_tf32;     // gradient buffer holds TF32-rounded values
+  std::vector<bool> bias_fused;    // per node: bias gradient already summed by a dgrad epilogue
   std::vector<bool> needs;         // value needs a gradient
   std::vector<float *> param_tmp;  // unused
   // DP bucketing
@@ -1255,12 +1257,13 @@ struct Bwd {
     }
     const Shape &a = S(d.in[0]), &b = S(d.in[1]);
     int rc = TX_OK;
+    const bool dz32 = dz == dy && grad_tf32[yv];  // dZ came TF32-rounded from a fused dgrad
     if (d.op == TX_OP_GEMM) {
       int ta = (int)d.iattr[0], tb = (int)d.iattr[1];
       int64_t M = ta ? a[1] : a[0], K = ta ? a[0] : a[1], N = tb ? b[0] : b[1];
       float alpha = (float)d.fattr[0];
-      // bias
-      if (rc == TX_OK && d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
+      // bias (unless the dgrad that produced dZ already summed it)
+      if (rc == TX_OK && d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]] && !bias_fused[ni]) {
         float *t; int acc;
         rc = target(d.in[2], &t, &acc);
         if (rc == TX_OK) rc = tx_bias_grad(ctx, dz, t, M, N, (float)d.fattr[1], acc);
@@ -1279,13 +1282,13 @@ struct Bwd {
           q.A = x; q.lda = a[1]; q.trans_a = ta ? 0 : 1;
           q.B = dz; q.ldb = N; q.trans_b = 0;
           q.C = t; q.ldc = N;
-          q.flags = x32 ? TX_GEMM_A_TF32 : 0;
+          q.flags = (x32 ? TX_GEMM_A_TF32 : 0) | (dz32 ? TX_GEMM_B_TF32 : 0);
         } else {    // dB[N,K] = dY^T op(A)
           q.M = N; q.N = K; q.K = M;
           q.A = dz; q.lda = N; q.trans_a = 1;
           q.B = x; q.ldb = a[1]; q.trans_b = ta ? 1 : 0;
           q.C = t; q.ldc = K;
-          q.flags = x32 ? TX_GEMM_B_TF32 : 0;
+          q.flags = (x32 ? TX_GEMM_B_TF32 : 0) | (dz32 ? TX_GEMM_A_TF32 : 0);
         }
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
         if (rc == TX_OK) wrote(d.in[1]);
@@ -1293,6 +1296,7 @@ struct Bwd {
       // dA
       if (rc == TX_OK && needs[d.in[0]]) {
         float *t; int acc;
+        int fused_node = -1;
         rc = dgrad_target(d.in[0], &t, &acc);
         tx_gemm_desc q; memset(&q, 0, sizeof q);
         q.alpha = alpha; q.beta = acc ? 1.f : 0.f; q.batch = 1;
@@ -1303,17 +1307,21 @@ struct Bwd {
           q.A = dz; q.lda = N; q.trans_a = 0;
           q.B = w; q.ldb = b[1]; q.trans_b = tb ? 0 : 1;
           q.C = t; q.ldc = K;
-          q.flags = w32 ? TX_GEMM_B_TF32 : 0;
-          fuse_dact(d.in[0], q);
+          q.flags = (w32 ? TX_GEMM_B_TF32 : 0) | (dz32 ? TX_GEMM_A_TF32 : 0);
+          fused_node = fuse_dact(d.in[0], q);
         } else {    // dA[K,M] = op(B) dY^T
           q.M = K; q.N = M; q.K = N;
           q.A = w; q.lda = b[1]; q.trans_a = tb ? 1 : 0;
           q.B = dz; q.ldb = N; q.trans_b = 1;
           q.C = t; q.ldc = M;
-          q.flags = w32 ? TX_GEMM_A_TF32 : 0;
+          q.flags = (w32 ? TX_GEMM_A_TF32 : 0) | (dz32 ? TX_GEMM_B_TF32 : 0);
         }
-        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
-        if (rc == TX_OK) wrote(d.in[0]);
+        bool rounded = false;
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
+        if (rc == TX_OK) {
+          fused_done(d.in[0], fused_node, rounded);
+          wrote(d.in[0]);
+        }
       }
     } else {  // MATMUL
       int64_t K = a.back(), N = b.back();
@@ -1328,7 +1336,7 @@ struct Bwd {
         q.M = K; q.N = N; q.K = M;
         bool x32 = false;
         q.A = gemm_operand(g, r, d.in[0], &x32); q.lda = K; q.trans_a = 1; q.stride_a = M * K;
-        q.flags = x32 ? TX_GEMM_A_TF32 : 0;
+        q.flags = (x32 ? TX_GEMM_A_TF32 : 0) | (dz32 ? TX_GEMM_B_TF32 : 0);
         q.B = dz; q.ldb = N; q.trans_b = 0; q.stride_b = M * N;
         q.C = t; q.ldc = N; q.stride_c = K * N;
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
@@ -1343,12 +1351,16 @@ struct Bwd {
         q.A = dz; q.lda = N; q.trans_a = 0; q.stride_a = M * N;
         bool w32 = false;
         q.B = gemm_operand(g, r, d.in[1], &w32); q.ldb = N; q.trans_b = 1; q.stride_b = weight2d ? 0 : K * N;
-        q.flags = w32 ? TX_GEMM_B_TF32 : 0;
+        q.flags = (w32 ? TX_GEMM_B_TF32 : 0) | (dz32 ? TX_GEMM_A_TF32 : 0);
         q.C = t; q.ldc = K; q.stride_c = M * K;
         if (weight2d) { q.M = M; q.batch = 1; }
-        fuse_dact(d.in[0], q);
-        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
-        if (rc == TX_OK) wrote(d.in[0]);
+        const int fused_node = fuse_dact(d.in[0], q);
+        bool rounded = false;
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
+        if (rc == TX_OK) {
+          fused_done(d.in[0], fused_node, rounded);
+          wrote(d.in[0]);
+        }
       }
     }
     if (dz_tmp) tx_free_raw(ctx, dz_tmp);
@@ -1358,18 +1370,48 @@ struct Bwd {
   int dgrad_target(int v, float **t, int *acc) { return target(v, t, acc); }
 
   // If v is the (sole-consumer) output of a fused Gemm+act, fold act' into this
-  // dgrad epilogue so the producer receives its pre-activation gradient.
-  void fuse_dact(int v, tx_gemm_desc &q) {
+  // dgrad epilogue so the producer receives its pre-activation gradient dZ.
+  // When the producer is a Gemm whose bias needs a gradient, the same epilogue
+  // also sums dZ's columns into it (the returned node's bias is then done);
+  // and since the producer's backward reads dZ only as a contraction operand,
+  // dZ is stored TF32-rounded in TF32 mode.  Returns the producer node whose
+  // bias gradient was fused, or -1.
+  int fuse_dact(int v, tx_gemm_desc &q) {
     const GValue &gv = g->values[v];
-    if (gv.kind != TX_VAL_ACT || gv.producer < 0 || gv.is_output) return;
+    if (gv.kind != TX_VAL_ACT || gv.producer < 0 || gv.is_output) return -1;
     const GNode &p = g->nodes[gv.producer];
-    if (p.fused_into < 0 || gv.consumers.size() != 1 || q.beta != 0.f) return;
-    const GNode &prod = g->nodes[p.fused_into];
-    if (prod.fused_out != v) return;
+    if (p.fused_into < 0 || gv.consumers.size() != 1 || q.beta != 0.f) return -1;
+    const int pi = p.fused_into;
+    const GNode &prod = g->nodes[pi];
+    if (prod.fused_out != v) return -1;
     q.dact = prod.fused_act;
-    q.dact_src = prod.fused_act == TX_ACT_GELU ? (const float *)r->extra[p.fused_into] : F(v);
+    q.dact_src = prod.fused_act == TX_ACT_GELU ? (const float *)r->extra[pi] : F(v);
     q.ld_dact = q.N;
     grad_preact[v] = true;
+    if (prod.d.op != TX_OP_GEMM && prod.d.op != TX_OP_MATMUL) return -1;
+    const bool has_bias = prod.d.op == TX_OP_GEMM && prod.d.n_in > 2 && prod.d.in[2] >= 0;
+    int fused = -1;
+    if (has_bias && needs[prod.d.in[2]] && q.batch <= 1) {
+      float *t; int acc;
+      if (target(prod.d.in[2], &t, &acc) == TX_OK) {
+        q.colsum = t;
+        q.colsum_scale = (float)prod.d.fattr[1];
+        q.colsum_acc = acc;
+        fused = pi;
+      }
+    }
+    if (ctx->math == TX_MATH_TF32 && (fused >= 0 || !has_bias || !needs[prod.d.in[2]]))
+      q.flags |= TX_GEMM_ROUND_OUT;
+    return fused;
+  }
+
+  // after a dgrad launched with fuse_dact: record what it produced
+  void fused_done(int v, int fused_node, bool rounded) {
+    grad_tf32[v] = rounded;
+    if (fused_node >= 0) {
+      bias_fused[fused_node] = true;
+      wrote(g->nodes[fused_node].d.in[2]);
+    }
   }
 
   int conv_backward(int ni) {
@@ -1694,6 +1736,8 @@ extern "C" int tx_graph_backward(tx_graph *g, tx_record *r, const float *const *
   b.grad.assign(nv, nullptr);
   b.grad_owned.assign(nv, false);
   b.grad_preact.assign(nv, false);
+  b.grad_tf32.assign(nv, false);
+  b.bias_fused.assign(g->nodes.size(), false);
   b.needs.assign(nv, false);
   b.param_done.assign(g->params.size(), false);
   b.param_pending.assign(g->params.size(), 0);

@@ -46,4 +46,22 @@ __device__ __forceinline__ float round_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// Column sums of a 32 x 32 chunk held one row per lane (v[j] = column j):
+// a reduce-scatter in five shuffle rounds (16 + 8 + 4 + 2 + 1 exchanges),
+// after which lane l holds the sum of column l over the 32 rows.  The order of
+// the additions is fixed, so the result is deterministic.
+__device__ __forceinline__ float colsum32(float (&w)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? w[i] : w[i + o];
+      const float keep = up ? w[i + o] : w[i];
+      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return w[0];
+}
+
 }  // namespace tx_epi

@@ -309,18 +309,42 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
   return TX_OK;
 }
 
-int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc) {
-  if (desc.M <= 0 || desc.N <= 0) return TX_OK;
+int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc, bool *rounded) {
+  if (rounded) *rounded = false;
   tx_gemm_desc d = desc;
   if (ctx->math != TX_MATH_TF32) d.flags = 0;  // TF32 operand / output rounding only applies there
-  const int skinny = gemm_skinny(ctx, d);
-  if (skinny != TX_ERR_UNSUPPORTED) return skinny;
-  if (ctx->math != TX_MATH_FP32) {
-    const int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
-    int rc = gemm_tcgen05(ctx, d, mode);
-    if (rc != TX_ERR_UNSUPPORTED) return rc;
+  if (d.M <= 0 || d.N <= 0) {
+    if (d.colsum && d.N > 0 && !d.colsum_acc)
+      TX_CUDA(ctx, cudaMemsetAsync(d.colsum, 0, d.N * sizeof(float), ctx->stream));
+    return TX_OK;
   }
-  return gemm_simt(ctx, d);
+  const bool want = d.colsum != nullptr;
+  if (want && (d.batch > 1 || d.ldc != d.N))
+    return tx_fail(ctx, TX_ERR_UNSUPPORTED, "fused column sums need batch 1 and ldc == N");
+  Scratch part(ctx, want ? (size_t)((d.M + 31) / 32) * d.N * sizeof(float) : 0);
+  if (want && !part.ptr) return TX_ERR_OOM;
+  FusedSum fs;
+  fs.part = part.as<float>();
+  FusedSum *pfs = want ? &fs : nullptr;
+  int rc = gemm_skinny(ctx, d, pfs);
+  if (rc == TX_ERR_UNSUPPORTED && ctx->math != TX_MATH_FP32) {
+    const int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
+    rc = gemm_tcgen05(ctx, d, mode, pfs);
+  }
+  if (rc == TX_ERR_UNSUPPORTED) {
+    tx_gemm_desc q = d;
+    if (want) q.flags &= ~TX_GEMM_ROUND_OUT;
+    rc = gemm_simt(ctx, q);
+  }
+  if (rc != TX_OK) return rc;
+  if (want) {
+    if (fs.fused)
+      TX_TRY(colsum_finish(ctx, fs.part, fs.rows, d.N, d.colsum, d.colsum_scale, d.colsum_acc));
+    else
+      TX_TRY(tx_bias_grad(ctx, d.C, d.colsum, d.M, d.N, d.colsum_scale, d.colsum_acc));
+  }
+  if (rounded) *rounded = (d.flags & TX_GEMM_ROUND_OUT) && (!want || fs.fused);
+  return TX_OK;
 }
 
 extern "C" int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc) {

@@ -224,12 +224,13 @@ __global__ void __launch_bounds__(256) k_gemm_small_k(const tx_gemm_desc d) {
 // carry no alternative code; B is staged once per block and the block walks
 // row tiles, so its instructions are reused instead of fetched once per warp.
 template <int TCOLS, int ACT, int DACT>
-__global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int row_tiles) {
+__global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int row_tiles, float *col_part) {
   constexpr int TPR = TCOLS / 4;
   constexpr int RG = 256 / TPR;
   constexpr int ROWS = RG * 8;
   __shared__ __align__(16) float Bs[SK_KMAX][TCOLS + 4];
   __shared__ float As[ROWS][SK_KMAX + 1];
+  __shared__ float red[RG][TCOLS];  // fused column sums: one row per row group
   const int64_t bz = blockIdx.z;
   const float *A = d.A + bz * d.stride_a;
   const float *B = d.B + bz * d.stride_b;
@@ -291,11 +292,11 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
         acc[i][3] = fmaf(a, b.w, acc[i][3]);
       }
     }
-    if (!col_ok) continue;
+    float csum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t gm = m0 + rg + RG * i;
-      if (gm >= d.M) continue;
+      if (!col_ok || gm >= d.M) continue;
       float o[4];
       const float bb[4] = {bias.x, bias.y, bias.z, bias.w};
       const float cc[4] = {cold[i].x, cold[i].y, cold[i].z, cold[i].w};
@@ -309,10 +310,26 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
         pre[j] = x;
         x = tx_epi::act(ACT, x);
         if (DACT != TX_ACT_NONE) x *= tx_epi::dact(DACT, ss[j]);
+        csum[j] += x;
         o[j] = round_out ? tx_epi::round_tf32(x) : x;
       }
       if (P) *reinterpret_cast<float4 *>(P + gm * d.ld_preact + gn) = make_float4(pre[0], pre[1], pre[2], pre[3]);
       *reinterpret_cast<float4 *>(C + gm * d.ldc + gn) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    if (col_part) {
+      // this tile's column sums: the row groups combined in a fixed order
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[rg][cg * 4 + j] = csum[j];
+      __syncthreads();
+      if (rg == 0 && col_ok) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float t = red[0][cg * 4 + j];
+#pragma unroll
+          for (int g = 1; g < RG; ++g) t += red[g][cg * 4 + j];
+          col_part[(int64_t)rt * d.N + gn + j] = t;
+        }
+      }
     }
   }
 }
@@ -559,7 +576,7 @@ int launch_small_m(tx_ctx *ctx, const tx_gemm_desc &d) {
 }
 
 template <int TCOLS, int ACT, int DACT>
-int launch_small_k2(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
+int launch_small_k2(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch, FusedSum *fs) {
   constexpr int ROWS = (256 / (TCOLS / 4)) * 8;
   const int64_t col_tiles = (d.N + TCOLS - 1) / TCOLS, row_tiles = (d.M + ROWS - 1) / ROWS;
   int64_t gy = 3 * (int64_t)ctx->num_sms / (col_tiles * batch);
@@ -567,26 +584,32 @@ int launch_small_k2(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
   if (gy > row_tiles) gy = row_tiles;
   if (col_tiles > 0x7fffffff || gy > 65535 || row_tiles > 0x7fffffff) return TX_ERR_UNSUPPORTED;
   dim3 grid((unsigned)col_tiles, (unsigned)gy, (unsigned)batch);
-  k_gemm_small_k2<TCOLS, ACT, DACT><<<grid, 256, 0, ctx->stream>>>(d, (int)row_tiles);
+  float *col_part = nullptr;
+  if (fs && batch == 1) {
+    col_part = fs->part;  // row_tiles <= ceil(M / 32) partial rows
+    fs->rows = row_tiles;
+    fs->fused = true;
+  }
+  k_gemm_small_k2<TCOLS, ACT, DACT><<<grid, 256, 0, ctx->stream>>>(d, (int)row_tiles, col_part);
   TX_LAUNCHED(ctx, "k_gemm_small_k2");
   return TX_OK;
 }
 
 template <int TCOLS>
-int launch_small_k2_act(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
+int launch_small_k2_act(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch, FusedSum *fs) {
   if (!d.dact) {
     switch (d.act) {
-      case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_RELU, TX_ACT_NONE>(ctx, d, batch);
-      case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_TANH, TX_ACT_NONE>(ctx, d, batch);
-      case TX_ACT_GELU: return launch_small_k2<TCOLS, TX_ACT_GELU, TX_ACT_NONE>(ctx, d, batch);
-      default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_NONE>(ctx, d, batch);
+      case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_RELU, TX_ACT_NONE>(ctx, d, batch, fs);
+      case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_TANH, TX_ACT_NONE>(ctx, d, batch, fs);
+      case TX_ACT_GELU: return launch_small_k2<TCOLS, TX_ACT_GELU, TX_ACT_NONE>(ctx, d, batch, fs);
+      default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_NONE>(ctx, d, batch, fs);
     }
   }
   if (d.act != TX_ACT_NONE) return TX_ERR_UNSUPPORTED;
   switch (d.dact) {
-    case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_RELU>(ctx, d, batch);
-    case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_TANH>(ctx, d, batch);
-    default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_GELU>(ctx, d, batch);
+    case TX_ACT_RELU: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_RELU>(ctx, d, batch, fs);
+    case TX_ACT_TANH: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_TANH>(ctx, d, batch, fs);
+    default: return launch_small_k2<TCOLS, TX_ACT_NONE, TX_ACT_GELU>(ctx, d, batch, fs);
   }
 }
 
@@ -599,12 +622,14 @@ bool small_k2_ok(const tx_gemm_desc &d, int64_t batch) {
 }
 
 template <int TCOLS>
-int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
+int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &desc, int64_t batch, FusedSum *fs) {
   constexpr int ROWS = (256 / (TCOLS / 4)) * 8;
-  if (small_k2_ok(d, batch)) {
-    const int rc = launch_small_k2_act<TCOLS>(ctx, d, batch);
+  if (small_k2_ok(desc, batch)) {
+    const int rc = launch_small_k2_act<TCOLS>(ctx, desc, batch, fs);
     if (rc != TX_ERR_UNSUPPORTED) return rc;
   }
+  tx_gemm_desc d = desc;
+  if (fs) d.flags &= ~TX_GEMM_ROUND_OUT;  // no fused sums here: C stays exact for the caller
   dim3 grid((unsigned)((d.N + TCOLS - 1) / TCOLS), (unsigned)((d.M + ROWS - 1) / ROWS), (unsigned)batch);
   if ((d.N + TCOLS - 1) / TCOLS > 0x7fffffff || (d.M + ROWS - 1) / ROWS > 65535)
     return TX_ERR_UNSUPPORTED;
@@ -617,15 +642,17 @@ int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &d, int64_t batch) {
 
 // Route the skinny shapes; TX_ERR_UNSUPPORTED leaves the shape to the
 // tensor-core / SIMT kernels.
-int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d) {
-  const int64_t batch = d.batch > 1 ? d.batch : 1;
-  if (d.K <= 0 || batch > 65535) return TX_ERR_UNSUPPORTED;
-  if (d.K <= SK_KMAX) {
-    if (d.N <= 32) return launch_small_k<32>(ctx, d, batch);
-    if (d.N <= 64) return launch_small_k<64>(ctx, d, batch);
-    if (d.N <= 128) return launch_small_k<128>(ctx, d, batch);
-    return launch_small_k<256>(ctx, d, batch);
+int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &desc, FusedSum *fs) {
+  const int64_t batch = desc.batch > 1 ? desc.batch : 1;
+  if (desc.K <= 0 || batch > 65535) return TX_ERR_UNSUPPORTED;
+  if (desc.K <= SK_KMAX) {
+    if (desc.N <= 32) return launch_small_k<32>(ctx, desc, batch, fs);
+    if (desc.N <= 64) return launch_small_k<64>(ctx, desc, batch, fs);
+    if (desc.N <= 128) return launch_small_k<128>(ctx, desc, batch, fs);
+    return launch_small_k<256>(ctx, desc, batch, fs);
   }
+  tx_gemm_desc d = desc;
+  if (fs) d.flags &= ~TX_GEMM_ROUND_OUT;  // the remaining kernels do not sum columns
   if (batch != 1) return TX_ERR_UNSUPPORTED;
   if (d.N <= 16 && !d.trans_a && d.M >= 64) {
     if (d.N <= 2) return launch_small_n<2>(ctx, d);

@@ -353,12 +353,30 @@ __device__ __forceinline__ void chunk_math(float (&v)[32], const float (&sv)[32]
     v[j] = x;
   }
   if (pre_tile) tile_row_store(pre_tile, lane, v);
-  const bool round_out = (d.flags & TX_GEMM_ROUND_OUT) != 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     float x = act_f(act, v[j]);
     if (dact != TX_ACT_NONE) x *= dact_f(dact, sv[j]);
-    v[j] = round_out ? tx_epi::round_tf32(x) : x;
+    v[j] = x;
+  }
+}
+
+// After the epilogue math of a chunk: the fused column sums of the unrounded
+// values (one partial row per 32 output rows), then the optional TF32 rounding
+// of what is stored.
+__device__ __forceinline__ void chunk_finish(float (&v)[32], const tx_gemm_desc &d, float *col_part,
+                                             int64_t row_tile, int64_t gn0, int lane) {
+  if (col_part) {
+    float w[32];
+    const bool row_ok = row_tile + lane < d.M;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = row_ok ? v[j] : 0.f;
+    const float cs = tx_epi::colsum32(w, lane);
+    if (gn0 + lane < d.N) col_part[(row_tile / 32) * d.N + gn0 + lane] = cs;
+  }
+  if (d.flags & TX_GEMM_ROUND_OUT) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = tx_epi::round_tf32(v[j]);
   }
 }
 
@@ -367,7 +385,7 @@ __global__ void __launch_bounds__(192, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
-              int tma_epi, int conv_mask) {
+              int tma_epi, int conv_mask, float *col_part) {
   using Cfg = TcCfg<BN, MODE>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -585,6 +603,7 @@ __global__ void __launch_bounds__(192, 1)
         } else {
           chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
         }
+        chunk_finish(v, d, col_part, row_tile, (int64_t)n0 + 32 * c, lane);
         tile_row_store(eb + slot * 4096, lane, v);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
         __syncwarp();
@@ -699,6 +718,7 @@ struct PWork {
   int total_kb, kb_per;  // kb_per > 0: split-K, the third item index is the split
   int stages;            // pipeline depth (runtime: the epilogue's tiles vary)
   int ep_stride;         // epilogue bytes per warp
+  float *col_part;       // fused column sums (one row per 32 output rows) or null
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -925,6 +945,7 @@ __global__ void __launch_bounds__(192, 1)
         } else {
           chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
         }
+        chunk_finish(v, d, w.col_part, row_tile, (int64_t)n0 + 32 * c, lane);
         tile_row_store(out_t + oslot * 4096, lane, v);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -988,6 +1009,7 @@ struct Maps {
   CUtensorMap a, b, c, s, p;
   int tma_epi = 0;
   int conv_mask = 3;  // MODE 1: operands to round in shared memory (bit 0 A, bit 1 B)
+  float *col_part = nullptr;  // fused column sums, TMA epilogue only
 };
 
 // `z` = batch count, or the number of K splits when kb_per_cta > 0
@@ -1002,7 +1024,7 @@ int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int 
   }
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
   kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
-                                                          kb_per_cta, m.tma_epi, m.conv_mask);
+                                                          kb_per_cta, m.tma_epi, m.conv_mask, m.col_part);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
@@ -1090,6 +1112,7 @@ int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m,
   const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
   PWork w;
   w.ep_stride = kinds * 8192;
+  w.col_part = m.col_part;
   w.stages = (kSmemMax - 1024 - kPTail - 4 * w.ep_stride) / stage;
   if (w.stages > 8) w.stages = 8;
   if (w.stages < 2) return TX_ERR_UNSUPPORTED;
@@ -1151,7 +1174,8 @@ Tiling pick_tiling(tx_ctx *ctx, int64_t M, int64_t N, int64_t K, int64_t batch, 
 }  // namespace
 
 // mode: 0 raw fp32 operands (hardware truncation), 1 TF32 round-to-nearest, 2 3xTF32
-int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) {
+  tx_gemm_desc d = desc;
   if (d.K <= 0 || d.M <= 0 || d.N <= 0) return TX_ERR_UNSUPPORTED;
   const int64_t batch = d.batch > 1 ? d.batch : 1;
   if (d.M >= (1ll << 31) || d.N >= (1ll << 31) || d.K >= (1ll << 31) || batch > 65535)
@@ -1210,6 +1234,17 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   int splits = tiling.splits;
   if (splits <= 1) {
     make_epilogue_maps(m, d, batch);
+    if (fs) {
+      // the TMA epilogue sums columns as it stores; otherwise C stays unrounded
+      // and the caller sums it
+      if (m.tma_epi && batch == 1) {
+        m.col_part = fs->part;
+        fs->rows = (d.M + 31) / 32;
+        fs->fused = true;
+      } else {
+        d.flags &= ~TX_GEMM_ROUND_OUT;
+      }
+    }
     if (persistent && m.tma_epi) {
       const int rc = launch_persistent(ctx, bn, d, m, batch, 0);
       if (rc != TX_ERR_UNSUPPORTED) return rc;
@@ -1218,6 +1253,7 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode) {
   }
   const int kb_per = (total_kb + splits - 1) / splits;
   splits = (total_kb + kb_per - 1) / kb_per;
+  if (fs) d.flags &= ~TX_GEMM_ROUND_OUT;  // the split reduction does not sum columns
   Scratch part(ctx, (size_t)splits * d.M * d.N * sizeof(float));
   if (!part.ptr) return TX_ERR_OOM;
   tx_gemm_desc raw = d;

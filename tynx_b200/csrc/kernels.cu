@@ -666,19 +666,6 @@ __global__ void k_colsum_final(const float *__restrict__ part, int64_t np, int64
   }
 }
 
-int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out, float scale,
-                  int acc) {
-  const bool vec = (cols % 4 == 0) && ((((uintptr_t)part) & 15) == 0);
-  const int64_t per_block = vec ? 128 : 32;
-  const int64_t blocks = (cols + per_block - 1) / per_block;
-  if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
-  if (vec)
-    k_colsum_final<true><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
-  else
-    k_colsum_final<false><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
-  TX_LAUNCHED(ctx, "k_colsum_final");
-  return TX_OK;
-}
 
 // ---- TF32 operand shadow ---------------------------------------------------------------
 __global__ void k_round_tf32(const float *__restrict__ src, float *__restrict__ dst, int64_t n) {
@@ -978,6 +965,20 @@ __global__ void k_sgd(const OptTensor *__restrict__ tensors, const OptChunk *__r
 }
 
 }  // namespace
+
+int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out, float scale,
+                  int acc) {
+  const bool vec = (cols % 4 == 0) && ((((uintptr_t)part) & 15) == 0);
+  const int64_t per_block = vec ? 128 : 32;
+  const int64_t blocks = (cols + per_block - 1) / per_block;
+  if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
+  if (vec)
+    k_colsum_final<true><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  else
+    k_colsum_final<false><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  TX_LAUNCHED(ctx, "k_colsum_final");
+  return TX_OK;
+}
 
 // ============================================================================
 // host entry points
