@@ -334,6 +334,12 @@ struct GNode {
   // reader of it rounds it so anyway (GEMM operands) or only looks at its sign
   // (the relu mask); set at graph creation
   bool round_out = false;
+  // MatMul / Gemm whose sole consumer multiplies (or divides) it by a constant
+  // scalar: the scale is folded into alpha and the result written to the
+  // scaling node's output (scale_out); that node is skipped (scaled_into)
+  float out_scale = 1.f;
+  int scale_out = -1;
+  int scaled_into = -1;
 };
 
 struct tx_graph {
@@ -650,6 +656,28 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     a.fused_into = i;
   }
 
+  // ---- scalar scale folded into the producing contraction -------------------------------------
+  for (int i = 0; i < n_nodes; ++i) {
+    GNode &n = g->nodes[i];
+    if ((n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL) || n.fused_act) continue;
+    const GValue &y = g->values[n.d.out[0]];
+    if (y.is_output || y.consumers.size() != 1) continue;
+    GNode &m = g->nodes[y.consumers[0]];
+    if (m.d.op != TX_OP_MUL && m.d.op != TX_OP_DIV) continue;
+    const int other = m.d.in[0] == n.d.out[0] ? m.d.in[1] : m.d.in[0];
+    if (m.d.op == TX_OP_DIV && m.d.in[0] != n.d.out[0]) continue;  // c / y is not a scale
+    if (other < 0 || other == n.d.out[0]) continue;
+    const GValue &c = g->values[other];
+    if (c.kind != TX_VAL_CONST || c.dtype != TX_DT_F32 || numel_of(c.shape) != 1 || !vals[other].h_data) continue;
+    // the scale must not change the output shape (a rank-raising scalar would)
+    if (c.shape.size() > y.shape.size() && !y.shape.empty()) continue;
+    const float cv = *(const float *)vals[other].h_data;
+    if (m.d.op == TX_OP_DIV && cv == 0.f) continue;
+    n.out_scale = m.d.op == TX_OP_MUL ? cv : 1.f / cv;
+    n.scale_out = m.d.out[0];
+    m.scaled_into = i;
+  }
+
   // ---- TF32 output rounding: results whose every reader is a contraction --------------------
   // (directly, or through reshapes and transposes, which move values unchanged)
   std::function<bool(int, int)> feeds_only_contractions = [&](int v, int depth) -> bool {
@@ -672,7 +700,8 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     GNode &n = g->nodes[i];
     if (n.d.op == TX_OP_GEMM || n.d.op == TX_OP_MATMUL) {
       if (n.fused_act == TX_ACT_TANH) continue;  // tanh' reads the stored output
-      n.round_out = feeds_only_contractions(n.fused_act ? n.fused_out : n.d.out[0], 0);
+      n.round_out = feeds_only_contractions(
+          n.fused_act ? n.fused_out : n.scale_out >= 0 ? n.scale_out : n.d.out[0], 0);
     } else if (n.d.op == TX_OP_LAYERNORM) {
       n.round_out = feeds_only_contractions(n.d.out[0], 0);
     }
@@ -855,7 +884,7 @@ struct Fwd {
   int gemm_node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
-    int yv = n.fused_act ? n.fused_out : d.out[0];
+    int yv = n.fused_act ? n.fused_out : n.scale_out >= 0 ? n.scale_out : d.out[0];
     TX_TRY(alloc_value(yv));
     const Shape &a = S(d.in[0]), &b = S(d.in[1]);
     tx_gemm_desc q;
@@ -914,6 +943,7 @@ struct Fwd {
       q.preact = (float *)r->extra[ni];
       q.ld_preact = q.N;
     }
+    q.alpha *= n.out_scale;
     q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0);
     if (n.round_out && ctx->math == TX_MATH_TF32) {
       q.flags |= TX_GEMM_ROUND_OUT;
@@ -966,7 +996,7 @@ struct Fwd {
   int node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
-    if (n.fused_into >= 0) return TX_OK;  // done by the producing GEMM
+    if (n.fused_into >= 0 || n.scaled_into >= 0) return TX_OK;  // done by the producing GEMM
     if (is_alias_op(d.op)) {
       r->buf[d.out[0]] = r->buf[d.in[0]];
       r->owned[d.out[0]] = false;
@@ -1239,7 +1269,7 @@ struct Bwd {
   int gemm_backward(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
-    int yv = n.fused_act ? n.fused_out : d.out[0];
+    int yv = n.fused_act ? n.fused_out : n.scale_out >= 0 ? n.scale_out : d.out[0];
     float *dy = grad[yv];
     if (!dy) return TX_OK;
     // gradient with respect to the pre-activation
@@ -1261,7 +1291,7 @@ struct Bwd {
     if (d.op == TX_OP_GEMM) {
       int ta = (int)d.iattr[0], tb = (int)d.iattr[1];
       int64_t M = ta ? a[1] : a[0], K = ta ? a[0] : a[1], N = tb ? b[0] : b[1];
-      float alpha = (float)d.fattr[0];
+      float alpha = (float)d.fattr[0] * n.out_scale;
       // bias (unless the dgrad that produced dZ already summed it)
       if (rc == TX_OK && d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]] && !bias_fused[ni]) {
         float *t; int acc;
@@ -1332,7 +1362,7 @@ struct Bwd {
         float *t; int acc;
         rc = target(d.in[1], &t, &acc);
         tx_gemm_desc q; memset(&q, 0, sizeof q);
-        q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
+        q.alpha = n.out_scale; q.beta = acc ? 1.f : 0.f; q.batch = batch;
         q.M = K; q.N = N; q.K = M;
         bool x32 = false;
         q.A = gemm_operand(g, r, d.in[0], &x32); q.lda = K; q.trans_a = 1; q.stride_a = M * K;
@@ -1346,7 +1376,7 @@ struct Bwd {
         float *t; int acc;
         rc = dgrad_target(d.in[0], &t, &acc);
         tx_gemm_desc q; memset(&q, 0, sizeof q);
-        q.alpha = 1.f; q.beta = acc ? 1.f : 0.f; q.batch = batch;
+        q.alpha = n.out_scale; q.beta = acc ? 1.f : 0.f; q.batch = batch;
         q.M = M; q.N = K; q.K = N;
         q.A = dz; q.lda = N; q.trans_a = 0; q.stride_a = M * N;
         bool w32 = false;
@@ -1505,6 +1535,7 @@ struct Bwd {
   int node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
+    if (n.scaled_into >= 0) return TX_OK;  // scale folded into the producing contraction's alpha
     if (n.fused_into >= 0) {
       // activation folded into the producing GEMM: hand the gradient over
       int src = d.out[0];

@@ -1081,7 +1081,7 @@ struct Tiling {
 };
 
 template <int BN, bool A_MN, bool B_MN>
-int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem) {
+int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
   auto kern = k_gemm_tcp<BN, A_MN, B_MN>;
   static bool configured[64] = {};
   const int dev = ctx->device & 63;
@@ -1089,25 +1089,29 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
     TX_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
     configured[dev] = true;
   }
-  const int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
+  int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
+  if (max_grid > 0 && grid > max_grid) grid = max_grid;
   kern<<<grid, 192, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
   TX_LAUNCHED(ctx, "k_gemm_tcp");
   return TX_OK;
 }
 
 template <int BN>
-int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem) {
+int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_p<BN, true, true>(ctx, d, m, w, smem);
-  if (a_mn) return launch_p<BN, true, false>(ctx, d, m, w, smem);
-  if (b_mn) return launch_p<BN, false, true>(ctx, d, m, w, smem);
-  return launch_p<BN, false, false>(ctx, d, m, w, smem);
+  if (a_mn && b_mn) return launch_p<BN, true, true>(ctx, d, m, w, smem, max_grid);
+  if (a_mn) return launch_p<BN, true, false>(ctx, d, m, w, smem, max_grid);
+  if (b_mn) return launch_p<BN, false, true>(ctx, d, m, w, smem, max_grid);
+  return launch_p<BN, false, false>(ctx, d, m, w, smem, max_grid);
 }
 
 // Persistent launch of d (raw split partials when kb_per > 0, z = splits or
 // batch).  TX_ERR_UNSUPPORTED when the stages would not fit next to the
 // epilogue's tiles.
-int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per) {
+// max_grid > 0 caps the CTA count (several tiles per CTA even when the tiles
+// would fit one wave, so that one tile's epilogue overlaps the next's main loop).
+int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per,
+                      int max_grid = 0) {
   const int stage = (TC_BM + bn) * TC_BK * 4;
   const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
   PWork w;
@@ -1125,9 +1129,9 @@ int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m,
   w.items = (int)items;
   const int smem = 1024 + w.stages * stage + 4 * w.ep_stride + kPTail;
   switch (bn) {
-    case 256: return launch_p_bn<256>(ctx, d, m, w, smem);
-    case 64: return launch_p_bn<64>(ctx, d, m, w, smem);
-    default: return launch_p_bn<128>(ctx, d, m, w, smem);
+    case 256: return launch_p_bn<256>(ctx, d, m, w, smem, max_grid);
+    case 64: return launch_p_bn<64>(ctx, d, m, w, smem, max_grid);
+    default: return launch_p_bn<128>(ctx, d, m, w, smem, max_grid);
   }
 }
 
