@@ -1,973 +1,25 @@
-// tcgen05 / TMEM / TMA fp32 contraction for sm_100a (kind::tf32).
-//
-// One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
-//   warp 0      TMA producer: loads 128x32 A and BNx32 B fp32 tiles per stage
-//               into a STAGES-deep shared-memory ring;
-//   warp 1      allocates TMEM (BN fp32 columns x 128 lanes) and, from one
-//               thread, issues tcgen05.mma.kind::tf32 (K = 8 per instruction,
-//               4 per stage), committing each stage back to the producer;
-//   warps 2..5  operand conversion during the main loop (see MODE), then the
-//               epilogue: tcgen05.ld the accumulator, transpose each 32x32
-//               chunk through shared memory, and apply alpha / bias / beta*C /
-//               activation / act' with coalesced loads and stores.
-// MODE selects how fp32 operands become TF32:
-//   0  raw: the tensor core reads fp32 and drops the 13 low mantissa bits
-//      (truncation, biased toward zero);
-//   1  round to nearest: warps 2..5 round each landed stage in place
-//      (cvt.rna.tf32) before the MMA consumes it (unbiased; ~2^-11 relative);
-//   2  3xTF32: each operand is split into big = rna(x) and small = rna(x - big)
-//      and C += A_big B_big + A_big B_small + A_small B_big (fp32-class accuracy).
-// Operands may be K-major or MN-major on either side, so the forward (X W^T),
-// dgrad (dY W) and wgrad (dY^T X) products of a Gemm map onto the same kernel
-// without transposes.  No TMA multicast is used anywhere.
-//
-// Every mbarrier wait is bounded (~2 s of %globaltimer).  On expiry the CTA
-// raises the context's device error flag, stops issuing work, lets every role
-// reach the final barrier (no named barriers that an early exit could strand),
-// frees TMEM and returns.
+// Host side of the tcgen05 contraction: tensor maps, tile and split choice,
+// and the dispatch between the one-tile, CTA-pair and persistent kernels
+// (kernels in gemm_tc_kern.cuh, instantiated by gemm_tc_m0/m1/m2/pair/pers.cu).
 #include <cuda.h>
 #include <cudaTypedefs.h>
-#include <math.h>
 
 #include <cstring>
 #include <mutex>
 
 #include "common.h"
-#include "epilogue.cuh"
+#include "gemm_tc.cuh"
+
+using namespace tx_tc;
 
 namespace {
 
-constexpr int TC_BM = 128;
-constexpr int TC_BK = 32;                         // fp32 elements per 128-byte swizzle row
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-constexpr int kConvThreads = 128;                 // warps 2..5
-
-template <int BN, int MODE>
-struct TcCfg {
-  static constexpr int A_BYTES = TC_BM * TC_BK * 4;
-  static constexpr int B_BYTES = BN * TC_BK * 4;
-  // 3xTF32 keeps the small halves of both operands next to the big ones
-  static constexpr int STAGE = (A_BYTES + B_BYTES) * (MODE == 2 ? 2 : 1);
-  static constexpr int STAGES = (196 * 1024 / STAGE) > 8 ? 8 : (196 * 1024 / STAGE);
-  static constexpr int TAIL = 2048;  // barriers, TMEM address, abort flag, per-warp bias rows
-  static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + TAIL;
-  // The TMA epilogue reuses the drained stages: per epilogue warp, two output,
-  // two pre-activation, two act'-source and two C tiles of 32 x 32 fp32.
-  static_assert(STAGES * STAGE >= 4 * 8 * 4096, "epilogue tiles must fit in the stage memory");
-  // The tensor core adds each MMA's products into the fp32 TMEM accumulator
-  // with a biased (toward zero) rounding, so the error grows with the number
-  // of MMAs in one chain.  k-blocks are dealt round-robin to NACC accumulators
-  // (BN columns each, within the 512 TMEM columns) that the epilogue sums with
-  // IEEE fp32 adds.
-  static constexpr int NACC = MODE == 2 ? (512 / BN > 4 ? 4 : 512 / BN) : (512 / BN >= 2 ? 2 : 1);
-  static constexpr int TMEM_COLS = BN * NACC;
-};
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false (and raises the flags) when the limit expires
-// or another role of the CTA has already given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err, int site) {
-  if (mbar_try(bar, parity)) return true;
-  uint64_t start = global_ns();
-  while (true) {
-    if (mbar_try(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (global_ns() - start > kWaitLimitNs) {
-      *abort_flag = 1;
-      if (atomicCAS(err, 0, DEVERR_TIMEOUT) == 0) err[1] = site;
-      return false;
-    }
-  }
-}
-
-// Wait for a phase regardless of the abort flag (a copy in flight must land
-// before its shared memory is released), still bounded in time.
-__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
-  const uint64_t start = global_ns();
-  while (!mbar_try(bar, parity) && global_ns() - start < kWaitLimitNs) {
-  }
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint64_t *bar,
-                                            int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
-               "r"(src), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-// A 32 x 32 fp32 tile as TMA writes and reads it with the 128-byte swizzle:
-// row r is 128 bytes at r * 128, and its 16-byte chunk j sits at chunk
-// j ^ (r & 7).  A thread that owns row r moves the row with 8 float4 accesses;
-// the 8 lanes of one shared-memory phase hit 8 different chunks.
-__device__ __forceinline__ void tile_row_load(const uint8_t *tile, int r, float (&v)[32]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 t = *reinterpret_cast<const float4 *>(tile + r * 128 + ((j ^ (r & 7)) << 4));
-    v[4 * j] = t.x;
-    v[4 * j + 1] = t.y;
-    v[4 * j + 2] = t.z;
-    v[4 * j + 3] = t.w;
-  }
-}
-__device__ __forceinline__ void tile_row_store(uint8_t *tile, int r, const float (&v)[32]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    *reinterpret_cast<float4 *>(tile + r * 128 + ((j ^ (r & 7)) << 4)) =
-        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ float to_tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-// Shared-memory matrix descriptor (sm_100 layout, version 1).  K-major tiles
-// use the 128-byte swizzle (layout 2: 8 rows x 128 B atoms); MN-major fp32 tiles
-// use the 128-byte swizzle with 32-byte atomicity (layout 1: 4 rows x 128 B
-// atoms), the only MN-major layout the tf32 MMA accepts.
-constexpr uint32_t kLayoutSW128 = 2;
-constexpr uint32_t kLayoutSW128Base32B = 1;
-
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // version
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-
-// descriptor of the k-th 8-deep slice of a staged operand tile
-template <bool MN>
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
-  // K-major: advance 32 bytes inside the swizzled 128-byte row (SBO = 8 rows).
-  // MN-major: 8 K rows (1024 bytes) per instruction, LBO = the 4 KB stride
-  // between 32-element MN blocks, SBO = 4 rows.
-  return MN ? smem_desc(base + k * 1024, 4096, 512, kLayoutSW128Base32B)
-            : smem_desc(base + k * 32, 16, 1024, kLayoutSW128);
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ float act_f(int act, float v) { return tx_epi::act(act, v); }
-__device__ __forceinline__ float dact_f(int act, float s) { return tx_epi::dact(act, s); }
-
-// Epilogue over one transposed 32x32 chunk: lane = column, rr walks rows.
-// The common cases (no beta, no pre-activation store, no act') run a tight
-// loop specialised on the activation; everything else takes the general path.
-template <int ACT>
-__device__ __forceinline__ void epi_rows_fast(const float *__restrict__ t, int lane,
-                                              float *__restrict__ cp, int64_t ldc, int rows,
-                                              float alpha, bool has_bias, float bias_v, bool round_out) {
-#pragma unroll 8
-  for (int rr = 0; rr < rows; ++rr) {
-    float x = alpha * t[rr * 33 + lane];
-    if (has_bias) x += bias_v;
-    x = act_f(ACT, x);
-    cp[rr * ldc] = round_out ? tx_epi::round_tf32(x) : x;
-  }
-}
-
-// Epilogue arguments that stay in registers across the chunk loop.
-struct EpiArgs {
-  float alpha, beta;
-  int act, dact;
-  float *C;
-  int64_t ldc;
-  float *preact;
-  int64_t ld_preact;
-  const float *dact_src;
-  int64_t ld_dact;
-  bool round_out;
-};
-
-// Epilogue with beta * C, a pre-activation store or act', specialised on the
-// activation pair so that the 32 unrolled rows hold only the math they run
-// (a runtime switch inlined 32 times spreads each row's few instructions over
-// tens of KB of code and the warps stall on instruction fetch).  All loads of
-// the chunk's rows are issued before the first store: the stores may alias the
-// loaded tensors, so interleaving them would cost one round trip per row.
-template <int ACT, int DACT>
-__device__ __forceinline__ void epi_rows_spec(const float *__restrict__ t, int lane, const EpiArgs &e,
-                                              int64_t row0, int64_t gn, int rows, bool has_bias,
-                                              float bias_v) {
-  const bool beta = e.beta != 0.f;
-  float cv[32], sv[32];
-#pragma unroll
-  for (int rr = 0; rr < 32; ++rr) {
-    const bool ok = rr < rows;
-    cv[rr] = (ok && beta) ? e.C[(row0 + rr) * e.ldc + gn] : 0.f;
-    sv[rr] = (DACT != TX_ACT_NONE && ok) ? __ldg(e.dact_src + (row0 + rr) * e.ld_dact + gn) : 0.f;
-  }
-#pragma unroll
-  for (int rr = 0; rr < 32; ++rr) {
-    if (rr < rows) {
-      float x = e.alpha * t[rr * 33 + lane];
-      if (has_bias) x += bias_v;
-      if (beta) x += e.beta * cv[rr];
-      if (e.preact) e.preact[(row0 + rr) * e.ld_preact + gn] = x;
-      x = act_f(ACT, x);
-      if (DACT != TX_ACT_NONE) x *= dact_f(DACT, sv[rr]);
-      e.C[(row0 + rr) * e.ldc + gn] = e.round_out ? tx_epi::round_tf32(x) : x;
-    }
-  }
-}
-
-// Both an activation and act' in one epilogue (no workload lowers to this):
-// compact runtime loop.
-__device__ __noinline__ void epi_rows_any(const float *__restrict__ t, int lane, const EpiArgs &e,
-                                          int64_t row0, int64_t gn, int rows, bool has_bias,
-                                          float bias_v) {
-#pragma unroll 1
-  for (int rr = 0; rr < rows; ++rr) {
-    const int64_t gm = row0 + rr;
-    float x = e.alpha * t[rr * 33 + lane];
-    if (has_bias) x += bias_v;
-    if (e.beta != 0.f) x += e.beta * e.C[gm * e.ldc + gn];
-    if (e.preact) e.preact[gm * e.ld_preact + gn] = x;
-    x = act_f(e.act, x);
-    x *= dact_f(e.dact, e.dact_src[gm * e.ld_dact + gn]);
-    e.C[gm * e.ldc + gn] = e.round_out ? tx_epi::round_tf32(x) : x;
-  }
-}
-
-// Hint the rows of a tensor this CTA's epilogue will read into L2 while the
-// main loop runs (bulk prefetch; in-bounds, 16-byte aligned spans only).
-__device__ __forceinline__ void prefetch_rows_l2(const float *base, int64_t ld, int64_t row0,
-                                                 int64_t rows, int64_t col0, int64_t cols, int lane) {
-  if (!base || cols <= 0 || rows <= 0) return;
-  const float *p0 = base + row0 * ld + col0;
-  uint32_t bytes = (uint32_t)(cols * 4) & ~15u;
-  if (((uintptr_t)p0 & 15) || (ld & 3) || bytes == 0) return;
-  for (int64_t r = lane; r < rows; r += 32) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p0 + r * ld), "r"(bytes)
-                 : "memory");
-  }
-}
-
-// Row-form epilogue of one 32-column chunk (this thread's accumulator row):
-// x = alpha * acc + bias (+ beta * C), optionally stored as the pre-activation,
-// then act and * act'(s).  ACT / DACT are compile-time (-1: runtime values).
-template <int ACT, int DACT>
-__device__ __forceinline__ void chunk_math(float (&v)[32], const float (&sv)[32], const float (&cv)[32],
-                                           const float *bw, const tx_gemm_desc &d, bool use_beta,
-                                           uint8_t *pre_tile, int lane) {
-  const int act = ACT >= 0 ? ACT : d.act;
-  const int dact = DACT >= 0 ? DACT : d.dact;
-  const bool has_bias = d.bias != nullptr;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float x = d.alpha * v[j];
-    if (has_bias) x += bw[j];
-    if (use_beta) x += d.beta * cv[j];
-    v[j] = x;
-  }
-  if (pre_tile) tile_row_store(pre_tile, lane, v);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float x = act_f(act, v[j]);
-    if (dact != TX_ACT_NONE) x *= dact_f(dact, sv[j]);
-    v[j] = x;
-  }
-}
-
-// After the epilogue math of a chunk: the fused column sums of the unrounded
-// values (one partial row per 32 output rows), then the optional TF32 rounding
-// of what is stored.
-__device__ __forceinline__ void chunk_finish(float (&v)[32], const tx_gemm_desc &d, float *col_part,
-                                             int64_t row_tile, int64_t gn0, int lane) {
-  if (col_part) {
-    float w[32];
-    const bool row_ok = row_tile + lane < d.M;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = row_ok ? v[j] : 0.f;
-    const float cs = tx_epi::colsum32(w, lane);
-    if (gn0 + lane < d.N) col_part[(row_tile / 32) * d.N + gn0 + lane] = cs;
-  }
-  if (d.flags & TX_GEMM_ROUND_OUT) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = tx_epi::round_tf32(v[j]);
-  }
-}
-
-template <int BN, bool A_MN, bool B_MN, int MODE>
-__global__ void __launch_bounds__(192, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
-              const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
-              int tma_epi, int conv_mask, float *col_part) {
-  using Cfg = TcCfg<BN, MODE>;
-  constexpr int STAGES = Cfg::STAGES;
-  constexpr int NACC = Cfg::NACC;
-  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *full = (uint64_t *)(smem + STAGES * Cfg::STAGE);
-  uint64_t *conv = full + STAGES;
-  uint64_t *empty = conv + STAGES;
-  uint64_t *accb = empty + STAGES;
-  uint64_t *ebar = accb + 1;  // two act'/C tile-load slots per epilogue warp
-  uint32_t *tmem_holder = (uint32_t *)(ebar + 8);
-  volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
-  float *bias_rows = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE + 1024);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * TC_BM;
-  const int n0 = blockIdx.x * BN;
-  const int bz = blockIdx.z;
-  // split-K (kb_per_cta > 0): blockIdx.z selects a range of k-blocks and a raw
-  // partial output slice; the operands have no batch dimension then
-  const int total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
-  const int kb_first = kb_per_cta > 0 ? bz * kb_per_cta : 0;
-  const int num_k = kb_per_cta > 0 ? min(kb_per_cta, total_kb - kb_first) : total_kb;
-  const int zc = kb_per_cta > 0 ? 0 : bz;
-  const int used_acc = num_k < NACC ? num_k : NACC;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], kConvThreads);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(accb, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&ebar[i], 1);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_holder)),
-                 "r"(Cfg::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      for (int kb = 0; kb < num_k; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 1)) break;
-        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-        const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
-        const uint32_t b_dst = a_dst + A_BYTES;
-        const int k0 = (kb_first + kb) * TC_BK;
-        if (A_MN) {
-#pragma unroll
-          for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
-        } else {
-          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
-        }
-        if (B_MN) {
-#pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
-        } else {
-          tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
-                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                             ((uint32_t)(TC_BM >> 4) << 24);
-      for (int kb = 0; kb < num_k; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        uint64_t *ready = MODE == 0 ? &full[s] : &conv[s];
-        if (!mbar_wait(ready, round & 1, abort_flag, err, 2)) break;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE);
-        const uint32_t b_base = a_base + A_BYTES;
-        const uint32_t acc = tmem + (uint32_t)((kb % NACC) * BN);
-        const bool fresh = kb < NACC;  // first k-block of this accumulator
-#pragma unroll
-        for (int k = 0; k < TC_BK / 8; ++k) {
-          const uint64_t ad = operand_desc<A_MN>(a_base, k);
-          const uint64_t bd = operand_desc<B_MN>(b_base, k);
-          tc_mma_tf32(acc, ad, bd, idesc, (fresh && k == 0) ? 0u : 1u);
-          if (MODE == 2) {
-            const uint32_t sa = a_base + A_BYTES + B_BYTES, sb = sa + A_BYTES;
-            tc_mma_tf32(acc, ad, operand_desc<B_MN>(sb, k), idesc, 1u);
-            tc_mma_tf32(acc, operand_desc<A_MN>(sa, k), bd, idesc, 1u);
-          }
-        }
-        tc_commit(&empty[s]);
-      }
-      tc_commit(accb);  // arrives once every MMA issued above has completed
-    }
-  } else {
-    const int ct = threadIdx.x - 64;  // 0..127
-    {
-      // the epilogue's reads of C (beta) and of the act' source hit L2, not DRAM
-      const int q = warp & 3;
-      const int64_t r0 = (int64_t)m0 + q * 32;
-      const int64_t nrows = d.M - r0 < 32 ? d.M - r0 : 32;
-      const int64_t ncols = d.N - n0 < BN ? d.N - n0 : BN;
-      const int64_t cb = (int64_t)bz * d.stride_c;
-      if (d.dact) prefetch_rows_l2(d.dact_src + cb, d.ld_dact, r0, nrows, n0, ncols, lane);
-      if (d.beta != 0.f) prefetch_rows_l2(d.C + cb, d.ldc, r0, nrows, n0, ncols, lane);
-    }
-    if (MODE != 0) {
-      // operand conversion, one stage behind the producer and one ahead of the MMA;
-      // in MODE 1 an operand that already holds TF32 values (conv_mask bit clear)
-      // is left alone
-      constexpr int N4 = (A_BYTES + B_BYTES) / 16;
-      const int i_begin = (MODE == 2 || (conv_mask & 1)) ? ct : A_BYTES / 16 + ct;
-      const int i_end = (MODE == 2 || (conv_mask & 2)) ? N4 : A_BYTES / 16;
-      for (int kb = 0; kb < num_k; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&full[s], round & 1, abort_flag, err, 4)) break;
-        float4 *p = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE);
-        float4 *q = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE + A_BYTES + B_BYTES);
-#pragma unroll 4
-        for (int i = i_begin; i < i_end; i += kConvThreads) {
-          float4 v = p[i];
-          float4 big = make_float4(to_tf32_rn(v.x), to_tf32_rn(v.y), to_tf32_rn(v.z), to_tf32_rn(v.w));
-          p[i] = big;
-          if (MODE == 2)
-            q[i] = make_float4(to_tf32_rn(v.x - big.x), to_tf32_rn(v.y - big.y),
-                               to_tf32_rn(v.z - big.z), to_tf32_rn(v.w - big.w));
-        }
-        // make the generic-proxy writes visible to the tensor core (async proxy)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&conv[s]);
-      }
-    }
-    // epilogue warps 2..5 -> TMEM lane quadrants 2,3,0,1
-    const int quad = warp & 3;
-    const bool have = mbar_wait(accb, 0, abort_flag, err, 3);
-    tc_fence_after();
-    if (have && !*abort_flag && tma_epi) {
-      // TMA epilogue.  Each thread keeps its accumulator row: the act' source
-      // and the beta*C input arrive as swizzled 32 x 32 tiles (TMA loads into a
-      // two-slot ring, issued two chunks ahead); results go to swizzled output
-      // (and pre-activation) tiles that one lane stores with TMA, double
-      // buffered.  The drained pipeline stages hold the tiles.
-      constexpr int NCH = BN / 32;
-      uint8_t *eb = smem + quad * (8 * 4096);
-      const bool need_s = d.dact != TX_ACT_NONE;
-      const bool need_c = d.beta != 0.f;
-      const bool need_p = d.preact != nullptr;
-      const bool loads = need_s || need_c;
-      const int row_tile = m0 + quad * 32;
-      float *bw = bias_rows + quad * 32;
-      auto issue = [&](int c) {
-        const int slot = c & 1;
-        uint64_t *bar = &ebar[quad * 2 + slot];
-        mbar_expect_tx(bar, (need_s ? 4096u : 0u) + (need_c ? 4096u : 0u));
-        if (need_s) tma_load_3d(smem_u32(eb + (4 + slot) * 4096), &mapS, bar, n0 + 32 * c, row_tile, bz);
-        if (need_c) tma_load_3d(smem_u32(eb + (6 + slot) * 4096), &mapC, bar, n0 + 32 * c, row_tile, bz);
-      };
-      int issued = 0, consumed = 0;
-      if (loads && lane == 0)
-        for (; issued < (NCH < 2 ? NCH : 2); ++issued) issue(issued);
-      issued = __shfl_sync(0xffffffffu, issued, 0);
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c) {
-        const int slot = c & 1;
-        float v[32], sv[32], cv[32];
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32);
-        tmem_ld32(lane_base, v);
-#pragma unroll 1
-        for (int a = 1; a < used_acc; ++a) {
-          float w[32];
-          tmem_ld32(lane_base + (uint32_t)(a * BN), w);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += w[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] = cv[j] = 0.f;
-        if (loads) {
-          if (!mbar_wait(&ebar[quad * 2 + slot], (c >> 1) & 1, abort_flag, err, 5)) break;
-          ++consumed;
-          if (need_s) tile_row_load(eb + (4 + slot) * 4096, lane, sv);
-          if (need_c) tile_row_load(eb + (6 + slot) * 4096, lane, cv);
-          __syncwarp();
-          if (lane == 0 && c + 2 < NCH) issue(c + 2);
-          if (c + 2 < NCH) ++issued;
-        }
-        const int64_t gnb = (int64_t)n0 + c * 32 + lane;
-        bw[lane] = (d.bias && gnb < d.N) ? d.bias[gnb] * d.bias_scale : 0.f;
-        if (lane == 0 && c >= 2) bulk_wait_read<1>();  // the tiles of chunk c - 2 are free
-        __syncwarp();
-        uint8_t *pre_tile = need_p ? eb + (2 + slot) * 4096 : nullptr;
-        if (!d.dact) {
-          switch (d.act) {
-            case TX_ACT_RELU: chunk_math<TX_ACT_RELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_TANH: chunk_math<TX_ACT_TANH, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_GELU: chunk_math<TX_ACT_GELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            default: chunk_math<TX_ACT_NONE, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-          }
-        } else if (d.act == TX_ACT_NONE) {
-          switch (d.dact) {
-            case TX_ACT_RELU: chunk_math<TX_ACT_NONE, TX_ACT_RELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_TANH: chunk_math<TX_ACT_NONE, TX_ACT_TANH>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            default: chunk_math<TX_ACT_NONE, TX_ACT_GELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-          }
-        } else {
-          chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
-        }
-        chunk_finish(v, d, col_part, row_tile, (int64_t)n0 + 32 * c, lane);
-        tile_row_store(eb + slot * 4096, lane, v);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&mapC, smem_u32(eb + slot * 4096), n0 + 32 * c, row_tile, bz);
-          if (need_p) tma_store_3d(&mapP, smem_u32(pre_tile), n0 + 32 * c, row_tile, bz);
-          bulk_commit();
-        }
-        __syncwarp();
-      }
-      // after an abort, let the tile loads already in flight land before the
-      // shared memory is released (bounded like every other wait)
-      for (int c = consumed; c < issued; ++c) mbar_drain(&ebar[quad * 2 + (c & 1)], (c >> 1) & 1);
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
-    } else if (have && !*abort_flag) {
-      // TMEM gives each thread one row; global memory wants a warp per row.
-      // Each 32x32 chunk is transposed through padded shared memory (the
-      // drained pipeline stages), then lanes walk columns so every load and
-      // store of the epilogue is a coalesced 128-byte row segment.
-      float *tile = reinterpret_cast<float *>(smem) + quad * (32 * 33);
-      const int64_t row0 = (int64_t)m0 + quad * 32;
-      float *C = d.C + (int64_t)bz * d.stride_c;
-      const int64_t cbase = bz * d.stride_c;
-      const bool round_out = (d.flags & TX_GEMM_ROUND_OUT) != 0;
-      const EpiArgs ea{d.alpha, d.beta, d.act, d.dact, C, d.ldc,
-                       d.preact ? d.preact + cbase : nullptr, d.ld_preact,
-                       d.dact_src ? d.dact_src + cbase : nullptr, d.ld_dact, round_out};
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c;
-        tmem_ld32(lane_base, v);
-#pragma unroll 1
-        for (int a = 1; a < used_acc; ++a) {
-          float w[32];
-          tmem_ld32(lane_base + (uint32_t)(a * BN), w);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += w[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tile[lane * 33 + j] = v[j];
-        __syncwarp();
-        const int64_t gn = (int64_t)n0 + c + lane;
-        const bool col_ok = gn < d.N;
-        const float bias_v = (d.bias && col_ok) ? d.bias[gn] * d.bias_scale : 0.f;
-        int rows = d.M - row0 < 32 ? (int)(d.M - row0) : 32;
-        if (!col_ok || rows < 0) rows = 0;
-        if (d.beta == 0.f && !d.preact && !d.dact) {
-          float *cp = C + row0 * d.ldc + gn;
-          switch (d.act) {
-            case TX_ACT_RELU: epi_rows_fast<TX_ACT_RELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
-            case TX_ACT_TANH: epi_rows_fast<TX_ACT_TANH>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
-            case TX_ACT_GELU: epi_rows_fast<TX_ACT_GELU>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
-            default: epi_rows_fast<TX_ACT_NONE>(tile, lane, cp, d.ldc, rows, d.alpha, d.bias != nullptr, bias_v, round_out); break;
-          }
-        } else if (!d.dact) {
-          const bool hb = d.bias != nullptr;
-          switch (d.act) {
-            case TX_ACT_RELU: epi_rows_spec<TX_ACT_RELU, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-            case TX_ACT_TANH: epi_rows_spec<TX_ACT_TANH, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-            case TX_ACT_GELU: epi_rows_spec<TX_ACT_GELU, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-            default: epi_rows_spec<TX_ACT_NONE, TX_ACT_NONE>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-          }
-        } else if (d.act == TX_ACT_NONE) {
-          const bool hb = d.bias != nullptr;
-          switch (d.dact) {
-            case TX_ACT_RELU: epi_rows_spec<TX_ACT_NONE, TX_ACT_RELU>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-            case TX_ACT_TANH: epi_rows_spec<TX_ACT_NONE, TX_ACT_TANH>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-            default: epi_rows_spec<TX_ACT_NONE, TX_ACT_GELU>(tile, lane, ea, row0, gn, rows, hb, bias_v); break;
-          }
-        } else {
-          epi_rows_any(tile, lane, ea, row0, gn, rows, d.bias != nullptr, bias_v);
-        }
-        __syncwarp();
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(Cfg::TMEM_COLS));
-  }
-}
-
-// ---- persistent variant ------------------------------------------------------------------
-// For operands that need no conversion (TF32 mode with pre-rounded operands,
-// or the truncating mode): one CTA per SM walks the output tiles (tile order:
-// N fastest, so CTAs that run together share A rows in L2).  The TMA / MMA
-// ring runs on across tiles, and TMEM holds two accumulator buffers, so the
-// MMA warp fills one while the epilogue warps drain the other.  The epilogue
-// has its own shared memory (the stages stay busy): per warp two output tiles
-// plus two pre-activation, act'-source and C tiles when the GEMM uses them.
-constexpr int kSmemMax = 232448;  // 227 KB opt-in
-constexpr int kPTail = 2048;
-
-template <int BN>
-struct PCfg {
-  static constexpr int NACC = BN == 256 ? 1 : 2;
-  static constexpr int ACC = BN * NACC;                 // columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC < 256 ? 256 : 2 * ACC;
-  static constexpr int A_BYTES = TC_BM * TC_BK * 4;
-  static constexpr int B_BYTES = BN * TC_BK * 4;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
-};
-
-struct PWork {
-  int tiles_m, tiles_n, items;
-  int total_kb, kb_per;  // kb_per > 0: split-K, the third item index is the split
-  int stages;            // pipeline depth (runtime: the epilogue's tiles vary)
-  int ep_stride;         // epilogue bytes per warp
-  float *col_part;       // fused column sums (one row per 32 output rows) or null
-};
-
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
-    k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
-               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, PWork w) {
-  using Cfg = PCfg<BN>;
-  constexpr int NACC = Cfg::NACC;
-  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int stages = w.stages;
-  uint8_t *ep = smem + stages * Cfg::STAGE;
-  uint8_t *tail = ep + 4 * w.ep_stride;
-  uint64_t *full = (uint64_t *)tail;
-  uint64_t *empty = full + 8;
-  uint64_t *tfull = empty + 8;
-  uint64_t *tempty = tfull + 2;
-  uint64_t *ebar = tempty + 2;
-  uint32_t *tmem_holder = (uint32_t *)(ebar + 8);
-  volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
-  float *bias_rows = reinterpret_cast<float *>(tail + 1024);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const bool split = w.kb_per > 0;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
-    }
-    for (int i = 0; i < 8; ++i) mbar_init(&ebar[i], 1);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_holder)),
-                 "r"(Cfg::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
-
-  // item -> (z, m tile, n tile) and its k-block range
-  auto decode = [&](int item, int &m0, int &n0, int &z, int &kb_first, int &num_k) {
-    const int nt = item % w.tiles_n;
-    const int t = item / w.tiles_n;
-    m0 = (t % w.tiles_m) * TC_BM;
-    n0 = nt * BN;
-    z = t / w.tiles_m;
-    kb_first = split ? z * w.kb_per : 0;
-    num_k = split ? min(w.kb_per, w.total_kb - kb_first) : w.total_kb;
-  };
-
-  if (warp == 0) {
-    if (lane == 0) {
-      uint32_t cnt = 0;
-      for (int item = blockIdx.x; item < w.items && !*abort_flag; item += gridDim.x) {
-        int m0, n0, z, kb_first, num_k;
-        decode(item, m0, n0, z, kb_first, num_k);
-        const int zc = split ? 0 : z;
-        for (int kb = 0; kb < num_k; ++kb, ++cnt) {
-          const int s = (int)(cnt % (uint32_t)stages);
-          const uint32_t round = cnt / (uint32_t)stages;
-          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 11)) break;
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-          const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
-          const uint32_t b_dst = a_dst + A_BYTES;
-          const int k0 = (kb_first + kb) * TC_BK;
-          if (A_MN) {
-#pragma unroll
-            for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
-          } else {
-            tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
-          }
-          if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
-          } else {
-            tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((A_MN ? 1u : 0u) << 15) |
-                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                             ((uint32_t)(TC_BM >> 4) << 24);
-      uint32_t cnt = 0;
-      int it = 0;
-      for (int item = blockIdx.x; item < w.items && !*abort_flag; item += gridDim.x, ++it) {
-        int m0, n0, z, kb_first, num_k;
-        decode(item, m0, n0, z, kb_first, num_k);
-        const int buf = it & 1;
-        const uint32_t use = (uint32_t)it >> 1;
-        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, err, 12)) break;
-        tc_fence_after();
-        bool ok = true;
-        for (int kb = 0; kb < num_k; ++kb, ++cnt) {
-          const int s = (int)(cnt % (uint32_t)stages);
-          const uint32_t round = cnt / (uint32_t)stages;
-          if (!mbar_wait(&full[s], round & 1, abort_flag, err, 13)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE);
-          const uint32_t b_base = a_base + A_BYTES;
-          const uint32_t acc = tmem + (uint32_t)(buf * Cfg::ACC + (kb % NACC) * BN);
-          const bool fresh = kb < NACC;
-#pragma unroll
-          for (int k = 0; k < TC_BK / 8; ++k)
-            tc_mma_tf32(acc, operand_desc<A_MN>(a_base, k), operand_desc<B_MN>(b_base, k), idesc,
-                        (fresh && k == 0) ? 0u : 1u);
-          tc_commit(&empty[s]);
-        }
-        if (!ok) break;
-        tc_commit(&tfull[buf]);  // arrives when every MMA of this tile has completed
-      }
-    }
-  } else {
-    const int quad = warp & 3;
-    uint8_t *eb = ep + quad * w.ep_stride;
-    const bool need_s = d.dact != TX_ACT_NONE;
-    const bool need_c = d.beta != 0.f;
-    const bool need_p = d.preact != nullptr;
-    const bool loads = need_s || need_c;
-    // per-warp tile slots: out[2], then pre[2], s[2], c[2] when used
-    uint8_t *out_t = eb;
-    uint8_t *pre_t = eb + 8192;
-    uint8_t *s_t = pre_t + (need_p ? 8192 : 0);
-    uint8_t *c_t = s_t + (need_s ? 8192 : 0);
-    float *bw = bias_rows + quad * 32;
-    constexpr int NCH = BN / 32;
-    uint32_t issued = 0, consumed = 0, chunk_seq = 0;
-    int it = 0;
-    bool alive = true;
-    for (int item = blockIdx.x; item < w.items && alive; item += gridDim.x, ++it) {
-      int m0, n0, z, kb_first, num_k;
-      decode(item, m0, n0, z, kb_first, num_k);
-      const int buf = it & 1;
-      const uint32_t use = (uint32_t)it >> 1;
-      const int row_tile = m0 + quad * 32;
-      const int used_acc = num_k < NACC ? num_k : NACC;
-      auto issue = [&](int c) {  // lane 0: act' / C tiles of chunk c into ring slot `issued & 1`
-        const int slot = issued & 1;
-        uint64_t *bar = &ebar[quad * 2 + slot];
-        mbar_expect_tx(bar, (need_s ? 4096u : 0u) + (need_c ? 4096u : 0u));
-        if (need_s) tma_load_3d(smem_u32(s_t + slot * 4096), &mapS, bar, n0 + 32 * c, row_tile, z);
-        if (need_c) tma_load_3d(smem_u32(c_t + slot * 4096), &mapC, bar, n0 + 32 * c, row_tile, z);
-      };
-      if (loads) {
-        for (int c = 0; c < (NCH < 2 ? NCH : 2); ++c) {
-          if (lane == 0) issue(c);
-          ++issued;
-        }
-      }
-      if (!mbar_wait(&tfull[buf], use & 1, abort_flag, err, 14)) break;
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c, ++chunk_seq) {
-        const int oslot = chunk_seq & 1;
-        float v[32], sv[32], cv[32];
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * Cfg::ACC + c * 32);
-        tmem_ld32(lane_base, v);
-#pragma unroll 1
-        for (int a = 1; a < used_acc; ++a) {
-          float t[32];
-          tmem_ld32(lane_base + (uint32_t)(a * BN), t);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += t[j];
-        }
-        if (c == NCH - 1) {
-          // this warp has read its rows of the accumulator: hand the buffer back
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[j] = cv[j] = 0.f;
-        if (loads) {
-          const int lslot = consumed & 1;
-          if (!mbar_wait(&ebar[quad * 2 + lslot], (consumed >> 1) & 1, abort_flag, err, 15)) {
-            alive = false;
-            break;
-          }
-          ++consumed;
-          if (need_s) tile_row_load(s_t + lslot * 4096, lane, sv);
-          if (need_c) tile_row_load(c_t + lslot * 4096, lane, cv);
-          __syncwarp();
-          if (c + 2 < NCH) {
-            if (lane == 0) issue(c + 2);
-            ++issued;
-          }
-        }
-        const int64_t gnb = (int64_t)n0 + c * 32 + lane;
-        bw[lane] = (d.bias && gnb < d.N) ? d.bias[gnb] * d.bias_scale : 0.f;
-        if (lane == 0 && chunk_seq >= 2) bulk_wait_read<1>();  // tiles of chunk_seq - 2 are free
-        __syncwarp();
-        uint8_t *pre_tile = need_p ? pre_t + oslot * 4096 : nullptr;
-        if (!d.dact) {
-          switch (d.act) {
-            case TX_ACT_RELU: chunk_math<TX_ACT_RELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_TANH: chunk_math<TX_ACT_TANH, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_GELU: chunk_math<TX_ACT_GELU, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            default: chunk_math<TX_ACT_NONE, TX_ACT_NONE>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-          }
-        } else if (d.act == TX_ACT_NONE) {
-          switch (d.dact) {
-            case TX_ACT_RELU: chunk_math<TX_ACT_NONE, TX_ACT_RELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            case TX_ACT_TANH: chunk_math<TX_ACT_NONE, TX_ACT_TANH>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-            default: chunk_math<TX_ACT_NONE, TX_ACT_GELU>(v, sv, cv, bw, d, need_c, pre_tile, lane); break;
-          }
-        } else {
-          chunk_math<-1, -1>(v, sv, cv, bw, d, need_c, pre_tile, lane);
-        }
-        chunk_finish(v, d, w.col_part, row_tile, (int64_t)n0 + 32 * c, lane);
-        tile_row_store(out_t + oslot * 4096, lane, v);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&mapC, smem_u32(out_t + oslot * 4096), n0 + 32 * c, row_tile, z);
-          if (need_p) tma_store_3d(&mapP, smem_u32(pre_tile), n0 + 32 * c, row_tile, z);
-          bulk_commit();
-        }
-        __syncwarp();
-      }
-    }
-    for (uint32_t c = consumed; c < issued; ++c) mbar_drain(&ebar[quad * 2 + (c & 1)], (c >> 1) & 1);
-    if (lane == 0) bulk_wait_read<0>();
-    __syncwarp();
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(Cfg::TMEM_COLS));
+int launch_any(tx_ctx *ctx, int mode, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z,
+               int kb_per_cta) {
+  switch (mode) {
+    case 0: return launch_mode0(ctx, bn, d, m, z, kb_per_cta);
+    case 2: return launch_mode2(ctx, bn, d, m, z, kb_per_cta);
+    default: return launch_mode1(ctx, bn, d, m, z, kb_per_cta);
   }
 }
 
@@ -1003,59 +55,6 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
   return r == CUDA_SUCCESS;
 }
 
-// Tensor maps of one launch: the operands, and for the TMA epilogue the
-// output (also the beta * C input), the act' source and the pre-activation.
-struct Maps {
-  CUtensorMap a, b, c, s, p;
-  int tma_epi = 0;
-  int conv_mask = 3;  // MODE 1: operands to round in shared memory (bit 0 A, bit 1 B)
-  float *col_part = nullptr;  // fused column sums, TMA epilogue only
-};
-
-// `z` = batch count, or the number of K splits when kb_per_cta > 0
-template <int BN, bool A_MN, bool B_MN, int MODE>
-int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
-  auto kern = k_gemm_tc<BN, A_MN, B_MN, MODE>;
-  static bool configured[64] = {};
-  int dev = ctx->device & 63;
-  if (!configured[dev]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN, MODE>::SMEM);
-    configured[dev] = true;
-  }
-  dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
-  kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
-                                                          kb_per_cta, m.tma_epi, m.conv_mask, m.col_part);
-  TX_LAUNCHED(ctx, "k_gemm_tc");
-  return TX_OK;
-}
-
-template <int BN, int MODE>
-int launch_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
-  const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_tc<BN, true, true, MODE>(ctx, d, m, z, kb_per_cta);
-  if (a_mn) return launch_tc<BN, true, false, MODE>(ctx, d, m, z, kb_per_cta);
-  if (b_mn) return launch_tc<BN, false, true, MODE>(ctx, d, m, z, kb_per_cta);
-  return launch_tc<BN, false, false, MODE>(ctx, d, m, z, kb_per_cta);
-}
-
-template <int MODE>
-int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per_cta) {
-  switch (bn) {
-    case 256: return launch_bn<256, MODE>(ctx, d, m, z, kb_per_cta);
-    case 64: return launch_bn<64, MODE>(ctx, d, m, z, kb_per_cta);
-    default: return launch_bn<128, MODE>(ctx, d, m, z, kb_per_cta);
-  }
-}
-
-int launch_any(tx_ctx *ctx, int mode, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z,
-               int kb_per_cta) {
-  switch (mode) {
-    case 0: return launch_mode<0>(ctx, bn, d, m, z, kb_per_cta);
-    case 2: return launch_mode<2>(ctx, bn, d, m, z, kb_per_cta);
-    default: return launch_mode<1>(ctx, bn, d, m, z, kb_per_cta);
-  }
-}
-
 // A row-major [batch][M][N] fp32 tensor TMA can tile: 16-byte aligned base,
 // row and batch strides that are 16-byte multiples.
 bool tma_tileable(const float *p, int64_t ld, int64_t batch, int64_t stride) {
@@ -1079,61 +78,6 @@ struct Tiling {
   int bn = 128;
   int splits = 1;
 };
-
-template <int BN, bool A_MN, bool B_MN>
-int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
-  auto kern = k_gemm_tcp<BN, A_MN, B_MN>;
-  static bool configured[64] = {};
-  const int dev = ctx->device & 63;
-  if (!configured[dev]) {
-    TX_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
-    configured[dev] = true;
-  }
-  int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
-  if (max_grid > 0 && grid > max_grid) grid = max_grid;
-  kern<<<grid, 192, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
-  TX_LAUNCHED(ctx, "k_gemm_tcp");
-  return TX_OK;
-}
-
-template <int BN>
-int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
-  const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_p<BN, true, true>(ctx, d, m, w, smem, max_grid);
-  if (a_mn) return launch_p<BN, true, false>(ctx, d, m, w, smem, max_grid);
-  if (b_mn) return launch_p<BN, false, true>(ctx, d, m, w, smem, max_grid);
-  return launch_p<BN, false, false>(ctx, d, m, w, smem, max_grid);
-}
-
-// Persistent launch of d (raw split partials when kb_per > 0, z = splits or
-// batch).  TX_ERR_UNSUPPORTED when the stages would not fit next to the
-// epilogue's tiles.
-// max_grid > 0 caps the CTA count (several tiles per CTA even when the tiles
-// would fit one wave, so that one tile's epilogue overlaps the next's main loop).
-int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per,
-                      int max_grid = 0) {
-  const int stage = (TC_BM + bn) * TC_BK * 4;
-  const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
-  PWork w;
-  w.ep_stride = kinds * 8192;
-  w.col_part = m.col_part;
-  w.stages = (kSmemMax - 1024 - kPTail - 4 * w.ep_stride) / stage;
-  if (w.stages > 8) w.stages = 8;
-  if (w.stages < 2) return TX_ERR_UNSUPPORTED;
-  w.tiles_m = (int)((d.M + TC_BM - 1) / TC_BM);
-  w.tiles_n = (int)((d.N + bn - 1) / bn);
-  w.total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
-  w.kb_per = kb_per;
-  const int64_t items = (int64_t)w.tiles_m * w.tiles_n * z;
-  if (items > 0x7fffffff) return TX_ERR_UNSUPPORTED;
-  w.items = (int)items;
-  const int smem = 1024 + w.stages * stage + 4 * w.ep_stride + kPTail;
-  switch (bn) {
-    case 256: return launch_p_bn<256>(ctx, d, m, w, smem, max_grid);
-    case 64: return launch_p_bn<64>(ctx, d, m, w, smem, max_grid);
-    default: return launch_p_bn<128>(ctx, d, m, w, smem, max_grid);
-  }
-}
 
 
 // Pick the tile width and the K split from a small cost model: waves of CTAs
@@ -1218,14 +162,21 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
     }
   }
   const int bn = tiling.bn;
+  // One-tile launches of 256-wide tiles without conversion and an MN-major B
+  // (the dgrad and wgrad products) run as CTA pairs when there are at least
+  // two row tiles: each SM stages half of B (eight 32-column boxes become
+  // four).  Measured main loops: 4096x1024x1024 dgrad 14.6 -> 12.4 us,
+  // 1024x1024x4096 wgrad (4 splits) 17.6 -> 14.4 us; with a K-major B the pair
+  // is slower (11.1 -> 12.2 us) and the single-CTA tile stays.
+  const bool pair = mode == 0 && bn == 256 && !persistent && d.M > TC_BM && !d.trans_b;
   bool ok;
   if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
     ok = make_map(&m.a, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
   else  // A stored M x K (K-major): box 32(K) x 128(M)
     ok = make_map(&m.a, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
   if (!ok) return TX_ERR_UNSUPPORTED;
-  if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N)
-    ok = make_map(&m.b, d.B, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
+  if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N), BN / 2 per CTA of a pair
+    ok = make_map(&m.b, d.B, d.K, d.N, d.ldb, batch, d.stride_b, pair ? bn / 2 : bn, false);
   else  // B stored K x N (MN-major): box 32(N) x 32(K)
     ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
@@ -1253,6 +204,7 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
       const int rc = launch_persistent(ctx, bn, d, m, batch, 0);
       if (rc != TX_ERR_UNSUPPORTED) return rc;
     }
+    if (pair) return launch_pair(ctx, d, m, batch, 0);
     return launch_any(ctx, mode, bn, d, m, batch, 0);
   }
   const int kb_per = (total_kb + splits - 1) / splits;
@@ -1275,7 +227,8 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
   make_epilogue_maps(m, raw, splits);
   int rc = TX_ERR_UNSUPPORTED;
   if (persistent && m.tma_epi) rc = launch_persistent(ctx, bn, raw, m, splits, kb_per);
-  if (rc == TX_ERR_UNSUPPORTED) rc = launch_any(ctx, mode, bn, raw, m, splits, kb_per);
+  if (rc == TX_ERR_UNSUPPORTED) rc = pair ? launch_pair(ctx, raw, m, splits, kb_per)
+                                          : launch_any(ctx, mode, bn, raw, m, splits, kb_per);
   TX_TRY(rc);
   return gemm_split_reduce(ctx, d, part.as<float>(), splits);
 }
