@@ -162,27 +162,26 @@ __global__ void k_gemm_split_reduce(tx_gemm_desc d, const float *__restrict__ pa
   const int64_t n = d.M * d.N;
   const float *src = part + gm * d.N + gn;
   if (vec && gn + 4 <= d.N) {
-    // partials are added in split order; loads are issued four at a time
-    float4 s = *reinterpret_cast<const float4 *>(src);
-    int p = 1;
-    for (; p + 4 <= splits; p += 4) {
-      float4 t[4];
+    // partials are added in split order (the first one starts the sum); up to
+    // eight loads are in flight before the adds
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < splits; p += 8) {
+      float4 t[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(src + (int64_t)(p + j) * n);
+      for (int j = 0; j < 8; ++j)
+        if (p + j < splits) t[j] = *reinterpret_cast<const float4 *>(src + (int64_t)(p + j) * n);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        s.x += t[j].x;
-        s.y += t[j].y;
-        s.z += t[j].z;
-        s.w += t[j].w;
+      for (int j = 0; j < 8; ++j) {
+        if (p + j >= splits) break;
+        if (p + j == 0) {
+          s = t[0];
+        } else {
+          s.x += t[j].x;
+          s.y += t[j].y;
+          s.z += t[j].z;
+          s.w += t[j].w;
+        }
       }
-    }
-    for (; p < splits; ++p) {
-      const float4 t = *reinterpret_cast<const float4 *>(src + (int64_t)p * n);
-      s.x += t.x;
-      s.y += t.y;
-      s.z += t.z;
-      s.w += t.w;
     }
     float4 o = make_float4(split_epilogue(d, s.x, gm, gn), split_epilogue(d, s.y, gm, gn + 1),
                            split_epilogue(d, s.z, gm, gn + 2), split_epilogue(d, s.w, gm, gn + 3));

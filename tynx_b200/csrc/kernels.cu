@@ -613,56 +613,34 @@ __global__ void k_layernorm_bwd(const float *__restrict__ x, const float *__rest
 // out[c] (+)= scale * sum_p part[p, c]   (fixed order)
 
 // Final column reduction of a [np, cols] partial-sum matrix: out = scale * sum
-// (+ out when acc).  Block (32, 8): with vec each thread owns 4 adjacent
-// columns, the 8 row groups take partial rows ty, ty + 8, ... in order with
-// four loads in flight, and the groups are combined in a fixed order.
-template <bool VEC>
-__global__ void k_colsum_final(const float *__restrict__ part, int64_t np, int64_t cols,
-                               float *__restrict__ out, float scale, int acc) {
-  constexpr int W = VEC ? 4 : 1;
-  __shared__ float sm[8][32 * W];
-  const int64_t c = ((int64_t)blockIdx.x * 32 + threadIdx.x) * W;
-  float s[W];
-#pragma unroll
-  for (int j = 0; j < W; ++j) s[j] = 0.f;
+// (+ out when acc).  Block (32, 32): lane x owns column 32 * blockIdx.x + x,
+// the 32 row groups take partial rows ty, ty + 32, ... in order with eight
+// loads in flight, and the groups are combined in a fixed order.
+__global__ void __launch_bounds__(1024) k_colsum_final(const float *__restrict__ part, int64_t np,
+                                                       int64_t cols, float *__restrict__ out, float scale,
+                                                       int acc) {
+  __shared__ float sm[32][33];
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
   if (c < cols) {
     int64_t p = threadIdx.y;
-    for (; p + 24 < np; p += 32) {
-      float v[4][W];
+    for (; p + 7 * 32 < np; p += 8 * 32) {
+      float v[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (VEC) {
-          const float4 t = *reinterpret_cast<const float4 *>(part + (p + 8 * i) * cols + c);
-          v[i][0] = t.x;
-          v[i][W > 1 ? 1 : 0] = t.y;
-          v[i][W > 2 ? 2 : 0] = t.z;
-          v[i][W > 3 ? 3 : 0] = t.w;
-        } else {
-          v[i][0] = part[(p + 8 * i) * cols + c];
-        }
-      }
+      for (int i = 0; i < 8; ++i) v[i] = part[(p + 32 * i) * cols + c];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < W; ++j) s[j] += v[i][j];
+      for (int i = 0; i < 8; ++i) s += v[i];
     }
-    for (; p < np; p += 8) {
-#pragma unroll
-      for (int j = 0; j < W; ++j) s[j] += part[p * cols + c + j];
-    }
+    for (; p < np; p += 32) s += part[p * cols + c];
   }
-#pragma unroll
-  for (int j = 0; j < W; ++j) sm[threadIdx.y][threadIdx.x * W + j] = s[j];
+  sm[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y == 0 && c < cols) {
+    float t = sm[0][threadIdx.x];
 #pragma unroll
-    for (int j = 0; j < W; ++j) {
-      float t = sm[0][threadIdx.x * W + j];
-#pragma unroll
-      for (int i = 1; i < 8; ++i) t += sm[i][threadIdx.x * W + j];
-      t *= scale;
-      out[c + j] = acc ? out[c + j] + t : t;
-    }
+    for (int i = 1; i < 32; ++i) t += sm[i][threadIdx.x];
+    t *= scale;
+    out[c] = acc ? out[c] + t : t;
   }
 }
 
@@ -968,14 +946,9 @@ __global__ void k_sgd(const OptTensor *__restrict__ tensors, const OptChunk *__r
 
 int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out, float scale,
                   int acc) {
-  const bool vec = (cols % 4 == 0) && ((((uintptr_t)part) & 15) == 0);
-  const int64_t per_block = vec ? 128 : 32;
-  const int64_t blocks = (cols + per_block - 1) / per_block;
+  const int64_t blocks = (cols + 31) / 32;
   if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
-  if (vec)
-    k_colsum_final<true><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
-  else
-    k_colsum_final<false><<<(unsigned)blocks, dim3(32, 8), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  k_colsum_final<<<(unsigned)blocks, dim3(32, 32), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
   TX_LAUNCHED(ctx, "k_colsum_final");
   return TX_OK;
 }
