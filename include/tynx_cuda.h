@@ -211,9 +211,10 @@ int tx_softmax_xent_bwd(tx_ctx *ctx, const float *d_logits, const int64_t *d_lab
                         int64_t rows, int64_t cols, const float *d_scale, float *d_dlogits,
                         int accumulate);
 /* Same result as tx_softmax_xent_fwd, for callers that cannot allocate device
- * memory: a host runtime that owns all of its HBM up front, or code issuing
- * work while a CUDA graph is being captured, where an allocation would be
- * recorded into the graph.  It has no counterpart in the reference.
+ * memory: a host runtime that reserves all of the GPU's memory for its own
+ * allocator and lends libraries only the buffers it passes in, or a
+ * latency-bound loop that cannot afford the device-wide synchronisation a
+ * cudaMalloc or cudaFree implies.  It has no counterpart in the reference.
  * The per-row losses go to a fixed 1 MiB device array built into the library
  * (held on every GPU that loads it until the process exits), so rows must be
  * at most 262144; larger inputs fail with TX_ERR_SHAPE.  Nothing is allocated:

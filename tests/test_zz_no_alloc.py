@@ -1,8 +1,9 @@
 """The allocation-free cross-entropy entry point agrees with the allocating one.
 
 ``tx_softmax_xent_fwd_noalloc`` serves callers that cannot allocate device memory
-(a host runtime that owns all of its HBM, or work issued while a CUDA graph is
-being captured).  It is called here through the C ABI, twice in a row on
+(a host runtime that reserves all of the GPU's memory for its own allocator, or
+a latency-bound loop that cannot pay for the device-wide synchronisation of
+cudaMalloc / cudaFree).  It is called here through the C ABI, twice in a row on
 different inputs, and must give the same loss as ``tx_softmax_xent_fwd`` within
 the 1e-5 relative tolerance the other cross-entropy tests use, without touching
 the context allocator.  The file is named to run last, and it also passes on
