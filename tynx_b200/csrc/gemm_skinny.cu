@@ -239,17 +239,31 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
   float *P = d.preact ? d.preact + bz * d.stride_c : nullptr;
   const int64_t n0 = (int64_t)blockIdx.x * TCOLS;
   const int K = (int)d.K;
-  for (int e = threadIdx.x; e < K * TCOLS; e += 256) {
-    int k, n;
-    if (d.trans_b) { k = e % K; n = e / K; }
-    else { n = e % TCOLS; k = e / TCOLS; }
-    const int64_t gn = n0 + n;
-    Bs[k][n] = gn < d.N ? (d.trans_b ? B[gn * d.ldb + k] : B[(int64_t)k * d.ldb + gn]) : 0.f;
-  }
   const int cg = threadIdx.x % TPR, rg = threadIdx.x / TPR;
   const int64_t gn = n0 + cg * 4;
   const bool col_ok = gn < d.N;  // N % 4 == 0: a group is all in or all out
   const bool beta = d.beta != 0.f;
+  // epilogue inputs (C for beta, the act' source) of a row tile: they do not
+  // depend on the products, so they are in flight while A and B are staged
+  float4 cold[8], sv[8];
+  auto load_epi = [&](int64_t m0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t gm = m0 + rg + RG * i;
+      const bool ok = col_ok && gm < d.M;
+      cold[i] = (ok && beta) ? *reinterpret_cast<const float4 *>(C + gm * d.ldc + gn) : make_float4(0.f, 0.f, 0.f, 0.f);
+      sv[i] = (ok && DACT != TX_ACT_NONE) ? *reinterpret_cast<const float4 *>(S + gm * d.ld_dact + gn)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if ((int)blockIdx.y < row_tiles) load_epi((int64_t)blockIdx.y * ROWS);
+  for (int e = threadIdx.x; e < K * TCOLS; e += 256) {
+    int k, n;
+    if (d.trans_b) { k = e % K; n = e / K; }
+    else { n = e % TCOLS; k = e / TCOLS; }
+    const int64_t gbn = n0 + n;
+    Bs[k][n] = gbn < d.N ? (d.trans_b ? B[gbn * d.ldb + k] : B[(int64_t)k * d.ldb + gbn]) : 0.f;
+  }
   float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
   if (d.bias && col_ok) {
     bias = make_float4(d.bias[gn] * d.bias_scale, d.bias[gn + 1] * d.bias_scale, d.bias[gn + 2] * d.bias_scale,
@@ -259,6 +273,7 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
 #pragma unroll 1
   for (int rt = blockIdx.y; rt < row_tiles; rt += gridDim.y) {
     const int64_t m0 = (int64_t)rt * ROWS;
+    if (rt != (int)blockIdx.y) load_epi(m0);  // the first tile's were issued above
     __syncthreads();  // the previous tile's readers of As are done
     for (int e = threadIdx.x; e < K * ROWS; e += 256) {
       int k, m;
@@ -268,16 +283,6 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
       As[m][k] = gm < d.M ? (d.trans_a ? A[(int64_t)k * d.lda + gm] : A[gm * d.lda + k]) : 0.f;
     }
     __syncthreads();
-    // epilogue inputs first: they do not depend on the products
-    float4 cold[8], sv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t gm = m0 + rg + RG * i;
-      const bool ok = col_ok && gm < d.M;
-      cold[i] = (ok && beta) ? *reinterpret_cast<const float4 *>(C + gm * d.ldc + gn) : make_float4(0.f, 0.f, 0.f, 0.f);
-      sv[i] = (ok && DACT != TX_ACT_NONE) ? *reinterpret_cast<const float4 *>(S + gm * d.ld_dact + gn)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;

@@ -833,17 +833,26 @@ struct OptHparams {
 
 // Adam / AdamW: one block per chunk.  Step counters: t = steps[i] + 1 for the
 // math; the last block to finish (atomic ticket) commits the increments.
-__global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__restrict__ chunks,
-                       int n_chunks, const OptHparams *__restrict__ hp_ptr, int64_t *steps,
-                       const int32_t *__restrict__ active_list, int n_active, int kind,
-                       int amsgrad, unsigned *ticket) {
+constexpr int64_t kAdamSub = 1024;  // elements per CTA: one float4 per thread (256 threads)
+
+// At most 64 registers, so several CTAs share an SM.
+__global__ void __launch_bounds__(256, 4)
+    k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__restrict__ chunks, int n_chunks,
+           const OptHparams *__restrict__ hp_ptr, int64_t *steps, const int32_t *__restrict__ active_list,
+           int n_active, int kind, int amsgrad, unsigned *ticket) {
   const OptHparams hp = *hp_ptr;
   const OptChunk ch = chunks[blockIdx.x];
   const OptTensor t = tensors[ch.tensor];
-  const int64_t step = steps[ch.tensor] + 1;
-  // bias corrections in double, rounded to f32 like mul_scalar/div_scalar(f64) on f32 data
-  const float bc1 = (float)(1.0 - pow(hp.beta1_d, (double)step));
-  const float bc2 = (float)(1.0 - pow(hp.beta2_d, (double)step));
+  // bias corrections in double, rounded to f32 like mul_scalar/div_scalar(f64)
+  // on f32 data; computed once per CTA (the double pow is long and register-hungry)
+  __shared__ float s_bc[2];
+  if (threadIdx.x == 0) {
+    const double step = (double)(steps[ch.tensor] + 1);
+    s_bc[0] = (float)(1.0 - pow(hp.beta1_d, step));
+    s_bc[1] = (float)(1.0 - pow(hp.beta2_d, step));
+  }
+  __syncthreads();
+  const float bc1 = s_bc[0], bc2 = s_bc[1];
   const bool coupled = (kind == 0) && hp.wd != 0.f;
   const bool decoupled = (kind == 1) && hp.wd != 0.f;
   // one element, in the order of adam.rs:458-509 (no FMA contraction)
@@ -862,12 +871,16 @@ __global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__
     if (decoupled) w = __fmul_rn(w, hp.decay_factor);
     w = __fsub_rn(w, upd);
   };
+  // this CTA's part of the chunk: blockIdx.y selects kAdamSub elements, so a
+  // thread updates one float4 (more resident warps hide the memory and
+  // division latencies)
   const int64_t end = ch.start + ch.len;
-  const bool vec = !amsgrad && (ch.start & 3) == 0 &&
+  const int64_t lo = ch.start + (int64_t)blockIdx.y * kAdamSub;
+  const int64_t hi = lo + kAdamSub < end ? lo + kAdamSub : end;
+  const bool vec = !amsgrad && (lo & 3) == 0 &&
                    ((((uintptr_t)t.w) | ((uintptr_t)t.g) | ((uintptr_t)t.m) | ((uintptr_t)t.v)) & 15) == 0;
-  int64_t i = ch.start + threadIdx.x * (vec ? 4 : 1);
   if (vec) {
-    for (; i + 3 < end; i += (int64_t)blockDim.x * 4) {
+    for (int64_t i = lo + threadIdx.x * 4; i + 3 < hi; i += (int64_t)blockDim.x * 4) {
       float4 w = *reinterpret_cast<float4 *>(t.w + i);
       const float4 g = *reinterpret_cast<const float4 *>(t.g + i);
       float4 m = *reinterpret_cast<float4 *>(t.m + i);
@@ -880,9 +893,9 @@ __global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__
       *reinterpret_cast<float4 *>(t.m + i) = m;
       *reinterpret_cast<float4 *>(t.v + i) = v;
     }
-    // ragged tail of the last chunk of a tensor
-    for (int64_t j = (end & ~int64_t(3)) + threadIdx.x; j < end && j >= ch.start; j += blockDim.x) {
-      if (j < (end & ~int64_t(3))) continue;
+    // ragged tail of the last chunk of a tensor (past the last multiple of 4)
+    const int64_t tail = (hi & ~int64_t(3)) > lo ? (hi & ~int64_t(3)) : lo;
+    for (int64_t j = tail + threadIdx.x; j < hi; j += blockDim.x) {
       float w = t.w[j], m = t.m[j], v = t.v[j];
       update(w, t.g[j], m, v, nullptr);
       t.w[j] = w;
@@ -890,7 +903,7 @@ __global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__
       t.v[j] = v;
     }
   } else {
-    for (; i < end; i += blockDim.x) {
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float w = t.w[i], m = t.m[i], v = t.v[i];
       update(w, t.g[i], m, v, amsgrad ? t.vmax + i : nullptr);
       t.w[i] = w;
@@ -902,7 +915,7 @@ __global__ void k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__
   if (threadIdx.x == 0) {
     __threadfence();
     unsigned done = atomicAdd(ticket, 1u);
-    if (done == (unsigned)n_chunks - 1) {
+    if (done == (unsigned)(gridDim.x * gridDim.y) - 1) {
       for (int i = 0; i < n_active; ++i) steps[active_list[i]] += 1;
       __threadfence();
       *ticket = 0u;
@@ -1464,7 +1477,8 @@ extern "C" int tx_optim_step(tx_optim *o, const uint8_t *active) {
                                              n_chunks, al.first, al.second, o->cfg.nesterov,
                                              o->d_ticket);
   } else {
-    k_adam<<<n_chunks, 256, 0, ctx->stream>>>(o->d_tensors, it->second.first, n_chunks, o->d_hp,
+    k_adam<<<dim3((unsigned)n_chunks, (unsigned)(kChunk / kAdamSub)), 256, 0, ctx->stream>>>(
+        o->d_tensors, it->second.first, n_chunks, o->d_hp,
                                               o->d_steps, al.first, al.second, o->cfg.kind,
                                               o->cfg.amsgrad, o->d_ticket);
   }
