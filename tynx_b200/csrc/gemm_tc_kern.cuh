@@ -1,16 +1,18 @@
 #pragma once
 // tcgen05 / TMEM / TMA fp32 contraction for sm_100a (kind::tf32).
 //
-// One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
+// One CTA computes a 128 x BN tile of C.  Warp roles (320 threads in the
+// one-tile kernel, 192 in the persistent one):
 //   warp 0      TMA producer: loads 128x32 A and BNx32 B fp32 tiles per stage
 //               into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM (BN fp32 columns x 128 lanes) and, from one
 //               thread, issues tcgen05.mma.kind::tf32 (K = 8 per instruction,
 //               4 per stage), committing each stage back to the producer;
-//   warps 2..5  operand conversion during the main loop (see MODE), then the
-//               epilogue: tcgen05.ld the accumulator, transpose each 32x32
-//               chunk through shared memory, and apply alpha / bias / beta*C /
-//               activation / act' with coalesced loads and stores.
+//   warps 2..5  operand conversion during the main loop (see MODE);
+//   warps 2..9  the epilogue, two warps per TMEM lane quadrant (warps 2..5 in
+//               the persistent kernel): tcgen05.ld the accumulator, apply
+//               alpha / bias / beta*C / activation / act', and store each
+//               32x32 chunk through swizzled shared memory by TMA.
 // MODE selects how fp32 operands become TF32:
 //   0  raw: the tensor core reads fp32 and drops the 13 low mantissa bits
 //      (truncation, biased toward zero);
@@ -56,14 +58,15 @@ struct TcCfg {
   // 3xTF32 keeps the small halves of both operands next to the big ones
   static constexpr int STAGE = (A_BYTES + B_BYTES) * (MODE == 2 ? 2 : 1);
   static constexpr int STAGES = (196 * 1024 / STAGE) > 8 ? 8 : (196 * 1024 / STAGE);
-  // barriers, TMEM address and abort flag in the first 1 KB, then each
-  // epilogue warp's copy of the tile's BN bias values
-  static constexpr int TAIL = 1024 + 4 * BN * 4;
+  // barriers, TMEM address and abort flag in the first 1 KB, then each of the
+  // eight epilogue warps' copy of the tile's BN bias values
+  static constexpr int TAIL = 1024 + 8 * BN * 4;
   static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + TAIL;
-  // The TMA epilogue reuses the drained stages: per epilogue warp, two output,
-  // two pre-activation, four act'-source and four C tiles of 32 x 32 fp32.
-  static constexpr int EPI_TILES = 12;
-  static_assert(STAGES * STAGE >= 4 * EPI_TILES * 4096, "epilogue tiles must fit in the stage memory");
+  // The TMA epilogue reuses the drained stages: 48 tiles of 32 x 32 fp32,
+  // six per warp when eight warps share the epilogue (two output tiles and
+  // two each of the pre-activation, act'-source and C tiles in use), eight
+  // per warp when four do.
+  static_assert(STAGES * STAGE >= 48 * 4096, "epilogue tiles must fit in the stage memory");
   // The tensor core adds each MMA's products into the fp32 TMEM accumulator
   // with a biased (toward zero) rounding, so the error grows with the number
   // of MMAs in one chain.  k-blocks are dealt round-robin to NACC accumulators
@@ -469,11 +472,13 @@ struct EpiWarp {
     }
     ++issued;
   }
-  // fill the free ring slots with the tile's next chunks
+  // fill the free ring slots with this warp's next chunks of the tile (chunk
+  // c0 + k * cstep for the k-th)
   template <int NCH>
-  __device__ __forceinline__ void fill(int &next, int n0, int row_tile, int z, int lane) {
-    while (next < NCH && issued - consumed < (uint32_t)NS) {
-      issue(n0 + 32 * next, row_tile, z, lane);
+  __device__ __forceinline__ void fill(int &next, int c0, int cstep, int n0, int row_tile, int z,
+                                       int lane) {
+    while (c0 + next * cstep < NCH && issued - consumed < (uint32_t)NS) {
+      issue(n0 + 32 * (c0 + next * cstep), row_tile, z, lane);
       ++next;
     }
   }
@@ -509,7 +514,7 @@ template <int BN, int NACC, int NS, int ACT, int DACT, bool LOADS, bool DUAL>
 __device__ __forceinline__ bool epi_tile(EpiWarp<NS> &e, const tx_gemm_desc &d, uint32_t tbase, int used_acc,
                                       const float *bias_w, float *bias_row, int n0, int row_tile, int z,
                                       float *col_part, int next, uint64_t *release, volatile int *abort_flag,
-                                      int *err, int site, int lane) {
+                                      int *err, int site, int lane, int c0, int cstep) {
   constexpr int NCH = BN / 32;
   const int act = ACT >= 0 ? ACT : d.act;
   const int dact = DACT >= 0 ? DACT : d.dact;
@@ -519,10 +524,10 @@ __device__ __forceinline__ bool epi_tile(EpiWarp<NS> &e, const tx_gemm_desc &d, 
     const int64_t gn = (int64_t)n0 + 32 * c + lane;
     return (has_bias && gn < d.N) ? d.bias[gn] * d.bias_scale : 0.f;
   };
-  float bnext = bias_w ? 0.f : bias_at(0);
-  if (LOADS) e.template fill<NCH>(next, n0, row_tile, z, lane);
+  float bnext = bias_w ? 0.f : bias_at(c0);
+  if (LOADS) e.template fill<NCH>(next, c0, cstep, n0, row_tile, z, lane);
 #pragma unroll 1
-  for (int c = 0; c < NCH; ++c) {
+  for (int c = c0; c < NCH; c += cstep) {
     float v[32];
     {
       uint32_t r0[32];
@@ -552,7 +557,7 @@ __device__ __forceinline__ bool epi_tile(EpiWarp<NS> &e, const tx_gemm_desc &d, 
         for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r0[j]);
       }
     }
-    if (release && c == NCH - 1) {
+    if (release && c + cstep >= NCH) {
       // this warp has read its rows of the accumulator: hand the buffer back
       tc_fence_before();
       __syncwarp();
@@ -576,13 +581,13 @@ __device__ __forceinline__ bool epi_tile(EpiWarp<NS> &e, const tx_gemm_desc &d, 
         for (int j = 0; j < 32; ++j) cv[j] = 0.f;
       }
       __syncwarp();  // every lane has read the slot before it is refilled
-      e.template fill<NCH>(next, n0, row_tile, z, lane);
+      e.template fill<NCH>(next, c0, cstep, n0, row_tile, z, lane);
     }
     const int oslot = (int)(e.seq & 1);
     const float *bb = bias_w + c * 32;
     if (!bias_w) {
       bias_row[lane] = bnext;
-      if (c + 1 < NCH) bnext = bias_at(c + 1);  // lands while this chunk is processed
+      if (c + cstep < NCH) bnext = bias_at(c + cstep);  // lands while this chunk is processed
       bb = bias_row;
     }
     if (lane == 0 && e.seq >= 2) bulk_wait_read<1>();  // the tiles of chunk seq - 2 are free
@@ -624,10 +629,10 @@ template <int BN, int NACC, int NS, bool DUAL>
 __device__ __forceinline__ bool epi_any(EpiWarp<NS> &e, const tx_gemm_desc &d, uint32_t tbase, int used_acc,
                                         const float *bias_w, float *bias_row, int n0, int row_tile, int z,
                                         float *col_part, int next, uint64_t *release, volatile int *abort_flag,
-                                        int *err, int site, int lane) {
+                                        int *err, int site, int lane, int c0 = 0, int cstep = 1) {
 #define TX_EPI(A, D, L)                                                                                 \
   epi_tile<BN, NACC, NS, A, D, L, DUAL>(e, d, tbase, used_acc, bias_w, bias_row, n0, row_tile, z, col_part, next, \
-                                  release, abort_flag, err, site, lane)
+                                  release, abort_flag, err, site, lane, c0, cstep)
   if (!e.need_s && !e.need_c) {  // no act' source: dact is none
     switch (d.act) {
       case TX_ACT_RELU: return TX_EPI(TX_ACT_RELU, TX_ACT_NONE, false);
@@ -661,7 +666,7 @@ __device__ __forceinline__ bool epi_any(EpiWarp<NS> &e, const tx_gemm_desc &d, u
 // even CTA (the leader) issues the MMAs for both, the odd one only loads its
 // operand halves and runs its own epilogue on its own TMEM rows.
 template <int BN, bool A_MN, bool B_MN, int MODE, bool PAIR = false>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
@@ -677,10 +682,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t *conv = full + STAGES;
   uint64_t *empty = conv + STAGES;
   uint64_t *accb = empty + STAGES;
-  uint64_t *ebar = accb + 1;  // four act'/C tile-load slots per epilogue warp
+  uint64_t *ebar = accb + 1;  // two act'/C tile-load slots per epilogue warp (eight warps)
   uint32_t *tmem_holder = (uint32_t *)(ebar + 16);
   volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
-  float *bias_all = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE + 1024);  // [4][BN]
+  float *bias_all = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE + 1024);  // [8][BN]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -820,8 +825,8 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    const int ct = threadIdx.x - 64;  // 0..127
-    {
+    const int ct = threadIdx.x - 64;  // 0..255; warps 2..5 (0..127) convert operands
+    if (warp < 6) {
       // the epilogue's reads of C (beta) and of the act' source hit L2, not DRAM
       const int q = warp & 3;
       const int64_t r0 = (int64_t)m0 + q * 32;
@@ -831,7 +836,7 @@ __global__ void __launch_bounds__(192, 1)
       if (d.dact) prefetch_rows_l2(d.dact_src + cb, d.ld_dact, r0, nrows, n0, ncols, lane);
       if (d.beta != 0.f) prefetch_rows_l2(d.C + cb, d.ldc, r0, nrows, n0, ncols, lane);
     }
-    if (MODE != 0) {
+    if (MODE != 0 && warp < 6) {
       // operand conversion, one stage behind the producer and one ahead of the MMA;
       // in MODE 1 an operand that already holds TF32 values (conv_mask bit clear)
       // is left alone
@@ -858,34 +863,45 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive(&conv[s]);
       }
     }
-    // epilogue warps 2..5 -> TMEM lane quadrants 2,3,0,1
+    // epilogue warps 2..9 -> TMEM lane quadrants 2,3,0,1,2,3,0,1.  Two warps
+    // share a quadrant and take alternate 32-column chunks, so two serial
+    // chains (TMEM load, math, shared store, TMA store) run per scheduler;
+    // when all of pre-activation, act' source and C are in use, warps 2..5
+    // alone take every chunk (six tiles per warp would not hold them).
+    const int ew = warp - 2;  // 0..7
     const int quad = warp & 3;
-    float *bias_w = bias_all + quad * BN;
-    stage_bias<BN>(bias_w, d, n0, lane);  // while the main loop runs
+    const int half = ew >> 2;
+    const bool need_s = d.dact != TX_ACT_NONE, need_c = d.beta != 0.f, need_p = d.preact != nullptr;
+    const int tiles_w = 2 + (need_p ? 2 : 0) + (need_s ? 2 : 0) + (need_c ? 2 : 0);
+    const bool wide = tiles_w <= 6;
+    const bool active = wide || half == 0;
+    float *bias_w = bias_all + ew * BN;
+    if (active) stage_bias<BN>(bias_w, d, n0, lane);  // while the main loop runs
     const bool have = mbar_wait(accb, 0, abort_flag, err, 3);
     tc_fence_after();
     if (have && !*abort_flag && tma_epi) {
-      // TMA epilogue over the drained pipeline stages: per warp two output,
-      // two pre-activation, four act'-source and four C tiles
-      EpiWarp<4> e;
-      uint8_t *eb = smem + quad * (Cfg::EPI_TILES * 4096);
-      e.out_t = eb;
-      e.pre_t = eb + 2 * 4096;
-      e.s_t = eb + 4 * 4096;
-      e.c_t = eb + 8 * 4096;
-      e.bars = &ebar[quad * 4];
-      e.map_c = &mapC;
-      e.map_s = &mapS;
-      e.map_p = &mapP;
-      e.issued = e.consumed = e.seq = 0;
-      e.need_s = d.dact != TX_ACT_NONE;
-      e.need_c = d.beta != 0.f;
-      e.need_p = d.preact != nullptr;
-      const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16);
-      epi_any<BN, NACC, 4, true>(e, d, tbase, used_acc, bias_w, nullptr, n0, m0 + quad * 32,
-                           bz, col_part, 0, nullptr, abort_flag, err, 5, lane);
-      e.drain(lane);
-    } else if (have && !*abort_flag) {
+      if (active) {
+        // TMA epilogue over the drained pipeline stages
+        EpiWarp<2> e;
+        uint8_t *eb = smem + ew * (wide ? 6 : 8) * 4096;
+        e.need_s = need_s;
+        e.need_c = need_c;
+        e.need_p = need_p;
+        e.out_t = eb;
+        e.pre_t = eb + 2 * 4096;
+        e.s_t = e.pre_t + (need_p ? 2 * 4096 : 0);
+        e.c_t = e.s_t + (need_s ? 2 * 4096 : 0);
+        e.bars = &ebar[ew * 2];
+        e.map_c = &mapC;
+        e.map_s = &mapS;
+        e.map_p = &mapP;
+        e.issued = e.consumed = e.seq = 0;
+        const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16);
+        epi_any<BN, NACC, 2, true>(e, d, tbase, used_acc, bias_w, nullptr, n0, m0 + quad * 32, bz, col_part,
+                                   0, nullptr, abort_flag, err, 5, lane, wide ? half : 0, wide ? 2 : 1);
+        e.drain(lane);
+      }
+    } else if (have && !*abort_flag && half == 0) {
       // TMEM gives each thread one row; global memory wants a warp per row.
       // Each 32x32 chunk is transposed through padded shared memory (the
       // drained pipeline stages), then lanes walk columns so every load and
@@ -1152,7 +1168,7 @@ __global__ void __launch_bounds__(192, 1)
       const int used_acc = num_k < NACC ? num_k : NACC;
       // the tile's first act' / C tiles, while its MMAs run
       int next = 0;
-      if (e.need_s || e.need_c) e.template fill<BN / 32>(next, n0, row_tile, z, lane);
+      if (e.need_s || e.need_c) e.template fill<BN / 32>(next, 0, 1, n0, row_tile, z, lane);
       if (!mbar_wait(&tfull[buf], use & 1, abort_flag, err, 14)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * Cfg::ACC);
@@ -1183,7 +1199,7 @@ int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int 
     configured[dev] = true;
   }
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
-  kern<<<grid, 192, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
+  kern<<<grid, 320, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
                                                           kb_per_cta, m.tma_epi, m.conv_mask, m.col_part);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
@@ -1209,7 +1225,7 @@ int launch_tc_pair(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z,
   const int64_t tiles_n = (d.N + 255) / 256;
   if (tiles_n > 65535) return TX_ERR_UNSUPPORTED;
   cfg.gridDim = dim3((unsigned)(2 * pairs_m), (unsigned)tiles_n, (unsigned)z);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(320, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
