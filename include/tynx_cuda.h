@@ -98,6 +98,22 @@ int tx_d2d(tx_ctx *ctx, void *d_dst, const void *d_src, size_t bytes);
 int tx_memset(tx_ctx *ctx, void *d_ptr, int value, size_t bytes);
 int tx_fill_f32(tx_ctx *ctx, float *d_ptr, int64_t n, float value);
 int tx_host_alloc(size_t bytes, void **h_out); /* pinned host memory */
+
+/* Upload ring for input batches (no counterpart in the reference, which reads
+ * its inputs from host memory on every step).  `depth` (2..16) device buffers
+ * of `bytes` each and a copy stream beside the compute stream.
+ * tx_prefetch_put copies `bytes` from h_src (pinned, for the copy to overlap)
+ * into the next buffer and returns it: the copy waits only for the compute
+ * work that read that buffer's previous batch (issued before the put after
+ * that batch's), and all compute work issued after the put waits for the copy.
+ * So with depth 2, putting batch i + 1 right after enqueuing step i uploads it
+ * while step i runs.  A returned buffer is valid until `depth` more puts; h_src
+ * must stay unchanged until the compute stream has passed the put.  Not
+ * allowed during a capture. */
+typedef struct tx_prefetch tx_prefetch;
+int tx_prefetch_create(tx_ctx *ctx, size_t bytes, int depth, tx_prefetch **out);
+int tx_prefetch_put(tx_prefetch *p, const void *h_src, size_t bytes, void **d_out);
+int tx_prefetch_destroy(tx_prefetch *p);
 int tx_host_free(void *h_ptr);
 /* Bytes currently held by the allocator (in use, cached). */
 int tx_mem_stats(tx_ctx *ctx, uint64_t *in_use, uint64_t *cached);

@@ -10,6 +10,7 @@ optimizer steps run on hand-written sm_100a kernels in ``libtynx_cuda.so``.
 from . import distributions, nn, optim
 from ._core import (
     Device,
+    Prefetcher,
     Tensor,
     arange,
     cat,
@@ -23,6 +24,7 @@ from ._core import (
     no_grad,
     ones,
     ones_like,
+    pinned,
     rand,
     randn,
     set_math_mode,
@@ -42,9 +44,9 @@ int64 = "int64"
 bool = "bool"  # noqa: A001  (mirrors tynx.bool)
 
 __all__ = [
-    "CompiledFunction", "Device", "ImportedModel", "Parameter", "Session", "Tensor",
+    "CompiledFunction", "Device", "ImportedModel", "Parameter", "Prefetcher", "Session", "Tensor",
     "TrainabilityReport", "arange", "cat", "compile", "distributions", "full", "full_like",
     "get_default_device", "is_grad_enabled", "load", "matmul", "maximum", "minimum", "nn",
-    "no_grad", "ones", "ones_like", "optim", "rand", "randn", "set_math_mode", "synchronize",
+    "no_grad", "ones", "ones_like", "optim", "pinned", "rand", "randn", "set_math_mode", "synchronize",
     "tensor", "zeros", "zeros_like",
 ]

@@ -1012,6 +1012,81 @@ def pinned(array) -> np.ndarray:
 _PINNED_OWNERS: dict = {}
 
 
+class _RingStorage(Storage):
+    """A buffer of a Prefetcher ring: not owned; keeps the ring alive."""
+
+    __slots__ = ("ring",)
+
+    def __init__(self, ctx: Context, nbytes: int, ptr: int, ring: "Prefetcher"):
+        super().__init__(ctx, nbytes, ptr=ptr, owned=False)
+        self.ring = ring
+
+
+class Prefetcher:
+    """Uploads input batches on a copy stream beside the compute stream.
+
+    ``Prefetcher(*like, depth=2)`` sets up, for each array of a batch (shaped
+    and typed like ``like``), ``depth`` device buffers.  ``put(*arrays)`` copies
+    one batch into the next buffers and returns it as Tensors.  Work issued on
+    the device after ``put`` waits for the copy; the copy itself waits only for
+    the work that read the same buffers ``depth`` batches earlier.  So putting
+    batch i + 1 right after launching step i uploads it while step i runs.
+
+    Sources should be page-locked (``pinned``) for the copy to overlap, and must
+    stay alive and unchanged until the step that reads them has finished.  A
+    returned Tensor's contents are replaced ``depth`` puts later.
+    """
+
+    def __init__(self, *like, depth: int = 2, device: Optional[Device] = None):
+        if depth < 2:
+            raise ValueError("Prefetcher needs depth >= 2")
+        self._ctx = context(device)
+        self._rings: list = []
+        self._specs: list = []
+        for a in like:
+            a = np.asarray(a)
+            dtype = _dtype_of(a)
+            nbytes = a.size * _DTYPES[dtype][1]
+            h = C.c_void_p()
+            check(lib.tx_prefetch_create(self._ctx.handle, max(nbytes, 1), depth, C.byref(h)),
+                  self._ctx.handle, "prefetcher")
+            self._rings.append(h.value)
+            self._specs.append((a.shape, dtype, nbytes))
+
+    def put(self, *arrays) -> tuple:
+        if len(arrays) != len(self._specs):
+            raise ValueError(f"expected {len(self._specs)} arrays, got {len(arrays)}")
+        out = []
+        for ring, (shape, dtype, nbytes), a in zip(self._rings, self._specs, arrays):
+            if not isinstance(a, np.ndarray) or a.shape != shape or a.dtype != _DTYPES[dtype][0] \
+                    or not a.flags["C_CONTIGUOUS"]:
+                raise TypeError(f"put expects a C-contiguous {dtype} array of shape {shape}")
+            d = C.c_void_p()
+            check(lib.tx_prefetch_put(ring, a.ctypes.data, nbytes, C.byref(d)), self._ctx.handle,
+                  "prefetch")
+            out.append(Tensor._view(_RingStorage(self._ctx, nbytes, d.value, self), 0, shape, dtype))
+        return tuple(out)
+
+    def close(self) -> None:
+        for ring in self._rings:
+            lib.tx_prefetch_destroy(ring)
+        self._rings = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass
+
+
+def _dtype_of(array: np.ndarray) -> str:
+    if array.dtype == np.bool_:
+        return "bool"
+    if np.issubdtype(array.dtype, np.integer):
+        return "int64"
+    return "float32"
+
+
 def tensor(data, *, dtype: Optional[str] = None, device: Optional[Device] = None,
            requires_grad: bool = False) -> Tensor:
     return Tensor(data, dtype=dtype, device=device, requires_grad=requires_grad)
