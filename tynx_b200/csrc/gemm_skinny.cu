@@ -346,8 +346,10 @@ __global__ void __launch_bounds__(256) k_gemm_small_k2(const tx_gemm_desc d, int
 // part != nullptr: blockIdx.y is the K split and raw sums go to part[y][M][N].
 constexpr int SN_KC = 1024;
 
+// Two blocks per SM (at most 128 registers): the launch below sizes the grid
+// for two, and at 176 registers one fitted and the grid ran in two waves.
 template <int NN>
-__global__ void __launch_bounds__(256) k_gemm_small_n(const tx_gemm_desc d, int kc, float *part) {
+__global__ void __launch_bounds__(256, 2) k_gemm_small_n(const tx_gemm_desc d, int kc, float *part) {
   extern __shared__ __align__(16) float bsm[];
   const int64_t k0 = (int64_t)blockIdx.y * kc;
   const int klen = (int)(d.K - k0 < kc ? d.K - k0 : kc);
