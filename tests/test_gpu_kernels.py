@@ -332,6 +332,8 @@ def test_broadcast_binary_matches_numpy(tx, op, sa, sb):
     ((256, 128, 4, 64), (0, 2, 1, 3), np.float32),   # head split
     ((256, 4, 128, 64), (0, 2, 1, 3), np.float32),   # head merge
     ((512, 3, 33, 17), (0, 2, 3, 1), np.float32),    # NCHW -> NHWC, ragged
+    ((256, 128, 4, 64), (0, 2, 3, 1), np.float32),   # attention keys, (s, h*d) -> (h*d, s)
+    ((256, 4, 64, 128), (0, 3, 1, 2), np.float32),   # and back (their gradient)
     ((1000, 3), (1, 0), np.float32),
     ((64, 5, 8), (2, 0, 1), np.int64),
 ])

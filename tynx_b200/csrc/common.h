@@ -123,6 +123,9 @@ int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int
 // (not latched) for layouts that are not [outer, reduced, inner].
 int nd_binary(tx_ctx *ctx, int op, const float *A, const int64_t *sa, const float *B, const int64_t *sb,
               float *out, const int64_t *shape, int ndim);
+// out[b][c][r] (+)= in[b][r][c]: batched transpose of [R, Cc] fp32 matrices
+// through shared-memory tiles (engine.cu).
+int batched_transpose(tx_ctx *ctx, const float *in, float *out, int64_t B, int64_t R, int64_t Cc, int acc);
 int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const int64_t *shape, int ndim,
             int elem_bytes, float scale, int acc);
 int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_t *out_shape, int ndim,

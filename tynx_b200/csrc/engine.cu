@@ -308,6 +308,10 @@ int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g) 
 
 }  // namespace
 
+int batched_transpose(tx_ctx *ctx, const float *in, float *out, int64_t B, int64_t R, int64_t Cc, int acc) {
+  return transpose_b(ctx, in, out, B, R, Cc, nullptr, nullptr, TX_ACT_NONE, acc);
+}
+
 // ============================================================================
 // graph structures
 // ============================================================================

@@ -336,6 +336,19 @@ int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const in
     return launch_copy<int64_t>(ctx, (const int64_t *)src, (int64_t *)out, c, n, 1.f, 0, false);
   }
   if (elem_bytes != 4) return TX_ERR_INVALID;
+  // A copy that swaps the two inner merged axes of a contiguous [B][R][Cc]
+  // source into [B][Cc][R] (attention's key transpose and its gradient) is a
+  // batched matrix transpose: shared-memory tiles keep both sides coalesced
+  // (element-wise, one side is strided by a whole row).
+  if (scale == 1.f && (c.nd == 2 || c.nd == 3)) {
+    const int o = c.nd - 2;  // [B?, Cc, R] in destination order
+    const int64_t Cc = c.shape[o], R = c.shape[o + 1];
+    const bool inner_swap = c.st[0][o] == 1 && c.st[0][o + 1] == Cc;
+    const bool batch_ok = c.nd == 2 || c.st[0][0] == R * Cc;
+    const int64_t B = c.nd == 3 ? c.shape[0] : 1;
+    if (inner_swap && batch_ok && B <= 65535 && (R + 31) / 32 <= 65535)
+      return batched_transpose(ctx, (const float *)src, (float *)out, B, R, Cc, acc);
+  }
   const void *ptrs[2] = {src, out};
   const bool vec = vectorizable(c, 1, ptrs) && ((uintptr_t)out & 15) == 0;
   return launch_copy<float>(ctx, (const float *)src, (float *)out, c, n, scale, acc, vec);
