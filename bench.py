@@ -333,19 +333,21 @@ def main() -> None:
     roofline = gemm_roofline(tx, ctx, ext, wl, per_rank, args.math)
 
     # ---- end to end through the public API with host buffers -------------------------
-    # A Prefetcher uploads batch i + 1 on its copy stream while step i runs;
-    # every step still includes its own upload and the read-back of its loss.
+    # A Prefetcher uploads the next two batches on its copy stream while step i
+    # runs; every step still includes its own upload and the read-back of its loss.
     pinned = [tuple(tx.pinned(np.ascontiguousarray(a[rows], dtype=np.dtype(_np_dtype(dt))))
                     for a, dt in zip(h, dtypes)) for h in host[args.warmup:]]
-    prefetch = tx.Prefetcher(*pinned[0], depth=2)
+    prefetch = tx.Prefetcher(*pinned[0], depth=3)
     barrier()
     t0 = time.perf_counter()
     losses = []
-    inputs = prefetch.put(*pinned[0])
+    for i in range(min(2, args.steps)):
+        prefetch.put(*pinned[i])
     for i in range(args.steps):
+        inputs = prefetch.get()
         loss = train_step(*inputs)
-        if i + 1 < args.steps:
-            inputs = prefetch.put(*pinned[i + 1])
+        if i + 2 < args.steps:
+            prefetch.put(*pinned[i + 2])
         losses.append(loss.item())
     barrier()
     e2e_s = time.perf_counter() - t0

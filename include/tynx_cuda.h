@@ -102,17 +102,20 @@ int tx_host_alloc(size_t bytes, void **h_out); /* pinned host memory */
 /* Upload ring for input batches (no counterpart in the reference, which reads
  * its inputs from host memory on every step).  `depth` (2..16) device buffers
  * of `bytes` each and a copy stream beside the compute stream.
- * tx_prefetch_put copies `bytes` from h_src (pinned, for the copy to overlap)
- * into the next buffer and returns it: the copy waits only for the compute
- * work that read that buffer's previous batch (issued before the put after
- * that batch's), and all compute work issued after the put waits for the copy.
- * So with depth 2, putting batch i + 1 right after enqueuing step i uploads it
- * while step i runs.  A returned buffer is valid until `depth` more puts; h_src
- * must stay unchanged until the compute stream has passed the put.  Not
- * allowed during a capture. */
+ * tx_prefetch_put queues the copy of `bytes` from h_src (pinned, for the copy
+ * to overlap; unchanged until the copy has run) into the next buffer; it does
+ * not order the compute stream.  tx_prefetch_get returns the buffer of the
+ * oldest queued batch and orders all compute work issued after it behind that
+ * batch's copy.  A buffer is refilled only after the compute work issued
+ * before the get that followed its previous batch, so a batch returned by get
+ * stays valid until depth - 1 further gets.  With depth 3: put batches 0 and 1,
+ * then per step get, launch the step, put the batch two ahead, read the loss.
+ * put fails (TX_ERR_INVALID) when it would run more than depth - 1 batches
+ * ahead of get.  Neither call is allowed during a capture. */
 typedef struct tx_prefetch tx_prefetch;
 int tx_prefetch_create(tx_ctx *ctx, size_t bytes, int depth, tx_prefetch **out);
-int tx_prefetch_put(tx_prefetch *p, const void *h_src, size_t bytes, void **d_out);
+int tx_prefetch_put(tx_prefetch *p, const void *h_src, size_t bytes);
+int tx_prefetch_get(tx_prefetch *p, void **d_out);
 int tx_prefetch_destroy(tx_prefetch *p);
 int tx_host_free(void *h_ptr);
 /* Bytes currently held by the allocator (in use, cached). */

@@ -1,9 +1,10 @@
 """The input upload ring (``tx.Prefetcher``, C ABI ``tx_prefetch_*``).
 
-Batches put through the ring arrive intact; a buffer is not overwritten while
-compute work issued before a later put still has to read it (the copy stream
-runs beside the compute stream, so this is the ordering the ring must keep);
-and a model fed from the ring gives the same outputs as one fed through
+Batches queued through the ring arrive intact and in order; a buffer is not
+refilled while compute work issued before a later ``get`` still has to read
+it (the copy stream runs beside the compute stream, so this is the ordering
+the ring must keep); putting further ahead than the ring holds is refused; and
+a model fed from the ring gives the same outputs as one fed through
 ``tx.Tensor``.
 """
 
@@ -21,35 +22,60 @@ def _batches(n, rows=64, cols=33, seed=3):
              tx.pinned(rng.integers(0, 10, rows).astype(np.int64))) for _ in range(n)]
 
 
-def test_batches_arrive_intact():
+def test_batches_arrive_intact_and_in_order():
     import tynx_b200 as tx
 
-    host = _batches(5)
-    pf = tx.Prefetcher(*host[0], depth=2)
-    for x, y in host:
-        tx_x, tx_y = pf.put(x, y)
-        np.testing.assert_array_equal(tx_x.numpy(), x)
-        np.testing.assert_array_equal(tx_y.numpy(), y)
+    host = _batches(6)
+    pf = tx.Prefetcher(*host[0], depth=3)
+    pf.put(*host[0])
+    pf.put(*host[1])
+    for i in range(6):
+        tx_x, tx_y = pf.get()
+        if i + 2 < 6:
+            pf.put(*host[i + 2])
+        np.testing.assert_array_equal(tx_x.numpy(), host[i][0])
+        np.testing.assert_array_equal(tx_y.numpy(), host[i][1])
     pf.close()
 
 
-def test_buffer_reuse_waits_for_earlier_readers():
+def test_buffer_refill_waits_for_earlier_readers():
     import tynx_b200 as tx
 
-    host = _batches(3, rows=256, cols=256)
+    host = _batches(4, rows=256, cols=256)
     pf = tx.Prefetcher(*host[0], depth=2)
     a = tx.randn(4096, 4096)
-    x0, _ = pf.put(*host[0])
+    pf.put(*host[0])
+    x0, _ = pf.get()
     # a long product ahead of the read of batch 0 on the compute stream
     slow = tx.matmul(a, a)
     slow = tx.matmul(slow, a)
     s0 = (x0 * 1.0).sum()  # reads buffer 0 after the products
     pf.put(*host[1])
-    pf.put(*host[2])  # reuses buffer 0: must wait for the read above
+    pf.get()               # releases buffer 0: everything above was issued before it
+    pf.put(*host[2])       # refills buffer 0: must wait for the read above
     want = float(host[0][0].astype(np.float64).sum())
     got = float(s0.item())
     assert abs(got - want) <= 1e-3 * max(1.0, abs(want)), (got, want)
     assert np.isfinite(float(slow.sum().item()))
+    pf.close()
+
+
+def test_put_refuses_to_run_past_the_ring():
+    import tynx_b200 as tx
+
+    host = _batches(3)
+    pf = tx.Prefetcher(*host[0], depth=2)
+    pf.put(*host[0])
+    pf.put(*host[1])
+    with pytest.raises(Exception):
+        pf.put(*host[2])  # both buffers hold batches nobody has taken
+    pf.get()
+    with pytest.raises(Exception):
+        pf.put(*host[2])  # buffer 0's batch is taken but not yet released by a later get
+    pf.get()
+    pf.put(*host[2])
+    x, y = pf.get()
+    np.testing.assert_array_equal(x.numpy(), host[2][0])
     pf.close()
 
 
@@ -63,13 +89,15 @@ def test_model_outputs_match_plain_tensors():
     for step in range(4):
         b = wl.make_batch(step)
         host.append((tx.pinned(b["x"].astype(np.float32)), tx.pinned(b["y"].astype(np.int64))))
-    pf = tx.Prefetcher(*host[0], depth=2)
-    x, y = pf.put(*host[0])
+    pf = tx.Prefetcher(*host[0], depth=3)
+    pf.put(*host[0])
+    pf.put(*host[1])
     for i in range(4):
+        x, _ = pf.get()
         out = model(x).numpy()
+        if i + 2 < 4:
+            pf.put(*host[i + 2])
         ref = model(tx.Tensor(host[i][0])).numpy()
-        if i + 1 < 4:
-            x, y = pf.put(*host[i + 1])
         np.testing.assert_array_equal(out, ref)
     pf.close()
 

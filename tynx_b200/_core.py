@@ -1025,19 +1025,26 @@ class _RingStorage(Storage):
 class Prefetcher:
     """Uploads input batches on a copy stream beside the compute stream.
 
-    ``Prefetcher(*like, depth=2)`` sets up, for each array of a batch (shaped
-    and typed like ``like``), ``depth`` device buffers.  ``put(*arrays)`` copies
-    one batch into the next buffers and returns it as Tensors.  Work issued on
-    the device after ``put`` waits for the copy; the copy itself waits only for
-    the work that read the same buffers ``depth`` batches earlier.  So putting
-    batch i + 1 right after launching step i uploads it while step i runs.
+    ``Prefetcher(*like, depth=3)`` sets up, for each array of a batch (shaped
+    and typed like ``like``), ``depth`` device buffers.  ``put(*arrays)`` queues
+    one batch's upload and returns at once; ``get()`` returns the oldest queued
+    batch as Tensors, and device work issued after it waits for that upload.
+    A training loop keeps ``depth - 1`` batches in flight::
 
-    Sources should be page-locked (``pinned``) for the copy to overlap, and must
-    stay alive and unchanged until the step that reads them has finished.  A
-    returned Tensor's contents are replaced ``depth`` puts later.
+        pf.put(*batch[0]); pf.put(*batch[1])
+        for i in range(steps):
+            x, y = pf.get()
+            loss = step(x, y)
+            if i + 2 < steps:
+                pf.put(*batch[i + 2])
+            loss.item()
+
+    so the uploads run while the steps do.  Sources should be page-locked
+    (``pinned``) and must stay alive and unchanged until their upload has run;
+    a batch from ``get`` stays valid for ``depth - 1`` further gets.
     """
 
-    def __init__(self, *like, depth: int = 2, device: Optional[Device] = None):
+    def __init__(self, *like, depth: int = 3, device: Optional[Device] = None):
         if depth < 2:
             raise ValueError("Prefetcher needs depth >= 2")
         self._ctx = context(device)
@@ -1053,17 +1060,21 @@ class Prefetcher:
             self._rings.append(h.value)
             self._specs.append((a.shape, dtype, nbytes))
 
-    def put(self, *arrays) -> tuple:
+    def put(self, *arrays) -> None:
         if len(arrays) != len(self._specs):
             raise ValueError(f"expected {len(self._specs)} arrays, got {len(arrays)}")
-        out = []
-        for ring, (shape, dtype, nbytes), a in zip(self._rings, self._specs, arrays):
+        for (shape, dtype, _), a in zip(self._specs, arrays):
             if not isinstance(a, np.ndarray) or a.shape != shape or a.dtype != _DTYPES[dtype][0] \
                     or not a.flags["C_CONTIGUOUS"]:
                 raise TypeError(f"put expects a C-contiguous {dtype} array of shape {shape}")
+        for ring, (_, _, nbytes), a in zip(self._rings, self._specs, arrays):
+            check(lib.tx_prefetch_put(ring, a.ctypes.data, nbytes), self._ctx.handle, "prefetch put")
+
+    def get(self) -> tuple:
+        out = []
+        for ring, (shape, dtype, nbytes) in zip(self._rings, self._specs):
             d = C.c_void_p()
-            check(lib.tx_prefetch_put(ring, a.ctypes.data, nbytes, C.byref(d)), self._ctx.handle,
-                  "prefetch")
+            check(lib.tx_prefetch_get(ring, C.byref(d)), self._ctx.handle, "prefetch get")
             out.append(Tensor._view(_RingStorage(self._ctx, nbytes, d.value, self), 0, shape, dtype))
         return tuple(out)
 

@@ -118,7 +118,8 @@ SIGNATURES = {
     "tx_free": [_vp, _vp],
     "tx_h2d": [_vp, _vp, _vp, C.c_size_t],
     "tx_prefetch_create": [_vp, C.c_size_t, C.c_int, C.POINTER(_vp)],
-    "tx_prefetch_put": [_vp, _vp, C.c_size_t, C.POINTER(_vp)],
+    "tx_prefetch_put": [_vp, _vp, C.c_size_t],
+    "tx_prefetch_get": [_vp, C.POINTER(_vp)],
     "tx_prefetch_destroy": [_vp],
     "tx_d2h": [_vp, _vp, _vp, C.c_size_t],
     "tx_d2d": [_vp, _vp, _vp, C.c_size_t],
