@@ -133,6 +133,8 @@ int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_
 
 // LayerNorm forward; round_tf32 stores y rounded to TF32 (for an output that
 // only feeds contractions; the backward reads x, mean and rstd, not y).
+int softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows, int64_t cols, int log,
+                int acc, bool round);
 int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
                   float *rstd, int64_t rows, int64_t cols, float eps, bool round_tf32);
 

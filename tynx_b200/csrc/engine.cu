@@ -1703,8 +1703,22 @@ struct Bwd {
         float *t; int acc;
         TX_TRY(target(xv, &t, &acc));
         int64_t cols = y.back();
-        TX_TRY(tx_softmax_bwd(ctx, F(yv), dy, t, ny / cols, cols, d.op == TX_OP_LOGSOFTMAX, acc));
+        // In TF32 mode the gradient of attention scores is read only by the
+        // scores' own contraction (dgrad and wgrad operands, which round it):
+        // store it rounded so that they run without operand conversion.
+        bool rnd = false;
+        const GValue &xg = g->values[xv];
+        if (ctx->math == TX_MATH_TF32 && !acc && d.op == TX_OP_SOFTMAX && xg.kind == TX_VAL_ACT &&
+            !xg.is_output && xg.consumers.size() == 1 && xg.producer >= 0) {
+          const GNode &p = g->nodes[xg.producer];
+          const GNode *c = nullptr;
+          if (p.scaled_into >= 0) c = &g->nodes[p.scaled_into];
+          else if ((p.d.op == TX_OP_GEMM || p.d.op == TX_OP_MATMUL) && !p.fused_act) c = &p;
+          rnd = c && (c->d.op == TX_OP_GEMM || c->d.op == TX_OP_MATMUL) && !c->fused_act;
+        }
+        TX_TRY(softmax_bwd(ctx, F(yv), dy, t, ny / cols, cols, d.op == TX_OP_LOGSOFTMAX, acc, rnd));
         wrote(xv);
+        grad_tf32[xv] = rnd;
         return TX_OK;
       }
       case TX_OP_REDUCEMEAN: case TX_OP_REDUCESUM: case TX_OP_GAP: {

@@ -219,7 +219,7 @@ __global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y
 
 __global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restrict__ dy,
                               float *__restrict__ dx, int64_t rows, int64_t cols, int log_mode,
-                              int acc) {
+                              int acc, int round) {
   int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
   int lane = threadIdx.x & 31;
   for (int64_t r = blockIdx.x * (int64_t)(blockDim.x / kWarp) + threadIdx.x / kWarp; r < rows;
@@ -236,7 +236,8 @@ __global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restri
     s = warp_sum(s);
     for (int64_t c = lane; c < cols; c += kWarp) {
       float g = log_mode ? gr[c] - expf(yr[c]) * s : yr[c] * (gr[c] - s);
-      dr[c] = acc ? dr[c] + g : g;
+      g = acc ? dr[c] + g : g;
+      dr[c] = round ? tx_epi::round_tf32(g) : g;
     }
   }
 }
@@ -281,7 +282,7 @@ __global__ void k_softmax_fwd_v(const float *__restrict__ x, float *__restrict__
 
 template <int VPL>
 __global__ void k_softmax_bwd_v(const float *__restrict__ y, const float *__restrict__ dy, float *__restrict__ dx,
-                                int64_t rows, int log_mode, int acc) {
+                                int64_t rows, int log_mode, int acc, int round) {
   constexpr int cols = VPL * 128;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
@@ -316,6 +317,9 @@ __global__ void k_softmax_bwd_v(const float *__restrict__ y, const float *__rest
         o.z += p.z;
         o.w += p.w;
       }
+      if (round)
+        o = make_float4(tx_epi::round_tf32(o.x), tx_epi::round_tf32(o.y), tx_epi::round_tf32(o.z),
+                        tx_epi::round_tf32(o.w));
       dr[j * 32 + lane] = o;
     }
   }
@@ -1072,24 +1076,32 @@ extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t row
   return TX_OK;
 }
 
-extern "C" int tx_softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows,
-                              int64_t cols, int log, int acc) {
-  if (!ctx) return TX_ERR_INVALID;
+// round: store dx rounded to TF32 (for a gradient whose only readers are
+// contractions that would round it anyway)
+int softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows, int64_t cols, int log,
+                int acc, bool round) {
   if (rows <= 0 || cols <= 0) return TX_OK;
+  const int rt = round ? 1 : 0;
   if (ln_vec(cols, {y, dy, dx}) && (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
     const unsigned blocks = rows_grid(rows, 8);
     switch (cols) {
-      case 128: k_softmax_bwd_v<1><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
-      case 256: k_softmax_bwd_v<2><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
-      case 512: k_softmax_bwd_v<4><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
-      default: k_softmax_bwd_v<8><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc); break;
+      case 128: k_softmax_bwd_v<1><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc, rt); break;
+      case 256: k_softmax_bwd_v<2><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc, rt); break;
+      case 512: k_softmax_bwd_v<4><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc, rt); break;
+      default: k_softmax_bwd_v<8><<<blocks, 256, 0, ctx->stream>>>(y, dy, dx, rows, log, acc, rt); break;
     }
     TX_LAUNCHED(ctx, "k_softmax_bwd_v");
     return TX_OK;
   }
-  k_softmax_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(y, dy, dx, rows, cols, log, acc);
+  k_softmax_bwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(y, dy, dx, rows, cols, log, acc, rt);
   TX_LAUNCHED(ctx, "k_softmax_bwd");
   return TX_OK;
+}
+
+extern "C" int tx_softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows,
+                              int64_t cols, int log, int acc) {
+  if (!ctx) return TX_ERR_INVALID;
+  return softmax_bwd(ctx, y, dy, dx, rows, cols, log, acc, false);
 }
 
 extern "C" int tx_softmax_xent_fwd(tx_ctx *ctx, const float *z, const int64_t *labels, int64_t rows,
