@@ -202,6 +202,50 @@ __global__ void k_im2col_nhwc(const float *__restrict__ xh, float *__restrict__ 
   }
 }
 
+// im2col for channel counts that are not multiples of 4 (the 3-channel input
+// of a first convolution) and rows of at most 64 columns: each lane builds one
+// row (its index decomposed once, taps walked in order) in shared memory, then
+// the warp stores its 32 rows as one contiguous run.  The element-wise kernel
+// spends four integer divisions per element and stores with a row stride.
+constexpr int kIm2colRowsMaxLdk = 64;
+
+__global__ void __launch_bounds__(128) k_im2col_rows(const float *__restrict__ xh, float *__restrict__ cols,
+                                                     ConvGeom g, int64_t M, int round_tf32) {
+  __shared__ float sm[4][32 * (kIm2colRowsMaxLdk + 1)];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ld = g.ldk + 1;  // odd row stride: the lanes' rows fall in different banks
+  float *tile = sm[warp];
+  for (int64_t m0 = ((int64_t)blockIdx.x * 4 + warp) * 32; m0 < M; m0 += (int64_t)gridDim.x * 128) {
+    const int64_t m = m0 + lane;
+    if (m < M) {
+      float *row = tile + lane * ld;
+      const int64_t ow = m % g.OW, t = m / g.OW, oh = t % g.OH, n = t / g.OH;
+      int k = 0;
+      for (int kh = 0; kh < g.KH; ++kh) {
+        const int ih = (int)oh * g.sh - g.pt + kh * g.dh;
+        for (int kw = 0; kw < g.KW; ++kw) {
+          const int iw = (int)ow * g.sw - g.pl + kw * g.dw;
+          const bool in = ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+          const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.C;
+          for (int c = 0; c < g.C; ++c, ++k) {
+            const float v = in ? p[c] : 0.f;
+            row[k] = round_tf32 ? tx_epi::round_tf32(v) : v;
+          }
+        }
+      }
+      for (; k < g.ldk; ++k) row[k] = 0.f;  // padding columns
+    }
+    __syncwarp();
+    const int64_t nrows = M - m0 < 32 ? M - m0 : 32;
+    float *dst = cols + m0 * g.ldk;
+    for (int i = lane; i < nrows * g.ldk; i += 32) {
+      const int r = i / g.ldk, k = i - r * g.ldk;
+      dst[i] = tile[r * ld + k];
+    }
+    __syncwarp();
+  }
+}
+
 // dxh[n][ih][iw][c] = sum over the taps that read (ih, iw) of dcols[m][(kh*KW + kw)*C + c]
 // (gather form: each input element is written once, no atomics).
 template <int V>
@@ -284,6 +328,13 @@ ConvGeom conv_geom(const Shape &x, const Shape &w, const Shape &y, const tx_node
 int im2col_nhwc(tx_ctx *ctx, const float *xh, float *cols, const ConvGeom &g, bool round_tf32) {
   const int64_t M = (int64_t)g.N * g.OH * g.OW;
   const bool vec = g.C % 4 == 0;
+  if (!vec && g.ldk <= kIm2colRowsMaxLdk) {
+    int64_t blocks = (M + 127) / 128;
+    if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
+    k_im2col_rows<<<(unsigned)(blocks < 1 ? 1 : blocks), 128, 0, ctx->stream>>>(xh, cols, g, M, round_tf32);
+    TX_LAUNCHED(ctx, "k_im2col_rows");
+    return TX_OK;
+  }
   const int64_t units = M * g.ldk / (vec ? 4 : 1);
   if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "im2col too large");
   if (vec)
