@@ -248,10 +248,13 @@ __global__ void __launch_bounds__(128) k_im2col_rows(const float *__restrict__ x
 
 // dxh[n][ih][iw][c] = sum over the taps that read (ih, iw) of dcols[m][(kh*KW + kw)*C + c]
 // (gather form: each input element is written once, no atomics).
-template <int V>
+// S: the stride when both strides equal it (1 or 2: the tap tests become masks
+// and shifts instead of runtime divisions), 0 for any strides.
+template <int V, int S>
 __global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict__ dxh, ConvGeom g,
                               uint32_t units) {
   const uint32_t cv = (uint32_t)g.C / V;
+  const int sh = S ? S : g.sh, sw = S ? S : g.sw;
   for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
     const uint32_t pix = u / cv, c = (u - pix * cv) * V;
     const uint32_t iw = pix % g.W, t = pix / g.W, ih = t % g.H, n = t / g.H;
@@ -260,13 +263,13 @@ __global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict
     for (int j = 0; j < V; ++j) s[j] = 0.f;
     for (int kh = 0; kh < g.KH; ++kh) {
       const int a = (int)ih + g.pt - kh * g.dh;
-      if (a < 0 || a % g.sh) continue;
-      const int oh = a / g.sh;
+      if (a < 0 || a % sh) continue;
+      const int oh = a / sh;
       if (oh >= g.OH) continue;
       for (int kw = 0; kw < g.KW; ++kw) {
         const int b = (int)iw + g.pl - kw * g.dw;
-        if (b < 0 || b % g.sw) continue;
-        const int ow = b / g.sw;
+        if (b < 0 || b % sw) continue;
+        const int ow = b / sw;
         if (ow >= g.OW) continue;
         const float *p = dcols + (((int64_t)n * g.OH + oh) * g.OW + ow) * g.ldk + (kh * g.KW + kw) * g.C + c;
         if (V == 4) {
@@ -349,10 +352,17 @@ int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g) 
   const bool vec = g.C % 4 == 0 && g.ldk % 4 == 0;
   const int64_t units = (int64_t)g.N * g.H * g.W * g.C / (vec ? 4 : 1);
   if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "col2im too large");
-  if (vec)
-    k_col2im_nhwc<4><<<grid_for(units, 256), 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
-  else
-    k_col2im_nhwc<1><<<grid_for(units, 256), 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+  const int S = g.sh == g.sw && (g.sh == 1 || g.sh == 2) ? g.sh : 0;
+  const dim3 grid(grid_for(units, 256));
+  if (vec) {
+    if (S == 1) k_col2im_nhwc<4, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    else if (S == 2) k_col2im_nhwc<4, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    else k_col2im_nhwc<4, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+  } else {
+    if (S == 1) k_col2im_nhwc<1, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    else if (S == 2) k_col2im_nhwc<1, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    else k_col2im_nhwc<1, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+  }
   TX_LAUNCHED(ctx, "k_col2im_nhwc");
   return TX_OK;
 }

@@ -652,6 +652,12 @@ int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &desc, int64_t batch, FusedSu
 int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &desc, FusedSum *fs) {
   const int64_t batch = desc.batch > 1 ? desc.batch : 1;
   if (desc.K <= 0 || batch > 65535) return TX_ERR_UNSUPPORTED;
+  // A short-K product with a large output whose operands are already TF32
+  // values (a first convolution over im2col columns) runs on the tensor core
+  // (persistent, no operand conversion) instead: its output dominates.
+  if (desc.K <= SK_KMAX && desc.K >= 16 && batch == 1 && !fs && desc.M >= 65536 && desc.N >= 32 &&
+      (desc.flags & TX_GEMM_A_TF32) && (desc.flags & TX_GEMM_B_TF32))
+    return TX_ERR_UNSUPPORTED;
   if (desc.K <= SK_KMAX) {
     if (desc.N <= 32) return launch_small_k<32>(ctx, desc, batch, fs);
     if (desc.N <= 64) return launch_small_k<64>(ctx, desc, batch, fs);
