@@ -23,6 +23,10 @@ struct Nd {
   int nd;
   int64_t shape[kNd];   // outermost first
   int64_t st[3][kNd];   // element strides of up to three operands
+  // ceil(2^64 / shape[k]) (0 for an extent of 1): for a 32-bit index x,
+  // x / shape[k] = mulhi64(x, rcp[k]) exactly (the error of the product is
+  // below 2^-32 < 1 / shape[k]), a few instructions instead of a division
+  uint64_t rcp[kNd];
 };
 
 // Drop size-1 axes and merge adjacent axes that are contiguous in every operand.
@@ -53,6 +57,7 @@ void canonicalize(int nd, const int64_t *shape, const int64_t *const *strides, i
   for (int i = 0; i < m; ++i) {
     c.shape[i] = sh[m - 1 - i];
     for (int o = 0; o < nops; ++o) c.st[o][i] = s[o][m - 1 - i];
+    c.rcp[i] = c.shape[i] >= 2 ? ~uint64_t(0) / (uint64_t)c.shape[i] + 1 : 0;
   }
 }
 
@@ -93,7 +98,11 @@ __device__ __forceinline__ void offsets(const Nd &c, I i, int64_t (&off)[NOPS]) 
   for (int o = 0; o < NOPS; ++o) off[o] = 0;
   for (int k = c.nd - 1; k >= 0; --k) {
     const I ext = (I)c.shape[k];
-    const I q = i / ext;
+    I q;
+    if constexpr (sizeof(I) == 4)
+      q = c.rcp[k] ? (I)__umul64hi((uint64_t)i, c.rcp[k]) : i;
+    else
+      q = i / ext;
     const I r = i - q * ext;
     i = q;
 #pragma unroll
