@@ -405,6 +405,13 @@ struct GNode {
   float out_scale = 1.f;
   int scale_out = -1;
   int scaled_into = -1;
+  // Conv -> Conv: the producer's (activated) output feeds only the consumer's
+  // input, so it stays channels-last in HBM ([N][H][W][C], in the value's
+  // buffer): the producer skips its output transpose and the consumer its
+  // input transpose; in the backward the consumer's dX is written
+  // channels-last and the producer applies act' elementwise
+  bool nhwc_out = false;
+  bool nhwc_in = false;
 };
 
 struct tx_graph {
@@ -721,6 +728,20 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     a.fused_into = i;
   }
 
+  // ---- channels-last hand-off between consecutive convolutions --------------------------------
+  for (int i = 0; i < n_nodes; ++i) {
+    GNode &n = g->nodes[i];
+    if (n.d.op != TX_OP_CONV) continue;
+    const int yv = n.fused_act ? n.fused_out : n.d.out[0];
+    const GValue &y = g->values[yv];
+    if (y.is_output || y.consumers.size() != 1) continue;
+    GNode &c = g->nodes[y.consumers[0]];
+    if (c.d.op != TX_OP_CONV || c.d.in[0] != yv || c.d.in[1] == yv || (c.d.n_in > 2 && c.d.in[2] == yv))
+      continue;
+    n.nhwc_out = true;
+    c.nhwc_in = true;
+  }
+
   // ---- scalar scale folded into the producing contraction -------------------------------------
   for (int i = 0; i < n_nodes; ++i) {
     GNode &n = g->nodes[i];
@@ -1029,16 +1050,20 @@ struct Fwd {
     const bool tf32 = ctx->math == TX_MATH_TF32;
     // channels-last input, (kh, kw, c) columns, weights permuted to match;
     // in TF32 mode both operands are stored rounded, so the GEMM reads them as is
-    Scratch xh(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
-        tmp(ctx, (size_t)M * OC * 4);
+    Scratch xh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
+        tmp(ctx, n.nhwc_out ? 0 : (size_t)M * OC * 4);
     float *cols = (float *)tx_alloc_raw(ctx, (size_t)M * cg.ldk * 4);
-    if (!xh.ptr || !wk.ptr || !tmp.ptr || !cols) {
+    if ((!n.nhwc_in && !xh.ptr) || !wk.ptr || (!n.nhwc_out && !tmp.ptr) || !cols) {
       tx_free_raw(ctx, cols);
       return TX_ERR_OOM;
     }
     r->extra[ni] = cols;  // saved for wgrad
-    TX_TRY(transpose_b(ctx, F(d.in[0]), xh.as<float>(), cg.N, cg.C, (int64_t)cg.H * cg.W));
-    TX_TRY(im2col_nhwc(ctx, xh.as<float>(), cols, cg, tf32));
+    const float *xin = F(d.in[0]);  // channels-last already when the producer kept it so
+    if (!n.nhwc_in) {
+      TX_TRY(transpose_b(ctx, F(d.in[0]), xh.as<float>(), cg.N, cg.C, (int64_t)cg.H * cg.W));
+      xin = xh.as<float>();
+    }
+    TX_TRY(im2col_nhwc(ctx, xin, cols, cg, tf32));
     k_weight_to_khwc<<<grid_for(OC * cg.ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
                                                                          cg.C, cg.KH, cg.KW, cg.ldk, tf32);
     TX_LAUNCHED(ctx, "k_weight_to_khwc");
@@ -1047,7 +1072,7 @@ struct Fwd {
     q.M = M; q.N = OC; q.K = cg.ldk;
     q.A = cols; q.lda = cg.ldk; q.trans_a = 0;
     q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 1;
-    q.C = tmp.as<float>(); q.ldc = OC; q.alpha = 1.f; q.batch = 1;
+    q.C = n.nhwc_out ? F(yv) : tmp.as<float>(); q.ldc = OC; q.alpha = 1.f; q.batch = 1;
     if (d.n_in > 2 && d.in[2] >= 0) {
       q.bias = F(d.in[2]);
       q.bias_scale = 1.f;
@@ -1055,6 +1080,7 @@ struct Fwd {
     q.act = n.fused_act;
     q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : 0;
     TX_TRY(gemm_dispatch(ctx, q));
+    if (n.nhwc_out) return TX_OK;  // the next convolution reads [N][OH][OW][OC]
     return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);
   }
 
@@ -1520,12 +1546,22 @@ struct Bwd {
     const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
     const int64_t K = (int64_t)cg.KH * cg.KW * cg.C;
     const bool tf32 = ctx->math == TX_MATH_TF32;
-    // dY (NCHW) -> [M, OC]; a fused activation's derivative is applied on the way
+    // dY (NCHW) -> [M, OC]; a fused activation's derivative is applied on the
+    // way.  A channels-last output got its dY channels-last from the next
+    // convolution: act' is then elementwise against the channels-last output.
     Scratch dyt(ctx, (size_t)M * OC * 4);
     if (!dyt.ptr) return TX_ERR_OOM;
     const bool apply_dact = n.fused_act && !grad_preact[yv];
-    TX_TRY(transpose_b(ctx, dy, dyt.as<float>(), cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
-                       apply_dact ? F(yv) : nullptr, apply_dact ? n.fused_act : TX_ACT_NONE));
+    if (n.nhwc_out) {
+      if (apply_dact)
+        TX_TRY(tx_unary_bwd(ctx, n.fused_act == TX_ACT_RELU ? TX_UN_RELU : TX_UN_TANH, F(yv), dy, dyt.as<float>(),
+                            M * OC, 0.f, 0.f, 0));
+      else
+        TX_TRY(tx_d2d(ctx, dyt.as<float>(), dy, (size_t)M * OC * 4));
+    } else {
+      TX_TRY(transpose_b(ctx, dy, dyt.as<float>(), cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
+                         apply_dact ? F(yv) : nullptr, apply_dact ? n.fused_act : TX_ACT_NONE));
+    }
     if (d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
       float *t; int acc;
       TX_TRY(target(d.in[2], &t, &acc));
@@ -1565,9 +1601,17 @@ struct Bwd {
       q.C = dcols.as<float>(); q.ldc = cg.ldk;
       q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
       TX_TRY(gemm_dispatch(ctx, q));
-      TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
-      TX_TRY(transpose_b(ctx, dxh.as<float>(), t, cg.N, (int64_t)cg.H * cg.W, cg.C, nullptr, nullptr,
-                         TX_ACT_NONE, acc));
+      if (n.nhwc_in && !acc) {
+        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), t, cg));  // the producer reads dX channels-last
+      } else if (n.nhwc_in) {
+        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
+        const int64_t nx = (int64_t)cg.N * cg.H * cg.W * cg.C, one = 1;
+        TX_TRY(nd_copy(ctx, dxh.as<float>(), &one, t, &nx, 1, 4, 1.f, acc));
+      } else {
+        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
+        TX_TRY(transpose_b(ctx, dxh.as<float>(), t, cg.N, (int64_t)cg.H * cg.W, cg.C, nullptr, nullptr,
+                           TX_ACT_NONE, acc));
+      }
       wrote(d.in[0]);
     }
     return TX_OK;
