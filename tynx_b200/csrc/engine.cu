@@ -250,9 +250,12 @@ __global__ void __launch_bounds__(128) k_im2col_rows(const float *__restrict__ x
 // (gather form: each input element is written once, no atomics).
 // S: the stride when both strides equal it (1 or 2: the tap tests become masks
 // and shifts instead of runtime divisions), 0 for any strides.
+// act_src (or null): multiply each sum by act'(act_src) at the same index
+// (the derivative of the activation fused into the convolution that produced
+// a channels-last input).
 template <int V, int S>
 __global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict__ dxh, ConvGeom g,
-                              uint32_t units) {
+                              uint32_t units, const float *__restrict__ act_src, int act) {
   const uint32_t cv = (uint32_t)g.C / V;
   const int sh = S ? S : g.sh, sw = S ? S : g.sw;
   for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
@@ -282,6 +285,11 @@ __global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict
           s[0] += *p;
         }
       }
+    }
+    if (act_src) {
+      const float *a = act_src + (int64_t)u * V;
+#pragma unroll
+      for (int j = 0; j < V; ++j) s[j] *= tx_epi::dact(act, a[j]);
     }
     float *o = dxh + (int64_t)u * V;
     if (V == 4)
@@ -348,20 +356,21 @@ int im2col_nhwc(tx_ctx *ctx, const float *xh, float *cols, const ConvGeom &g, bo
   return TX_OK;
 }
 
-int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g) {
+int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g, const float *act_src = nullptr,
+                int act = TX_ACT_NONE) {
   const bool vec = g.C % 4 == 0 && g.ldk % 4 == 0;
   const int64_t units = (int64_t)g.N * g.H * g.W * g.C / (vec ? 4 : 1);
   if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "col2im too large");
   const int S = g.sh == g.sw && (g.sh == 1 || g.sh == 2) ? g.sh : 0;
   const dim3 grid(grid_for(units, 256));
   if (vec) {
-    if (S == 1) k_col2im_nhwc<4, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
-    else if (S == 2) k_col2im_nhwc<4, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
-    else k_col2im_nhwc<4, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    if (S == 1) k_col2im_nhwc<4, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
+    else if (S == 2) k_col2im_nhwc<4, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
+    else k_col2im_nhwc<4, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
   } else {
-    if (S == 1) k_col2im_nhwc<1, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
-    else if (S == 2) k_col2im_nhwc<1, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
-    else k_col2im_nhwc<1, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units);
+    if (S == 1) k_col2im_nhwc<1, 1><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
+    else if (S == 2) k_col2im_nhwc<1, 2><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
+    else k_col2im_nhwc<1, 0><<<grid, 256, 0, ctx->stream>>>(dcols, dxh, g, (uint32_t)units, act_src, act);
   }
   TX_LAUNCHED(ctx, "k_col2im_nhwc");
   return TX_OK;
@@ -1549,23 +1558,24 @@ struct Bwd {
     // dY (NCHW) -> [M, OC]; a fused activation's derivative is applied on the
     // way.  A channels-last output got its dY channels-last from the next
     // convolution: act' is then elementwise against the channels-last output.
-    Scratch dyt(ctx, (size_t)M * OC * 4);
-    if (!dyt.ptr) return TX_ERR_OOM;
     const bool apply_dact = n.fused_act && !grad_preact[yv];
-    if (n.nhwc_out) {
-      if (apply_dact)
-        TX_TRY(tx_unary_bwd(ctx, n.fused_act == TX_ACT_RELU ? TX_UN_RELU : TX_UN_TANH, F(yv), dy, dyt.as<float>(),
-                            M * OC, 0.f, 0.f, 0));
-      else
-        TX_TRY(tx_d2d(ctx, dyt.as<float>(), dy, (size_t)M * OC * 4));
+    // a channels-last dY whose act' the next convolution applied is used as is
+    const bool dy_ready = n.nhwc_out && !apply_dact;
+    Scratch dyt(ctx, dy_ready ? 0 : (size_t)M * OC * 4);
+    if (!dy_ready && !dyt.ptr) return TX_ERR_OOM;
+    float *dz = dy_ready ? dy : dyt.as<float>();
+    if (dy_ready) {
+    } else if (n.nhwc_out) {
+      TX_TRY(tx_unary_bwd(ctx, n.fused_act == TX_ACT_RELU ? TX_UN_RELU : TX_UN_TANH, F(yv), dy, dz, M * OC, 0.f,
+                          0.f, 0));
     } else {
-      TX_TRY(transpose_b(ctx, dy, dyt.as<float>(), cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
+      TX_TRY(transpose_b(ctx, dy, dz, cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
                          apply_dact ? F(yv) : nullptr, apply_dact ? n.fused_act : TX_ACT_NONE));
     }
     if (d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
       float *t; int acc;
       TX_TRY(target(d.in[2], &t, &acc));
-      TX_TRY(tx_bias_grad(ctx, dyt.as<float>(), t, M, OC, 1.f, acc));
+      TX_TRY(tx_bias_grad(ctx, dz, t, M, OC, 1.f, acc));
       wrote(d.in[2]);
     }
     if (needs[d.in[1]]) {  // dW_khwc[OC, ldk] = dY^T cols, then back to [OC, C, KH, KW]
@@ -1575,7 +1585,7 @@ struct Bwd {
       if (!dwk.ptr) return TX_ERR_OOM;
       tx_gemm_desc q; memset(&q, 0, sizeof q);
       q.M = OC; q.N = cg.ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
-      q.A = dyt.as<float>(); q.lda = OC; q.trans_a = 1;
+      q.A = dz; q.lda = OC; q.trans_a = 1;
       q.B = (const float *)r->extra[ni]; q.ldb = cg.ldk; q.trans_b = 0;
       q.C = dwk.as<float>(); q.ldc = cg.ldk;
       q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
@@ -1596,13 +1606,23 @@ struct Bwd {
       TX_LAUNCHED(ctx, "k_weight_to_khwc");
       tx_gemm_desc q; memset(&q, 0, sizeof q);
       q.M = M; q.N = cg.ldk; q.K = OC; q.alpha = 1.f; q.batch = 1;
-      q.A = dyt.as<float>(); q.lda = OC; q.trans_a = 0;
+      q.A = dz; q.lda = OC; q.trans_a = 0;
       q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 0;
       q.C = dcols.as<float>(); q.ldc = cg.ldk;
       q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
       TX_TRY(gemm_dispatch(ctx, q));
       if (n.nhwc_in && !acc) {
-        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), t, cg));  // the producer reads dX channels-last
+        // the producer reads dX channels-last; its fused activation's
+        // derivative is applied here, against its channels-last output
+        const int xv = d.in[0];
+        const GValue &xg = g->values[xv];
+        int pc = xg.producer;
+        if (pc >= 0 && g->nodes[pc].fused_into >= 0) pc = g->nodes[pc].fused_into;
+        const GNode *pn = pc >= 0 ? &g->nodes[pc] : nullptr;
+        const bool fuse = pn && pn->d.op == TX_OP_CONV && pn->nhwc_out && pn->fused_act &&
+                          (pn->fused_act == TX_ACT_RELU || pn->fused_act == TX_ACT_TANH) && pn->fused_out == xv;
+        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), t, cg, fuse ? F(xv) : nullptr, fuse ? pn->fused_act : TX_ACT_NONE));
+        if (fuse) grad_preact[xv] = true;
       } else if (n.nhwc_in) {
         TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
         const int64_t nx = (int64_t)cg.N * cg.H * cg.W * cg.C, one = 1;
