@@ -397,6 +397,11 @@ struct GValue {
   int producer = -1;
   bool is_output = false;
   int input_index = -1;
+  // TF32 mode: this value's gradient is written once, by a contraction of its
+  // sole consumer, and read only as a contraction operand (by its producing
+  // MatMul, directly or through reshapes and transposes), so the contraction
+  // that writes it may store it rounded; set at graph creation
+  bool grad_round = false;
 };
 
 struct GNode {
@@ -801,6 +806,38 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
       n.round_out = feeds_only_contractions(n.d.out[0], 0);
     }
   }
+  // ---- TF32 gradient rounding: gradients whose every reader is a contraction -----------------
+  // The gradient of v is read by the backward of v's producer: a MatMul (no
+  // fused activation, no bias) reads it only as an operand of its dgrad and
+  // wgrad; a reshape or a transpose copies it unchanged to its own input's
+  // gradient.  v must have one consumer that reads it once, so that its
+  // gradient has one writer and is never summed.
+  std::function<bool(int, int)> grad_feeds_only_contractions = [&](int v, int depth) -> bool {
+    const GValue &gv = g->values[v];
+    if (gv.kind != TX_VAL_ACT || gv.is_output || gv.producer < 0 || gv.consumers.size() != 1 || depth > 8)
+      return false;
+    const tx_node_desc &cd = g->nodes[gv.consumers[0]].d;
+    int reads = 0;
+    for (int k = 0; k < cd.n_in; ++k) reads += cd.in[k] == v;
+    if (reads != 1) return false;
+    // a contraction whose backward reads dY only as a dgrad / wgrad operand
+    auto plain = [](const GNode &n) {
+      return !n.fused_act && (n.d.op == TX_OP_MATMUL ||
+                              (n.d.op == TX_OP_GEMM && (n.d.n_in <= 2 || n.d.in[2] < 0)));
+    };
+    const GNode &p = g->nodes[gv.producer];
+    if (p.fused_into >= 0) return false;  // act' is applied elementwise to this gradient
+    if (p.scaled_into >= 0) {             // the gradient of a folded scale's output
+      const GNode &m = g->nodes[p.scaled_into];
+      return m.scale_out == v && plain(m);
+    }
+    if (p.d.op == TX_OP_MATMUL || p.d.op == TX_OP_GEMM) return p.d.out[0] == v && p.scale_out < 0 && plain(p);
+    if (is_alias_op(p.d.op) || p.d.op == TX_OP_TRANSPOSE)
+      return p.d.out[0] == v && grad_feeds_only_contractions(p.d.in[0], depth + 1);
+    return false;
+  };
+  for (int v = 0; v < (int)g->values.size(); ++v) g->values[v].grad_round = grad_feeds_only_contractions(v, 0);
+
   g->input_round.assign(g->inputs.size(), false);
   for (size_t i = 0; i < g->inputs.size(); ++i)
     g->input_round[i] = g->values[g->inputs[i]].dtype == TX_DT_F32 &&
@@ -1420,8 +1457,13 @@ struct Bwd {
           q.C = t; q.ldc = K;
           q.flags = (x32 ? TX_GEMM_B_TF32 : 0) | (dz32 ? TX_GEMM_A_TF32 : 0);
         }
-        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
-        if (rc == TX_OK) wrote(d.in[1]);
+        round_grad(d.in[1], q);
+        bool rounded = false;
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
+        if (rc == TX_OK) {
+          grad_tf32[d.in[1]] = rounded;
+          wrote(d.in[1]);
+        }
       }
       // dA
       if (rc == TX_OK && needs[d.in[0]]) {
@@ -1446,6 +1488,7 @@ struct Bwd {
           q.C = t; q.ldc = M;
           q.flags = (w32 ? TX_GEMM_A_TF32 : 0) | (dz32 ? TX_GEMM_B_TF32 : 0);
         }
+        round_grad(d.in[0], q);
         bool rounded = false;
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
         if (rc == TX_OK) {
@@ -1469,8 +1512,13 @@ struct Bwd {
         q.flags = (x32 ? TX_GEMM_A_TF32 : 0) | (dz32 ? TX_GEMM_B_TF32 : 0);
         q.B = dz; q.ldb = N; q.trans_b = 0; q.stride_b = M * N;
         q.C = t; q.ldc = N; q.stride_c = K * N;
-        if (rc == TX_OK) rc = gemm_dispatch(ctx, q);
-        if (rc == TX_OK) wrote(d.in[1]);
+        round_grad(d.in[1], q);
+        bool rounded = false;
+        if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
+        if (rc == TX_OK) {
+          grad_tf32[d.in[1]] = rounded;
+          wrote(d.in[1]);
+        }
       }
       if (rc == TX_OK && needs[d.in[0]]) {  // dA = dY B^T
         float *t; int acc;
@@ -1485,6 +1533,7 @@ struct Bwd {
         q.C = t; q.ldc = K; q.stride_c = M * K;
         if (weight2d) { q.M = M; q.batch = 1; }
         const int fused_node = fuse_dact(d.in[0], q);
+        round_grad(d.in[0], q);
         bool rounded = false;
         if (rc == TX_OK) rc = gemm_dispatch(ctx, q, &rounded);
         if (rc == TX_OK) {
@@ -1498,6 +1547,14 @@ struct Bwd {
   }
 
   int dgrad_target(int v, float **t, int *acc) { return target(v, t, acc); }
+
+  // TF32 mode: a gradient that only contractions read (GValue::grad_round) is
+  // stored rounded by the contraction that writes it, as those readers would
+  // round it anyway; recorded in grad_tf32 from what gemm_dispatch reports
+  void round_grad(int v, tx_gemm_desc &q) {
+    if (ctx->math == TX_MATH_TF32 && q.beta == 0.f && !q.dact && !q.colsum && g->values[v].grad_round)
+      q.flags |= TX_GEMM_ROUND_OUT;
+  }
 
   // If v is the (sole-consumer) output of a fused Gemm+act, fold act' into this
   // dgrad epilogue so the producer receives its pre-activation gradient dZ.
@@ -1696,6 +1753,7 @@ struct Bwd {
         grad_owned[xv] = true;
         grad_owned[yv] = false;
         grad_preact[xv] = grad_preact[yv];
+        grad_tf32[xv] = grad_tf32[yv] && gx.grad_round;  // nothing else will add to it
         wrote(xv);
         return TX_OK;
       }
@@ -1707,6 +1765,7 @@ struct Bwd {
       } else {
         TX_TRY(tx_d2d(ctx, t, dy, ny * 4));
       }
+      grad_tf32[xv] = !acc && grad_tf32[yv] && gx.grad_round;
       wrote(xv);
       return TX_OK;
     }
@@ -1883,6 +1942,8 @@ struct Bwd {
         }
         float *t; int acc;
         TX_TRY(target(xv, &t, &acc));
+        // a transpose moves values unchanged; the flag passes on where nothing else adds to dX
+        grad_tf32[xv] = !acc && grad_tf32[yv] && g->values[xv].grad_round;
         if (!acc) {
           TX_TRY(tx_strided_copy(ctx, dy, ss, t, x.data(), nd, 4));
         } else {
