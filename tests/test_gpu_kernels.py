@@ -282,6 +282,60 @@ def test_fused_column_sums(tx, M, N, K, ta, tb, dact, acc):
     assert (got == ref).all() or (got.view(np.uint32) == _np_round_tf32(ref).view(np.uint32)).all()
 
 
+@pytest.mark.parametrize("tb", [0, 1])
+@pytest.mark.parametrize("kind", ["gelu", "gelu_dgrad"])
+def test_persistent_gelu_epilogue(tx, kind, tb):
+    """More 128 x 256 tiles than SMs and operands already TF32: the persistent
+    kernel, whose GELU / GELU' epilogue is shared by eight warps (two per TMEM
+    lane quadrant, alternate 32-column chunks).  Against float64 on the same
+    operands: C, the stored pre-activation, and the fused column sums of C."""
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N_
+
+    M, Nn, K = 8192, 1024, 256
+    rng = np.random.default_rng(17 + tb)
+    A = _np_round_tf32(rng.standard_normal((M, K)).astype(np.float32))
+    B = _np_round_tf32((rng.standard_normal((Nn, K) if tb else (K, Nn)) * 0.1).astype(np.float32))
+    S = rng.standard_normal((M, Nn)).astype(np.float32)
+    bias = rng.standard_normal(Nn).astype(np.float32)
+    prior = rng.standard_normal(Nn).astype(np.float32)
+    ctx = _core.context()
+    ctx.math = "tf32"
+    a, b, s, bb, cs = (tx.Tensor(v) for v in (A, B, S, bias, prior))
+    c, p = tx.zeros(M, Nn), tx.zeros(M, Nn)
+    d = N_.GemmDesc()
+    d.M, d.N, d.K = M, Nn, K
+    d.A, d.lda, d.trans_a = a.ptr, K, 0
+    d.B, d.ldb, d.trans_b = b.ptr, B.shape[1], tb
+    d.C, d.ldc = c.ptr, Nn
+    d.alpha, d.batch = 0.5, 1
+    d.flags = N_.TX_GEMM_A_TF32 | N_.TX_GEMM_B_TF32
+    if kind == "gelu":
+        d.bias, d.bias_scale, d.act = bb.ptr, 1.0, N_.ACT["gelu"]
+        d.preact, d.ld_preact = p.ptr, Nn
+    else:
+        d.dact_src, d.ld_dact, d.dact = s.ptr, Nn, N_.ACT["gelu"]
+        d.colsum, d.colsum_scale, d.colsum_acc = cs.ptr, 0.25, 1
+        d.flags |= N_.TX_GEMM_ROUND_OUT
+    ctx.check(N_.lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
+    got = c.numpy()
+    prod = A.astype(np.float64) @ (B.T if tb else B).astype(np.float64)
+    if kind == "gelu":
+        pre = 0.5 * prod + bias
+        want = _np_act("gelu", pre)
+        scale = float(np.abs(pre).max())
+        assert float(np.abs(got - want).max()) < 1e-5 * scale
+        assert float(np.abs(p.numpy() - pre).max()) < 1e-5 * scale
+    else:
+        want = 0.5 * prod * _np_dact("gelu", S.astype(np.float64))
+        scale = float(np.abs(want).max())
+        # C stored TF32-rounded: half a TF32 unit of each value on top
+        assert (np.abs(got - want) <= 1e-5 * scale + np.abs(want) * 2.0 ** -11).all()
+        np.testing.assert_array_equal(got.view(np.uint32), _np_round_tf32(got).view(np.uint32))
+        want_cs = 0.25 * want.sum(axis=0) + prior
+        assert float(np.abs(cs.numpy() - want_cs).max()) <= 1e-5 * float(np.abs(want).sum(axis=0).max())
+
+
 def _strides(shape):
     st, acc = [], 1
     for e in reversed(shape):

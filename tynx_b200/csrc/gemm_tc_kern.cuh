@@ -2,7 +2,7 @@
 // tcgen05 / TMEM / TMA fp32 contraction for sm_100a (kind::tf32).
 //
 // One CTA computes a 128 x BN tile of C.  Warp roles (320 threads in the
-// one-tile kernel, 192 in the persistent one):
+// one-tile kernel, 192 or 320 in the persistent one):
 //   warp 0      TMA producer: loads 128x32 A and BNx32 B fp32 tiles per stage
 //               into a STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM (BN fp32 columns x 128 lanes) and, from one
@@ -10,7 +10,8 @@
 //               4 per stage), committing each stage back to the producer;
 //   warps 2..5  operand conversion during the main loop (see MODE);
 //   warps 2..9  the epilogue, two warps per TMEM lane quadrant (warps 2..5 in
-//               the persistent kernel): tcgen05.ld the accumulator, apply
+//               the persistent kernel unless its epilogue is a GELU or GELU'):
+//               tcgen05.ld the accumulator, apply
 //               alpha / bias / beta*C / activation / act', and store each
 //               32x32 chunk through swizzled shared memory by TMA.
 // MODE selects how fp32 operands become TF32:
@@ -990,8 +991,11 @@ __global__ void __launch_bounds__(320, 1)
 // MMA warp fills one while the epilogue warps drain the other.  The epilogue
 // has its own shared memory (the stages stay busy): per warp two output tiles
 // plus two pre-activation, act'-source and C tiles when the GEMM uses them.
+// EW epilogue warps: 4 (one per TMEM lane quadrant), or 8 for epilogues whose
+// arithmetic outweighs a tile's main loop (GELU and its derivative): two warps
+// per quadrant then take alternate 32-column chunks.
 constexpr int kSmemMax = 232448;  // 227 KB opt-in
-constexpr int kPTail = 2048;  // barriers, then each epilogue warp's 32 bias values
+constexpr int kPTail = 2048;  // barriers, then each epilogue warp's 32 bias values (8 warps at most)
 
 template <int BN>
 struct PCfg {
@@ -1011,8 +1015,8 @@ struct PWork {
   float *col_part;       // fused column sums (one row per 32 output rows) or null
 };
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, bool A_MN, bool B_MN, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
                const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, PWork w) {
@@ -1023,15 +1027,16 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int stages = w.stages;
   uint8_t *ep = smem + stages * Cfg::STAGE;
-  uint8_t *tail = ep + 4 * w.ep_stride;
+  static_assert(EW == 4 || EW == 8, "one or two epilogue warps per TMEM lane quadrant");
+  uint8_t *tail = ep + EW * w.ep_stride;
   uint64_t *full = (uint64_t *)tail;
   uint64_t *empty = full + 8;
   uint64_t *tfull = empty + 8;
   uint64_t *tempty = tfull + 2;
   uint64_t *ebar = tempty + 2;
-  uint32_t *tmem_holder = (uint32_t *)(ebar + 8);
+  uint32_t *tmem_holder = (uint32_t *)(ebar + 2 * EW);
   volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
-  float *bias_rows = reinterpret_cast<float *>(tail + 1024);  // [4][32]
+  float *bias_rows = reinterpret_cast<float *>(tail + 1024);  // [EW][32]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1044,9 +1049,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty[b], EW);  // one arrival per epilogue warp
     }
-    for (int i = 0; i < 8; ++i) mbar_init(&ebar[i], 1);
+    for (int i = 0; i < 2 * EW; ++i) mbar_init(&ebar[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1140,8 +1145,11 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    const int quad = warp & 3;
-    uint8_t *eb = ep + quad * w.ep_stride;
+    const int ew = warp - 2;        // 0 .. EW-1
+    const int quad = warp & 3;      // the TMEM lane quadrant this warp may read
+    const int c0 = ew >> 2;         // first chunk; then every cstep-th
+    constexpr int cstep = EW / 4;
+    uint8_t *eb = ep + ew * w.ep_stride;
     EpiWarp<2> e;
     e.need_s = d.dact != TX_ACT_NONE;
     e.need_c = d.beta != 0.f;
@@ -1151,12 +1159,12 @@ __global__ void __launch_bounds__(192, 1)
     e.pre_t = eb + 8192;
     e.s_t = e.pre_t + (e.need_p ? 8192 : 0);
     e.c_t = e.s_t + (e.need_s ? 8192 : 0);
-    e.bars = &ebar[quad * 2];
+    e.bars = &ebar[ew * 2];
     e.map_c = &mapC;
     e.map_s = &mapS;
     e.map_p = &mapP;
     e.issued = e.consumed = e.seq = 0;
-    float *bias_row = bias_rows + quad * 32;
+    float *bias_row = bias_rows + ew * 32;
     int it = 0;
     bool alive = true;
     for (int item = blockIdx.x; item < w.items && alive; item += gridDim.x, ++it) {
@@ -1168,12 +1176,12 @@ __global__ void __launch_bounds__(192, 1)
       const int used_acc = num_k < NACC ? num_k : NACC;
       // the tile's first act' / C tiles, while its MMAs run
       int next = 0;
-      if (e.need_s || e.need_c) e.template fill<BN / 32>(next, 0, 1, n0, row_tile, z, lane);
+      if (e.need_s || e.need_c) e.template fill<BN / 32>(next, c0, cstep, n0, row_tile, z, lane);
       if (!mbar_wait(&tfull[buf], use & 1, abort_flag, err, 14)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * Cfg::ACC);
       alive = epi_any<BN, NACC, 2, false>(e, d, tbase, used_acc, nullptr, bias_row, n0, row_tile, z, w.col_part,
-                                   next, &tempty[buf], abort_flag, err, 15, lane);
+                                   next, &tempty[buf], abort_flag, err, 15, lane, c0, cstep);
     }
     e.drain(lane);
   }
@@ -1270,9 +1278,9 @@ int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64
 
 
 #ifdef TX_TC_PERSISTENT_TU
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int EW>
 int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
-  auto kern = k_gemm_tcp<BN, A_MN, B_MN>;
+  auto kern = k_gemm_tcp<BN, A_MN, B_MN, EW>;
   static bool configured[64] = {};
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
@@ -1281,18 +1289,18 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
   }
   int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
   if (max_grid > 0 && grid > max_grid) grid = max_grid;
-  kern<<<grid, 192, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
+  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
   TX_LAUNCHED(ctx, "k_gemm_tcp");
   return TX_OK;
 }
 
-template <int BN>
+template <int BN, int EW>
 int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (a_mn && b_mn) return launch_p<BN, true, true>(ctx, d, m, w, smem, max_grid);
-  if (a_mn) return launch_p<BN, true, false>(ctx, d, m, w, smem, max_grid);
-  if (b_mn) return launch_p<BN, false, true>(ctx, d, m, w, smem, max_grid);
-  return launch_p<BN, false, false>(ctx, d, m, w, smem, max_grid);
+  if (a_mn && b_mn) return launch_p<BN, true, true, EW>(ctx, d, m, w, smem, max_grid);
+  if (a_mn) return launch_p<BN, true, false, EW>(ctx, d, m, w, smem, max_grid);
+  if (b_mn) return launch_p<BN, false, true, EW>(ctx, d, m, w, smem, max_grid);
+  return launch_p<BN, false, false, EW>(ctx, d, m, w, smem, max_grid);
 }
 
 // Persistent launch of d (raw split partials when kb_per > 0, z = splits or
@@ -1307,7 +1315,13 @@ int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Map
   PWork w;
   w.ep_stride = kinds * 8192;
   w.col_part = m.col_part;
-  w.stages = (kSmemMax - 1024 - kPTail - 4 * w.ep_stride) / stage;
+  // a GELU (or GELU') epilogue costs more than a 256-wide tile's main loop:
+  // eight epilogue warps, when two stages still fit beside their tiles
+  int ew = 4;
+  if (bn == 256 && (d.act == TX_ACT_GELU || d.dact == TX_ACT_GELU) &&
+      (kSmemMax - 1024 - kPTail - 8 * w.ep_stride) / stage >= 2)
+    ew = 8;
+  w.stages = (kSmemMax - 1024 - kPTail - ew * w.ep_stride) / stage;
   if (w.stages > 8) w.stages = 8;
   if (w.stages < 2) return TX_ERR_UNSUPPORTED;
   w.tiles_m = (int)((d.M + TC_BM - 1) / TC_BM);
@@ -1317,11 +1331,13 @@ int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Map
   const int64_t items = (int64_t)w.tiles_m * w.tiles_n * z;
   if (items > 0x7fffffff) return TX_ERR_UNSUPPORTED;
   w.items = (int)items;
-  const int smem = 1024 + w.stages * stage + 4 * w.ep_stride + kPTail;
+  const int smem = 1024 + w.stages * stage + ew * w.ep_stride + kPTail;
   switch (bn) {
-    case 256: return launch_p_bn<256>(ctx, d, m, w, smem, max_grid);
-    case 64: return launch_p_bn<64>(ctx, d, m, w, smem, max_grid);
-    default: return launch_p_bn<128>(ctx, d, m, w, smem, max_grid);
+    case 256:
+      return ew == 8 ? launch_p_bn<256, 8>(ctx, d, m, w, smem, max_grid)
+                     : launch_p_bn<256, 4>(ctx, d, m, w, smem, max_grid);
+    case 64: return launch_p_bn<64, 4>(ctx, d, m, w, smem, max_grid);
+    default: return launch_p_bn<128, 4>(ctx, d, m, w, smem, max_grid);
   }
 }
 
