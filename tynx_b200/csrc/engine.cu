@@ -1424,7 +1424,8 @@ struct Bwd {
     }
     const Shape &a = S(d.in[0]), &b = S(d.in[1]);
     int rc = TX_OK;
-    const bool dz32 = dz == dy && grad_tf32[yv];  // dZ came TF32-rounded from a fused dgrad
+    bool dz32 = dz == dy && grad_tf32[yv];  // dZ came TF32-rounded from a fused dgrad
+    float *dz_rnd = nullptr;
     if (d.op == TX_OP_GEMM) {
       int ta = (int)d.iattr[0], tb = (int)d.iattr[1];
       int64_t M = ta ? a[1] : a[0], K = ta ? a[0] : a[1], N = tb ? b[0] : b[1];
@@ -1501,6 +1502,21 @@ struct Bwd {
       bool weight2d = b.size() == 2;
       int64_t M = weight2d ? numel_of(a) / K : a[a.size() - 2];
       int64_t batch = weight2d ? 1 : numel_of(a) / (M * K);
+      // TF32 mode: a dZ that the dgrad would round into scratch anyway (at
+      // most half the size of dA, more 128 x 256 tiles of dA than SMs) is
+      // rounded once here, and the wgrad reads the same copy without
+      // conversion (the second MatMul of a 256 -> 1024 -> 256 FFN over 32768
+      // rows: wgrad 53 -> 40 us)
+      if (ctx->math == TX_MATH_TF32 && !dz32 && weight2d && needs[d.in[0]] && needs[d.in[1]] && 2 * N <= K &&
+          M * K > (int64_t)ctx->num_sms * 128 * 256) {
+        dz_rnd = (float *)tx_alloc_raw(ctx, M * N * 4);
+        if (!dz_rnd) rc = TX_ERR_OOM;
+        if (rc == TX_OK) rc = tx_round_tf32(ctx, dz, dz_rnd, M * N);
+        if (rc == TX_OK) {
+          dz = dz_rnd;
+          dz32 = true;
+        }
+      }
       if (rc == TX_OK && needs[d.in[1]]) {  // dB = A^T dY
         float *t; int acc;
         rc = target(d.in[1], &t, &acc);
@@ -1543,6 +1559,7 @@ struct Bwd {
       }
     }
     if (dz_tmp) tx_free_raw(ctx, dz_tmp);
+    if (dz_rnd) tx_free_raw(ctx, dz_rnd);
     return rc;
   }
 
