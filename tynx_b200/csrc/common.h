@@ -131,10 +131,14 @@ int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const in
 int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_t *out_shape, int ndim,
               float *y, float scale, int acc);
 
-// LayerNorm forward; round_tf32 stores y rounded to TF32 (for an output that
-// only feeds contractions; the backward reads x, mean and rstd, not y).
+// Softmax over rows; y32 (may be null, not with log): a second copy of y
+// rounded to TF32 for the contractions that read it, while the backward
+// reads the exact y.  The backward's round stores dx rounded to TF32.
+int softmax_fwd(tx_ctx *ctx, const float *x, float *y, float *y32, int64_t rows, int64_t cols, int log);
 int softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t rows, int64_t cols, int log,
                 int acc, bool round);
+// LayerNorm forward; round_tf32 stores y rounded to TF32 (for an output that
+// only feeds contractions; the backward reads x, mean and rstd, not y).
 int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
                   float *rstd, int64_t rows, int64_t cols, float eps, bool round_tf32);
 

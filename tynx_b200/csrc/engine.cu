@@ -413,6 +413,11 @@ struct GNode {
   // reader of it rounds it so anyway (GEMM operands) or only looks at its sign
   // (the relu mask); set at graph creation
   bool round_out = false;
+  // Softmax whose output is read only as a contraction operand (attention
+  // probabilities): in TF32 mode it also stores a rounded copy (the record's
+  // extra for the node) that those contractions read without conversion; the
+  // backward reads the exact output
+  bool round_copy = false;
   // MatMul / Gemm whose sole consumer multiplies (or divides) it by a constant
   // scalar: the scale is folded into alpha and the result written to the
   // scaling node's output (scale_out); that node is skipped (scaled_into)
@@ -804,6 +809,16 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
           n.fused_act ? n.fused_out : n.scale_out >= 0 ? n.scale_out : n.d.out[0], 0);
     } else if (n.d.op == TX_OP_LAYERNORM) {
       n.round_out = feeds_only_contractions(n.d.out[0], 0);
+    } else if (n.d.op == TX_OP_SOFTMAX) {
+      const GValue &y = g->values[n.d.out[0]];
+      bool only = !y.is_output && !y.consumers.empty();
+      for (int c : y.consumers) {
+        const tx_node_desc &cd = g->nodes[c].d;
+        if (cd.op != TX_OP_GEMM && cd.op != TX_OP_MATMUL) only = false;
+        for (int k = 2; k < cd.n_in; ++k)
+          if (cd.in[k] == n.d.out[0]) only = false;  // a bias is not a contraction operand
+      }
+      n.round_copy = only;
     }
   }
   // ---- TF32 gradient rounding: gradients whose every reader is a contraction -----------------
@@ -991,6 +1006,10 @@ const float *gemm_operand(tx_graph *g, tx_record *r, int v, bool *tf32) {
   if (r->shadow && gv.kind == TX_VAL_PARAM) {
     *tf32 = true;
     return g->flat_tf32 + g->param_offset[gv.param_index];
+  }
+  if (gv.producer >= 0 && g->nodes[gv.producer].round_copy && r->extra[gv.producer]) {
+    *tf32 = true;  // the softmax's rounded copy
+    return (const float *)r->extra[gv.producer];
   }
   *tf32 = r->tf32[v];
   return (const float *)r->buf[v];
@@ -1204,7 +1223,12 @@ struct Fwd {
         int ax = norm_axis(d.iattr[0], (int64_t)x.size());
         if (ax != (int)x.size() - 1) return fail(g, TX_ERR_UNSUPPORTED, "Softmax over a non-final axis is not supported on CUDA");
         int64_t cols = x.back();
-        return tx_softmax_fwd(ctx, F(d.in[0]), F(yv), ny / cols, cols, d.op == TX_OP_LOGSOFTMAX);
+        float *y32 = nullptr;
+        if (n.round_copy && ctx->math == TX_MATH_TF32) {
+          r->extra[ni] = y32 = (float *)tx_alloc_raw(ctx, ny * 4);
+          if (!y32) return TX_ERR_OOM;
+        }
+        return softmax_fwd(ctx, F(d.in[0]), F(yv), y32, ny / cols, cols, d.op == TX_OP_LOGSOFTMAX);
       }
       case TX_OP_REDUCEMEAN: case TX_OP_REDUCESUM: case TX_OP_GAP: {
         const Shape &x = S(d.in[0]);

@@ -243,9 +243,11 @@ __global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restri
 }
 
 // Register-resident softmax for rows of VPL * 128 floats: a warp per row,
-// one HBM read of x (and of y, dy in the backward).
+// one HBM read of x (and of y, dy in the backward).  y32 (softmax only, may be
+// null): a second copy of y rounded to TF32, for contractions that read y.
 template <int VPL>
-__global__ void k_softmax_fwd_v(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int log_mode) {
+__global__ void k_softmax_fwd_v(const float *__restrict__ x, float *__restrict__ y, float *__restrict__ y32,
+                                int64_t rows, int log_mode) {
   constexpr int cols = VPL * 128;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / kWarp);
@@ -272,10 +274,16 @@ __global__ void k_softmax_fwd_v(const float *__restrict__ x, float *__restrict__
         yr[j * 32 + lane] = make_float4((v[j].x - m) - lse, (v[j].y - m) - lse, (v[j].z - m) - lse, (v[j].w - m) - lse);
     } else {
       const float inv = 1.0f / s;
+      float4 *yq = y32 ? reinterpret_cast<float4 *>(y32 + r * cols) : nullptr;
 #pragma unroll
-      for (int j = 0; j < VPL; ++j)
-        yr[j * 32 + lane] = make_float4(expf(v[j].x - m) * inv, expf(v[j].y - m) * inv, expf(v[j].z - m) * inv,
-                                        expf(v[j].w - m) * inv);
+      for (int j = 0; j < VPL; ++j) {
+        const float4 p = make_float4(expf(v[j].x - m) * inv, expf(v[j].y - m) * inv, expf(v[j].z - m) * inv,
+                                     expf(v[j].w - m) * inv);
+        yr[j * 32 + lane] = p;
+        if (yq)
+          yq[j * 32 + lane] = make_float4(tx_epi::round_tf32(p.x), tx_epi::round_tf32(p.y),
+                                          tx_epi::round_tf32(p.z), tx_epi::round_tf32(p.w));
+      }
     }
   }
 }
@@ -1057,23 +1065,29 @@ static bool ln_vec(int64_t cols, std::initializer_list<const void *> ptrs) {
   return true;
 }
 
-extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int log) {
-  if (!ctx) return TX_ERR_INVALID;
+// y32 (may be null; not with log): also store y rounded to TF32 there
+int softmax_fwd(tx_ctx *ctx, const float *x, float *y, float *y32, int64_t rows, int64_t cols, int log) {
+  if (!ctx || (y32 && log)) return TX_ERR_INVALID;
   if (rows <= 0 || cols <= 0) return TX_OK;
-  if (ln_vec(cols, {x, y}) && (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
+  if (ln_vec(cols, {x, y}) && (!y32 || ln_vec(cols, {y32})) &&
+      (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
     const unsigned blocks = rows_grid(rows, 8);
     switch (cols) {
-      case 128: k_softmax_fwd_v<1><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
-      case 256: k_softmax_fwd_v<2><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
-      case 512: k_softmax_fwd_v<4><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
-      default: k_softmax_fwd_v<8><<<blocks, 256, 0, ctx->stream>>>(x, y, rows, log); break;
+      case 128: k_softmax_fwd_v<1><<<blocks, 256, 0, ctx->stream>>>(x, y, y32, rows, log); break;
+      case 256: k_softmax_fwd_v<2><<<blocks, 256, 0, ctx->stream>>>(x, y, y32, rows, log); break;
+      case 512: k_softmax_fwd_v<4><<<blocks, 256, 0, ctx->stream>>>(x, y, y32, rows, log); break;
+      default: k_softmax_fwd_v<8><<<blocks, 256, 0, ctx->stream>>>(x, y, y32, rows, log); break;
     }
     TX_LAUNCHED(ctx, "k_softmax_fwd_v");
     return TX_OK;
   }
   k_softmax_fwd<<<rows_grid(rows, 8), 256, 0, ctx->stream>>>(x, y, rows, cols, log);
   TX_LAUNCHED(ctx, "k_softmax_fwd");
-  return TX_OK;
+  return y32 ? tx_round_tf32(ctx, y, y32, rows * cols) : TX_OK;
+}
+
+extern "C" int tx_softmax_fwd(tx_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int log) {
+  return softmax_fwd(ctx, x, y, nullptr, rows, cols, log);
 }
 
 // round: store dx rounded to TF32 (for a gradient whose only readers are
