@@ -406,18 +406,22 @@ def ctypes_stream(ctx) -> int:
 
 
 def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
-    """Time the step's largest forward GEMM alone (CUDA events on the engine stream)."""
+    """Time the step's largest forward GEMM alone (CUDA events on the engine stream),
+    with the operand layout and epilogue it has in the step."""
     import torch
 
     from tynx_b200 import _core
 
     peaks, source = _peaks()
     # largest GEMM of the MLP classifier / policy: hidden x hidden forward
+    tb, act, with_bias, with_preact = True, "relu", True, False
     if wl.name in ("mlp_classifier", "mlp_policy"):
         hidden = 1024 if wl.name == "mlp_classifier" else 256
         M, N_, K = per_rank, hidden, hidden
     elif wl.name == "transformer":
+        # the first FFN MatMul: weight stored K x N, GELU, pre-activation kept
         M, N_, K = per_rank * 128, 1024, 256
+        tb, act, with_bias, with_preact = False, "gelu", False, True
     elif wl.name == "ppo":
         M, N_, K = per_rank, 512, 512
     else:
@@ -426,9 +430,10 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
 
     rng = np.random.default_rng(0)
     A = tx.Tensor(rng.standard_normal((M, K)).astype(np.float32))
-    B = tx.Tensor(rng.standard_normal((N_, K)).astype(np.float32))
+    B = tx.Tensor(rng.standard_normal((N_, K) if tb else (K, N_)).astype(np.float32))
     Cm = tx.zeros(M, N_)
     bias = tx.zeros(N_)
+    pre = tx.zeros(M, N_) if with_preact else None
     flags = 0
     if math == "tf32":
         # as in the step: the activation arrives TF32-rounded from the previous
@@ -439,8 +444,9 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
         flags = N.TX_GEMM_A_TF32 | N.TX_GEMM_B_TF32 | N.TX_GEMM_ROUND_OUT
 
     def launch():
-        _core.gemm(ctx, M, N_, K, A.ptr, K, False, B.ptr, K, True, Cm.ptr, N_, bias=bias.ptr,
-                   act="relu", flags=flags)
+        _core.gemm(ctx, M, N_, K, A.ptr, K, False, B.ptr, K if tb else N_, tb, Cm.ptr, N_,
+                   bias=bias.ptr if with_bias else None, act=act, flags=flags,
+                   preact=pre.ptr if pre is not None else None)
 
     for _ in range(5):
         launch()
@@ -479,10 +485,21 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
         entry = json.loads(tpath.read_text()).get(wl.name)
         if entry and per_rank == wl.batch:
             traffic = entry["traffic_bytes"]
-    return {"bound": "tensor", "kernel": f"gemm {M}x{N_}x{K} +bias+relu ({math})",
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": traffic, "traffic_unit": "bytes/launch", "duration_us": ms * 1e3,
-            "peak_source": note}
+    epi = ("+bias" if with_bias else "") + f"+{act}" + ("+preact" if with_preact else "")
+    # algorithmic HBM bytes: A and B read once, C (and the pre-activation) written once
+    nbytes = 4.0 * (M * K + K * N_ + M * N_ * (2 if with_preact else 1) + (N_ if with_bias else 0))
+    out = {"kernel": f"gemm {M}x{N_}x{K} {epi} ({math})", "flops": flops, "algorithmic_bytes": nbytes,
+           "traffic": traffic, "traffic_unit": "bytes/launch", "duration_us": ms * 1e3}
+    if nbytes / (peaks["hbm_gbs"] * 1e9) > flops / (peak * 1e12):
+        # the stores outweigh the math: bound by HBM
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out.update({"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{source} HBM copy bandwidth",
+                    "tflops": achieved})
+    else:
+        out.update({"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "peak_source": note})
+    return out
 
 
 if __name__ == "__main__":

@@ -898,7 +898,7 @@ def matmul(a: Tensor, b: Tensor) -> Tensor:
 
 
 def gemm(ctx: Context, M, N_, K, A, lda, ta, B, ldb, tb, Cp, ldc, *, alpha=1.0, beta=0.0,
-         bias=None, bias_scale=1.0, act="none", flags=0) -> None:
+         bias=None, bias_scale=1.0, act="none", flags=0, preact=None, ld_preact=0) -> None:
     d = N.GemmDesc()
     d.M, d.N, d.K = M, N_, K
     d.A, d.lda, d.trans_a = A, lda, int(ta)
@@ -909,6 +909,8 @@ def gemm(ctx: Context, M, N_, K, A, lda, ta, B, ldb, tb, Cp, ldc, *, alpha=1.0, 
     d.act = N.ACT[act]
     d.batch = 1
     d.flags = flags
+    if preact is not None:
+        d.preact, d.ld_preact = preact, ld_preact or N_
     ctx.check(lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
 
 
