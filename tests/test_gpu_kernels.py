@@ -501,6 +501,46 @@ def test_layernorm_matches_oracle(tx, cols):
     assert _rel(DB.numpy(), tb.grad) < 1e-5
 
 
+@pytest.mark.parametrize("cols", [256, 100])
+def test_layernorm_param_grads_accumulate_and_stand_alone(tx, cols):
+    """dgamma and dbeta are reduced in one launch when both are wanted; asking
+    for one of them, or accumulating into existing values, gives the same
+    fixed-order sums bit for bit."""
+    from tynx_b200 import _native as N
+    from tynx_b200._core import context
+
+    ctx = context()
+    rng = np.random.default_rng(5)
+    rows = 2000
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    g = rng.standard_normal(cols).astype(np.float32)
+    dy = rng.standard_normal((rows, cols)).astype(np.float32)
+    prior_g = rng.standard_normal(cols).astype(np.float32)
+    prior_b = rng.standard_normal(cols).astype(np.float32)
+    X, G, DY = (tx.Tensor(v) for v in (x, g, dy))
+    Y, mean, rstd, DX = tx.zeros(rows, cols), tx.zeros(rows), tx.zeros(rows), tx.zeros(rows, cols)
+    ctx.check(N.lib.tx_layernorm_fwd(ctx.handle, X.ptr, G.ptr, tx.zeros(cols).ptr, Y.ptr, mean.ptr,
+                                     rstd.ptr, rows, cols, C.c_float(1e-5)))
+
+    def bwd(dg, db, acc):
+        ctx.check(N.lib.tx_layernorm_bwd(ctx.handle, X.ptr, G.ptr, mean.ptr, rstd.ptr, DY.ptr, DX.ptr,
+                                         dg.ptr if dg is not None else None,
+                                         db.ptr if db is not None else None, rows, cols, 0, acc))
+
+    DG, DB = tx.zeros(cols), tx.zeros(cols)
+    bwd(DG, DB, 0)
+    dg, db = DG.numpy(), DB.numpy()
+    only_g, only_b = tx.zeros(cols), tx.zeros(cols)
+    bwd(only_g, None, 0)
+    bwd(None, only_b, 0)
+    np.testing.assert_array_equal(only_g.numpy(), dg)
+    np.testing.assert_array_equal(only_b.numpy(), db)
+    AG, AB = tx.Tensor(prior_g), tx.Tensor(prior_b)
+    bwd(AG, AB, 1)
+    np.testing.assert_array_equal(AG.numpy(), prior_g + dg)
+    np.testing.assert_array_equal(AB.numpy(), prior_b + db)
+
+
 def test_adam_is_bit_exact_with_oracle(tx):
     from oracle import flex_oracle as fo
     from tynx_b200 import optim

@@ -627,11 +627,16 @@ __global__ void k_layernorm_bwd(const float *__restrict__ x, const float *__rest
 // Final column reduction of a [np, cols] partial-sum matrix: out = scale * sum
 // (+ out when acc).  Block (32, 32): lane x owns column 32 * blockIdx.x + x,
 // the 32 row groups take partial rows ty, ty + 32, ... in order with eight
-// loads in flight, and the groups are combined in a fixed order.
+// loads in flight, and the groups are combined in a fixed order.  blockIdx.y
+// = 1 reduces a second matrix stored right after the first into out1.
 __global__ void __launch_bounds__(1024) k_colsum_final(const float *__restrict__ part, int64_t np,
-                                                       int64_t cols, float *__restrict__ out, float scale,
-                                                       int acc) {
+                                                       int64_t cols, float *__restrict__ out,
+                                                       float *__restrict__ out1, float scale, int acc) {
   __shared__ float sm[32][33];
+  if (blockIdx.y) {
+    part += np * cols;
+    out = out1;
+  }
   const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
   if (c < cols) {
@@ -973,7 +978,24 @@ int colsum_finish(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, floa
                   int acc) {
   const int64_t blocks = (cols + 31) / 32;
   if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
-  k_colsum_final<<<(unsigned)blocks, dim3(32, 32), 0, ctx->stream>>>(part, np, cols, out, scale, acc);
+  k_colsum_final<<<(unsigned)blocks, dim3(32, 32), 0, ctx->stream>>>(part, np, cols, out, nullptr, scale, acc);
+  TX_LAUNCHED(ctx, "k_colsum_final");
+  return TX_OK;
+}
+
+// Two column reductions in one launch: [np, cols] partials at part into out0
+// and the next [np, cols] into out1 (either output may be null: then one)
+static int colsum_finish2(tx_ctx *ctx, const float *part, int64_t np, int64_t cols, float *out0, float *out1,
+                          float scale, int acc) {
+  if (!out0 || !out1) {
+    if (out0) TX_TRY(colsum_finish(ctx, part, np, cols, out0, scale, acc));
+    if (out1) TX_TRY(colsum_finish(ctx, part + np * cols, np, cols, out1, scale, acc));
+    return TX_OK;
+  }
+  const int64_t blocks = (cols + 31) / 32;
+  if (blocks > 0x7fffffff) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "column reduction too wide");
+  k_colsum_final<<<dim3((unsigned)blocks, 2), dim3(32, 32), 0, ctx->stream>>>(part, np, cols, out0, out1, scale,
+                                                                              acc);
   TX_LAUNCHED(ctx, "k_colsum_final");
   return TX_OK;
 }
@@ -1238,9 +1260,7 @@ extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma,
       default: k_layernorm_bwd_v<4><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, gamma, mean, rstd, dy, dx, pg, pb, rows, acc_dx); break;
     }
     TX_LAUNCHED(ctx, "k_layernorm_bwd_v");
-    if (dgamma) TX_TRY(colsum_finish(ctx, pg, blocks, cols, dgamma, 1.f, acc_p));
-    if (dbeta) TX_TRY(colsum_finish(ctx, pb, blocks, cols, dbeta, 1.f, acc_p));
-    return TX_OK;
+    return colsum_finish2(ctx, pg, blocks, cols, dgamma, dbeta, 1.f, acc_p);  // pb follows pg
   }
   const int warps = 4;
   size_t smem = 2 * (size_t)warps * cols * sizeof(float);
@@ -1257,13 +1277,7 @@ extern "C" int tx_layernorm_bwd(tx_ctx *ctx, const float *x, const float *gamma,
   k_layernorm_bwd<<<(unsigned)blocks, warps * 32, smem, ctx->stream>>>(x, gamma, mean, rstd, dy, dx,
                                                                       pg, pb, rows, cols, acc_dx);
   TX_LAUNCHED(ctx, "k_layernorm_bwd");
-  if (dgamma) {
-    TX_TRY(colsum_finish(ctx, pg, blocks, cols, dgamma, 1.f, acc_p));
-  }
-  if (dbeta) {
-    TX_TRY(colsum_finish(ctx, pb, blocks, cols, dbeta, 1.f, acc_p));
-  }
-  return TX_OK;
+  return colsum_finish2(ctx, pg, blocks, cols, dgamma, dbeta, 1.f, acc_p);  // pb follows pg
 }
 
 extern "C" int tx_gather_rows(tx_ctx *ctx, const float *table, int64_t rows, int64_t width,
