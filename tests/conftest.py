@@ -30,3 +30,19 @@ def fixtures() -> dict:
 @pytest.fixture(scope="session")
 def expected() -> dict:
     return json.loads((GOLDEN / "expected.json").read_text())
+
+
+@pytest.fixture(scope="session")
+def gemm_line_model() -> bytes:
+    """The one-node Gemm of the reference's line-fitting test: y = x W + b with
+    x [4, 1], W [1, 1] and b [1] initializers, both zero (opset 13)."""
+    import numpy as np
+
+    from tynx_b200.onnx import proto
+
+    nodes = [proto.encode_node("Gemm", ["x", "weight", "bias"], ["y"], name="layer")]
+    inits = [proto.encode_tensor("weight", np.zeros((1, 1), np.float32)),
+             proto.encode_tensor("bias", np.zeros(1, np.float32))]
+    return proto.encode_model(nodes, inits, [proto.encode_value_info("x", proto.FLOAT, [4, 1])],
+                              [proto.encode_value_info("y", proto.FLOAT, [4, 1])],
+                              graph_name="imported_training_test", opset=13)

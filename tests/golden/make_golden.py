@@ -190,6 +190,20 @@ EXPECTED = {
             },
         },
     },
+    # A one-node Gemm (x [4, 1], weight [1, 1] and bias [1] initializers, both
+    # zero; opset 13, no transpose attributes) built in the test code, not a
+    # hex fixture: the tests build the same model with the package's encoder.
+    "gemm_learns_line": {
+        "source": "crates/tynx-train/src/imported_model/tests.rs:62-140 (model: :647-657, :844-863)",
+        "input": [[-1.0], [0.0], [1.0], [2.0]],
+        "target": [[-1.0], [1.0], [3.0], [5.0]],
+        "lr": 0.1,
+        "steps": 100,
+        "output_before": [0.0, 0.0, 0.0, 0.0],
+        "weight": 2.0,
+        "bias": 1.0,
+        "tolerance": 1e-3,
+    },
 }
 
 

@@ -249,3 +249,38 @@ def test_composed_models_converge(tx, fixtures, expected, name):
     final = tx.nn.functional.mse_loss(model(x), target).item()
     assert final < initial * spec["final_ratio_below"]
     assert all(p.grad is not None for _, p in model.named_parameters())
+
+
+def test_gemm_learns_line(tx, gemm_line_model, expected):
+    """100 SGD steps on the mean squared error fit y = 2x + 1 through the
+    imported Gemm on the GPU; the first forward reads the zero initializers,
+    the next forward the updated slots; the final slots agree with the oracle
+    run of the same steps."""
+    from oracle import flex_oracle as fo
+    from tynx_b200.onnx import ir
+
+    case = expected["gemm_learns_line"]
+    names = {"weight": "head.weight", "bias": "head.bias"}
+    model = tx.load(gemm_line_model, trainable="auto", simplify=False, initializer_names=names)
+    x, target = tx.Tensor(case["input"]), tx.Tensor(case["target"])
+    assert model(x).flatten().tolist() == case["output_before"]
+    opt = tx.optim.SGD(model.named_parameters(), lr=case["lr"])
+    ref = fo.OracleModel(ir.load_training_graph(gemm_line_model, initializer_names=names))
+    ref_opt = fo.SGD(ref.named_parameters(), lr=case["lr"])
+    xs, ts = np.asarray(case["input"], np.float32), np.asarray(case["target"], np.float32)
+    for _ in range(case["steps"]):
+        opt.zero_grad()
+        tx.nn.functional.mse_loss(model(x), target).backward()
+        opt.step()
+        ref_opt.zero_grad()
+        fo.mse_loss(ref(xs), ts).backward()
+        ref_opt.step()
+    p = {n: float(v.numpy().reshape(-1)[0]) for n, v in model.named_parameters()}
+    r = {n: float(v.data.reshape(-1)[0]) for n, v in ref.named_parameters()}
+    tol = case["tolerance"]
+    assert abs(p["head.weight"] - case["weight"]) < tol
+    assert abs(p["head.bias"] - case["bias"]) < tol
+    for n in r:
+        assert abs(p[n] - r[n]) <= 1e-5 * max(1.0, abs(r[n])), (n, p[n], r[n])
+    np.testing.assert_allclose(model(x).numpy(), ts, atol=tol)
+

@@ -233,3 +233,26 @@ def test_conv_finite_differences():
             flat[i] = old
             assert math.isclose(tensor.grad.reshape(-1)[i], (up - down) / 1.0, rel_tol=1e-3,
                                 abs_tol=1e-3)
+
+
+def test_gemm_learns_line(gemm_line_model, expected):
+    """100 SGD steps on the mean squared error fit y = 2x + 1 through the
+    imported Gemm; the first forward reads the zero initializers."""
+    case = expected["gemm_learns_line"]
+    model = fo.OracleModel(ir.load_training_graph(gemm_line_model,
+                                                  initializer_names={"weight": "head.weight",
+                                                                     "bias": "head.bias"}))
+    x = np.asarray(case["input"], np.float32)
+    target = np.asarray(case["target"], np.float32)
+    assert model(x).data.reshape(-1).tolist() == case["output_before"]
+    opt = fo.SGD(model.named_parameters(), lr=case["lr"])
+    for _ in range(case["steps"]):
+        opt.zero_grad()
+        fo.mse_loss(model(x), target).backward()
+        opt.step()
+    params = dict(model.named_parameters())
+    tol = case["tolerance"]
+    assert abs(float(params["head.weight"].data.reshape(-1)[0]) - case["weight"]) < tol
+    assert abs(float(params["head.bias"].data.reshape(-1)[0]) - case["bias"]) < tol
+    np.testing.assert_allclose(model(x).data, target, atol=tol)
+
