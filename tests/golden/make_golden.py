@@ -204,6 +204,27 @@ EXPECTED = {
         "bias": 1.0,
         "tolerance": 1e-3,
     },
+    # Central differences of one input element (the graphs are one Conv / one
+    # LayerNormalization node; the reference builds them with its eager API).
+    "conv2d_finite_difference": {
+        "source": "crates/tynx-python/tests/test_training_robustness.py:17-36",
+        "input": [[[[0.2, -0.4], [0.7, 1.1]]]],
+        "weight": [[[[0.5, -0.25], [0.75, 0.1]]]],
+        "element": 0,
+        "epsilon": 1e-3,
+        "rel": 2e-3,
+        "abs": 2e-3,
+    },
+    "layer_norm_finite_difference": {
+        "source": "crates/tynx-python/tests/test_training_robustness.py:39-59",
+        "input": [[0.5, -1.0, 2.0]],
+        "coefficients": [0.25, -0.5, 1.5],
+        "eps": 1e-5,
+        "element": 1,
+        "epsilon": 1e-3,
+        "rel": 3e-3,
+        "abs": 3e-3,
+    },
 }
 
 

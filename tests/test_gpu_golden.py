@@ -284,3 +284,49 @@ def test_gemm_learns_line(tx, gemm_line_model, expected):
         assert abs(p[n] - r[n]) <= 1e-5 * max(1.0, abs(r[n])), (n, p[n], r[n])
     np.testing.assert_allclose(model(x).numpy(), ts, atol=tol)
 
+
+def _one_node_model(op, x_shape, y_shape, inits, **attrs):
+    from tynx_b200.onnx import proto
+
+    names = [n for n, _ in inits]
+    return proto.encode_model(
+        [proto.encode_node(op, ["x", *names], ["y"], name="layer", **attrs)],
+        [proto.encode_tensor(n, np.asarray(v, np.float32)) for n, v in inits],
+        [proto.encode_value_info("x", proto.FLOAT, list(x_shape))],
+        [proto.encode_value_info("y", proto.FLOAT, list(y_shape))], opset=17)
+
+
+def _central_difference(f, x0, i, e):
+    up, down = x0.copy(), x0.copy()
+    up.reshape(-1)[i] += np.float32(e)
+    down.reshape(-1)[i] -= np.float32(e)
+    return (f(up) - f(down)) / (2 * e)
+
+
+def test_reference_finite_difference_points(tx, expected):
+    """The reference's central-difference checks on its inputs, through
+    one-node imported graphs on the GPU: the Conv input gradient at element 0
+    and the LayerNormalization input gradient of sum(y * coefficients) at
+    element 1."""
+    c = expected["conv2d_finite_difference"]
+    x0 = np.asarray(c["input"], np.float32)
+    w = np.asarray(c["weight"], np.float32)
+    conv = tx.load(_one_node_model("Conv", x0.shape, (1, 1, 1, 1), [("w", w)]), trainable="auto",
+                   simplify=False)
+    x = tx.Tensor(x0, requires_grad=True)
+    conv(x).sum().backward()
+    numerical = _central_difference(lambda v: conv(tx.Tensor(v)).sum().item(), x0, c["element"], c["epsilon"])
+    assert x.grad.flatten().tolist()[c["element"]] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
+
+    c = expected["layer_norm_finite_difference"]
+    x0 = np.asarray(c["input"], np.float32)
+    coef = tx.Tensor(c["coefficients"])
+    ln = tx.load(_one_node_model("LayerNormalization", x0.shape, x0.shape,
+                                 [("scale", np.ones(3)), ("shift", np.zeros(3))], axis=-1,
+                                 epsilon=c["eps"]), trainable="auto", simplify=False)
+    x = tx.Tensor(x0, requires_grad=True)
+    (ln(x) * coef).sum().backward()
+    numerical = _central_difference(lambda v: (ln(tx.Tensor(v)) * coef).sum().item(), x0, c["element"],
+                                    c["epsilon"])
+    assert x.grad.flatten().tolist()[c["element"]] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
+

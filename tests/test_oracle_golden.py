@@ -256,3 +256,44 @@ def test_gemm_learns_line(gemm_line_model, expected):
     assert abs(float(params["head.bias"].data.reshape(-1)[0]) - case["bias"]) < tol
     np.testing.assert_allclose(model(x).data, target, atol=tol)
 
+
+def test_reference_finite_difference_points(expected):
+    """The reference's own central-difference checks, on its inputs: the
+    conv2d input gradient at element 0 and the LayerNorm (unit scale, zero
+    shift) input gradient of sum(y * coefficients) at element 1."""
+    c = expected["conv2d_finite_difference"]
+    w = fo.T(np.asarray(c["weight"], np.float32))
+
+    def conv_sum(values):
+        return float(fo.conv2d(fo.T(values), w, None, (1, 1), (0, 0, 0, 0), (1, 1)).data.sum())
+
+    x0 = np.asarray(c["input"], np.float32)
+    x = fo.T(x0.copy(), requires_grad=True)
+    y = fo.conv2d(x, w, None, (1, 1), (0, 0, 0, 0), (1, 1))
+    y.backward(np.ones_like(y.data))
+    i, e = c["element"], c["epsilon"]
+    up, down = x0.copy(), x0.copy()
+    up.reshape(-1)[i] += np.float32(e)
+    down.reshape(-1)[i] -= np.float32(e)
+    numerical = (conv_sum(up) - conv_sum(down)) / (2 * e)
+    assert x.grad.reshape(-1)[i] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
+
+    c = expected["layer_norm_finite_difference"]
+    coef = np.asarray(c["coefficients"], np.float32)
+    scale, shift = fo.T(np.ones(3, np.float32)), fo.T(np.zeros(3, np.float32))
+
+    def ln_sum(values):
+        (out,) = fo.layer_norm(fo.T(values), scale, shift, -1, c["eps"], 1)
+        return float((out.data * coef).sum())
+
+    x0 = np.asarray(c["input"], np.float32)
+    x = fo.T(x0.copy(), requires_grad=True)
+    (y,) = fo.layer_norm(x, scale, shift, -1, c["eps"], 1)
+    y.backward(np.broadcast_to(coef, y.data.shape).copy())
+    i, e = c["element"], c["epsilon"]
+    up, down = x0.copy(), x0.copy()
+    up.reshape(-1)[i] += np.float32(e)
+    down.reshape(-1)[i] -= np.float32(e)
+    numerical = (ln_sum(up) - ln_sum(down)) / (2 * e)
+    assert x.grad.reshape(-1)[i] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
+
