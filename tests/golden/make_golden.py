@@ -190,6 +190,15 @@ EXPECTED = {
             },
         },
     },
+    # One scalar parameter (2.0) with a set gradient; "after" values are
+    # asserted exactly in f32 by the reference, the momentum trajectory to 1e-6.
+    "sgd_goldens": {
+        "source": "crates/tynx-train/src/optimizer.rs:487-535",
+        "weight": 2.0,
+        "plain": {"grad": 3.0, "lr": 0.1, "after": 1.7},
+        "weight_decay": {"grad": 3.0, "lr": 0.1, "weight_decay": 0.5, "after": 1.6},
+        "momentum": {"grad": 2.0, "lr": 0.1, "momentum": 0.9, "dampening": 0.5, "trajectory": [1.8, 1.52]},
+    },
     # A one-node Gemm (x [4, 1], weight [1, 1] and bias [1] initializers, both
     # zero; opset 13, no transpose attributes) built in the test code, not a
     # hex fixture: the tests build the same model with the package's encoder.

@@ -106,6 +106,36 @@ def test_batched_matmul(tx, fixtures, expected):
     assert w.grad.flatten().tolist() == pytest.approx(case["weight_grad"])
 
 
+def test_sgd_goldens(tx, fixtures, expected):
+    """The reference's SGD known answers on a slot holding 2.0: plain and
+    coupled weight decay exactly in f32, momentum with dampening over two
+    steps (the first takes the gradient undamped) to 1e-6."""
+    case = expected["sgd_goldens"]
+
+    def weight():
+        p = dict(_load(tx, fixtures, "_GEMM_MODEL").named_parameters())["weight"]
+        assert p.item() == case["weight"]
+        return p
+
+    c = case["plain"]
+    p = weight()
+    p.grad = tx.Tensor([[c["grad"]]])
+    tx.optim.SGD([p], lr=c["lr"]).step()
+    assert np.float32(p.item()) == np.float32(c["after"])
+    c = case["weight_decay"]
+    p = weight()
+    p.grad = tx.Tensor([[c["grad"]]])
+    tx.optim.SGD([p], lr=c["lr"], weight_decay=c["weight_decay"]).step()
+    assert np.float32(p.item()) == np.float32(c["after"])
+    c = case["momentum"]
+    p = weight()
+    opt = tx.optim.SGD([p], lr=c["lr"], momentum=c["momentum"], dampening=c["dampening"])
+    for want in c["trajectory"]:
+        p.grad = tx.Tensor([[c["grad"]]])
+        opt.step()
+        assert p.item() == pytest.approx(want, abs=1e-6)
+
+
 def test_adam_goldens(tx, fixtures, expected):
     model = _load(tx, fixtures, "_GEMM_MODEL")
     w = dict(model.named_parameters())["weight"]

@@ -127,6 +127,30 @@ def test_amsgrad(expected):
     assert abs(p.data[0] - case["final"]) < 1e-6
 
 
+def test_sgd_goldens(expected):
+    """Plain SGD and coupled weight decay land exactly on the f32 values the
+    reference asserts; momentum with dampening follows its two-step trajectory
+    (the first step takes the gradient undamped)."""
+    case = expected["sgd_goldens"]
+    c = case["plain"]
+    p = _scalar_param(case["weight"])
+    p.grad = np.asarray([c["grad"]], np.float32)
+    fo.SGD([p], lr=c["lr"]).step()
+    assert p.data[0] == np.float32(c["after"])
+    c = case["weight_decay"]
+    p = _scalar_param(case["weight"])
+    p.grad = np.asarray([c["grad"]], np.float32)
+    fo.SGD([p], lr=c["lr"], weight_decay=c["weight_decay"]).step()
+    assert p.data[0] == np.float32(c["after"])
+    c = case["momentum"]
+    p = _scalar_param(case["weight"])
+    opt = fo.SGD([p], lr=c["lr"], momentum=c["momentum"], dampening=c["dampening"])
+    for want in c["trajectory"]:
+        p.grad = np.asarray([c["grad"]], np.float32)
+        opt.step()
+        assert abs(p.data[0] - want) < 1e-6
+
+
 def test_softmax_and_log_softmax(expected):
     case = expected["softmax_axis0"]
     y = fo.softmax(fo.T(np.asarray(case["input"], np.float32)), case["axis"])
