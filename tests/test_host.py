@@ -106,3 +106,39 @@ def test_trainability_roles_follow_consumers(fixtures):
     g = ir.load_training_graph(data)
     assert g.report.trainable_parameters == []
     assert any("no registered trainable role" in w for w in g.report.warnings)
+
+
+def test_trainability_roles_by_operand():
+    """Which initializers train, operand by operand, as the reference's
+    trainability tests state it (trainability.rs:1243-1259, 1385-1432): a
+    Gather trains its data table but not its indices; a Clip's bound
+    initializers stay constant; a Linear weight in float16 is reported as an
+    error, since training requires float32."""
+    from tynx_b200.onnx import ir, proto
+
+    def model(nodes, inits, inputs, outputs):
+        return proto.encode_model(nodes, inits, inputs, outputs)
+
+    g = ir.load_training_graph(model(
+        [proto.encode_node("Gather", ["data", "idx"], ["y"], name="gather", axis=0)],
+        [proto.encode_tensor("data", np.zeros((4, 2), np.float32)),
+         proto.encode_tensor("idx", np.zeros(1, np.int64))],
+        [], [proto.encode_value_info("y", proto.FLOAT, [1, 2])]))
+    assert g.report.trainable_parameters == ["data"]
+
+    g = ir.load_training_graph(model(
+        [proto.encode_node("Clip", ["x", "lo", "hi"], ["y"], name="relu6")],
+        [proto.encode_tensor("lo", np.zeros(1, np.float32)),
+         proto.encode_tensor("hi", np.full(1, 6.0, np.float32))],
+        [proto.encode_value_info("x", proto.FLOAT, [2, 2])],
+        [proto.encode_value_info("y", proto.FLOAT, [2, 2])]))
+    assert g.report.trainable_parameters == []
+
+    g = ir.load_training_graph(model(
+        [proto.encode_node("Gemm", ["x", "weight", "bias"], ["y"], name="linear")],
+        [proto.encode_tensor("weight", np.zeros((2, 2), np.float16)),
+         proto.encode_tensor("bias", np.zeros(2, np.float32))],
+        [proto.encode_value_info("x", proto.FLOAT, [1, 2])],
+        [proto.encode_value_info("y", proto.FLOAT, [1, 2])]))
+    assert any("requires float32" in e for e in g.report.errors)
+
