@@ -142,3 +142,42 @@ def test_trainability_roles_by_operand():
         [proto.encode_value_info("y", proto.FLOAT, [1, 2])]))
     assert any("requires float32" in e for e in g.report.errors)
 
+
+def test_selected_output_reports_influencing_blocked_and_unused_parameters():
+    """Two branches from one input: policy = Relu(Gemm) trains, diagnostic =
+    Ceil(Gemm) has no backward rule (trainability.rs:1434-1475).  Selecting
+    policy leaves the diagnostic parameters unused; selecting diagnostic is
+    not trainable, and the one issue names the Ceil node and the parameters it
+    cuts off."""
+    from tynx_b200.onnx import ir, proto
+
+    z = lambda *shape: np.zeros(shape, np.float32)  # noqa: E731
+    data = proto.encode_model(
+        [proto.encode_node("Gemm", ["x", "policy.weight", "policy.bias"], ["policy_hidden"],
+                           name="policy_linear"),
+         proto.encode_node("Relu", ["policy_hidden"], ["policy"], name="policy_relu"),
+         proto.encode_node("Gemm", ["x", "diagnostic.weight", "diagnostic.bias"], ["diagnostic_hidden"],
+                           name="diagnostic_linear"),
+         proto.encode_node("Ceil", ["diagnostic_hidden"], ["diagnostic"], name="diagnostic_round")],
+        [proto.encode_tensor("policy.weight", z(2, 2)), proto.encode_tensor("policy.bias", z(2)),
+         proto.encode_tensor("diagnostic.weight", z(2, 2)), proto.encode_tensor("diagnostic.bias", z(2))],
+        [proto.encode_value_info("x", proto.FLOAT, [1, 2])],
+        [proto.encode_value_info("policy", proto.FLOAT, [1, 2]),
+         proto.encode_value_info("diagnostic", proto.FLOAT, [1, 2])])
+
+    policy = ir.load_training_graph(data, outputs=["policy"]).report
+    assert policy.is_trainable
+    assert policy.output_parameters["policy"] == ["policy.bias", "policy.weight"]
+    assert policy.backward_issues == []
+    assert policy.unused_parameters == ["diagnostic.bias", "diagnostic.weight"]
+    policy.require_trainable()
+
+    diagnostic = ir.load_training_graph(data, outputs=["diagnostic"]).report
+    assert not diagnostic.is_trainable
+    assert len(diagnostic.backward_issues) == 1
+    issue = diagnostic.backward_issues[0]
+    assert "Ceil" in issue and "diagnostic_round" in issue
+    assert "diagnostic.bias, diagnostic.weight" in issue
+    with pytest.raises(ValueError, match="not trainable"):
+        diagnostic.require_trainable()
+

@@ -358,6 +358,22 @@ def build_training_graph(
 
     # --- backward paths (trainability.rs:684-826) ----------------------------------
     producer = {out: op for op in ops for out in op.outputs}
+
+    def upstream_parameters(values) -> list[str]:
+        # every parameter that feeds these values, through any operator
+        found, seen, stack = set(), set(), [v for v in values if v]
+        while stack:
+            value = stack.pop()
+            if value in seen:
+                continue
+            seen.add(value)
+            if value in parameter_of_value:
+                found.add(parameter_of_value[value])
+            elif value in producer:
+                stack.extend(i for i in producer[value].inputs if i)
+        return sorted(found)
+
+    blocked: set[str] = set()
     for out in selected:
         reached: list[str] = []
         seen: set[str] = set()
@@ -376,15 +392,18 @@ def build_training_graph(
             if op.op_type not in DIFFERENTIABLE:
                 touches = any(i in parameter_of_value or i in producer for i in op.inputs if i)
                 if touches:
+                    # the issue names the parameters it cuts off from the output
+                    behind = upstream_parameters(op.inputs)
                     report.backward_issues.append(
                         f"{op.op_type} node '{op.name}' on the path to output '{out}' has no "
-                        "backward rule"
+                        "backward rule" + (f" (blocks {', '.join(behind)})" if behind else "")
                     )
+                    blocked.update(behind)
                 continue
             stack.extend(i for i in op.inputs if i)
         report.output_parameters[out] = sorted(set(reached))
     used = {p for names in report.output_parameters.values() for p in names}
-    report.unused_parameters = sorted(set(parameters) - used)
+    report.unused_parameters = sorted(set(parameters) - used - blocked)
 
     return TrainingGraph(
         ops=ops,
