@@ -181,3 +181,21 @@ def test_selected_output_reports_influencing_blocked_and_unused_parameters():
     with pytest.raises(ValueError, match="not trainable"):
         diagnostic.require_trainable()
 
+
+def test_operator_without_backward_rule_is_reported_by_name():
+    """A Det after a Gemm (trainability.rs:1477-1505): the model is not
+    trainable and the printed report names the node, so the user can act."""
+    from tynx_b200.onnx import ir, proto
+
+    z = lambda *shape: np.zeros(shape, np.float32)  # noqa: E731
+    data = proto.encode_model(
+        [proto.encode_node("Gemm", ["x", "matrix.weight", "matrix.bias"], ["matrix_value"], name="matrix"),
+         proto.encode_node("Det", ["matrix_value"], ["score"], name="determinant")],
+        [proto.encode_tensor("matrix.weight", z(2, 2)), proto.encode_tensor("matrix.bias", z(2))],
+        [proto.encode_value_info("x", proto.FLOAT, [1, 2])],
+        [proto.encode_value_info("score", proto.FLOAT, [1])])
+    report = ir.load_training_graph(data).report
+    assert not report.is_trainable
+    assert report.backward_issues and "Det" in report.backward_issues[0]
+    assert "determinant" in str(report)
+
