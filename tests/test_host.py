@@ -199,3 +199,18 @@ def test_operator_without_backward_rule_is_reported_by_name():
     assert report.backward_issues and "Det" in report.backward_issues[0]
     assert "determinant" in str(report)
 
+
+def test_trainability_report_entries_read_by_key(fixtures):
+    """Report entries answer by key as the reference's Python report does
+    (test_imported_model.py:401-454): roles, and synthetic_name False for an
+    initializer that keeps its ONNX name."""
+    import tynx_b200 as tx
+    from tynx_b200.onnx import ir
+
+    report = ir.load_training_graph(fixtures["_MATMUL_MODEL"]).report
+    assert isinstance(report, tx.TrainabilityReport)
+    assert report.trainable_parameters == ["encoder.weight"]
+    assert report.initializers[0]["synthetic_name"] is False
+    assert report.initializers[0]["role"] == report.initializers[0].role == "parameter"
+    assert "Trainable parameters" in str(report)
+

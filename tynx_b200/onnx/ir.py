@@ -108,11 +108,17 @@ class InitializerUse:
 
 @dataclass
 class InitializerReport:
+    """One initializer's entry in the report; read by attribute or, as the
+    reference's Python report entries are, by key (``entry["role"]``).
+    ``synthetic_name`` is True for a name the importer generated; names here
+    are always the ONNX initializer's own or the caller's override."""
+
     name: str
     role: str
     dtype: str
     shape: tuple
     uses: list[InitializerUse] = field(default_factory=list)
+    synthetic_name: bool = False
 
     def as_dict(self) -> dict:
         return {
@@ -121,7 +127,11 @@ class InitializerReport:
             "dtype": self.dtype,
             "shape": list(self.shape),
             "uses": [u.__dict__ for u in self.uses],
+            "synthetic_name": self.synthetic_name,
         }
+
+    def __getitem__(self, key: str):
+        return self.as_dict()[key]
 
 
 @dataclass
