@@ -360,3 +360,66 @@ def test_reference_finite_difference_points(tx, expected):
                                     c["epsilon"])
     assert x.grad.flatten().tolist()[c["element"]] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
 
+
+_HEAD = {"weight": "head.weight", "bias": "head.bias"}
+
+
+def test_model_report_output_selection_and_strict_state_dict(tx, fixtures):
+    """The model's structured, output-specific trainability report and its
+    strict state_dict (test_imported_model.py:369-419)."""
+    model = _load(tx, fixtures, "_GEMM_MODEL", initializer_names=_HEAD)
+    report = model.trainability_report()
+    out = model.outputs[0]
+    assert isinstance(report, tx.TrainabilityReport)
+    assert report.is_trainable is True
+    assert report.selected_outputs == [out]
+    assert sorted(report.trainable_parameters) == ["head.bias", "head.weight"]
+    assert sorted(report.output_parameters[out]) == ["head.bias", "head.weight"]
+    assert report.backward_issues == []
+    assert {entry["role"] for entry in report.initializers} >= {"parameter"}
+    assert "Trainable parameters" in str(report)
+    report.require_trainable()
+    assert model.require_trainable(outputs=[out]).selected_outputs == [out]
+    with pytest.raises(ValueError, match=r"requested output.*not a declared"):
+        model.require_trainable(outputs=["missing"])
+    state = model.state_dict()
+    assert sorted(state) == ["head.bias", "head.weight"]
+    with pytest.raises(ValueError, match="state_dict key mismatch"):
+        model.load_state_dict({"head.weight": state["head.weight"]})
+
+
+def test_simplified_model_keeps_declared_output_names(tx, fixtures):
+    """test_imported_model.py:422-438."""
+    model = tx.load(fixtures["_GEMM_MODEL"], trainable="auto", simplify=True, initializer_names=_HEAD)
+    assert model.outputs == ["y"]
+    report = model.trainability_report()
+    assert report.selected_outputs == ["y"] and "y" in report.output_parameters
+    selected = model.require_trainable(outputs=["y"])
+    assert selected.selected_outputs == ["y"] and "y" in selected.output_parameters
+
+
+@pytest.mark.parametrize("simplify", [False, True])
+def test_matmul_initializer_keeps_its_onnx_name(tx, fixtures, simplify):
+    """test_imported_model.py:441-453."""
+    model = tx.load(fixtures["_MATMUL_MODEL"], trainable="auto", simplify=simplify)
+    assert [name for name, _ in model.named_parameters()] == ["encoder.weight"]
+    report = model.trainability_report()
+    assert report.trainable_parameters == ["encoder.weight"]
+    assert report.initializers[0]["synthetic_name"] is False
+    assert model(tx.Tensor([[3.0], [4.0]])).flatten().tolist() == [6.0, 8.0]
+
+
+def test_no_grad_call_is_detached_and_plain_load_is_inference(tx, fixtures):
+    """test_imported_model.py:378-398."""
+    model = tx.load(fixtures["_GEMM_MODEL"], trainable=True, simplify=False, initializer_names=_HEAD)
+    with tx.no_grad():
+        output = model(tx.Tensor([[2.0], [-1.0]], requires_grad=True))
+    assert output.requires_grad is False
+    session = tx.load(fixtures["_GEMM_MODEL"], simplify=False)
+    assert isinstance(session, tx.Session)
+    x = tx.Tensor([[2.0], [-1.0]], requires_grad=True)
+    positional, named = session(x), session.run(x=x)
+    assert isinstance(positional, tx.Tensor) and isinstance(named, tx.Tensor)
+    assert positional.flatten().tolist() == pytest.approx([5.0, -1.0])
+    assert named.flatten().tolist() == pytest.approx([5.0, -1.0])
+
