@@ -466,19 +466,22 @@ class ImportedModel:
 
     # -- call ------------------------------------------------------------------------------
     def _bind(self, args, kwargs) -> list[Tensor]:
+        """Positional inputs in declaration order, then named ones; the
+        TypeErrors name what is missing, unexpected or given twice, in the
+        reference's wording (test_imported_model.py:483-487)."""
         names = self.inputs
         if len(args) > len(names):
             raise TypeError(f"model takes {len(names)} inputs, got {len(args)}")
         bound: dict[str, object] = dict(zip(names, args))
         for key, value in kwargs.items():
             if key not in names:
-                raise TypeError(f"unknown model input {key!r}; inputs are {names}")
+                raise TypeError(f"unexpected input {key!r}; the model's inputs are {names}")
             if key in bound:
-                raise TypeError(f"input {key!r} given twice")
+                raise TypeError(f"got multiple values for input {key!r}")
             bound[key] = value
         missing = [n for n in names if n not in bound]
         if missing:
-            raise TypeError(f"missing model inputs {missing}")
+            raise TypeError(f"missing required inputs {missing}")
         tensors = []
         for name, dtype, rank in zip(names, self._input_dtypes, self._input_ranks):
             value = bound[name]
