@@ -423,3 +423,42 @@ def test_no_grad_call_is_detached_and_plain_load_is_inference(tx, fixtures):
     assert positional.flatten().tolist() == pytest.approx([5.0, -1.0])
     assert named.flatten().tolist() == pytest.approx([5.0, -1.0])
 
+
+def test_model_binds_named_inputs_and_returns_named_outputs(tx, fixtures):
+    """Two inputs, two outputs (test_imported_model.py:456-487): positional and
+    named binding, a dict of outputs in declaration order, input gradients,
+    and the binding errors."""
+    model = _load(tx, fixtures, "_MULTI_MODEL")
+    first = tx.Tensor([[1.0], [2.0]], requires_grad=True)
+    second = tx.Tensor([[3.0], [4.0]], requires_grad=True)
+    positional = model(first, second)
+    assert isinstance(positional, dict) and list(positional) == model.outputs
+    assert positional[model.outputs[0]].flatten().tolist() == pytest.approx([4.0, 6.0])
+    assert positional[model.outputs[1]].flatten().tolist() == pytest.approx([3.0, 8.0])
+    named = model(**{model.inputs[1]: second, model.inputs[0]: first})
+    (named[model.outputs[0]].sum() + named[model.outputs[1]].sum()).backward()
+    assert first.grad.flatten().tolist() == pytest.approx([4.0, 5.0])
+    assert second.grad.flatten().tolist() == pytest.approx([2.0, 3.0])
+    with pytest.raises(TypeError, match="missing required inputs"):
+        model(first)
+    with pytest.raises(TypeError, match="unexpected input"):
+        model(first, unknown=second)
+    with pytest.raises(TypeError, match="multiple values"):
+        model(first, **{model.inputs[0]: second, model.inputs[1]: second})
+
+
+def test_conv_weights_and_bias_train_in_place(tx, fixtures):
+    """800 SGD steps fit the imported convolution to its target
+    (test_imported_model.py:182-199)."""
+    model = _load(tx, fixtures, "_CONV_MODEL")
+    opt = tx.optim.SGD(model.named_parameters(), lr=0.05)
+    x = tx.Tensor([[[[1.0, 2.0], [3.0, 4.0]]]])
+    target = tx.Tensor([[[[3.0, 5.0], [7.0, 9.0]]]])
+    for _ in range(800):
+        opt.zero_grad()
+        tx.nn.functional.mse_loss(model(x), target).backward()
+        opt.step()
+    assert model(x).flatten().tolist() == pytest.approx(target.flatten().tolist(), abs=1e-3)
+    params = dict(model.named_parameters())
+    assert params["weight"].grad is not None and params["bias"].grad is not None
+
