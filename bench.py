@@ -1,7 +1,11 @@
 """Training-step throughput of the B200 engine (samples/s, fwd+bwd+Adam).
 
-Default workload: the MLP classifier (784->1024 relu ->1024 relu ->10, fp32
-storage, global batch 4096 sharded across ranks, cross-entropy, Adam 1e-3).
+Default workload: the transformer encoder fine-tune (token + positional
+embedding 8192x256 / 128x256, four pre-norm layers of d_model 256, 4 heads, FFN
+1024 GELU, mean-pool, Gemm 256->2; global batch 256 sequences x 128 tokens
+sharded across ranks; cross-entropy; Adam 1e-4), the largest of the five
+configurations on one GPU.  ``--workload`` selects another one
+(mlp_policy, mlp_classifier, ppo, cnn).
 One step = zero_grad, forward, fused softmax-cross-entropy, backward (with the
 NCCL gradient all-reduce inside backward when N > 1) and one Adam step,
 captured once with ``tynx_b200.compile`` and replayed as a CUDA graph.
@@ -16,7 +20,9 @@ the K step times; barrier + synchronize on both sides; the job time is the max
 over ranks.  ``e2e`` repeats the measurement through the public API with the
 step's inputs copied from pinned host memory and the loss read back each step
 (host clock, max over ranks).  ``--impl reference`` times the CPU oracle (the
-numpy restatement of the reference's Flex training step) on a bounded sample.
+numpy restatement of the reference's Flex training step) with every host
+thread, each step on a bounded sample of the global batch; it imports only the
+host-side workload and ONNX modules, never the CUDA library.
 """
 
 from __future__ import annotations
@@ -30,6 +36,12 @@ import tempfile
 import threading
 import time
 from pathlib import Path
+
+if "--impl" in sys.argv and "reference" in sys.argv:
+    # The CPU arm uses every host thread for BLAS, whatever the launcher set
+    # (torchrun exports OMP_NUM_THREADS=1 to every rank).
+    for _var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_var] = str(os.cpu_count() or 1)
 
 import numpy as np
 
@@ -138,54 +150,96 @@ def _cpu_step_fn(wl):
     return step
 
 
+def _head(batch: dict, rows: int) -> dict:
+    """The first `rows` samples of a batch (every per-sample array sliced)."""
+    return {k: (v[:rows] if isinstance(v, np.ndarray) and v.ndim >= 1 else v) for k, v in batch.items()}
+
+
+def _sample_rows(wl, step, per_step_s: float) -> tuple[int, float]:
+    """Rows of the global batch one CPU step may take so that it lasts about
+    per_step_s: one cold step on 1/16 of the batch, then a timed one, scaled."""
+    rows = max(1, wl.batch // 16)
+    step(_head(wl.make_batch(0), rows))  # cold
+    t0 = time.perf_counter()
+    step(_head(wl.make_batch(1), rows))
+    per_row = (time.perf_counter() - t0) / rows
+    fit = int(per_step_s / max(per_row, 1e-9))
+    # a power-of-two fraction of the batch, at least 1/16 of it
+    sample = wl.batch
+    while sample > rows and sample > fit:
+        sample //= 2
+    return sample, per_row
+
+
+def bench_config(wl, world: int) -> dict:
+    """The workload description both arms print (identical dicts)."""
+    return {"workload": wl.name, "global_batch": wl.batch, "per_gpu_batch": wl.batch // world,
+            "parallelism": f"dp{world}", "l2": "flushed between steps (512 MiB write)",
+            "flop_per_step": wl.flop_per_step}
+
+
 def cpu_baseline(wl, budget_s: float = 15.0) -> dict:
-    """Time the oracle's step on the host cores (bounded sample)."""
+    """Time the oracle's step on the host cores: a bounded sample of the
+    workload (whole steps on a slice of the global batch), all host threads."""
     step = _cpu_step_fn(wl)
-    b0 = wl.make_batch(0)
-    step(b0)  # cold step, excluded
+    sample, _ = _sample_rows(wl, step, budget_s / 8)
     times = []
     start = time.perf_counter()
-    i = 1
+    i = 2
     while time.perf_counter() - start < budget_s and i < 50:
+        b = _head(wl.make_batch(i), sample)
         t0 = time.perf_counter()
-        step(wl.make_batch(i))
+        step(b)
         times.append(time.perf_counter() - t0)
         i += 1
     med = float(np.median(times))
     cores = os.cpu_count() or 1
-    return {"value": wl.batch / med, "unit": "samples/s", "cores": cores, "kind": "port",
-            "sample": f"{len(times)} full {wl.name} steps (batch {wl.batch}) of the numpy oracle "
-                      f"(multithreaded BLAS, {cores} host threads), median step {med * 1e3:.1f} ms"}
+    return {"value": sample / med, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} {wl.name} training steps of the numpy oracle on {sample} of the "
+                      f"{wl.batch} samples of a global batch (multithreaded BLAS, {cores} host "
+                      f"threads), median step {med * 1e3:.1f} ms"}
 
 
 def run_reference(args) -> None:
+    """The reference arm: the oracle's training step (the CPU restatement of the
+    reference's Flex step), every host thread, on a bounded sample per step.
+    Under torchrun only rank 0 runs; the other ranks exit without work."""
     world, rank, _ = _dist_env()
     if rank != 0:
         return
-    from tynx_b200 import workloads
+    from tynx_b200 import workloads  # host-side module: the CUDA library stays unmapped
 
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(os.cpu_count() or 1)
+    except Exception:  # pragma: no cover - the environment variables already ask for it
+        pass
     wl = workloads.WORKLOADS[args.workload]()
     step = _cpu_step_fn(wl)
+    # the whole run (warm-up + timed) stays near two minutes of host time
+    sample, _ = _sample_rows(wl, step, 120.0 / (args.steps + args.warmup))
     for i in range(args.warmup):
-        step(wl.make_batch(i))
+        step(_head(wl.make_batch(i), sample))
     times = []
     for i in range(args.steps):
-        b = wl.make_batch(args.warmup + i)
+        b = _head(wl.make_batch(args.warmup + i), sample)
         t0 = time.perf_counter()
         step(b)
         times.append(time.perf_counter() - t0)
     total = float(sum(times))
-    value = wl.batch * args.steps / total
+    value = sample * args.steps / total
     cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": "train samples/s (fwd+bwd+Adam)", "value": value,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "global_batch": wl.batch},
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy; BASELINE names no dataset)",
+        "config": bench_config(wl, world),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} steps of the numpy restatement of the Flex "
-                                   f"training step at batch {wl.batch} ({cores} host threads)"},
+                         "sample": f"each step: the numpy restatement of the Flex training step on "
+                                   f"{sample} of the {wl.batch} samples of the global batch "
+                                   f"({cores} host threads)"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -197,7 +251,7 @@ def main() -> None:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--workload", default="mlp_classifier")
+    parser.add_argument("--workload", default="transformer")
     parser.add_argument("--math", default="tf32", choices=["tf32", "3xtf32", "fp32", "tf32trunc"])
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -374,10 +428,8 @@ def main() -> None:
             "vs_baseline": None,
             "dtype": "tf32" if args.math == "tf32" else args.math,
             "data": "synthetic (seeded numpy; BASELINE names no dataset)",
-            "config": {"workload": wl.name, "global_batch": wl.batch, "per_gpu_batch": per_rank,
-                       "parallelism": f"dp{world}", "math": args.math,
-                       "l2": "flushed between steps (512 MiB write)",
-                       "flop_per_step": wl.flop_per_step},
+            "config": bench_config(wl, world),
+            "math": args.math,
             "achieved_tflops": wl.flop_per_step / (ms_per_step / 1e3) / 1e12,
             "roofline": roofline,
             "e2e": e2e,

@@ -5,7 +5,8 @@
  * The reference (blaind/tynx) runs every tensor operation through Burn
  * (burn-flex on CPU, burn-autodiff for backward rules, CubeCL/wgpu on GPUs);
  * there is no C ABI upstream.  This header is the drop-in boundary a
- * `tynx-cuda-sys` crate binds with `extern "C"`.  Each
+ * `tynx-cuda-sys` crate binds with `extern "C"` (crates/tynx-cuda-sys in this
+ * repository holds that block as Rust source).  Each
  * group names the reference function or type it replaces (path:line inside
  * the reference project).
  *
@@ -107,8 +108,10 @@ int tx_host_alloc(size_t bytes, void **h_out); /* pinned host memory */
  * not order the compute stream.  tx_prefetch_get returns the buffer of the
  * oldest queued batch and orders all compute work issued after it behind that
  * batch's copy.  A buffer is refilled only after the compute work issued
- * before the get that followed its previous batch, so a batch returned by get
- * stays valid until depth - 1 further gets.  With depth 3: put batches 0 and 1,
+ * before the get that followed its previous batch: a batch returned by get
+ * stays valid for the device work issued before the next get (work issued
+ * after that get may see the buffer refilled), while up to depth - 1 further
+ * batches upload beside it.  With depth 3: put batches 0 and 1,
  * then per step get, launch the step, put the batch two ahead, read the loss.
  * put fails (TX_ERR_INVALID) when it would run more than depth - 1 batches
  * ahead of get.  Neither call is allowed during a capture. */
@@ -171,9 +174,15 @@ typedef struct tx_gemm_desc {
 /* flags: in TX_MATH_TF32 (round-to-nearest) mode the contraction rounds each
  * operand element to TF32 (cvt.rna).  An operand whose buffer already holds
  * such values (A_TF32 / B_TF32) is used as is; ROUND_OUT stores C rounded the
- * same way, for a result that only feeds further contractions.  Other math
- * modes ignore the flags. */
-enum { TX_GEMM_A_TF32 = 1, TX_GEMM_B_TF32 = 2, TX_GEMM_ROUND_OUT = 4 };
+ * same way, for a result that only feeds further contractions.  EXACT asks
+ * for fp32-class accuracy in that mode (3xTF32: each operand split into a
+ * TF32 head and a TF32 tail, three products per k-block); it overrides
+ * A_TF32 / B_TF32, so both operands must hold unrounded values.  The graph
+ * engine sets it on forward contractions whose result passes through a ReLU,
+ * whose mask is discontinuous: a TF32 rounding of the pre-activation flips it
+ * wherever the value lies within ~2^-11 of zero, and every flip moves a whole
+ * gradient entry.  Other math modes ignore the flags. */
+enum { TX_GEMM_A_TF32 = 1, TX_GEMM_B_TF32 = 2, TX_GEMM_ROUND_OUT = 4, TX_GEMM_EXACT = 8 };
 int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc);
 /* dst[i] = src[i] rounded to TF32 (round to nearest, ties away from zero;
  * dst may equal src).  The operand shadow of TX_GEMM_A_TF32 / B_TF32. */

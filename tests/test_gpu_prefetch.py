@@ -60,6 +60,35 @@ def test_buffer_refill_waits_for_earlier_readers():
     pf.close()
 
 
+def test_depth_three_refill_waits_for_readers_issued_before_the_next_get():
+    """With depth 3, batch g is valid for work issued before get g + 1 while
+    two more batches upload; put g + 3 refills its buffer only after that work."""
+    import tynx_b200 as tx
+
+    host = _batches(5, rows=256, cols=256)
+    pf = tx.Prefetcher(*host[0], depth=3)
+    a = tx.randn(4096, 4096)
+    pf.put(*host[0])
+    pf.put(*host[1])
+    pf.put(*host[2])
+    x0, _ = pf.get()
+    slow = tx.matmul(tx.matmul(a, a), a)
+    s0 = (x0 * 1.0).sum()  # reads buffer 0 behind the products, before the next get
+    x1, _ = pf.get()       # releases buffer 0 for put 3
+    pf.put(*host[3])       # refills buffer 0: must wait for the read above
+    s1 = (x1 * 1.0).sum()
+    x2, _ = pf.get()
+    pf.put(*host[4])       # refills buffer 1 after the read of x1
+    x3, _ = pf.get()
+    for got, want in ((s0, host[0][0]), (s1, host[1][0])):
+        want = float(want.astype(np.float64).sum())
+        assert abs(float(got.item()) - want) <= 1e-3 * max(1.0, abs(want)), (float(got.item()), want)
+    np.testing.assert_array_equal(x2.numpy(), host[2][0])
+    np.testing.assert_array_equal(x3.numpy(), host[3][0])
+    assert np.isfinite(float(slow.sum().item()))
+    pf.close()
+
+
 def test_put_refuses_to_run_past_the_ring():
     import tynx_b200 as tx
 

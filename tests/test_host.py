@@ -214,3 +214,47 @@ def test_trainability_report_entries_read_by_key(fixtures):
     assert report.initializers[0]["role"] == report.initializers[0].role == "parameter"
     assert "Trainable parameters" in str(report)
 
+
+
+def test_checkpoint_arguments_and_payload_validation(tmp_path):
+    """Host-side checkpoint rules: both argument orders, and the payload checks
+    of ``crates/tynx-python/python/tynx/checkpoint.py:314-331``."""
+    import json
+
+    from tynx_b200 import checkpoint as ck
+
+    class Opt:
+        def state_dict(self):
+            return {}
+
+        def load_state_dict(self, state):
+            pass
+
+    model, opt = object(), Opt()
+    assert ck._split_args("a.json", model, opt, "save")[1:] == (model, opt)
+    assert ck._split_args(model, opt, "a.json", "load")[1:] == (model, opt)
+    assert ck._split_args(model, "a.json", None, "save")[1:] == (model, None)
+    with pytest.raises(TypeError, match="expects"):
+        ck._split_args(model, opt, None, "save")
+    with pytest.raises(TypeError, match="must provide state_dict"):
+        ck._split_args("a.json", model, object(), "save")
+    with pytest.raises(ValueError, match="requires its optimizer"):
+        ck._check_scheduler(None, object())
+    path = tmp_path / "x.json"
+    path.write_text("{not json")
+    with pytest.raises(ValueError, match="invalid Tynx checkpoint JSON"):
+        ck._read(path)
+    path.write_text(json.dumps({"format": "other", "version": 1}))
+    with pytest.raises(ValueError, match="not a Tynx training checkpoint"):
+        ck._read(path)
+    path.write_text(json.dumps({"format": "tynx.training", "version": 7}))
+    with pytest.raises(ValueError, match="unsupported Tynx checkpoint version 7"):
+        ck._read(path)
+    assert ck._encode({"b": (1, 2.5), "a": [None, True]}) == \
+        {"b": {"__type__": "tuple", "items": [1, 2.5]}, "a": [None, True]}
+    with pytest.raises(TypeError, match="string keys"):
+        ck._encode({1: 2})
+    with pytest.raises(ValueError, match="unknown checkpoint value type"):
+        ck._decode({"__type__": "set"})
+    with pytest.raises(ValueError, match="does not match declared shape"):
+        ck._decode({"__type__": "tensor", "dtype": "float32", "shape": [2], "data": [1.0]})

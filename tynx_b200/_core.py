@@ -1042,8 +1042,10 @@ class Prefetcher:
             loss.item()
 
     so the uploads run while the steps do.  Sources should be page-locked
-    (``pinned``) and must stay alive and unchanged until their upload has run;
-    a batch from ``get`` stays valid for ``depth - 1`` further gets.
+    (``pinned``) and must stay alive and unchanged until their upload has run.
+    A batch from ``get`` stays valid for the device work issued before the
+    next ``get``: after that call its buffer may be refilled by a ``put``, so
+    keep a copy (``clone()``) of anything needed longer.
     """
 
     def __init__(self, *like, depth: int = 3, device: Optional[Device] = None):

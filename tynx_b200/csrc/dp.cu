@@ -73,16 +73,25 @@ extern "C" int tx_dp_init(tx_ctx *ctx, int world, int rank, const uint8_t *id128
   DpState *s = new DpState();
   ncclResult_t r = ncclCommInitRankConfig(&s->comm, world, id, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
+    if (s->comm) ncclCommAbort(s->comm);
     delete s;
     return nccl_fail(ctx, r, "ncclCommInitRankConfig");
   }
   int rc = nccl_wait(ctx, s->comm, timeout_ms, "communicator initialisation");
   if (rc != TX_OK) {
+    // nccl_wait aborts the communicator itself when its deadline expires
+    if (rc != TX_ERR_TIMEOUT) ncclCommAbort(s->comm);
     delete s;
     return rc;
   }
-  cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming);
-  cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming);
+  cudaError_t e = cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    if (s->fork) cudaEventDestroy(s->fork);
+    ncclCommAbort(s->comm);
+    delete s;
+    return tx_cuda_fail(ctx, e, "tx_dp_init: event creation");
+  }
   ctx->nccl = s;
   ctx->world = world;
   ctx->rank = rank;

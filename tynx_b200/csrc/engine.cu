@@ -431,6 +431,14 @@ struct GNode {
   // channels-last and the producer applies act' elementwise
   bool nhwc_out = false;
   bool nhwc_in = false;
+  // TF32 mode: a forward contraction whose result passes through a ReLU runs
+  // to fp32-class accuracy (TX_GEMM_EXACT) on unrounded operands.  The mask
+  // is discontinuous: a TF32 rounding of the pre-activation flips it wherever
+  // the value lies within ~2^-11 of zero, and each flip moves a whole gradient
+  // entry (on the MLP classifier at batch 4096 ~900 flips of 8M, a 2e-3
+  // relative error of the first layer's weight gradient).  Its backward
+  // products stay TF32.
+  bool exact = false;
 };
 
 struct tx_graph {
@@ -747,6 +755,15 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     a.fused_into = i;
   }
 
+  // ---- exact forward products under a ReLU mask ----------------------------------------------
+  for (int i = 0; i < n_nodes; ++i) {
+    GNode &n = g->nodes[i];
+    if (n.d.op != TX_OP_GEMM && n.d.op != TX_OP_MATMUL && n.d.op != TX_OP_CONV) continue;
+    bool relu = n.fused_act == TX_ACT_RELU;
+    for (int c : g->values[n.d.out[0]].consumers) relu |= g->nodes[c].d.op == TX_OP_RELU;
+    n.exact = relu;
+  }
+
   // ---- channels-last hand-off between consecutive convolutions --------------------------------
   for (int i = 0; i < n_nodes; ++i) {
     GNode &n = g->nodes[i];
@@ -791,6 +808,7 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
     for (int c : gv.consumers) {
       const tx_node_desc &cd = g->nodes[c].d;
       if (cd.op == TX_OP_GEMM || cd.op == TX_OP_MATMUL) {
+        if (g->nodes[c].exact) return false;  // reads the unrounded operand
         for (int k = 2; k < cd.n_in; ++k)
           if (cd.in[k] == v) return false;  // a bias is not a contraction operand
       } else if (is_alias_op(cd.op) || cd.op == TX_OP_TRANSPOSE) {
@@ -1001,8 +1019,12 @@ namespace {
 // Pointer a contraction reads value v from, and whether those values are
 // already TF32-rounded (TX_GEMM_A_TF32 / B_TF32): parameters come from the
 // rounded shadow refreshed at the start of the forward.
-const float *gemm_operand(tx_graph *g, tx_record *r, int v, bool *tf32) {
+const float *gemm_operand(tx_graph *g, tx_record *r, int v, bool *tf32, bool exact = false) {
   const GValue &gv = g->values[v];
+  if (exact) {  // the unrounded values (parameters from the flat buffer itself)
+    *tf32 = false;
+    return (const float *)r->buf[v];
+  }
   if (r->shadow && gv.kind == TX_VAL_PARAM) {
     *tf32 = true;
     return g->flat_tf32 + g->param_offset[gv.param_index];
@@ -1044,6 +1066,7 @@ struct Fwd {
     q.batch = 1;
     q.act = n.fused_act;
     bool a32 = false, b32 = false;
+    const bool ex = n.exact && ctx->math == TX_MATH_TF32;
     if (n.fused_act == TX_ACT_GELU) {
       r->extra[ni] = tx_alloc_raw(ctx, numel_of(S(yv)) * 4);
       if (!r->extra[ni]) return TX_ERR_OOM;
@@ -1054,9 +1077,9 @@ struct Fwd {
       q.M = q.trans_a ? a[1] : a[0];
       q.K = q.trans_a ? a[0] : a[1];
       q.N = q.trans_b ? b[0] : b[1];
-      q.A = gemm_operand(g, r, d.in[0], &a32);
+      q.A = gemm_operand(g, r, d.in[0], &a32, ex);
       q.lda = a[1];
-      q.B = gemm_operand(g, r, d.in[1], &b32);
+      q.B = gemm_operand(g, r, d.in[1], &b32, ex);
       q.ldb = b[1];
       q.alpha = (float)d.fattr[0];
       if (d.n_in > 2 && d.in[2] >= 0) {
@@ -1072,17 +1095,17 @@ struct Fwd {
       q.N = b.back();
       if (b.size() == 2) {
         q.M = numel_of(a) / q.K;
-        q.A = gemm_operand(g, r, d.in[0], &a32);
+        q.A = gemm_operand(g, r, d.in[0], &a32, ex);
         q.lda = q.K;
-        q.B = gemm_operand(g, r, d.in[1], &b32);
+        q.B = gemm_operand(g, r, d.in[1], &b32, ex);
         q.ldb = q.N;
       } else {
         q.M = a[a.size() - 2];
         q.batch = numel_of(a) / (q.M * q.K);
-        q.A = gemm_operand(g, r, d.in[0], &a32);
+        q.A = gemm_operand(g, r, d.in[0], &a32, ex);
         q.lda = q.K;
         q.stride_a = q.M * q.K;
-        q.B = gemm_operand(g, r, d.in[1], &b32);
+        q.B = gemm_operand(g, r, d.in[1], &b32, ex);
         q.ldb = q.N;
         q.stride_b = q.K * q.N;
         q.stride_c = q.M * q.N;
@@ -1095,7 +1118,7 @@ struct Fwd {
       q.ld_preact = q.N;
     }
     q.alpha *= n.out_scale;
-    q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0);
+    q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0) | (ex ? TX_GEMM_EXACT : 0);
     if (n.round_out && ctx->math == TX_MATH_TF32) {
       q.flags |= TX_GEMM_ROUND_OUT;
       r->tf32[yv] = true;
@@ -1112,7 +1135,8 @@ struct Fwd {
     const Shape &y = S(d.out[0]);
     const ConvGeom cg = conv_geom(x, w, y, d);
     const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
-    const bool tf32 = ctx->math == TX_MATH_TF32;
+    const bool ex = n.exact && ctx->math == TX_MATH_TF32;
+    const bool tf32 = ctx->math == TX_MATH_TF32 && !ex;
     // channels-last input, (kh, kw, c) columns, weights permuted to match;
     // in TF32 mode both operands are stored rounded, so the GEMM reads them as is
     Scratch xh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
@@ -1143,7 +1167,7 @@ struct Fwd {
       q.bias_scale = 1.f;
     }
     q.act = n.fused_act;
-    q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : 0;
+    q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : ex ? TX_GEMM_EXACT : 0;
     TX_TRY(gemm_dispatch(ctx, q));
     if (n.nhwc_out) return TX_OK;  // the next convolution reads [N][OH][OW][OC]
     return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);

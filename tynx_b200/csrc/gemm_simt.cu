@@ -329,8 +329,14 @@ int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc, bool *rounded) {
   FusedSum *pfs = want ? &fs : nullptr;
   int rc = gemm_skinny(ctx, d, pfs);
   if (rc == TX_ERR_UNSUPPORTED && ctx->math != TX_MATH_FP32) {
-    const int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
-    rc = gemm_tcgen05(ctx, d, mode, pfs);
+    int mode = ctx->math == TX_MATH_3XTF32 ? 2 : ctx->math == TX_MATH_TF32_TRUNC ? 0 : 1;
+    tx_gemm_desc e = d;
+    if (ctx->math == TX_MATH_TF32 && (d.flags & TX_GEMM_EXACT)) {
+      // fp32-class product in TF32 mode: both operands are split in the kernel
+      mode = 2;
+      e.flags &= ~(TX_GEMM_A_TF32 | TX_GEMM_B_TF32);
+    }
+    rc = gemm_tcgen05(ctx, e, mode, pfs);
   }
   if (rc == TX_ERR_UNSUPPORTED) {
     tx_gemm_desc q = d;

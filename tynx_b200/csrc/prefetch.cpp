@@ -10,7 +10,9 @@
 // before this get has been issued, which includes the readers of the batch
 // handed out by the previous get) and ordering the compute stream after that
 // batch's copy.  Batch n's copy waits for the mark of get n - depth + 1, after
-// which nothing reads the batch that buffer held before.
+// which nothing reads the batch that buffer held before.  So a batch handed
+// out by get g is valid for work issued before get g + 1, while batches
+// g + 1 .. g + depth - 1 upload into the other buffers.
 #include <vector>
 
 #include "common.h"

@@ -423,14 +423,16 @@ class ImportedModel:
     def state_dict(self) -> dict[str, Tensor]:
         return {name: p.detach() for name, p in self._params.items()}
 
-    def load_state_dict(self, state: dict, strict: bool = True) -> None:
-        missing = sorted(set(self._params) - set(state))
-        unexpected = sorted(set(state) - set(self._params))
-        if strict and (missing or unexpected):
-            raise ValueError(f"state_dict key mismatch: missing {missing}, unexpected {unexpected}")
-        for name, value in state.items():
-            if name in self._params:
-                self._params[name].copy_(value)
+    def load_state_dict(self, state: dict, strict: bool = True):
+        """Copy tensors into the live parameters by name after validating every
+        name, shape and dtype (``crates/tynx-python/python/tynx/nn/state.py``
+        ``_prepare_state_dict_load``); returns the missing and unexpected names."""
+        from .checkpoint import prepare_model_state
+
+        names, result = prepare_model_state(self, state, strict)
+        for name in names:
+            self._params[name].copy_(state[name])
+        return result
 
     def trainability_report(self) -> ir.TrainabilityReport:
         return self._graph_ir.report

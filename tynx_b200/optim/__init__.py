@@ -25,11 +25,16 @@ from ..imported import Parameter
 _KIND = {"adam": 0, "adamw": 1, "sgd": 2}
 
 
-def _collect(parameters) -> list[Parameter]:
+def _collect(parameters) -> tuple[list[Parameter], Optional[list[str]]]:
+    """Unique parameters in first-occurrence order, and their names when the
+    optimizer was built from ``named_parameters()`` (the names key its state
+    dictionary, ``crates/tynx-python/src/optimizer.rs:208-217``)."""
     items = list(parameters)
     if not items:
         raise ValueError("optimizer requires at least one Parameter")
     out: list[Parameter] = []
+    names: list[str] = []
+    named = all(isinstance(item, tuple) for item in items)
     seen: set[int] = set()
     for item in items:
         if isinstance(item, dict):
@@ -40,14 +45,16 @@ def _collect(parameters) -> list[Parameter]:
         if id(p) not in seen:
             seen.add(id(p))
             out.append(p)
-    return out
+            if named:
+                names.append(str(item[0]))
+    return out, (names if named else None)
 
 
 class _Optimizer:
     _kind = "adam"
 
     def __init__(self, parameters, **options):
-        self._params = _collect(parameters)
+        self._params, self._names = _collect(parameters)
         ctx = self._params[0].ctx
         for p in self._params:
             if p.ctx is not ctx:
@@ -57,13 +64,20 @@ class _Optimizer:
         self._cfg.kind = _KIND[self._kind]
         self._options = dict(options)
         self._apply_options()
+        self._handle = None
+        self._create()
+
+    def _create(self) -> None:
+        """(Re)create the native optimizer with zero state for the current options."""
+        if self._handle:
+            lib.tx_optim_destroy(self._handle)
+            self._handle = None
         handle = C.c_void_p()
-        n = len(self._params)
         values = N.ptr_array([p.ptr for p in self._params])
         grads = N.ptr_array([p._grad_ptr for p in self._params])
         numel = N.i64_array([p.numel for p in self._params])
-        ctx.check(lib.tx_optim_create(ctx.handle, C.byref(self._cfg), n, values, grads, numel,
-                                      C.byref(handle)), "optimizer")
+        self._ctx.check(lib.tx_optim_create(self._ctx.handle, C.byref(self._cfg), len(self._params),
+                                            values, grads, numel, C.byref(handle)), "optimizer")
         self._handle = handle
         self._synced = dict(self._options)
 
@@ -126,43 +140,149 @@ class _Optimizer:
         active = (C.c_uint8 * len(self._params))(*[int(p.grad_defined) for p in self._params])
         self._ctx.check(lib.tx_optim_step(self._handle, active), "optimizer step")
 
+    # -- state dictionaries (crates/tynx-python/src/optimizer/state.rs) ------------------
+    _STATE_VERSION = 1
+    _TITLE = {"adam": "Adam", "adamw": "AdamW", "sgd": "SGD"}
+
+    def _named(self) -> list[str]:
+        if self._names is None:
+            raise ValueError(f"{self._TITLE[self._kind]}.state_dict() requires construction from "
+                             "model.named_parameters()")
+        return self._names
+
+    def _config_dict(self) -> dict:
+        c = self._cfg
+        if self._kind == "sgd":
+            return {"lr": c.lr, "momentum": c.momentum, "dampening": c.dampening,
+                    "weight_decay": c.weight_decay, "nesterov": bool(c.nesterov)}
+        return {"lr": c.lr, "betas": (c.beta1, c.beta2), "eps": c.eps,
+                "weight_decay": c.weight_decay, "amsgrad": bool(c.amsgrad)}
+
+    def _slots(self) -> tuple:
+        """(state key, native slot) pairs present under the current options."""
+        if self._kind == "sgd":
+            return (("momentum_buffer", 3),) if self._cfg.momentum != 0 else ()
+        slots = (("exp_avg", 0), ("exp_avg_sq", 1))
+        return slots + ((("max_exp_avg_sq", 2),) if self._cfg.amsgrad else ())
+
+    def _state_tensor(self, index: int, which: int) -> Tensor:
+        ptr = C.c_void_p()
+        self._ctx.check(lib.tx_optim_state_ptr(self._handle, index, which, C.byref(ptr)))
+        p = self._params[index]
+        out = Tensor._empty(p.shape, "float32", self._ctx)
+        self._ctx.check(lib.tx_d2d(self._ctx.handle, out.ptr, ptr.value, out.nbytes))
+        return out
+
     def state_dict(self) -> dict:
+        """Name-keyed configuration and adaptive state in the reference's layout:
+        ``version``, ``optimizer``, ``parameter_names`` (sorted), ``config`` and a
+        ``state`` entry (step + moments as Tensors) for every parameter that has
+        been stepped (``adam.rs:339-354``, ``state.rs:71-114``)."""
+        names = self._named()
+        self._sync()
         steps = (C.c_int64 * len(self._params))()
         self._ctx.check(lib.tx_optim_get_steps(self._handle, steps))
         state = {}
-        slots = (("first_moment", 0), ("second_moment", 1)) if self._kind != "sgd" else \
-            (("momentum", 3),) if self._cfg.momentum != 0 else ()
-        if self._kind != "sgd" and self._cfg.amsgrad:
-            slots = slots + (("max_second_moment", 2),)
-        for i, p in enumerate(self._params):
-            entry = {"step": int(steps[i])}
-            for key, which in slots:
+        for i, name in enumerate(names):
+            if steps[i] <= 0:
+                continue
+            entry: dict = {} if self._kind == "sgd" else {"step": int(steps[i])}
+            for key, which in self._slots():
+                entry[key] = self._state_tensor(i, which)
+            if entry:
+                state[name] = entry
+        return {"version": self._STATE_VERSION, "optimizer": self._TITLE[self._kind],
+                "parameter_names": sorted(names), "config": self._config_dict(), "state": state}
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Restore configuration and state by parameter name; nothing changes
+        unless the whole dictionary validates (``state.rs:116-160``,
+        ``optimizer.rs:400-455``)."""
+        title = self._TITLE[self._kind]
+        names = self._named()
+        if not isinstance(state_dict, dict):
+            raise TypeError(f"{title} state_dict must be a dictionary")
+
+        def required(d, key):
+            if key not in d:
+                raise ValueError(f"state_dict is missing field {key!r}")
+            return d[key]
+
+        version = required(state_dict, "version")
+        if version != self._STATE_VERSION:
+            raise ValueError(f"unsupported optimizer state_dict version {version}; "
+                             f"expected {self._STATE_VERSION}")
+        kind = required(state_dict, "optimizer")
+        if kind != title:
+            raise ValueError(f"cannot load {kind} state into {title} optimizer")
+        config = required(state_dict, "config")
+        entries = required(state_dict, "state")
+        if not isinstance(config, dict) or not isinstance(entries, dict):
+            raise TypeError("state_dict fields 'config' and 'state' must be dictionaries")
+        saved = list(required(state_dict, "parameter_names"))
+        if len(set(saved)) != len(saved) or any(not str(n).strip() for n in saved):
+            raise ValueError(f"{title} parameter names must be unique and non-empty")
+        missing = sorted(set(names) - set(saved))
+        unexpected = sorted(set(saved) - set(names))
+        if missing or unexpected:
+            raise ValueError(f"{title} parameter names do not match: missing={missing!r}, "
+                             f"unexpected={unexpected!r}")
+        for name in entries:
+            if name not in set(saved):
+                raise ValueError(f"{title} state for unknown parameter name {name!r}")
+        options = dict(self._options)
+        if self._kind == "sgd":
+            for key in ("lr", "momentum", "dampening", "weight_decay", "nesterov"):
+                options[key] = required(config, key)
+        else:
+            for key in ("lr", "betas", "eps", "weight_decay", "amsgrad"):
+                options[key] = required(config, key)
+            options["betas"] = tuple(options["betas"])
+        index = {n: i for i, n in enumerate(names)}
+        host: dict = {}
+        for name, entry in entries.items():
+            if not isinstance(entry, dict):
+                raise TypeError(f"{title} state for {name!r} must be a dictionary")
+            p = self._params[index[name]]
+            step = 1 if self._kind == "sgd" else required(entry, "step")
+            if self._kind != "sgd" and (not isinstance(step, int) or step <= 0):
+                raise ValueError(f"{title} state step for {name!r} must be positive")
+            arrays = {}
+            keys = [k for k, _ in self._slots_for(options)]
+            for key in keys:
+                value = required(entry, key)
+                array = value.numpy() if isinstance(value, Tensor) else np.asarray(value, np.float32)
+                if tuple(array.shape) != tuple(p.shape):
+                    raise ValueError(f"{title} state {key!r} for {name!r} has shape {array.shape}, "
+                                     f"expected {tuple(p.shape)}")
+                arrays[key] = np.ascontiguousarray(array, dtype=np.float32)
+            host[name] = (int(step), arrays)
+        # everything validated: publish
+        previous = dict(self._options)
+        self._options = options
+        try:
+            self._apply_options()
+        except Exception:
+            self._options = previous
+            self._apply_options()
+            raise
+        self._create()
+        steps = (C.c_int64 * len(self._params))()
+        for name, (step, arrays) in host.items():
+            i = index[name]
+            steps[i] = step
+            for key, which in self._slots():
                 ptr = C.c_void_p()
                 self._ctx.check(lib.tx_optim_state_ptr(self._handle, i, which, C.byref(ptr)))
-                host = np.empty(p.shape, np.float32)
-                self._ctx.check(lib.tx_d2h(self._ctx.handle, host.ctypes.data, ptr.value, host.nbytes))
-                entry[key] = host
-            state[getattr(p, "name", str(i))] = entry
-        return {"kind": self._kind, "options": dict(self._options), "state": state}
-
-    def load_state_dict(self, state: dict) -> None:
-        self._options.update(state.get("options", {}))
-        self._sync()
-        entries = state.get("state", {})
-        steps = (C.c_int64 * len(self._params))()
-        for i, p in enumerate(self._params):
-            entry = entries.get(getattr(p, "name", str(i)))
-            if entry is None:
-                continue
-            steps[i] = int(entry["step"])
-            for key, which in (("first_moment", 0), ("second_moment", 1), ("max_second_moment", 2),
-                               ("momentum", 3)):
-                if key in entry:
-                    ptr = C.c_void_p()
-                    self._ctx.check(lib.tx_optim_state_ptr(self._handle, i, which, C.byref(ptr)))
-                    host = np.ascontiguousarray(entry[key], dtype=np.float32)
-                    self._ctx.check(lib.tx_h2d(self._ctx.handle, ptr.value, host.ctypes.data, host.nbytes))
+                a = arrays[key]
+                self._ctx.check(lib.tx_h2d(self._ctx.handle, ptr.value, a.ctypes.data, a.nbytes))
         self._ctx.check(lib.tx_optim_set_steps(self._handle, steps))
+
+    def _slots_for(self, options: dict) -> tuple:
+        if self._kind == "sgd":
+            return (("momentum_buffer", 3),) if float(options.get("momentum", 0.0)) != 0 else ()
+        slots = (("exp_avg", 0), ("exp_avg_sq", 1))
+        return slots + ((("max_exp_avg_sq", 2),) if options.get("amsgrad") else ())
 
     def __del__(self):
         try:
