@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define TYNX_CUDA_ABI_VERSION 1
+#define TYNX_CUDA_ABI_VERSION 2
 
 /* ---- status codes (TynxError, crates/tynx/src/error.rs:1-122) ----------- */
 enum {
@@ -263,6 +263,58 @@ int tx_layernorm_bwd(tx_ctx *ctx, const float *d_x, const float *d_gamma, const 
                      float *d_dbeta, int64_t rows, int64_t cols, int accumulate_dx,
                      int accumulate_params);
 
+/* BatchNormalization with its running statistics fixed (the only training
+ * form the reference accepts: one output, mean / var are buffers):
+ * y = ((x - mean) / sqrt(var + eps)) * scale + bias over x viewed as
+ * [N][C][L] (L = product of the spatial dims, 1 for rank 2).  The backward
+ * writes dx = (dy * scale) / sqrt(var + eps) (when d_dx is non-null) and the
+ * affine gradients dscale = sum dy * xhat, dbias = sum dy over N and L (when
+ * non-null; both or neither).
+ * replaces: execute_batch_normalization
+ * (crates/tynx-train/src/imported_model/executor.rs:371-448), batch_normalization
+ * (crates/tynx/src/interpreter/normalization.rs:20-58) and their Burn backward. */
+int tx_batchnorm_fwd(tx_ctx *ctx, const float *d_x, const float *d_scale, const float *d_bias,
+                     const float *d_mean, const float *d_var, float *d_y, int64_t N, int64_t C,
+                     int64_t L, float eps);
+int tx_batchnorm_bwd(tx_ctx *ctx, const float *d_x, const float *d_dy, const float *d_scale,
+                     const float *d_mean, const float *d_var, float *d_dx, float *d_dscale,
+                     float *d_dbias, int64_t N, int64_t C, int64_t L, float eps, int accumulate_dx,
+                     int accumulate_params);
+/* GroupNormalization over x viewed as [N][groups][C / groups][L], per-channel
+ * scale and bias [C]; InstanceNormalization is groups == C.  The forward saves
+ * each (n, group) row's mean and sqrt(var + eps) (d_mean, d_sdev: N * groups).
+ * replaces: group_normalization_values / instance_normalization_values
+ * (crates/tynx/src/interpreter/normalization.rs:73-106, 213-273) and their Burn
+ * backward. */
+int tx_groupnorm_fwd(tx_ctx *ctx, const float *d_x, const float *d_scale, const float *d_bias,
+                     float *d_y, float *d_mean, float *d_sdev, int64_t N, int64_t C, int64_t L,
+                     int64_t groups, float eps);
+int tx_groupnorm_bwd(tx_ctx *ctx, const float *d_x, const float *d_dy, const float *d_scale,
+                     const float *d_mean, const float *d_sdev, float *d_dx, float *d_dscale,
+                     float *d_dbias, int64_t N, int64_t C, int64_t L, int64_t groups,
+                     int accumulate_dx, int accumulate_params);
+/* PRelu y = x >= 0 ? x : slope * x with slope broadcast to `shape` through
+ * slope_strides (0 on broadcast axes).  The backward writes dx (when non-null)
+ * and, into d_dslope_full (shape `shape`, when non-null), dy * x where x < 0,
+ * which the caller sums down to the slope's shape.
+ * replaces: DynTensor::prelu (crates/tynx/src/tensor.rs:1911-1934). */
+int tx_prelu_fwd(tx_ctx *ctx, const float *d_x, const float *d_slope, const int64_t *slope_strides,
+                 float *d_y, const int64_t *shape, int ndim);
+int tx_prelu_bwd(tx_ctx *ctx, const float *d_x, const float *d_slope, const int64_t *slope_strides,
+                 const float *d_dy, float *d_dx, float *d_dslope_full, const int64_t *shape, int ndim,
+                 int accumulate_dx);
+/* 2-D max pooling over `planes` (= N * C) planes of H x W; geom = {kh, kw,
+ * sh, sw, pad_top, pad_left, dil_h, dil_w, out_h, out_w}.  Taps outside the
+ * input count as -inf.  d_argmax (int32, one per output) records the chosen
+ * tap (h * W + w; the first maximal one in window order); the backward routes
+ * each output gradient there, summing in a fixed order.
+ * replaces: max_pool2d (crates/tynx/src/interpreter/pooling.rs:360-426) and Burn's
+ * max_pool2d backward. */
+int tx_maxpool2d_fwd(tx_ctx *ctx, const float *d_x, float *d_y, int32_t *d_argmax, int64_t planes,
+                     int64_t H, int64_t W, const int64_t *geom);
+int tx_maxpool2d_bwd(tx_ctx *ctx, const float *d_dy, const int32_t *d_argmax, float *d_dx,
+                     int64_t planes, int64_t H, int64_t W, const int64_t *geom, int accumulate);
+
 /* Row gather out[i, :] = table[idx[i], :] (negative indices wrap once) and its
  * backward scatter-add.  replaces: gather_values (crates/tynx/src/interpreter/gather.rs:18-58),
  * DynTensor::select (tensor.rs:1450) and Burn select_assign. */
@@ -319,7 +371,8 @@ enum {
   TX_OP_SUB, TX_OP_MUL, TX_OP_DIV, TX_OP_RELU, TX_OP_TANH, TX_OP_GELU, TX_OP_SIGMOID,
   TX_OP_EXP, TX_OP_LOG, TX_OP_NEG, TX_OP_SOFTMAX, TX_OP_LOGSOFTMAX, TX_OP_REDUCEMEAN,
   TX_OP_REDUCESUM, TX_OP_GAP, TX_OP_RESHAPE, TX_OP_TRANSPOSE, TX_OP_FLATTEN,
-  TX_OP_SQUEEZE, TX_OP_UNSQUEEZE, TX_OP_IDENTITY, TX_OP_CLIP, TX_OP_PRELU
+  TX_OP_SQUEEZE, TX_OP_UNSQUEEZE, TX_OP_IDENTITY, TX_OP_CLIP, TX_OP_PRELU,
+  TX_OP_BATCHNORM, TX_OP_GROUPNORM, TX_OP_MAXPOOL
 };
 enum { TX_VAL_INPUT = 0, TX_VAL_PARAM = 1, TX_VAL_CONST = 2, TX_VAL_ACT = 3 };
 enum { TX_DT_F32 = 0, TX_DT_I64 = 1 };
@@ -333,7 +386,7 @@ typedef struct tx_value_desc {
 typedef struct tx_node_desc {
   int32_t op;                /* TX_OP_* */
   int32_t n_in, n_out;
-  int32_t in[4], out[3];     /* value ids; -1 for an absent optional input */
+  int32_t in[6], out[3];     /* value ids; -1 for an absent optional input */
   int64_t iattr[8];          /* op-specific integers */
   double fattr[4];           /* op-specific reals */
   int32_t n_ints; int64_t ints[16]; /* list attributes (perm, pads, strides, axes, shape) */
@@ -346,6 +399,10 @@ int tx_graph_destroy(tx_graph *g);
 int tx_graph_param_count(tx_graph *g, int *out);
 int tx_graph_param(tx_graph *g, int index, int32_t *value_id, float **d_value, float **d_grad,
                    int64_t *numel);
+/* Device storage of a parameter or constant value (the BatchNorm running
+ * statistics are constants the forward reads from here: writing them changes
+ * the next forward, as ImportedModel buffers do in the reference). */
+int tx_graph_value_ptr(tx_graph *g, int value_id, void **d_out);
 int tx_graph_grad_defined(tx_graph *g, int index, int *out);
 int tx_graph_set_grad_defined(tx_graph *g, int index, int defined);
 /* Shape inference for given input shapes; fills output ranks and shapes. */

@@ -654,7 +654,124 @@ def run_op(op, vals: list) -> list:
         if nd != 2:
             raise NotImplementedError("oracle Conv supports 1-D and 2-D kernels")
         return [conv2d(x, W, vals[2] if len(vals) > 2 else None, strides, pads, dil, a["group"])]
+    if t == "BatchNormalization":
+        return [batch_norm(x, vals[1], vals[2], vals[3], vals[4], a["epsilon"])]
+    if t == "InstanceNormalization":
+        return [group_norm(x, vals[1], vals[2], x.shape[1], a["epsilon"])]
+    if t == "GroupNormalization":
+        return [group_norm(x, vals[1], vals[2], int(a["num_groups"]), a["epsilon"])]
+    if t == "MaxPool":
+        return [max_pool(x, a)]
     raise NotImplementedError(f"oracle has no rule for {t}")
+
+
+def sqrt_(a: T) -> T:
+    out = np.sqrt(a.data).astype(F32)
+    return _node(out, (a,), lambda g: (g / (F32(2) * out),))
+
+
+def _channel(p: T, rank: int) -> T:
+    """A [C] tensor reshaped to broadcast over axis 1 of a rank-`rank` input."""
+    shape = [1] * rank
+    shape[1] = p.shape[0]
+    return reshape(p, shape)
+
+
+def batch_norm(x: T, scale: T, bias: T, mean_: T, var: T, eps: float) -> T:
+    """BatchNormalization with fixed running statistics, composed as
+    ``crates/tynx-train/src/imported_model/executor.rs:441-445``:
+    ((x - mean) / sqrt(var + eps)) * scale + bias.  mean / var are buffers."""
+    r = x.data.ndim
+    m = T(_channel(mean_, r).data)
+    v = T(_channel(var, r).data)
+    sd = sqrt_(v + T(np.asarray(eps, dtype=F32)))
+    return (x - m) / sd * _channel(scale, r) + _channel(bias, r)
+
+
+def group_norm(x: T, scale: T, bias: T, groups: int, eps: float) -> T:
+    """Group normalization (InstanceNormalization is groups == C), composed as
+    ``crates/tynx/src/interpreter/normalization.rs:73-106, 213-273``: mean and
+    biased variance of each (sample, group) over its channels and positions,
+    centred / sqrt(var + eps), then the per-channel affine."""
+    shape = x.shape
+    n, c = shape[0], shape[1]
+    grouped = reshape(x, [n, groups, c // groups] + list(shape[2:]))
+    axes = tuple(range(2, grouped.data.ndim))
+    mu = mean(grouped, axes, keepdims=True)
+    centred = grouped - mu
+    var = mean(centred * centred, axes, keepdims=True)
+    normal = reshape(centred / sqrt_(var + T(np.asarray(eps, dtype=F32))), shape)
+    r = len(shape)
+    return normal * _channel(scale, r) + _channel(bias, r)
+
+
+def _pool_axis(size: int, k: int, s: int, d: int, begin: int, end: int, auto_pad: str,
+               ceil: bool) -> tuple[int, int]:
+    """Start padding and output length of one pooled axis
+    (``crates/tynx/src/interpreter/spatial.rs:102-151``)."""
+    eff = (k - 1) * d + 1
+    if auto_pad == "VALID":
+        begin = end = 0
+    elif auto_pad in ("SAME_UPPER", "SAME_LOWER"):
+        out = -(-size // s)
+        total = max((out - 1) * s + eff - size, 0)
+        small, large = total // 2, total - total // 2
+        begin, end = (large, small) if auto_pad == "SAME_LOWER" else (small, large)
+    padded = size + begin + end
+    if padded < eff:
+        raise ValueError("MaxPool window larger than its padded input")
+    out = (padded - eff) // s + 1
+    if ceil:
+        out = -(-(padded - eff) // s) + 1
+        if out > 0 and (out - 1) * s >= size + begin:
+            out -= 1
+    return begin, out
+
+
+def max_pool(x: T, a: dict) -> T:
+    """MaxPool over the -inf padded input (``pooling.rs:360-426``); the gradient
+    goes to the first maximal tap in window order."""
+    k = list(a["kernel_shape"])
+    st, dil, pads = list(a["strides"]), list(a["dilations"]), list(a["pads"])
+    data = x.data
+    one_d = len(k) == 1
+    if one_d:
+        data = data[:, :, None, :]
+        k, st, dil, pads = [1] + k, [1] + st, [1] + dil, [0, pads[0], 0, pads[1]]
+    n, c, h, w = data.shape
+    auto, ceil = a.get("auto_pad", "NOTSET"), bool(a.get("ceil_mode", 0))
+    pt, oh = _pool_axis(h, k[0], st[0], dil[0], pads[0], pads[2], auto, ceil)
+    pl, ow = _pool_axis(w, k[1], st[1], dil[1], pads[1], pads[3], auto, ceil)
+    best = np.full((n, c, oh, ow), -np.inf, dtype=F32)
+    arg = np.full((n, c, oh, ow), -1, dtype=np.int64)
+    rows = np.arange(oh) * st[0] - pt
+    cols = np.arange(ow) * st[1] - pl
+    for kh in range(k[0]):
+        hh = rows + kh * dil[0]
+        vh = (hh >= 0) & (hh < h)
+        for kw in range(k[1]):
+            ww = cols + kw * dil[1]
+            vw = (ww >= 0) & (ww < w)
+            valid = vh[:, None] & vw[None, :]
+            tap = data[:, :, np.clip(hh, 0, h - 1)[:, None], np.clip(ww, 0, w - 1)[None, :]]
+            take = valid & ((tap > best) | (arg < 0))
+            best = np.where(take, tap, best).astype(F32)
+            pos = np.clip(hh, 0, h - 1)[:, None] * w + np.clip(ww, 0, w - 1)[None, :]
+            arg = np.where(take, pos, arg)
+    out = best[:, :, 0, :] if one_d else best
+
+    def back(g):
+        g4 = g[:, :, None, :] if one_d else g
+        dx = np.zeros((n * c, h * w), dtype=F32)
+        flat = arg.reshape(n * c, -1)
+        src = g4.reshape(n * c, -1)
+        ok = flat >= 0
+        rows_ = np.repeat(np.arange(n * c)[:, None], flat.shape[1], axis=1)
+        np.add.at(dx, (rows_[ok], flat[ok]), src[ok])
+        dx = dx.reshape(n, c, h, w)
+        return (dx[:, :, 0, :] if one_d else dx,)
+
+    return _node(np.ascontiguousarray(out), (x,), back)
 
 
 def layer_norm(x: T, scale: T, bias: Optional[T], axis: int, eps: float, n_out: int):

@@ -46,3 +46,49 @@ def gemm_line_model() -> bytes:
     return proto.encode_model(nodes, inits, [proto.encode_value_info("x", proto.FLOAT, [4, 1])],
                               [proto.encode_value_info("y", proto.FLOAT, [4, 1])],
                               graph_name="imported_training_test", opset=13)
+
+
+def _one_node_model(op, inputs, inits, x_shape, y_shape, opset, graph_name, **attrs):
+    import numpy as np  # noqa: F401
+
+    from tynx_b200.onnx import proto
+
+    nodes = [proto.encode_node(op, inputs, ["y"], name="norm" if "Norm" in op else
+                               "activation" if op == "PRelu" else "node", **attrs)]
+    encoded = [proto.encode_tensor(name, array) for name, array in inits]
+    return proto.encode_model(nodes, encoded, [proto.encode_value_info("x", proto.FLOAT, x_shape)],
+                              [proto.encode_value_info("y", proto.FLOAT, y_shape)],
+                              graph_name=graph_name, opset=opset)
+
+
+@pytest.fixture(scope="session")
+def new_op_models() -> dict:
+    """The one-node models of the reference's trainable-operator tests
+    (crates/tynx-train/src/imported_model/tests.rs:671-700, 772-831): BatchNorm
+    with fixed statistics, PRelu with a scalar slope, Instance- and
+    GroupNormalization with unit scale and zero bias."""
+    import numpy as np
+
+    f = np.float32
+    return {
+        "batch_norm": (_one_node_model(
+            "BatchNormalization", ["x", "scale", "bias", "mean", "variance"],
+            [("scale", np.array([2, 3], f)), ("bias", np.array([0.5, -1], f)),
+             ("mean", np.array([1, 2], f)), ("variance", np.array([4, 9], f))],
+            [2, 2], [2, 2], 13, "imported_batch_norm_test"),
+            {"scale": "norm.weight", "bias": "norm.bias", "mean": "norm.running_mean",
+             "variance": "norm.running_var"}),
+        "prelu": (_one_node_model("PRelu", ["x", "slope"], [("slope", np.array([0.25], f))],
+                                  [2], [2], 13, "unsupported_slot_report"),
+                  {"slope": "activation.weight"}),
+        "instance_norm": (_one_node_model(
+            "InstanceNormalization", ["x", "scale", "bias"],
+            [("scale", np.ones(2, f)), ("bias", np.zeros(2, f))], [1, 2, 2], [1, 2, 2], 13,
+            "imported_InstanceNormalization_test"),
+            {"scale": "norm.weight", "bias": "norm.bias"}),
+        "group_norm": (_one_node_model(
+            "GroupNormalization", ["x", "scale", "bias"],
+            [("scale", np.ones(4, f)), ("bias", np.zeros(4, f))], [1, 4, 2], [1, 4, 2], 18,
+            "imported_GroupNormalization_test", num_groups=2),
+            {"scale": "norm.weight", "bias": "norm.bias"}),
+    }

@@ -19,7 +19,7 @@ def test_library_exports_every_declared_symbol():
     missing = [name for name in declared if not hasattr(lib, name)]
     assert not missing, missing
     assert declared == set(_native.SIGNATURES), declared ^ set(_native.SIGNATURES)
-    assert lib.tx_abi_version() == 1
+    assert lib.tx_abi_version() == 2
 
 
 def test_no_gpu_calls_fail_cleanly_without_a_device():

@@ -321,3 +321,71 @@ def test_reference_finite_difference_points(expected):
     numerical = (ln_sum(up) - ln_sum(down)) / (2 * e)
     assert x.grad.reshape(-1)[i] == pytest.approx(numerical, rel=c["rel"], abs=c["abs"])
 
+
+
+def _new_op(new_op_models, name):
+    data, names = new_op_models[name]
+    return fo.OracleModel(ir.load_training_graph(data, initializer_names=names))
+
+
+def test_batch_norm_trains_affine_state_with_frozen_statistics(new_op_models):
+    """crates/tynx-train/src/imported_model/tests.rs:447-480."""
+    model = _new_op(new_op_models, "batch_norm")
+    graph = ir.load_training_graph(new_op_models["batch_norm"][0],
+                                   initializer_names=new_op_models["batch_norm"][1])
+    assert sorted(graph.buffers) == ["norm.running_mean", "norm.running_var"]
+    y = model(np.array([[3, 8], [5, 11]], np.float32))
+    np.testing.assert_array_equal(y.data.reshape(-1), [2.5, 5.0, 4.5, 8.0])
+    fo.sum_(y).backward()
+    p = dict(model.named_parameters())
+    assert sorted(p) == ["norm.bias", "norm.weight"]
+    np.testing.assert_array_equal(p["norm.weight"].grad, [3.0, 5.0])
+    np.testing.assert_array_equal(p["norm.bias"].grad, [2.0, 2.0])
+
+
+def test_batch_norm_uses_running_statistics():
+    """crates/tynx/src/interpreter/normalization.rs:408-440 (epsilon 0)."""
+    x = fo.T(np.array([1, 3, 2, 6], np.float32).reshape(1, 2, 2))
+    y = fo.batch_norm(x, fo.T(np.array([2, 0.5], np.float32)), fo.T(np.array([1, -1], np.float32)),
+                      fo.T(np.array([1, 2], np.float32)), fo.T(np.array([4, 1], np.float32)), 0.0)
+    np.testing.assert_array_equal(y.data.reshape(-1), [1.0, 3.0, -1.0, 1.0])
+
+
+def test_prelu_trains_its_slope(new_op_models):
+    """crates/tynx-train/src/imported_model/tests.rs:527-568."""
+    model = _new_op(new_op_models, "prelu")
+    x = np.array([-2.0, 3.0], np.float32)
+    y = model(x)
+    np.testing.assert_array_equal(y.data, [-0.5, 3.0])
+    fo.sum_(y).backward()
+    slope = dict(model.named_parameters())["activation.weight"]
+    np.testing.assert_array_equal(slope.grad, [-2.0])
+    fo.SGD(model.named_parameters(), lr=0.1).step()
+    np.testing.assert_allclose(model(x).data, [-0.9, 3.0], rtol=1e-6)
+
+
+def test_instance_norm_custom_epsilon():
+    """crates/tynx/src/interpreter/normalization.rs:505-545."""
+    eps = 1e-3
+    x = fo.T(np.array([1, 3, 2, 6], np.float32).reshape(1, 2, 2))
+    y = fo.group_norm(x, fo.T(np.array([2, 0.5], np.float32)), fo.T(np.array([1, -1], np.float32)), 2, eps)
+    first, second = 1 / np.sqrt(np.float32(1 + eps)), 2 / np.sqrt(np.float32(4 + eps))
+    np.testing.assert_allclose(y.data.reshape(-1),
+                               [1 - 2 * first, 1 + 2 * first, -1 - 0.5 * second, -1 + 0.5 * second],
+                               atol=1e-5)
+
+
+@pytest.mark.parametrize("name,x", [("instance_norm", [[[1, 3], [2, 6]]]),
+                                    ("group_norm", [[[1, 3], [2, 6], [-1, 1], [4, 8]]])])
+def test_instance_and_group_norm_train_affine_slots(new_op_models, name, x):
+    """crates/tynx-train/src/imported_model/tests.rs:570-644: loss = sum(y^2) + sum(y)."""
+    model = _new_op(new_op_models, name)
+    x = np.asarray(x, np.float32)
+    y = model(x)
+    before = y.data.copy()
+    (fo.sum_(y * y) + fo.sum_(y)).backward()
+    p = dict(model.named_parameters())
+    assert sorted(p) == ["norm.bias", "norm.weight"]
+    assert all(q.grad is not None for q in p.values())
+    fo.SGD(model.named_parameters(), lr=0.05).step()
+    assert not np.array_equal(model(x).data, before)

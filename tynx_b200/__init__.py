@@ -28,7 +28,7 @@ _FROM = {
                "ones", "ones_like", "pinned", "rand", "randn", "set_math_mode", "synchronize",
                "tensor", "zeros", "zeros_like"),
     ".compiler": ("CompiledFunction", "compile"),
-    ".imported": ("ImportedModel", "Parameter", "Session", "load"),
+    ".imported": ("Buffer", "ImportedModel", "Parameter", "Session", "load"),
     ".checkpoint": ("save_checkpoint", "load_checkpoint"),
     ".onnx.ir": ("TrainabilityReport",),
 }

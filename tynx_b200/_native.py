@@ -42,7 +42,8 @@ BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "min": 4, "max": 5, "le": 6, "ge"
 OP = {name: i + 1 for i, name in enumerate([
     "GEMM", "MATMUL", "CONV", "GATHER", "LAYERNORM", "ADD", "SUB", "MUL", "DIV", "RELU", "TANH",
     "GELU", "SIGMOID", "EXP", "LOG", "NEG", "SOFTMAX", "LOGSOFTMAX", "REDUCEMEAN", "REDUCESUM",
-    "GAP", "RESHAPE", "TRANSPOSE", "FLATTEN", "SQUEEZE", "UNSQUEEZE", "IDENTITY", "CLIP", "PRELU"])}
+    "GAP", "RESHAPE", "TRANSPOSE", "FLATTEN", "SQUEEZE", "UNSQUEEZE", "IDENTITY", "CLIP", "PRELU",
+    "BATCHNORM", "GROUPNORM", "MAXPOOL"])}
 VAL_INPUT, VAL_PARAM, VAL_CONST, VAL_ACT = 0, 1, 2, 3
 DT_F32, DT_I64 = 0, 1
 
@@ -82,7 +83,7 @@ class ValueDesc(C.Structure):
 class NodeDesc(C.Structure):
     _fields_ = [
         ("op", C.c_int32), ("n_in", C.c_int32), ("n_out", C.c_int32),
-        ("inp", C.c_int32 * 4), ("out", C.c_int32 * 3),
+        ("inp", C.c_int32 * 6), ("out", C.c_int32 * 3),
         ("iattr", C.c_int64 * 8), ("fattr", C.c_double * 4),
         ("n_ints", C.c_int32), ("ints", C.c_int64 * 16),
     ]
@@ -148,6 +149,14 @@ SIGNATURES = {
     "tx_softmax_xent_fwd_noalloc": [_vp, _vp, _vp, _i64, _i64, _vp],
     "tx_layernorm_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f],
     "tx_layernorm_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32],
+    "tx_batchnorm_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f],
+    "tx_batchnorm_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f, _i32, _i32],
+    "tx_groupnorm_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f],
+    "tx_groupnorm_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32],
+    "tx_prelu_fwd": [_vp, _vp, _vp, _p64, _vp, _p64, _i32],
+    "tx_prelu_bwd": [_vp, _vp, _vp, _p64, _vp, _vp, _vp, _p64, _i32, _i32],
+    "tx_maxpool2d_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64],
+    "tx_maxpool2d_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64, _i32],
     "tx_gather_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_scatter_add_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_take_last": [_vp, _vp, _vp, _vp, _i64, _i64],
@@ -163,6 +172,7 @@ SIGNATURES = {
     "tx_optim_get_steps": [_vp, _p64],
     "tx_optim_set_steps": [_vp, _p64],
     "tx_optim_destroy": [_vp],
+    "tx_graph_value_ptr": [_vp, _i32, C.POINTER(_vp)],
     "tx_graph_create": [_vp, C.POINTER(ValueDesc), _i32, C.POINTER(NodeDesc), _i32, _p32, _i32,
                         C.POINTER(_vp)],
     "tx_graph_destroy": [_vp],

@@ -506,6 +506,56 @@ void bstrides(const Shape &s, const Shape &out, int64_t *st) {
 
 int norm_axis(int64_t axis, int64_t rank) { return (int)(axis < 0 ? axis + rank : axis); }
 
+// MaxPool geometry {kh, kw, sh, sw, pad_top, pad_left, dh, dw, oh, ow} from the
+// node's attributes (ints: kh, kw, sh, sw, pt, pl, pb, pr, dh, dw; iattr[0]
+// ceil_mode, iattr[1] auto_pad: 0 NOTSET, 1 VALID, 2 SAME_UPPER, 3 SAME_LOWER)
+// and the input's spatial size.  Per axis it resolves the padding as
+// crates/tynx/src/interpreter/spatial.rs:102-151 does (auto_pad, then the extra
+// end padding that ceil_mode needs, the last window starting inside the input
+// or its start padding); windows run over the -inf padded input.
+bool pool_geom(const tx_node_desc &d, int64_t H, int64_t W, int64_t geom[10]) {
+  const int64_t in[2] = {H, W};
+  int64_t start[2], out[2];
+  for (int a = 0; a < 2; ++a) {
+    const int64_t k = d.ints[a], s = d.ints[2 + a], dil = d.ints[8 + a];
+    if (k <= 0 || s <= 0 || dil <= 0) return false;
+    const int64_t eff = (k - 1) * dil + 1;
+    int64_t b = d.ints[4 + a], e = d.ints[6 + a];
+    if (d.iattr[1] == 1) {
+      b = e = 0;
+    } else if (d.iattr[1] >= 2) {
+      const int64_t o = (in[a] + s - 1) / s;
+      int64_t total = (o - 1) * s + eff - in[a];
+      if (total < 0) total = 0;
+      const int64_t small = total / 2, large = total - small;
+      b = d.iattr[1] == 3 ? large : small;
+      e = d.iattr[1] == 3 ? small : large;
+    }
+    const int64_t padded = in[a] + b + e;
+    if (padded < eff) return false;
+    int64_t o = (padded - eff) / s + 1;
+    if (d.iattr[0]) {
+      o = (padded - eff + s - 1) / s + 1;
+      if (o > 0 && (o - 1) * s >= in[a] + b) --o;
+    }
+    start[a] = b;
+    out[a] = o;
+  }
+  const int64_t g[10] = {d.ints[0], d.ints[1], d.ints[2], d.ints[3], start[0], start[1],
+                         d.ints[8], d.ints[9], out[0], out[1]};
+  for (int i = 0; i < 10; ++i) geom[i] = g[i];
+  return true;
+}
+
+// [N][C][L] view of a rank >= 2 tensor (L = product of the dims after C).
+void ncl(const Shape &x, int64_t *N, int64_t *C, int64_t *L) {
+  *N = x[0];
+  *C = x[1];
+  int64_t l = 1;
+  for (size_t i = 2; i < x.size(); ++i) l *= x[i];
+  *L = l;
+}
+
 int infer_node(tx_graph *g, const GNode &n, std::vector<Shape> &S) {
   const tx_node_desc &d = n.d;
   auto in = [&](int i) -> const Shape & { return S[d.in[i]]; };
@@ -592,6 +642,49 @@ int infer_node(tx_graph *g, const GNode &n, std::vector<Shape> &S) {
     case TX_OP_GAP: {
       out = in(0);
       for (size_t i = 2; i < out.size(); ++i) out[i] = 1;
+      return TX_OK;
+    }
+    case TX_OP_PRELU: {
+      const Shape &x = in(0), &sl = in(1);
+      Shape b;
+      if (sl.size() > x.size() || !broadcast_shapes(x, sl, b) || b != x)
+        return fail(g, TX_ERR_SHAPE, "PRelu slope shape " + shape_str(sl) + " cannot broadcast to input shape " +
+                                         shape_str(x));
+      out = x;
+      return TX_OK;
+    }
+    case TX_OP_BATCHNORM: case TX_OP_GROUPNORM: {
+      const Shape &x = in(0);
+      const bool bn = d.op == TX_OP_BATCHNORM;
+      if (x.size() < (bn ? 2u : 3u))
+        return fail(g, TX_ERR_SHAPE, std::string(bn ? "BatchNormalization" : "Instance/GroupNormalization") +
+                                         " requires rank at least " + (bn ? "2" : "3") + ", got " + shape_str(x));
+      const int64_t C = x[1];
+      for (int k = 1; k < d.n_in; ++k) {
+        if (d.in[k] < 0) return fail(g, TX_ERR_INVALID, "normalization inputs are required");
+        if (numel_of(in(k)) != C || in(k).size() != 1)
+          return fail(g, TX_ERR_SHAPE, "normalization input " + std::to_string(k) + " expects [" +
+                                           std::to_string(C) + "], got " + shape_str(in(k)));
+      }
+      if (!bn) {
+        const int64_t groups = d.iattr[0] > 0 ? d.iattr[0] : C;
+        if (C % groups)
+          return fail(g, TX_ERR_SHAPE, "GroupNormalization channels " + std::to_string(C) +
+                                           " are not divisible by " + std::to_string(groups) + " groups");
+      }
+      out = x;
+      return TX_OK;
+    }
+    case TX_OP_MAXPOOL: {
+      const Shape &x = in(0);
+      if (x.size() != 4 && x.size() != 3)
+        return fail(g, TX_ERR_UNSUPPORTED, "MaxPool on CUDA supports 1-D and 2-D pooling, got " + shape_str(x));
+      int64_t geom[10];
+      const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
+      if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
+      out = x;
+      if (x.size() == 4) out[2] = geom[8];
+      out.back() = geom[9];
       return TX_OK;
     }
     case TX_OP_RESHAPE: {
@@ -721,7 +814,7 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
   for (int i = 0; i < n_nodes; ++i) {
     g->nodes[i].d = nodes[i];
     const tx_node_desc &d = nodes[i];
-    if (d.n_in < 0 || d.n_in > 4 || d.n_out < 1 || d.n_out > 3 || d.n_ints < 0 || d.n_ints > 16)
+    if (d.n_in < 0 || d.n_in > 6 || d.n_out < 1 || d.n_out > 3 || d.n_ints < 0 || d.n_ints > 16)
       return tx_fail(ctx, TX_ERR_INVALID, "malformed node descriptor");
     for (int k = 0; k < d.n_in; ++k) {
       if (d.in[k] < -1 || d.in[k] >= n_values) return tx_fail(ctx, TX_ERR_INVALID, "node input id out of range");
@@ -953,6 +1046,15 @@ extern "C" int tx_graph_param(tx_graph *g, int i, int32_t *vid, float **value, f
   if (value) *value = (float *)v.dev;
   if (grad) *grad = v.grad;
   if (numel) *numel = numel_of(v.shape);
+  return TX_OK;
+}
+
+extern "C" int tx_graph_value_ptr(tx_graph *g, int value_id, void **out) {
+  if (!g || !out || value_id < 0 || value_id >= (int)g->values.size()) return TX_ERR_INVALID;
+  const GValue &v = g->values[value_id];
+  if (v.kind != TX_VAL_CONST && v.kind != TX_VAL_PARAM)
+    return tx_fail(g->ctx, TX_ERR_INVALID, "only parameters and constants have storage of their own");
+  *out = v.dev;
   return TX_OK;
 }
 
@@ -1226,6 +1328,39 @@ struct Fwd {
         if (rnd) r->tf32[yv] = true;
         return layernorm_fwd(ctx, F(d.in[0]), F(d.in[1]), beta, F(yv), mean, rstd, rows, cols,
                              (float)d.fattr[0], rnd);
+      }
+      case TX_OP_PRELU: {
+        int64_t ss[TX_MAX_DIMS];
+        bstrides(S(d.in[1]), y, ss);
+        return tx_prelu_fwd(ctx, F(d.in[0]), F(d.in[1]), ss, F(yv), y.data(), (int)y.size());
+      }
+      case TX_OP_BATCHNORM: {
+        int64_t N, C, L;
+        ncl(S(d.in[0]), &N, &C, &L);
+        return tx_batchnorm_fwd(ctx, F(d.in[0]), F(d.in[1]), F(d.in[2]), F(d.in[3]), F(d.in[4]), F(yv), N, C, L,
+                                (float)d.fattr[0]);
+      }
+      case TX_OP_GROUPNORM: {
+        int64_t N, C, L;
+        ncl(S(d.in[0]), &N, &C, &L);
+        const int64_t groups = d.iattr[0] > 0 ? d.iattr[0] : C;
+        float *mean = (float *)tx_alloc_raw(ctx, (N * groups + 1) * 4);
+        float *sdev = (float *)tx_alloc_raw(ctx, (N * groups + 1) * 4);
+        r->extra[ni] = mean;
+        if (sdev) r->extra2[ni].push_back(sdev);
+        if (!mean || !sdev) return TX_ERR_OOM;
+        return tx_groupnorm_fwd(ctx, F(d.in[0]), F(d.in[1]), F(d.in[2]), F(yv), mean, sdev, N, C, L, groups,
+                                (float)d.fattr[0]);
+      }
+      case TX_OP_MAXPOOL: {
+        const Shape &x = S(d.in[0]);
+        const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
+        int64_t geom[10];
+        if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
+        int32_t *arg = (int32_t *)tx_alloc_raw(ctx, ny * 4 + 4);
+        r->extra[ni] = arg;
+        if (!arg) return TX_ERR_OOM;
+        return tx_maxpool2d_fwd(ctx, F(d.in[0]), F(yv), arg, x[0] * x[1], H, W, geom);
       }
       case TX_OP_ADD: case TX_OP_SUB: case TX_OP_MUL: case TX_OP_DIV: {
         int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS];
@@ -1760,6 +1895,14 @@ struct Bwd {
   }
 
   // dX (+)= reduce_to_shape(src) for broadcast binary backward
+  // dst (+)= src over n elements
+  int add_or_copy(float *dst, const float *src, int64_t n, int acc) {
+    if (!acc) return tx_d2d(ctx, dst, src, n * 4);
+    k_axpy<<<grid_for(n, 256), 256, 0, ctx->stream>>>(dst, src, n, 1.f);
+    TX_LAUNCHED(ctx, "k_axpy");
+    return TX_OK;
+  }
+
   int reduce_into(int v, const float *src, const Shape &from, float scale) {
     float *t; int acc;
     TX_TRY(target(v, &t, &acc));
@@ -1889,6 +2032,76 @@ struct Bwd {
         if (dx) wrote(xv);
         if (dg) wrote(gv);
         if (db) wrote(bv);
+        return TX_OK;
+      }
+      case TX_OP_PRELU: {
+        const int xv0 = d.in[0], sv = d.in[1];
+        float *dx = nullptr, *tmp = nullptr;
+        int xacc = 0;
+        if (needs[xv0]) TX_TRY(target(xv0, &dx, &xacc));
+        if (needs[sv]) {
+          tmp = (float *)tx_alloc_raw(ctx, ny * 4 + 4);
+          if (!tmp) return TX_ERR_OOM;
+        }
+        int64_t ss[TX_MAX_DIMS];
+        bstrides(S(sv), y, ss);
+        int rc = tx_prelu_bwd(ctx, F(xv0), F(sv), ss, dy, dx, tmp, y.data(), (int)y.size(), xacc);
+        if (rc == TX_OK && dx) wrote(xv0);
+        if (rc == TX_OK && tmp) rc = reduce_into(sv, tmp, y, 1.f);
+        tx_free_raw(ctx, tmp);
+        return rc;
+      }
+      case TX_OP_BATCHNORM: case TX_OP_GROUPNORM: {
+        const int xv0 = d.in[0], sv = d.in[1], bv = d.in[2];
+        int64_t N, C, L;
+        ncl(S(xv0), &N, &C, &L);
+        float *dx = nullptr;
+        int xacc = 0;
+        if (needs[xv0]) TX_TRY(target(xv0, &dx, &xacc));
+        // the affine gradients: both or neither (a missing one goes to scratch)
+        const bool want = needs[sv] || needs[bv];
+        float *ds = nullptr, *db = nullptr;
+        int sacc = 0, bacc = 0;
+        Scratch spare(ctx, want ? (size_t)C * 4 : 0);
+        if (want) {
+          if (needs[sv]) TX_TRY(target(sv, &ds, &sacc)); else ds = spare.as<float>();
+          if (needs[bv]) TX_TRY(target(bv, &db, &bacc)); else db = spare.as<float>();
+        }
+        // one accumulate flag covers both affine outputs: accumulate into scratch when they differ
+        Scratch tmp2(ctx, want && sacc != bacc ? (size_t)C * 8 : 0);
+        float *ds_w = ds, *db_w = db;
+        const int pacc = want && sacc == bacc ? sacc : 0;
+        if (want && sacc != bacc) {
+          ds_w = tmp2.as<float>();
+          db_w = tmp2.as<float>() + C;
+        }
+        if (d.op == TX_OP_BATCHNORM) {
+          TX_TRY(tx_batchnorm_bwd(ctx, F(xv0), dy, F(sv), F(d.in[3]), F(d.in[4]), dx, ds_w, db_w, N, C, L,
+                                  (float)d.fattr[0], xacc, pacc));
+        } else {
+          const int64_t groups = d.iattr[0] > 0 ? d.iattr[0] : C;
+          TX_TRY(tx_groupnorm_bwd(ctx, F(xv0), dy, F(sv), (const float *)r->extra[ni], (const float *)r->extra2[ni][0],
+                                  dx, ds_w, db_w, N, C, L, groups, xacc, pacc));
+        }
+        if (want && sacc != bacc) {
+          if (needs[sv]) TX_TRY(add_or_copy(ds, ds_w, C, sacc));
+          if (needs[bv]) TX_TRY(add_or_copy(db, db_w, C, bacc));
+        }
+        if (dx) wrote(xv0);
+        if (needs[sv]) wrote(sv);
+        if (needs[bv]) wrote(bv);
+        return TX_OK;
+      }
+      case TX_OP_MAXPOOL: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
+        int64_t geom[10];
+        if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        TX_TRY(tx_maxpool2d_bwd(ctx, dy, (const int32_t *)r->extra[ni], t, x[0] * x[1], H, W, geom, acc));
+        wrote(xv);
         return TX_OK;
       }
       case TX_OP_ADD: case TX_OP_SUB: {

@@ -35,8 +35,11 @@ _OP_MAP = {
     "Log": "LOG", "Neg": "NEG", "Softmax": "SOFTMAX", "LogSoftmax": "LOGSOFTMAX",
     "ReduceMean": "REDUCEMEAN", "ReduceSum": "REDUCESUM", "GlobalAveragePool": "GAP",
     "Reshape": "RESHAPE", "Transpose": "TRANSPOSE", "Flatten": "FLATTEN", "Squeeze": "SQUEEZE",
-    "Unsqueeze": "UNSQUEEZE", "Identity": "IDENTITY", "Clip": "CLIP",
+    "Unsqueeze": "UNSQUEEZE", "Identity": "IDENTITY", "Clip": "CLIP", "PRelu": "PRELU",
+    "BatchNormalization": "BATCHNORM", "InstanceNormalization": "GROUPNORM",
+    "GroupNormalization": "GROUPNORM", "MaxPool": "MAXPOOL",
 }
+_AUTO_PAD = {"NOTSET": 0, "": 0, "VALID": 1, "SAME_UPPER": 2, "SAME_LOWER": 3}
 
 _ELEM_TO_DTYPE = {proto.FLOAT: "float32", proto.INT64: "int64", proto.INT32: "int64",
                   proto.DOUBLE: "float32", proto.BOOL: "bool"}
@@ -123,6 +126,38 @@ class Parameter(Tensor):
 
     def __repr__(self) -> str:
         return f"Parameter({self.name!r}, shape={self.shape})"
+
+
+class Buffer(Tensor):
+    """Persistent non-trainable state of an imported model (the BatchNorm
+    running statistics): a view of the engine's own storage, read by every
+    forward and never touched by backward or the optimizer
+    (``crates/tynx-train/src/backward_support.rs:165-167``)."""
+
+    __slots__ = ("name", "_graph")
+
+    @classmethod
+    def _slot(cls, graph: "_Graph", name: str, shape, ptr: int, dtype: str = "float32"):
+        b = object.__new__(cls)
+        b._init(Storage(graph.ctx, _nbytes(shape) * (2 if dtype == "int64" else 1), ptr=ptr,
+                        owned=False), 0, shape, dtype, False)
+        b.name = name
+        b._graph = graph
+        return b
+
+    def copy_(self, value) -> "Buffer":
+        from ._core import _DTYPES
+
+        array = np.ascontiguousarray(np.asarray(value.numpy() if isinstance(value, Tensor) else value,
+                                                dtype=_DTYPES[self.dtype][0]))
+        if array.shape != self.shape:
+            raise ValueError(f"value shape {array.shape} does not match buffer {self.shape}")
+        self.ctx.check(lib.tx_h2d(self.ctx.handle, self.ptr, array.ctypes.data, array.nbytes))
+        self.ctx.sync()
+        return self
+
+    def __repr__(self) -> str:
+        return f"Buffer({self.name!r}, shape={self.shape})"
 
 
 def _note(param, kind: str) -> None:
@@ -290,6 +325,25 @@ def lower(graph: ir.TrainingGraph):
             d.iattr[0] = int(a["group"])
         elif t == "Gather":
             d.iattr[0] = int(a["axis"])
+        elif t == "BatchNormalization":
+            d.fattr[0] = float(a["epsilon"])
+        elif t in ("InstanceNormalization", "GroupNormalization"):
+            # InstanceNormalization is group normalization with one group per channel
+            d.iattr[0] = int(a["num_groups"]) if t == "GroupNormalization" else 0
+            d.fattr[0] = float(a["epsilon"])
+        elif t == "MaxPool":
+            k, st, dil, pads = (list(a["kernel_shape"]), list(a["strides"]), list(a["dilations"]),
+                                list(a["pads"]))
+            if len(k) == 1:  # 1-D pooling runs as 2-D over a unit height
+                k, st, dil, pads = [1] + k, [1] + st, [1] + dil, [0, pads[0], 0, pads[1]]
+            if len(k) != 2:
+                raise NotImplementedError(f"{len(k)}-D MaxPool is not supported by the CUDA engine")
+            if a.get("auto_pad", "NOTSET") not in _AUTO_PAD:
+                raise ValueError(f"MaxPool node {op.name!r}: unknown auto_pad {a['auto_pad']!r}")
+            # ONNX pads are [x1_begin, x2_begin, x1_end, x2_end]
+            ints = [k[0], k[1], st[0], st[1], pads[0], pads[1], pads[2], pads[3], dil[0], dil[1]]
+            d.iattr[0] = int(a["ceil_mode"])
+            d.iattr[1] = _AUTO_PAD[a.get("auto_pad", "NOTSET")]
         elif t == "LayerNormalization":
             d.iattr[0] = int(a["axis"])
             d.fattr[0] = float(a["epsilon"])
@@ -334,7 +388,7 @@ def lower(graph: ir.TrainingGraph):
         d.n_ints = len(ints)
         for i, v in enumerate(ints):
             d.ints[i] = int(v)
-        if len(ins) > 4 or len(op.outputs) > 3:
+        if len(ins) > 6 or len(op.outputs) > 3:
             raise NotImplementedError(f"node {op.name!r} has too many inputs or outputs")
         d.n_in = len(ins)
         for i, name in enumerate(ins):
@@ -395,6 +449,15 @@ class ImportedModel:
             name = param_names[i]
             shape = tuple(self._graph_ir.parameters[name].shape)
             self._params[name] = Parameter._slot(self._graph, i, name, shape, vptr.value, gptr.value)
+        self._buffers: dict[str, Buffer] = {}
+        for value, public in self._graph_ir.buffer_of_value.items():
+            if value not in ids:
+                continue  # a buffer no node reads
+            ptr = C.c_void_p()
+            self._ctx.check(lib.tx_graph_value_ptr(handle, ids[value], C.byref(ptr)))
+            array = self._graph_ir.buffers[public]
+            dtype = "int64" if array.dtype.kind in "iu" else "float32"
+            self._buffers[public] = Buffer._slot(self._graph, public, tuple(array.shape), ptr.value, dtype)
         self.training = True
         self._shape_cache: dict = {}
         from .compiler import register_model
@@ -420,8 +483,17 @@ class ImportedModel:
     def parameters(self) -> list[Parameter]:
         return list(self._params.values())
 
+    def named_buffers(self) -> list[tuple[str, Buffer]]:
+        return list(self._buffers.items())
+
+    def buffers(self) -> list[Buffer]:
+        return list(self._buffers.values())
+
     def state_dict(self) -> dict[str, Tensor]:
-        return {name: p.detach() for name, p in self._params.items()}
+        """Detached copies of every parameter and buffer, by stable name."""
+        state = {name: p.detach().clone() for name, p in self._params.items()}
+        state.update({name: b.detach().clone() for name, b in self._buffers.items()})
+        return state
 
     def load_state_dict(self, state: dict, strict: bool = True):
         """Copy tensors into the live parameters by name after validating every
@@ -431,7 +503,7 @@ class ImportedModel:
 
         names, result = prepare_model_state(self, state, strict)
         for name in names:
-            self._params[name].copy_(state[name])
+            (self._params.get(name) or self._buffers[name]).copy_(state[name])
         return result
 
     def trainability_report(self) -> ir.TrainabilityReport:

@@ -38,7 +38,8 @@ DIFFERENTIABLE = {
     "Gemm", "MatMul", "Conv", "Gather", "LayerNormalization", "Add", "Sub", "Mul", "Div",
     "Relu", "Tanh", "Gelu", "Sigmoid", "Exp", "Log", "Neg", "Softmax", "LogSoftmax",
     "ReduceMean", "ReduceSum", "GlobalAveragePool", "Reshape", "Transpose", "Flatten",
-    "Squeeze", "Unsqueeze", "Identity", "Clip", "PRelu",
+    "Squeeze", "Unsqueeze", "Identity", "Clip", "PRelu", "BatchNormalization",
+    "InstanceNormalization", "GroupNormalization", "MaxPool",
 }
 # Operators that carry no gradient to their inputs but are allowed on a path.
 NON_DIFFERENTIABLE_OK = {"Constant", "Shape"}
@@ -207,6 +208,7 @@ class TrainingGraph:
     constants: dict[str, np.ndarray]  # ONNX value name -> constant array
     report: TrainabilityReport
     opset: int
+    buffer_of_value: dict = field(default_factory=dict)  # ONNX value name -> stable buffer name
 
 
 def _dtype_name(array: np.ndarray) -> str:
@@ -242,6 +244,33 @@ def _normalize_attrs(node: proto.Node, opset: int) -> dict:
             raise LoadError(f"Conv node {node.name!r}: auto_pad={auto_pad} is not supported")
     elif t == "Gelu":
         a.setdefault("approximate", "none")
+    elif t == "BatchNormalization":
+        # An absent epsilon adds nothing: the reference's imported BatchNorm
+        # test (crates/tynx-train/src/imported_model/tests.rs:447-480) asserts
+        # y == [2.5, 5.0, 4.5, 8.0] exactly for var [4, 9] with no epsilon
+        # attribute, which holds in f32 only if var + eps == var.
+        a.setdefault("epsilon", 0.0)
+        if int(a.get("training_mode", 0)) or len(node.outputs) != 1:
+            raise LoadError(f"BatchNormalization node {node.name!r}: training outputs are not "
+                            "supported (the running statistics are fixed buffers)")
+    elif t == "InstanceNormalization":
+        a.setdefault("epsilon", 1e-5)
+    elif t == "GroupNormalization":
+        a.setdefault("epsilon", 1e-5)
+        if "num_groups" not in a:
+            raise LoadError(f"GroupNormalization node {node.name!r} has no num_groups attribute")
+    elif t == "MaxPool":
+        if "kernel_shape" not in a:
+            raise LoadError(f"MaxPool node {node.name!r} has no kernel_shape attribute")
+        nd = len(a["kernel_shape"])
+        a.setdefault("strides", [1] * nd)
+        a.setdefault("dilations", [1] * nd)
+        a.setdefault("pads", [0] * (2 * nd))
+        a.setdefault("ceil_mode", 0)
+        a.setdefault("auto_pad", "NOTSET")
+        if len(node.outputs) > 1:
+            raise LoadError(f"MaxPool node {node.name!r}: the indices output is not supported "
+                            "for training")
     return a
 
 
@@ -351,6 +380,7 @@ def build_training_graph(
     parameters: dict[str, np.ndarray] = {}
     parameter_of_value: dict[str, str] = {}
     buffers: dict[str, np.ndarray] = {}
+    buffer_of_value: dict[str, str] = {}
     for value in order:
         array = initializers[value]
         public = rename.get(value, value)
@@ -360,6 +390,7 @@ def build_training_graph(
         elif roles[value] == BUFFER:
             buffers[public] = np.array(array, copy=True)
             constants[value] = buffers[public]
+            buffer_of_value[value] = public
         else:
             constants[value] = np.array(array, copy=True)
     for value, array in initializers.items():
@@ -422,6 +453,7 @@ def build_training_graph(
         parameters=parameters,
         parameter_of_value=parameter_of_value,
         buffers=buffers,
+        buffer_of_value=buffer_of_value,
         constants=constants,
         report=report,
         opset=opset,

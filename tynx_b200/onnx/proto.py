@@ -469,10 +469,13 @@ def encode_node(op_type: str, inputs, outputs, name: str = "", **attributes) -> 
 
 
 def encode_value_info(name: str, elem_type: int, shape) -> bytes:
-    dims = b""
-    for d in shape:
-        dims += _len_field(1, _int_field(1, d) if isinstance(d, int) else _str_field(2, str(d)))
-    tensor_type = _int_field(1, elem_type) + _len_field(2, dims)
+    """ValueInfoProto; ``shape`` None leaves the shape unstated."""
+    tensor_type = _int_field(1, elem_type)
+    if shape is not None:
+        dims = b""
+        for d in shape:
+            dims += _len_field(1, _int_field(1, d) if isinstance(d, int) else _str_field(2, str(d)))
+        tensor_type += _len_field(2, dims)
     return _str_field(1, name) + _len_field(2, _len_field(1, tensor_type))
 
 
