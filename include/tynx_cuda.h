@@ -315,6 +315,27 @@ int tx_maxpool2d_fwd(tx_ctx *ctx, const float *d_x, float *d_y, int32_t *d_argma
 int tx_maxpool2d_bwd(tx_ctx *ctx, const float *d_dy, const int32_t *d_argmax, float *d_dx,
                      int64_t planes, int64_t H, int64_t W, const int64_t *geom, int accumulate);
 
+/* Fused multi-head attention over the merged layout: q, k, v, out (and dout,
+ * dq, dk, dv) are [batch * seq, ld] row-major with head h in columns
+ * h * head_dim .. h * head_dim + head_dim - 1.  out = softmax(scale * q k^T) v
+ * per (sequence, head); the backward writes dq, dk, dv (flags bit 1:
+ * accumulate into them; bit 2: store them rounded to TF32).  Forward flags:
+ * bit 0 the inputs already hold TF32 values (else they are rounded to nearest
+ * on chip), bit 1 store out rounded to TF32.  head_dim 64, seq 1..128; TF32
+ * tensor-core products, fp32 softmax.  One CTA per (sequence, head): no
+ * score, probability or head-split tensor is written to device memory.
+ * replaces: the attention block of an imported graph (MatMul
+ * crates/tynx/src/interpreter/matrix.rs:238-255, Softmax softmax.rs:9-17 and
+ * the Reshape / Transpose head split and merge, shape.rs:118-152) and its
+ * Burn backward. */
+int tx_attention_fwd(tx_ctx *ctx, const float *d_q, const float *d_k, const float *d_v, int64_t ld_in,
+                     float *d_out, int64_t ld_out, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t head_dim, float scale, int flags);
+int tx_attention_bwd(tx_ctx *ctx, const float *d_q, const float *d_k, const float *d_v, int64_t ld_in,
+                     const float *d_dout, int64_t ld_dout, float *d_dq, float *d_dk, float *d_dv,
+                     int64_t ld_grad, int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                     float scale, int flags);
+
 /* Row gather out[i, :] = table[idx[i], :] (negative indices wrap once) and its
  * backward scatter-add.  replaces: gather_values (crates/tynx/src/interpreter/gather.rs:18-58),
  * DynTensor::select (tensor.rs:1450) and Burn select_assign. */

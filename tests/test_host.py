@@ -258,3 +258,25 @@ def test_checkpoint_arguments_and_payload_validation(tmp_path):
         ck._decode({"__type__": "set"})
     with pytest.raises(ValueError, match="does not match declared shape"):
         ck._decode({"__type__": "tensor", "dtype": "float32", "shape": [2], "data": [1.0]})
+
+
+def test_rust_sys_crate_declares_every_header_function():
+    """crates/tynx-cuda-sys/src/lib.rs (the FFI crate a Tynx integration
+    compiles) declares every function of include/tynx_cuda.h with the same
+    number of parameters, and its node descriptor matches the header's."""
+    header = (ROOT / "include" / "tynx_cuda.h").read_text()
+    header = re.sub(r"/\*.*?\*/", "", header, flags=re.S)
+    rust = (ROOT / "crates" / "tynx-cuda-sys" / "src" / "lib.rs").read_text()
+    c_funcs = {n: a for n, a in re.findall(r"^int (tx_\w+)\((.*?)\);", header, flags=re.S | re.M)}
+    r_funcs = dict(re.findall(r"pub fn (tx_\w+)\((.*?)\) -> c_int;", rust))
+    assert set(c_funcs) == set(r_funcs), set(c_funcs) ^ set(r_funcs)
+
+    def count(args):
+        args = " ".join(args.split())
+        return 0 if args in ("", "void") else args.count(",") + 1
+
+    for name, args in c_funcs.items():
+        assert count(args) == count(r_funcs[name]), name
+    assert "pub inp: [i32; 6]" in rust and "int32_t in[6], out[3];" in header
+    assert re.search(r"TYNX_CUDA_ABI_VERSION: c_int = (\d+)", rust).group(1) == \
+        re.search(r"#define TYNX_CUDA_ABI_VERSION (\d+)", header).group(1)

@@ -157,6 +157,9 @@ SIGNATURES = {
     "tx_prelu_bwd": [_vp, _vp, _vp, _p64, _vp, _vp, _vp, _p64, _i32, _i32],
     "tx_maxpool2d_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64],
     "tx_maxpool2d_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64, _i32],
+    "tx_attention_fwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _f, _i32],
+    "tx_attention_bwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                         _f, _i32],
     "tx_gather_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_scatter_add_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_take_last": [_vp, _vp, _vp, _vp, _i64, _i64],

@@ -29,6 +29,13 @@
 #include "common.h"
 #include "epilogue.cuh"
 
+extern "C" int tx_attention_fwd(tx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld_in,
+                                float *out, int64_t ld_out, int64_t batch, int64_t seq, int64_t heads,
+                                int64_t head_dim, float scale, int flags);  // attn.cu
+extern "C" int tx_attention_bwd(tx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld_in,
+                                const float *dout, int64_t ld_dout, float *dq, float *dk, float *dv,
+                                int64_t ld_grad, int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+                                float scale, int flags);  // attn.cu
 int dp_allreduce_range(tx_ctx *ctx, float *buf, int64_t n);  // dp.cu
 int dp_event_fork(tx_ctx *ctx);                               // compute -> comm
 int dp_event_join(tx_ctx *ctx);                               // comm -> compute
@@ -439,6 +446,21 @@ struct GNode {
   // relative error of the first layer's weight gradient).  Its backward
   // products stay TF32.
   bool exact = false;
+  // member of a fused attention block (tx_graph::attn index), or -1
+  int attn = -1;
+};
+
+// An attention block the fused kernels can run: q, k, v are [B, S, H * D]
+// projection outputs; Reshape -> Transpose(0,2,1,3) (Transpose(0,2,3,1) for k)
+// -> MatMul(qh, kh) (-> scale) -> Softmax -> MatMul(., vh) -> Transpose(0,2,1,3)
+// -> Reshape produces `out` [B, S, H * D].  Every intermediate value has that
+// one reader, so none of them is needed once the block runs fused.
+struct AttnPlan {
+  int q = -1, k = -1, v = -1, out = -1;
+  int split_q = -1;             // the Reshape of q: its output shape gives H and D
+  int first = -1, last = -1;    // node index range of the block
+  float scale = 1.f;
+  bool round_out = false;       // TF32 mode: out only feeds contractions
 };
 
 struct tx_graph {
@@ -458,6 +480,7 @@ struct tx_graph {
   bool dp = false;
   int64_t bucket_bytes = 0;
   std::vector<int> grad_final_order;  // param indices in the order grads become final
+  std::vector<AttnPlan> attn;          // fused attention blocks
 };
 
 struct tx_record {
@@ -470,6 +493,7 @@ struct tx_record {
   std::vector<bool> tf32;  // per value: the buffer holds TF32-rounded values
   bool shadow = false;     // parameters read by GEMMs come from flat_tf32
   bool tracking = false;
+  std::vector<uint8_t> attn_fused;  // per tx_graph::attn block: ran as the fused kernels
 };
 
 namespace {
@@ -932,6 +956,97 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
       n.round_copy = only;
     }
   }
+  // ---- fused attention blocks -------------------------------------------------------------------
+  {
+    auto single = [&](int v) {
+      return v >= 0 && !g->values[v].is_output && g->values[v].consumers.size() == 1 &&
+             g->values[v].kind == TX_VAL_ACT;
+    };
+    auto prod = [&](int v) { return v >= 0 ? g->values[v].producer : -1; };
+    auto is_perm = [&](int ni, std::initializer_list<int> perm) {
+      const tx_node_desc &t = g->nodes[ni].d;
+      if (t.op != TX_OP_TRANSPOSE || t.n_ints != (int)perm.size()) return false;
+      int i = 0;
+      for (int p : perm)
+        if (t.ints[i++] != p) return false;
+      return true;
+    };
+    // value x = Transpose(perm)(Reshape(src)) with single readers on the way: returns src, or -1
+    auto split_of = [&](int x, std::initializer_list<int> perm, int *reshape_node, std::vector<int> &nodes) {
+      if (!single(x)) return -1;
+      const int t = prod(x);
+      if (t < 0 || !is_perm(t, perm)) return -1;
+      const int y = g->nodes[t].d.in[0];
+      if (!single(y)) return -1;
+      const int rsh = prod(y);
+      if (rsh < 0 || g->nodes[rsh].d.op != TX_OP_RESHAPE) return -1;
+      const int src = g->nodes[rsh].d.in[0];
+      if (!single(src)) return -1;
+      nodes.push_back(t);
+      nodes.push_back(rsh);
+      *reshape_node = rsh;
+      return src;
+    };
+    for (int si = 0; si < n_nodes; ++si) {
+      GNode &sn = g->nodes[si];
+      if (sn.d.op != TX_OP_SOFTMAX || (sn.d.iattr[0] != -1 && sn.d.iattr[0] != 3)) continue;
+      std::vector<int> nodes{si};
+      const int x = sn.d.in[0];
+      if (!single(x)) continue;
+      int m1 = -1;
+      float scale = 1.f;
+      const int px = prod(x);
+      if (px < 0) continue;
+      if (g->nodes[px].scaled_into >= 0) {
+        m1 = g->nodes[px].scaled_into;
+        scale = g->nodes[m1].out_scale;
+        nodes.push_back(px);
+      } else if (g->nodes[px].d.op == TX_OP_MATMUL && g->nodes[px].scale_out < 0) {
+        m1 = px;
+      }
+      if (m1 < 0 || g->nodes[m1].d.op != TX_OP_MATMUL || g->nodes[m1].fused_act) continue;
+      nodes.push_back(m1);
+      int rq = -1, rk = -1, rv = -1;
+      const int q = split_of(g->nodes[m1].d.in[0], {0, 2, 1, 3}, &rq, nodes);
+      const int k = split_of(g->nodes[m1].d.in[1], {0, 2, 3, 1}, &rk, nodes);
+      const int probs = sn.d.out[0];
+      if (q < 0 || k < 0 || !single(probs)) continue;
+      const int m2 = g->values[probs].consumers[0];
+      GNode &mn = g->nodes[m2];
+      if (mn.d.op != TX_OP_MATMUL || mn.d.in[0] != probs || mn.d.in[1] == probs || mn.fused_act ||
+          mn.scale_out >= 0)
+        continue;
+      nodes.push_back(m2);
+      const int v = split_of(mn.d.in[1], {0, 2, 1, 3}, &rv, nodes);
+      const int ctxv = mn.d.out[0];
+      if (v < 0 || !single(ctxv)) continue;
+      const int to = g->values[ctxv].consumers[0];
+      if (!is_perm(to, {0, 2, 1, 3}) || !single(g->nodes[to].d.out[0])) continue;
+      const int ro = g->values[g->nodes[to].d.out[0]].consumers[0];
+      if (g->nodes[ro].d.op != TX_OP_RESHAPE) continue;
+      if (q == k || q == v || k == v) continue;
+      bool taken = false;
+      for (int ni : nodes) taken |= g->nodes[ni].attn >= 0;
+      if (taken) continue;
+      nodes.push_back(to);
+      nodes.push_back(ro);
+      AttnPlan a;
+      a.q = q;
+      a.k = k;
+      a.v = v;
+      a.out = g->nodes[ro].d.out[0];
+      a.split_q = rq;
+      a.scale = scale;
+      a.first = *std::min_element(nodes.begin(), nodes.end());
+      a.last = *std::max_element(nodes.begin(), nodes.end());
+      a.round_out = feeds_only_contractions(a.out, 0);
+      // the last member must run after q, k and v exist: every member reads
+      // (through the chain) one of them, and the block ends at the merge
+      for (int ni : nodes) g->nodes[ni].attn = (int)g->attn.size();
+      g->attn.push_back(a);
+    }
+  }
+
   // ---- TF32 gradient rounding: gradients whose every reader is a contraction -----------------
   // The gradient of v is read by the backward of v's producer: a MatMul (no
   // fused activation, no bias) reads it only as an operand of its dgrad and
@@ -1275,9 +1390,33 @@ struct Fwd {
     return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);
   }
 
+  // The fused kernels take the block when the contractions run in TF32 and the
+  // shapes fit them (q, k, v [B, S <= 128, H * 64]); otherwise its nodes run one
+  // by one.
+  bool attn_ok(const AttnPlan &a) {
+    if (ctx->math != TX_MATH_TF32) return false;
+    const Shape &q = S(a.q), &sp = S(g->nodes[a.split_q].d.out[0]);
+    if (q.size() != 3 || S(a.k) != q || S(a.v) != q || sp.size() != 4) return false;
+    return sp[0] == q[0] && sp[1] == q[1] && sp[3] == 64 && sp[2] * 64 == q[2] && q[1] >= 1 && q[1] <= 128;
+  }
+
+  int attn_forward(const AttnPlan &a) {
+    TX_TRY(alloc_value(a.out));
+    const Shape &q = S(a.q);
+    const int64_t B = q[0], Sq = q[1], E = q[2];
+    const int flags = ((r->tf32[a.q] && r->tf32[a.k] && r->tf32[a.v]) ? 1 : 0) | (a.round_out ? 2 : 0);
+    if (a.round_out) r->tf32[a.out] = true;
+    return tx_attention_fwd(ctx, F(a.q), F(a.k), F(a.v), E, F(a.out), E, B, Sq, E / 64, 64, a.scale, flags);
+  }
+
   int node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
+    if (n.attn >= 0) {
+      const AttnPlan &a = g->attn[n.attn];
+      if (ni == a.first) r->attn_fused[n.attn] = attn_ok(a);
+      if (r->attn_fused[n.attn]) return ni == a.last ? attn_forward(a) : TX_OK;
+    }
     if (n.fused_into >= 0 || n.scaled_into >= 0) return TX_OK;  // done by the producing GEMM
     if (is_alias_op(d.op)) {
       r->buf[d.out[0]] = r->buf[d.in[0]];
@@ -1435,6 +1574,7 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
   r->extra.assign(g->nodes.size(), nullptr);
   r->extra2.assign(g->nodes.size(), {});
   r->tf32.assign(nv, false);
+  r->attn_fused.assign(g->attn.size(), 0);
   if (ctx->math == TX_MATH_TF32 && g->flat_len > 0) {
     // the contractions of this forward (and of its backward) read parameters
     // from a TF32-rounded copy, refreshed here so that it always matches the
@@ -1926,9 +2066,40 @@ struct Bwd {
     return rc;
   }
 
+  int attn_backward(const AttnPlan &a) {
+    const float *dout = grad[a.out];
+    if (!dout) return TX_OK;
+    const Shape &q = S(a.q);
+    const int64_t B = q[0], Sq = q[1], E = q[2];
+    float *t[3];
+    int acc[3];
+    const int vs[3] = {a.q, a.k, a.v};
+    for (int i = 0; i < 3; ++i) TX_TRY(target(vs[i], &t[i], &acc[i]));
+    const bool all_acc = acc[0] && acc[1] && acc[2];
+    if (!all_acc && (acc[0] || acc[1] || acc[2]))  // one launch writes all three: accumulate into zeroed ones
+      for (int i = 0; i < 3; ++i)
+        if (!acc[i]) TX_CUDA(ctx, cudaMemsetAsync(t[i], 0, numel_of(q) * 4, ctx->stream));
+    const bool any_acc = acc[0] || acc[1] || acc[2];
+    const bool rnd = ctx->math == TX_MATH_TF32 && !any_acc && g->values[a.q].grad_round &&
+                     g->values[a.k].grad_round && g->values[a.v].grad_round;
+    const int flags = ((r->tf32[a.q] && r->tf32[a.k] && r->tf32[a.v] && grad_tf32[a.out]) ? 1 : 0) |
+                      (any_acc ? 2 : 0) | (rnd ? 4 : 0);
+    TX_TRY(tx_attention_bwd(ctx, F(a.q), F(a.k), F(a.v), E, dout, E, t[0], t[1], t[2], E, B, Sq, E / 64, 64,
+                            a.scale, flags));
+    for (int i = 0; i < 3; ++i) {
+      grad_tf32[vs[i]] = rnd;
+      wrote(vs[i]);
+    }
+    return TX_OK;
+  }
+
   int node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
+    if (n.attn >= 0 && r->attn_fused[n.attn]) {
+      const AttnPlan &a = g->attn[n.attn];
+      return ni == a.last ? attn_backward(a) : TX_OK;
+    }
     if (n.scaled_into >= 0) return TX_OK;  // scale folded into the producing contraction's alpha
     if (n.fused_into >= 0) {
       // activation folded into the producing GEMM: hand the gradient over
