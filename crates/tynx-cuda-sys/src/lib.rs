@@ -166,6 +166,7 @@ pub struct tx_gemm_desc {
     pub colsum: *mut f32,
     pub colsum_scale: f32,
     pub colsum_acc: i32,
+    pub B_lo: *const f32,
 }
 
 #[repr(C)]

@@ -170,6 +170,10 @@ typedef struct tx_gemm_desc {
    * sum over rows of C[:, n], taken before any TF32 output rounding;
    * colsum_acc != 0 adds to colsum.  batch must be 1. */
   float *colsum; float colsum_scale; int32_t colsum_acc;
+  /* optional, TX_MATH_TF32 only: the TF32 tail of B (B_lo = rna(B0 - B) for
+   * the weights B0 whose TF32 head rna(B0) is B), same layout as B; the
+   * product becomes op(A) (B + B_lo), fp32-class in B */
+  const float *B_lo;
 } tx_gemm_desc;
 /* flags: in TX_MATH_TF32 (round-to-nearest) mode the contraction rounds each
  * operand element to TF32 (cvt.rna).  An operand whose buffer already holds
@@ -187,6 +191,11 @@ int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc);
 /* dst[i] = src[i] rounded to TF32 (round to nearest, ties away from zero;
  * dst may equal src).  The operand shadow of TX_GEMM_A_TF32 / B_TF32. */
 int tx_round_tf32(tx_ctx *ctx, const float *d_src, float *d_dst, int64_t n);
+/* d_hi[i] = rna(src[i]) and d_lo[i] = rna(src[i] - d_hi[i]) (TF32 head and
+ * tail: hi + lo equals src to about 2^-22 relative).  The graph engine splits
+ * its parameters so every forward contraction multiplies by the weights to
+ * fp32-class accuracy (tx_gemm_desc.B_lo). */
+int tx_split_tf32(tx_ctx *ctx, const float *d_src, float *d_hi, float *d_lo, int64_t n);
 
 /* Elementwise.  replaces: DynTensor activations (tensor.rs:2002-2240) and
  * broadcast arithmetic (tensor.rs:1637-1700). */

@@ -70,6 +70,7 @@ class GemmDesc(C.Structure):
         ("batch", C.c_int64), ("stride_a", C.c_int64), ("stride_b", C.c_int64),
         ("stride_c", C.c_int64), ("flags", C.c_int32),
         ("colsum", C.c_void_p), ("colsum_scale", C.c_float), ("colsum_acc", C.c_int32),
+        ("B_lo", C.c_void_p),
     ]
 
 
@@ -166,6 +167,7 @@ SIGNATURES = {
     "tx_take_last_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i32],
     "tx_bias_grad": [_vp, _vp, _vp, _i64, _i64, _f, _i32],
     "tx_round_tf32": [_vp, _vp, _vp, _i64],
+    "tx_split_tf32": [_vp, _vp, _vp, _vp, _i64],
     "tx_optim_create": [_vp, C.POINTER(OptimCfg), _i32, C.POINTER(_vp), C.POINTER(_vp), _p64,
                         C.POINTER(_vp)],
     "tx_optim_set_lr": [_vp, C.c_double],

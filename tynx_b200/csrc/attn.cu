@@ -32,7 +32,8 @@
 //
 // Numerics (TF32 mode): operands are rounded to nearest TF32 (cvt.rna) in
 // shared memory unless the caller states they already are; softmax is
-// exp(x - max) * (1 / sum) in fp32 with expf, as the unfused softmax kernel.
+// exp(x - max) * (1 / sum) in fp32 with the hardware exponential (__expf, a
+// few ulp; the products around it are TF32).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -169,6 +170,92 @@ __device__ __forceinline__ void tld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tcgen05.ld without the wait; the registers are valid after tld_wait() and
+// regs_after_wait(), which keeps every use of them behind the wait
+__device__ __forceinline__ void tld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void regs_after_wait(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),
+                 "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+                 "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+                 "+r"(r[31]));
+}
+// a thread's whole 128-column row of a TMEM tile: four loads in flight, one wait
+__device__ __forceinline__ void tld128(uint32_t trow, float (&v)[128]) {
+  uint32_t r0[32], r1[32], r2[32], r3[32];
+  tld32_issue(trow, r0);
+  tld32_issue(trow + 32, r1);
+  tld32_issue(trow + 64, r2);
+  tld32_issue(trow + 96, r3);
+  tld_wait();
+  regs_after_wait(r0);
+  regs_after_wait(r1);
+  regs_after_wait(r2);
+  regs_after_wait(r3);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] = __uint_as_float(r0[j]);
+    v[32 + j] = __uint_as_float(r1[j]);
+    v[64 + j] = __uint_as_float(r2[j]);
+    v[96 + j] = __uint_as_float(r3[j]);
+  }
+}
+// 32 columns of a thread's TMEM row from registers (visible to later loads of
+// this thread after tst_wait())
+__device__ __forceinline__ void tst32(uint32_t taddr, const float *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+      "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Softmax of scale * row over its valid keys, in place: v becomes P (0 on
+// masked keys and on rows past the sequence).  exp via the __expf intrinsic.
+__device__ __forceinline__ void softmax_row(float (&v)[128], float scale, int seq, bool live) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 128; ++j) {
+    v[j] *= scale;
+    if (j < seq) m = fmaxf(m, v[j]);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 128; ++j) {
+    v[j] = j < seq ? __expf(v[j] - m) : 0.f;
+    sum += v[j];
+  }
+  const float inv = live ? 1.0f / sum : 0.f;
+#pragma unroll
+  for (int j = 0; j < 128; ++j) v[j] *= inv;
+}
+
 // Round `bytes` of shared memory to TF32 in place (128 threads, float4 steps).
 __device__ __forceinline__ void round_region(uint8_t *p, int bytes, int t) {
   float4 *q = reinterpret_cast<float4 *>(p);
@@ -221,45 +308,6 @@ __device__ __forceinline__ void store_row(uint32_t trow, float *dst, bool live, 
       d4[j] = w;
     }
   }
-}
-
-struct SoftRow {
-  float m = -INFINITY, inv = 0.f;
-};
-
-// Row statistics of softmax(scale * S) over the valid keys (TMEM columns
-// 0..127 of this thread's lane): max, then 1 / sum of exp(x - max).
-__device__ __forceinline__ SoftRow row_stats(uint32_t trow, float scale, int seq) {
-  SoftRow s;
-  float m = -INFINITY;
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    tld32(trow + c * 32, v);
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c * 32 + j < seq) m = fmaxf(m, v[j] * scale);
-  }
-  float sum = 0.f;
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    tld32(trow + c * 32, v);
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c * 32 + j < seq) sum += expf(v[j] * scale - m);
-  }
-  s.m = m;
-  s.inv = 1.0f / sum;
-  return s;
-}
-
-// P's 32 values of key block c for this row (0 for masked keys or rows)
-__device__ __forceinline__ void row_probs(uint32_t trow, int c, const SoftRow &st, float scale, int seq,
-                                          bool live, float (&p)[32]) {
-  tld32(trow + c * 32, p);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) p[j] = (live && c * 32 + j < seq) ? expf(p[j] * scale - st.m) * st.inv : 0.f;
 }
 
 // ---- forward --------------------------------------------------------------------------------
@@ -343,15 +391,15 @@ __global__ void __launch_bounds__(192, 2)
     const bool ok_s = __all_sync(0xffffffffu, bar_wait(b_s, abort_flag, err, 4));
     fence_after();
     if (ok_s) {
-      const SoftRow st = row_stats(trow, scale, seq);
-      const bool live = r < seq;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float p[32];
-        row_probs(trow, c, st, scale, seq, live, p);
+      float p[128];
+      tld128(trow, p);
+      softmax_row(p, scale, seq, r < seq);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) p[j] = rn_tf32(p[j]);
-        put_row(sp + c * 16384, r, p);
+      for (int c = 0; c < 4; ++c) {
+        float q[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) q[j] = rn_tf32(p[c * 32 + j]);
+        put_row(sp + c * 16384, r, q);
       }
     }
     fence_async_smem();
@@ -520,36 +568,37 @@ __global__ void __launch_bounds__(192, 1)
     }
     bool ok = __all_sync(0xffffffffu, bar_wait(b_s, abort_flag, err, 23));
     fence_after();
-    SoftRow st;
+    float p[128];
     float dsum = 0.f;
     if (ok) {
-      st = row_stats(trow, scale, seq);
+      tld128(trow, p);
+      softmax_row(p, scale, seq, live);
       // P^T for dV, and D = rowsum(P * dP)
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float p[32], g[32];
-        row_probs(trow, c, st, scale, seq, live, p);
+        float g[32], q[32];
         tld32(trow + 128 + c * 32, g);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          dsum += p[j] * g[j];
-          p[j] = rn_tf32(p[j]);
+          dsum += p[c * 32 + j] * g[j];
+          q[j] = rn_tf32(p[c * 32 + j]);
         }
-        put_col(R0, r, c, p);
+        put_col(R0, r, c, q);
       }
     }
     fence_async_smem();
     bar_arrive(b_pt);
-    if (ok) {  // dS rows for dQ
-#pragma unroll 1
+    if (ok) {  // dS rows for dQ; dS also replaces dP in TMEM for the dS^T pass
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float p[32], g[32];
-        row_probs(trow, c, st, scale, seq, live, p);
+        float g[32];
         tld32(trow + 128 + c * 32, g);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) p[j] = rn_tf32(p[j] * (g[j] - dsum) * scale);
-        put_row(R2 + c * 16384, r, p);
+        for (int j = 0; j < 32; ++j) g[j] = rn_tf32(p[c * 32 + j] * (g[j] - dsum) * scale);
+        put_row(R2 + c * 16384, r, g);
+        tst32(trow + 128 + c * 32, g);
       }
+      tst_wait();
     }
     fence_async_smem();
     bar_arrive(b_ds);
@@ -561,12 +610,9 @@ __global__ void __launch_bounds__(192, 1)
       // dS^T into the P^T region for dK
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        float p[32], g[32];
-        row_probs(trow, c, st, scale, seq, live, p);
+        float g[32];
         tld32(trow + 128 + c * 32, g);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) p[j] = rn_tf32(p[j] * (g[j] - dsum) * scale);
-        put_col(R0, r, c, p);
+        put_col(R0, r, c, g);
       }
     }
     fence_async_smem();

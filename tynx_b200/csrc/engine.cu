@@ -475,6 +475,7 @@ struct tx_graph {
   float *flat_values = nullptr;
   float *flat_grads = nullptr;
   float *flat_tf32 = nullptr;  // TF32-rounded copy of flat_values (GEMM operands)
+  float *flat_lo = nullptr;    // TF32 tail of flat_values (forward contractions: head + tail)
   int64_t flat_len = 0;
   // DP
   bool dp = false;
@@ -1144,6 +1145,7 @@ extern "C" int tx_graph_destroy(tx_graph *g) {
   if (g->flat_values) cudaFree(g->flat_values);
   if (g->flat_grads) cudaFree(g->flat_grads);
   if (g->flat_tf32) cudaFree(g->flat_tf32);
+  if (g->flat_lo) cudaFree(g->flat_lo);
   delete g;
   return TX_OK;
 }
@@ -1336,6 +1338,15 @@ struct Fwd {
     }
     q.alpha *= n.out_scale;
     q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0) | (ex ? TX_GEMM_EXACT : 0);
+    // TF32 mode: a weight operand enters the forward product as head + tail
+    // (fp32-class in the weights; the activation stays TF32).  Rounding the
+    // weights is a systematic perturbation that the whole backward inherits:
+    // on the transformer encoder it sets most of the TF32 gradient error
+    // (1.2e-3 relative with rounded weights, 0.9e-3 with split ones, float64
+    // emulation of every product).
+    const GValue &wv = g->values[d.in[1]];
+    if (!ex && r->shadow && b32 && wv.kind == TX_VAL_PARAM)
+      q.B_lo = g->flat_lo + g->param_offset[wv.param_index];
     if (n.round_out && ctx->math == TX_MATH_TF32) {
       q.flags |= TX_GEMM_ROUND_OUT;
       r->tf32[yv] = true;
@@ -1580,7 +1591,8 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
     // from a TF32-rounded copy, refreshed here so that it always matches the
     // fp32 values whatever changed them since
     if (!g->flat_tf32) TX_CUDA(ctx, cudaMalloc(&g->flat_tf32, g->flat_len * sizeof(float)));
-    TX_TRY(tx_round_tf32(ctx, g->flat_values, g->flat_tf32, g->flat_len));
+    if (!g->flat_lo) TX_CUDA(ctx, cudaMalloc(&g->flat_lo, g->flat_len * sizeof(float)));
+    TX_TRY(tx_split_tf32(ctx, g->flat_values, g->flat_tf32, g->flat_lo, g->flat_len));
     r->shadow = true;
   }
   for (size_t i = 0; i < g->inputs.size(); ++i) {

@@ -313,7 +313,36 @@ int gemm_simt(tx_ctx *ctx, const tx_gemm_desc &d) {
 int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc, bool *rounded) {
   if (rounded) *rounded = false;
   tx_gemm_desc d = desc;
-  if (ctx->math != TX_MATH_TF32) d.flags = 0;  // TF32 operand / output rounding only applies there
+  if (ctx->math != TX_MATH_TF32) {
+    d.flags = 0;  // TF32 operand / output rounding only applies there
+    d.B_lo = nullptr;
+  }
+  if (d.B_lo && d.M > 0 && d.N > 0) {
+    // split weights: the persistent tcgen05 kernel takes the head and the
+    // tail in one pass; any other path computes C = alpha A B_lo first, then
+    // alpha A B + C with the epilogue (beta 1)
+    if (d.colsum || d.beta != 0.f || (d.flags & TX_GEMM_EXACT))
+      return tx_fail(ctx, TX_ERR_UNSUPPORTED, "split weights with beta, column sums or EXACT");
+    int rc = gemm_tcgen05(ctx, d, (d.flags & TX_GEMM_A_TF32) ? 0 : 1, nullptr);
+    if (rc != TX_ERR_UNSUPPORTED) {
+      if (rounded) *rounded = rc == TX_OK && (d.flags & TX_GEMM_ROUND_OUT);
+      return rc;
+    }
+    tx_gemm_desc lo = d;
+    lo.B = d.B_lo;
+    lo.B_lo = nullptr;
+    lo.bias = nullptr;
+    lo.act = TX_ACT_NONE;
+    lo.preact = nullptr;
+    lo.dact = TX_ACT_NONE;
+    lo.dact_src = nullptr;
+    lo.flags &= ~TX_GEMM_ROUND_OUT;
+    TX_TRY(gemm_dispatch(ctx, lo));
+    tx_gemm_desc hi = d;
+    hi.B_lo = nullptr;
+    hi.beta = 1.f;
+    return gemm_dispatch(ctx, hi, rounded);
+  }
   if (d.M <= 0 || d.N <= 0) {
     if (d.colsum && d.N > 0 && !d.colsum_acc)
       TX_CUDA(ctx, cudaMemsetAsync(d.colsum, 0, d.N * sizeof(float), ctx->stream));

@@ -218,6 +218,16 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
   else  // B stored K x N (MN-major): box 32(N) x 32(K)
     ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
+  // split weights (B head + tail) run on the persistent kernel only; other
+  // shapes report unsupported and the dispatcher runs two products instead
+  if (d.B_lo) {
+    if (!persistent || tiling.splits > 1 || d.trans_a || ((uintptr_t)d.B_lo & 15)) return TX_ERR_UNSUPPORTED;
+    if (d.trans_b)
+      ok = make_map(&m.b2, d.B_lo, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
+    else
+      ok = make_map(&m.b2, d.B_lo, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
+    if (!ok) return TX_ERR_UNSUPPORTED;
+  }
 
   // Split K across CTAs when the output has fewer tiles than SMs (the weight
   // gradients of small layers, whose reduction runs over the whole batch):
@@ -240,7 +250,9 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
     }
     if (persistent && m.tma_epi) {
       const int rc = launch_persistent(ctx, bn, d, m, batch, 0);
-      if (rc != TX_ERR_UNSUPPORTED) return rc;
+      if (rc != TX_ERR_UNSUPPORTED || d.B_lo) return rc;
+    } else if (d.B_lo) {
+      return TX_ERR_UNSUPPORTED;
     }
     if (pair) return launch_pair(ctx, d, m, batch, 0);
     return launch_any(ctx, mode, bn, d, m, batch, 0);

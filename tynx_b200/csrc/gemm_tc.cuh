@@ -17,6 +17,7 @@ constexpr int TC_BK = 32;  // fp32 elements per 128-byte swizzle row
 // output (also the beta * C input), the act' source and the pre-activation.
 struct Maps {
   CUtensorMap a, b, c, s, p;
+  CUtensorMap b2;  // the TF32 tail of B (tx_gemm_desc.B_lo), persistent kernel only
   int tma_epi = 0;
   int conv_mask = 3;  // MODE 1: operands to round in shared memory (bit 0 A, bit 1 B)
   float *col_part = nullptr;  // fused column sums, TMA epilogue only

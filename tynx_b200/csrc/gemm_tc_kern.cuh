@@ -997,14 +997,17 @@ __global__ void __launch_bounds__(320, 1)
 constexpr int kSmemMax = 232448;  // 227 KB opt-in
 constexpr int kPTail = 2048;  // barriers, then each epilogue warp's 32 bias values (8 warps at most)
 
-template <int BN>
+// BLO: B arrives as a TF32 head and tail (two tiles per stage) and each
+// k-slice issues A B + A B_lo, so the weights enter the product to fp32-class
+// accuracy while A stays TF32.
+template <int BN, bool BLO = false>
 struct PCfg {
   static constexpr int NACC = BN == 256 ? 1 : 2;
   static constexpr int ACC = BN * NACC;                 // columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC < 256 ? 256 : 2 * ACC;
   static constexpr int A_BYTES = TC_BM * TC_BK * 4;
   static constexpr int B_BYTES = BN * TC_BK * 4;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGE = A_BYTES + B_BYTES * (BLO ? 2 : 1);
 };
 
 struct PWork {
@@ -1015,12 +1018,13 @@ struct PWork {
   float *col_part;       // fused column sums (one row per 32 output rows) or null
 };
 
-template <int BN, bool A_MN, bool B_MN, int EW>
+template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
     k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
-               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, PWork w) {
-  using Cfg = PCfg<BN>;
+               const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapB2,
+               const tx_gemm_desc d, int *err, PWork w) {
+  using Cfg = PCfg<BN, BLO>;
   constexpr int NACC = Cfg::NACC;
   constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
@@ -1088,7 +1092,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const int s = (int)(cnt % (uint32_t)stages);
           const uint32_t round = cnt / (uint32_t)stages;
           if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 11)) break;
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES * (BLO ? 2 : 1));
           const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
           const uint32_t b_dst = a_dst + A_BYTES;
           const int k0 = (kb_first + kb) * TC_BK;
@@ -1103,6 +1107,16 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
           } else {
             tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
+          }
+          if (BLO) {
+            const uint32_t l_dst = b_dst + B_BYTES;
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_3d(l_dst + j * 4096, &mapB2, &full[s], n0 + 32 * j, k0, zc);
+            } else {
+              tma_load_3d(l_dst, &mapB2, &full[s], k0, n0, zc);
+            }
           }
         }
       }
@@ -1135,9 +1149,11 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const uint32_t acc = tmem + (uint32_t)(buf * Cfg::ACC + (kb % NACC) * BN);
           const bool fresh = kb < NACC;
 #pragma unroll
-          for (int k = 0; k < TC_BK / 8; ++k)
-            tc_mma_tf32(acc, operand_desc<A_MN>(a_base, k), operand_desc<B_MN>(b_base, k), idesc,
-                        (fresh && k == 0) ? 0u : 1u);
+          for (int k = 0; k < TC_BK / 8; ++k) {
+            const uint64_t ad = operand_desc<A_MN>(a_base, k);
+            tc_mma_tf32(acc, ad, operand_desc<B_MN>(b_base, k), idesc, (fresh && k == 0) ? 0u : 1u);
+            if (BLO) tc_mma_tf32(acc, ad, operand_desc<B_MN>(b_base + B_BYTES, k), idesc, 1u);
+          }
           tc_commit(&empty[s]);
         }
         if (!ok) break;
@@ -1278,9 +1294,9 @@ int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64
 
 
 #ifdef TX_TC_PERSISTENT_TU
-template <int BN, bool A_MN, bool B_MN, int EW>
+template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false>
 int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
-  auto kern = k_gemm_tcp<BN, A_MN, B_MN, EW>;
+  auto kern = k_gemm_tcp<BN, A_MN, B_MN, EW, BLO>;
   static bool configured[64] = {};
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
@@ -1289,7 +1305,7 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
   }
   int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
   if (max_grid > 0 && grid > max_grid) grid = max_grid;
-  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, w);
+  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, m.b2, d, ctx->d_err, w);
   TX_LAUNCHED(ctx, "k_gemm_tcp");
   return TX_OK;
 }
@@ -1297,6 +1313,11 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
 template <int BN, int EW>
 int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
+  if (d.B_lo) {  // split weights: forward layouts only (A K-major)
+    if (a_mn) return TX_ERR_UNSUPPORTED;
+    return b_mn ? launch_p<BN, false, true, EW, true>(ctx, d, m, w, smem, max_grid)
+                : launch_p<BN, false, false, EW, true>(ctx, d, m, w, smem, max_grid);
+  }
   if (a_mn && b_mn) return launch_p<BN, true, true, EW>(ctx, d, m, w, smem, max_grid);
   if (a_mn) return launch_p<BN, true, false, EW>(ctx, d, m, w, smem, max_grid);
   if (b_mn) return launch_p<BN, false, true, EW>(ctx, d, m, w, smem, max_grid);
@@ -1310,7 +1331,7 @@ int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &
 // would fit one wave, so that one tile's epilogue overlaps the next's main loop).
 int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per,
                            int max_grid) {
-  const int stage = (TC_BM + bn) * TC_BK * 4;
+  const int stage = (TC_BM + bn * (d.B_lo ? 2 : 1)) * TC_BK * 4;
   const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
   PWork w;
   w.ep_stride = kinds * 8192;

@@ -682,6 +682,18 @@ __global__ void k_round_tf32(const float *__restrict__ src, float *__restrict__ 
   }
 }
 
+// TF32 head and tail: hi = rna(x), lo = rna(x - hi) (x - hi is exact in fp32)
+__global__ void k_split_tf32(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
+                             int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float x = src[i];
+    const float h = tx_epi::round_tf32(x);
+    hi[i] = h;
+    lo[i] = tx_epi::round_tf32(x - h);
+  }
+}
+
 // ---- gather / scatter (gather.rs:18-58; select / select_assign) -------------------------
 __global__ void k_gather_rows(const float *__restrict__ table, int64_t rows, int64_t width,
                               const int64_t *__restrict__ idx, int64_t n, float *__restrict__ out,
@@ -850,26 +862,31 @@ struct OptHparams {
 
 // Adam / AdamW: one block per chunk.  Step counters: t = steps[i] + 1 for the
 // math; the last block to finish (atomic ticket) commits the increments.
-constexpr int64_t kAdamSub = 1024;  // elements per CTA: one float4 per thread (256 threads)
+// The bias corrections of each tensor's next update, bc[2i] = 1 - beta1^t and
+// bc[2i+1] = 1 - beta2^t (in double, rounded to f32 as mul_scalar /
+// div_scalar(f64) on f32 data round them), live in device memory: written by
+// k_adam_bc when the step counters or the betas are set, and by the last block
+// of each step for the tensors it advanced, so no block evaluates pow().
+__global__ void k_adam_bc(const int64_t *__restrict__ steps, float *__restrict__ bc, int n, double beta1,
+                          double beta2) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const double t = (double)(steps[i] + 1);
+    bc[2 * i] = (float)(1.0 - pow(beta1, t));
+    bc[2 * i + 1] = (float)(1.0 - pow(beta2, t));
+  }
+}
+
+constexpr int64_t kAdamSub = 2048;  // elements per CTA: two float4 per thread (256 threads)
 
 // At most 64 registers, so several CTAs share an SM.
 __global__ void __launch_bounds__(256, 4)
     k_adam(const OptTensor *__restrict__ tensors, const OptChunk *__restrict__ chunks, int n_chunks,
-           const OptHparams *__restrict__ hp_ptr, int64_t *steps, const int32_t *__restrict__ active_list,
-           int n_active, int kind, int amsgrad, unsigned *ticket) {
+           const OptHparams *__restrict__ hp_ptr, int64_t *steps, float *__restrict__ bc,
+           const int32_t *__restrict__ active_list, int n_active, int kind, int amsgrad, unsigned *ticket) {
   const OptHparams hp = *hp_ptr;
   const OptChunk ch = chunks[blockIdx.x];
   const OptTensor t = tensors[ch.tensor];
-  // bias corrections in double, rounded to f32 like mul_scalar/div_scalar(f64)
-  // on f32 data; computed once per CTA (the double pow is long and register-hungry)
-  __shared__ float s_bc[2];
-  if (threadIdx.x == 0) {
-    const double step = (double)(steps[ch.tensor] + 1);
-    s_bc[0] = (float)(1.0 - pow(hp.beta1_d, step));
-    s_bc[1] = (float)(1.0 - pow(hp.beta2_d, step));
-  }
-  __syncthreads();
-  const float bc1 = s_bc[0], bc2 = s_bc[1];
+  const float bc1 = bc[2 * ch.tensor], bc2 = bc[2 * ch.tensor + 1];
   const bool coupled = (kind == 0) && hp.wd != 0.f;
   const bool decoupled = (kind == 1) && hp.wd != 0.f;
   // one element, in the order of adam.rs:458-509 (no FMA contraction)
@@ -897,18 +914,40 @@ __global__ void __launch_bounds__(256, 4)
   const bool vec = !amsgrad && (lo & 3) == 0 &&
                    ((((uintptr_t)t.w) | ((uintptr_t)t.g) | ((uintptr_t)t.m) | ((uintptr_t)t.v)) & 15) == 0;
   if (vec) {
-    for (int64_t i = lo + threadIdx.x * 4; i + 3 < hi; i += (int64_t)blockDim.x * 4) {
-      float4 w = *reinterpret_cast<float4 *>(t.w + i);
-      const float4 g = *reinterpret_cast<const float4 *>(t.g + i);
-      float4 m = *reinterpret_cast<float4 *>(t.m + i);
-      float4 v = *reinterpret_cast<float4 *>(t.v + i);
-      update(w.x, g.x, m.x, v.x, nullptr);
-      update(w.y, g.y, m.y, v.y, nullptr);
-      update(w.z, g.z, m.z, v.z, nullptr);
-      update(w.w, g.w, m.w, v.w, nullptr);
-      *reinterpret_cast<float4 *>(t.w + i) = w;
-      *reinterpret_cast<float4 *>(t.m + i) = m;
-      *reinterpret_cast<float4 *>(t.v + i) = v;
+    // both of a thread's float4 groups are loaded before either is updated,
+    // so each thread keeps 128 bytes of loads in flight
+    const int64_t i0 = lo + threadIdx.x * 4, i1 = i0 + (int64_t)blockDim.x * 4;
+    const bool h0 = i0 + 3 < hi, h1 = i1 + 3 < hi;
+    float4 w0, g0, m0, v0, w1, g1, m1, v1;
+    if (h0) {
+      w0 = *reinterpret_cast<float4 *>(t.w + i0);
+      g0 = *reinterpret_cast<const float4 *>(t.g + i0);
+      m0 = *reinterpret_cast<float4 *>(t.m + i0);
+      v0 = *reinterpret_cast<float4 *>(t.v + i0);
+    }
+    if (h1) {
+      w1 = *reinterpret_cast<float4 *>(t.w + i1);
+      g1 = *reinterpret_cast<const float4 *>(t.g + i1);
+      m1 = *reinterpret_cast<float4 *>(t.m + i1);
+      v1 = *reinterpret_cast<float4 *>(t.v + i1);
+    }
+    if (h0) {
+      update(w0.x, g0.x, m0.x, v0.x, nullptr);
+      update(w0.y, g0.y, m0.y, v0.y, nullptr);
+      update(w0.z, g0.z, m0.z, v0.z, nullptr);
+      update(w0.w, g0.w, m0.w, v0.w, nullptr);
+      *reinterpret_cast<float4 *>(t.w + i0) = w0;
+      *reinterpret_cast<float4 *>(t.m + i0) = m0;
+      *reinterpret_cast<float4 *>(t.v + i0) = v0;
+    }
+    if (h1) {
+      update(w1.x, g1.x, m1.x, v1.x, nullptr);
+      update(w1.y, g1.y, m1.y, v1.y, nullptr);
+      update(w1.z, g1.z, m1.z, v1.z, nullptr);
+      update(w1.w, g1.w, m1.w, v1.w, nullptr);
+      *reinterpret_cast<float4 *>(t.w + i1) = w1;
+      *reinterpret_cast<float4 *>(t.m + i1) = m1;
+      *reinterpret_cast<float4 *>(t.v + i1) = v1;
     }
     // ragged tail of the last chunk of a tensor (past the last multiple of 4)
     const int64_t tail = (hi & ~int64_t(3)) > lo ? (hi & ~int64_t(3)) : lo;
@@ -928,12 +967,23 @@ __global__ void __launch_bounds__(256, 4)
       t.v[i] = v;
     }
   }
+  __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    unsigned done = atomicAdd(ticket, 1u);
-    if (done == (unsigned)(gridDim.x * gridDim.y) - 1) {
-      for (int i = 0; i < n_active; ++i) steps[active_list[i]] += 1;
+    s_last = atomicAdd(ticket, 1u) == (unsigned)(gridDim.x * gridDim.y) - 1;
+  }
+  __syncthreads();
+  if (s_last) {  // every block has read the step counters and corrections: advance them
+    for (int i = threadIdx.x; i < n_active; i += blockDim.x) {
+      const int k = active_list[i];
+      const int64_t done = steps[k] + 1;
+      steps[k] = done;
+      bc[2 * k] = (float)(1.0 - pow(hp.beta1_d, (double)(done + 1)));
+      bc[2 * k + 1] = (float)(1.0 - pow(hp.beta2_d, (double)(done + 1)));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
       __threadfence();
       *ticket = 0u;
     }
@@ -1331,6 +1381,14 @@ extern "C" int tx_round_tf32(tx_ctx *ctx, const float *src, float *dst, int64_t 
   return TX_OK;
 }
 
+extern "C" int tx_split_tf32(tx_ctx *ctx, const float *src, float *hi, float *lo, int64_t n) {
+  if (!ctx || (n > 0 && (!src || !hi || !lo))) return TX_ERR_INVALID;
+  if (n <= 0) return TX_OK;
+  k_split_tf32<<<grid_for(n, 256), 256, 0, ctx->stream>>>(src, hi, lo, n);
+  TX_LAUNCHED(ctx, "k_split_tf32");
+  return TX_OK;
+}
+
 extern "C" int tx_bias_grad(tx_ctx *ctx, const float *dy, float *db, int64_t M, int64_t N,
                             float scale, int acc) {
   if (!ctx) return TX_ERR_INVALID;
@@ -1373,6 +1431,7 @@ struct tx_optim {
   int64_t *d_steps = nullptr;
   OptHparams *d_hp = nullptr;
   unsigned *d_ticket = nullptr;
+  float *d_bc = nullptr;  // per tensor: the next update's two bias corrections (Adam)
   std::vector<float *> state;  // m, v, vmax per tensor (SGD: momentum in m)
   // chunk tables keyed by active mask
   std::map<std::vector<uint8_t>, std::pair<OptChunk *, int>> tables;
@@ -1383,6 +1442,15 @@ struct tx_optim {
 // blocks (about 450 for 1.9 M parameters) to keep every SM streaming
 static const int64_t kChunk = 4096;
 static int build_table(tx_optim *o, const std::vector<uint8_t> &key);
+
+// bias corrections of every tensor's next update from its step counter
+static int refresh_bias_corrections(tx_optim *o) {
+  if (o->cfg.kind == 2 || !o->d_bc) return TX_OK;
+  k_adam_bc<<<grid_for(o->n, 128), 128, 0, o->ctx->stream>>>(o->d_steps, o->d_bc, o->n, o->cfg.beta1,
+                                                             o->cfg.beta2);
+  TX_LAUNCHED(o->ctx, "k_adam_bc");
+  return TX_OK;
+}
 
 static int upload_hparams(tx_optim *o) {
   if (o->ctx->capturing)
@@ -1404,6 +1472,7 @@ static int upload_hparams(tx_optim *o) {
   h.one_minus_dampening = (float)(1.0 - c.dampening);
   // stream-ordered after earlier steps that read the old values
   TX_CUDA(o->ctx, cudaMemcpyAsync(o->d_hp, &h, sizeof h, cudaMemcpyHostToDevice, o->ctx->stream));
+  TX_TRY(refresh_bias_corrections(o));
   TX_CUDA(o->ctx, cudaStreamSynchronize(o->ctx->stream));
   return TX_OK;
 }
@@ -1440,6 +1509,7 @@ extern "C" int tx_optim_create(tx_ctx *ctx, const tx_optim_cfg *cfg, int n, floa
   TX_CUDA(ctx, cudaMalloc(&o->d_steps, n * sizeof(int64_t)));
   TX_CUDA(ctx, cudaMalloc(&o->d_hp, sizeof(OptHparams)));
   TX_CUDA(ctx, cudaMalloc(&o->d_ticket, sizeof(unsigned)));
+  TX_CUDA(ctx, cudaMalloc(&o->d_bc, 2 * n * sizeof(float)));
   TX_CUDA(ctx, cudaMemcpyAsync(o->d_tensors, o->host_tensors.data(), n * sizeof(OptTensor),
                                cudaMemcpyHostToDevice, ctx->stream));
   TX_CUDA(ctx, cudaMemsetAsync(o->d_steps, 0, n * sizeof(int64_t), ctx->stream));
@@ -1518,9 +1588,8 @@ extern "C" int tx_optim_step(tx_optim *o, const uint8_t *active) {
                                              o->d_ticket);
   } else {
     k_adam<<<dim3((unsigned)n_chunks, (unsigned)(kChunk / kAdamSub)), 256, 0, ctx->stream>>>(
-        o->d_tensors, it->second.first, n_chunks, o->d_hp,
-                                              o->d_steps, al.first, al.second, o->cfg.kind,
-                                              o->cfg.amsgrad, o->d_ticket);
+        o->d_tensors, it->second.first, n_chunks, o->d_hp, o->d_steps, o->d_bc, al.first, al.second,
+        o->cfg.kind, o->cfg.amsgrad, o->d_ticket);
   }
   TX_LAUNCHED(ctx, "optimizer step");
   return TX_OK;
@@ -1545,6 +1614,7 @@ extern "C" int tx_optim_set_steps(tx_optim *o, const int64_t *h) {
   if (!o || !h) return TX_ERR_INVALID;
   TX_CUDA(o->ctx, cudaMemcpyAsync(o->d_steps, h, o->n * sizeof(int64_t), cudaMemcpyHostToDevice,
                                   o->ctx->stream));
+  TX_TRY(refresh_bias_corrections(o));
   TX_CUDA(o->ctx, cudaStreamSynchronize(o->ctx->stream));
   return TX_OK;
 }
@@ -1562,6 +1632,7 @@ extern "C" int tx_optim_destroy(tx_optim *o) {
   cudaFree(o->d_steps);
   cudaFree(o->d_hp);
   cudaFree(o->d_ticket);
+  cudaFree(o->d_bc);
   delete o;
   return TX_OK;
 }
