@@ -242,6 +242,7 @@ extern "C" {
     pub fn tx_exec_node_count(exec: *mut tx_exec, kernels: *mut i64, total: *mut i64) -> c_int;
     pub fn tx_gemm(ctx: *mut tx_ctx, desc: *const tx_gemm_desc) -> c_int;
     pub fn tx_round_tf32(ctx: *mut tx_ctx, d_src: *const f32, d_dst: *mut f32, n: i64) -> c_int;
+    pub fn tx_split_tf32(ctx: *mut tx_ctx, d_src: *const f32, d_hi: *mut f32, d_lo: *mut f32, n: i64) -> c_int;
     pub fn tx_unary(ctx: *mut tx_ctx, op: c_int, d_x: *const f32, d_y: *mut f32, n: i64, a: f32, b: f32) -> c_int;
     pub fn tx_unary_bwd(ctx: *mut tx_ctx, op: c_int, d_src: *const f32, d_dy: *const f32, d_dx: *mut f32, n: i64, a: f32, b: f32, accumulate: c_int) -> c_int;
     pub fn tx_binary(ctx: *mut tx_ctx, op: c_int, d_a: *const f32, a_strides: *const i64, d_b: *const f32, b_strides: *const i64, d_out: *mut f32, out_shape: *const i64, ndim: c_int) -> c_int;
