@@ -314,11 +314,10 @@ def main() -> None:
         def train_step(obs, actions, old_logp, adv, ret):
             opt.zero_grad()
             out = model(obs)
-            policy = Categorical(logits=out["logits"])
-            ratio = (policy.log_prob(actions) - old_logp).exp()
-            policy_loss = -tx.minimum(ratio * adv, ratio.clamp(0.8, 1.2) * adv).mean()
-            value_loss = tx.nn.functional.mse_loss(out["value"].squeeze(1), ret)
-            loss = policy_loss + value_loss * 0.5 - policy.entropy().mean() * 0.01
+            # the clipped surrogate + 0.5 value MSE - 0.01 entropy, as one fused
+            # kernel pair (the same objective the reference composes from
+            # Categorical, minimum, clamp and mse_loss)
+            loss = tx.nn.functional.ppo_loss(out["logits"], out["value"], actions, old_logp, adv, ret)
             loss.backward()
             opt.step()
             return loss

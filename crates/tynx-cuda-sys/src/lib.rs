@@ -265,6 +265,8 @@ extern "C" {
     pub fn tx_maxpool2d_bwd(ctx: *mut tx_ctx, d_dy: *const f32, d_argmax: *const i32, d_dx: *mut f32, planes: i64, H: i64, W: i64, geom: *const i64, accumulate: c_int) -> c_int;
     pub fn tx_attention_fwd(ctx: *mut tx_ctx, d_q: *const f32, d_k: *const f32, d_v: *const f32, ld_in: i64, d_out: *mut f32, ld_out: i64, batch: i64, seq: i64, heads: i64, head_dim: i64, scale: f32, flags: c_int) -> c_int;
     pub fn tx_attention_bwd(ctx: *mut tx_ctx, d_q: *const f32, d_k: *const f32, d_v: *const f32, ld_in: i64, d_dout: *const f32, ld_dout: i64, d_dq: *mut f32, d_dk: *mut f32, d_dv: *mut f32, ld_grad: i64, batch: i64, seq: i64, heads: i64, head_dim: i64, scale: f32, flags: c_int) -> c_int;
+    pub fn tx_ppo_loss_fwd(ctx: *mut tx_ctx, d_logits: *const f32, rows: i64, cols: i64, d_values: *const f32, d_actions: *const i64, d_old_log_prob: *const f32, d_advantages: *const f32, d_returns: *const f32, clip: f32, value_coef: f32, entropy_coef: f32, d_loss: *mut f32) -> c_int;
+    pub fn tx_ppo_loss_bwd(ctx: *mut tx_ctx, d_logits: *const f32, rows: i64, cols: i64, d_values: *const f32, d_actions: *const i64, d_old_log_prob: *const f32, d_advantages: *const f32, d_returns: *const f32, clip: f32, value_coef: f32, entropy_coef: f32, d_dloss: *const f32, d_dlogits: *mut f32, d_dvalues: *mut f32, accumulate_logits: c_int, accumulate_values: c_int) -> c_int;
     pub fn tx_gather_rows(ctx: *mut tx_ctx, d_table: *const f32, rows: i64, width: i64, d_idx: *const i64, n_idx: i64, d_out: *mut f32) -> c_int;
     pub fn tx_scatter_add_rows(ctx: *mut tx_ctx, d_table: *mut f32, rows: i64, width: i64, d_idx: *const i64, n_idx: i64, d_src: *const f32) -> c_int;
     pub fn tx_take_last(ctx: *mut tx_ctx, d_x: *const f32, d_idx: *const i64, d_out: *mut f32, rows: i64, cols: i64) -> c_int;

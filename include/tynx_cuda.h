@@ -345,6 +345,27 @@ int tx_attention_bwd(tx_ctx *ctx, const float *d_q, const float *d_k, const floa
                      int64_t ld_grad, int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
                      float scale, int flags);
 
+/* Clipped-surrogate PPO objective over [rows, cols] policy logits (cols <=
+ * 64), per-row value estimates, int64 actions, behaviour log-probabilities,
+ * advantages and returns:
+ *   loss = -mean(min(r A, clamp(r, 1 - clip, 1 + clip) A))
+ *          + value_coef * mean((value - ret)^2) - entropy_coef * mean(entropy)
+ * with r = exp(log_softmax(logits)[action] - old_log_prob) and the entropy of
+ * the row's categorical distribution.  The backward writes d logits and (when
+ * d_dvalues is non-null) d values, scaled by the upstream gradient *d_dloss.
+ * Out-of-range actions raise the device index flag.
+ * replaces: the composed objective of crates/tynx-python/tests/test_ppo.py:53-64
+ * (Categorical, crates/tynx-python/python/tynx/distributions.py:47-104; mse_loss,
+ * crates/tynx-python/python/tynx/nn/functional.py:126-130), about twenty taped ops. */
+int tx_ppo_loss_fwd(tx_ctx *ctx, const float *d_logits, int64_t rows, int64_t cols, const float *d_values,
+                    const int64_t *d_actions, const float *d_old_log_prob, const float *d_advantages,
+                    const float *d_returns, float clip, float value_coef, float entropy_coef, float *d_loss);
+int tx_ppo_loss_bwd(tx_ctx *ctx, const float *d_logits, int64_t rows, int64_t cols, const float *d_values,
+                    const int64_t *d_actions, const float *d_old_log_prob, const float *d_advantages,
+                    const float *d_returns, float clip, float value_coef, float entropy_coef,
+                    const float *d_dloss, float *d_dlogits, float *d_dvalues, int accumulate_logits,
+                    int accumulate_values);
+
 /* Row gather out[i, :] = table[idx[i], :] (negative indices wrap once) and its
  * backward scatter-add.  replaces: gather_values (crates/tynx/src/interpreter/gather.rs:18-58),
  * DynTensor::select (tensor.rs:1450) and Burn select_assign. */

@@ -161,6 +161,9 @@ SIGNATURES = {
     "tx_attention_fwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _f, _i32],
     "tx_attention_bwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                          _f, _i32],
+    "tx_ppo_loss_fwd": [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _f, _f, _f, _vp],
+    "tx_ppo_loss_bwd": [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _f, _f, _f, _vp, _vp, _vp, _i32,
+                        _i32],
     "tx_gather_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_scatter_add_rows": [_vp, _vp, _i64, _i64, _vp, _i64, _vp],
     "tx_take_last": [_vp, _vp, _vp, _vp, _i64, _i64],
