@@ -28,6 +28,7 @@
 
 #include "common.h"
 #include "epilogue.cuh"
+#include "gemm_tc.cuh"
 
 extern "C" int tx_attention_fwd(tx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld_in,
                                 float *out, int64_t ld_out, int64_t batch, int64_t seq, int64_t heads,
@@ -333,6 +334,95 @@ __global__ void k_weight_from_khwc(const float *__restrict__ dwk, float *__restr
   }
 }
 
+// wt[(t * C + c) * OC + o] = w[o][c][kh][kw], t = kh * KW + kw (optionally TF32-rounded):
+// the data-gradient product's weight rows, one [C][OC] block per tap
+__global__ void k_weight_to_tco(const float *__restrict__ w, float *__restrict__ wt, int OC, int C, int KH, int KW,
+                                int round_tf32) {
+  const int64_t n = (int64_t)OC * C * KH * KW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int o = (int)(i % OC);
+    const int64_t r = i / OC;
+    const int c = (int)(r % C), t = (int)(r / C);
+    const int kh = t / KW, kw = t - kh * KW;
+    const float v = w[(((int64_t)o * C + c) * KH + kh) * KW + kw];
+    wt[i] = round_tf32 ? tx_epi::round_tf32(v) : v;
+  }
+}
+
+// ---- implicit-GEMM convolution ---------------------------------------------------------
+// The tcgen05 product reads its activation operand straight from the
+// channels-last tensor with shifted TMA boxes (tx_tc::GatherOp), so no im2col
+// columns are written or read:
+//   forward   Y[p][o]  = sum_(t,c) X[pixel(p) + tap(t)][c] Wk[o][(t, c)]   A gathered, 128 pixels per tile
+//   wgrad     dWk[o][(t,c)] = sum_p dY[p][o] X[pixel(p) + tap(t)][c]         B gathered, 32 pixels per sub-tile
+//   dgrad     for each phase (ph, pw) of the stride, the input pixels
+//             (sh a + ph, sw b + pw) take the taps with (ph + pt - kh dh) % sh == 0:
+//             dX[(a, b)][c] = sum_(t,o) dY[(a + dh_t, b + dw_t)][o] W[o][c][t]
+//             with A gathered from dY (stride 1) and the output written
+//             through a strided view of dX.
+// A tile of R pixels is one box when it covers whole rows of one image (or
+// whole images): R pixels of an OH x OW grid as {bw, bh, bn}.
+bool pixel_box(int64_t OH, int64_t OW, int R, uint32_t &bw, uint32_t &bh, uint32_t &bn) {
+  if (OH <= 0 || OW <= 0) return false;
+  if (OW % R == 0) {
+    bw = (uint32_t)R; bh = 1; bn = 1;
+    return true;
+  }
+  if (R % OW != 0) return false;
+  if (OH * OW >= R) {
+    if (OH % (R / OW)) return false;
+    bw = (uint32_t)OW; bh = (uint32_t)(R / OW); bn = 1;
+    return true;
+  }
+  if (R % (OH * OW)) return false;
+  bw = (uint32_t)OW; bh = (uint32_t)OH; bn = (uint32_t)(R / (OH * OW));
+  return true;
+}
+
+// the tcgen05 operand mode for the context's math (as gemm_dispatch picks it)
+int tc_mode(tx_ctx *ctx, tx_gemm_desc &q) {
+  if (ctx->math != TX_MATH_TF32) q.flags = 0;
+  if (ctx->math == TX_MATH_3XTF32) return 2;
+  if (ctx->math == TX_MATH_TF32_TRUNC) return 0;
+  if (q.flags & TX_GEMM_EXACT) {
+    q.flags &= ~(TX_GEMM_A_TF32 | TX_GEMM_B_TF32);
+    return 2;
+  }
+  return 1;
+}
+
+// the tap offsets of a forward / weight-gradient gather (every tap, in (kh, kw) order)
+bool conv_gather_fwd(const ConvGeom &g, int R, tx_tc::ConvGemm &cv) {
+  if (g.C % 32 || g.KH * g.KW > tx_tc::kGatherTaps || g.sh > 8 || g.sw > 8) return false;
+  uint32_t bw, bh, bn;
+  if (!pixel_box(g.OH, g.OW, R, bw, bh, bn)) return false;
+  if (bw * g.sw > 256 || bh * g.sh > 256 || bn > 256) return false;
+  memset(&cv, 0, sizeof cv);
+  tx_tc::GatherOp &op = cv.op;
+  op.cblocks = g.C / 32;
+  op.ntaps = g.KH * g.KW;
+  op.ohw = g.OH * g.OW;
+  op.ow = g.OW;
+  op.sw = g.sw;
+  op.sh = g.sh;
+  for (int kh = 0; kh < g.KH; ++kh)
+    for (int kw = 0; kw < g.KW; ++kw) {
+      const int t = kh * g.KW + kw;
+      const int ox = kw * g.dw - g.pl, oy = kh * g.dh - g.pt;
+      if (ox < -32768 || ox > 32767 || oy < -32768 || oy > 32767) return false;
+      op.offx[t] = (int16_t)ox;
+      op.offy[t] = (int16_t)oy;
+      op.wtap[t] = (int16_t)t;
+    }
+  cv.box[0] = 32;
+  cv.box[1] = bw * g.sw;
+  cv.box[2] = bh * g.sh;
+  cv.box[3] = bn;
+  cv.estr_w = (uint32_t)g.sw;
+  cv.estr_h = (uint32_t)g.sh;
+  return true;
+}
+
 ConvGeom conv_geom(const Shape &x, const Shape &w, const Shape &y, const tx_node_desc &d) {
   ConvGeom g;
   g.N = (int)x[0]; g.C = (int)x[1]; g.H = (int)x[2]; g.W = (int)x[3];
@@ -495,6 +585,9 @@ struct tx_record {
   bool shadow = false;     // parameters read by GEMMs come from flat_tf32
   bool tracking = false;
   std::vector<uint8_t> attn_fused;  // per tx_graph::attn block: ran as the fused kernels
+  std::vector<uint8_t> conv_implicit;  // per node: the convolution ran as an implicit GEMM
+                                       // (extra holds its channels-last input, or null when
+                                       // the input value is channels-last itself)
 };
 
 namespace {
@@ -1354,6 +1447,60 @@ struct Fwd {
     return gemm_dispatch(ctx, q);
   }
 
+  // The forward as an implicit GEMM: A gathered from the channels-last input
+  // (kept for the weight gradient), B the (kh, kw, c)-ordered weights.  In
+  // TF32 mode the kernel rounds the gathered tiles in shared memory, as the
+  // explicit columns were rounded.  TX_ERR_UNSUPPORTED: the geometry does not
+  // fit the boxes, and the explicit path runs.
+  int conv_forward_implicit(int ni, const ConvGeom &cg, bool ex, bool tf32) {
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    tx_tc::ConvGemm cv;
+    if (!conv_gather_fwd(cg, tx_tc::TC_BM, cv)) return TX_ERR_UNSUPPORTED;
+    const int yv = n.fused_act ? n.fused_out : d.out[0];
+    const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = S(d.in[1])[0];
+    const int64_t K = (int64_t)cg.KH * cg.KW * cg.C;
+    Scratch wk(ctx, (size_t)OC * K * 4), tmp(ctx, n.nhwc_out ? 0 : (size_t)M * OC * 4);
+    if (!wk.ptr || (!n.nhwc_out && !tmp.ptr)) return TX_ERR_OOM;
+    float *xh = nullptr;
+    const float *xin = F(d.in[0]);
+    if (!n.nhwc_in) {
+      xh = (float *)tx_alloc_raw(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4);
+      if (!xh) return TX_ERR_OOM;
+      r->extra[ni] = xh;  // the weight gradient gathers from it
+      TX_TRY(transpose_b(ctx, F(d.in[0]), xh, cg.N, cg.C, (int64_t)cg.H * cg.W));
+      xin = xh;
+    }
+    cv.op.a = 1;
+    cv.src = {xin, cg.N, cg.H, cg.W, cg.C};
+    k_weight_to_khwc<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC, cg.C,
+                                                                    cg.KH, cg.KW, (int)K, tf32);
+    TX_LAUNCHED(ctx, "k_weight_to_khwc");
+    tx_gemm_desc q;
+    memset(&q, 0, sizeof q);
+    q.M = M; q.N = OC; q.K = K;
+    q.A = xin; q.lda = K; q.trans_a = 0;
+    q.B = wk.as<float>(); q.ldb = K; q.trans_b = 1;
+    q.C = n.nhwc_out ? F(yv) : tmp.as<float>(); q.ldc = OC; q.alpha = 1.f; q.batch = 1;
+    if (d.n_in > 2 && d.in[2] >= 0) {
+      q.bias = F(d.in[2]);
+      q.bias_scale = 1.f;
+    }
+    q.act = n.fused_act;
+    q.flags = tf32 ? TX_GEMM_B_TF32 : ex ? TX_GEMM_EXACT : 0;
+    const int mode = tc_mode(ctx, q);
+    const int rc = gemm_conv_tc(ctx, q, mode, cv);
+    if (rc == TX_ERR_UNSUPPORTED) {
+      tx_free_raw(ctx, xh);
+      r->extra[ni] = nullptr;
+      return rc;
+    }
+    TX_TRY(rc);
+    r->conv_implicit[ni] = 1;
+    if (n.nhwc_out) return TX_OK;
+    return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);
+  }
+
   int conv_node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
@@ -1365,6 +1512,10 @@ struct Fwd {
     const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
     const bool ex = n.exact && ctx->math == TX_MATH_TF32;
     const bool tf32 = ctx->math == TX_MATH_TF32 && !ex;
+    if (ctx->math != TX_MATH_FP32) {
+      const int rc = conv_forward_implicit(ni, cg, ex, tf32);
+      if (rc != TX_ERR_UNSUPPORTED) return rc;
+    }
     // channels-last input, (kh, kw, c) columns, weights permuted to match;
     // in TF32 mode both operands are stored rounded, so the GEMM reads them as is
     Scratch xh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
@@ -1586,6 +1737,7 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
   r->extra2.assign(g->nodes.size(), {});
   r->tf32.assign(nv, false);
   r->attn_fused.assign(g->attn.size(), 0);
+  r->conv_implicit.assign(g->nodes.size(), 0);
   if (ctx->math == TX_MATH_TF32 && g->flat_len > 0) {
     // the contractions of this forward (and of its backward) read parameters
     // from a TF32-rounded copy, refreshed here so that it always matches the
@@ -1953,6 +2105,111 @@ struct Bwd {
     }
   }
 
+  // dX as one implicit GEMM per phase of the stride (see the implicit-GEMM
+  // note above the kernels): A gathered from the channels-last dY with the
+  // phase's tap shifts, B the taps' [C][OC] weight blocks, the output written
+  // through a view of dX with the phase's origin and strides (and act' of a
+  // channels-last producer applied there, as col2im applied it).
+  // TX_ERR_UNSUPPORTED with `launched` false: nothing ran, and the columns path runs.
+  int conv_dgrad_implicit(int ni, const ConvGeom &cg, const float *dz, float *t, int acc, bool &launched) {
+    launched = false;
+    GNode &n = g->nodes[ni];
+    const tx_node_desc &d = n.d;
+    const int64_t OC = S(d.in[1])[0];
+    if (OC % 32 || cg.C % 4 || cg.H % cg.sh || cg.W % cg.sw || cg.KH * cg.KW > tx_tc::kGatherTaps) return TX_ERR_UNSUPPORTED;
+    const int Hp = cg.H / cg.sh, Wp = cg.W / cg.sw;
+    uint32_t bw, bh, bn;
+    if (!pixel_box(Hp, Wp, tx_tc::TC_BM, bw, bh, bn) || bw > 256 || bh > 256 || bn > 256) return TX_ERR_UNSUPPORTED;
+    if (!(Wp % 32 == 0 || 32 % Wp == 0)) return TX_ERR_UNSUPPORTED;
+    // every phase must take at least one tap (else part of dX has no product)
+    auto phase_taps = [&](int ph, int pw, tx_tc::GatherOp &op) {
+      int nt = 0;
+      for (int kh = 0; kh < cg.KH; ++kh) {
+        const int a = ph + cg.pt - kh * cg.dh;
+        if (((a % cg.sh) + cg.sh) % cg.sh) continue;
+        for (int kw = 0; kw < cg.KW; ++kw) {
+          const int b = pw + cg.pl - kw * cg.dw;
+          if (((b % cg.sw) + cg.sw) % cg.sw) continue;
+          op.offx[nt] = (int16_t)(b / cg.sw);  // exact quotients (b, a divisible)
+          op.offy[nt] = (int16_t)(a / cg.sh);
+          op.wtap[nt] = (int16_t)(kh * cg.KW + kw);
+          ++nt;
+        }
+      }
+      return nt;
+    };
+    for (int ph = 0; ph < cg.sh; ++ph)
+      for (int pw = 0; pw < cg.sw; ++pw) {
+        tx_tc::GatherOp probe;
+        if (phase_taps(ph, pw, probe) == 0) return TX_ERR_UNSUPPORTED;
+      }
+    // the producer's act' against its channels-last output, when nothing accumulates
+    const int xv = d.in[0];
+    const GValue &xg = g->values[xv];
+    int pc = xg.producer;
+    if (pc >= 0 && g->nodes[pc].fused_into >= 0) pc = g->nodes[pc].fused_into;
+    const GNode *pn = pc >= 0 ? &g->nodes[pc] : nullptr;
+    const bool fuse = n.nhwc_in && !acc && pn && pn->d.op == TX_OP_CONV && pn->nhwc_out && pn->fused_act &&
+                      (pn->fused_act == TX_ACT_RELU || pn->fused_act == TX_ACT_TANH) && pn->fused_out == xv;
+    const bool tf32 = ctx->math == TX_MATH_TF32;
+    const int64_t taps = (int64_t)cg.KH * cg.KW;
+    Scratch wt(ctx, (size_t)taps * cg.C * OC * 4),
+        dxh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4);
+    if (!wt.ptr || (!n.nhwc_in && !dxh.ptr)) return TX_ERR_OOM;
+    k_weight_to_tco<<<grid_for(taps * cg.C * OC, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wt.as<float>(), (int)OC,
+                                                                             cg.C, cg.KH, cg.KW, tf32);
+    TX_LAUNCHED(ctx, "k_weight_to_tco");
+    launched = true;  // from here a refusal is an error (part of dX may be written)
+    float *dst = n.nhwc_in ? t : dxh.as<float>();
+    for (int ph = 0; ph < cg.sh; ++ph)
+      for (int pw = 0; pw < cg.sw; ++pw) {
+        tx_tc::ConvGemm cv;
+        memset(&cv, 0, sizeof cv);
+        tx_tc::GatherOp &op = cv.op;
+        op.ntaps = phase_taps(ph, pw, op);
+        op.a = 1;
+        op.b = 2;
+        op.cblocks = (int)(OC / 32);
+        op.ohw = Hp * Wp;
+        op.ow = Wp;
+        op.sw = 1;
+        op.sh = 1;
+        op.brows = cg.C;
+        op.wsplit = Wp;
+        cv.src = {dz, cg.N, cg.OH, cg.OW, OC};
+        cv.box[0] = 32; cv.box[1] = bw; cv.box[2] = bh; cv.box[3] = bn;
+        cv.estr_w = cv.estr_h = 1;
+        cv.b_inner = OC;
+        cv.b_rows = taps * cg.C;
+        cv.out_rows = (int64_t)cg.N * Hp;
+        cv.out_sw = (int64_t)cg.sw * cg.C;
+        cv.out_sr = (int64_t)cg.sh * cg.W * cg.C;
+        const int64_t origin = ((int64_t)ph * cg.W + pw) * cg.C;
+        tx_gemm_desc q;
+        memset(&q, 0, sizeof q);
+        q.M = (int64_t)cg.N * Hp * Wp; q.N = cg.C; q.K = op.ntaps * OC;
+        q.A = dz; q.lda = OC; q.trans_a = 0;
+        q.B = wt.as<float>(); q.ldb = OC; q.trans_b = 1;
+        q.C = dst + origin; q.ldc = cg.C; q.alpha = 1.f; q.batch = 1;
+        if (n.nhwc_in && acc) q.beta = 1.f;
+        if (fuse) {
+          q.dact = pn->fused_act;
+          q.dact_src = F(xv) + origin;
+          q.ld_dact = cg.C;
+        }
+        q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+        const int mode = tc_mode(ctx, q);
+        const int rc = gemm_conv_tc(ctx, q, mode, cv);
+        if (rc == TX_ERR_UNSUPPORTED) return tx_fail(ctx, rc, "implicit data gradient: the product was refused");
+        TX_TRY(rc);
+      }
+    if (fuse) grad_preact[xv] = true;
+    if (!n.nhwc_in)
+      return transpose_b(ctx, dxh.as<float>(), t, cg.N, (int64_t)cg.H * cg.W, cg.C, nullptr, nullptr, TX_ACT_NONE,
+                         acc);
+    return TX_OK;
+  }
+
   int conv_backward(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
@@ -1995,10 +2252,35 @@ struct Bwd {
       tx_gemm_desc q; memset(&q, 0, sizeof q);
       q.M = OC; q.N = cg.ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
       q.A = dz; q.lda = OC; q.trans_a = 1;
-      q.B = (const float *)r->extra[ni]; q.ldb = cg.ldk; q.trans_b = 0;
       q.C = dwk.as<float>(); q.ldc = cg.ldk;
-      q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
-      TX_TRY(gemm_dispatch(ctx, q));
+      if (r->conv_implicit[ni]) {
+        // B gathered from the channels-last input, 32 pixels per sub-tile;
+        // without a fitting box the columns are built here after all
+        const float *xin = r->extra[ni] ? (const float *)r->extra[ni] : F(d.in[0]);
+        tx_tc::ConvGemm cv;
+        int rc = TX_ERR_UNSUPPORTED;
+        q.B = xin; q.ldb = cg.ldk; q.trans_b = 0;
+        if (conv_gather_fwd(cg, 32, cv)) {
+          cv.op.b = 1;
+          cv.src = {xin, cg.N, cg.H, cg.W, cg.C};
+          tx_gemm_desc e = q;
+          const int mode = tc_mode(ctx, e);
+          rc = gemm_conv_tc(ctx, e, mode, cv);
+        }
+        Scratch cols(ctx, rc == TX_ERR_UNSUPPORTED ? (size_t)M * cg.ldk * 4 : 0);
+        if (rc == TX_ERR_UNSUPPORTED) {
+          if (!cols.ptr) return TX_ERR_OOM;
+          TX_TRY(im2col_nhwc(ctx, xin, cols.as<float>(), cg, tf32));
+          q.B = cols.as<float>();
+          q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+          rc = gemm_dispatch(ctx, q);
+        }
+        TX_TRY(rc);
+      } else {
+        q.B = (const float *)r->extra[ni]; q.ldb = cg.ldk; q.trans_b = 0;
+        q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+        TX_TRY(gemm_dispatch(ctx, q));
+      }
       k_weight_from_khwc<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(dwk.as<float>(), t, (int)OC, cg.C,
                                                                         cg.KH, cg.KW, cg.ldk, acc);
       TX_LAUNCHED(ctx, "k_weight_from_khwc");
@@ -2007,6 +2289,15 @@ struct Bwd {
     if (needs[d.in[0]]) {  // dcols[M, ldk] = dY W_khwc ; dx = col2im(dcols) -> NCHW
       float *t; int acc;
       TX_TRY(target(d.in[0], &t, &acc));
+      if (ctx->math != TX_MATH_FP32) {
+        bool launched = false;
+        const int rc = conv_dgrad_implicit(ni, cg, dz, t, acc, launched);
+        if (rc != TX_ERR_UNSUPPORTED || launched) {
+          TX_TRY(rc);
+          wrote(d.in[0]);
+          return TX_OK;
+        }
+      }
       Scratch wk(ctx, (size_t)OC * cg.ldk * 4), dcols(ctx, (size_t)M * cg.ldk * 4),
           dxh(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4);
       if (!wk.ptr || !dcols.ptr || !dxh.ptr) return TX_ERR_OOM;

@@ -55,6 +55,40 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// 4-D map over a channels-last [n][h][w][c] tensor (dims {c, w, h, n}) whose
+// boxes step estr_w / estr_h elements along w / h: the operand tiles of an
+// implicit-GEMM convolution.  Coordinates outside the tensor read zeros.
+bool make_map_4d(CUtensorMap *map, const ConvTensor &t, const uint32_t box[4], uint32_t estr_w, uint32_t estr_h,
+                 bool mn_major) {
+  if (!t.base || ((uintptr_t)t.base & 15) || (t.c & 3)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)t.c, (cuuint64_t)t.w, (cuuint64_t)t.h, (cuuint64_t)t.n};
+  cuuint64_t strides[3] = {(cuuint64_t)(t.c * 4), (cuuint64_t)(t.w * t.c * 4), (cuuint64_t)(t.h * t.w * t.c * 4)};
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1u, estr_w, estr_h, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)t.base, dims, strides, bx, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Output-side 3-D view [rows][wsplit][N] (element strides sw, sr) with
+// 32 x 32-element boxes: an output chunk of 32 GEMM rows is min(wsplit, 32)
+// view columns by 32 / that many view rows.
+bool make_view_map(CUtensorMap *map, const float *base, int64_t N, int wsplit, int64_t rows, int64_t sw,
+                   int64_t sr) {
+  if (!base || ((uintptr_t)base & 15) || (sw & 3) || (sr & 3)) return false;
+  const uint32_t bw = wsplit < 32 ? (uint32_t)wsplit : 32u;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)wsplit, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)(sw * 4), (cuuint64_t)(sr * 4)};
+  cuuint32_t box[3] = {32u, bw, 32u / bw};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // A row-major [batch][M][N] fp32 tensor TMA can tile: 16-byte aligned base,
 // row and batch strides that are 16-byte multiples.
 bool tma_tileable(const float *p, int64_t ld, int64_t batch, int64_t stride) {
@@ -121,8 +155,11 @@ Tiling pick_tiling(tx_ctx *ctx, int64_t M, int64_t N, int64_t K, int64_t batch, 
 
 }  // namespace
 
-// mode: 0 raw fp32 operands (hardware truncation), 1 TF32 round-to-nearest, 2 3xTF32
-int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) {
+namespace {
+
+// mode: 0 raw fp32 operands (hardware truncation), 1 TF32 round-to-nearest, 2 3xTF32.
+// cv (or null): gathered operands of an implicit-GEMM convolution.
+int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, const ConvGemm *cv) {
   tx_gemm_desc d = desc;
   if (d.K <= 0 || d.M <= 0 || d.N <= 0) return TX_ERR_UNSUPPORTED;
   const int64_t batch = d.batch > 1 ? d.batch : 1;
@@ -154,7 +191,13 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
   // each tile's epilogue overlaps the next tile's main loop.  Measured on the
   // transformer's 32768x1024x256 dgrad with GELU': 180 us in 1024 one-tile CTAs.
   int64_t pre_na = 0, pre_nb = 0;
-  if (mode == 1 && tiling.splits == 1 && tma_tileable(d.C, d.ldc, batch, d.stride_c) &&
+  if (cv) {
+    // the gathered operands are no dense matrices to pre-round; a view
+    // output takes neither split partials nor fused column sums
+    if (d.B_lo || (cv->op.wsplit && (fs || d.preact || batch > 1))) return TX_ERR_UNSUPPORTED;
+    if (cv->op.wsplit) tiling.splits = 1;
+  }
+  if (!cv && mode == 1 && tiling.splits == 1 && tma_tileable(d.C, d.ldc, batch, d.stride_c) &&
       (!d.dact || tma_tileable(d.dact_src, d.ld_dact, batch, d.stride_c)) &&
       (!d.preact || tma_tileable(d.preact, d.ld_preact, batch, d.stride_c))) {
     const int pbn = d.N > 128 ? 256 : d.N > 64 ? 128 : 64;
@@ -206,18 +249,25 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
   // four).  Measured main loops: 4096x1024x1024 dgrad 14.6 -> 12.4 us,
   // 1024x1024x4096 wgrad (4 splits) 17.6 -> 14.4 us; with a K-major B the pair
   // is slower (11.1 -> 12.2 us) and the single-CTA tile stays.
-  const bool pair = mode == 0 && bn == 256 && !persistent && d.M > TC_BM && !d.trans_b;
+  const bool pair = mode == 0 && bn == 256 && !persistent && d.M > TC_BM && !d.trans_b && !cv;
   bool ok;
-  if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
+  if (cv && cv->op.a)  // 128 pixels of the activation per tile: K-major, 128-byte swizzle
+    ok = make_map_4d(&m.a, cv->src, cv->box, cv->estr_w, cv->estr_h, false);
+  else if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
     ok = make_map(&m.a, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
   else  // A stored M x K (K-major): box 32(K) x 128(M)
     ok = make_map(&m.a, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
   if (!ok) return TX_ERR_UNSUPPORTED;
-  if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N), BN / 2 per CTA of a pair
+  if (cv && cv->op.b == 1)  // 32 pixels by 32 channels per sub-tile: MN-major
+    ok = make_map_4d(&m.b, cv->src, cv->box, cv->estr_w, cv->estr_h, true);
+  else if (cv && cv->op.b == 2)  // a tap's weight rows, K-major
+    ok = make_map(&m.b, d.B, cv->b_inner, cv->b_rows, d.ldb, 1, 0, bn, false);
+  else if (d.trans_b)  // B stored N x K (K-major): box 32(K) x BN(N), BN / 2 per CTA of a pair
     ok = make_map(&m.b, d.B, d.K, d.N, d.ldb, batch, d.stride_b, pair ? bn / 2 : bn, false);
   else  // B stored K x N (MN-major): box 32(N) x 32(K)
     ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
+  if (cv) m.g = cv->op;
   // split weights (B head + tail) run on the persistent kernel only; other
   // shapes report unsupported and the dispatcher runs two products instead
   if (d.B_lo) {
@@ -236,7 +286,15 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
   const int total_kb = (int)((d.K + TC_BK - 1) / TC_BK);
   int splits = tiling.splits;
   if (splits <= 1) {
-    make_epilogue_maps(m, d, batch);
+    if (cv && cv->op.wsplit) {
+      const int ws = cv->op.wsplit;
+      if (!make_view_map(&m.c, d.C, d.N, ws, cv->out_rows, cv->out_sw, cv->out_sr)) return TX_ERR_UNSUPPORTED;
+      if (d.dact && !make_view_map(&m.s, d.dact_src, d.N, ws, cv->out_rows, cv->out_sw, cv->out_sr))
+        return TX_ERR_UNSUPPORTED;
+      m.tma_epi = 1;
+    } else {
+      make_epilogue_maps(m, d, batch);
+    }
     if (fs) {
       // the TMA epilogue sums columns as it stores; otherwise C stays unrounded
       // and the caller sums it
@@ -281,4 +339,18 @@ int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs) 
                                           : launch_any(ctx, mode, bn, raw, m, splits, kb_per);
   TX_TRY(rc);
   return gemm_split_reduce(ctx, d, part.as<float>(), splits);
+}
+
+}  // namespace
+
+int gemm_tcgen05(tx_ctx *ctx, const tx_gemm_desc &d, int mode, FusedSum *fs) {
+  return tc_product(ctx, d, mode, fs, nullptr);
+}
+
+int gemm_conv_tc(tx_ctx *ctx, const tx_gemm_desc &d, int mode, const ConvGemm &cv) {
+  if (d.K <= 0 || d.M <= 0 || d.N <= 0) return TX_ERR_UNSUPPORTED;
+  if (cv.op.cblocks <= 0 || cv.op.ntaps <= 0 || cv.op.ntaps > kGatherTaps || cv.op.ohw <= 0 || cv.op.ow <= 0)
+    return TX_ERR_UNSUPPORTED;
+  if (!load_encode()) return TX_ERR_UNSUPPORTED;
+  return tc_product(ctx, d, mode, nullptr, &cv);
 }

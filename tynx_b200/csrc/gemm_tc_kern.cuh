@@ -147,6 +147,56 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint64_t *bar, int c,
+                                            int x, int y, int n) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(map), "r"(smem_u32(bar)), "r"(c), "r"(x), "r"(y), "r"(n)
+      : "memory");
+}
+
+// The box of the pixels from p of an implicit-GEMM operand (GatherOp), tap t,
+// channel block cb.  Boxes that start outside the tensor read zeros there: the
+// convolution's padding.
+__device__ __forceinline__ void gather_box(uint32_t dst, const CUtensorMap *map, uint64_t *bar,
+                                           const tx_tc::GatherOp &g, int64_t p, int t, int cb) {
+  const int64_t n = p / g.ohw;
+  const int r = (int)(p - n * g.ohw);
+  const int oh = r / g.ow, ow = r - oh * g.ow;
+  tma_load_4d(dst, map, bar, cb * 32, ow * g.sw + g.offx[t], oh * g.sh + g.offy[t], (int)n);
+}
+
+// Bytes of B one k-block brings: a gathered weight-gradient operand has no
+// sub-tile past the last column group (those columns are never stored).
+template <int BN>
+__device__ __forceinline__ uint32_t gather_b_bytes(const tx_tc::GatherOp &g, int n0) {
+  if (g.b != 1) return BN * TC_BK * 4;
+  int groups = g.ntaps * g.cblocks - n0 / 32;
+  groups = groups < 0 ? 0 : groups > BN / 32 ? BN / 32 : groups;
+  return (uint32_t)groups * 4096u;
+}
+
+// The operand loads of global k-block kg of the tile at (m0, n0) for gathered
+// operands (the dense ones are the caller's).
+template <int BN>
+__device__ __forceinline__ void gather_loads(const tx_tc::GatherOp &g, const CUtensorMap *mapA,
+                                             const CUtensorMap *mapB, uint64_t *bar, uint32_t a_dst,
+                                             uint32_t b_dst, int m0, int n0, int kg) {
+  if (g.a) gather_box(a_dst, mapA, bar, g, m0, kg / g.cblocks, kg % g.cblocks);
+  if (g.b == 1) {
+    const int groups = g.ntaps * g.cblocks;
+#pragma unroll 1
+    for (int j = 0; j < BN / 32; ++j) {
+      const int grp = n0 / 32 + j;
+      if (grp < groups) gather_box(b_dst + j * 4096, mapB, bar, g, (int64_t)kg * TC_BK, grp / g.cblocks, grp % g.cblocks);
+    }
+  } else if (g.b == 2) {
+    const int t = kg / g.cblocks;
+    tma_load_3d(b_dst, mapB, bar, (kg % g.cblocks) * 32, g.wtap[t] * g.brows + n0, 0);
+  }
+}
+
 // CTA-pair load: the copy lands in this CTA's shared memory and completes
 // its bytes on the barrier at `bar_cluster` (a shared::cluster address, the
 // leader CTA's barrier for both CTAs of the pair).
@@ -461,15 +511,28 @@ struct EpiWarp {
   const CUtensorMap *map_c, *map_s, *map_p;
   uint32_t issued, consumed, seq;
   bool need_s, need_c, need_p;
+  int wsplit;  // > 0: output row y sits at (y % wsplit, y / wsplit) of 3-D views (GatherOp)
 
+  // the map coordinates of output row y, batch z
+  __device__ __forceinline__ void rows(int y, int z, int &y2, int &z2) const {
+    if (wsplit > 0) {
+      y2 = y % wsplit;
+      z2 = y / wsplit;
+    } else {
+      y2 = y;
+      z2 = z;
+    }
+  }
   // act' / C tiles of the chunk at column x into the next ring slot
   __device__ __forceinline__ void issue(int x, int y, int z, int lane) {
     const int slot = (int)(issued % NS);
     if (lane == 0) {
       uint64_t *bar = &bars[slot];
+      int y2, z2;
+      rows(y, z, y2, z2);
       mbar_expect_tx(bar, (need_s ? 4096u : 0u) + (need_c ? 4096u : 0u));
-      if (need_s) tma_load_3d(smem_u32(s_t + slot * 4096), map_s, bar, x, y, z);
-      if (need_c) tma_load_3d(smem_u32(c_t + slot * 4096), map_c, bar, x, y, z);
+      if (need_s) tma_load_3d(smem_u32(s_t + slot * 4096), map_s, bar, x, y2, z2);
+      if (need_c) tma_load_3d(smem_u32(c_t + slot * 4096), map_c, bar, x, y2, z2);
     }
     ++issued;
   }
@@ -613,8 +676,10 @@ __device__ __forceinline__ bool epi_tile(EpiWarp<NS> &e, const tx_gemm_desc &d, 
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
     __syncwarp();
     if (lane == 0) {
-      tma_store_3d(e.map_c, smem_u32(e.out_t + oslot * 4096), n0 + 32 * c, row_tile, z);
-      if (pre_tile) tma_store_3d(e.map_p, smem_u32(pre_tile), n0 + 32 * c, row_tile, z);
+      int y2, z2;
+      e.rows(row_tile, z, y2, z2);
+      tma_store_3d(e.map_c, smem_u32(e.out_t + oslot * 4096), n0 + 32 * c, y2, z2);
+      if (pre_tile) tma_store_3d(e.map_p, smem_u32(pre_tile), n0 + 32 * c, y2, z2);
       bulk_commit();
     }
     __syncwarp();
@@ -671,7 +736,7 @@ __global__ void __launch_bounds__(320, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
               const __grid_constant__ CUtensorMap mapP, const tx_gemm_desc d, int *err, int kb_per_cta,
-              int tma_epi, int conv_mask, float *col_part) {
+              int tma_epi, int conv_mask, float *col_part, const __grid_constant__ tx_tc::GatherOp gop) {
   static_assert(!PAIR || MODE == 0, "operand conversion is per CTA");
   using Cfg = TcCfg<BN, MODE, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
@@ -766,14 +831,17 @@ __global__ void __launch_bounds__(320, 1)
           }
           continue;
         }
-        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-        if (A_MN) {
+        mbar_expect_tx(&full[s], A_BYTES + gather_b_bytes<BN>(gop, n0));
+        if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
+        if (gop.a) {
+        } else if (A_MN) {
 #pragma unroll
           for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
         } else {
           tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
         }
-        if (B_MN) {
+        if (gop.b) {
+        } else if (B_MN) {
 #pragma unroll
           for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
         } else {
@@ -897,6 +965,7 @@ __global__ void __launch_bounds__(320, 1)
         e.map_s = &mapS;
         e.map_p = &mapP;
         e.issued = e.consumed = e.seq = 0;
+        e.wsplit = gop.wsplit;
         const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16);
         epi_any<BN, NACC, 2, true>(e, d, tbase, used_acc, bias_w, nullptr, n0, m0 + quad * 32, bz, col_part,
                                    0, nullptr, abort_flag, err, 5, lane, wide ? half : 0, wide ? 2 : 1);
@@ -1023,7 +1092,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
                const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapB2,
-               const tx_gemm_desc d, int *err, PWork w) {
+               const tx_gemm_desc d, int *err, PWork w, const __grid_constant__ tx_tc::GatherOp gop) {
   using Cfg = PCfg<BN, BLO>;
   constexpr int NACC = Cfg::NACC;
   constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
@@ -1092,17 +1161,20 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const int s = (int)(cnt % (uint32_t)stages);
           const uint32_t round = cnt / (uint32_t)stages;
           if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort_flag, err, 11)) break;
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES * (BLO ? 2 : 1));
+          mbar_expect_tx(&full[s], A_BYTES + gather_b_bytes<BN>(gop, n0) + (BLO ? B_BYTES : 0));
           const uint32_t a_dst = smem_u32(smem + s * Cfg::STAGE);
           const uint32_t b_dst = a_dst + A_BYTES;
           const int k0 = (kb_first + kb) * TC_BK;
-          if (A_MN) {
+          if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
+          if (gop.a) {
+          } else if (A_MN) {
 #pragma unroll
             for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
           } else {
             tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
           }
-          if (B_MN) {
+          if (gop.b) {
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
           } else {
@@ -1180,6 +1252,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     e.map_s = &mapS;
     e.map_p = &mapP;
     e.issued = e.consumed = e.seq = 0;
+    e.wsplit = gop.wsplit;
     float *bias_row = bias_rows + ew * 32;
     int it = 0;
     bool alive = true;
@@ -1224,7 +1297,7 @@ int launch_tc(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, int 
   }
   dim3 grid((unsigned)((d.N + BN - 1) / BN), (unsigned)((d.M + TC_BM - 1) / TC_BM), (unsigned)z);
   kern<<<grid, 320, TcCfg<BN, MODE>::SMEM, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, d, ctx->d_err,
-                                                          kb_per_cta, m.tma_epi, m.conv_mask, m.col_part);
+                                                          kb_per_cta, m.tma_epi, m.conv_mask, m.col_part, m.g);
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
@@ -1260,7 +1333,7 @@ int launch_tc_pair(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   TX_CUDA(ctx, cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.c, m.s, m.p, d, ctx->d_err, kb_per_cta,
-                                  m.tma_epi, m.conv_mask, m.col_part));
+                                  m.tma_epi, m.conv_mask, m.col_part, m.g));
   TX_LAUNCHED(ctx, "k_gemm_tc");
   return TX_OK;
 }
@@ -1305,7 +1378,7 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
   }
   int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
   if (max_grid > 0 && grid > max_grid) grid = max_grid;
-  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, m.b2, d, ctx->d_err, w);
+  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, m.b2, d, ctx->d_err, w, m.g);
   TX_LAUNCHED(ctx, "k_gemm_tcp");
   return TX_OK;
 }
