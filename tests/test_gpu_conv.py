@@ -135,3 +135,38 @@ def test_conv_gradient_accumulates_across_backward_calls(tx):
     p = dict(model.named_parameters())
     for n, q in ref.named_parameters():
         assert _rel(p[n].grad.numpy(), q.grad) <= 2e-5, n
+
+
+def _single_conv(rng, x_shape, cout, k, group=1, **attrs):
+    from tynx_b200.onnx import proto
+
+    cin = x_shape[1]
+    w = (rng.standard_normal((cout, cin // group) + tuple(k)) / np.sqrt(cin // group * np.prod(k))).astype(np.float32)
+    b = (rng.standard_normal(cout) * 0.1).astype(np.float32)
+    nodes = [proto.encode_node("Conv", ["x", "w", "b"], ["y"], name="conv", kernel_shape=list(k), group=group,
+                               **attrs)]
+    inits = [proto.encode_tensor("w", w), proto.encode_tensor("b", b)]
+    return proto.encode_model(nodes, inits, [proto.encode_value_info("x", proto.FLOAT, list(x_shape))],
+                              [proto.encode_value_info("y", proto.FLOAT, None)], opset=13)
+
+
+# grouped and 1-D convolutions (the explicit columns, one product per group):
+# (input shape, out channels, kernel, group, attributes)
+VARIANTS = {
+    "grouped_2": ((3, 16, 12, 10), 32, (3, 3), 2, {"pads": [1, 1, 1, 1]}),
+    "grouped_4_strided": ((2, 32, 15, 15), 64, (3, 3), 4, {"pads": [1, 0, 1, 2], "strides": [2, 2]}),
+    "depthwise": ((4, 8, 9, 9), 8, (3, 3), 8, {"pads": [1, 1, 1, 1]}),
+    "depthwise_multiplier_2": ((2, 6, 11, 7), 12, (3, 2), 6, {"dilations": [2, 1]}),
+    "conv1d": ((4, 8, 40), 16, (5,), 1, {"pads": [2, 1], "strides": [2]}),
+    "conv1d_dilated_grouped": ((3, 12, 33), 24, (3,), 3, {"dilations": [3], "pads": [3, 3]}),
+}
+
+
+@pytest.mark.parametrize("math,tol", [("3xtf32", 2e-5), ("fp32", 2e-5), ("tf32", 3e-3)])
+@pytest.mark.parametrize("name", sorted(VARIANTS))
+def test_grouped_and_1d_conv_match_oracle(tx, name, math, tol):
+    shape, cout, k, group, attrs = VARIANTS[name]
+    rng = np.random.default_rng(100 + sorted(VARIANTS).index(name))
+    tx.set_math_mode(math)
+    x = rng.standard_normal(shape).astype(np.float32)
+    _check(tx, _single_conv(rng, shape, cout, k, group, **attrs), x, tol)

@@ -165,6 +165,9 @@ int transpose_b(tx_ctx *ctx, const float *in, float *out, int64_t B, int64_t R, 
 struct ConvGeom {
   int N, C, H, W, KH, KW, OH, OW, sh, sw, pt, pl, dh, dw;
   int ldk;  // columns per im2col row (K = KH*KW*C rounded up to 4, zero padded)
+  // grouped convolution: C is one group's channels; a pixel's channels-last
+  // row holds ctot channels and the group's start at coff
+  int groups = 1, ctot = 0, coff = 0;
 };
 
 // cols[m][(kh*KW + kw)*C + c] = xh[n][ih][iw][c] (0 outside the image and in
@@ -185,7 +188,7 @@ __global__ void k_im2col_nhwc(const float *__restrict__ xh, float *__restrict__ 
       const uint32_t ow = m % g.OW, t = m / g.OW, oh = t % g.OH, n = t / g.OH;
       const int ih = (int)oh * g.sh - g.pt + (int)kh * g.dh, iw = (int)ow * g.sw - g.pl + (int)kw * g.dw;
       if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
-        const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.C + c;
+        const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.ctot + g.coff + c;
         if (V == 4) {
           const float4 t4 = *reinterpret_cast<const float4 *>(p);
           v[0] = t4.x;
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(128) k_im2col_rows(const float *__restrict__ x
         for (int kw = 0; kw < g.KW; ++kw) {
           const int iw = (int)ow * g.sw - g.pl + kw * g.dw;
           const bool in = ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-          const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.C;
+          const float *p = xh + (((int64_t)n * g.H + ih) * g.W + iw) * g.ctot + g.coff;
           for (int c = 0; c < g.C; ++c, ++k) {
             const float v = in ? p[c] : 0.f;
             row[k] = round_tf32 ? tx_epi::round_tf32(v) : v;
@@ -254,8 +257,9 @@ __global__ void __launch_bounds__(128) k_im2col_rows(const float *__restrict__ x
   }
 }
 
-// dxh[n][ih][iw][c] = sum over the taps that read (ih, iw) of dcols[m][(kh*KW + kw)*C + c]
-// (gather form: each input element is written once, no atomics).
+// dxh[n][ih][iw][coff + c] = sum over the taps that read (ih, iw) of
+// dcols[m][(kh*KW + kw)*C + c] (gather form: each input element is written
+// once, no atomics).
 // S: the stride when both strides equal it (1 or 2: the tap tests become masks
 // and shifts instead of runtime divisions), 0 for any strides.
 // act_src (or null): multiply each sum by act'(act_src) at the same index
@@ -294,12 +298,13 @@ __global__ void k_col2im_nhwc(const float *__restrict__ dcols, float *__restrict
         }
       }
     }
+    const int64_t at = (int64_t)pix * g.ctot + g.coff + c;  // the group's channels of this pixel
     if (act_src) {
-      const float *a = act_src + (int64_t)u * V;
+      const float *a = act_src + at;
 #pragma unroll
       for (int j = 0; j < V; ++j) s[j] *= tx_epi::dact(act, a[j]);
     }
-    float *o = dxh + (int64_t)u * V;
+    float *o = dxh + at;
     if (V == 4)
       *reinterpret_cast<float4 *>(o) = make_float4(s[0], s[V > 1 ? 1 : 0], s[V > 2 ? 2 : 0], s[V > 3 ? 3 : 0]);
     else
@@ -423,19 +428,35 @@ bool conv_gather_fwd(const ConvGeom &g, int R, tx_tc::ConvGemm &cv) {
   return true;
 }
 
+// A 1-D convolution ([N][C][L] input, [OC][C][K] weights) is the 2-D one
+// over a unit height (the lowering writes unit height, stride and dilation
+// and zero vertical padding); the memory layouts coincide.
 ConvGeom conv_geom(const Shape &x, const Shape &w, const Shape &y, const tx_node_desc &d) {
   ConvGeom g;
-  g.N = (int)x[0]; g.C = (int)x[1]; g.H = (int)x[2]; g.W = (int)x[3];
-  g.KH = (int)w[2]; g.KW = (int)w[3]; g.OH = (int)y[2]; g.OW = (int)y[3];
+  const bool one = x.size() == 3;
+  g.N = (int)x[0]; g.C = (int)x[1]; g.H = one ? 1 : (int)x[2]; g.W = (int)x.back();
+  g.KH = one ? 1 : (int)w[2]; g.KW = (int)w.back(); g.OH = one ? 1 : (int)y[2]; g.OW = (int)y.back();
   g.sh = (int)d.ints[0]; g.sw = (int)d.ints[1]; g.pt = (int)d.ints[2]; g.pl = (int)d.ints[3];
   g.dh = (int)d.ints[6]; g.dw = (int)d.ints[7];
+  g.ldk = (g.KH * g.KW * g.C + 3) & ~3;
+  g.ctot = g.C;
+  return g;
+}
+
+// one group's geometry of a grouped convolution (C = that group's channels)
+ConvGeom conv_group(const ConvGeom &all, int groups, int gi) {
+  ConvGeom g = all;
+  g.groups = groups;
+  g.C = all.C / groups;
+  g.ctot = all.C;
+  g.coff = gi * g.C;
   g.ldk = (g.KH * g.KW * g.C + 3) & ~3;
   return g;
 }
 
 int im2col_nhwc(tx_ctx *ctx, const float *xh, float *cols, const ConvGeom &g, bool round_tf32) {
   const int64_t M = (int64_t)g.N * g.OH * g.OW;
-  const bool vec = g.C % 4 == 0;
+  const bool vec = g.C % 4 == 0 && g.ctot % 4 == 0 && g.coff % 4 == 0;
   if (!vec && g.ldk <= kIm2colRowsMaxLdk) {
     int64_t blocks = (M + 127) / 128;
     if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
@@ -455,7 +476,7 @@ int im2col_nhwc(tx_ctx *ctx, const float *xh, float *cols, const ConvGeom &g, bo
 
 int col2im_nhwc(tx_ctx *ctx, const float *dcols, float *dxh, const ConvGeom &g, const float *act_src = nullptr,
                 int act = TX_ACT_NONE) {
-  const bool vec = g.C % 4 == 0 && g.ldk % 4 == 0;
+  const bool vec = g.C % 4 == 0 && g.ldk % 4 == 0 && g.ctot % 4 == 0 && g.coff % 4 == 0;
   const int64_t units = (int64_t)g.N * g.H * g.W * g.C / (vec ? 4 : 1);
   if (units >= (int64_t(1) << 32)) return tx_fail(ctx, TX_ERR_UNSUPPORTED, "col2im too large");
   const int S = g.sh == g.sw && (g.sh == 1 || g.sh == 2) ? g.sh : 0;
@@ -709,14 +730,20 @@ int infer_node(tx_graph *g, const GNode &n, std::vector<Shape> &S) {
     }
     case TX_OP_CONV: {
       const Shape &x = in(0), &w = in(1);
-      if (x.size() != 4 || w.size() != 4) return fail(g, TX_ERR_UNSUPPORTED, "only 2-D Conv is supported on CUDA");
-      if (d.iattr[0] != 1) return fail(g, TX_ERR_UNSUPPORTED, "grouped Conv is not supported on CUDA");
-      if (x[1] != w[1]) return fail(g, TX_ERR_SHAPE, "Conv channel mismatch");
+      if (!((x.size() == 4 && w.size() == 4) || (x.size() == 3 && w.size() == 3)))
+        return fail(g, TX_ERR_UNSUPPORTED, "only 1-D and 2-D Conv are supported on CUDA");
+      const int64_t groups = d.iattr[0];
+      if (groups < 1 || x[1] != w[1] * groups || w[0] % groups)
+        return fail(g, TX_ERR_SHAPE, "Conv channel mismatch: input " + shape_str(x) + ", weight " + shape_str(w) +
+                                         ", " + std::to_string(groups) + " group(s)");
+      const bool one = x.size() == 3;
       int64_t sh = d.ints[0], sw = d.ints[1], pt = d.ints[2], pl = d.ints[3], pb = d.ints[4],
               pr = d.ints[5], dh = d.ints[6], dw = d.ints[7];
-      int64_t oh = (x[2] + pt + pb - dh * (w[2] - 1) - 1) / sh + 1;
-      int64_t ow = (x[3] + pl + pr - dw * (w[3] - 1) - 1) / sw + 1;
-      out = {x[0], w[0], oh, ow};
+      const int64_t H = one ? 1 : x[2], KH = one ? 1 : w[2];
+      int64_t oh = (H + pt + pb - dh * (KH - 1) - 1) / sh + 1;
+      int64_t ow = (x.back() + pl + pr - dw * (w.back() - 1) - 1) / sw + 1;
+      if (oh < 1 || ow < 1) return fail(g, TX_ERR_SHAPE, "Conv kernel larger than its padded input");
+      out = one ? Shape{x[0], w[0], ow} : Shape{x[0], w[0], oh, ow};
       return TX_OK;
     }
     case TX_OP_GATHER: {
@@ -1512,15 +1539,20 @@ struct Fwd {
     const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
     const bool ex = n.exact && ctx->math == TX_MATH_TF32;
     const bool tf32 = ctx->math == TX_MATH_TF32 && !ex;
-    if (ctx->math != TX_MATH_FP32) {
+    const int G = d.iattr[0];
+    if (ctx->math != TX_MATH_FP32 && G == 1) {
       const int rc = conv_forward_implicit(ni, cg, ex, tf32);
       if (rc != TX_ERR_UNSUPPORTED) return rc;
     }
-    // channels-last input, (kh, kw, c) columns, weights permuted to match;
-    // in TF32 mode both operands are stored rounded, so the GEMM reads them as is
-    Scratch xh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * cg.ldk * 4),
+    // channels-last input, (kh, kw, c) columns per group, weights permuted to
+    // match; in TF32 mode both operands are stored rounded, so the GEMM reads
+    // them as is.  A grouped convolution runs one product per group over its
+    // channel slice (columns [G][M][ldk_g], weights [OC][ldk_g]).
+    const ConvGeom g0 = conv_group(cg, G, 0);
+    const int64_t ldk = g0.ldk, OCg = OC / G;
+    Scratch xh(ctx, n.nhwc_in ? 0 : (size_t)cg.N * cg.H * cg.W * cg.C * 4), wk(ctx, (size_t)OC * ldk * 4),
         tmp(ctx, n.nhwc_out ? 0 : (size_t)M * OC * 4);
-    float *cols = (float *)tx_alloc_raw(ctx, (size_t)M * cg.ldk * 4);
+    float *cols = (float *)tx_alloc_raw(ctx, (size_t)G * M * ldk * 4);
     if ((!n.nhwc_in && !xh.ptr) || !wk.ptr || (!n.nhwc_out && !tmp.ptr) || !cols) {
       tx_free_raw(ctx, cols);
       return TX_ERR_OOM;
@@ -1531,23 +1563,25 @@ struct Fwd {
       TX_TRY(transpose_b(ctx, F(d.in[0]), xh.as<float>(), cg.N, cg.C, (int64_t)cg.H * cg.W));
       xin = xh.as<float>();
     }
-    TX_TRY(im2col_nhwc(ctx, xin, cols, cg, tf32));
-    k_weight_to_khwc<<<grid_for(OC * cg.ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
-                                                                         cg.C, cg.KH, cg.KW, cg.ldk, tf32);
+    for (int gi = 0; gi < G; ++gi) TX_TRY(im2col_nhwc(ctx, xin, cols + gi * M * ldk, conv_group(cg, G, gi), tf32));
+    k_weight_to_khwc<<<grid_for(OC * ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
+                                                                      g0.C, cg.KH, cg.KW, (int)ldk, tf32);
     TX_LAUNCHED(ctx, "k_weight_to_khwc");
-    tx_gemm_desc q;
-    memset(&q, 0, sizeof q);
-    q.M = M; q.N = OC; q.K = cg.ldk;
-    q.A = cols; q.lda = cg.ldk; q.trans_a = 0;
-    q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 1;
-    q.C = n.nhwc_out ? F(yv) : tmp.as<float>(); q.ldc = OC; q.alpha = 1.f; q.batch = 1;
-    if (d.n_in > 2 && d.in[2] >= 0) {
-      q.bias = F(d.in[2]);
-      q.bias_scale = 1.f;
+    for (int gi = 0; gi < G; ++gi) {
+      tx_gemm_desc q;
+      memset(&q, 0, sizeof q);
+      q.M = M; q.N = OCg; q.K = ldk;
+      q.A = cols + gi * M * ldk; q.lda = ldk; q.trans_a = 0;
+      q.B = wk.as<float>() + gi * OCg * ldk; q.ldb = ldk; q.trans_b = 1;
+      q.C = (n.nhwc_out ? F(yv) : tmp.as<float>()) + gi * OCg; q.ldc = OC; q.alpha = 1.f; q.batch = 1;
+      if (d.n_in > 2 && d.in[2] >= 0) {
+        q.bias = F(d.in[2]) + gi * OCg;
+        q.bias_scale = 1.f;
+      }
+      q.act = n.fused_act;
+      q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : ex ? TX_GEMM_EXACT : 0;
+      TX_TRY(gemm_dispatch(ctx, q));
     }
-    q.act = n.fused_act;
-    q.flags = tf32 ? (TX_GEMM_A_TF32 | TX_GEMM_B_TF32) : ex ? TX_GEMM_EXACT : 0;
-    TX_TRY(gemm_dispatch(ctx, q));
     if (n.nhwc_out) return TX_OK;  // the next convolution reads [N][OH][OW][OC]
     return transpose_b(ctx, tmp.as<float>(), F(yv), cg.N, (int64_t)cg.OH * cg.OW, OC);
   }
@@ -2219,7 +2253,6 @@ struct Bwd {
     const Shape &x = S(d.in[0]), &w = S(d.in[1]), &y = S(d.out[0]);
     const ConvGeom cg = conv_geom(x, w, y, d);
     const int64_t M = (int64_t)cg.N * cg.OH * cg.OW, OC = w[0];
-    const int64_t K = (int64_t)cg.KH * cg.KW * cg.C;
     const bool tf32 = ctx->math == TX_MATH_TF32;
     // dY (NCHW) -> [M, OC]; a fused activation's derivative is applied on the
     // way.  A channels-last output got its dY channels-last from the next
@@ -2244,22 +2277,27 @@ struct Bwd {
       TX_TRY(tx_bias_grad(ctx, dz, t, M, OC, 1.f, acc));
       wrote(d.in[2]);
     }
+    // per group g (one group unless the convolution is grouped): columns
+    // [M][ldk_g] of the channel slice, weights rows [g OCg, (g + 1) OCg)
+    const int G = d.iattr[0];
+    const ConvGeom g0 = conv_group(cg, G, 0);
+    const int64_t ldk = g0.ldk, OCg = OC / G;
     if (needs[d.in[1]]) {  // dW_khwc[OC, ldk] = dY^T cols, then back to [OC, C, KH, KW]
       float *t; int acc;
       TX_TRY(target(d.in[1], &t, &acc));
-      Scratch dwk(ctx, (size_t)OC * cg.ldk * 4);
+      Scratch dwk(ctx, (size_t)OC * ldk * 4);
       if (!dwk.ptr) return TX_ERR_OOM;
       tx_gemm_desc q; memset(&q, 0, sizeof q);
-      q.M = OC; q.N = cg.ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
+      q.M = OC; q.N = ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
       q.A = dz; q.lda = OC; q.trans_a = 1;
-      q.C = dwk.as<float>(); q.ldc = cg.ldk;
+      q.C = dwk.as<float>(); q.ldc = ldk;
       if (r->conv_implicit[ni]) {
         // B gathered from the channels-last input, 32 pixels per sub-tile;
         // without a fitting box the columns are built here after all
         const float *xin = r->extra[ni] ? (const float *)r->extra[ni] : F(d.in[0]);
         tx_tc::ConvGemm cv;
         int rc = TX_ERR_UNSUPPORTED;
-        q.B = xin; q.ldb = cg.ldk; q.trans_b = 0;
+        q.B = xin; q.ldb = ldk; q.trans_b = 0;
         if (conv_gather_fwd(cg, 32, cv)) {
           cv.op.b = 1;
           cv.src = {xin, cg.N, cg.H, cg.W, cg.C};
@@ -2267,7 +2305,7 @@ struct Bwd {
           const int mode = tc_mode(ctx, e);
           rc = gemm_conv_tc(ctx, e, mode, cv);
         }
-        Scratch cols(ctx, rc == TX_ERR_UNSUPPORTED ? (size_t)M * cg.ldk * 4 : 0);
+        Scratch cols(ctx, rc == TX_ERR_UNSUPPORTED ? (size_t)M * ldk * 4 : 0);
         if (rc == TX_ERR_UNSUPPORTED) {
           if (!cols.ptr) return TX_ERR_OOM;
           TX_TRY(im2col_nhwc(ctx, xin, cols.as<float>(), cg, tf32));
@@ -2277,19 +2315,25 @@ struct Bwd {
         }
         TX_TRY(rc);
       } else {
-        q.B = (const float *)r->extra[ni]; q.ldb = cg.ldk; q.trans_b = 0;
-        q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
-        TX_TRY(gemm_dispatch(ctx, q));
+        for (int gi = 0; gi < G; ++gi) {
+          tx_gemm_desc e = q;
+          e.M = OCg;
+          e.A = dz + gi * OCg;
+          e.B = (const float *)r->extra[ni] + gi * M * ldk; e.ldb = ldk; e.trans_b = 0;
+          e.C = dwk.as<float>() + gi * OCg * ldk;
+          e.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+          TX_TRY(gemm_dispatch(ctx, e));
+        }
       }
-      k_weight_from_khwc<<<grid_for(OC * K, 256), 256, 0, ctx->stream>>>(dwk.as<float>(), t, (int)OC, cg.C,
-                                                                        cg.KH, cg.KW, cg.ldk, acc);
+      k_weight_from_khwc<<<grid_for(OC * g0.C * cg.KH * cg.KW, 256), 256, 0, ctx->stream>>>(
+          dwk.as<float>(), t, (int)OC, g0.C, cg.KH, cg.KW, (int)ldk, acc);
       TX_LAUNCHED(ctx, "k_weight_from_khwc");
       wrote(d.in[1]);
     }
     if (needs[d.in[0]]) {  // dcols[M, ldk] = dY W_khwc ; dx = col2im(dcols) -> NCHW
       float *t; int acc;
       TX_TRY(target(d.in[0], &t, &acc));
-      if (ctx->math != TX_MATH_FP32) {
+      if (ctx->math != TX_MATH_FP32 && G == 1) {
         bool launched = false;
         const int rc = conv_dgrad_implicit(ni, cg, dz, t, acc, launched);
         if (rc != TX_ERR_UNSUPPORTED || launched) {
@@ -2298,37 +2342,38 @@ struct Bwd {
           return TX_OK;
         }
       }
-      Scratch wk(ctx, (size_t)OC * cg.ldk * 4), dcols(ctx, (size_t)M * cg.ldk * 4),
+      Scratch wk(ctx, (size_t)OC * ldk * 4), dcols(ctx, (size_t)M * ldk * 4),
           dxh(ctx, (size_t)cg.N * cg.H * cg.W * cg.C * 4);
       if (!wk.ptr || !dcols.ptr || !dxh.ptr) return TX_ERR_OOM;
-      k_weight_to_khwc<<<grid_for(OC * cg.ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
-                                                                           cg.C, cg.KH, cg.KW, cg.ldk, tf32);
+      k_weight_to_khwc<<<grid_for(OC * ldk, 256), 256, 0, ctx->stream>>>(F(d.in[1]), wk.as<float>(), (int)OC,
+                                                                        g0.C, cg.KH, cg.KW, (int)ldk, tf32);
       TX_LAUNCHED(ctx, "k_weight_to_khwc");
-      tx_gemm_desc q; memset(&q, 0, sizeof q);
-      q.M = M; q.N = cg.ldk; q.K = OC; q.alpha = 1.f; q.batch = 1;
-      q.A = dz; q.lda = OC; q.trans_a = 0;
-      q.B = wk.as<float>(); q.ldb = cg.ldk; q.trans_b = 0;
-      q.C = dcols.as<float>(); q.ldc = cg.ldk;
-      q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
-      TX_TRY(gemm_dispatch(ctx, q));
-      if (n.nhwc_in && !acc) {
-        // the producer reads dX channels-last; its fused activation's
-        // derivative is applied here, against its channels-last output
-        const int xv = d.in[0];
-        const GValue &xg = g->values[xv];
-        int pc = xg.producer;
-        if (pc >= 0 && g->nodes[pc].fused_into >= 0) pc = g->nodes[pc].fused_into;
-        const GNode *pn = pc >= 0 ? &g->nodes[pc] : nullptr;
-        const bool fuse = pn && pn->d.op == TX_OP_CONV && pn->nhwc_out && pn->fused_act &&
-                          (pn->fused_act == TX_ACT_RELU || pn->fused_act == TX_ACT_TANH) && pn->fused_out == xv;
-        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), t, cg, fuse ? F(xv) : nullptr, fuse ? pn->fused_act : TX_ACT_NONE));
-        if (fuse) grad_preact[xv] = true;
-      } else if (n.nhwc_in) {
-        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
+      // the producer reads dX channels-last; its fused activation's
+      // derivative is applied here, against its channels-last output
+      const int xv = d.in[0];
+      const GValue &xg = g->values[xv];
+      int pc = xg.producer;
+      if (pc >= 0 && g->nodes[pc].fused_into >= 0) pc = g->nodes[pc].fused_into;
+      const GNode *pn = pc >= 0 ? &g->nodes[pc] : nullptr;
+      const bool fuse = n.nhwc_in && !acc && pn && pn->d.op == TX_OP_CONV && pn->nhwc_out && pn->fused_act &&
+                        (pn->fused_act == TX_ACT_RELU || pn->fused_act == TX_ACT_TANH) && pn->fused_out == xv;
+      float *dst = (n.nhwc_in && !acc) ? t : dxh.as<float>();
+      for (int gi = 0; gi < G; ++gi) {
+        tx_gemm_desc q; memset(&q, 0, sizeof q);
+        q.M = M; q.N = ldk; q.K = OCg; q.alpha = 1.f; q.batch = 1;
+        q.A = dz + gi * OCg; q.lda = OC; q.trans_a = 0;
+        q.B = wk.as<float>() + gi * OCg * ldk; q.ldb = ldk; q.trans_b = 0;
+        q.C = dcols.as<float>(); q.ldc = ldk;
+        q.flags = tf32 ? TX_GEMM_B_TF32 : 0;
+        TX_TRY(gemm_dispatch(ctx, q));
+        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dst, conv_group(cg, G, gi), fuse ? F(xv) : nullptr,
+                           fuse ? pn->fused_act : TX_ACT_NONE));
+      }
+      if (fuse) grad_preact[xv] = true;
+      if (n.nhwc_in && acc) {
         const int64_t nx = (int64_t)cg.N * cg.H * cg.W * cg.C, one = 1;
         TX_TRY(nd_copy(ctx, dxh.as<float>(), &one, t, &nx, 1, 4, 1.f, acc));
-      } else {
-        TX_TRY(col2im_nhwc(ctx, dcols.as<float>(), dxh.as<float>(), cg));
+      } else if (!n.nhwc_in) {
         TX_TRY(transpose_b(ctx, dxh.as<float>(), t, cg.N, (int64_t)cg.H * cg.W, cg.C, nullptr, nullptr,
                            TX_ACT_NONE, acc));
       }

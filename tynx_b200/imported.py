@@ -318,7 +318,9 @@ def lower(graph: ir.TrainingGraph):
             strides = list(a.get("strides") or [1] * nd)
             pads = list(a.get("pads") or [0] * (2 * nd))
             dil = list(a.get("dilations") or [1] * nd)
-            if nd != 2:
+            if nd == 1:  # 1-D convolution runs as 2-D over a unit height
+                strides, dil, pads = [1] + strides, [1] + dil, [0, pads[0], 0, pads[1]]
+            elif nd != 2:
                 raise NotImplementedError(f"{nd}-D Conv is not supported by the CUDA engine")
             # ONNX pads are [x1_begin, x2_begin, x1_end, x2_end]
             ints = strides + [pads[0], pads[1], pads[2], pads[3]] + dil
