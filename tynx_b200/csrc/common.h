@@ -142,6 +142,16 @@ int softmax_bwd(tx_ctx *ctx, const float *y, const float *dy, float *dx, int64_t
 int layernorm_fwd(tx_ctx *ctx, const float *x, const float *gamma, const float *beta, float *y, float *mean,
                   float *rstd, int64_t rows, int64_t cols, float eps, bool round_tf32);
 
+// Direct convolution for short filters (conv_direct.cu): C * KH * KW < 32 and
+// OC <= 64.  geom = {N, C, H, W, KH, KW, OH, OW, sh, sw, pt, pl, dh, dw}; x is
+// NCHW; y NCHW or channels-last; dz channels-last [N * OH * OW][OC]; dw is
+// [OC][C][KH][KW], db (or null) [OC].  TX_ERR_UNSUPPORTED for other shapes.
+bool conv_direct_ok(int C, int KH, int KW, int OC);
+int conv_direct_fwd(tx_ctx *ctx, const float *x, const float *w, const float *bias, float *y, const int *geom, int OC,
+                    int act, bool nhwc_out);
+int conv_direct_wgrad(tx_ctx *ctx, const float *x, const float *dz, const int *geom, int OC, float *dw, float *db,
+                      int acc_w, int acc_b);
+
 // grid sizing helper
 inline unsigned grid_for(int64_t n, int threads, int64_t max_blocks = 148 * 16) {
   int64_t b = (n + threads - 1) / threads;

@@ -606,9 +606,10 @@ struct tx_record {
   bool shadow = false;     // parameters read by GEMMs come from flat_tf32
   bool tracking = false;
   std::vector<uint8_t> attn_fused;  // per tx_graph::attn block: ran as the fused kernels
-  std::vector<uint8_t> conv_implicit;  // per node: the convolution ran as an implicit GEMM
-                                       // (extra holds its channels-last input, or null when
-                                       // the input value is channels-last itself)
+  std::vector<uint8_t> conv_implicit;  // per node: the convolution ran as an implicit GEMM (1;
+                                       // extra holds its channels-last input, or null when
+                                       // the input value is channels-last itself) or as the
+                                       // direct short-filter kernel (2; it reads the NCHW input)
 };
 
 namespace {
@@ -1540,6 +1541,13 @@ struct Fwd {
     const bool ex = n.exact && ctx->math == TX_MATH_TF32;
     const bool tf32 = ctx->math == TX_MATH_TF32 && !ex;
     const int G = d.iattr[0];
+    if (G == 1 && !n.nhwc_in && conv_direct_ok(cg.C, cg.KH, cg.KW, (int)OC)) {
+      const int geom[14] = {cg.N, cg.C, cg.H, cg.W, cg.KH, cg.KW, cg.OH, cg.OW, cg.sh, cg.sw, cg.pt, cg.pl, cg.dh, cg.dw};
+      const float *bias = d.n_in > 2 && d.in[2] >= 0 ? F(d.in[2]) : nullptr;
+      TX_TRY(conv_direct_fwd(ctx, F(d.in[0]), F(d.in[1]), bias, F(yv), geom, (int)OC, n.fused_act, n.nhwc_out));
+      r->conv_implicit[ni] = 2;
+      return TX_OK;
+    }
     if (ctx->math != TX_MATH_FP32 && G == 1) {
       const int rc = conv_forward_implicit(ni, cg, ex, tf32);
       if (rc != TX_ERR_UNSUPPORTED) return rc;
@@ -2271,7 +2279,18 @@ struct Bwd {
       TX_TRY(transpose_b(ctx, dy, dz, cg.N, OC, (int64_t)cg.OH * cg.OW, nullptr,
                          apply_dact ? F(yv) : nullptr, apply_dact ? n.fused_act : TX_ACT_NONE));
     }
-    if (d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]]) {
+    const bool direct = r->conv_implicit[ni] == 2;
+    const bool bias_grad = d.n_in > 2 && d.in[2] >= 0 && needs[d.in[2]];
+    if (direct && needs[d.in[1]]) {
+      // weight and bias gradients in one pass over the NCHW input and dZ
+      const int geom[14] = {cg.N, cg.C, cg.H, cg.W, cg.KH, cg.KW, cg.OH, cg.OW, cg.sh, cg.sw, cg.pt, cg.pl, cg.dh, cg.dw};
+      float *tw, *tb = nullptr; int aw, ab = 0;
+      TX_TRY(target(d.in[1], &tw, &aw));
+      if (bias_grad) TX_TRY(target(d.in[2], &tb, &ab));
+      TX_TRY(conv_direct_wgrad(ctx, F(d.in[0]), dz, geom, (int)OC, tw, tb, aw, ab));
+      wrote(d.in[1]);
+      if (bias_grad) wrote(d.in[2]);
+    } else if (bias_grad) {
       float *t; int acc;
       TX_TRY(target(d.in[2], &t, &acc));
       TX_TRY(tx_bias_grad(ctx, dz, t, M, OC, 1.f, acc));
@@ -2282,7 +2301,7 @@ struct Bwd {
     const int G = d.iattr[0];
     const ConvGeom g0 = conv_group(cg, G, 0);
     const int64_t ldk = g0.ldk, OCg = OC / G;
-    if (needs[d.in[1]]) {  // dW_khwc[OC, ldk] = dY^T cols, then back to [OC, C, KH, KW]
+    if (!direct && needs[d.in[1]]) {  // dW_khwc[OC, ldk] = dY^T cols, then back to [OC, C, KH, KW]
       float *t; int acc;
       TX_TRY(target(d.in[1], &t, &acc));
       Scratch dwk(ctx, (size_t)OC * ldk * 4);
@@ -2291,7 +2310,7 @@ struct Bwd {
       q.M = OC; q.N = ldk; q.K = M; q.alpha = 1.f; q.batch = 1;
       q.A = dz; q.lda = OC; q.trans_a = 1;
       q.C = dwk.as<float>(); q.ldc = ldk;
-      if (r->conv_implicit[ni]) {
+      if (r->conv_implicit[ni] == 1) {
         // B gathered from the channels-last input, 32 pixels per sub-tile;
         // without a fitting box the columns are built here after all
         const float *xin = r->extra[ni] ? (const float *)r->extra[ni] : F(d.in[0]);

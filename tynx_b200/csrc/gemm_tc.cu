@@ -228,18 +228,34 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
     m.conv_mask = 0;
     mode = 0;
   }
-  // Without operand conversion, shapes with more 128 x 256 tiles than SMs run
-  // persistently: the epilogue of one tile overlaps the next tile's main loop
-  // (measured: 32768x1024x256 100 -> 70 us, 32768x256x256 33 -> 27 us); one
-  // wave gains nothing from it and keeps two interleaved accumulators.
+  // Shapes with more tiles than SMs run persistently: the epilogue of one tile
+  // overlaps the next tile's main loop (measured without conversion:
+  // 32768x1024x256 100 -> 70 us, 32768x256x256 33 -> 27 us).  One wave gains
+  // nothing and keeps two interleaved accumulators.  With operand conversion
+  // the one-tile kernel keeps every stage and the epilogue in one CTA per SM,
+  // so its setup (barriers, TMEM, tensor-map fetches) and epilogue are paid
+  // once per tile with nothing overlapping them: products of three or more
+  // waves, or of two waves of short tiles (at most 16 k-blocks: the implicit
+  // convolutions), run persistently too, on tiles at most 128 wide (64 for
+  // 3xTF32) that keep the one-tile kernel's accumulator count.
   bool persistent = false;
-  if (mode == 0 && tiling.splits == 1) {
-    // narrow outputs (batched attention products) need more waves to pay off
-    const int pbn = d.N > 128 ? 256 : d.N > 64 ? 128 : 64;
-    const int64_t tiles = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + pbn - 1) / pbn) * batch;
-    if (tiles > (pbn == 256 ? 1 : 2) * (int64_t)ctx->num_sms) {
-      persistent = true;
-      tiling.bn = pbn;
+  if (tiling.splits == 1) {
+    if (mode == 0) {
+      // narrow outputs (batched attention products) need more waves to pay off
+      const int pbn = d.N > 128 ? 256 : d.N > 64 ? 128 : 64;
+      const int64_t tiles = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + pbn - 1) / pbn) * batch;
+      if (tiles > (pbn == 256 ? 1 : 2) * (int64_t)ctx->num_sms) {
+        persistent = true;
+        tiling.bn = pbn;
+      }
+    } else {
+      const int64_t tiles = ((d.M + TC_BM - 1) / TC_BM) * ((d.N + tiling.bn - 1) / tiling.bn) * batch;
+      const int64_t waves = (tiles + ctx->num_sms - 1) / ctx->num_sms;
+      const int64_t kblocks = (d.K + TC_BK - 1) / TC_BK;
+      if (waves >= 3 || (waves >= 2 && kblocks <= 16)) {
+        persistent = true;
+        tiling.bn = mode == 2 || d.N <= 64 ? 64 : 128;
+      }
     }
   }
   const int bn = tiling.bn;
@@ -307,7 +323,9 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
       }
     }
     if (persistent && m.tma_epi) {
-      const int rc = launch_persistent(ctx, bn, d, m, batch, 0);
+      const int rc = mode == 0   ? launch_persistent(ctx, bn, d, m, batch, 0)
+                     : mode == 1 ? launch_persistent_round(ctx, bn, d, m, batch, 0)
+                                 : launch_persistent_split(ctx, bn, d, m, batch, 0);
       if (rc != TX_ERR_UNSUPPORTED || d.B_lo) return rc;
     } else if (d.B_lo) {
       return TX_ERR_UNSUPPORTED;
@@ -334,7 +352,7 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
   raw.flags = d.flags & ~TX_GEMM_ROUND_OUT;  // partials stay exact; the reduction rounds
   make_epilogue_maps(m, raw, splits);
   int rc = TX_ERR_UNSUPPORTED;
-  if (persistent && m.tma_epi) rc = launch_persistent(ctx, bn, raw, m, splits, kb_per);
+  if (persistent && mode == 0 && m.tma_epi) rc = launch_persistent(ctx, bn, raw, m, splits, kb_per);
   if (rc == TX_ERR_UNSUPPORTED) rc = pair ? launch_pair(ctx, raw, m, splits, kb_per)
                                           : launch_any(ctx, mode, bn, raw, m, splits, kb_per);
   TX_TRY(rc);

@@ -79,6 +79,11 @@ int launch_pair(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, int64_t z, in
 // would not fit next to the epilogue's tiles
 int launch_persistent(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per,
                       int max_grid = 0);
+// persistent with operand conversion in shared memory: TF32 rounding of the
+// operands m.conv_mask selects (gemm_tc_pers1.cu), or the 3xTF32 split of
+// both, tiles at most 128 wide (gemm_tc_pers2.cu)
+int launch_persistent_round(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per);
+int launch_persistent_split(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per);
 
 }  // namespace tx_tc
 

@@ -1069,14 +1069,23 @@ constexpr int kPTail = 2048;  // barriers, then each epilogue warp's 32 bias val
 // BLO: B arrives as a TF32 head and tail (two tiles per stage) and each
 // k-slice issues A B + A B_lo, so the weights enter the product to fp32-class
 // accuracy while A stays TF32.
-template <int BN, bool BLO = false>
+// MODE (as in the one-tile kernel): 0 operands used as loaded; 1 four
+// conversion warps round each landed stage to TF32 in place; 2 they split
+// both operands into big and small halves (the small ones in the stage's
+// second half) and each k-slice issues three MMAs.  With conversion the tiles
+// are at most 128 wide, so that each of the two TMEM buffers holds as many
+// accumulators as the one-tile kernel keeps (the chains of truncating TMEM
+// adds, and so the products' rounding, stay as short).
+template <int BN, bool BLO = false, int MODE = 0>
 struct PCfg {
-  static constexpr int NACC = BN == 256 ? 1 : 2;
+  static_assert(MODE == 0 || BN <= 128, "persistent tiles with operand conversion are at most 128 wide");
+  static constexpr int NACC = MODE == 2 ? (512 / (2 * BN) > 4 ? 4 : 512 / (2 * BN)) : (BN == 256 ? 1 : 2);
   static constexpr int ACC = BN * NACC;                 // columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC < 256 ? 256 : 2 * ACC;
   static constexpr int A_BYTES = TC_BM * TC_BK * 4;
   static constexpr int B_BYTES = BN * TC_BK * 4;
-  static constexpr int STAGE = A_BYTES + B_BYTES * (BLO ? 2 : 1);
+  static constexpr int STAGE = (A_BYTES + B_BYTES * (BLO ? 2 : 1)) * (MODE == 2 ? 2 : 1);
+  static constexpr int CONV_THREADS = MODE ? kConvThreads : 0;
 };
 
 struct PWork {
@@ -1085,15 +1094,17 @@ struct PWork {
   int stages;            // pipeline depth (runtime: the epilogue's tiles vary)
   int ep_stride;         // epilogue bytes per warp
   float *col_part;       // fused column sums (one row per 32 output rows) or null
+  int conv_mask;         // MODE 1: operands to round (bit 0 A, bit 1 B)
 };
 
-template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false>
-__global__ void __launch_bounds__(64 + 32 * EW, 1)
+template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false, int MODE = 0>
+__global__ void __launch_bounds__(64 + 32 * EW + PCfg<BN, BLO, MODE>::CONV_THREADS, 1)
     k_gemm_tcp(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapS,
                const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapB2,
                const tx_gemm_desc d, int *err, PWork w, const __grid_constant__ tx_tc::GatherOp gop) {
-  using Cfg = PCfg<BN, BLO>;
+  static_assert(MODE == 0 || !BLO, "split weights take no operand conversion");
+  using Cfg = PCfg<BN, BLO, MODE>;
   constexpr int NACC = Cfg::NACC;
   constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
@@ -1107,7 +1118,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   uint64_t *tfull = empty + 8;
   uint64_t *tempty = tfull + 2;
   uint64_t *ebar = tempty + 2;
-  uint32_t *tmem_holder = (uint32_t *)(ebar + 2 * EW);
+  uint64_t *conv = ebar + 2 * EW;  // MODE >= 1: stage converted (kConvThreads arrivals)
+  uint32_t *tmem_holder = (uint32_t *)(conv + 8);
   volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
   float *bias_rows = reinterpret_cast<float *>(tail + 1024);  // [EW][32]
 
@@ -1119,6 +1131,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], kConvThreads);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -1211,7 +1224,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         for (int kb = 0; kb < num_k; ++kb, ++cnt) {
           const int s = (int)(cnt % (uint32_t)stages);
           const uint32_t round = cnt / (uint32_t)stages;
-          if (!mbar_wait(&full[s], round & 1, abort_flag, err, 13)) {
+          if (!mbar_wait(MODE == 0 ? &full[s] : &conv[s], round & 1, abort_flag, err, 13)) {
             ok = false;
             break;
           }
@@ -1223,13 +1236,54 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 #pragma unroll
           for (int k = 0; k < TC_BK / 8; ++k) {
             const uint64_t ad = operand_desc<A_MN>(a_base, k);
-            tc_mma_tf32(acc, ad, operand_desc<B_MN>(b_base, k), idesc, (fresh && k == 0) ? 0u : 1u);
+            const uint64_t bd = operand_desc<B_MN>(b_base, k);
+            tc_mma_tf32(acc, ad, bd, idesc, (fresh && k == 0) ? 0u : 1u);
             if (BLO) tc_mma_tf32(acc, ad, operand_desc<B_MN>(b_base + B_BYTES, k), idesc, 1u);
+            if (MODE == 2) {
+              const uint32_t sa = a_base + A_BYTES + B_BYTES, sb = sa + A_BYTES;
+              tc_mma_tf32(acc, ad, operand_desc<B_MN>(sb, k), idesc, 1u);
+              tc_mma_tf32(acc, operand_desc<A_MN>(sa, k), bd, idesc, 1u);
+            }
           }
           tc_commit(&empty[s]);
         }
         if (!ok) break;
         tc_commit(&tfull[buf]);  // arrives when every MMA of this tile has completed
+      }
+    }
+  } else if (MODE != 0 && warp >= 2 + EW) {
+    // operand conversion, one stage behind the producer and one ahead of the
+    // MMA, over the same k-block sequence
+    const int ct = threadIdx.x - (64 + 32 * EW);  // 0 .. kConvThreads - 1
+    constexpr int N4 = (A_BYTES + B_BYTES) / 16;
+    const int i_begin = (MODE == 2 || (w.conv_mask & 1)) ? ct : A_BYTES / 16 + ct;
+    const int i_end = (MODE == 2 || (w.conv_mask & 2)) ? N4 : A_BYTES / 16;
+    uint32_t cnt = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < w.items && alive; item += gridDim.x) {
+      int m0, n0, z, kb_first, num_k;
+      decode(item, m0, n0, z, kb_first, num_k);
+      for (int kb = 0; kb < num_k; ++kb, ++cnt) {
+        const int s = (int)(cnt % (uint32_t)stages);
+        const uint32_t round = cnt / (uint32_t)stages;
+        if (!mbar_wait(&full[s], round & 1, abort_flag, err, 16)) {
+          alive = false;
+          break;
+        }
+        float4 *pa = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE);
+        float4 *pq = reinterpret_cast<float4 *>(smem + s * Cfg::STAGE + A_BYTES + B_BYTES);
+#pragma unroll 4
+        for (int i = i_begin; i < i_end; i += kConvThreads) {
+          const float4 v = pa[i];
+          const float4 big = make_float4(to_tf32_rn(v.x), to_tf32_rn(v.y), to_tf32_rn(v.z), to_tf32_rn(v.w));
+          pa[i] = big;
+          if (MODE == 2)
+            pq[i] = make_float4(to_tf32_rn(v.x - big.x), to_tf32_rn(v.y - big.y), to_tf32_rn(v.z - big.z),
+                                to_tf32_rn(v.w - big.w));
+        }
+        // the generic-proxy writes become visible to the tensor core (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&conv[s]);
       }
     }
   } else {
@@ -1367,9 +1421,9 @@ int launch_mode(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64
 
 
 #ifdef TX_TC_PERSISTENT_TU
-template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false>
+template <int BN, bool A_MN, bool B_MN, int EW, bool BLO = false, int MODE = 0>
 int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
-  auto kern = k_gemm_tcp<BN, A_MN, B_MN, EW, BLO>;
+  auto kern = k_gemm_tcp<BN, A_MN, B_MN, EW, BLO, MODE>;
   static bool configured[64] = {};
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
@@ -1378,43 +1432,51 @@ int launch_p(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, 
   }
   int grid = w.items < ctx->num_sms ? w.items : ctx->num_sms;
   if (max_grid > 0 && grid > max_grid) grid = max_grid;
-  kern<<<grid, 64 + 32 * EW, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, m.b2, d, ctx->d_err, w, m.g);
+  constexpr int threads = 64 + 32 * EW + PCfg<BN, BLO, MODE>::CONV_THREADS;
+  kern<<<grid, threads, smem, ctx->stream>>>(m.a, m.b, m.c, m.s, m.p, m.b2, d, ctx->d_err, w, m.g);
   TX_LAUNCHED(ctx, "k_gemm_tcp");
   return TX_OK;
 }
 
-template <int BN, int EW>
+template <int BN, int EW, int MODE>
 int launch_p_bn(tx_ctx *ctx, const tx_gemm_desc &d, const Maps &m, const PWork &w, int smem, int max_grid) {
   const bool a_mn = d.trans_a != 0, b_mn = d.trans_b == 0;
-  if (d.B_lo) {  // split weights: forward layouts only (A K-major)
-    if (a_mn) return TX_ERR_UNSUPPORTED;
-    return b_mn ? launch_p<BN, false, true, EW, true>(ctx, d, m, w, smem, max_grid)
-                : launch_p<BN, false, false, EW, true>(ctx, d, m, w, smem, max_grid);
+  if constexpr (MODE == 0) {
+    if (d.B_lo) {  // split weights: forward layouts only (A K-major)
+      if (a_mn) return TX_ERR_UNSUPPORTED;
+      return b_mn ? launch_p<BN, false, true, EW, true>(ctx, d, m, w, smem, max_grid)
+                  : launch_p<BN, false, false, EW, true>(ctx, d, m, w, smem, max_grid);
+    }
+  } else {
+    if (d.B_lo) return TX_ERR_UNSUPPORTED;
   }
-  if (a_mn && b_mn) return launch_p<BN, true, true, EW>(ctx, d, m, w, smem, max_grid);
-  if (a_mn) return launch_p<BN, true, false, EW>(ctx, d, m, w, smem, max_grid);
-  if (b_mn) return launch_p<BN, false, true, EW>(ctx, d, m, w, smem, max_grid);
-  return launch_p<BN, false, false, EW>(ctx, d, m, w, smem, max_grid);
+  if (a_mn && b_mn) return launch_p<BN, true, true, EW, false, MODE>(ctx, d, m, w, smem, max_grid);
+  if (a_mn) return launch_p<BN, true, false, EW, false, MODE>(ctx, d, m, w, smem, max_grid);
+  if (b_mn) return launch_p<BN, false, true, EW, false, MODE>(ctx, d, m, w, smem, max_grid);
+  return launch_p<BN, false, false, EW, false, MODE>(ctx, d, m, w, smem, max_grid);
 }
 
 // Persistent launch of d (raw split partials when kb_per > 0, z = splits or
-// batch).  TX_ERR_UNSUPPORTED when the stages would not fit next to the
-// epilogue's tiles.
+// batch) with operand mode MODE.  TX_ERR_UNSUPPORTED when the stages would
+// not fit next to the epilogue's tiles (or a 3xTF32 tile is wider than 128).
 // max_grid > 0 caps the CTA count (several tiles per CTA even when the tiles
 // would fit one wave, so that one tile's epilogue overlaps the next's main loop).
+template <int MODE>
 int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Maps &m, int64_t z, int kb_per,
                            int max_grid) {
-  const int stage = (TC_BM + bn * (d.B_lo ? 2 : 1)) * TC_BK * 4;
+  if (MODE != 0 && bn > 128) return TX_ERR_UNSUPPORTED;
+  const int stage = (TC_BM + bn * (d.B_lo ? 2 : 1)) * TC_BK * 4 * (MODE == 2 ? 2 : 1);
   const int kinds = 1 + (d.preact ? 1 : 0) + (d.dact ? 1 : 0) + (d.beta != 0.f ? 1 : 0);
   PWork w;
   w.ep_stride = kinds * 8192;
   w.col_part = m.col_part;
+  w.conv_mask = m.conv_mask;
   // a GELU (or GELU') epilogue costs more than a 256-wide tile's main loop,
   // and so does any epilogue after a short reduction (K <= 512: at most 16
   // k-blocks per tile): eight epilogue warps, when two stages still fit
   // beside their tiles
   int ew = 4;
-  if (bn == 256 && (d.act == TX_ACT_GELU || d.dact == TX_ACT_GELU || d.K <= 512) &&
+  if (MODE == 0 && bn == 256 && (d.act == TX_ACT_GELU || d.dact == TX_ACT_GELU || d.K <= 512) &&
       (kSmemMax - 1024 - kPTail - 8 * w.ep_stride) / stage >= 2)
     ew = 8;
   w.stages = (kSmemMax - 1024 - kPTail - ew * w.ep_stride) / stage;
@@ -1428,12 +1490,17 @@ int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Map
   if (items > 0x7fffffff) return TX_ERR_UNSUPPORTED;
   w.items = (int)items;
   const int smem = 1024 + w.stages * stage + ew * w.ep_stride + kPTail;
-  switch (bn) {
-    case 256:
-      return ew == 8 ? launch_p_bn<256, 8>(ctx, d, m, w, smem, max_grid)
-                     : launch_p_bn<256, 4>(ctx, d, m, w, smem, max_grid);
-    case 64: return launch_p_bn<64, 4>(ctx, d, m, w, smem, max_grid);
-    default: return launch_p_bn<128, 4>(ctx, d, m, w, smem, max_grid);
+  if constexpr (MODE != 0) {
+    return bn == 64 ? launch_p_bn<64, 4, MODE>(ctx, d, m, w, smem, max_grid)
+                    : launch_p_bn<128, 4, MODE>(ctx, d, m, w, smem, max_grid);
+  } else {
+    switch (bn) {
+      case 256:
+        return ew == 8 ? launch_p_bn<256, 8, MODE>(ctx, d, m, w, smem, max_grid)
+                       : launch_p_bn<256, 4, MODE>(ctx, d, m, w, smem, max_grid);
+      case 64: return launch_p_bn<64, 4, MODE>(ctx, d, m, w, smem, max_grid);
+      default: return launch_p_bn<128, 4, MODE>(ctx, d, m, w, smem, max_grid);
+    }
   }
 }
 
