@@ -75,14 +75,19 @@ __device__ __forceinline__ void load_patch(const float *__restrict__ x, const Di
   }
 }
 
-// One thread per output pixel, kPix threads per block.
+// A block tile is kPix pixels x OCP channels in 32 x (OCP / 8) work items of
+// four consecutive pixels x eight channels (item it: pixels 4 (it % 32) ..,
+// channels 8 (it / 32) ..), so each k step reads one float4 of patch values
+// and two of weights for 32 FMAs.  Patches are staged k-major (pt[k][pixel])
+// by one thread per pixel with independent loads.
 template <int OCP>
 __global__ void __launch_bounds__(kPix) k_conv_direct_fwd(const float *__restrict__ x, const float *__restrict__ w,
                                                           const float *__restrict__ bias, float *__restrict__ y,
                                                           DirectGeom g, int act, int nhwc_out) {
-  __shared__ __align__(16) float ws[kDirectK][OCP];  // ws[k][o] = w[o][k]
+  constexpr int OG = OCP / 8;  // channel groups of eight
+  __shared__ __align__(16) float ws[kDirectK][OCP];   // ws[k][o] = w[o][k]
+  __shared__ __align__(16) float pt[kDirectK][kPix + 4];  // pt[k][pixel]
   __shared__ float bs[OCP];
-  __shared__ __align__(16) float tile[kPix * OCP];   // channels-last staging of the block's outputs
   __shared__ PatchTable tab;
   for (int e = threadIdx.x; e < kDirectK * OCP; e += blockDim.x) {
     const int k = e / OCP, o = e % OCP;
@@ -90,48 +95,64 @@ __global__ void __launch_bounds__(kPix) k_conv_direct_fwd(const float *__restric
   }
   for (int o = threadIdx.x; o < OCP; o += blockDim.x) bs[o] = (bias && o < g.OC) ? bias[o] : 0.f;
   build_table(g, tab);
-  __syncthreads();
   const int64_t M = (int64_t)g.N * g.OH * g.OW;
+  const int64_t hw = (int64_t)g.OH * g.OW;
+  // kPix / 4 = 32 pixel quads x OG channel groups = 32 OG work items per tile,
+  // kPix threads: each thread takes items it, it + kPix, ...
   for (int64_t p0 = (int64_t)blockIdx.x * kPix; p0 < M; p0 += (int64_t)gridDim.x * kPix) {
-    const int64_t p = p0 + threadIdx.x;
-    float acc[OCP];
-#pragma unroll
-    for (int o = 0; o < OCP; ++o) acc[o] = 0.f;
-    if (p < M) {
+    __syncthreads();  // the table is built / the previous tile's patches are consumed
+    {
+      const int64_t p = p0 + threadIdx.x;
       float v[kDirectK];
-      load_patch<kDirectK>(x, g, tab, p, 0, v);
+      if (p < M) {
+        load_patch<kDirectK>(x, g, tab, p, 0, v);
+      } else {
 #pragma unroll
+        for (int k = 0; k < kDirectK; ++k) v[k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < kDirectK; ++k) pt[k][threadIdx.x] = v[k];
+    }
+    __syncthreads();
+    for (int it = threadIdx.x; it < 32 * OG; it += blockDim.x) {
+      const int q = it % 32, og = it / 32;
+      const int px = 4 * q, o0 = 8 * og;
+      float acc[4][8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
       for (int k = 0; k < kDirectK; ++k) {
-        // slots past K hold zeros and ws is zero there: no test needed
+        const float4 pv = *reinterpret_cast<const float4 *>(&pt[k][px]);
+        const float4 w0 = *reinterpret_cast<const float4 *>(&ws[k][o0]);
+        const float4 w1 = *reinterpret_cast<const float4 *>(&ws[k][o0 + 4]);
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+        const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int o = 0; o < OCP; o += 4) {
-          const float4 wv = *reinterpret_cast<const float4 *>(&ws[k][o]);
-          acc[o] = fmaf(v[k], wv.x, acc[o]);
-          acc[o + 1] = fmaf(v[k], wv.y, acc[o + 1]);
-          acc[o + 2] = fmaf(v[k], wv.z, acc[o + 2]);
-          acc[o + 3] = fmaf(v[k], wv.w, acc[o + 3]);
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(pa[i], wa[j], acc[i][j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t p = p0 + px + i;
+        if (p >= M) break;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = tx_epi::act(act, acc[i][j] + bs[o0 + j]);
+        if (nhwc_out) {
+          float *dst = y + p * g.OC + o0;
+          if (o0 + 8 <= g.OC && (g.OC & 3) == 0) {
+            reinterpret_cast<float4 *>(dst)[0] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            reinterpret_cast<float4 *>(dst)[1] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+          } else {
+            for (int j = 0; j < 8 && o0 + j < g.OC; ++j) dst[j] = acc[i][j];
+          }
+        } else {
+          const int64_t n = p / hw, r = p - n * hw;
+          for (int j = 0; j < 8 && o0 + j < g.OC; ++j) y[(n * g.OC + o0 + j) * hw + r] = acc[i][j];
         }
       }
-#pragma unroll
-      for (int o = 0; o < OCP; ++o) acc[o] = tx_epi::act(act, acc[o] + bs[o]);
-    }
-    if (!nhwc_out) {
-      if (p < M) {
-        const int64_t hw = (int64_t)g.OH * g.OW, n = p / hw, r = p - n * hw;
-        for (int o = 0; o < g.OC; ++o) y[(n * g.OC + o) * hw + r] = acc[o];  // lanes: consecutive pixels
-      }
-      continue;
-    }
-    // channels-last: the block's rows are one contiguous run of y
-    __syncthreads();  // the previous tile's staging has been read
-#pragma unroll
-    for (int o = 0; o < OCP; ++o) tile[threadIdx.x * OCP + ((o + threadIdx.x) % OCP)] = acc[o];
-    __syncthreads();
-    const int rows = M - p0 < kPix ? (int)(M - p0) : kPix;
-    float *dst = y + p0 * g.OC;
-    for (int e = threadIdx.x; e < rows * g.OC; e += blockDim.x) {
-      const int r = e / g.OC, o = e - r * g.OC;
-      dst[e] = tile[r * OCP + ((o + r) % OCP)];
     }
   }
 }

@@ -55,6 +55,24 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// 4-D map of an MN-major operand stored [batch][outer = K][ld] with inner = MN
+// a multiple of 32: dims {32, K, MN / 32, batch}, so a box {32, 32, nblk, 1}
+// brings nblk consecutive 32-column blocks in one copy (the 128-byte swizzle
+// with 32-byte atoms, as the per-block boxes).
+bool make_map_mn4(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
+                  int64_t batch_stride, int nblk) {
+  if (inner % 32 || nblk < 1 || nblk > 8) return false;
+  cuuint64_t dims[4] = {32u, (cuuint64_t)outer, (cuuint64_t)(inner / 32), (cuuint64_t)batch};
+  int64_t bs = batch > 1 ? batch_stride : ld * outer;
+  cuuint64_t strides[3] = {(cuuint64_t)(ld * 4), 128u, (cuuint64_t)(((bs * 4) + 15) & ~int64_t(15))};
+  cuuint32_t box[4] = {32u, 32u, (cuuint32_t)nblk, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 4-D map over a channels-last [n][h][w][c] tensor (dims {c, w, h, n}) whose
 // boxes step estr_w / estr_h elements along w / h: the operand tiles of an
 // implicit-GEMM convolution.  Coordinates outside the tensor read zeros.
@@ -284,12 +302,27 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
     ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
   if (cv) m.g = cv->op;
+  // dense MN-major operands whose MN extent is a multiple of 32: one box per
+  // tile instead of one per 32-column block (the per-block maps stay when the
+  // 4-D map is refused)
+  CUtensorMap mn4;
+  if (d.trans_a && !(cv && cv->op.a) && make_map_mn4(&mn4, d.A, d.M, d.K, d.lda, batch, d.stride_a, TC_BM / 32)) {
+    m.a = mn4;
+    m.g.amn = 1;
+  }
+  if (!d.trans_b && !(cv && cv->op.b) &&
+      make_map_mn4(&mn4, d.B, d.N, d.K, d.ldb, batch, d.stride_b, (pair ? bn / 2 : bn) / 32)) {
+    m.b = mn4;
+    m.g.bmn = 1;
+  }
   // split weights (B head + tail) run on the persistent kernel only; other
   // shapes report unsupported and the dispatcher runs two products instead
   if (d.B_lo) {
     if (!persistent || tiling.splits > 1 || d.trans_a || ((uintptr_t)d.B_lo & 15)) return TX_ERR_UNSUPPORTED;
     if (d.trans_b)
       ok = make_map(&m.b2, d.B_lo, d.K, d.N, d.ldb, batch, d.stride_b, bn, false);
+    else if (m.g.bmn)  // the same 4-D form as B
+      ok = make_map_mn4(&m.b2, d.B_lo, d.N, d.K, d.ldb, batch, d.stride_b, bn / 32);
     else
       ok = make_map(&m.b2, d.B_lo, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
     if (!ok) return TX_ERR_UNSUPPORTED;

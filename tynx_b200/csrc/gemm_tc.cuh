@@ -34,6 +34,10 @@ struct GatherOp {
   int wsplit;   // > 0: the output-side maps are 3-D [rows][wsplit][N] views and
                 //      output row y sits at (y % wsplit, y / wsplit)
   int16_t offx[kGatherTaps], offy[kGatherTaps], wtap[kGatherTaps];
+  // dense MN-major operands (not gathered): 1 when the map is 4-D {32, K,
+  // MN / 32, batch} and a tile's 32-column blocks come in one box instead of
+  // one box each (the MN extent a multiple of 32)
+  int amn, bmn;
 };
 
 // Tensor maps of one launch: the operands, and for the TMA epilogue the

@@ -156,6 +156,20 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// An MN-major operand tile of nblk 32-column blocks (4 KB each, consecutive in
+// shared memory) starting at column c0: one box of a 4-D map when `merged`,
+// else one 3-D box per block.  TMA issue is serial per SM, so fewer boxes keep
+// the producer ahead.
+__device__ __forceinline__ void load_mn(uint32_t dst, const CUtensorMap *map, uint64_t *bar, int merged, int nblk,
+                                        int c0, int k0, int z) {
+  if (merged) {
+    tma_load_4d(dst, map, bar, 0, k0, c0 / 32, z);
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < nblk; ++j) tma_load_3d(dst + j * 4096, map, bar, c0 + 32 * j, k0, z);
+  }
+}
+
 // The box of the pixels from p of an implicit-GEMM operand (GatherOp), tap t,
 // channel block cb.  Boxes that start outside the tensor read zeros there: the
 // convolution's padding.
@@ -206,6 +220,15 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(map), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster,
+                                                 int c, int x, int y, int n) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar_cluster), "r"(c), "r"(x), "r"(y), "r"(n)
       : "memory");
 }
 
@@ -816,14 +839,18 @@ __global__ void __launch_bounds__(320, 1)
           // expects the bytes of both
           const uint32_t fb = map_to_rank(smem_u32(&full[s]), 0);
           if (rank == 0) mbar_expect_tx(&full[s], 2 * (A_BYTES + B_BYTES));
-          if (A_MN) {
+          if (A_MN && gop.amn) {
+            tma_load_4d_pair(a_dst, &mapA, fb, 0, k0, m0 / 32, zc);
+          } else if (A_MN) {
 #pragma unroll
             for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d_pair(a_dst + j * 4096, &mapA, fb, m0 + 32 * j, k0, zc);
           } else {
             tma_load_3d_pair(a_dst, &mapA, fb, k0, m0, zc);
           }
           const int nb = n0 + (int)rank * (BN / 2);
-          if (B_MN) {
+          if (B_MN && gop.bmn) {
+            tma_load_4d_pair(b_dst, &mapB, fb, 0, k0, nb / 32, zc);
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_3d_pair(b_dst + j * 4096, &mapB, fb, nb + 32 * j, k0, zc);
           } else {
@@ -835,15 +862,13 @@ __global__ void __launch_bounds__(320, 1)
         if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
         if (gop.a) {
         } else if (A_MN) {
-#pragma unroll
-          for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
+          load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, zc);
         } else {
           tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
         }
         if (gop.b) {
         } else if (B_MN) {
-#pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
+          load_mn(b_dst, &mapB, &full[s], gop.bmn, BN / 32, n0, k0, zc);
         } else {
           tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
         }
@@ -1181,24 +1206,20 @@ __global__ void __launch_bounds__(64 + 32 * EW + PCfg<BN, BLO, MODE>::CONV_THREA
           if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
           if (gop.a) {
           } else if (A_MN) {
-#pragma unroll
-            for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d(a_dst + j * 4096, &mapA, &full[s], m0 + 32 * j, k0, zc);
+            load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, zc);
           } else {
             tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
           }
           if (gop.b) {
           } else if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 32; ++j) tma_load_3d(b_dst + j * 4096, &mapB, &full[s], n0 + 32 * j, k0, zc);
+            load_mn(b_dst, &mapB, &full[s], gop.bmn, BN / 32, n0, k0, zc);
           } else {
             tma_load_3d(b_dst, &mapB, &full[s], k0, n0, zc);
           }
           if (BLO) {
             const uint32_t l_dst = b_dst + B_BYTES;
             if (B_MN) {
-#pragma unroll
-              for (int j = 0; j < BN / 32; ++j)
-                tma_load_3d(l_dst + j * 4096, &mapB2, &full[s], n0 + 32 * j, k0, zc);
+              load_mn(l_dst, &mapB2, &full[s], gop.bmn, BN / 32, n0, k0, zc);
             } else {
               tma_load_3d(l_dst, &mapB2, &full[s], k0, n0, zc);
             }
