@@ -215,7 +215,7 @@ def run_reference(args) -> None:
         threadpool_limits(os.cpu_count() or 1)
     except Exception:  # pragma: no cover - the environment variables already ask for it
         pass
-    wl = workloads.WORKLOADS[args.workload]()
+    wl = make_workload(workloads, args)
     step = _cpu_step_fn(wl)
     # the whole run (warm-up + timed) stays near two minutes of host time
     sample, _ = _sample_rows(wl, step, 120.0 / (args.steps + args.warmup))
@@ -246,6 +246,14 @@ def run_reference(args) -> None:
     print(json.dumps(line))
 
 
+def make_workload(workloads, args):
+    """The workload at its configured size, or at --global-batch."""
+    if not args.global_batch:
+        return workloads.WORKLOADS[args.workload]()
+    key = "minibatch" if args.workload == "ppo" else "batch"
+    return workloads.WORKLOADS[args.workload](**{key: args.global_batch})
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -258,6 +266,9 @@ def main() -> None:
     parser.add_argument("--cpu-budget", type=float, default=15.0)
     parser.add_argument("--bucket-mb", type=float, default=2.0,
                         help="gradient all-reduce bucket size when N > 1")
+    parser.add_argument("--global-batch", type=int, default=0,
+                        help="override the workload's global batch (PPO: the minibatch); with --gpus 1 "
+                             "at the N-GPU per-rank batch it times the same per-GPU work without the exchange")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -279,7 +290,7 @@ def main() -> None:
     from tynx_b200.distributed import init_data_parallel, shard
 
     tx.set_math_mode(args.math)
-    wl = workloads.WORKLOADS[args.workload]()
+    wl = make_workload(workloads, args)
     per_rank = wl.batch // world
     rows = shard(wl.batch, world, rank)
     ctx = _core.context()
