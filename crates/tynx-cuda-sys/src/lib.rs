@@ -61,6 +61,13 @@ pub const TX_UN_SQRT: c_int = 8;
 pub const TX_UN_ABS: c_int = 9;
 pub const TX_UN_SCALE: c_int = 10;
 pub const TX_UN_POW: c_int = 11;
+pub const TX_UN_ERF: c_int = 12;
+pub const TX_UN_LEAKYRELU: c_int = 13;
+pub const TX_UN_SOFTPLUS: c_int = 14;
+pub const TX_UN_ELU: c_int = 15;
+pub const TX_UN_HARDSIGMOID: c_int = 16;
+pub const TX_UN_SOFTSIGN: c_int = 17;
+pub const TX_UN_RECIPROCAL: c_int = 18;
 pub const TX_BIN_ADD: c_int = 0;
 pub const TX_BIN_SUB: c_int = 1;
 pub const TX_BIN_MUL: c_int = 2;
@@ -102,6 +109,15 @@ pub const TX_OP_PRELU: c_int = 29;
 pub const TX_OP_BATCHNORM: c_int = 30;
 pub const TX_OP_GROUPNORM: c_int = 31;
 pub const TX_OP_MAXPOOL: c_int = 32;
+pub const TX_OP_UNARY: c_int = 33;
+pub const TX_OP_BINARY: c_int = 34;
+pub const TX_OP_CONCAT: c_int = 35;
+pub const TX_OP_SLICE: c_int = 36;
+pub const TX_OP_SPLIT: c_int = 37;
+pub const TX_OP_EXPAND: c_int = 38;
+pub const TX_OP_AVGPOOL: c_int = 39;
+pub const TX_OP_REDUCEMAX: c_int = 40;
+pub const TX_OP_REDUCEMIN: c_int = 41;
 pub const TX_VAL_INPUT: c_int = 0;
 pub const TX_VAL_PARAM: c_int = 1;
 pub const TX_VAL_CONST: c_int = 2;
@@ -263,6 +279,8 @@ extern "C" {
     pub fn tx_prelu_bwd(ctx: *mut tx_ctx, d_x: *const f32, d_slope: *const f32, slope_strides: *const i64, d_dy: *const f32, d_dx: *mut f32, d_dslope_full: *mut f32, shape: *const i64, ndim: c_int, accumulate_dx: c_int) -> c_int;
     pub fn tx_maxpool2d_fwd(ctx: *mut tx_ctx, d_x: *const f32, d_y: *mut f32, d_argmax: *mut i32, planes: i64, H: i64, W: i64, geom: *const i64) -> c_int;
     pub fn tx_maxpool2d_bwd(ctx: *mut tx_ctx, d_dy: *const f32, d_argmax: *const i32, d_dx: *mut f32, planes: i64, H: i64, W: i64, geom: *const i64, accumulate: c_int) -> c_int;
+    pub fn tx_avgpool2d_fwd(ctx: *mut tx_ctx, d_x: *const f32, d_y: *mut f32, planes: i64, H: i64, W: i64, geom: *const i64, count_include_pad: c_int) -> c_int;
+    pub fn tx_avgpool2d_bwd(ctx: *mut tx_ctx, d_dy: *const f32, d_dx: *mut f32, planes: i64, H: i64, W: i64, geom: *const i64, count_include_pad: c_int, accumulate: c_int) -> c_int;
     pub fn tx_attention_fwd(ctx: *mut tx_ctx, d_q: *const f32, d_k: *const f32, d_v: *const f32, ld_in: i64, d_out: *mut f32, ld_out: i64, batch: i64, seq: i64, heads: i64, head_dim: i64, scale: f32, flags: c_int) -> c_int;
     pub fn tx_attention_bwd(ctx: *mut tx_ctx, d_q: *const f32, d_k: *const f32, d_v: *const f32, ld_in: i64, d_dout: *const f32, ld_dout: i64, d_dq: *mut f32, d_dk: *mut f32, d_dv: *mut f32, ld_grad: i64, batch: i64, seq: i64, heads: i64, head_dim: i64, scale: f32, flags: c_int) -> c_int;
     pub fn tx_ppo_loss_fwd(ctx: *mut tx_ctx, d_logits: *const f32, rows: i64, cols: i64, d_values: *const f32, d_actions: *const i64, d_old_log_prob: *const f32, d_advantages: *const f32, d_returns: *const f32, clip: f32, value_coef: f32, entropy_coef: f32, d_loss: *mut f32) -> c_int;

@@ -203,7 +203,9 @@ enum {
   TX_UN_NEG = 0, TX_UN_EXP = 1, TX_UN_LOG = 2, TX_UN_RELU = 3, TX_UN_TANH = 4,
   TX_UN_GELU = 5, TX_UN_SIGMOID = 6, TX_UN_CLAMP = 7, TX_UN_SQRT = 8, TX_UN_ABS = 9,
   TX_UN_SCALE = 10, /* y = a*x + b */
-  TX_UN_POW = 11    /* y = x^a */
+  TX_UN_POW = 11,   /* y = x^a */
+  TX_UN_ERF = 12, TX_UN_LEAKYRELU = 13 /* slope a */, TX_UN_SOFTPLUS = 14, TX_UN_ELU = 15 /* alpha a */,
+  TX_UN_HARDSIGMOID = 16 /* max(0, min(1, a*x + b)) */, TX_UN_SOFTSIGN = 17, TX_UN_RECIPROCAL = 18
 };
 int tx_unary(tx_ctx *ctx, int op, const float *d_x, float *d_y, int64_t n, float a, float b);
 /* dx (+)= dy * op'(x or y).  `src` is y for EXP/TANH/SIGMOID/RELU, x otherwise. */
@@ -323,6 +325,14 @@ int tx_maxpool2d_fwd(tx_ctx *ctx, const float *d_x, float *d_y, int32_t *d_argma
                      int64_t H, int64_t W, const int64_t *geom);
 int tx_maxpool2d_bwd(tx_ctx *ctx, const float *d_dy, const int32_t *d_argmax, float *d_dx,
                      int64_t planes, int64_t H, int64_t W, const int64_t *geom, int accumulate);
+/* ONNX AveragePool over [planes][H][W]: geom as tx_maxpool2d_fwd followed by
+ * the bottom and right padding; the divisor counts the taps inside the input,
+ * or with count_include_pad inside the padded input.  replaces: the
+ * AveragePool arm of crates/tynx/src/interpreter/pooling.rs. */
+int tx_avgpool2d_fwd(tx_ctx *ctx, const float *d_x, float *d_y, int64_t planes, int64_t H, int64_t W,
+                     const int64_t *geom, int count_include_pad);
+int tx_avgpool2d_bwd(tx_ctx *ctx, const float *d_dy, float *d_dx, int64_t planes, int64_t H, int64_t W,
+                     const int64_t *geom, int count_include_pad, int accumulate);
 
 /* Fused multi-head attention over the merged layout: q, k, v, out (and dout,
  * dq, dk, dv) are [batch * seq, ld] row-major with head h in columns
@@ -423,7 +433,19 @@ enum {
   TX_OP_EXP, TX_OP_LOG, TX_OP_NEG, TX_OP_SOFTMAX, TX_OP_LOGSOFTMAX, TX_OP_REDUCEMEAN,
   TX_OP_REDUCESUM, TX_OP_GAP, TX_OP_RESHAPE, TX_OP_TRANSPOSE, TX_OP_FLATTEN,
   TX_OP_SQUEEZE, TX_OP_UNSQUEEZE, TX_OP_IDENTITY, TX_OP_CLIP, TX_OP_PRELU,
-  TX_OP_BATCHNORM, TX_OP_GROUPNORM, TX_OP_MAXPOOL
+  TX_OP_BATCHNORM, TX_OP_GROUPNORM, TX_OP_MAXPOOL,
+  /* iattr[0] a TX_UN_* code, fattr[0..1] its a, b: Sqrt, Abs, Reciprocal, Erf,
+   * LeakyRelu, Softplus, Elu, HardSigmoid, Softsign, Pow by a constant */
+  TX_OP_UNARY,
+  /* iattr[0] TX_BIN_MAX / MIN / POW, broadcasting (Max, Min, Pow) */
+  TX_OP_BINARY,
+  TX_OP_CONCAT,     /* iattr[0] axis; up to 6 inputs */
+  TX_OP_SLICE,      /* ints: n_axes, axes[n], starts[n], ends[n], steps[n] (n <= 3) */
+  TX_OP_SPLIT,      /* iattr[0] axis; ints: the outputs' sizes (up to 3 outputs) */
+  TX_OP_EXPAND,     /* ints: the target shape (numpy broadcasting) */
+  TX_OP_AVGPOOL,    /* as TX_OP_MAXPOOL; iattr[2] count_include_pad */
+  TX_OP_REDUCEMAX,  /* ints: axes (none: all); iattr[0] keepdims; inference only */
+  TX_OP_REDUCEMIN
 };
 enum { TX_VAL_INPUT = 0, TX_VAL_PARAM = 1, TX_VAL_CONST = 2, TX_VAL_ACT = 3 };
 enum { TX_DT_F32 = 0, TX_DT_I64 = 1 };

@@ -662,7 +662,230 @@ def run_op(op, vals: list) -> list:
         return [group_norm(x, vals[1], vals[2], int(a["num_groups"]), a["epsilon"])]
     if t == "MaxPool":
         return [max_pool(x, a)]
+    if t in _UNARY_RULES:
+        return [_unary(x, t, a)]
+    if t == "Pow":
+        if vals[1].data.size == 1:
+            return [power(x, float(vals[1].data.reshape(-1)[0]))]
+        return [pow_(x, vals[1])]
+    if t in ("Max", "Min"):
+        out = vals[0]
+        for v in vals[1:]:
+            out = maximum(out, v) if t == "Max" else minimum(out, v)
+        return [out]
+    if t == "Concat":
+        return [concat(vals, a["axis"])]
+    if t == "Slice":
+        if len(vals) > 1:
+            starts, ends = _const_ints(vals[1]), _const_ints(vals[2])
+            axes = _const_ints(vals[3]) if len(vals) > 3 and vals[3] is not None else list(range(len(starts)))
+            steps = _const_ints(vals[4]) if len(vals) > 4 and vals[4] is not None else [1] * len(starts)
+        else:
+            starts, ends = list(a["starts"]), list(a["ends"])
+            axes = list(a.get("axes") or range(len(starts)))
+            steps = [1] * len(starts)
+        return [slice_(x, starts, ends, axes, steps)]
+    if t == "Split":
+        sizes = a.get("split") or (_const_ints(vals[1]) if len(vals) > 1 and vals[1] is not None else None)
+        axis = a["axis"] % x.data.ndim
+        if not sizes:
+            n_out = len(op.outputs)
+            part = -(-x.shape[axis] // n_out)
+            sizes = [min(part, x.shape[axis] - part * i) for i in range(n_out)]
+        outs, at = [], 0
+        for size in sizes:
+            outs.append(slice_(x, [at], [at + size], [axis], [1]))
+            at += size
+        return outs
+    if t == "Expand":
+        target = _const_ints(vals[1])
+        shape = np.broadcast_shapes(tuple(x.shape), tuple(target))
+        return [expand(x, shape)]
+    if t == "AveragePool":
+        return [avg_pool(x, a)]
+    if t in ("ReduceMax", "ReduceMin", "GlobalMaxPool"):
+        if t == "GlobalMaxPool":
+            axes, keep = list(range(2, x.data.ndim)), True
+        else:
+            axes = a.get("axes") or _const_ints(vals[1] if len(vals) > 1 else None)
+            axes, keep = axes or list(range(x.data.ndim)), bool(a["keepdims"])
+        return [extremum(x, axes, keep, t != "ReduceMin")]
+    if t == "Dropout":
+        return [x]
     raise NotImplementedError(f"oracle has no rule for {t}")
+
+
+# -- the inference arms of interpreter/unary.rs, pow.rs, concat.rs, slice.rs,
+# split.rs, expand.rs, pooling.rs and reduction.rs (forward) with the
+# derivatives backward_support.rs validates --------------------------------------
+
+def _erf_np(x: np.ndarray) -> np.ndarray:
+    return np.vectorize(math.erf, otypes=[np.float64])(x)
+
+
+def _unary_leaky(x, a):
+    alpha = F32(a["alpha"])
+    return np.where(x >= 0, x, alpha * x), np.where(x >= 0, F32(1), alpha)
+
+
+def _unary_softplus(x, a):
+    xd = x.astype(np.float64)
+    y = np.where(xd > 20, xd, np.log1p(np.exp(np.minimum(xd, 20))))
+    return y, 1.0 / (1.0 + np.exp(-xd))
+
+
+def _unary_elu(x, a):
+    alpha = float(a["alpha"])
+    xd = x.astype(np.float64)
+    return np.where(xd > 0, xd, alpha * (np.exp(xd) - 1)), np.where(xd > 0, 1.0, alpha * np.exp(xd))
+
+
+def _unary_hardsigmoid(x, a):
+    al, be = F32(a["alpha"]), F32(a["beta"])
+    t = al * x + be
+    return np.clip(t, 0, 1), np.where((t > 0) & (t < 1), al, F32(0))
+
+
+def _unary_softsign(x, a):
+    d = F32(1) + np.abs(x)
+    return x / d, F32(1) / (d * d)
+
+
+_UNARY_RULES = {
+    "Sqrt": lambda x, a: (np.sqrt(x), F32(0.5) / np.sqrt(x)),
+    "Abs": lambda x, a: (np.abs(x), np.sign(x)),
+    "Reciprocal": lambda x, a: (F32(1) / x, -F32(1) / (x * x)),
+    "Erf": lambda x, a: (_erf_np(x.astype(np.float64)), 2.0 / math.sqrt(math.pi) * np.exp(-x.astype(np.float64) ** 2)),
+    "LeakyRelu": _unary_leaky,
+    "Softplus": _unary_softplus,
+    "Elu": _unary_elu,
+    "HardSigmoid": _unary_hardsigmoid,
+    "Softsign": _unary_softsign,
+}
+
+
+def _unary(x: T, t: str, a: dict) -> T:
+    y, dy = _UNARY_RULES[t](x.data, a)
+    y, dy = np.asarray(y, dtype=F32), np.asarray(dy, dtype=F32)
+    return _node(y, (x,), lambda g: (g * dy,))
+
+
+def pow_(a: T, b: T) -> T:
+    out = np.power(a.data, b.data).astype(F32)
+    return _node(out, (a, b),
+                 lambda g: (_unbroadcast(g * b.data * np.power(a.data, b.data - F32(1)), a.shape),
+                            _unbroadcast(g * out * np.log(a.data), b.shape)))
+
+
+def concat(vals: list, axis: int) -> T:
+    axis = axis % vals[0].data.ndim
+    out = np.concatenate([v.data for v in vals], axis=axis).astype(F32)
+    bounds = np.cumsum([0] + [v.shape[axis] for v in vals])
+
+    def back(g):
+        return tuple(np.take(g, np.arange(bounds[i], bounds[i + 1]), axis=axis) for i in range(len(vals)))
+
+    return _node(out, tuple(vals), back)
+
+
+def slice_(x: T, starts, ends, axes, steps) -> T:
+    index = [slice(None)] * x.data.ndim
+    for s, e, ax, st in zip(starts, ends, axes, steps):
+        ax = ax % x.data.ndim
+        dim = x.shape[ax]
+        s, e = int(s), int(e)
+        if s < 0:
+            s += dim
+        if e < 0:
+            e += dim
+        if st > 0:
+            s, e = min(max(s, 0), dim), min(max(e, 0), dim)
+        else:
+            s, e = min(max(s, 0), dim - 1), min(max(e, -1), dim - 1)
+        index[ax] = slice(s, e if e >= 0 else None, int(st))
+    index = tuple(index)
+    out = np.ascontiguousarray(x.data[index])
+
+    def back(g):
+        dx = np.zeros(x.shape, dtype=F32)
+        dx[index] = g
+        return (dx,)
+
+    return _node(out, (x,), back)
+
+
+def avg_pool(x: T, a: dict) -> T:
+    """AveragePool: the mean of each window's taps inside the input (with
+    count_include_pad, of those inside the explicitly padded input)."""
+    k = list(a["kernel_shape"])
+    st, dil, pads = list(a["strides"]), list(a["dilations"]), list(a["pads"])
+    data = x.data
+    one_d = len(k) == 1
+    if one_d:
+        data = data[:, :, None, :]
+        k, st, dil, pads = [1] + k, [1] + st, [1] + dil, [0, pads[0], 0, pads[1]]
+    n, c, h, w = data.shape
+    auto, ceil = a.get("auto_pad", "NOTSET"), bool(a.get("ceil_mode", 0))
+    pt, oh = _pool_axis(h, k[0], st[0], dil[0], pads[0], pads[2], auto, ceil)
+    pl, ow = _pool_axis(w, k[1], st[1], dil[1], pads[1], pads[3], auto, ceil)
+    pb = pads[2] if auto == "NOTSET" else max((oh - 1) * st[0] + (k[0] - 1) * dil[0] + 1 - h - pt, 0)
+    pr = pads[3] if auto == "NOTSET" else max((ow - 1) * st[1] + (k[1] - 1) * dil[1] + 1 - w - pl, 0)
+    if auto == "VALID":
+        pb = pr = 0
+    inc = bool(a.get("count_include_pad", 0))
+    total = np.zeros((n, c, oh, ow), dtype=np.float64)
+    rows = np.arange(oh) * st[0] - pt
+    cols = np.arange(ow) * st[1] - pl
+    lo_h, hi_h = (-pt, h + pb) if inc else (0, h)
+    lo_w, hi_w = (-pl, w + pr) if inc else (0, w)
+    cnt_h = sum(((rows + kh * dil[0] >= lo_h) & (rows + kh * dil[0] < hi_h)).astype(np.int64) for kh in range(k[0]))
+    cnt_w = sum(((cols + kw * dil[1] >= lo_w) & (cols + kw * dil[1] < hi_w)).astype(np.int64) for kw in range(k[1]))
+    cnt = (cnt_h[:, None] * cnt_w[None, :]).astype(np.float64)
+    taps = []
+    for kh in range(k[0]):
+        hh = rows + kh * dil[0]
+        vh = (hh >= 0) & (hh < h)
+        for kw in range(k[1]):
+            ww = cols + kw * dil[1]
+            vw = (ww >= 0) & (ww < w)
+            valid = vh[:, None] & vw[None, :]
+            tap = data[:, :, np.clip(hh, 0, h - 1)[:, None], np.clip(ww, 0, w - 1)[None, :]]
+            total += np.where(valid, tap, 0)
+            taps.append((np.clip(hh, 0, h - 1), np.clip(ww, 0, w - 1), valid))
+    safe = np.where(cnt > 0, cnt, 1)
+    out = np.where(cnt > 0, total / safe, 0).astype(F32)
+
+    def back(g):
+        g4 = (g[:, :, None, :] if one_d else g).astype(np.float64) / safe
+        dx = np.zeros((n, c, h, w), dtype=np.float64)
+        for hh, ww, valid in taps:
+            contrib = np.where(valid & (cnt > 0), g4, 0)
+            np.add.at(dx, (slice(None), slice(None), hh[:, None], ww[None, :]), contrib)
+        dx = dx.astype(F32)
+        return (dx[:, :, 0, :] if one_d else dx,)
+
+    return _node(np.ascontiguousarray(out[:, :, 0, :] if one_d else out), (x,), back)
+
+
+def extremum(x: T, axes, keepdims: bool, is_max: bool) -> T:
+    """ReduceMax / ReduceMin; the gradient goes to the first extremal element."""
+    nd = x.data.ndim
+    axes = sorted(ax % nd for ax in axes)
+    keep = [i for i in range(nd) if i not in axes]
+    moved = np.transpose(x.data, keep + axes)
+    flat = moved.reshape(moved.shape[:len(keep)] + (-1,))
+    idx = (np.argmax if is_max else np.argmin)(flat, axis=-1)
+    val = np.take_along_axis(flat, idx[..., None], axis=-1)[..., 0].astype(F32)
+    out_shape = [1 if i in axes else x.shape[i] for i in range(nd)] if keepdims else [x.shape[i] for i in keep]
+
+    def back(g):
+        gf = np.zeros(flat.shape, dtype=F32)
+        np.put_along_axis(gf, idx[..., None], np.asarray(g, dtype=F32).reshape(idx.shape)[..., None], axis=-1)
+        dx_moved = gf.reshape(moved.shape)
+        inv = np.argsort(keep + axes)
+        return (np.ascontiguousarray(np.transpose(dx_moved, inv)),)
+
+    return _node(val.reshape(out_shape), (x,), back)
 
 
 def sqrt_(a: T) -> T:

@@ -37,13 +37,15 @@ MAX_DIMS = 8
 ACT = {"none": 0, "relu": 1, "tanh": 2, "gelu": 3}
 TX_GEMM_A_TF32, TX_GEMM_B_TF32, TX_GEMM_ROUND_OUT, TX_GEMM_EXACT = 1, 2, 4, 8
 UN = {"neg": 0, "exp": 1, "log": 2, "relu": 3, "tanh": 4, "gelu": 5, "sigmoid": 6, "clamp": 7,
-      "sqrt": 8, "abs": 9, "scale": 10, "pow": 11}
+      "sqrt": 8, "abs": 9, "scale": 10, "pow": 11, "erf": 12, "leakyrelu": 13, "softplus": 14, "elu": 15,
+      "hardsigmoid": 16, "softsign": 17, "reciprocal": 18}
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "min": 4, "max": 5, "le": 6, "ge": 7, "pow": 8}
 OP = {name: i + 1 for i, name in enumerate([
     "GEMM", "MATMUL", "CONV", "GATHER", "LAYERNORM", "ADD", "SUB", "MUL", "DIV", "RELU", "TANH",
     "GELU", "SIGMOID", "EXP", "LOG", "NEG", "SOFTMAX", "LOGSOFTMAX", "REDUCEMEAN", "REDUCESUM",
     "GAP", "RESHAPE", "TRANSPOSE", "FLATTEN", "SQUEEZE", "UNSQUEEZE", "IDENTITY", "CLIP", "PRELU",
-    "BATCHNORM", "GROUPNORM", "MAXPOOL"])}
+    "BATCHNORM", "GROUPNORM", "MAXPOOL", "UNARY", "BINARY", "CONCAT", "SLICE", "SPLIT", "EXPAND",
+    "AVGPOOL", "REDUCEMAX", "REDUCEMIN"])}
 VAL_INPUT, VAL_PARAM, VAL_CONST, VAL_ACT = 0, 1, 2, 3
 DT_F32, DT_I64 = 0, 1
 
@@ -158,6 +160,8 @@ SIGNATURES = {
     "tx_prelu_bwd": [_vp, _vp, _vp, _p64, _vp, _vp, _vp, _p64, _i32, _i32],
     "tx_maxpool2d_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64],
     "tx_maxpool2d_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _p64, _i32],
+    "tx_avgpool2d_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _p64, _i32],
+    "tx_avgpool2d_bwd": [_vp, _vp, _vp, _i64, _i64, _i64, _p64, _i32, _i32],
     "tx_attention_fwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _f, _i32],
     "tx_attention_bwd": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                          _f, _i32],

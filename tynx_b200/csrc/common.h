@@ -130,6 +130,18 @@ int nd_copy(tx_ctx *ctx, const void *src, const int64_t *ss, void *out, const in
             int elem_bytes, float scale, int acc);
 int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_t *out_shape, int ndim,
               float *y, float scale, int acc);
+// out[os] (+)= src (contiguous over `shape`): a strided destination.
+int nd_scatter(tx_ctx *ctx, const float *src, float *out, const int64_t *os, const int64_t *shape, int ndim,
+               int acc);
+// out (contiguous over `shape`) = dy * d(A op B)/d(operand `which`) for op MAX / MIN / POW.
+int nd_binary_grad(tx_ctx *ctx, int op, int which, const float *A, const int64_t *sa, const float *B,
+                   const int64_t *sb, const float *dy, float *out, const int64_t *shape, int ndim);
+// y[o][i] = max / min over r of x[o][r][i] (contiguous x), arg (or null) the
+// first r attaining it; the backward routes dy there
+int reduce_maxmin(tx_ctx *ctx, const float *x, float *y, int32_t *arg, int64_t outer, int64_t red, int64_t inner,
+                  bool is_max);
+int reduce_maxmin_bwd(tx_ctx *ctx, const float *dy, const int32_t *arg, float *dx, int64_t outer, int64_t red,
+                      int64_t inner, int acc);
 
 // Softmax over rows; y32 (may be null, not with log): a second copy of y
 // rounded to TF32 for the contractions that read it, while the backward

@@ -653,9 +653,10 @@ int norm_axis(int64_t axis, int64_t rank) { return (int)(axis < 0 ? axis + rank 
 // crates/tynx/src/interpreter/spatial.rs:102-151 does (auto_pad, then the extra
 // end padding that ceil_mode needs, the last window starting inside the input
 // or its start padding); windows run over the -inf padded input.
-bool pool_geom(const tx_node_desc &d, int64_t H, int64_t W, int64_t geom[10]) {
+// geom: kh, kw, sh, sw, pt, pl, dh, dw, oh, ow, then the end padding pb, pr
+bool pool_geom(const tx_node_desc &d, int64_t H, int64_t W, int64_t geom[12]) {
   const int64_t in[2] = {H, W};
-  int64_t start[2], out[2];
+  int64_t start[2], out[2], endp[2];
   for (int a = 0; a < 2; ++a) {
     const int64_t k = d.ints[a], s = d.ints[2 + a], dil = d.ints[8 + a];
     if (k <= 0 || s <= 0 || dil <= 0) return false;
@@ -680,10 +681,102 @@ bool pool_geom(const tx_node_desc &d, int64_t H, int64_t W, int64_t geom[10]) {
     }
     start[a] = b;
     out[a] = o;
+    endp[a] = e;
   }
-  const int64_t g[10] = {d.ints[0], d.ints[1], d.ints[2], d.ints[3], start[0], start[1],
-                         d.ints[8], d.ints[9], out[0], out[1]};
-  for (int i = 0; i < 10; ++i) geom[i] = g[i];
+  const int64_t g[12] = {d.ints[0], d.ints[1], d.ints[2], d.ints[3], start[0], start[1],
+                         d.ints[8], d.ints[9], out[0], out[1], endp[0], endp[1]};
+  for (int i = 0; i < 12; ++i) geom[i] = g[i];
+  return true;
+}
+
+// row-major element strides of a contiguous tensor of shape s
+void cstrides(const Shape &s, int64_t *st) {
+  int64_t acc = 1;
+  for (int64_t i = (int64_t)s.size() - 1; i >= 0; --i) {
+    st[i] = acc;
+    acc *= s[i];
+  }
+}
+
+// ONNX Slice on x: per axis the first element, the step and the count
+// (negative starts / ends count from the end; both are clamped as the
+// operator specifies for the step's sign).  ints: n, axes[n], starts[n],
+// ends[n], steps[n].
+bool slice_params(const tx_node_desc &d, const Shape &x, int64_t *first, int64_t *step, Shape &out) {
+  const int n = (int)d.ints[0];
+  const int64_t r = (int64_t)x.size();
+  out = x;
+  for (int64_t i = 0; i < r; ++i) {
+    first[i] = 0;
+    step[i] = 1;
+  }
+  for (int k = 0; k < n; ++k) {
+    int64_t a = d.ints[1 + k];
+    if (a < 0) a += r;
+    if (a < 0 || a >= r) return false;
+    const int64_t D = x[a];
+    int64_t st = d.ints[1 + n + k], en = d.ints[1 + 2 * n + k], t = d.ints[1 + 3 * n + k];
+    if (t == 0) return false;
+    if (st < 0) st += D;
+    if (en < 0) en += D;
+    int64_t len;
+    if (t > 0) {
+      st = st < 0 ? 0 : st > D ? D : st;
+      en = en < 0 ? 0 : en > D ? D : en;
+      len = en > st ? (en - st + t - 1) / t : 0;
+    } else {
+      st = st < 0 ? 0 : st > D - 1 ? D - 1 : st;
+      en = en < -1 ? -1 : en > D - 1 ? D - 1 : en;
+      len = st > en ? (st - en + (-t) - 1) / (-t) : 0;
+    }
+    first[a] = st;
+    step[a] = t;
+    out[a] = len;
+  }
+  return true;
+}
+
+// [outer, reduced, inner] of a max / min reduction over `axes` (ints; none:
+// all), when the reduced axes form one block after dropping unit axes
+// the reduced axes of a max / min reduction: ints (none: all), or with
+// iattr[1] the spatial axes 2.. (GlobalMaxPool)
+bool maxmin_axes(const tx_node_desc &d, int64_t r, std::vector<bool> &rd) {
+  rd.assign(r, d.n_ints == 0 && !d.iattr[1]);
+  if (d.iattr[1]) {
+    for (int64_t i = 2; i < r; ++i) rd[i] = true;
+    return true;
+  }
+  for (int i = 0; i < d.n_ints; ++i) {
+    int64_t a = d.ints[i];
+    if (a < 0) a += r;
+    if (a < 0 || a >= r) return false;
+    rd[a] = true;
+  }
+  return true;
+}
+
+bool maxmin_block(const tx_node_desc &d, const Shape &x, int64_t *outer, int64_t *red, int64_t *inner) {
+  const int64_t r = (int64_t)x.size();
+  std::vector<bool> rd;
+  if (!maxmin_axes(d, r, rd)) return false;
+  int first = -1, last = -1;
+  for (int64_t i = 0; i < r; ++i)
+    if (rd[i] && x[i] != 1) {
+      if (first < 0) first = (int)i;
+      last = (int)i;
+    }
+  *outer = *red = *inner = 1;
+  if (first < 0) {  // only unit axes reduced: a copy
+    for (int64_t i = 0; i < r; ++i) *outer *= x[i];
+    return true;
+  }
+  for (int i = first; i <= last; ++i)
+    if (!rd[i] && x[i] != 1) return false;
+  for (int64_t i = 0; i < r; ++i) {
+    if (i < first) *outer *= x[i];
+    else if (i <= last) *red *= x[i];
+    else *inner *= x[i];
+  }
   return true;
 }
 
@@ -821,11 +914,77 @@ int infer_node(tx_graph *g, const GNode &n, std::vector<Shape> &S) {
       out = x;
       return TX_OK;
     }
+    case TX_OP_UNARY:
+      if (d.iattr[0] < TX_UN_NEG || d.iattr[0] > TX_UN_RECIPROCAL) return fail(g, TX_ERR_INVALID, "unknown unary op");
+      out = in(0);
+      return TX_OK;
+    case TX_OP_BINARY:
+      if (d.iattr[0] != TX_BIN_MAX && d.iattr[0] != TX_BIN_MIN && d.iattr[0] != TX_BIN_POW)
+        return fail(g, TX_ERR_INVALID, "unknown binary op");
+      if (!broadcast_shapes(in(0), in(1), out))
+        return fail(g, TX_ERR_SHAPE, "cannot broadcast " + shape_str(in(0)) + " with " + shape_str(in(1)));
+      return TX_OK;
+    case TX_OP_CONCAT: {
+      const Shape &x = in(0);
+      const int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+      out = x;
+      for (int k = 1; k < d.n_in; ++k) {
+        const Shape &o = in(k);
+        if (o.size() != x.size()) return fail(g, TX_ERR_SHAPE, "Concat inputs differ in rank");
+        for (size_t i = 0; i < x.size(); ++i)
+          if ((int)i != ax && o[i] != x[i])
+            return fail(g, TX_ERR_SHAPE, "Concat inputs " + shape_str(x) + " and " + shape_str(o) + " differ off axis");
+        out[ax] += o[ax];
+      }
+      return TX_OK;
+    }
+    case TX_OP_SLICE: {
+      int64_t first[TX_MAX_DIMS], step[TX_MAX_DIMS];
+      if (!slice_params(d, in(0), first, step, out)) return fail(g, TX_ERR_SHAPE, "Slice axes or steps out of range");
+      return TX_OK;
+    }
+    case TX_OP_SPLIT: {
+      const Shape &x = in(0);
+      const int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+      if (d.n_ints && d.n_ints != d.n_out) return fail(g, TX_ERR_SHAPE, "Split sizes and outputs differ in number");
+      const int64_t part = (x[ax] + d.n_out - 1) / d.n_out;  // equal parts, the last one smaller
+      int64_t total = 0;
+      for (int k = 0; k < d.n_out; ++k) {
+        Shape o = x;
+        o[ax] = d.n_ints ? d.ints[k] : std::min(part, x[ax] - total);
+        if (o[ax] < 0) return fail(g, TX_ERR_SHAPE, "Split sizes exceed the axis of " + shape_str(x));
+        total += o[ax];
+        S[d.out[k]] = o;
+      }
+      if (total != x[ax]) return fail(g, TX_ERR_SHAPE, "Split sizes do not add up to the axis of " + shape_str(x));
+      return TX_OK;
+    }
+    case TX_OP_EXPAND: {
+      Shape target(d.ints, d.ints + d.n_ints);
+      if (!broadcast_shapes(in(0), target, out))
+        return fail(g, TX_ERR_SHAPE, "cannot expand " + shape_str(in(0)) + " to " + shape_str(target));
+      return TX_OK;
+    }
+    case TX_OP_REDUCEMAX: case TX_OP_REDUCEMIN: {
+      const Shape &x = in(0);
+      int64_t o, rd, inn;
+      if (!maxmin_block(d, x, &o, &rd, &inn))
+        return fail(g, TX_ERR_UNSUPPORTED, "ReduceMax / ReduceMin over non-adjacent axes is not supported on CUDA");
+      std::vector<bool> red;
+      maxmin_axes(d, (int64_t)x.size(), red);
+      out.clear();
+      for (size_t i = 0; i < x.size(); ++i) {
+        if (!red[i]) out.push_back(x[i]);
+        else if (d.iattr[0]) out.push_back(1);
+      }
+      return TX_OK;
+    }
+    case TX_OP_AVGPOOL:
     case TX_OP_MAXPOOL: {
       const Shape &x = in(0);
       if (x.size() != 4 && x.size() != 3)
-        return fail(g, TX_ERR_UNSUPPORTED, "MaxPool on CUDA supports 1-D and 2-D pooling, got " + shape_str(x));
-      int64_t geom[10];
+        return fail(g, TX_ERR_UNSUPPORTED, "pooling on CUDA supports 1-D and 2-D windows, got " + shape_str(x));
+      int64_t geom[12];
       const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
       if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
       out = x;
@@ -1695,10 +1854,78 @@ struct Fwd {
         return tx_groupnorm_fwd(ctx, F(d.in[0]), F(d.in[1]), F(d.in[2]), F(yv), mean, sdev, N, C, L, groups,
                                 (float)d.fattr[0]);
       }
+      case TX_OP_UNARY:
+        return tx_unary(ctx, (int)d.iattr[0], F(d.in[0]), F(yv), ny, (float)d.fattr[0], (float)d.fattr[1]);
+      case TX_OP_BINARY: {
+        int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS];
+        bstrides(S(d.in[0]), y, sa);
+        bstrides(S(d.in[1]), y, sb);
+        return tx_binary(ctx, (int)d.iattr[0], F(d.in[0]), sa, F(d.in[1]), sb, F(yv), y.data(), (int)y.size());
+      }
+      case TX_OP_CONCAT: {
+        // each input into its slab of the output
+        const int ax = norm_axis(d.iattr[0], (int64_t)y.size());
+        int64_t ys[TX_MAX_DIMS];
+        cstrides(y, ys);
+        int64_t at = 0;
+        for (int k = 0; k < d.n_in; ++k) {
+          const Shape &xk = S(d.in[k]);
+          TX_TRY(nd_scatter(ctx, F(d.in[k]), F(yv) + at * ys[ax], ys, xk.data(), (int)xk.size(), 0));
+          at += xk[ax];
+        }
+        return TX_OK;
+      }
+      case TX_OP_SLICE: {
+        const Shape &x = S(d.in[0]);
+        int64_t first[TX_MAX_DIMS], step[TX_MAX_DIMS], xs[TX_MAX_DIMS], ss[TX_MAX_DIMS];
+        Shape o;
+        slice_params(d, x, first, step, o);
+        cstrides(x, xs);
+        int64_t base = 0;
+        for (size_t i = 0; i < x.size(); ++i) {
+          base += first[i] * xs[i];
+          ss[i] = step[i] * xs[i];
+        }
+        return nd_copy(ctx, F(d.in[0]) + base, ss, F(yv), y.data(), (int)y.size(), 4, 1.f, 0);
+      }
+      case TX_OP_SPLIT: {
+        const Shape &x = S(d.in[0]);
+        const int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+        int64_t xs[TX_MAX_DIMS];
+        cstrides(x, xs);
+        int64_t at = 0;
+        for (int k = 0; k < d.n_out; ++k) {
+          if (k > 0) TX_TRY(alloc_value(d.out[k]));
+          const Shape &ok = S(d.out[k]);
+          TX_TRY(nd_copy(ctx, F(d.in[0]) + at * xs[ax], xs, F(d.out[k]), ok.data(), (int)ok.size(), 4, 1.f, 0));
+          at += ok[ax];
+        }
+        return TX_OK;
+      }
+      case TX_OP_EXPAND: {
+        int64_t sx[TX_MAX_DIMS];
+        bstrides(S(d.in[0]), y, sx);
+        return nd_copy(ctx, F(d.in[0]), sx, F(yv), y.data(), (int)y.size(), 4, 1.f, 0);
+      }
+      case TX_OP_REDUCEMAX: case TX_OP_REDUCEMIN: {
+        int64_t o, rd, inn;
+        maxmin_block(d, S(d.in[0]), &o, &rd, &inn);
+        int32_t *arg = (int32_t *)tx_alloc_raw(ctx, ny * 4 + 4);
+        r->extra[ni] = arg;
+        if (!arg) return TX_ERR_OOM;
+        return reduce_maxmin(ctx, F(d.in[0]), F(yv), arg, o, rd, inn, d.op == TX_OP_REDUCEMAX);
+      }
+      case TX_OP_AVGPOOL: {
+        const Shape &x = S(d.in[0]);
+        const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
+        int64_t geom[12];
+        if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "AveragePool window larger than its padded input");
+        return tx_avgpool2d_fwd(ctx, F(d.in[0]), F(yv), x[0] * x[1], H, W, geom, (int)d.iattr[2]);
+      }
       case TX_OP_MAXPOOL: {
         const Shape &x = S(d.in[0]);
         const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
-        int64_t geom[10];
+        int64_t geom[12];
         if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
         int32_t *arg = (int32_t *)tx_alloc_raw(ctx, ny * 4 + 4);
         r->extra[ni] = arg;
@@ -2147,6 +2374,31 @@ struct Bwd {
     }
   }
 
+  // dX = the outputs' gradients in their slabs (zeros where an output has none)
+  int split_backward(int ni) {
+    const tx_node_desc &d = g->nodes[ni].d;
+    const int xv = d.in[0];
+    if (!needs[xv]) return TX_OK;
+    bool any = false;
+    for (int k = 0; k < d.n_out; ++k) any |= grad[d.out[k]] != nullptr;
+    if (!any) return TX_OK;
+    const Shape &x = S(xv);
+    const int ax = norm_axis(d.iattr[0], (int64_t)x.size());
+    int64_t xs[TX_MAX_DIMS];
+    cstrides(x, xs);
+    float *t; int acc;
+    TX_TRY(target(xv, &t, &acc));
+    if (!acc) TX_CUDA(ctx, cudaMemsetAsync(t, 0, numel_of(x) * 4, ctx->stream));
+    int64_t at = 0;
+    for (int k = 0; k < d.n_out; ++k) {
+      const Shape &ok = S(d.out[k]);
+      if (grad[d.out[k]]) TX_TRY(nd_scatter(ctx, grad[d.out[k]], t + at * xs[ax], xs, ok.data(), (int)ok.size(), 1));
+      at += ok[ax];
+    }
+    wrote(xv);
+    return TX_OK;
+  }
+
   // dX as one implicit GEMM per phase of the stride (see the implicit-GEMM
   // note above the kernels): A gathered from the channels-last dY with the
   // phase's tap shifts, B the taps' [C][OC] weight blocks, the output written
@@ -2485,6 +2737,7 @@ struct Bwd {
       case TX_OP_CONV: return conv_backward(ni);
       default: break;
     }
+    if (d.op == TX_OP_SPLIT) return split_backward(ni);
     int yv = d.out[0];
     float *dy = grad[yv];
     if (!dy) return TX_OK;
@@ -2630,11 +2883,95 @@ struct Bwd {
         if (needs[bv]) wrote(bv);
         return TX_OK;
       }
+      case TX_OP_UNARY: {
+        if (!needs[xv]) return TX_OK;
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        TX_TRY(tx_unary_bwd(ctx, (int)d.iattr[0], F(xv), dy, t, ny, (float)d.fattr[0], (float)d.fattr[1], acc));
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_BINARY: {
+        int64_t sa[TX_MAX_DIMS], sb[TX_MAX_DIMS];
+        bstrides(S(d.in[0]), y, sa);
+        bstrides(S(d.in[1]), y, sb);
+        for (int k = 0; k < 2; ++k) {
+          if (!needs[d.in[k]]) continue;
+          float *tmp = (float *)tx_alloc_raw(ctx, ny * 4 + 4);
+          if (!tmp) return TX_ERR_OOM;
+          int rc = nd_binary_grad(ctx, (int)d.iattr[0], k, F(d.in[0]), sa, F(d.in[1]), sb, dy, tmp, y.data(),
+                                  (int)y.size());
+          if (rc == TX_OK) rc = reduce_into(d.in[k], tmp, y, 1.f);
+          tx_free_raw(ctx, tmp);
+          TX_TRY(rc);
+        }
+        return TX_OK;
+      }
+      case TX_OP_CONCAT: {
+        const int ax = norm_axis(d.iattr[0], (int64_t)y.size());
+        int64_t ys[TX_MAX_DIMS];
+        cstrides(y, ys);
+        int64_t at = 0;
+        for (int k = 0; k < d.n_in; ++k) {
+          const Shape &xk = S(d.in[k]);
+          if (needs[d.in[k]]) {
+            float *t; int acc;
+            TX_TRY(target(d.in[k], &t, &acc));
+            TX_TRY(nd_copy(ctx, dy + at * ys[ax], ys, t, xk.data(), (int)xk.size(), 4, 1.f, acc));
+            wrote(d.in[k]);
+          }
+          at += xk[ax];
+        }
+        return TX_OK;
+      }
+      case TX_OP_SLICE: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        int64_t first[TX_MAX_DIMS], step[TX_MAX_DIMS], xs[TX_MAX_DIMS], ss[TX_MAX_DIMS];
+        Shape o;
+        slice_params(d, x, first, step, o);
+        cstrides(x, xs);
+        int64_t base = 0;
+        for (size_t i = 0; i < x.size(); ++i) {
+          base += first[i] * xs[i];
+          ss[i] = step[i] * xs[i];
+        }
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        if (!acc) TX_CUDA(ctx, cudaMemsetAsync(t, 0, numel_of(x) * 4, ctx->stream));
+        TX_TRY(nd_scatter(ctx, dy, t + base, ss, y.data(), (int)y.size(), 1));
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_EXPAND:
+        return needs[xv] ? reduce_into(xv, dy, y, 1.f) : TX_OK;
+      case TX_OP_REDUCEMAX: case TX_OP_REDUCEMIN: {
+        if (!needs[xv]) return TX_OK;
+        int64_t o, rd, inn;
+        maxmin_block(d, S(xv), &o, &rd, &inn);
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        TX_TRY(reduce_maxmin_bwd(ctx, dy, (const int32_t *)r->extra[ni], t, o, rd, inn, acc));
+        wrote(xv);
+        return TX_OK;
+      }
+      case TX_OP_AVGPOOL: {
+        if (!needs[xv]) return TX_OK;
+        const Shape &x = S(xv);
+        const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
+        int64_t geom[12];
+        if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "AveragePool window larger than its padded input");
+        float *t; int acc;
+        TX_TRY(target(xv, &t, &acc));
+        TX_TRY(tx_avgpool2d_bwd(ctx, dy, t, x[0] * x[1], H, W, geom, (int)d.iattr[2], acc));
+        wrote(xv);
+        return TX_OK;
+      }
       case TX_OP_MAXPOOL: {
         if (!needs[xv]) return TX_OK;
         const Shape &x = S(xv);
         const int64_t H = x.size() == 4 ? x[2] : 1, W = x.back();
-        int64_t geom[10];
+        int64_t geom[12];
         if (!pool_geom(d, H, W, geom)) return fail(g, TX_ERR_SHAPE, "MaxPool window larger than its padded input");
         float *t; int acc;
         TX_TRY(target(xv, &t, &acc));

@@ -59,6 +59,13 @@ __device__ __forceinline__ float unary_f(int op, float x, float a, float b) {
     case TX_UN_ABS: return fabsf(x);
     case TX_UN_SCALE: return a * x + b;
     case TX_UN_POW: return powf(x, a);
+    case TX_UN_ERF: return erff(x);
+    case TX_UN_LEAKYRELU: return x >= 0.f ? x : a * x;
+    case TX_UN_SOFTPLUS: return x > 20.f ? x : log1pf(expf(x));  // ln(1 + e^x), e^x beyond fp32 past 20
+    case TX_UN_ELU: return x > 0.f ? x : a * (expf(x) - 1.f);
+    case TX_UN_HARDSIGMOID: return fminf(fmaxf(a * x + b, 0.f), 1.f);
+    case TX_UN_SOFTSIGN: return x / (1.f + fabsf(x));
+    case TX_UN_RECIPROCAL: return 1.f / x;
   }
   return x;
 }
@@ -79,6 +86,19 @@ __device__ __forceinline__ float unary_grad(int op, float s, float a, float b) {
     case TX_UN_ABS: return s > 0.f ? 1.f : (s < 0.f ? -1.f : 0.f);
     case TX_UN_SCALE: return a;
     case TX_UN_POW: return a * powf(s, a - 1.f);
+    case TX_UN_ERF: return 1.1283791670955126f * expf(-s * s);  // 2 / sqrt(pi) e^(-x^2)
+    case TX_UN_LEAKYRELU: return s >= 0.f ? 1.f : a;
+    case TX_UN_SOFTPLUS: return 1.f / (1.f + expf(-s));
+    case TX_UN_ELU: return s > 0.f ? 1.f : a * expf(s);
+    case TX_UN_HARDSIGMOID: {
+      const float t = a * s + b;
+      return (t > 0.f && t < 1.f) ? a : 0.f;
+    }
+    case TX_UN_SOFTSIGN: {
+      const float d = 1.f + fabsf(s);
+      return 1.f / (d * d);
+    }
+    case TX_UN_RECIPROCAL: return -1.f / (s * s);
   }
   return 1.f;
 }
@@ -1069,7 +1089,7 @@ extern "C" int tx_fill_f32(tx_ctx *ctx, float *y, int64_t n, float v) {
 }
 
 extern "C" int tx_unary(tx_ctx *ctx, int op, const float *x, float *y, int64_t n, float a, float b) {
-  if (!ctx || op < 0 || op > TX_UN_POW) return TX_ERR_INVALID;
+  if (!ctx || op < 0 || op > TX_UN_RECIPROCAL) return TX_ERR_INVALID;
   if (n <= 0) return TX_OK;
   k_unary<<<grid_for((n + 3) / 4, 256), 256, 0, ctx->stream>>>(op, x, y, n, a, b);
   TX_LAUNCHED(ctx, "k_unary");
@@ -1078,7 +1098,7 @@ extern "C" int tx_unary(tx_ctx *ctx, int op, const float *x, float *y, int64_t n
 
 extern "C" int tx_unary_bwd(tx_ctx *ctx, int op, const float *s, const float *dy, float *dx,
                             int64_t n, float a, float b, int acc) {
-  if (!ctx || op < 0 || op > TX_UN_POW) return TX_ERR_INVALID;
+  if (!ctx || op < 0 || op > TX_UN_RECIPROCAL) return TX_ERR_INVALID;
   if (n <= 0) return TX_OK;
   k_unary_bwd<<<grid_for(n, 256), 256, 0, ctx->stream>>>(op, s, dy, dx, n, a, b, acc);
   TX_LAUNCHED(ctx, "k_unary_bwd");

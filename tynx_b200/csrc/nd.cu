@@ -428,3 +428,128 @@ int nd_reduce(tx_ctx *ctx, const float *x, const int64_t *in_shape, const int64_
   }
   return TX_OK;
 }
+
+// ---- scatter, broadcast max / min / pow gradients, max / min reductions ----------------
+// (Concat, Slice, Split and their gradients; Max / Min / Pow backward;
+// ReduceMax / ReduceMin / GlobalMaxPool, crates/tynx/src/interpreter/
+// reduction.rs and extrema.rs for the inference arms.)
+namespace {
+
+// out[off(i)] (+)= src[i]: a contiguous source into a strided destination
+template <typename I>
+__global__ void k_scatter_nd(const float *__restrict__ src, float *__restrict__ out, Nd c, I n, int acc) {
+  for (I i = blockIdx.x * (I)blockDim.x + threadIdx.x; i < n; i += (I)gridDim.x * blockDim.x) {
+    int64_t off[1];
+    offsets<I, 1>(c, i, off);
+    float *o = out + off[0];
+    *o = acc ? *o + src[i] : src[i];
+  }
+}
+
+// d out / d operand `which` of a broadcast MAX / MIN / POW, times dy, over the
+// output shape (the caller reduces it to the operand's shape).  Ties go to A,
+// as the forward takes A when a >= b (MAX) or a <= b (MIN).
+template <typename I>
+__global__ void k_binary_grad_nd(int op, int which, const float *__restrict__ A, const float *__restrict__ B,
+                                 const float *__restrict__ dy, float *__restrict__ out, Nd c, I n) {
+  for (I i = blockIdx.x * (I)blockDim.x + threadIdx.x; i < n; i += (I)gridDim.x * blockDim.x) {
+    int64_t off[2];
+    offsets<I, 2>(c, i, off);
+    const float a = A[off[0]], b = B[off[1]], g = dy[i];
+    float r = 0.f;
+    if (op == TX_BIN_MAX || op == TX_BIN_MIN) {
+      const bool take_a = op == TX_BIN_MAX ? a >= b : a <= b;
+      r = (which == 0) == take_a ? g : 0.f;
+    } else if (op == TX_BIN_POW) {
+      r = which == 0 ? g * b * powf(a, b - 1.f) : g * powf(a, b) * logf(a);
+    }
+    out[i] = r;
+  }
+}
+
+// y[o][i] = max (or min) over r of x[o][r][i], arg[o][i] = the first r that
+// attains it (a NaN wins at its first occurrence)
+__global__ void k_reduce_maxmin(const float *__restrict__ x, float *__restrict__ y, int32_t *__restrict__ arg,
+                                int64_t outer, int64_t red, int64_t inner, int is_max) {
+  const int64_t n = outer * inner;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = t / inner, i = t - o * inner;
+    const float *p = x + o * red * inner + i;
+    float m = p[0];
+    int32_t at = 0;
+    for (int64_t r = 1; r < red && m == m; ++r) {
+      const float v = p[r * inner];
+      if (v != v || (is_max ? v > m : v < m)) {
+        m = v;
+        at = (int32_t)r;
+      }
+    }
+    y[t] = m;
+    if (arg) arg[t] = at;
+  }
+}
+
+// dx[o][arg[o][i]][i] += dy[o][i] (dx zeroed first unless accumulating)
+__global__ void k_reduce_maxmin_bwd(const float *__restrict__ dy, const int32_t *__restrict__ arg,
+                                    float *__restrict__ dx, int64_t outer, int64_t red, int64_t inner) {
+  const int64_t n = outer * inner;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = t / inner, i = t - o * inner;
+    dx[(o * red + arg[t]) * inner + i] += dy[t];
+  }
+}
+
+}  // namespace
+
+// out[os] (+)= src (contiguous, `shape`); os: the destination's element strides.
+int nd_scatter(tx_ctx *ctx, const float *src, float *out, const int64_t *os, const int64_t *shape, int ndim,
+               int acc) {
+  int64_t n = 1;
+  for (int k = 0; k < ndim; ++k) n *= shape[k];
+  if (n <= 0) return TX_OK;
+  Nd c;
+  const int64_t *st[1] = {os};
+  canonicalize(ndim, shape, st, 1, c);
+  const unsigned blocks = grid_for(n, 256);
+  if (n < (int64_t(1) << 31))
+    k_scatter_nd<uint32_t><<<blocks, 256, 0, ctx->stream>>>(src, out, c, (uint32_t)n, acc);
+  else
+    k_scatter_nd<uint64_t><<<blocks, 256, 0, ctx->stream>>>(src, out, c, (uint64_t)n, acc);
+  TX_LAUNCHED(ctx, "k_scatter_nd");
+  return TX_OK;
+}
+
+int nd_binary_grad(tx_ctx *ctx, int op, int which, const float *A, const int64_t *sa, const float *B,
+                   const int64_t *sb, const float *dy, float *out, const int64_t *shape, int ndim) {
+  int64_t n = 1;
+  for (int k = 0; k < ndim; ++k) n *= shape[k];
+  if (n <= 0) return TX_OK;
+  // dy and out are contiguous over `shape`: only A and B need strides
+  Nd c;
+  const int64_t *st[2] = {sa, sb};
+  canonicalize(ndim, shape, st, 2, c);
+  const unsigned blocks = grid_for(n, 256);
+  if (n < (int64_t(1) << 31))
+    k_binary_grad_nd<uint32_t><<<blocks, 256, 0, ctx->stream>>>(op, which, A, B, dy, out, c, (uint32_t)n);
+  else
+    k_binary_grad_nd<uint64_t><<<blocks, 256, 0, ctx->stream>>>(op, which, A, B, dy, out, c, (uint64_t)n);
+  TX_LAUNCHED(ctx, "k_binary_grad_nd");
+  return TX_OK;
+}
+
+int reduce_maxmin(tx_ctx *ctx, const float *x, float *y, int32_t *arg, int64_t outer, int64_t red, int64_t inner,
+                  bool is_max) {
+  if (outer * inner <= 0 || red <= 0) return TX_OK;
+  k_reduce_maxmin<<<grid_for(outer * inner, 256), 256, 0, ctx->stream>>>(x, y, arg, outer, red, inner, is_max);
+  TX_LAUNCHED(ctx, "k_reduce_maxmin");
+  return TX_OK;
+}
+
+int reduce_maxmin_bwd(tx_ctx *ctx, const float *dy, const int32_t *arg, float *dx, int64_t outer, int64_t red,
+                      int64_t inner, int acc) {
+  if (outer * inner <= 0 || red <= 0) return TX_OK;
+  if (!acc) TX_CUDA(ctx, cudaMemsetAsync(dx, 0, (size_t)outer * red * inner * sizeof(float), ctx->stream));
+  k_reduce_maxmin_bwd<<<grid_for(outer * inner, 256), 256, 0, ctx->stream>>>(dy, arg, dx, outer, red, inner);
+  TX_LAUNCHED(ctx, "k_reduce_maxmin_bwd");
+  return TX_OK;
+}

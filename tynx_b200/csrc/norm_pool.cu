@@ -414,6 +414,77 @@ extern "C" int tx_prelu_bwd(tx_ctx *ctx, const float *x, const float *slope, con
   return check_launch(ctx, "k_prelu_bwd");
 }
 
+// ---- average pooling (ONNX AveragePool; the inference arm of
+// crates/tynx/src/interpreter/pooling.rs) --------------------------------------------------
+// The divisor of a window is the number of its taps inside the input, or with
+// count_include_pad the number inside the padded input [-PT, H + PB) x
+// [-PL, W + PR) (a ceil-mode window that runs past the padding counts only
+// what it covers).
+__device__ __forceinline__ int avg_count(const PoolGeom &p, int oh, int ow, int pb, int pr, int include_pad) {
+  const int lo_h = include_pad ? -p.PT : 0, hi_h = include_pad ? p.H + pb : p.H;
+  const int lo_w = include_pad ? -p.PL : 0, hi_w = include_pad ? p.W + pr : p.W;
+  int ch = 0, cw = 0;
+  for (int kh = 0; kh < p.KH; ++kh) {
+    const int h = oh * p.SH - p.PT + kh * p.DH;
+    ch += h >= lo_h && h < hi_h;
+  }
+  for (int kw = 0; kw < p.KW; ++kw) {
+    const int w = ow * p.SW - p.PL + kw * p.DW;
+    cw += w >= lo_w && w < hi_w;
+  }
+  return ch * cw;
+}
+
+__global__ void k_avgpool_fwd(const float *__restrict__ x, float *__restrict__ y, PoolGeom p, int64_t planes,
+                              int pb, int pr, int include_pad) {
+  const int64_t n = planes * p.OH * p.OW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int ow = (int)(i % p.OW);
+    const int oh = (int)((i / p.OW) % p.OH);
+    const int64_t plane = i / ((int64_t)p.OW * p.OH);
+    const float *xp = x + plane * (int64_t)p.H * p.W;
+    float sum = 0.f;
+    for (int kh = 0; kh < p.KH; ++kh) {
+      const int h = oh * p.SH - p.PT + kh * p.DH;
+      if (h < 0 || h >= p.H) continue;
+      for (int kw = 0; kw < p.KW; ++kw) {
+        const int w = ow * p.SW - p.PL + kw * p.DW;
+        if (w >= 0 && w < p.W) sum += xp[h * p.W + w];
+      }
+    }
+    const int cnt = avg_count(p, oh, ow, pb, pr, include_pad);
+    y[i] = cnt > 0 ? sum / (float)cnt : 0.f;
+  }
+}
+
+// dx[h][w] (+)= sum over the windows that read (h, w) of dy / count (gather form)
+__global__ void k_avgpool_bwd(const float *__restrict__ dy, float *__restrict__ dx, PoolGeom p, int64_t planes,
+                              int pb, int pr, int include_pad, int acc) {
+  const int64_t n = planes * p.H * p.W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % p.W);
+    const int h = (int)((i / p.W) % p.H);
+    const int64_t plane = i / ((int64_t)p.W * p.H);
+    const float *dp = dy + plane * (int64_t)p.OH * p.OW;
+    float s = 0.f;
+    for (int kh = 0; kh < p.KH; ++kh) {
+      const int a = h + p.PT - kh * p.DH;
+      if (a < 0 || a % p.SH) continue;
+      const int oh = a / p.SH;
+      if (oh >= p.OH) continue;
+      for (int kw = 0; kw < p.KW; ++kw) {
+        const int b = w + p.PL - kw * p.DW;
+        if (b < 0 || b % p.SW) continue;
+        const int ow = b / p.SW;
+        if (ow >= p.OW) continue;
+        const int cnt = avg_count(p, oh, ow, pb, pr, include_pad);
+        if (cnt > 0) s += dp[oh * p.OW + ow] / (float)cnt;
+      }
+    }
+    dx[i] = acc ? dx[i] + s : s;
+  }
+}
+
 static int pool_geom(tx_ctx *ctx, int64_t H, int64_t W, const int64_t *g, PoolGeom *p) {
   // g: kh, kw, sh, sw, pt, pl, dh, dw, oh, ow
   for (int i = 0; i < 10; ++i)
@@ -446,4 +517,29 @@ extern "C" int tx_maxpool2d_bwd(tx_ctx *ctx, const float *dy, const int32_t *arg
   if (n == 0) return TX_OK;
   k_maxpool_bwd<<<grid_for(n, kThreads), kThreads, 0, ctx->stream>>>(dy, argmax, dx, p, planes, acc);
   return check_launch(ctx, "k_maxpool_bwd");
+}
+
+// geom: as tx_maxpool2d_fwd, then the bottom and right padding (pb, pr)
+extern "C" int tx_avgpool2d_fwd(tx_ctx *ctx, const float *x, float *y, int64_t planes, int64_t H, int64_t W,
+                                const int64_t *geom, int count_include_pad) {
+  if (!ctx || !geom || planes < 0 || geom[10] < 0 || geom[11] < 0) return TX_ERR_INVALID;
+  PoolGeom p;
+  TX_TRY(pool_geom(ctx, H, W, geom, &p));
+  const int64_t n = planes * p.OH * p.OW;
+  if (n == 0) return TX_OK;
+  k_avgpool_fwd<<<grid_for(n, kThreads), kThreads, 0, ctx->stream>>>(x, y, p, planes, (int)geom[10], (int)geom[11],
+                                                                     count_include_pad);
+  return check_launch(ctx, "k_avgpool_fwd");
+}
+
+extern "C" int tx_avgpool2d_bwd(tx_ctx *ctx, const float *dy, float *dx, int64_t planes, int64_t H, int64_t W,
+                                const int64_t *geom, int count_include_pad, int acc) {
+  if (!ctx || !geom || planes < 0 || geom[10] < 0 || geom[11] < 0) return TX_ERR_INVALID;
+  PoolGeom p;
+  TX_TRY(pool_geom(ctx, H, W, geom, &p));
+  const int64_t n = planes * p.H * p.W;
+  if (n == 0) return TX_OK;
+  k_avgpool_bwd<<<grid_for(n, kThreads), kThreads, 0, ctx->stream>>>(dy, dx, p, planes, (int)geom[10],
+                                                                     (int)geom[11], count_include_pad, acc);
+  return check_launch(ctx, "k_avgpool_bwd");
 }

@@ -38,7 +38,17 @@ _OP_MAP = {
     "Unsqueeze": "UNSQUEEZE", "Identity": "IDENTITY", "Clip": "CLIP", "PRelu": "PRELU",
     "BatchNormalization": "BATCHNORM", "InstanceNormalization": "GROUPNORM",
     "GroupNormalization": "GROUPNORM", "MaxPool": "MAXPOOL",
+    "Sqrt": "UNARY", "Abs": "UNARY", "Reciprocal": "UNARY", "Erf": "UNARY", "LeakyRelu": "UNARY",
+    "Softplus": "UNARY", "Elu": "UNARY", "HardSigmoid": "UNARY", "Softsign": "UNARY", "Pow": "BINARY",
+    "Max": "BINARY", "Min": "BINARY", "Concat": "CONCAT", "Slice": "SLICE", "Split": "SPLIT",
+    "Expand": "EXPAND", "AveragePool": "AVGPOOL", "ReduceMax": "REDUCEMAX", "ReduceMin": "REDUCEMIN",
+    "GlobalMaxPool": "REDUCEMAX", "Dropout": "IDENTITY",
 }
+# the unary operators' kernel codes and their (a, b) from the attributes
+_UNARY = {"Sqrt": ("sqrt", None), "Abs": ("abs", None), "Reciprocal": ("reciprocal", None),
+          "Erf": ("erf", None), "LeakyRelu": ("leakyrelu", ("alpha",)), "Softplus": ("softplus", None),
+          "Elu": ("elu", ("alpha",)), "HardSigmoid": ("hardsigmoid", ("alpha", "beta")),
+          "Softsign": ("softsign", None)}
 _AUTO_PAD = {"NOTSET": 0, "": 0, "VALID": 1, "SAME_UPPER": 2, "SAME_LOWER": 3}
 
 _ELEM_TO_DTYPE = {proto.FLOAT: "float32", proto.INT64: "int64", proto.INT32: "int64",
@@ -374,6 +384,91 @@ def lower(graph: ir.TrainingGraph):
                 axes = _const_ints(graph, ins[1])
             ints = list(axes or [])
             ins = ins[:1]
+        elif t in _UNARY:
+            code, names = _UNARY[t]
+            d.iattr[0] = N.UN[code]
+            for i, name in enumerate(names or ()):
+                d.fattr[i] = float(a[name])
+        elif t == "Pow":
+            exponent = graph.constants.get(ins[1]) if len(ins) > 1 else None
+            if exponent is not None and np.asarray(exponent).size == 1:
+                # a constant scalar exponent: the unary power (its gradient
+                # reaches the base only, as the reference's)
+                d.op = N.OP["UNARY"]
+                d.iattr[0] = N.UN["pow"]
+                d.fattr[0] = float(np.asarray(exponent).reshape(-1)[0])
+                ins = ins[:1]
+            else:
+                d.iattr[0] = N.BIN["pow"]
+        elif t in ("Max", "Min"):
+            if len(ins) == 1:
+                d.op = N.OP["IDENTITY"]
+            elif len(ins) != 2:
+                raise NotImplementedError(f"{t} over {len(ins)} inputs is not supported by the CUDA engine")
+            else:
+                d.iattr[0] = N.BIN["max" if t == "Max" else "min"]
+        elif t == "Concat":
+            d.iattr[0] = int(a["axis"])
+        elif t == "Slice":
+            if len(ins) > 1:  # opset >= 10: starts, ends, axes, steps as inputs
+                starts = _const_ints(graph, ins[1])
+                ends = _const_ints(graph, ins[2])
+                axes = _const_ints(graph, ins[3]) if len(ins) > 3 and ins[3] else list(range(len(starts)))
+                steps = _const_ints(graph, ins[4]) if len(ins) > 4 and ins[4] else [1] * len(starts)
+            else:
+                starts, ends = list(a["starts"]), list(a["ends"])
+                axes = list(a.get("axes") or range(len(starts)))
+                steps = [1] * len(starts)
+            if len(axes) > 3:
+                raise NotImplementedError(f"Slice node {op.name!r} over more than 3 axes")
+            big = (1 << 62)
+            clip = [max(-big, min(big, int(v))) for v in ends]
+            ints = [len(axes)] + list(axes) + list(starts) + clip + list(steps)
+            ins = ins[:1]
+        elif t == "Split":
+            d.iattr[0] = int(a["axis"])
+            sizes = a.get("split")
+            if sizes is None and len(ins) > 1 and ins[1]:
+                sizes = _const_ints(graph, ins[1])
+            # no sizes: equal parts of the runtime extent (the engine's shapes),
+            # the last one smaller when they do not divide it
+            ints = list(sizes or [])
+            ins = ins[:1]
+        elif t == "Expand":
+            ints = _const_ints(graph, ins[1])
+            ins = ins[:1]
+        elif t in ("ReduceMax", "ReduceMin", "GlobalMaxPool"):
+            if t == "GlobalMaxPool":
+                axes = "spatial"
+            else:
+                axes = a.get("axes")
+                if axes is None and len(ins) > 1 and ins[1]:
+                    axes = _const_ints(graph, ins[1])
+                if not axes and a.get("noop_with_empty_axes", 0):
+                    raise NotImplementedError(f"{t} noop_with_empty_axes")
+            ints = [] if axes == "spatial" else list(axes or [])
+            d.iattr[0] = 1 if t == "GlobalMaxPool" else int(a["keepdims"])
+            d.iattr[1] = int(axes == "spatial")
+            ins = ins[:1]
+        elif t == "Dropout":
+            if len(ins) > 2 and ins[2]:
+                mode = graph.constants.get(ins[2])
+                if mode is None or bool(np.asarray(mode).reshape(-1)[0]):
+                    raise NotImplementedError(f"Dropout node {op.name!r} in training mode")
+            ins = ins[:1]
+        elif t == "AveragePool":
+            k, st, dil, pads = (list(a["kernel_shape"]), list(a["strides"]), list(a["dilations"]),
+                                list(a["pads"]))
+            if len(k) == 1:  # 1-D pooling runs as 2-D over a unit height
+                k, st, dil, pads = [1] + k, [1] + st, [1] + dil, [0, pads[0], 0, pads[1]]
+            if len(k) != 2:
+                raise NotImplementedError(f"{len(k)}-D AveragePool is not supported by the CUDA engine")
+            if a.get("auto_pad", "NOTSET") not in _AUTO_PAD:
+                raise ValueError(f"AveragePool node {op.name!r}: unknown auto_pad {a['auto_pad']!r}")
+            ints = [k[0], k[1], st[0], st[1], pads[0], pads[1], pads[2], pads[3], dil[0], dil[1]]
+            d.iattr[0] = int(a["ceil_mode"])
+            d.iattr[1] = _AUTO_PAD[a.get("auto_pad", "NOTSET")]
+            d.iattr[2] = int(a["count_include_pad"])
         elif t == "Clip":
             lo = a.get("min")
             hi = a.get("max")

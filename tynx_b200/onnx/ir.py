@@ -40,6 +40,10 @@ DIFFERENTIABLE = {
     "ReduceMean", "ReduceSum", "GlobalAveragePool", "Reshape", "Transpose", "Flatten",
     "Squeeze", "Unsqueeze", "Identity", "Clip", "PRelu", "BatchNormalization",
     "InstanceNormalization", "GroupNormalization", "MaxPool",
+    # smooth unary operations, extrema, layout and pooling (backward_support.rs:70-100)
+    "Sqrt", "Abs", "Reciprocal", "Erf", "LeakyRelu", "Softplus", "Elu", "HardSigmoid", "Softsign",
+    "Pow", "Max", "Min", "Concat", "Slice", "Split", "Expand", "AveragePool", "ReduceMax",
+    "ReduceMin", "GlobalMaxPool", "Dropout",
 }
 # Operators that carry no gradient to their inputs but are allowed on a path.
 NON_DIFFERENTIABLE_OK = {"Constant", "Shape"}
@@ -259,6 +263,35 @@ def _normalize_attrs(node: proto.Node, opset: int) -> dict:
         a.setdefault("epsilon", 1e-5)
         if "num_groups" not in a:
             raise LoadError(f"GroupNormalization node {node.name!r} has no num_groups attribute")
+    elif t in ("ReduceMax", "ReduceMin"):
+        a.setdefault("keepdims", 1)
+    elif t == "LeakyRelu":
+        a.setdefault("alpha", 0.01)
+    elif t == "Elu":
+        a.setdefault("alpha", 1.0)
+    elif t == "HardSigmoid":
+        a.setdefault("alpha", 0.2)
+        a.setdefault("beta", 0.5)
+    elif t in ("Concat", "Split"):
+        a.setdefault("axis", 0)
+        if t == "Concat" and "axis" not in node.attributes:
+            raise LoadError(f"Concat node {node.name!r} has no axis attribute")
+    elif t == "Dropout":
+        # inference semantics: the identity; a mask output or a training flag
+        # would need the random mask (backward_support.rs: Dropout is
+        # differentiable only when inference-only)
+        if len(node.outputs) > 1:
+            raise LoadError(f"Dropout node {node.name!r}: the mask output is not supported")
+    elif t == "AveragePool":
+        if "kernel_shape" not in a:
+            raise LoadError(f"AveragePool node {node.name!r} has no kernel_shape attribute")
+        nd = len(a["kernel_shape"])
+        a.setdefault("strides", [1] * nd)
+        a.setdefault("dilations", [1] * nd)
+        a.setdefault("pads", [0] * (2 * nd))
+        a.setdefault("ceil_mode", 0)
+        a.setdefault("auto_pad", "NOTSET")
+        a.setdefault("count_include_pad", 0)
     elif t == "MaxPool":
         if "kernel_shape" not in a:
             raise LoadError(f"MaxPool node {node.name!r} has no kernel_shape attribute")
