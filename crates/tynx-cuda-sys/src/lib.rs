@@ -264,6 +264,8 @@ extern "C" {
     pub fn tx_binary(ctx: *mut tx_ctx, op: c_int, d_a: *const f32, a_strides: *const i64, d_b: *const f32, b_strides: *const i64, d_out: *mut f32, out_shape: *const i64, ndim: c_int) -> c_int;
     pub fn tx_reduce_to(ctx: *mut tx_ctx, d_x: *const f32, in_shape: *const i64, d_out: *mut f32, out_shape: *const i64, ndim: c_int, mean: c_int, accumulate: c_int) -> c_int;
     pub fn tx_strided_copy(ctx: *mut tx_ctx, d_src: *const c_void, src_strides: *const i64, d_dst: *mut c_void, shape: *const i64, ndim: c_int, elem_bytes: c_int) -> c_int;
+    pub fn tx_dropout_fwd(ctx: *mut tx_ctx, d_x: *const f32, d_y: *mut f32, d_mask: *mut f32, n: i64, p: f32, seed: u64, d_counter: *mut u64) -> c_int;
+    pub fn tx_strided_scatter(ctx: *mut tx_ctx, d_src: *const f32, d_dst: *mut f32, dst_strides: *const i64, shape: *const i64, ndim: c_int, accumulate: c_int) -> c_int;
     pub fn tx_softmax_fwd(ctx: *mut tx_ctx, d_x: *const f32, d_y: *mut f32, rows: i64, cols: i64, log: c_int) -> c_int;
     pub fn tx_softmax_bwd(ctx: *mut tx_ctx, d_y: *const f32, d_dy: *const f32, d_dx: *mut f32, rows: i64, cols: i64, log: c_int, accumulate: c_int) -> c_int;
     pub fn tx_softmax_xent_fwd(ctx: *mut tx_ctx, d_logits: *const f32, d_labels: *const i64, rows: i64, cols: i64, d_loss: *mut f32) -> c_int;

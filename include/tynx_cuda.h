@@ -230,6 +230,18 @@ int tx_reduce_to(tx_ctx *ctx, const float *d_x, const int64_t *in_shape, float *
 /* Copy with arbitrary element strides (transpose / expand materialisation). */
 int tx_strided_copy(tx_ctx *ctx, const void *d_src, const int64_t *src_strides, void *d_dst,
                     const int64_t *shape, int ndim, int elem_bytes);
+/* Training-mode dropout: mask[i] = 0 with probability p, else 1 / (1 - p),
+ * y = x * mask, drawn from a counter-based stream keyed by `seed` and the
+ * device counter *d_counter, which the call advances (so a replayed CUDA graph
+ * draws a new mask each time); d_counter = NULL uses the context's own counter
+ * (zero when the context is created).  replaces: the Dropout of the capture IR
+ * (crates/tynx-capture/src/lib.rs, UnaryOp::Dropout). */
+int tx_dropout_fwd(tx_ctx *ctx, const float *d_x, float *d_y, float *d_mask, int64_t n, float p, uint64_t seed,
+                   uint64_t *d_counter);
+/* dst[dst_strides] (+)= src (contiguous over `shape`): the gradient of a
+ * strided view (slicing), Concat's slabs. */
+int tx_strided_scatter(tx_ctx *ctx, const float *d_src, float *d_dst, const int64_t *dst_strides,
+                       const int64_t *shape, int ndim, int accumulate);
 
 /* Softmax / log-softmax over the last axis of a [rows, cols] view.
  * replaces: softmax / log_softmax (crates/tynx/src/interpreter/softmax.rs:9-17,

@@ -149,7 +149,8 @@ def _check_op(tx, model_bytes, x_np, exact_forward=False, tol=1e-5):
     fo.sum_(yr * fo.T(w)).backward()
 
     def rel(a, b):
-        return float(np.linalg.norm(np.float64(a) - b) / max(np.linalg.norm(np.float64(b)), 1e-30))
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
     assert rel(x.grad.numpy(), xr.grad) <= tol, rel(x.grad.numpy(), xr.grad)
     p = dict(model.named_parameters())

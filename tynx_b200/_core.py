@@ -571,6 +571,55 @@ class Tensor:
             return _unary("pow", self, float(exponent))
         return _binary("pow", self, exponent)
 
+    def __rpow__(self, base):
+        # base ** x = exp(x ln base) for a positive python scalar base
+        # (ReversePowerScalar of the capture IR)
+        if not isinstance(base, (int, float)):
+            return _binary("pow", base, self)
+        if base <= 0:
+            raise ValueError("a scalar base of a tensor power must be positive")
+        return _unary("exp", _scale(self, float(np.log(base)), 0.0))
+
+    def __getitem__(self, index) -> "Tensor":
+        return _getitem(self, index)
+
+    def repeat(self, *sizes) -> "Tensor":
+        """Tile along each axis (leading sizes add axes), as torch.Tensor.repeat."""
+        if len(sizes) == 1 and isinstance(sizes[0], (tuple, list)):
+            sizes = tuple(sizes[0])
+        if len(sizes) < self.ndim:
+            raise ValueError("repeat needs at least one size per axis")
+        x = self.reshape((1,) * (len(sizes) - self.ndim) + self.shape)
+        inter = []
+        for s in x.shape:
+            inter += [1, s]
+        tiled = []
+        for r, s in zip(sizes, x.shape):
+            tiled += [r, s]
+        out = x.reshape(tuple(inter)).expand(tuple(tiled))
+        return out.reshape(tuple(r * s for r, s in zip(sizes, x.shape)))
+
+    def erf(self):
+        return _unary("erf", self)
+
+    def reciprocal(self):
+        return _unary("reciprocal", self)
+
+    def softplus(self):
+        return _unary("softplus", self)
+
+    def softsign(self):
+        return _unary("softsign", self)
+
+    def leaky_relu(self, negative_slope: float = 0.01):
+        return _unary("leakyrelu", self, float(negative_slope))
+
+    def elu(self, alpha: float = 1.0):
+        return _unary("elu", self, float(alpha))
+
+    def hardsigmoid(self, alpha: float = 1.0 / 6.0, beta: float = 0.5):
+        return _unary("hardsigmoid", self, float(alpha), float(beta))
+
     def __matmul__(self, other):
         return matmul(self, other)
 
@@ -759,7 +808,14 @@ def _binary(op: str, a, b) -> Tensor:
                     inv = _scale_nograd(mask, -1.0, 1.0)
                     gb = _sum_to(_binary_raw("mul", g, inv, g.shape), B.shape)
             elif op == "pow":
-                raise NotImplementedError("gradient of tensor ** tensor")
+                # d(a^b)/da = b a^(b-1), d(a^b)/db = a^b ln a
+                if need_a:
+                    t = _binary_raw("pow", A, _scale_nograd(B, 1.0, -1.0), g.shape)
+                    t = _binary_raw("mul", t, B, g.shape)
+                    ga = _sum_to(_binary_raw("mul", g, t, g.shape), A.shape)
+                if need_b:
+                    t = _binary_raw("mul", Y, _unary_nograd("log", A), g.shape)
+                    gb = _sum_to(_binary_raw("mul", g, t, g.shape), B.shape)
             return [ga, gb]
 
         out._attach(Fn(op, [a, b], backward))
@@ -777,6 +833,66 @@ def _scale_nograd(x: Tensor, a: float, b: float) -> Tensor:
     x.ctx.check(lib.tx_unary(x.ctx.handle, N.UN["scale"], x.ptr, out.ptr, x.numel, C.c_float(a),
                              C.c_float(b)))
     return out
+
+
+def _getitem(x: Tensor, index) -> Tensor:
+    """Basic indexing: integers, slices (any step), Ellipsis and None; a
+    strided copy forward, a strided scatter into zeros backward (the Slice of
+    the capture IR)."""
+    if not isinstance(index, tuple):
+        index = (index,)
+    if any(isinstance(i, (Tensor, list, np.ndarray)) for i in index):
+        raise NotImplementedError("advanced indexing is not supported; use gather")
+    n_real = sum(1 for i in index if i is not None and i is not Ellipsis)
+    if n_real > x.ndim:
+        raise IndexError(f"too many indices for a tensor of rank {x.ndim}")
+    expanded = []
+    for i in index:
+        if i is Ellipsis:
+            expanded += [slice(None)] * (x.ndim - n_real)
+        else:
+            expanded.append(i)
+    if Ellipsis not in index:
+        expanded += [slice(None)] * (x.ndim - n_real)
+    st = _contig_strides(x.shape)
+    offset, shape, strides, out_shape = 0, [], [], []
+    axis = 0
+    for i in expanded:
+        if i is None:
+            out_shape.append(1)
+            continue
+        dim = x.shape[axis]
+        if isinstance(i, (int, np.integer)):
+            k = int(i) + (dim if i < 0 else 0)
+            if not 0 <= k < dim:
+                raise IndexError(f"index {int(i)} is out of bounds for axis {axis} with size {dim}")
+            offset += k * st[axis]
+        elif isinstance(i, slice):
+            start, stop, step = i.indices(dim)
+            length = len(range(start, stop, step))
+            offset += start * st[axis] if length else 0
+            shape.append(length)
+            strides.append(step * st[axis])
+            out_shape.append(length)
+        else:
+            raise TypeError(f"unsupported index {i!r}")
+        axis += 1
+    out = Tensor._empty(tuple(shape), x.dtype, x.ctx)
+    if out.numel:
+        x.ctx.check(lib.tx_strided_copy(x.ctx.handle, x.ptr + offset * x.itemsize, N.i64_array(strides), out.ptr,
+                                        N.i64_array(shape), len(shape), x.itemsize))
+    if _needs_grad(x):
+        src_shape, base = x.shape, offset
+
+        def backward(g, shape=tuple(shape), strides=tuple(strides)):
+            dx = full(src_shape, 0.0, ctx=g[0].ctx)
+            if g[0].numel:
+                g[0].ctx.check(lib.tx_strided_scatter(g[0].ctx.handle, g[0].ptr, dx.ptr + base * 4,
+                                                      N.i64_array(strides), N.i64_array(shape), len(shape), 1))
+            return [dx]
+
+        out._attach(Fn("getitem", [x], backward))
+    return out.reshape(tuple(out_shape)) if tuple(out_shape) != tuple(shape) else out
 
 
 def minimum(a, b) -> Tensor:

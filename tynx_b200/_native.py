@@ -145,6 +145,8 @@ SIGNATURES = {
     "tx_binary": [_vp, _i32, _vp, _p64, _vp, _p64, _vp, _p64, _i32],
     "tx_reduce_to": [_vp, _vp, _p64, _vp, _p64, _i32, _i32, _i32],
     "tx_strided_copy": [_vp, _vp, _p64, _vp, _p64, _i32, _i32],
+    "tx_strided_scatter": [_vp, _vp, _vp, _p64, _p64, _i32, _i32],
+    "tx_dropout_fwd": [_vp, _vp, _vp, _vp, _i64, C.c_float, C.c_uint64, _vp],
     "tx_softmax_fwd": [_vp, _vp, _vp, _i64, _i64, _i32],
     "tx_softmax_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32],
     "tx_softmax_xent_fwd": [_vp, _vp, _vp, _i64, _i64, _vp],

@@ -43,6 +43,7 @@ struct tx_ctx {
   int err_code = 0;
   std::string err_msg;
   int *d_err = nullptr;  // device error flag [4]
+  uint64_t *d_rng = nullptr;  // call counter of the dropout stream
   bool capturing = false;
   // data parallel
   void *nccl = nullptr;

@@ -54,7 +54,11 @@ extern "C" int tx_ctx_create(int device, int math_mode, tx_ctx **out) {
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->comm, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->d_err, 4 * sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->d_err, 0, 4 * sizeof(int)) != cudaSuccess) {
+      cudaMemset(ctx->d_err, 0, 4 * sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_rng, sizeof(uint64_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_rng, 0, sizeof(uint64_t)) != cudaSuccess) {
+    cudaFree(ctx->d_err);
+    cudaFree(ctx->d_rng);
     delete ctx;
     return TX_ERR_CUDA;
   }
@@ -408,6 +412,7 @@ extern "C" int tx_ctx_destroy(tx_ctx *ctx) {
   for (auto &kv : ctx->alloc.live) cudaFree(kv.first);
   for (void *p : ctx->alloc.quarantine) cudaFree(p);
   cudaFree(ctx->d_err);
+  cudaFree(ctx->d_rng);
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm);
   delete ctx;

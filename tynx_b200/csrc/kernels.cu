@@ -1148,6 +1148,56 @@ extern "C" int tx_strided_copy(tx_ctx *ctx, const void *src, const int64_t *ss, 
   return nd_copy(ctx, src, ss, dst, shape, ndim, elem_bytes, 1.f, 0);
 }
 
+// ---- training-mode dropout (the capture IR's Dropout: a device random stream
+// that advances with every call, so a replayed graph draws new masks) ----------
+// u = the SplitMix64 finaliser (Steele, Lea and Flood, "Fast splittable
+// pseudorandom number generators", OOPSLA 2014) of (seed, call counter, element)
+// -> 24 uniform bits; the element is kept when u >= p and scaled by 1 / (1 - p).
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z ^= z >> 30;
+  z *= 0xbf58476d1ce4e5b9ull;
+  z ^= z >> 27;
+  z *= 0x94d049bb133111ebull;
+  z ^= z >> 31;
+  return z;
+}
+
+__global__ void k_dropout(const float *__restrict__ x, float *__restrict__ y, float *__restrict__ mask, int64_t n,
+                          float p, uint64_t seed, const uint64_t *__restrict__ counter) {
+  const uint64_t ctr = *counter;
+  const float keep_scale = 1.f / (1.f - p);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = mix64(seed ^ mix64(ctr * 0x9e3779b97f4a7c15ull + (uint64_t)i));
+    const float u = (float)(h >> 40) * (1.f / 16777216.f);
+    const float m = u >= p ? keep_scale : 0.f;
+    mask[i] = m;
+    y[i] = x[i] * m;
+  }
+}
+
+__global__ void k_counter_add(uint64_t *counter) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *counter += 1;
+}
+
+extern "C" int tx_dropout_fwd(tx_ctx *ctx, const float *x, float *y, float *mask, int64_t n, float p, uint64_t seed,
+                              uint64_t *d_counter) {
+  if (!ctx || !(p >= 0.f && p < 1.f)) return TX_ERR_INVALID;
+  if (!d_counter) d_counter = ctx->d_rng;
+  if (n > 0) {
+    k_dropout<<<grid_for(n, 256), 256, 0, ctx->stream>>>(x, y, mask, n, p, seed, d_counter);
+    TX_LAUNCHED(ctx, "k_dropout");
+  }
+  k_counter_add<<<1, 32, 0, ctx->stream>>>(d_counter);
+  TX_LAUNCHED(ctx, "k_counter_add");
+  return TX_OK;
+}
+
+extern "C" int tx_strided_scatter(tx_ctx *ctx, const float *src, float *dst, const int64_t *dst_strides,
+                                  const int64_t *shape, int ndim, int acc) {
+  if (!ctx || ndim < 0 || ndim > TX_MAX_DIMS) return TX_ERR_INVALID;
+  return nd_scatter(ctx, src, dst, dst_strides, shape, ndim, acc);
+}
+
 // rows whose width is a multiple of 128 (up to 1024) on 16-byte aligned buffers
 // take the register-resident float4 kernels
 static bool ln_vec(int64_t cols, std::initializer_list<const void *> ptrs) {
