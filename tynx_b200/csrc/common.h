@@ -117,6 +117,7 @@ int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &d, bool *rounded = nullptr);
 // Bandwidth-shaped kernels for K <= 32, N <= 16 or M <= 16; TX_ERR_UNSUPPORTED
 // (not latched) for every other shape.
 int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &d, FusedSum *fs = nullptr);
+bool skinny_shape(const tx_gemm_desc &d);
 int gemm_split_reduce(tx_ctx *ctx, const tx_gemm_desc &d, const float *part, int splits);
 
 // N-d bandwidth kernels on canonicalised shapes (nd.cu).  Strides in elements,

@@ -323,7 +323,8 @@ int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc, bool *rounded) {
     // alpha A B + C with the epilogue (beta 1)
     if (d.colsum || d.beta != 0.f || (d.flags & TX_GEMM_EXACT))
       return tx_fail(ctx, TX_ERR_UNSUPPORTED, "split weights with beta, column sums or EXACT");
-    int rc = gemm_tcgen05(ctx, d, (d.flags & TX_GEMM_A_TF32) ? 0 : 1, nullptr);
+    // (skinny shapes take the FFMA kernels for both products)
+    int rc = skinny_shape(d) ? TX_ERR_UNSUPPORTED : gemm_tcgen05(ctx, d, (d.flags & TX_GEMM_A_TF32) ? 0 : 1, nullptr);
     if (rc != TX_ERR_UNSUPPORTED) {
       if (rounded) *rounded = rc == TX_OK && (d.flags & TX_GEMM_ROUND_OUT);
       return rc;

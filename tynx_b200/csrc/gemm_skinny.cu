@@ -647,6 +647,14 @@ int launch_small_k(tx_ctx *ctx, const tx_gemm_desc &desc, int64_t batch, FusedSu
 
 }  // namespace
 
+// Whether gemm_skinny takes a batch-1 product without fused column sums
+// (the short-K rule aside, which it only narrows).
+bool skinny_shape(const tx_gemm_desc &d) {
+  if (d.K <= 0 || d.batch > 1) return false;
+  if (d.K <= SK_KMAX) return true;
+  return (d.N <= 16 && !d.trans_a) || (d.M <= 16 && !d.trans_b && d.N >= 64);
+}
+
 // Route the skinny shapes; TX_ERR_UNSUPPORTED leaves the shape to the
 // tensor-core / SIMT kernels.
 int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &desc, FusedSum *fs) {
@@ -667,7 +675,7 @@ int gemm_skinny(tx_ctx *ctx, const tx_gemm_desc &desc, FusedSum *fs) {
   tx_gemm_desc d = desc;
   if (fs) d.flags &= ~TX_GEMM_ROUND_OUT;  // the remaining kernels do not sum columns
   if (batch != 1) return TX_ERR_UNSUPPORTED;
-  if (d.N <= 16 && !d.trans_a && d.M >= 64) {
+  if (d.N <= 16 && !d.trans_a) {
     if (d.N <= 2) return launch_small_n<2>(ctx, d);
     if (d.N <= 4) return launch_small_n<4>(ctx, d);
     if (d.N <= 8) return launch_small_n<8>(ctx, d);

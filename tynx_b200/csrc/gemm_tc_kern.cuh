@@ -1493,9 +1493,9 @@ int launch_persistent_impl(tx_ctx *ctx, int bn, const tx_gemm_desc &d, const Map
   w.col_part = m.col_part;
   w.conv_mask = m.conv_mask;
   // a GELU (or GELU') epilogue costs more than a 256-wide tile's main loop:
-  // eight epilogue warps, when two stages still fit beside their tiles (for
-  // short reductions, K <= 512, eight warps measured no faster than four:
-  // transformer step 4.199 against 4.200 ms)
+  // eight epilogue warps, when two stages still fit beside their tiles (also
+  // for short reductions: with four warps on the K = 256 GELU' data gradients
+  // the transformer step at batch 256 measured 4.34 against 4.21 ms)
   int ew = 4;
   if (MODE == 0 && bn == 256 && (d.act == TX_ACT_GELU || d.dact == TX_ACT_GELU) &&
       (kSmemMax - 1024 - kPTail - 8 * w.ep_stride) / stage >= 2)
