@@ -256,10 +256,10 @@ __device__ __forceinline__ void softmax_row(float (&v)[128], float scale, int se
   for (int j = 0; j < 128; ++j) v[j] *= inv;
 }
 
-// Round `bytes` of shared memory to TF32 in place (128 threads, float4 steps).
-__device__ __forceinline__ void round_region(uint8_t *p, int bytes, int t) {
+// Round `bytes` of shared memory to TF32 in place (nt threads, float4 steps).
+__device__ __forceinline__ void round_region(uint8_t *p, int bytes, int t, int nt = 128) {
   float4 *q = reinterpret_cast<float4 *>(p);
-  for (int i = t; i < bytes / 16; i += 128) {
+  for (int i = t; i < bytes / 16; i += nt) {
     float4 v = q[i];
     q[i] = make_float4(rn_tf32(v.x), rn_tf32(v.y), rn_tf32(v.z), rn_tf32(v.w));
   }
@@ -285,29 +285,31 @@ __device__ __forceinline__ void put_col(uint8_t *tiles, int r, int c, const floa
   }
 }
 
-// Store a thread's row of a [128 x 64] TMEM accumulator (columns col..col+63)
-// to global memory (row < seq only; all lanes take part in the TMEM loads).
-__device__ __forceinline__ void store_row(uint32_t trow, float *dst, bool live, bool acc, bool rnd) {
-#pragma unroll 1
-  for (int c = 0; c < kDim / 32; ++c) {
-    float v[32];
-    tld32(trow + c * 32, v);
-    if (!live) continue;
-    float4 *d4 = reinterpret_cast<float4 *>(dst + c * 32);
+// Store 32 columns of a thread's row of a TMEM accumulator (at taddr) to
+// global memory (row < seq only; all lanes take part in the TMEM load).
+__device__ __forceinline__ void store_chunk(uint32_t taddr, float *dst, bool live, bool acc, bool rnd) {
+  float v[32];
+  tld32(taddr, v);
+  if (!live) return;
+  float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      if (acc) {
-        const float4 o = d4[j];
-        w.x += o.x;
-        w.y += o.y;
-        w.z += o.z;
-        w.w += o.w;
-      }
-      if (rnd) w = make_float4(rn_tf32(w.x), rn_tf32(w.y), rn_tf32(w.z), rn_tf32(w.w));
-      d4[j] = w;
+  for (int j = 0; j < 8; ++j) {
+    float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    if (acc) {
+      const float4 o = d4[j];
+      w.x += o.x;
+      w.y += o.y;
+      w.z += o.z;
+      w.w += o.w;
     }
+    if (rnd) w = make_float4(rn_tf32(w.x), rn_tf32(w.y), rn_tf32(w.z), rn_tf32(w.w));
+    d4[j] = w;
   }
+}
+
+// Named barrier of the two epilogue warps that share a TMEM lane quadrant.
+__device__ __forceinline__ void pair_sync(int quad) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
 }
 
 // ---- forward --------------------------------------------------------------------------------
@@ -436,9 +438,15 @@ __global__ void __launch_bounds__(192, 2)
 // R4 dO (MN-major; then Q MN-major) | R5 K (MN-major) | tail.  P^T (64 KB) overlays R0..R1
 // after S and dP are computed; dS (64 KB) overlays R2..R3; dS^T overlays P^T once dV is done.
 // TMEM columns: S 0..127 | dP 128..255 | dV 256..319 | dQ 320..383 | dK 384..447.
-constexpr int kBwdSmem = 6 * kTile + 1024 + 1024;
+// Eight epilogue warps, two per TMEM lane quadrant: the warp of half h takes
+// key columns 64h .. 64h + 63 of its 32 rows (score chunks 2h, 2h + 1) and
+// output chunk h of dV, dQ and dK; the row max, row sum and rowsum(P * dP) of
+// the two halves meet in the tail (3 x [2][128] floats after the barriers).
+constexpr int kBwdEpi = 256;                      // epilogue threads
+constexpr int kBwdTail = 4096;
+constexpr int kBwdSmem = 6 * kTile + kBwdTail + 1024;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + kBwdEpi, 1)
     k_attn_bwd(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                const __grid_constant__ CUtensorMap mqn, const __grid_constant__ CUtensorMap mkn,
@@ -453,6 +461,8 @@ __global__ void __launch_bounds__(192, 1)
            *b_dst = bars + 10, *b_dk = bars + 11;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 16);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  float *xmax = reinterpret_cast<float *>(sm + 6 * kTile + 1024);  // [2][128] per half
+  float *xsum = xmax + 2 * kRows, *xd = xsum + 2 * kRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x / heads, h = blockIdx.x % heads;
   const int row0 = b * seq, col0 = h * kDim;
@@ -462,14 +472,14 @@ __global__ void __launch_bounds__(192, 1)
     bar_init(b_ld1, 1);
     bar_init(b_ld2, 1);
     bar_init(b_ld3, 1);
-    bar_init(b_cv, 128);
-    bar_init(b_cv3, 128);
+    bar_init(b_cv, kBwdEpi);
+    bar_init(b_cv3, kBwdEpi);
     bar_init(b_s, 1);
-    bar_init(b_pt, 128);
-    bar_init(b_ds, 128);
+    bar_init(b_pt, kBwdEpi);
+    bar_init(b_ds, kBwdEpi);
     bar_init(b_dv, 1);
     bar_init(b_dq, 1);
-    bar_init(b_dst, 128);
+    bar_init(b_dst, kBwdEpi);
     bar_init(b_dk, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -556,47 +566,86 @@ __global__ void __launch_bounds__(192, 1)
       if (issued3) bar_drain(b_ld3);
     }
   } else if (warp >= 2) {
-    const int t = threadIdx.x - 64;
+    const int t = threadIdx.x - 64;     // 0 .. kBwdEpi - 1
+    const int half = (warp - 2) >> 2;   // key columns 64 * half ..
     const int quad = warp & 3, r = quad * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const bool live = r < seq;
     if (!rounded) {
-      if (bar_wait(b_ld1, abort_flag, err, 21)) round_region(sm, 4 * kTile, t);
-      if (bar_wait(b_ld2, abort_flag, err, 22)) round_region(R4, 2 * kTile, t);
+      if (bar_wait(b_ld1, abort_flag, err, 21)) round_region(sm, 4 * kTile, t, kBwdEpi);
+      if (bar_wait(b_ld2, abort_flag, err, 22)) round_region(R4, 2 * kTile, t, kBwdEpi);
       fence_async_smem();
       bar_arrive(b_cv);
     }
     bool ok = __all_sync(0xffffffffu, bar_wait(b_s, abort_flag, err, 23));
     fence_after();
-    float p[128];
+    // Softmax of this half's 64 keys against the row's max and sum (every
+    // pair barrier below is reached by both warps whatever `ok` says).
+    float p[64];
+    float m = -INFINITY;
+    if (ok) {
+      uint32_t r0[32], r1[32];
+      tld32_issue(trow + half * 64, r0);
+      tld32_issue(trow + half * 64 + 32, r1);
+      tld_wait();
+      regs_after_wait(r0);
+      regs_after_wait(r1);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        p[j] = __uint_as_float(r0[j]) * scale;
+        p[32 + j] = __uint_as_float(r1[j]) * scale;
+      }
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (half * 64 + j < seq) m = fmaxf(m, p[j]);
+    }
+    xmax[half * kRows + r] = m;
+    pair_sync(quad);
+    m = fmaxf(xmax[r], xmax[kRows + r]);
+    float sum = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        p[j] = half * 64 + j < seq ? __expf(p[j] - m) : 0.f;
+        sum += p[j];
+      }
+    }
+    xsum[half * kRows + r] = sum;
+    pair_sync(quad);
+    sum = xsum[r] + xsum[kRows + r];
+    const float inv = live ? 1.0f / sum : 0.f;
     float dsum = 0.f;
     if (ok) {
-      tld128(trow, p);
-      softmax_row(p, scale, seq, live);
-      // P^T for dV, and D = rowsum(P * dP)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int j = 0; j < 64; ++j) p[j] *= inv;
+      // P^T for dV, and this half's share of D = rowsum(P * dP)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         float g[32], q[32];
-        tld32(trow + 128 + c * 32, g);
+        tld32(trow + 128 + (2 * half + c) * 32, g);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           dsum += p[c * 32 + j] * g[j];
           q[j] = rn_tf32(p[c * 32 + j]);
         }
-        put_col(R0, r, c, q);
+        put_col(R0, r, 2 * half + c, q);
       }
     }
+    xd[half * kRows + r] = dsum;
     fence_async_smem();
     bar_arrive(b_pt);
+    pair_sync(quad);
+    dsum = xd[r] + xd[kRows + r];
     if (ok) {  // dS rows for dQ; dS also replaces dP in TMEM for the dS^T pass
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
+        const int cc = 2 * half + c;
         float g[32];
-        tld32(trow + 128 + c * 32, g);
+        tld32(trow + 128 + cc * 32, g);
 #pragma unroll
         for (int j = 0; j < 32; ++j) g[j] = rn_tf32(p[c * 32 + j] * (g[j] - dsum) * scale);
-        put_row(R2 + c * 16384, r, g);
-        tst32(trow + 128 + c * 32, g);
+        put_row(R2 + cc * 16384, r, g);
+        tst32(trow + 128 + cc * 32, g);
       }
       tst_wait();
     }
@@ -606,28 +655,28 @@ __global__ void __launch_bounds__(192, 1)
     ok = __all_sync(0xffffffffu, ok && bar_wait(b_dv, abort_flag, err, 24));
     fence_after();
     if (ok) {
-      store_row(trow + 256, dv + (int64_t)(row0 + r) * ldg + col0, live, acc, rnd);
+      store_chunk(trow + 256 + half * 32, dv + (int64_t)(row0 + r) * ldg + col0 + half * 32, live, acc, rnd);
       // dS^T into the P^T region for dK
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float g[32];
-        tld32(trow + 128 + c * 32, g);
-        put_col(R0, r, c, g);
+        tld32(trow + 128 + (2 * half + c) * 32, g);
+        put_col(R0, r, 2 * half + c, g);
       }
     }
     fence_async_smem();
     bar_arrive(b_dst);
     if (!rounded) {
-      if (ok && bar_wait(b_ld3, abort_flag, err, 25)) round_region(R4, kTile, t);
+      if (ok && bar_wait(b_ld3, abort_flag, err, 25)) round_region(R4, kTile, t, kBwdEpi);
       fence_async_smem();
       bar_arrive(b_cv3);
     }
     ok = __all_sync(0xffffffffu, ok && bar_wait(b_dq, abort_flag, err, 26));
     fence_after();
-    if (ok) store_row(trow + 320, dq + (int64_t)(row0 + r) * ldg + col0, live, acc, rnd);
+    if (ok) store_chunk(trow + 320 + half * 32, dq + (int64_t)(row0 + r) * ldg + col0 + half * 32, live, acc, rnd);
     ok = __all_sync(0xffffffffu, ok && bar_wait(b_dk, abort_flag, err, 27));
     fence_after();
-    if (ok) store_row(trow + 384, dk + (int64_t)(row0 + r) * ldg + col0, live, acc, rnd);
+    if (ok) store_chunk(trow + 384 + half * 32, dk + (int64_t)(row0 + r) * ldg + col0 + half * 32, live, acc, rnd);
   }
   fence_before();
   __syncthreads();
@@ -722,7 +771,7 @@ extern "C" int tx_attention_bwd(tx_ctx *ctx, const float *q, const float *k, con
     TX_CUDA(ctx, cudaFuncSetAttribute(k_attn_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
     attr = true;
   }
-  k_attn_bwd<<<(unsigned)(batch * heads), 192, kBwdSmem, ctx->stream>>>(
+  k_attn_bwd<<<(unsigned)(batch * heads), 64 + kBwdEpi, kBwdSmem, ctx->stream>>>(
       mq, mk, mv, mdo, mqn, mkn, mdon, dq, dk, dv, ld_grad, (int)seq, (int)heads, scale, flags & 7, ctx->d_err);
   TX_LAUNCHED(ctx, "k_attn_bwd");
   return TX_OK;
