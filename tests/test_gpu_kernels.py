@@ -635,3 +635,24 @@ def test_bias_grad_and_reductions(tx):
     t = tx.Tensor(x)
     np.testing.assert_allclose(t.mean(1).numpy(), x.mean(1), rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(t.sum().numpy(), [x.astype(np.float64).sum()], rtol=1e-5)
+
+
+def test_gelu_and_derivative_within_2e7_of_float64(tx):
+    """GELU and GELU' of the elementwise kernels (the GEMM epilogues share the
+    same device functions) against float64 erf over [-12, 12] and a few edge
+    values: absolute error at most 3e-7 * max(1, |x|)."""
+    from scipy.special import erf
+
+    x = np.concatenate([np.linspace(-12.0, 12.0, 240001),
+                        [0.0, -0.0, 1e-30, -1e-30, 1e-6, -1e-6, 0.75, -0.75]]).astype(np.float32)
+    t = tx.Tensor(x, requires_grad=True)
+    y = t.gelu()
+    y.sum().backward()
+    x64 = x.astype(np.float64)
+    cdf = 0.5 * (1.0 + erf(x64 / np.sqrt(2.0)))
+    pdf = np.exp(-0.5 * x64 * x64) / np.sqrt(2.0 * np.pi)
+    bound = 3e-7 * np.maximum(1.0, np.abs(x64))
+    err_y = np.abs(y.numpy().astype(np.float64) - x64 * cdf)
+    err_g = np.abs(t.grad.numpy().astype(np.float64) - (cdf + x64 * pdf))
+    assert np.all(err_y <= bound), float((err_y / bound).max())
+    assert np.all(err_g <= bound), float((err_g / bound).max())

@@ -37,13 +37,10 @@ __device__ __forceinline__ void raise_flag(int *flag, int code, int a, int b) {
   }
 }
 
-// ---- activations (exact-erf GELU as in crates/tynx/src/interpreter/unary.rs:234) --------
-__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-__device__ __forceinline__ float gelu_grad(float x) {
-  float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-  float pdf = expf(-0.5f * x * x) * 0.39894228040143268f;
-  return cdf + x * pdf;
-}
+// ---- activations (erf GELU as in crates/tynx/src/interpreter/unary.rs:234; the
+// GEMM epilogues' form, so fused and standalone GELU give the same bits) --------
+__device__ __forceinline__ float gelu_f(float x) { return tx_epi::gelu(x); }
+__device__ __forceinline__ float gelu_grad(float x) { return tx_epi::gelu_grad(x); }
 
 __device__ __forceinline__ float unary_f(int op, float x, float a, float b) {
   switch (op) {
