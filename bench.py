@@ -545,7 +545,7 @@ def gemm_roofline(tx, ctx, ext, wl, per_rank: int, math: str) -> dict:
     tpath = ROOT / "profiles" / "roofline_traffic.json"
     if tpath.exists() and math == "tf32":
         entry = json.loads(tpath.read_text()).get(wl.name)
-        if entry and per_rank == wl.batch:
+        if entry and per_rank == wl.batch == entry.get("batch"):
             traffic = entry["traffic_bytes"]
     epi = ("+bias" if with_bias else "") + f"+{act}" + ("+preact" if with_preact else "")
     # algorithmic HBM bytes: A and B read once, C (and the pre-activation) written once
