@@ -893,7 +893,8 @@ __global__ void k_adam_bc(const int64_t *__restrict__ steps, float *__restrict__
   }
 }
 
-constexpr int64_t kAdamSub = 2048;  // elements per CTA: two float4 per thread (256 threads)
+constexpr int64_t kChunk_ = 4096;   // elements per optimizer chunk (kChunk below)
+constexpr int64_t kAdamSub = 2048;  // elements per CTA piece: two float4 per thread (256 threads)
 
 // At most 64 registers, so several CTAs share an SM.
 __global__ void __launch_bounds__(256, 4)
@@ -901,9 +902,7 @@ __global__ void __launch_bounds__(256, 4)
            const OptHparams *__restrict__ hp_ptr, int64_t *steps, float *__restrict__ bc,
            const int32_t *__restrict__ active_list, int n_active, int kind, int amsgrad, unsigned *ticket) {
   const OptHparams hp = *hp_ptr;
-  const OptChunk ch = chunks[blockIdx.x];
-  const OptTensor t = tensors[ch.tensor];
-  const float bc1 = bc[2 * ch.tensor], bc2 = bc[2 * ch.tensor + 1];
+  float bc1 = 1.f, bc2 = 1.f;  // the current piece's tensor's bias corrections
   const bool coupled = (kind == 0) && hp.wd != 0.f;
   const bool decoupled = (kind == 1) && hp.wd != 0.f;
   // one element, in the order of adam.rs:458-509 (no FMA contraction)
@@ -922,11 +921,22 @@ __global__ void __launch_bounds__(256, 4)
     if (decoupled) w = __fmul_rn(w, hp.decay_factor);
     w = __fsub_rn(w, upd);
   };
-  // this CTA's part of the chunk: blockIdx.y selects kAdamSub elements, so a
-  // thread updates one float4 (more resident warps hide the memory and
-  // division latencies)
+  // One wave of CTAs walks the kAdamSub-element pieces of the chunks in order
+  // (piece p: chunk p / subs, part p % subs): no partial last wave, and the
+  // next piece's chunk entry is fetched before this piece is updated, so the
+  // dependent descriptor loads overlap the stream.
+  constexpr int subs = (int)(kChunk_ / kAdamSub);
+  const int total = n_chunks * subs;
+  int p = blockIdx.x;
+  OptChunk ch_next = p < total ? chunks[p / subs] : OptChunk{0, 0, 0};
+  for (; p < total; p += gridDim.x) {
+  const OptChunk ch = ch_next;
+  if (p + (int)gridDim.x < total) ch_next = chunks[(p + gridDim.x) / subs];
+  const OptTensor t = tensors[ch.tensor];
+  bc1 = bc[2 * ch.tensor];
+  bc2 = bc[2 * ch.tensor + 1];
   const int64_t end = ch.start + ch.len;
-  const int64_t lo = ch.start + (int64_t)blockIdx.y * kAdamSub;
+  const int64_t lo = ch.start + (int64_t)(p % subs) * kAdamSub;
   const int64_t hi = lo + kAdamSub < end ? lo + kAdamSub : end;
   const bool vec = !amsgrad && (lo & 3) == 0 &&
                    ((((uintptr_t)t.w) | ((uintptr_t)t.g) | ((uintptr_t)t.m) | ((uintptr_t)t.v)) & 15) == 0;
@@ -983,6 +993,7 @@ __global__ void __launch_bounds__(256, 4)
       t.m[i] = m;
       t.v[i] = v;
     }
+  }
   }
   __shared__ int s_last;
   __syncthreads();
@@ -1507,7 +1518,7 @@ struct tx_optim {
 
 // elements per optimizer block: 4 float4 per thread at 256 threads, and enough
 // blocks (about 450 for 1.9 M parameters) to keep every SM streaming
-static const int64_t kChunk = 4096;
+static const int64_t kChunk = kChunk_;
 static int build_table(tx_optim *o, const std::vector<uint8_t> &key);
 
 // bias corrections of every tensor's next update from its step counter
@@ -1654,7 +1665,15 @@ extern "C" int tx_optim_step(tx_optim *o, const uint8_t *active) {
                                              n_chunks, al.first, al.second, o->cfg.nesterov,
                                              o->d_ticket);
   } else {
-    k_adam<<<dim3((unsigned)n_chunks, (unsigned)(kChunk / kAdamSub)), 256, 0, ctx->stream>>>(
+    const int64_t pieces = (int64_t)n_chunks * (kChunk / kAdamSub);
+    static int per_sm[64] = {};  // resident 256-thread CTAs per SM, per device
+    if (!per_sm[ctx->device & 63]) {
+      int nb = 0;
+      TX_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_adam, 256, 0));
+      per_sm[ctx->device & 63] = nb > 0 ? nb : 1;
+    }
+    const int64_t wave = (int64_t)ctx->num_sms * per_sm[ctx->device & 63];
+    k_adam<<<(unsigned)(pieces < wave ? pieces : wave), 256, 0, ctx->stream>>>(
         o->d_tensors, it->second.first, n_chunks, o->d_hp, o->d_steps, o->d_bc, al.first, al.second,
         o->cfg.kind, o->cfg.amsgrad, o->d_ticket);
   }
