@@ -49,6 +49,7 @@ pub const TX_GEMM_A_TF32: c_int = 1;
 pub const TX_GEMM_B_TF32: c_int = 2;
 pub const TX_GEMM_ROUND_OUT: c_int = 4;
 pub const TX_GEMM_EXACT: c_int = 8;
+pub const TX_GEMM_A_SHARED: c_int = 16;
 pub const TX_UN_NEG: c_int = 0;
 pub const TX_UN_EXP: c_int = 1;
 pub const TX_UN_LOG: c_int = 2;

@@ -185,8 +185,11 @@ typedef struct tx_gemm_desc {
  * engine sets it on forward contractions whose result passes through a ReLU,
  * whose mask is discontinuous: a TF32 rounding of the pre-activation flips it
  * wherever the value lies within ~2^-11 of zero, and every flip moves a whole
- * gradient entry.  Other math modes ignore the flags. */
-enum { TX_GEMM_A_TF32 = 1, TX_GEMM_B_TF32 = 2, TX_GEMM_ROUND_OUT = 4, TX_GEMM_EXACT = 8 };
+ * gradient entry.  Other math modes ignore the flags, except A_SHARED: a
+ * batched product (batch > 1) whose A is one matrix for every batch entry
+ * (stride_a must be 0), as when sibling projections of one input run as one
+ * launch over weights stored back to back. */
+enum { TX_GEMM_A_TF32 = 1, TX_GEMM_B_TF32 = 2, TX_GEMM_ROUND_OUT = 4, TX_GEMM_EXACT = 8, TX_GEMM_A_SHARED = 16 };
 int tx_gemm(tx_ctx *ctx, const tx_gemm_desc *desc);
 /* dst[i] = src[i] rounded to TF32 (round to nearest, ties away from zero;
  * dst may equal src).  The operand shadow of TX_GEMM_A_TF32 / B_TF32. */

@@ -656,3 +656,61 @@ def test_gelu_and_derivative_within_2e7_of_float64(tx):
     err_g = np.abs(t.grad.numpy().astype(np.float64) - (cdf + x64 * pdf))
     assert np.all(err_y <= bound), float((err_y / bound).max())
     assert np.all(err_g <= bound), float((err_g / bound).max())
+
+
+def _tf32_rn(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((u + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+@pytest.mark.parametrize("math,split,tol", [("tf32", False, 2e-3), ("3xtf32", False, 1e-5), ("fp32", False, 1e-5),
+                                            ("tf32", True, 5e-5)])
+@pytest.mark.parametrize("M,N,K", [(4096, 256, 256), (32768, 256, 256), (300, 96, 64)])
+def test_batched_product_with_shared_a(tx, math, split, tol, M, N, K):
+    """TX_GEMM_A_SHARED: one A for a batch of three B stored back to back
+    (with padding between them) into three C slices, equal to the three
+    products.  split: the engine's form for projections, the weights as a
+    TF32 head and tail (B_lo) and A already TF32, compared with A_tf32 @ B."""
+    import ctypes as C
+
+    from tynx_b200 import _core
+    from tynx_b200 import _native as N_
+
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    spacing = K * N + 64
+    Bflat = rng.standard_normal(3 * spacing).astype(np.float32)
+    Bs = [Bflat[z * spacing:z * spacing + K * N].reshape(K, N) for z in range(3)]
+    ctx = _core.context()
+    ctx.math = math
+    try:
+        flags = N_.TX_GEMM_A_SHARED
+        if split:
+            A = _tf32_rn(A)
+            head = _tf32_rn(Bflat)
+            tail = _tf32_rn(Bflat - head)
+            b, blo = tx.Tensor(head), tx.Tensor(tail)
+            flags |= N_.TX_GEMM_A_TF32 | N_.TX_GEMM_B_TF32
+        else:
+            b, blo = tx.Tensor(Bflat), None
+        a = tx.Tensor(A)
+        c = tx.Tensor(np.zeros((3, M, N), np.float32))
+        d = N_.GemmDesc()
+        d.M, d.N, d.K = M, N, K
+        d.A, d.lda, d.trans_a = a.ptr, K, 0
+        d.B, d.ldb, d.trans_b = b.ptr, N, 0
+        d.C, d.ldc = c.ptr, N
+        d.alpha, d.bias_scale = 1.0, 1.0
+        d.batch, d.stride_a, d.stride_b, d.stride_c = 3, 0, spacing, M * N
+        d.flags = flags
+        if blo is not None:
+            d.B_lo = blo.ptr
+        ctx.check(N_.lib.tx_gemm(ctx.handle, C.byref(d)), "gemm")
+        got = c.numpy()
+    finally:
+        ctx.math = "tf32"
+    A64 = A.astype(np.float64)
+    for z in range(3):
+        ref = A64 @ Bs[z].astype(np.float64)
+        err = np.linalg.norm(got[z] - ref) / np.linalg.norm(ref)
+        assert err <= tol, (z, err)

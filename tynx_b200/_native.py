@@ -35,7 +35,7 @@ TX_MATH = {"tf32": 0, "3xtf32": 1, "fp32": 2, "tf32trunc": 3}
 MAX_DIMS = 8
 
 ACT = {"none": 0, "relu": 1, "tanh": 2, "gelu": 3}
-TX_GEMM_A_TF32, TX_GEMM_B_TF32, TX_GEMM_ROUND_OUT, TX_GEMM_EXACT = 1, 2, 4, 8
+TX_GEMM_A_TF32, TX_GEMM_B_TF32, TX_GEMM_ROUND_OUT, TX_GEMM_EXACT, TX_GEMM_A_SHARED = 1, 2, 4, 8, 16
 UN = {"neg": 0, "exp": 1, "log": 2, "relu": 3, "tanh": 4, "gelu": 5, "sigmoid": 6, "clamp": 7,
       "sqrt": 8, "abs": 9, "scale": 10, "pow": 11, "erf": 12, "leakyrelu": 13, "softplus": 14, "elu": 15,
       "hardsigmoid": 16, "softsign": 17, "reciprocal": 18}

@@ -559,6 +559,9 @@ struct GNode {
   bool exact = false;
   // member of a fused attention block (tx_graph::attn index), or -1
   int attn = -1;
+  // member of a group of sibling projections run as one batched product
+  // (tx_graph::proj index), or -1
+  int proj = -1;
 };
 
 // An attention block the fused kernels can run: q, k, v are [B, S, H * D]
@@ -572,6 +575,19 @@ struct AttnPlan {
   int first = -1, last = -1;    // node index range of the block
   float scale = 1.f;
   bool round_out = false;       // TF32 mode: out only feeds contractions
+};
+
+// Sibling projections of one input: MatMuls X @ W_z (z = 0, 1, 2) whose
+// weights are parameters of one shape stored back to back (spacing elements
+// apart) and whose results have no other writer (the q, k and v of a fused
+// attention block).  They run as one batched product over the three weights
+// with A shared, writing three consecutive slices of one allocation.
+struct ProjGroup {
+  int node[3] = {-1, -1, -1};   // in weight-offset order
+  int out[3] = {-1, -1, -1};
+  int weight0 = -1;             // value id of the lowest-offset weight
+  int leader = -1;              // the first of the three nodes to run
+  int64_t spacing = 0;          // elements between consecutive weights
 };
 
 struct tx_graph {
@@ -593,6 +609,7 @@ struct tx_graph {
   int64_t bucket_bytes = 0;
   std::vector<int> grad_final_order;  // param indices in the order grads become final
   std::vector<AttnPlan> attn;          // fused attention blocks
+  std::vector<ProjGroup> proj;         // batched sibling projections
 };
 
 struct tx_record {
@@ -606,6 +623,7 @@ struct tx_record {
   bool shadow = false;     // parameters read by GEMMs come from flat_tf32
   bool tracking = false;
   std::vector<uint8_t> attn_fused;  // per tx_graph::attn block: ran as the fused kernels
+  std::vector<uint8_t> proj_done;   // per tx_graph::proj group: ran as one batched product
   std::vector<uint8_t> conv_implicit;  // per node: the convolution ran as an implicit GEMM (1;
                                        // extra holds its channels-last input, or null when
                                        // the input value is channels-last itself) or as the
@@ -1402,6 +1420,45 @@ extern "C" int tx_graph_create(tx_ctx *ctx, const tx_value_desc *vals, int n_val
                                    numel_of(v.shape) * sizeof(float), cudaMemcpyHostToDevice,
                                    ctx->stream));
   }
+  // ---- sibling projections of a fused attention block (needs the layout) ----------------------
+  for (const AttnPlan &a : g->attn) {
+    const int outs[3] = {a.q, a.k, a.v};
+    int pn[3], w[3];
+    int64_t off[3];
+    bool ok = true;
+    for (int z = 0; z < 3 && ok; ++z) {
+      pn[z] = g->values[outs[z]].producer;
+      if (pn[z] < 0) {
+        ok = false;
+        break;
+      }
+      const GNode &n = g->nodes[pn[z]];
+      ok = n.d.op == TX_OP_MATMUL && n.d.n_in == 2 && n.fused_act == TX_ACT_NONE && n.scale_out < 0 &&
+           !n.exact && n.out_scale == 1.f && n.attn < 0 && n.proj < 0 && n.d.out[0] == outs[z];
+      if (!ok) break;
+      w[z] = n.d.in[1];
+      const GValue &wv = g->values[w[z]];
+      ok = wv.kind == TX_VAL_PARAM && wv.shape.size() == 2 && n.d.in[0] == g->nodes[pn[0]].d.in[0] &&
+           wv.shape == g->values[w[0]].shape && n.round_out == g->nodes[pn[0]].round_out &&
+           g->values[outs[z]].shape == g->values[outs[0]].shape;
+      if (ok) off[z] = g->param_offset[wv.param_index];
+    }
+    if (!ok) continue;
+    int ord[3] = {0, 1, 2};
+    std::sort(ord, ord + 3, [&](int x, int y) { return off[x] < off[y]; });
+    const int64_t sp = off[ord[1]] - off[ord[0]];
+    if (sp <= 0 || off[ord[2]] - off[ord[1]] != sp || (sp & 3)) continue;
+    ProjGroup pg;
+    for (int z = 0; z < 3; ++z) {
+      pg.node[z] = pn[ord[z]];
+      pg.out[z] = outs[ord[z]];
+    }
+    pg.weight0 = w[ord[0]];
+    pg.leader = std::min(pn[0], std::min(pn[1], pn[2]));
+    pg.spacing = sp;
+    for (int z = 0; z < 3; ++z) g->nodes[pn[z]].proj = (int)g->proj.size();
+    g->proj.push_back(pg);
+  }
   for (int i = 0; i < n_values; ++i) {
     GValue &v = g->values[i];
     if (v.kind != TX_VAL_CONST) continue;
@@ -1553,9 +1610,64 @@ struct Fwd {
     return TX_OK;
   }
 
+  // The leader of a projection group runs the three products as one batched
+  // launch (A shared, the weights as a batch of three); TX_ERR_UNSUPPORTED
+  // when the outputs already have buffers (each member then runs alone).
+  int proj_forward(const ProjGroup &pg) {
+    for (int z = 0; z < 3; ++z)
+      if (r->buf[pg.out[z]]) return TX_ERR_UNSUPPORTED;
+    const GNode &n0 = g->nodes[pg.node[0]];
+    const Shape &a = S(n0.d.in[0]), &b = S(pg.weight0);
+    const int64_t K = a.back(), N = b.back(), M = numel_of(a) / K;
+    for (int z = 0; z < 3; ++z)
+      if (numel_of(S(pg.out[z])) != M * N) return TX_ERR_UNSUPPORTED;
+    float *blk = (float *)tx_alloc_raw(ctx, (size_t)(3 * M * N) * 4);
+    if (!blk) return TX_ERR_OOM;
+    for (int z = 0; z < 3; ++z) {
+      r->buf[pg.out[z]] = blk + z * M * N;
+      r->owned[pg.out[z]] = z == 0;  // the first slice's value frees the whole block
+    }
+    tx_gemm_desc q;
+    memset(&q, 0, sizeof q);
+    q.alpha = 1.f;
+    q.bias_scale = 1.f;
+    q.M = M;
+    q.N = N;
+    q.K = K;
+    q.batch = 3;
+    bool a32 = false, b32 = false;
+    q.A = gemm_operand(g, r, n0.d.in[0], &a32);
+    q.lda = K;
+    q.stride_a = 0;
+    q.B = gemm_operand(g, r, pg.weight0, &b32);
+    q.ldb = N;
+    q.stride_b = pg.spacing;
+    q.C = blk;
+    q.ldc = N;
+    q.stride_c = M * N;
+    q.flags = (a32 ? TX_GEMM_A_TF32 : 0) | (b32 ? TX_GEMM_B_TF32 : 0) | TX_GEMM_A_SHARED;
+    if (r->shadow && b32) q.B_lo = g->flat_lo + g->param_offset[g->values[pg.weight0].param_index];
+    if (n0.round_out && ctx->math == TX_MATH_TF32) {
+      q.flags |= TX_GEMM_ROUND_OUT;
+      for (int z = 0; z < 3; ++z) r->tf32[pg.out[z]] = true;
+    }
+    return gemm_dispatch(ctx, q);
+  }
+
   int gemm_node(int ni) {
     GNode &n = g->nodes[ni];
     const tx_node_desc &d = n.d;
+    if (n.proj >= 0) {
+      if (r->proj_done[n.proj]) return TX_OK;
+      const ProjGroup &pg = g->proj[n.proj];
+      if (ni == pg.leader) {
+        const int rc = proj_forward(pg);
+        if (rc != TX_ERR_UNSUPPORTED) {
+          if (rc == TX_OK) r->proj_done[n.proj] = 1;
+          return rc;
+        }
+      }
+    }
     int yv = n.fused_act ? n.fused_out : n.scale_out >= 0 ? n.scale_out : d.out[0];
     TX_TRY(alloc_value(yv));
     const Shape &a = S(d.in[0]), &b = S(d.in[1]);
@@ -2006,6 +2118,7 @@ extern "C" int tx_graph_forward(tx_graph *g, const void *const *d_inputs, const 
   r->extra2.assign(g->nodes.size(), {});
   r->tf32.assign(nv, false);
   r->attn_fused.assign(g->attn.size(), 0);
+  r->proj_done.assign(g->proj.size(), 0);
   r->conv_implicit.assign(g->nodes.size(), 0);
   if (ctx->math == TX_MATH_TF32 && g->flat_len > 0) {
     // the contractions of this forward (and of its backward) read parameters

@@ -314,7 +314,7 @@ int gemm_dispatch(tx_ctx *ctx, const tx_gemm_desc &desc, bool *rounded) {
   if (rounded) *rounded = false;
   tx_gemm_desc d = desc;
   if (ctx->math != TX_MATH_TF32) {
-    d.flags = 0;  // TF32 operand / output rounding only applies there
+    d.flags &= TX_GEMM_A_SHARED;  // TF32 operand / output rounding only applies there
     d.B_lo = nullptr;
   }
   if (d.B_lo && d.M > 0 && d.N > 0) {

@@ -187,6 +187,11 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
   if (((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) || (d.lda & 3) || (d.ldb & 3))
     return TX_ERR_UNSUPPORTED;
   if (batch > 1 && ((d.stride_a & 3) || (d.stride_b & 3))) return TX_ERR_UNSUPPORTED;
+  // one A for every batch entry: its tensor map has a single batch entry and
+  // the kernels load it at batch 0
+  const bool a_shared = (d.flags & TX_GEMM_A_SHARED) && batch > 1;
+  if ((d.flags & TX_GEMM_A_SHARED) && batch > 1 && d.stride_a != 0) return TX_ERR_INVALID;
+  const int64_t a_batch = a_shared ? 1 : batch;
   // rows shorter than half a swizzle row waste most of each tile; SIMT is better
   const int64_t a_inner = d.trans_a ? d.M : d.K;
   const int64_t b_inner = d.trans_b ? d.K : d.N;
@@ -215,7 +220,7 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
     if (d.B_lo || (cv->op.wsplit && (fs || d.preact || batch > 1))) return TX_ERR_UNSUPPORTED;
     if (cv->op.wsplit) tiling.splits = 1;
   }
-  if (!cv && mode == 1 && tiling.splits == 1 && tma_tileable(d.C, d.ldc, batch, d.stride_c) &&
+  if (!cv && !a_shared && mode == 1 && tiling.splits == 1 && tma_tileable(d.C, d.ldc, batch, d.stride_c) &&
       (!d.dact || tma_tileable(d.dact_src, d.ld_dact, batch, d.stride_c)) &&
       (!d.preact || tma_tileable(d.preact, d.ld_preact, batch, d.stride_c))) {
     const int pbn = d.N > 128 ? 256 : d.N > 64 ? 128 : 64;
@@ -265,14 +270,15 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
       if (tiles > (pbn == 256 ? 1 : 2) * (int64_t)ctx->num_sms) {
         persistent = true;
         tiling.bn = pbn;
-      } else if (d.B_lo && batch == 1) {
+      } else if (d.B_lo) {
         // split weights in one launch at any size (the head and tail products
         // share one main loop and one epilogue, where the one-tile kernel
         // would run a second product through beta * C; transformer step at
         // batch 32: 1.66 -> 1.42 ms); narrower tiles while a wave would leave
         // a quarter of the SMs idle
         int qbn = pbn;
-        while (qbn > 64 && ((d.M + TC_BM - 1) / TC_BM) * ((d.N + qbn - 1) / qbn) * 4 < 3 * (int64_t)ctx->num_sms)
+        while (qbn > 64 && ((d.M + TC_BM - 1) / TC_BM) * ((d.N + qbn - 1) / qbn) * batch * 4 <
+                               3 * (int64_t)ctx->num_sms)
           qbn /= 2;
         persistent = true;
         tiling.bn = qbn;
@@ -299,9 +305,9 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
   if (cv && cv->op.a)  // 128 pixels of the activation per tile: K-major, 128-byte swizzle
     ok = make_map_4d(&m.a, cv->src, cv->box, cv->estr_w, cv->estr_h, false);
   else if (d.trans_a)  // A stored K x M (MN-major): box 32(M) x 32(K)
-    ok = make_map(&m.a, d.A, d.M, d.K, d.lda, batch, d.stride_a, 32, true);
+    ok = make_map(&m.a, d.A, d.M, d.K, d.lda, a_batch, d.stride_a, 32, true);
   else  // A stored M x K (K-major): box 32(K) x 128(M)
-    ok = make_map(&m.a, d.A, d.K, d.M, d.lda, batch, d.stride_a, TC_BM, false);
+    ok = make_map(&m.a, d.A, d.K, d.M, d.lda, a_batch, d.stride_a, TC_BM, false);
   if (!ok) return TX_ERR_UNSUPPORTED;
   if (cv && cv->op.b == 1)  // 32 pixels by 32 channels per sub-tile: MN-major
     ok = make_map_4d(&m.b, cv->src, cv->box, cv->estr_w, cv->estr_h, true);
@@ -313,11 +319,12 @@ int tc_product(tx_ctx *ctx, const tx_gemm_desc &desc, int mode, FusedSum *fs, co
     ok = make_map(&m.b, d.B, d.N, d.K, d.ldb, batch, d.stride_b, 32, true);
   if (!ok) return TX_ERR_UNSUPPORTED;
   if (cv) m.g = cv->op;
+  m.g.ashared = a_shared ? 1 : 0;
   // dense MN-major operands whose MN extent is a multiple of 32: one box per
   // tile instead of one per 32-column block (the per-block maps stay when the
   // 4-D map is refused)
   CUtensorMap mn4;
-  if (d.trans_a && !(cv && cv->op.a) && make_map_mn4(&mn4, d.A, d.M, d.K, d.lda, batch, d.stride_a, TC_BM / 32)) {
+  if (d.trans_a && !(cv && cv->op.a) && make_map_mn4(&mn4, d.A, d.M, d.K, d.lda, a_batch, d.stride_a, TC_BM / 32)) {
     m.a = mn4;
     m.g.amn = 1;
   }

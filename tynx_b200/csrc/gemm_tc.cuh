@@ -38,6 +38,7 @@ struct GatherOp {
   // MN / 32, batch} and a tile's 32-column blocks come in one box instead of
   // one box each (the MN extent a multiple of 32)
   int amn, bmn;
+  int ashared;  // 1: A is one matrix for every batch entry (loaded at batch 0)
 };
 
 // Tensor maps of one launch: the operands, and for the TMA epilogue the

@@ -840,12 +840,13 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t fb = map_to_rank(smem_u32(&full[s]), 0);
           if (rank == 0) mbar_expect_tx(&full[s], 2 * (A_BYTES + B_BYTES));
           if (A_MN && gop.amn) {
-            tma_load_4d_pair(a_dst, &mapA, fb, 0, k0, m0 / 32, zc);
+            tma_load_4d_pair(a_dst, &mapA, fb, 0, k0, m0 / 32, gop.ashared ? 0 : zc);
           } else if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < TC_BM / 32; ++j) tma_load_3d_pair(a_dst + j * 4096, &mapA, fb, m0 + 32 * j, k0, zc);
+            for (int j = 0; j < TC_BM / 32; ++j)
+              tma_load_3d_pair(a_dst + j * 4096, &mapA, fb, m0 + 32 * j, k0, gop.ashared ? 0 : zc);
           } else {
-            tma_load_3d_pair(a_dst, &mapA, fb, k0, m0, zc);
+            tma_load_3d_pair(a_dst, &mapA, fb, k0, m0, gop.ashared ? 0 : zc);
           }
           const int nb = n0 + (int)rank * (BN / 2);
           if (B_MN && gop.bmn) {
@@ -862,9 +863,9 @@ __global__ void __launch_bounds__(320, 1)
         if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
         if (gop.a) {
         } else if (A_MN) {
-          load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, zc);
+          load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, gop.ashared ? 0 : zc);
         } else {
-          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
+          tma_load_3d(a_dst, &mapA, &full[s], k0, m0, gop.ashared ? 0 : zc);
         }
         if (gop.b) {
         } else if (B_MN) {
@@ -1206,9 +1207,9 @@ __global__ void __launch_bounds__(64 + 32 * EW + PCfg<BN, BLO, MODE>::CONV_THREA
           if (gop.a || gop.b) gather_loads<BN>(gop, &mapA, &mapB, &full[s], a_dst, b_dst, m0, n0, kb_first + kb);
           if (gop.a) {
           } else if (A_MN) {
-            load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, zc);
+            load_mn(a_dst, &mapA, &full[s], gop.amn, TC_BM / 32, m0, k0, gop.ashared ? 0 : zc);
           } else {
-            tma_load_3d(a_dst, &mapA, &full[s], k0, m0, zc);
+            tma_load_3d(a_dst, &mapA, &full[s], k0, m0, gop.ashared ? 0 : zc);
           }
           if (gop.b) {
           } else if (B_MN) {
