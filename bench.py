@@ -234,7 +234,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": "train samples/s (fwd+bwd+Adam)", "value": value,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy; BASELINE names no dataset)",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy; the reference names no dataset)",
         "config": bench_config(wl, world),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
                          "sample": f"each step: the numpy restatement of the Flex training step on "
@@ -437,7 +437,7 @@ def main() -> None:
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "tf32" if args.math == "tf32" else args.math,
-            "data": "synthetic (seeded numpy; BASELINE names no dataset)",
+            "data": "synthetic (seeded numpy; the reference names no dataset)",
             "config": bench_config(wl, world),
             "math": args.math,
             "achieved_tflops": wl.flop_per_step / (ms_per_step / 1e3) / 1e12,
