@@ -835,34 +835,38 @@ def _scale_nograd(x: Tensor, a: float, b: float) -> Tensor:
     return out
 
 
-def _getitem(x: Tensor, index) -> Tensor:
-    """Basic indexing: integers, slices (any step), Ellipsis and None; a
-    strided copy forward, a strided scatter into zeros backward (the Slice of
-    the capture IR)."""
+def _index_plan(shape: tuple, index) -> tuple:
+    """Basic indexing of a contiguous tensor of `shape` (integers, slices with
+    any step, Ellipsis, None) as a strided view: (element offset of the first
+    element, view shape, view strides in elements, result shape with the
+    inserted unit axes)."""
     if not isinstance(index, tuple):
         index = (index,)
     if any(isinstance(i, (Tensor, list, np.ndarray)) for i in index):
         raise NotImplementedError("advanced indexing is not supported; use gather")
+    ndim = len(shape)
     n_real = sum(1 for i in index if i is not None and i is not Ellipsis)
-    if n_real > x.ndim:
-        raise IndexError(f"too many indices for a tensor of rank {x.ndim}")
+    if n_real > ndim:
+        raise IndexError(f"too many indices for a tensor of rank {ndim}")
+    if sum(1 for i in index if i is Ellipsis) > 1:
+        raise IndexError("an index can only have a single ellipsis")
     expanded = []
     for i in index:
         if i is Ellipsis:
-            expanded += [slice(None)] * (x.ndim - n_real)
+            expanded += [slice(None)] * (ndim - n_real)
         else:
             expanded.append(i)
     if Ellipsis not in index:
-        expanded += [slice(None)] * (x.ndim - n_real)
-    st = _contig_strides(x.shape)
-    offset, shape, strides, out_shape = 0, [], [], []
+        expanded += [slice(None)] * (ndim - n_real)
+    st = _contig_strides(shape)
+    offset, vshape, strides, out_shape = 0, [], [], []
     axis = 0
     for i in expanded:
         if i is None:
             out_shape.append(1)
             continue
-        dim = x.shape[axis]
-        if isinstance(i, (int, np.integer)):
+        dim = shape[axis]
+        if isinstance(i, (int, np.integer)) and not isinstance(i, bool):
             k = int(i) + (dim if i < 0 else 0)
             if not 0 <= k < dim:
                 raise IndexError(f"index {int(i)} is out of bounds for axis {axis} with size {dim}")
@@ -871,20 +875,28 @@ def _getitem(x: Tensor, index) -> Tensor:
             start, stop, step = i.indices(dim)
             length = len(range(start, stop, step))
             offset += start * st[axis] if length else 0
-            shape.append(length)
+            vshape.append(length)
             strides.append(step * st[axis])
             out_shape.append(length)
         else:
             raise TypeError(f"unsupported index {i!r}")
         axis += 1
-    out = Tensor._empty(tuple(shape), x.dtype, x.ctx)
+    return offset, tuple(vshape), tuple(strides), tuple(out_shape)
+
+
+def _getitem(x: Tensor, index) -> Tensor:
+    """Basic indexing: integers, slices (any step), Ellipsis and None; a
+    strided copy forward, a strided scatter into zeros backward (the Slice of
+    the capture IR)."""
+    offset, shape, strides, out_shape = _index_plan(tuple(x.shape), index)
+    out = Tensor._empty(shape, x.dtype, x.ctx)
     if out.numel:
         x.ctx.check(lib.tx_strided_copy(x.ctx.handle, x.ptr + offset * x.itemsize, N.i64_array(strides), out.ptr,
                                         N.i64_array(shape), len(shape), x.itemsize))
     if _needs_grad(x):
         src_shape, base = x.shape, offset
 
-        def backward(g, shape=tuple(shape), strides=tuple(strides)):
+        def backward(g, shape=shape, strides=strides):
             dx = full(src_shape, 0.0, ctx=g[0].ctx)
             if g[0].numel:
                 g[0].ctx.check(lib.tx_strided_scatter(g[0].ctx.handle, g[0].ptr, dx.ptr + base * 4,
@@ -892,7 +904,7 @@ def _getitem(x: Tensor, index) -> Tensor:
             return [dx]
 
         out._attach(Fn("getitem", [x], backward))
-    return out.reshape(tuple(out_shape)) if tuple(out_shape) != tuple(shape) else out
+    return out.reshape(out_shape) if out_shape != shape else out
 
 
 def minimum(a, b) -> Tensor:
