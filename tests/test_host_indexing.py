@@ -94,3 +94,23 @@ def test_pool_output_length_matches_oracle(ceil):
                             continue
                         _, want = _pool_axis(size, k, s, d, p, p, "NOTSET", ceil)
                         assert _pool_out(size, k, s, p, d, ceil) == want, (size, k, s, p, d, ceil)
+
+
+def test_repeat_plan_matches_numpy_tile():
+    from tynx_b200._core import _repeat_plan
+
+    rng = np.random.default_rng(1)
+    for _ in range(500):
+        ndim = int(rng.integers(0, 4))
+        shape = tuple(int(s) for s in rng.integers(1, 5, ndim))
+        sizes = tuple(int(r) for r in rng.integers(0, 4, ndim + int(rng.integers(0, 3))))
+        if not sizes:
+            continue
+        x = rng.standard_normal(shape).astype(np.float32)
+        inter, tiled, final = _repeat_plan(shape, sizes)
+        got = np.broadcast_to(x.reshape(inter), tiled).reshape(final)
+        np.testing.assert_array_equal(got, np.tile(x, sizes))
+    with pytest.raises(ValueError):
+        _repeat_plan((2, 3), (2,))
+    with pytest.raises(ValueError):
+        _repeat_plan((2,), (-1,))

@@ -587,17 +587,8 @@ class Tensor:
         """Tile along each axis (leading sizes add axes), as torch.Tensor.repeat."""
         if len(sizes) == 1 and isinstance(sizes[0], (tuple, list)):
             sizes = tuple(sizes[0])
-        if len(sizes) < self.ndim:
-            raise ValueError("repeat needs at least one size per axis")
-        x = self.reshape((1,) * (len(sizes) - self.ndim) + self.shape)
-        inter = []
-        for s in x.shape:
-            inter += [1, s]
-        tiled = []
-        for r, s in zip(sizes, x.shape):
-            tiled += [r, s]
-        out = x.reshape(tuple(inter)).expand(tuple(tiled))
-        return out.reshape(tuple(r * s for r, s in zip(sizes, x.shape)))
+        inter, tiled, final = _repeat_plan(tuple(self.shape), tuple(sizes))
+        return self.reshape(inter).expand(tiled).reshape(final)
 
     def erf(self):
         return _unary("erf", self)
@@ -833,6 +824,22 @@ def _scale_nograd(x: Tensor, a: float, b: float) -> Tensor:
     x.ctx.check(lib.tx_unary(x.ctx.handle, N.UN["scale"], x.ptr, out.ptr, x.numel, C.c_float(a),
                              C.c_float(b)))
     return out
+
+
+def _repeat_plan(shape: tuple, sizes: tuple) -> tuple:
+    """Tensor.repeat as reshape -> expand -> reshape: each axis of size s gets
+    a unit axis before it that broadcasts to its repeat count r (leading sizes
+    add axes of size 1 first); returns the three shapes."""
+    if len(sizes) < len(shape):
+        raise ValueError("repeat needs at least one size per axis")
+    if any(not isinstance(r, (int, np.integer)) or r < 0 for r in sizes):
+        raise ValueError("repeat sizes must be non-negative integers")
+    full_shape = (1,) * (len(sizes) - len(shape)) + tuple(shape)
+    inter, tiled = [], []
+    for r, s in zip(sizes, full_shape):
+        inter += [1, s]
+        tiled += [int(r), s]
+    return tuple(inter), tuple(tiled), tuple(int(r) * s for r, s in zip(sizes, full_shape))
 
 
 def _index_plan(shape: tuple, index) -> tuple:
